@@ -1,0 +1,397 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Gemma-4 MoE block (BASELINE metric: MoE-block tokens/s;
+headline workload = configs[1], butterquant decode batch 64).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
+
+A step is one MoE-block forward over one batch of synthetic tokens through the
+C ABI (gm_moe_forward).  `value` is tokens/s with inputs resident in HBM;
+`e2e` is the same metric through the blocking entry point gm_moe_forward_sync
+with pinned host buffers (H2D of x and D2H of the output inside the timed
+region).  `--impl reference` times the CPU restatement of the reference path
+(oracle/, the Mojo reference cannot be built here) on the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mojo-gemma4-cpu_b200")
+sys.path.insert(0, ROOT)
+sys.path.insert(0, PKG)
+
+H, E, TOPK, I, GU = 2816, 128, 8, 704, 1408
+BQ_EXPERT_GU_BYTES = GU * H + GU * 4          # int8 rows + f32 row scales
+BQ_EXPERT_DN_BYTES = H * I + H * 4
+BQ_EXPERT_BYTES = BQ_EXPERT_GU_BYTES + BQ_EXPERT_DN_BYTES   # 5,964,288
+BF16_EXPERT_BYTES = (GU * H + H * I) * 2                     # 11,894,784
+FLOP_PER_TOKEN = TOPK * (2 * GU * H + 2 * H * I)              # 95,158,272
+
+WORKLOADS = {
+    # name: (tokens per step per GPU, weight format)
+    "bq-decode-b64": (64, "bq"),
+    "bq-decode-b8": (8, "bq"),
+    "bq-decode-b1": (1, "bq"),
+    "bf16-decode-b16": (16, "bf16"),
+    "bq-prefill-4k": (4096, "bq"),
+    "bf16-prefill-4k": (4096, "bf16"),
+}
+METRIC = "MoE-block tokens/s at 1/2/4/8 B200 (decode b=64, prefill 4k); % of roofline"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--workload", default="bq-decode-b64", choices=sorted(WORKLOADS))
+    p.add_argument("--impl", default="gmoe", choices=["gmoe", "reference"])
+    p.add_argument("--cpu-seconds", type=float, default=12.0,
+                   help="bounded CPU-baseline sample length")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--batches", type=int, default=8, help="distinct token batches cycled")
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", "clocks_bench_%d.csv" % os.getpid())
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[4:]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for _, _, r in rows:
+            for n, v in zip(names, r[1:5]):
+                if "Active" in v and "Not" not in v:
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def build_layer(fmt, seed, device_rank):
+    import synth
+    raw = synth.make_layer(seed=seed, device="cuda")
+    if fmt == "bq":
+        return synth.bq_layer(raw), raw
+    return synth.bf16_layer(raw), raw
+
+
+def register(blk, fmt, L):
+    if fmt == "bq":
+        blk.register_bq(0, L["gate_up"], L["gate_up_scale"], L["down"], L["down_scale"],
+                        L["router_centered"], L["router_scale"], L["per_expert_scale"],
+                        L["pre_ffn_norm_2"])
+    else:
+        blk.register_bf16(0, L["gate_up"], L["down"], L["router_proj"], L["router_scale"],
+                          L["per_expert_scale"], L["pre_ffn_norm_2"])
+
+
+def cpu_baseline_sample(fmt, T, seconds, raw_cpu, xs_cpu):
+    """Time the oracle (CPU restatement of the reference path, all host cores)
+    on repeated forwards of the same workload until `seconds` have elapsed."""
+    from oracle import oracle as O
+    import numpy as np
+    import synth
+    L = {}
+    if fmt == "bq":
+        gu_q, gu_s = O.quantize_rows(raw_cpu["gate_up"].reshape(E * GU, H), 128, raw_cpu["pre_ffn_norm_2"])
+        dn_q, dn_s = O.quantize_rows(raw_cpu["down"].reshape(E * H, I), 64)
+        L = {"router_centered": O.router_center(raw_cpu["router_proj"]),
+             "router_scale": O.bake_router_scale(raw_cpu["router_scale"]),
+             "pes": raw_cpu["per_expert_scale"], "gamma2": O.bake_split_gain(raw_cpu["pre_ffn_norm_2"]),
+             "gu_q": gu_q, "gu_scale": gu_s, "gu_cs": O.colsum(gu_q, H, True).reshape(-1),
+             "dn_q": dn_q, "dn_scale": dn_s, "dn_cs": O.colsum(dn_q, 64, False)}
+        fwd = O.bq_forward
+    else:
+        L = {"router_proj": raw_cpu["router_proj"], "router_scale": O.bake_router_scale(raw_cpu["router_scale"]),
+             "pes": raw_cpu["per_expert_scale"], "gamma2": raw_cpu["pre_ffn_norm_2"],
+             "w_gu": raw_cpu["gate_up"], "w_dn": raw_cpu["down"]}
+        fwd = O.bf16_forward
+    fwd(xs_cpu[0][:min(T, 4)], L)  # warm (page in weights)
+    n_tok, t0, i = 0, time.perf_counter(), 0
+    while True:
+        x = xs_cpu[i % len(xs_cpu)]
+        fwd(x, L)
+        n_tok += x.shape[0]
+        i += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return n_tok / el, i, O.lib().orc_num_threads()
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement timed on this host (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    os.environ.setdefault("GMOE_ORACLE_VARIANT", "native")
+    from oracle import build as ob
+    try:
+        ob.build("native")
+    except Exception:
+        os.environ["GMOE_ORACLE_VARIANT"] = "portable"
+    import synth
+    T, fmt = WORKLOADS[args.workload]
+    raw = {k: synth.to_numpy(v) for k, v in synth.make_layer(seed=0x6E6D6F45, device="cpu").items()}
+    xs = [synth.to_numpy(synth.make_tokens(T, seed=s)) for s in range(2)]
+    # each step is one forward of T tokens; the run is bounded by --cpu-seconds
+    rate, iters, cores = cpu_baseline_sample(fmt, T, max(1.0, args.cpu_seconds), raw, xs)
+    line = {"metric": METRIC, "value": rate, "unit": "tokens/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": iters, "warmup": 1, "ms_per_step": 1e3 * T / rate,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "i8" if fmt == "bq" else "bf16", "data": "synthetic",
+            "config": {"workload": args.workload, "tokens_per_step": T, "weights": fmt},
+            "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": "%d forwards of %d tokens (%.0f s) of the C++ restatement" % (iters, T, args.cpu_seconds)},
+            "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+    import gmoe
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    T, fmt = WORKLOADS[args.workload]
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+
+    L, raw = build_layer(fmt, 0x6E6D6F45, local)
+    blk = gmoe.MoeBlock(T, 1, device=local)
+    register(blk, fmt, L)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1000 + rank)
+    xs = [torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16) for _ in range(args.batches)]
+    outs = [torch.empty(T, H, dtype=torch.bfloat16, device="cuda") for _ in range(args.batches)]
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        blk.forward(0, xs[i % len(xs)], outs[i % len(xs)], T, stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    value = world * T * args.steps / (ms / 1e3)
+
+    # ---- end to end through the blocking entry point with pinned host buffers
+    xh = [x.cpu().pin_memory() for x in xs]
+    oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    for i in range(3):
+        blk.forward_sync(0, xh[i % len(xh)], oh, T)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        blk.forward_sync(0, xh[i % len(xh)], oh, T)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * T * args.steps / e2e_s
+
+    # ---- roofline of the dominant kernel (expert phase 1), CUDA events on the
+    # launching stream around the same per-stage entry points the forward uses
+    roof = roofline(blk, fmt, L, xs, T, args.steps, stream)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "i8" if fmt == "bq" else "bf16",
+        "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights; random-init, no checkpoint)",
+        "config": {"workload": args.workload, "tokens_per_step": T, "weights": fmt,
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "inputs larger than L2: %d distinct token batches, routed expert weights %.0f MB per step"
+                         % (len(xs), roof.get("weight_mb", 0))},
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2},
+        "gpu_launches": 7 * args.steps,
+        "roofline": {k: roof[k] for k in ("bound", "achieved", "peak", "unit", "frac", "traffic")},
+        "roofline_detail": roof["detail"],
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_leg(fmt, T, args, raw)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    blk.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def cpu_leg(fmt, T, args, raw_dev):
+    import synth
+    os.environ.setdefault("GMOE_ORACLE_VARIANT", "native")
+    from oracle import build as ob
+    try:
+        ob.build("native")
+    except Exception:
+        os.environ["GMOE_ORACLE_VARIANT"] = "portable"
+    raw_cpu = {k: synth.to_numpy(v) for k, v in raw_dev.items()}
+    import torch
+    g = torch.Generator(device="cpu")
+    g.manual_seed(7)
+    xs = [synth.to_numpy(torch.randn(T, H, generator=g).to(torch.bfloat16)) for _ in range(2)]
+    rate, iters, cores = cpu_baseline_sample(fmt, T, args.cpu_seconds, raw_cpu, xs)
+    return {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": "%d forwards of %d tokens over %.0f s (C++ restatement of the reference path, OpenMP)"
+                      % (iters, T, args.cpu_seconds)}
+
+
+def roofline(blk, fmt, L, xs, T, steps, stream):
+    """Time the dominant kernel (phase 1 gate/up) per launch with CUDA events
+    on its stream, over `steps` launches on the same inputs the forward uses."""
+    import torch
+    import gmoe
+    hbm, tf, src = peaks()
+    x = xs[0]
+    lg = torch.empty(T, E, dtype=torch.float32, device="cuda")
+    idx = torch.empty(T, TOPK, dtype=torch.int32, device="cuda")
+    w = torch.empty(T, TOPK, dtype=torch.float32, device="cuda")
+    off = torch.empty(E + 1, dtype=torch.int32, device="cuda")
+    routes = torch.empty(T * TOPK, 2, dtype=torch.int32, device="cuda")
+    pos = torch.empty(T * TOPK, dtype=torch.int32, device="cuda")
+    chunk = torch.empty(E + 1, dtype=torch.int32, device="cuda")
+    R = T * TOPK
+    s = stream
+    if fmt == "bq":
+        gmoe.call("gm_router_select", x, L["router_centered"], L["router_scale"], L["per_expert_scale"],
+                  T, lg, idx, w, s)
+        gmoe.call("gm_build_expert_schedules", idx, w, T, 0, E, 16, off, routes, pos, chunk, s)
+        xq = torch.empty(T, H, dtype=torch.int8, device="cuda")
+        xsa = torch.empty(T, dtype=torch.float32, device="cuda")
+        gmoe.call("gm_bq_norm_quant", x, L["pre_ffn_norm_2"], T, xq, xsa, s)
+        bq = torch.empty(R, I, dtype=torch.int8, device="cuda")
+        bsa = torch.empty(R, 11, dtype=torch.float32, device="cuda")
+
+        def launch():
+            gmoe.call("gm_bq_phase1_gate_up", xq, xsa, off, routes, chunk, E, T, L["gate_up"],
+                      L["gate_up_scale"], bq, bsa, None, s)
+        per_expert = BQ_EXPERT_GU_BYTES
+    else:
+        gmoe.call("gm_router_select", x, L["router_proj"], L["router_scale"], L["per_expert_scale"],
+                  T, lg, idx, w, s)
+        gmoe.call("gm_build_expert_schedules", idx, w, T, 0, E, 8, off, routes, pos, chunk, s)
+        xn = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        gmoe.call("gm_rms_norm", x, L["pre_ffn_norm_2"], T, xn, s)
+        bucket = torch.empty(R, I, dtype=torch.bfloat16, device="cuda")
+
+        def launch():
+            gmoe.call("gm_phase1_gate_up_bf16", xn, off, routes, chunk, E, T, L["gate_up"], bucket, s)
+        per_expert = GU * H * 2
+    torch.cuda.synchronize()
+    distinct = int(torch.unique(idx).numel())
+    for _ in range(3):
+        launch()
+    # flush L2 between timed launches: 256 MB write (> 126 MB L2)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    tot = 0.0
+    n = max(5, min(steps, 50))
+    for _ in range(n):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        launch()
+        b.record(s)
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    avg_ms = tot / n
+    if T >= 1024:
+        flops = 2.0 * T * TOPK * GU * H
+        ach = flops / (avg_ms / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": tf, "unit": "TFLOP/s", "frac": ach / tf,
+                "traffic": None, "weight_mb": distinct * per_expert / 1e6,
+                "detail": {"kernel": "phase1_gate_up", "avg_launch_us": avg_ms * 1e3,
+                           "flop_per_launch": flops, "peak_source": src + " (bf16 burst)"}}
+    algo = distinct * per_expert + T * H + T * 4 + R * (I + 11 * 4)
+    ach = algo / (avg_ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+            "traffic": None, "weight_mb": distinct * per_expert / 1e6,
+            "detail": {"kernel": "phase1_gate_up", "avg_launch_us": avg_ms * 1e3,
+                       "distinct_experts": distinct, "bytes_per_launch": algo,
+                       "bytes_per_expert": per_expert, "peak_source": src + " (hbm copy)"}}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,213 @@
+/* gmoe.h -- C ABI of the B200 (sm_100a) Gemma-4 mixture-of-experts block.
+ *
+ * Drop-in for the MoE operator of the Mojo CPU engine CoffeeVampir3/Mojo-Gemma4-CPU.
+ * Every entry point names the reference interface it replaces (paths are
+ * inside that project).  All pointers are plain addresses; bf16 tensors are
+ * 16-bit words; no PyTorch or other framework types cross this boundary.
+ *
+ * Conventions
+ *  - Return value: GM_OK (0) or a negative GM_E* status.  Nothing aborts or
+ *    traps; the text of the last failure is available from gm_last_error().
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *    Entry points taking a stream are asynchronous and stream-ordered.
+ *  - Device pointers unless stated otherwise.
+ *  - Dimensions are fixed by the model: hidden 2816, 128 experts, top-8,
+ *    expert intermediate 704 (gate|up fused 1408), down FWHT block 64
+ *    (modeling/gemma4_common.mojo:5,23-28).
+ */
+#ifndef GMOE_H
+#define GMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GM_OK 0
+#define GM_EINVAL (-1)   /* bad argument or shape */
+#define GM_ECUDA (-2)    /* CUDA runtime error */
+#define GM_ENOMEM (-3)   /* device allocation failed */
+#define GM_ENCCL (-4)    /* collective error */
+#define GM_ETIMEOUT (-5) /* bounded wait expired */
+#define GM_ESTATE (-6)   /* call out of order (e.g. layer not registered) */
+
+#define GM_HIDDEN 2816
+#define GM_NUM_EXPERTS 128
+#define GM_TOP_K 8
+#define GM_INTERMEDIATE 704
+#define GM_GATE_UP 1408
+#define GM_DOWN_BLOCK 64
+#define GM_ROUTE_CHUNK_BQ 16   /* route_chunk the butterquant expert kernels expect */
+#define GM_ROUTE_CHUNK_BF16 8  /* route_chunk the bf16 expert kernels expect */
+
+/* kernels/moe_router.mojo:33-36 SparseRoute{token, weight}. */
+typedef struct gm_sparse_route {
+  int32_t token;
+  float weight;
+} gm_sparse_route_t;
+
+typedef struct gm_moe gm_moe_t;
+
+const char* gm_version(void);
+
+/* Text of the last failure on this handle; with h == NULL, of the last failed
+ * stateless call on the calling thread. */
+const char* gm_last_error(const gm_moe_t* h);
+
+/* ---------------------------------------------------------------- handle --
+ * Replaces the per-model state the reference keeps for the MoE: expert weights
+ * in per-rank arenas (modeling/gemma_4_moe_bq.mojo:872-918 init_state /
+ * model_init) and the phase-scoped MoE scratch (Gemma4FfnMoeScratch,
+ * modeling/gemma_4_moe_bq.mojo:275-360).  Workspace is allocated once here for
+ * `max_tokens` tokens per call; calls never allocate.
+ * rank/degree: expert-parallel placement, experts [rank*128/degree,
+ * (rank+1)*128/degree) live on this handle (modeling/model_spec.mojo:106-110). */
+int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, int rank,
+                  int degree);
+int gm_moe_destroy(gm_moe_t* h);
+size_t gm_moe_workspace_bytes(int max_tokens);
+
+/* Butterquant layer weights, exactly in the reference's in-memory layout
+ * (host or device pointers; copied to the handle's device memory):
+ *   gate_up      int8, VNNI-packed [epr*1408][2816] (butterquant/vnni.mojo:31-83),
+ *                rows FWHT-128-rotated and split-gain scaled (quant/quantizer.mojo:963-1051)
+ *   gate_up_scale f32 [epr*1408] (amax/127)
+ *   down         int8, VNNI-packed [epr*2816][704], FWHT-64 rotated
+ *   down_scale   f32 [epr*2816]
+ *   router_centered bf16 [128][2816] (butterquant/kernels.mojo:218-224)
+ *   router_scale bf16 [2816], baked * 1/sqrt(2816) (modeling/gemma4_topology.mojo:362-388)
+ *   per_expert_scale bf16 [128]
+ *   pre_ffn_norm_2 bf16 [2816], split-gain baked (butterquant/kernels.mojo:37-45)
+ * epr = 128/degree; the expert tensors hold this rank's experts only, as the
+ * reference's row-block sharded bindings do (modeling/loader.mojo:113-125).
+ * The colsum sidecars of ButterquantWeight (butterquant/weight.mojo:50-64) are
+ * not taken: the kernels use signed x signed dots, which need none
+ * (quantization_docs/butterquant.md section 2.5). */
+int gm_moe_register_layer_bq(gm_moe_t* h, int layer, const void* gate_up,
+                             const float* gate_up_scale, const void* down,
+                             const float* down_scale, const void* router_centered,
+                             const void* router_scale, const void* per_expert_scale,
+                             const void* pre_ffn_norm_2);
+
+/* bf16 layer weights (modeling/gemma_4_moe.mojo): gate_up bf16 [epr][1408][2816],
+ * down bf16 [epr][2816][704], router_proj bf16 [128][2816], router_scale
+ * (baked), per_expert_scale, pre_ffn_norm_2 (raw gain, not split-baked). */
+int gm_moe_register_layer_bf16(gm_moe_t* h, int layer, const void* gate_up, const void* down,
+                               const void* router_proj, const void* router_scale,
+                               const void* per_expert_scale, const void* pre_ffn_norm_2);
+
+/* The MoE operator.  Replaces dispatch_bq_moe (modeling/gemma_4_moe_bq.mojo:
+ * 630-713) or, for a bf16 layer, dispatch_moe (modeling/gemma_4_moe.mojo:
+ * 493-566): x_input bf16 [T][2816] -> moe_out bf16 [T][2816].  At degree > 1
+ * the output is this rank's partial (its experts only, rounded to bf16), i.e.
+ * the value the reference holds just before dispatch_allreduce_inplace
+ * (kernels/reductions.mojo:186-204); summing the partials across ranks is the
+ * caller's exchange step.
+ * Asynchronous on `stream`; x and out are device pointers. */
+int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void* stream);
+
+/* Blocking form with the reference's calling convention (the reference's
+ * dispatchers fan out and join before returning, kernels/helpers.mojo:295-327):
+ * x and out may be host or device memory; host buffers are staged through the
+ * handle's device buffers. */
+int gm_moe_forward_sync(gm_moe_t* h, int layer, const void* x, void* out, int T);
+
+/* ----------------------------------------------------- per-stage kernels --
+ * Stateless entry points, one per reference dispatcher, for tests and for
+ * callers that own their scratch.  Device pointers. */
+
+/* dispatch_router_expert + dispatch_merge_router_candidates
+ * (kernels/moe_router.mojo:206-244,333-389): logits_ws f32 [T][128] (also an
+ * output), route_idx i32 [T][8] (logit-descending, ties to the lower id),
+ * route_w f32 [T][8] (softmax over the 8, times per_expert_scale). */
+int gm_router_select(const void* x, const void* router_w, const void* router_scale,
+                     const void* per_expert_scale, int T, float* logits_ws, int32_t* route_idx,
+                     float* route_w, void* stream);
+
+/* dispatch_build_expert_schedules (kernels/moe_router.mojo:109-145) for the
+ * experts [expert_base, expert_base+epr): expert_offset i32 [epr+1], routes
+ * [T*8] (stable, token-major).  Extra outputs: route_pos i32 [T*8] (position of
+ * route (t,k) in `routes`, -1 if not local) and chunk_off i32 [epr+1] (prefix
+ * of ceil(n_e/route_chunk), the work split of the expert kernels). */
+int gm_build_expert_schedules(const int32_t* route_idx, const float* route_w, int T,
+                              int expert_base, int epr, int route_chunk, int32_t* expert_offset,
+                              gm_sparse_route_t* routes, int32_t* route_pos, int32_t* chunk_off,
+                              void* stream);
+
+/* dispatch_rms_norm (kernels/rmsnorm.mojo:117) as used by dispatch_moe:
+ * out = bf16(x*inv_rms*gamma). */
+int gm_rms_norm(const void* x, const void* gamma, int T, void* out, void* stream);
+
+/* dispatch_bq_norm_quant (butterquant_kernels/linear.mojo:58-82, block 128):
+ * x_i8 [T][2816], x_sa f32 [T] (raw absmax). */
+int gm_bq_norm_quant(const void* x, const void* gamma, int T, int8_t* x_i8, float* x_sa,
+                     void* stream);
+
+/* dispatch_bq_phase1_gate_up (butterquant_kernels/moe.mojo:132-164) fused with
+ * dispatch_bq_block_quant of its output (butterquant_kernels/linear.mojo:
+ * 182-205): bucket_i8 [R][704] + bucket_sa f32 [R][11]; bucket_bf16 [R][704]
+ * (the reference's intermediate) is also written when non-NULL.  chunk_off
+ * must come from gm_build_expert_schedules with route_chunk = GM_ROUTE_CHUNK_BQ.
+ * T bounds the work (R <= T*8).  gate_up: VNNI-packed, as for register_layer_bq. */
+int gm_bq_phase1_gate_up(const int8_t* x_i8, const float* x_sa, const int32_t* expert_offset,
+                         const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr, int T,
+                         const void* gate_up, const float* gate_up_scale, int8_t* bucket_i8,
+                         float* bucket_sa, void* bucket_bf16, void* stream);
+
+/* dispatch_bq_block_quant[64, fwht] (butterquant_kernels/linear.mojo:182-205)
+ * on a bf16 bucket [rows][704]. */
+int gm_bq_block_quant(const void* bucket, long rows, int8_t* q, float* sa, void* stream);
+
+/* dispatch_bq_phase2_down (butterquant_kernels/moe.mojo:298-335) without the
+ * final accumulation: y f32 [R][2816], y[r] = facc*down_scale*route_weight of
+ * route r.  gm_combine performs the per-token accumulation. */
+int gm_bq_phase2_down(const int8_t* bucket_i8, const float* bucket_sa, const int32_t* expert_offset,
+                      const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr, int T,
+                      const void* down, const float* down_scale, float* y, void* stream);
+
+/* dispatch_phase1_gate_up (kernels/moe_experts.mojo:165-197), bf16; chunk_off
+ * from route_chunk = GM_ROUTE_CHUNK_BF16.  bucket bf16 [R][704]. */
+int gm_phase1_gate_up_bf16(const void* x_normed, const int32_t* expert_offset,
+                           const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr,
+                           int T, const void* gate_up, void* bucket, void* stream);
+
+/* dispatch_phase2_down (kernels/moe_experts.mojo:322-353) without the final
+ * accumulation: y f32 [R][2816] = dot * route_weight. */
+int gm_phase2_down_bf16(const void* bucket, const int32_t* expert_offset,
+                        const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr, int T,
+                        const void* down, float* y, void* stream);
+
+/* The accumulation tail of the phase-2 kernels (butterquant_kernels/moe.mojo:
+ * 252-290): out[t] = bf16(sum of y[route_pos[t][k]] over the token's local
+ * routes in ascending expert order, starting from 0). */
+int gm_combine(const int32_t* route_idx, const int32_t* route_pos, const float* y, int T,
+               void* out, void* stream);
+
+/* ------------------------------------------------------- weight producer --
+ * On-device restatement of the reference quantizer (quant/quantizer.mojo:
+ * 963-1051 do_quant with butterquant/kernels.mojo:148-168 rotate_and_quant),
+ * bit-identical to it: w bf16 [rows][cols] (* sqrt|gamma| if gamma != NULL),
+ * FWHT-`fwht_block` along K, per-row absmax int8 q [rows][cols] row-major,
+ * scale f32 [rows] = amax/127.  cols/block: 2816/128 or 704/64. */
+int gm_bq_quantize_rows(const void* w, long rows, int cols, const void* gamma, int fwht_block,
+                        int8_t* q, float* scale, void* stream);
+
+/* butterquant/vnni.mojo:31-83 pack (and its inverse). rows%32 == 0, cols%64 == 0. */
+int gm_vnni_pack(const int8_t* q, long rows, int cols, int8_t* packed, void* stream);
+int gm_vnni_unpack(const int8_t* packed, long rows, int cols, int8_t* q, void* stream);
+
+/* butterquant/kernels.mojo:218-224 router_center_softmax: out = bf16(W - mean_rows(W)). */
+int gm_router_center(const void* w, int rows, int cols, void* out, void* stream);
+
+/* butterquant/kernels.mojo:37-45 bake_split_gain_in_place (out may equal g). */
+int gm_bake_split_gain(const void* g, void* out, int n, void* stream);
+
+/* modeling/gemma4_topology.mojo:362-388 router scale bake: out = bf16(s/sqrt(2816)). */
+int gm_bake_router_scale(const void* s, void* out, int n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GMOE_H */

@@ -1,0 +1,174 @@
+// act_quant.cu -- activation preparation of the MoE block.
+//
+//  * bq_norm_quant: butterquant/runtime.mojo:11-37 prepare_norm_activation
+//    [per_block=False, block=128] as dispatched by
+//    butterquant_kernels/linear.mojo:58-82: v = x*inv_rms*gamma' (gamma' is the
+//    split-gain baked pre_feedforward_layernorm_2), FWHT-128 per block, one
+//    absmax over the whole row, int8 = clamp(roundeven(v*127/amax)), sa = amax.
+//  * block_quant: butterquant/runtime.mojo:62-79 prepare_block_activation
+//    [block=64, apply_fwht=True] (butterquant_kernels/linear.mojo:182-205) on
+//    the bf16 bucket: FWHT-64 then per-64-block absmax int8.
+//  * rms_norm_bf16: kernels/rmsnorm.mojo:21-47 bf16(x*inv_rms*gamma) for the
+//    bf16 expert path (modeling/gemma_4_moe.mojo:537-541).
+//
+// One warp per row.  For the 128-wide FWHT lane l holds elements 4l..4l+3 of
+// each block (butterfly strides 1,2 in registers, 4..64 across lanes); for the
+// 64-wide FWHT lane l holds 2l, 2l+1 (stride 1 in registers, 2..32 across).
+#include "gm_kernels.h"
+
+namespace gm {
+
+// FWHT-128 of the block held as v[0..3] = elements 4*lane+j.
+__device__ __forceinline__ void fwht128_lane4(float (&v)[4], int lane) {
+  float a, b;
+  a = v[0]; b = v[1]; v[0] = __fadd_rn(a, b); v[1] = __fsub_rn(a, b);
+  a = v[2]; b = v[3]; v[2] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
+  a = v[0]; b = v[2]; v[0] = __fadd_rn(a, b); v[2] = __fsub_rn(a, b);
+  a = v[1]; b = v[3]; v[1] = __fadd_rn(a, b); v[3] = __fsub_rn(a, b);
+#pragma unroll
+  for (int m = 1; m <= 16; m <<= 1)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = fwht_xor_stage(v[j], lane, m);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = __fmul_rn(v[j], fwht_scale_128());
+}
+
+// FWHT-64 of the block held as v[0..1] = elements 2*lane+j.
+__device__ __forceinline__ void fwht64_lane2(float& v0, float& v1, int lane) {
+  float a = v0, b = v1;
+  v0 = __fadd_rn(a, b);
+  v1 = __fsub_rn(a, b);
+#pragma unroll
+  for (int m = 1; m <= 16; m <<= 1) {
+    v0 = fwht_xor_stage(v0, lane, m);
+    v1 = fwht_xor_stage(v1, lane, m);
+  }
+  v0 = __fmul_rn(v0, fwht_scale_64());
+  v1 = __fmul_rn(v1, fwht_scale_64());
+}
+
+__global__ void __launch_bounds__(256)
+bq_norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, int T,
+                     int8_t* __restrict__ xi8, float* __restrict__ xsa) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  constexpr int NBLK = H / NORM_BLOCK;  // 22
+  const uint16_t* xr = x + (size_t)t * H;
+  float v[NBLK][4];
+  float ss = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    uint2 raw = *reinterpret_cast<const uint2*>(xr + b * NORM_BLOCK + 4 * lane);
+    v[b][0] = bf2f(raw.x & 0xFFFFu);
+    v[b][1] = bf2f(raw.x >> 16);
+    v[b][2] = bf2f(raw.y & 0xFFFFu);
+    v[b][3] = bf2f(raw.y >> 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[b][j], v[b][j]));
+  }
+  ss = warp_sum(ss);
+  const float inv = inv_rms_from_sumsq(ss);
+  float amax = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    uint2 g = *reinterpret_cast<const uint2*>(gamma + b * NORM_BLOCK + 4 * lane);
+    float gv[4] = {bf2f(g.x & 0xFFFFu), bf2f(g.x >> 16), bf2f(g.y & 0xFFFFu), bf2f(g.y >> 16)};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[b][j] = __fmul_rn(__fmul_rn(v[b][j], inv), gv[j]);
+    fwht128_lane4(v[b], lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) amax = fmaxf(amax, fabsf(v[b][j]));
+  }
+  amax = warp_max(amax);
+  const float qinv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+  int8_t* dst = xi8 + (size_t)t * H;
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) packed |= (uint32_t)(quantize_i8(v[b][j], qinv) & 0xFF) << (8 * j);
+    *reinterpret_cast<uint32_t*>(dst + b * NORM_BLOCK + 4 * lane) = packed;
+  }
+  if (lane == 0) xsa[t] = amax;
+}
+
+__global__ void __launch_bounds__(256)
+block_quant_kernel(const uint16_t* __restrict__ src, long rows, int8_t* __restrict__ qi8,
+                   float* __restrict__ sa) {
+  const int lane = threadIdx.x & 31;
+  const long r = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const uint16_t* row = src + r * I;
+#pragma unroll
+  for (int b = 0; b < NB_DOWN; ++b) {
+    uint32_t raw = *reinterpret_cast<const uint32_t*>(row + b * DOWN_BLOCK + 2 * lane);
+    float v0 = bf2f(raw & 0xFFFFu), v1 = bf2f(raw >> 16);
+    fwht64_lane2(v0, v1, lane);
+    float amax = warp_max(fmaxf(fabsf(v0), fabsf(v1)));
+    float qinv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    uint32_t q = (uint32_t)(quantize_i8(v0, qinv) & 0xFF) | ((uint32_t)(quantize_i8(v1, qinv) & 0xFF) << 8);
+    *reinterpret_cast<uint16_t*>(qi8 + r * I + b * DOWN_BLOCK + 2 * lane) = (uint16_t)q;
+    if (lane == 0) sa[r * NB_DOWN + b] = amax;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, int T,
+                     uint16_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  constexpr int NBLK = H / NORM_BLOCK;
+  const uint16_t* xr = x + (size_t)t * H;
+  float v[NBLK][4];
+  float ss = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    uint2 raw = *reinterpret_cast<const uint2*>(xr + b * NORM_BLOCK + 4 * lane);
+    v[b][0] = bf2f(raw.x & 0xFFFFu);
+    v[b][1] = bf2f(raw.x >> 16);
+    v[b][2] = bf2f(raw.y & 0xFFFFu);
+    v[b][3] = bf2f(raw.y >> 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[b][j], v[b][j]));
+  }
+  ss = warp_sum(ss);
+  const float inv = inv_rms_from_sumsq(ss);
+  uint16_t* dst = out + (size_t)t * H;
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    uint2 g = *reinterpret_cast<const uint2*>(gamma + b * NORM_BLOCK + 4 * lane);
+    float gv[4] = {bf2f(g.x & 0xFFFFu), bf2f(g.x >> 16), bf2f(g.y & 0xFFFFu), bf2f(g.y >> 16)};
+    uint16_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = f2bf(__fmul_rn(__fmul_rn(v[b][j], inv), gv[j]));
+    uint2 w;
+    w.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+    w.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+    *reinterpret_cast<uint2*>(dst + b * NORM_BLOCK + 4 * lane) = w;
+  }
+}
+
+cudaError_t launch_bq_norm_quant(const uint16_t* x, const uint16_t* gamma, int T, int8_t* xi8,
+                                 float* xsa, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  bq_norm_quant_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, gamma, T, xi8, xsa);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_block_quant(const uint16_t* bucket, long rows, int8_t* qi8, float* sa,
+                               cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  block_quant_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(bucket, rows, qi8, sa);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int T, uint16_t* out,
+                                 cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  rms_norm_bf16_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, gamma, T, out);
+  return cudaGetLastError();
+}
+
+}  // namespace gm

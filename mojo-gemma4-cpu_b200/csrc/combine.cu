@@ -1,0 +1,59 @@
+// combine.cu -- weighted combine of the per-route expert outputs.
+//
+// Reference: the phase-2 kernels accumulate acc[token] (zero-initialised f32)
+// over experts in ascending id order and store bf16(acc)
+// (butterquant_kernels/moe.mojo:252-290, kernels/moe_experts.mojo:255-314).
+// Here every route's contribution y[pos] = dot*sw*w already sits in f32, and
+// this kernel re-creates exactly that summation order per token: the token's
+// <=8 local routes are sorted by expert id and added left to right starting
+// from 0.0f, then rounded to bf16 with RNE (butterquant/convert.mojo:13-17).
+#include "gm_kernels.h"
+
+namespace gm {
+
+__global__ void __launch_bounds__(352)
+combine_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict__ route_pos,
+               const float* __restrict__ ybuf, int T, uint16_t* __restrict__ out) {
+  __shared__ int s_pos[TOPK];
+  __shared__ int s_n;
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int ex[TOPK], ps[TOPK], n = 0;
+    for (int k = 0; k < TOPK; ++k) {
+      const int p = route_pos[t * TOPK + k];
+      if (p < 0) continue;
+      const int e = route_idx[t * TOPK + k];
+      int m = n++;
+      while (m > 0 && ex[m - 1] > e) { ex[m] = ex[m - 1]; ps[m] = ps[m - 1]; --m; }
+      ex[m] = e;
+      ps[m] = p;
+    }
+    for (int k = 0; k < n; ++k) s_pos[k] = ps[k];
+    s_n = n;
+  }
+  __syncthreads();
+  const int n = s_n;
+  for (int c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int k = 0; k < n; ++k) {
+      const float4 y = *reinterpret_cast<const float4*>(ybuf + (size_t)s_pos[k] * H + c4 * 4);
+      acc.x = __fadd_rn(acc.x, y.x);
+      acc.y = __fadd_rn(acc.y, y.y);
+      acc.z = __fadd_rn(acc.z, y.z);
+      acc.w = __fadd_rn(acc.w, y.w);
+    }
+    uint2 o;
+    o.x = (uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16);
+    o.y = (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16);
+    *reinterpret_cast<uint2*>(out + (size_t)t * H + c4 * 4) = o;
+  }
+}
+
+cudaError_t launch_combine(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
+                           int T, uint16_t* out, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  combine_kernel<<<T, 352, 0, s>>>(route_idx, route_pos, ybuf, T, out);
+  return cudaGetLastError();
+}
+
+}  // namespace gm

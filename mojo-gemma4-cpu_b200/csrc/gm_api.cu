@@ -1,0 +1,478 @@
+// gm_api.cu -- the C ABI of include/gmoe.h: handle, weight registration, the
+// MoE operator and the per-stage entry points.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/gmoe.h"
+#include "gm_kernels.h"
+
+using namespace gm;
+
+namespace {
+
+thread_local std::string g_tls_error;
+
+struct Layer {
+  int kind = 0;  // 0 empty, 1 butterquant, 2 bf16
+  int8_t* gu_q = nullptr;      // bq: VNNI-packed [epr*GU][H]
+  float* gu_scale = nullptr;   // bq: [epr*GU]
+  int8_t* dn_q = nullptr;      // bq: VNNI-packed [epr*H][I]
+  float* dn_scale = nullptr;   // bq: [epr*H]
+  uint16_t* gu_bf16 = nullptr;  // bf16: [epr][GU][H]
+  uint16_t* dn_bf16 = nullptr;  // bf16: [epr][H][I]
+  uint16_t* router = nullptr;   // [E][H]
+  uint16_t* rscale = nullptr;   // [H]
+  uint16_t* pes = nullptr;      // [E]
+  uint16_t* gamma2 = nullptr;   // [H]
+};
+
+}  // namespace
+
+struct gm_moe {
+  int device = 0, max_tokens = 0, num_layers = 0, rank = 0, degree = 1;
+  int expert_base = 0, epr = E;
+  std::vector<Layer> layers;
+  std::string err;
+  // workspace (one allocation, carved)
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  float* logits = nullptr;
+  int32_t* route_idx = nullptr;
+  float* route_w = nullptr;
+  int32_t* route_pos = nullptr;
+  int32_t* expert_offset = nullptr;
+  int32_t* chunk_off = nullptr;
+  SparseRoute* routes = nullptr;
+  int8_t* x_i8 = nullptr;
+  float* x_sa = nullptr;
+  uint16_t* x_normed = nullptr;
+  uint16_t* bucket = nullptr;
+  int8_t* bucket_i8 = nullptr;
+  float* bucket_sa = nullptr;
+  float* ybuf = nullptr;
+  uint16_t* x_stage = nullptr;
+  uint16_t* out_stage = nullptr;
+  cudaStream_t own_stream = nullptr;
+};
+
+namespace {
+
+int set_err(gm_moe* h, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (h) h->err = buf;
+  g_tls_error = buf;
+  return code;
+}
+
+int cuda_check(gm_moe* h, cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return GM_OK;
+  return set_err(h, e == cudaErrorMemoryAllocation ? GM_ENOMEM : GM_ECUDA, "%s: %s", what,
+                 cudaGetErrorString(e));
+}
+
+#define GM_TRY(h, expr, what)                         \
+  do {                                                \
+    int _rc = cuda_check((h), (expr), (what));        \
+    if (_rc != GM_OK) return _rc;                     \
+  } while (0)
+
+inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct Carve {
+  size_t off = 0;
+  template <typename T>
+  size_t take(size_t count) {
+    off = align_up(off, 256);
+    size_t o = off;
+    off += count * sizeof(T);
+    return o;
+  }
+};
+
+struct WsLayout {
+  size_t logits, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
+      x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, total;
+};
+
+WsLayout ws_layout(int max_tokens) {
+  const size_t T = (size_t)max_tokens, R = T * TOPK;
+  Carve c;
+  WsLayout L;
+  L.logits = c.take<float>(T * E);
+  L.route_idx = c.take<int32_t>(R);
+  L.route_w = c.take<float>(R);
+  L.route_pos = c.take<int32_t>(R);
+  L.expert_offset = c.take<int32_t>(E + 1);
+  L.chunk_off = c.take<int32_t>(E + 1);
+  L.routes = c.take<SparseRoute>(R);
+  L.x_i8 = c.take<int8_t>(T * H);
+  L.x_sa = c.take<float>(T);
+  L.x_normed = c.take<uint16_t>(T * H);
+  L.bucket = c.take<uint16_t>(R * I);
+  L.bucket_i8 = c.take<int8_t>(R * I);
+  L.bucket_sa = c.take<float>(R * NB_DOWN);
+  L.ybuf = c.take<float>(R * H);
+  L.x_stage = c.take<uint16_t>(T * H);
+  L.out_stage = c.take<uint16_t>(T * H);
+  L.total = align_up(c.off, 256);
+  return L;
+}
+
+template <typename T>
+int dev_copy(gm_moe* h, T** dst, const void* src, size_t count, const char* what) {
+  if (!src) return set_err(h, GM_EINVAL, "%s: NULL pointer", what);
+  if (*dst) {
+    cudaFree(*dst);
+    *dst = nullptr;
+  }
+  GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(dst), count * sizeof(T)), what);
+  GM_TRY(h, cudaMemcpy(*dst, src, count * sizeof(T), cudaMemcpyDefault), what);
+  return GM_OK;
+}
+
+void free_layer(Layer& L) {
+  void* ptrs[] = {L.gu_q, L.gu_scale, L.dn_q, L.dn_scale, L.gu_bf16, L.dn_bf16,
+                  L.router, L.rscale, L.pes, L.gamma2};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  L = Layer{};
+}
+
+int check_layer(gm_moe* h, int layer) {
+  if (!h) return set_err(nullptr, GM_EINVAL, "NULL handle");
+  if (layer < 0 || layer >= h->num_layers)
+    return set_err(h, GM_EINVAL, "layer %d out of range [0,%d)", layer, h->num_layers);
+  return GM_OK;
+}
+
+bool is_device_ptr(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gm_version(void) { return "gmoe 0.1 (sm_100a)"; }
+
+const char* gm_last_error(const gm_moe_t* h) {
+  return h ? h->err.c_str() : g_tls_error.c_str();
+}
+
+size_t gm_moe_workspace_bytes(int max_tokens) {
+  return max_tokens > 0 ? ws_layout(max_tokens).total : 0;
+}
+
+int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, int rank,
+                  int degree) {
+  if (!out) return set_err(nullptr, GM_EINVAL, "gm_moe_create: NULL out");
+  *out = nullptr;
+  if (max_tokens <= 0 || num_layers <= 0)
+    return set_err(nullptr, GM_EINVAL, "gm_moe_create: max_tokens=%d num_layers=%d", max_tokens,
+                   num_layers);
+  if (degree < 1 || E % degree || rank < 0 || rank >= degree)
+    return set_err(nullptr, GM_EINVAL, "gm_moe_create: rank=%d degree=%d (degree must divide 128)",
+                   rank, degree);
+  if (cudaSetDevice(device) != cudaSuccess)
+    return set_err(nullptr, GM_ECUDA, "gm_moe_create: cudaSetDevice(%d) failed", device);
+  gm_moe* h = new gm_moe();
+  h->device = device;
+  h->max_tokens = max_tokens;
+  h->num_layers = num_layers;
+  h->rank = rank;
+  h->degree = degree;
+  h->epr = E / degree;
+  h->expert_base = rank * h->epr;
+  h->layers.resize(num_layers);
+  WsLayout L = ws_layout(max_tokens);
+  cudaError_t e = cudaMalloc(&h->ws, L.total);
+  if (e != cudaSuccess) {
+    int rc = set_err(nullptr, GM_ENOMEM, "gm_moe_create: workspace of %zu bytes: %s", L.total,
+                     cudaGetErrorString(e));
+    delete h;
+    return rc;
+  }
+  h->ws_bytes = L.total;
+  char* b = static_cast<char*>(h->ws);
+  h->logits = reinterpret_cast<float*>(b + L.logits);
+  h->route_idx = reinterpret_cast<int32_t*>(b + L.route_idx);
+  h->route_w = reinterpret_cast<float*>(b + L.route_w);
+  h->route_pos = reinterpret_cast<int32_t*>(b + L.route_pos);
+  h->expert_offset = reinterpret_cast<int32_t*>(b + L.expert_offset);
+  h->chunk_off = reinterpret_cast<int32_t*>(b + L.chunk_off);
+  h->routes = reinterpret_cast<SparseRoute*>(b + L.routes);
+  h->x_i8 = reinterpret_cast<int8_t*>(b + L.x_i8);
+  h->x_sa = reinterpret_cast<float*>(b + L.x_sa);
+  h->x_normed = reinterpret_cast<uint16_t*>(b + L.x_normed);
+  h->bucket = reinterpret_cast<uint16_t*>(b + L.bucket);
+  h->bucket_i8 = reinterpret_cast<int8_t*>(b + L.bucket_i8);
+  h->bucket_sa = reinterpret_cast<float*>(b + L.bucket_sa);
+  h->ybuf = reinterpret_cast<float*>(b + L.ybuf);
+  h->x_stage = reinterpret_cast<uint16_t*>(b + L.x_stage);
+  h->out_stage = reinterpret_cast<uint16_t*>(b + L.out_stage);
+  if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaFree(h->ws);
+    delete h;
+    return set_err(nullptr, GM_ECUDA, "gm_moe_create: stream creation failed");
+  }
+  *out = h;
+  return GM_OK;
+}
+
+int gm_moe_destroy(gm_moe_t* h) {
+  if (!h) return GM_OK;
+  cudaSetDevice(h->device);
+  for (auto& L : h->layers) free_layer(L);
+  if (h->ws) cudaFree(h->ws);
+  if (h->own_stream) cudaStreamDestroy(h->own_stream);
+  delete h;
+  return GM_OK;
+}
+
+int gm_moe_register_layer_bq(gm_moe_t* h, int layer, const void* gate_up,
+                             const float* gate_up_scale, const void* down,
+                             const float* down_scale, const void* router_centered,
+                             const void* router_scale, const void* per_expert_scale,
+                             const void* pre_ffn_norm_2) {
+  int rc = check_layer(h, layer);
+  if (rc) return rc;
+  GM_TRY(h, cudaSetDevice(h->device), "register_layer_bq");
+  Layer& L = h->layers[layer];
+  free_layer(L);
+  const size_t epr = (size_t)h->epr;
+  if ((rc = dev_copy(h, &L.gu_q, gate_up, epr * GU * H, "gate_up"))) return rc;
+  if ((rc = dev_copy(h, &L.gu_scale, gate_up_scale, epr * GU, "gate_up_scale"))) return rc;
+  if ((rc = dev_copy(h, &L.dn_q, down, epr * H * I, "down"))) return rc;
+  if ((rc = dev_copy(h, &L.dn_scale, down_scale, epr * H, "down_scale"))) return rc;
+  if ((rc = dev_copy(h, &L.router, router_centered, (size_t)E * H, "router_centered"))) return rc;
+  if ((rc = dev_copy(h, &L.rscale, router_scale, (size_t)H, "router_scale"))) return rc;
+  if ((rc = dev_copy(h, &L.pes, per_expert_scale, (size_t)E, "per_expert_scale"))) return rc;
+  if ((rc = dev_copy(h, &L.gamma2, pre_ffn_norm_2, (size_t)H, "pre_ffn_norm_2"))) return rc;
+  L.kind = 1;
+  return GM_OK;
+}
+
+int gm_moe_register_layer_bf16(gm_moe_t* h, int layer, const void* gate_up, const void* down,
+                               const void* router_proj, const void* router_scale,
+                               const void* per_expert_scale, const void* pre_ffn_norm_2) {
+  int rc = check_layer(h, layer);
+  if (rc) return rc;
+  GM_TRY(h, cudaSetDevice(h->device), "register_layer_bf16");
+  Layer& L = h->layers[layer];
+  free_layer(L);
+  const size_t epr = (size_t)h->epr;
+  if ((rc = dev_copy(h, &L.gu_bf16, gate_up, epr * GU * H, "gate_up"))) return rc;
+  if ((rc = dev_copy(h, &L.dn_bf16, down, epr * H * I, "down"))) return rc;
+  if ((rc = dev_copy(h, &L.router, router_proj, (size_t)E * H, "router_proj"))) return rc;
+  if ((rc = dev_copy(h, &L.rscale, router_scale, (size_t)H, "router_scale"))) return rc;
+  if ((rc = dev_copy(h, &L.pes, per_expert_scale, (size_t)E, "per_expert_scale"))) return rc;
+  if ((rc = dev_copy(h, &L.gamma2, pre_ffn_norm_2, (size_t)H, "pre_ffn_norm_2"))) return rc;
+  L.kind = 2;
+  return GM_OK;
+}
+
+int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void* stream) {
+  int rc = check_layer(h, layer);
+  if (rc) return rc;
+  const Layer& L = h->layers[layer];
+  if (L.kind == 0) return set_err(h, GM_ESTATE, "layer %d has no registered weights", layer);
+  if (T < 0 || T > h->max_tokens)
+    return set_err(h, GM_EINVAL, "T=%d outside [0, max_tokens=%d]", T, h->max_tokens);
+  if (T == 0) return GM_OK;
+  if (!x || !out) return set_err(h, GM_EINVAL, "NULL x/out");
+  cudaStream_t s = S(stream);
+  const uint16_t* xb = static_cast<const uint16_t*>(x);
+  GM_TRY(h, launch_router(xb, L.router, L.rscale, L.pes, T, h->logits, h->route_idx, h->route_w, s),
+         "router");
+  const int rc_chunk = L.kind == 1 ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
+  GM_TRY(h, launch_build_schedule(h->route_idx, h->route_w, T, h->expert_base, h->epr, rc_chunk,
+                                  h->expert_offset, h->routes, h->route_pos, h->chunk_off, s),
+         "build_schedules");
+  if (L.kind == 1) {
+    GM_TRY(h, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, s), "bq_norm_quant");
+    GM_TRY(h, launch_bq_phase1(h->x_i8, h->x_sa, h->expert_offset, h->routes, h->chunk_off, h->epr,
+                               T, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
+           "bq_phase1");
+    GM_TRY(h, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
+                               h->chunk_off, h->epr, T, L.dn_q, L.dn_scale, h->ybuf, s),
+           "bq_phase2");
+  } else {
+    GM_TRY(h, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, s), "rms_norm");
+    GM_TRY(h, launch_bf16_phase1(h->x_normed, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
+                                 L.gu_bf16, h->bucket, s),
+           "phase1_bf16");
+    GM_TRY(h, launch_bf16_phase2(h->bucket, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
+                                 L.dn_bf16, h->ybuf, s),
+           "phase2_bf16");
+  }
+  GM_TRY(h, launch_combine(h->route_idx, h->route_pos, h->ybuf, T, static_cast<uint16_t*>(out), s),
+         "combine");
+  return GM_OK;
+}
+
+int gm_moe_forward_sync(gm_moe_t* h, int layer, const void* x, void* out, int T) {
+  int rc = check_layer(h, layer);
+  if (rc) return rc;
+  if (T < 0 || T > h->max_tokens)
+    return set_err(h, GM_EINVAL, "T=%d outside [0, max_tokens=%d]", T, h->max_tokens);
+  if (T == 0) return GM_OK;
+  GM_TRY(h, cudaSetDevice(h->device), "forward_sync");
+  cudaStream_t s = h->own_stream;
+  const size_t bytes = (size_t)T * H * sizeof(uint16_t);
+  const bool x_dev = is_device_ptr(x), o_dev = is_device_ptr(out);
+  const void* xd = x;
+  if (!x_dev) {
+    GM_TRY(h, cudaMemcpyAsync(h->x_stage, x, bytes, cudaMemcpyHostToDevice, s), "stage x");
+    xd = h->x_stage;
+  }
+  void* od = o_dev ? out : h->out_stage;
+  if ((rc = gm_moe_forward(h, layer, xd, od, T, s))) return rc;
+  if (!o_dev) GM_TRY(h, cudaMemcpyAsync(out, od, bytes, cudaMemcpyDeviceToHost, s), "stage out");
+  GM_TRY(h, cudaStreamSynchronize(s), "forward_sync");
+  return GM_OK;
+}
+
+// ------------------------------------------------------------ per-stage
+#define STAGE(expr, what)                                            \
+  do {                                                               \
+    cudaError_t _e = (expr);                                         \
+    if (_e != cudaSuccess) return cuda_check(nullptr, _e, (what));   \
+    return GM_OK;                                                    \
+  } while (0)
+
+int gm_router_select(const void* x, const void* router_w, const void* router_scale,
+                     const void* per_expert_scale, int T, float* logits_ws, int32_t* route_idx,
+                     float* route_w, void* stream) {
+  if (T < 0) return set_err(nullptr, GM_EINVAL, "router_select: T=%d", T);
+  STAGE(launch_router(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(router_w),
+                      static_cast<const uint16_t*>(router_scale),
+                      static_cast<const uint16_t*>(per_expert_scale), T, logits_ws, route_idx,
+                      route_w, S(stream)),
+        "router_select");
+}
+
+int gm_build_expert_schedules(const int32_t* route_idx, const float* route_w, int T,
+                              int expert_base, int epr, int route_chunk, int32_t* expert_offset,
+                              gm_sparse_route_t* routes, int32_t* route_pos, int32_t* chunk_off,
+                              void* stream) {
+  if (T < 0 || epr < 1 || epr > E || route_chunk < 1)
+    return set_err(nullptr, GM_EINVAL, "build_expert_schedules: T=%d epr=%d route_chunk=%d", T, epr,
+                   route_chunk);
+  STAGE(launch_build_schedule(route_idx, route_w, T, expert_base, epr, route_chunk, expert_offset,
+                              reinterpret_cast<SparseRoute*>(routes), route_pos, chunk_off,
+                              S(stream)),
+        "build_expert_schedules");
+}
+
+int gm_rms_norm(const void* x, const void* gamma, int T, void* out, void* stream) {
+  STAGE(launch_rms_norm_bf16(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gamma),
+                             T, static_cast<uint16_t*>(out), S(stream)),
+        "rms_norm");
+}
+
+int gm_bq_norm_quant(const void* x, const void* gamma, int T, int8_t* x_i8, float* x_sa,
+                     void* stream) {
+  STAGE(launch_bq_norm_quant(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gamma),
+                             T, x_i8, x_sa, S(stream)),
+        "bq_norm_quant");
+}
+
+int gm_bq_phase1_gate_up(const int8_t* x_i8, const float* x_sa, const int32_t* expert_offset,
+                         const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr, int T,
+                         const void* gate_up, const float* gate_up_scale, int8_t* bucket_i8,
+                         float* bucket_sa, void* bucket_bf16, void* stream) {
+  if (epr < 1 || epr > E || T < 0) return set_err(nullptr, GM_EINVAL, "bq_phase1: epr=%d T=%d", epr, T);
+  STAGE(launch_bq_phase1(x_i8, x_sa, expert_offset, reinterpret_cast<const SparseRoute*>(routes),
+                         chunk_off, epr, T, static_cast<const int8_t*>(gate_up), gate_up_scale,
+                         bucket_i8, bucket_sa, static_cast<uint16_t*>(bucket_bf16), S(stream)),
+        "bq_phase1_gate_up");
+}
+
+int gm_bq_block_quant(const void* bucket, long rows, int8_t* q, float* sa, void* stream) {
+  STAGE(launch_block_quant(static_cast<const uint16_t*>(bucket), rows, q, sa, S(stream)),
+        "bq_block_quant");
+}
+
+int gm_bq_phase2_down(const int8_t* bucket_i8, const float* bucket_sa, const int32_t* expert_offset,
+                      const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr, int T,
+                      const void* down, const float* down_scale, float* y, void* stream) {
+  if (epr < 1 || epr > E || T < 0) return set_err(nullptr, GM_EINVAL, "bq_phase2: epr=%d T=%d", epr, T);
+  STAGE(launch_bq_phase2(bucket_i8, bucket_sa, expert_offset,
+                         reinterpret_cast<const SparseRoute*>(routes), chunk_off, epr, T,
+                         static_cast<const int8_t*>(down), down_scale, y, S(stream)),
+        "bq_phase2_down");
+}
+
+int gm_phase1_gate_up_bf16(const void* x_normed, const int32_t* expert_offset,
+                           const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr,
+                           int T, const void* gate_up, void* bucket, void* stream) {
+  if (epr < 1 || epr > E || T < 0) return set_err(nullptr, GM_EINVAL, "phase1_bf16: epr=%d T=%d", epr, T);
+  STAGE(launch_bf16_phase1(static_cast<const uint16_t*>(x_normed), expert_offset,
+                           reinterpret_cast<const SparseRoute*>(routes), chunk_off, epr, T,
+                           static_cast<const uint16_t*>(gate_up), static_cast<uint16_t*>(bucket),
+                           S(stream)),
+        "phase1_gate_up_bf16");
+}
+
+int gm_phase2_down_bf16(const void* bucket, const int32_t* expert_offset,
+                        const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr, int T,
+                        const void* down, float* y, void* stream) {
+  if (epr < 1 || epr > E || T < 0) return set_err(nullptr, GM_EINVAL, "phase2_bf16: epr=%d T=%d", epr, T);
+  STAGE(launch_bf16_phase2(static_cast<const uint16_t*>(bucket), expert_offset,
+                           reinterpret_cast<const SparseRoute*>(routes), chunk_off, epr, T,
+                           static_cast<const uint16_t*>(down), y, S(stream)),
+        "phase2_down_bf16");
+}
+
+int gm_combine(const int32_t* route_idx, const int32_t* route_pos, const float* y, int T,
+               void* out, void* stream) {
+  STAGE(launch_combine(route_idx, route_pos, y, T, static_cast<uint16_t*>(out), S(stream)),
+        "combine");
+}
+
+int gm_bq_quantize_rows(const void* w, long rows, int cols, const void* gamma, int fwht_block,
+                        int8_t* q, float* scale, void* stream) {
+  STAGE(launch_quantize_rows(static_cast<const uint16_t*>(w), rows, cols,
+                             static_cast<const uint16_t*>(gamma), fwht_block, q, scale, S(stream)),
+        "bq_quantize_rows");
+}
+
+int gm_vnni_pack(const int8_t* q, long rows, int cols, int8_t* packed, void* stream) {
+  STAGE(launch_vnni_permute(q, rows, cols, packed, 0, S(stream)), "vnni_pack");
+}
+
+int gm_vnni_unpack(const int8_t* packed, long rows, int cols, int8_t* q, void* stream) {
+  STAGE(launch_vnni_permute(packed, rows, cols, q, 1, S(stream)), "vnni_unpack");
+}
+
+int gm_router_center(const void* w, int rows, int cols, void* out, void* stream) {
+  STAGE(launch_router_center(static_cast<const uint16_t*>(w), rows, cols,
+                             static_cast<uint16_t*>(out), S(stream)),
+        "router_center");
+}
+
+int gm_bake_split_gain(const void* g, void* out, int n, void* stream) {
+  STAGE(launch_bake(static_cast<const uint16_t*>(g), static_cast<uint16_t*>(out), n, 0, S(stream)),
+        "bake_split_gain");
+}
+
+int gm_bake_router_scale(const void* s, void* out, int n, void* stream) {
+  STAGE(launch_bake(static_cast<const uint16_t*>(s), static_cast<uint16_t*>(out), n, 1, S(stream)),
+        "bake_router_scale");
+}
+
+}  // extern "C"

@@ -1,0 +1,48 @@
+// gm_kernels.h -- internal launchers of the MoE block kernels (not the C ABI;
+// the public boundary is include/gmoe.h).
+#pragma once
+#include <algorithm>
+#include "gm_common.cuh"
+
+namespace gm {
+
+int max_route_chunks(int T, int epr, int rc);
+
+cudaError_t launch_router(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
+                          const uint16_t* pes, int T, float* logits, int32_t* route_idx,
+                          float* route_w, cudaStream_t s);
+cudaError_t launch_build_schedule(const int32_t* route_idx, const float* route_w, int T,
+                                  int expert_base, int epr, int route_chunk,
+                                  int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
+                                  int32_t* chunk_off, cudaStream_t s);
+cudaError_t launch_bq_norm_quant(const uint16_t* x, const uint16_t* gamma, int T, int8_t* xi8,
+                                 float* xsa, cudaStream_t s);
+cudaError_t launch_block_quant(const uint16_t* bucket, long rows, int8_t* qi8, float* sa,
+                               cudaStream_t s);
+cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int T, uint16_t* out,
+                                 cudaStream_t s);
+cudaError_t launch_bq_phase1(const int8_t* xi8, const float* xsa, const int32_t* expert_offset,
+                             const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
+                             const int8_t* w_gu, const float* gu_scale, int8_t* bucket_i8,
+                             float* bucket_sa, uint16_t* bucket_bf16, cudaStream_t s);
+cudaError_t launch_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t* expert_offset,
+                             const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
+                             const int8_t* w_dn, const float* dn_scale, float* ybuf,
+                             cudaStream_t s);
+cudaError_t launch_bf16_phase1(const uint16_t* xn, const int32_t* expert_offset,
+                               const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
+                               const uint16_t* w_gu, uint16_t* bucket, cudaStream_t s);
+cudaError_t launch_bf16_phase2(const uint16_t* bucket, const int32_t* expert_offset,
+                               const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
+                               const uint16_t* w_dn, float* ybuf, cudaStream_t s);
+cudaError_t launch_combine(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
+                           int T, uint16_t* out, cudaStream_t s);
+cudaError_t launch_quantize_rows(const uint16_t* w, long rows, int cols, const uint16_t* gamma,
+                                 int block, int8_t* q, float* scale, cudaStream_t s);
+cudaError_t launch_vnni_permute(const int8_t* src, long rows, int cols, int8_t* dst, int dir,
+                                cudaStream_t s);
+cudaError_t launch_router_center(const uint16_t* w, int rows, int cols, uint16_t* out,
+                                 cudaStream_t s);
+cudaError_t launch_bake(const uint16_t* in, uint16_t* out, int n, int kind, cudaStream_t s);
+
+}  // namespace gm

@@ -1,0 +1,129 @@
+// schedule.cu -- token-to-expert dispatch schedule.
+//
+// Reference: kernels/moe_router.mojo:72-101 (BuildScheduleKernel): histogram of
+// the routes that fall in this rank's expert range, exclusive prefix sum into
+// expert_offset[epr+1], then a STABLE permute (token-major, then slot k) of
+// SparseRoute{token, weight} records into per-expert segments.
+//
+// B200 shape: one 1024-thread CTA.  The histogram uses shared-memory atomics;
+// the stable rank of a route inside its expert segment is computed per
+// 1024-token chunk from per-expert token bitmasks (popcount of the bits below
+// the token), so the output order is exactly the reference's sequential order.
+// Extra outputs for the GPU pipeline: route_pos[t*8+k] (segment position of
+// each route, -1 if the expert is not local) and chunk_off[epr+1] (prefix of
+// ceil(n_e / route_chunk), the work decomposition of the expert kernels).
+#include "gm_kernels.h"
+
+namespace gm {
+
+__global__ void __launch_bounds__(1024)
+build_schedule_kernel(const int32_t* __restrict__ route_idx, const float* __restrict__ route_w,
+                      int T, int expert_base, int epr, int route_chunk,
+                      int32_t* __restrict__ expert_offset, SparseRoute* __restrict__ routes,
+                      int32_t* __restrict__ route_pos, int32_t* __restrict__ chunk_off) {
+  __shared__ int cnt[E];
+  __shared__ int base[E];
+  __shared__ uint32_t mask[E][32];
+  __shared__ int wpre[E][33];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E; e += 1024) cnt[e] = 0;
+  __syncthreads();
+  const int R = T * TOPK;
+  for (int i = tid; i < R; i += 1024) {
+    int e = route_idx[i] - expert_base;
+    if (e >= 0 && e < epr) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (tid < 32) {
+    // warp-level exclusive scans over <=128 experts (4 per lane)
+    int c[4], cc[4];
+    int s = 0, sc = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int e = tid * 4 + j;
+      c[j] = e < epr ? cnt[e] : 0;
+      cc[j] = e < epr ? (c[j] + route_chunk - 1) / route_chunk : 0;
+      s += c[j];
+      sc += cc[j];
+    }
+    int inc = s, incc = sc;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      int o = __shfl_up_sync(0xffffffffu, inc, m);
+      int oc = __shfl_up_sync(0xffffffffu, incc, m);
+      if (tid >= m) { inc += o; incc += oc; }
+    }
+    int run = inc - s, crun = incc - sc;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int e = tid * 4 + j;
+      if (e < epr) {
+        expert_offset[e] = run;
+        base[e] = run;
+        chunk_off[e] = crun;
+      }
+      run += c[j];
+      crun += cc[j];
+    }
+    if (tid == 31) {
+      expert_offset[epr] = run;
+      chunk_off[epr] = crun;
+    }
+  }
+  __syncthreads();
+
+  for (int c0 = 0; c0 < T; c0 += 1024) {
+    for (int i = tid; i < epr * 32; i += 1024) mask[i >> 5][i & 31] = 0u;
+    __syncthreads();
+    const int t = c0 + tid;
+    int le[TOPK];
+#pragma unroll
+    for (int k = 0; k < TOPK; ++k) {
+      le[k] = -1;
+      if (t < T) {
+        int e = route_idx[t * TOPK + k] - expert_base;
+        if (e >= 0 && e < epr) {
+          le[k] = e;
+          atomicOr(&mask[e][tid >> 5], 1u << (tid & 31));
+        }
+      }
+    }
+    __syncthreads();
+    if (tid < epr) {
+      int s = 0;
+      for (int w = 0; w < 32; ++w) {
+        wpre[tid][w] = s;
+        s += __popc(mask[tid][w]);
+      }
+      wpre[tid][32] = s;
+    }
+    __syncthreads();
+    if (t < T) {
+#pragma unroll
+      for (int k = 0; k < TOPK; ++k) {
+        int pos = -1;
+        int e = le[k];
+        if (e >= 0) {
+          pos = base[e] + wpre[e][tid >> 5] +
+                __popc(mask[e][tid >> 5] & ((1u << (tid & 31)) - 1u));
+          routes[pos] = SparseRoute{t, route_w[t * TOPK + k]};
+        }
+        route_pos[t * TOPK + k] = pos;
+      }
+    }
+    __syncthreads();
+    if (tid < epr) base[tid] += wpre[tid][32];
+    __syncthreads();
+  }
+}
+
+cudaError_t launch_build_schedule(const int32_t* route_idx, const float* route_w, int T,
+                                  int expert_base, int epr, int route_chunk,
+                                  int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
+                                  int32_t* chunk_off, cudaStream_t s) {
+  build_schedule_kernel<<<1, 1024, 0, s>>>(route_idx, route_w, T, expert_base, epr, route_chunk,
+                                           expert_offset, routes, route_pos, chunk_off);
+  return cudaGetLastError();
+}
+
+}  // namespace gm

@@ -1,0 +1,158 @@
+"""Python binding of libgmoe.so (include/gmoe.h) over ctypes.
+
+Host-side mirror of the reference's MoE operator (dispatch_bq_moe,
+modeling/gemma_4_moe_bq.mojo:630-713; dispatch_moe, modeling/gemma_4_moe.mojo:
+493-566): `MoeBlock.forward(layer, x, out, T)` with the reference's argument
+meaning (x_input -> moe_out, seq_len tokens).  Device buffers are passed as raw
+addresses (torch tensors' data_ptr(), or any integer address); torch is only
+the allocator used by tests and the benchmark, never a compute path here.
+
+The library is required: importing this module on a machine without
+libgmoe.so raises, and every call that returns a non-zero status raises
+GmoeError with the library's error text.  There is no fallback path.
+"""
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgmoe.so")
+
+HIDDEN, NUM_EXPERTS, TOP_K, INTERMEDIATE, GATE_UP, DOWN_BLOCK = 2816, 128, 8, 704, 1408, 64
+NB_DOWN = INTERMEDIATE // DOWN_BLOCK
+ROUTE_CHUNK_BQ, ROUTE_CHUNK_BF16 = 16, 8
+
+STATUS = {0: "GM_OK", -1: "GM_EINVAL", -2: "GM_ECUDA", -3: "GM_ENOMEM", -4: "GM_ENCCL",
+          -5: "GM_ETIMEOUT", -6: "GM_ESTATE"}
+
+# Every symbol include/gmoe.h declares, with its ctypes signature.
+_vp, _i32, _i64, _sz = C.c_void_p, C.c_int, C.c_long, C.c_size_t
+SIGNATURES = {
+    "gm_version": (C.c_char_p, []),
+    "gm_last_error": (C.c_char_p, [_vp]),
+    "gm_moe_create": (_i32, [C.POINTER(_vp), _i32, _i32, _i32, _i32, _i32]),
+    "gm_moe_destroy": (_i32, [_vp]),
+    "gm_moe_workspace_bytes": (_sz, [_i32]),
+    "gm_moe_register_layer_bq": (_i32, [_vp, _i32] + [_vp] * 8),
+    "gm_moe_register_layer_bf16": (_i32, [_vp, _i32] + [_vp] * 6),
+    "gm_moe_forward": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp]),
+    "gm_moe_forward_sync": (_i32, [_vp, _i32, _vp, _vp, _i32]),
+    "gm_router_select": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "gm_build_expert_schedules": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "gm_rms_norm": (_i32, [_vp, _vp, _i32, _vp, _vp]),
+    "gm_bq_norm_quant": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
+    "gm_bq_phase1_gate_up": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "gm_bq_block_quant": (_i32, [_vp, _i64, _vp, _vp, _vp]),
+    "gm_bq_phase2_down": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "gm_phase1_gate_up_bf16": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp]),
+    "gm_phase2_down_bf16": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp]),
+    "gm_combine": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
+    "gm_bq_quantize_rows": (_i32, [_vp, _i64, _i32, _vp, _i32, _vp, _vp, _vp]),
+    "gm_vnni_pack": (_i32, [_vp, _i64, _i32, _vp, _vp]),
+    "gm_vnni_unpack": (_i32, [_vp, _i64, _i32, _vp, _vp]),
+    "gm_router_center": (_i32, [_vp, _i32, _i32, _vp, _vp]),
+    "gm_bake_split_gain": (_i32, [_vp, _vp, _i32, _vp]),
+    "gm_bake_router_scale": (_i32, [_vp, _vp, _i32, _vp]),
+}
+
+
+class GmoeError(RuntimeError):
+    pass
+
+
+_LIB = None
+
+
+def lib():
+    """Load libgmoe.so (raises if it has not been built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise GmoeError("libgmoe.so not built at %s (run __graft_entry__.build())" % LIB_PATH)
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def _addr(t):
+    """Raw address of a tensor-like (torch tensor, numpy array, int, None)."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    if hasattr(t, "ctypes"):
+        return t.ctypes.data
+    raise TypeError("cannot take the address of %r" % type(t))
+
+
+def _stream(s):
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return s.cuda_stream  # torch.cuda.Stream
+
+
+def check(rc, handle=None):
+    if rc != 0:
+        msg = lib().gm_last_error(handle)
+        raise GmoeError("%s: %s" % (STATUS.get(rc, rc), msg.decode() if msg else ""))
+    return rc
+
+
+def call(name, *args):
+    """Call a stateless entry point; addresses/streams are converted."""
+    fn = getattr(lib(), name)
+    conv = []
+    for a, ty in zip(args, fn.argtypes):
+        conv.append(_addr(a) if ty is _vp else a)
+    return check(fn(*conv))
+
+
+class MoeBlock:
+    """A gm_moe_t handle: weights of `num_layers` MoE blocks plus workspace for
+    `max_tokens` tokens per call, expert shard `rank` of `degree`."""
+
+    def __init__(self, max_tokens, num_layers=1, device=0, rank=0, degree=1):
+        h = C.c_void_p()
+        check(lib().gm_moe_create(C.byref(h), device, max_tokens, num_layers, rank, degree))
+        self.h = h
+        self.max_tokens, self.num_layers, self.rank, self.degree = max_tokens, num_layers, rank, degree
+        self.epr = NUM_EXPERTS // degree
+
+    def close(self):
+        if self.h:
+            lib().gm_moe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def register_bq(self, layer, gate_up, gate_up_scale, down, down_scale, router_centered,
+                    router_scale, per_expert_scale, pre_ffn_norm_2):
+        check(lib().gm_moe_register_layer_bq(
+            self.h, layer, _addr(gate_up), _addr(gate_up_scale), _addr(down), _addr(down_scale),
+            _addr(router_centered), _addr(router_scale), _addr(per_expert_scale),
+            _addr(pre_ffn_norm_2)), self.h)
+
+    def register_bf16(self, layer, gate_up, down, router_proj, router_scale, per_expert_scale,
+                      pre_ffn_norm_2):
+        check(lib().gm_moe_register_layer_bf16(
+            self.h, layer, _addr(gate_up), _addr(down), _addr(router_proj), _addr(router_scale),
+            _addr(per_expert_scale), _addr(pre_ffn_norm_2)), self.h)
+
+    def forward(self, layer, x, out, T, stream=None):
+        """Asynchronous on `stream`: x, out device bf16 [T][2816]."""
+        check(lib().gm_moe_forward(self.h, layer, _addr(x), _addr(out), T, _stream(stream)), self.h)
+
+    def forward_sync(self, layer, x, out, T):
+        """Blocking; x/out may be host (e.g. pinned) or device buffers."""
+        check(lib().gm_moe_forward_sync(self.h, layer, _addr(x), _addr(out), T), self.h)

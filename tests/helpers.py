@@ -1,0 +1,81 @@
+"""Shared test helpers: seeded raw layers and the oracle-side preparation of
+the butterquant / bf16 layer (the checker's own copy of every tensor)."""
+import numpy as np
+
+from oracle import oracle as O
+
+H, E, I, GU = O.H, O.E, O.I, O.GU
+
+
+def raw_layer_np(seed=1234, weight_std=0.02, router_std=0.02, stress=False):
+    """Seeded raw bf16 layer as uint16 numpy arrays (host)."""
+    rng = np.random.default_rng(seed)
+
+    def normal(shape, std=1.0, mean=0.0):
+        a = rng.standard_normal(size=shape, dtype=np.float32)
+        a *= np.float32(std)
+        a += np.float32(mean)
+        return O.f32_to_bf16(a)
+
+    L = {
+        "router_proj": normal((E, H), router_std),
+        "gate_up": normal((E, GU, H), weight_std),
+        "down": normal((E, H, I), weight_std),
+    }
+    if stress:
+        L["router_scale"] = normal((H,), 0.25, 1.0)
+        L["per_expert_scale"] = normal((E,), 0.25, 1.0)
+        L["pre_ffn_norm_2"] = normal((H,), 0.25, 1.0)
+    else:
+        one = O.f32_to_bf16(np.ones(1, np.float32))[0]
+        L["router_scale"] = np.full(H, one, np.uint16)
+        L["per_expert_scale"] = np.full(E, one, np.uint16)
+        L["pre_ffn_norm_2"] = np.full(H, one, np.uint16)
+    return L
+
+
+def tokens_np(T, seed=99, std=1.0):
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal(size=(T, H), dtype=np.float32) * np.float32(std)
+    return O.f32_to_bf16(a)
+
+
+def oracle_bq_layer(raw):
+    """Quantize/pack/bake exactly as the reference quantizer + model_init."""
+    gu_q, gu_s = O.quantize_rows(raw["gate_up"].reshape(E * GU, H), 128, raw["pre_ffn_norm_2"])
+    dn_q, dn_s = O.quantize_rows(raw["down"].reshape(E * H, I), 64)
+    return {
+        "router_centered": O.router_center(raw["router_proj"]),
+        "router_scale": O.bake_router_scale(raw["router_scale"]),
+        "pes": raw["per_expert_scale"],
+        "gamma2": O.bake_split_gain(raw["pre_ffn_norm_2"]),
+        "gu_q": gu_q, "gu_scale": gu_s, "gu_cs": O.colsum(gu_q, H, True).reshape(-1),
+        "dn_q": dn_q, "dn_scale": dn_s, "dn_cs": O.colsum(dn_q, 64, False),
+    }
+
+
+def oracle_bf16_layer(raw):
+    return {
+        "router_proj": raw["router_proj"],
+        "router_scale": O.bake_router_scale(raw["router_scale"]),
+        "pes": raw["per_expert_scale"],
+        "gamma2": raw["pre_ffn_norm_2"],
+        "w_gu": raw["gate_up"],
+        "w_dn": raw["down"],
+    }
+
+
+def topk_margin(logits):
+    """Gap between the 8th and 9th largest logit per token."""
+    s = -np.sort(-logits, axis=1)
+    return s[:, 7] - s[:, 8]
+
+
+def rel_err(out_u16, ref_u16, rows=None):
+    o = O.bf16_to_f32(out_u16).astype(np.float64)
+    r = O.bf16_to_f32(ref_u16).astype(np.float64)
+    if rows is not None:
+        o, r = o[rows], r[rows]
+    if r.size == 0:
+        return 0.0
+    return float(np.abs(o - r).max() / max(np.abs(r).max(), 1e-30))

@@ -1,0 +1,56 @@
+"""The C-ABI library loads and exports every entry point include/gmoe.h
+declares (CPU only: no compute calls)."""
+import ctypes
+import os
+import re
+
+import gmoe
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gmoe.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(gm_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_expected_surface():
+    names = declared_functions()
+    for must in ("gm_moe_create", "gm_moe_forward", "gm_moe_forward_sync", "gm_router_select",
+                 "gm_build_expert_schedules", "gm_bq_phase1_gate_up", "gm_bq_phase2_down",
+                 "gm_combine"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(gmoe.LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    assert set(declared_functions()) == set(gmoe.SIGNATURES)
+
+
+def test_version_and_error_text_without_gpu():
+    L = gmoe.lib()
+    assert b"sm_100a" in L.gm_version()
+    assert L.gm_last_error(None) is not None
+
+
+def test_create_rejects_bad_arguments():
+    L = gmoe.lib()
+    h = ctypes.c_void_p()
+    assert L.gm_moe_create(ctypes.byref(h), 0, 0, 1, 0, 1) == -1          # max_tokens
+    assert L.gm_moe_create(ctypes.byref(h), 0, 16, 1, 0, 3) == -1         # degree ∤ 128
+    assert L.gm_moe_create(ctypes.byref(h), 0, 16, 1, 2, 2) == -1         # rank >= degree
+    assert b"degree" in L.gm_last_error(None)
+
+
+def test_workspace_size_grows_with_tokens():
+    L = gmoe.lib()
+    a, b = L.gm_moe_workspace_bytes(16), L.gm_moe_workspace_bytes(1024)
+    assert 0 < a < b
+    assert L.gm_moe_workspace_bytes(0) == 0

@@ -1,0 +1,221 @@
+"""CPU self-checks of the oracle (the reference restatement used as checker).
+
+The reference has no golden vectors for its MoE path, so these pin the
+oracle against mathematics and against independent numpy restatements:
+FWHT orthonormality, the quantizer's spec identities
+(quantization_docs/butterquant.md 1.1-1.4, 2.4-2.5), the VNNI layout
+formula, the router against softmax->argsort->renorm on the same logits, the
+router-merge invariant of benchmarks/benchmark_router_merge.mojo:120-135, and
+the stable schedule order of kernels/moe_router.mojo:72-101."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from helpers import raw_layer_np, tokens_np, oracle_bq_layer, oracle_bf16_layer, rel_err, topk_margin
+
+H, E, I, GU, TOPK = O.H, O.E, O.I, O.GU, O.TOPK
+
+
+def sylvester(n):
+    m = np.array([[1.0]])
+    while m.shape[0] < n:
+        m = np.block([[m, m], [m, -m]])
+    return m
+
+
+@pytest.mark.parametrize("block", [64, 128])
+def test_fwht_matches_hadamard_and_is_involution(block):
+    rng = np.random.default_rng(0)
+    v = rng.standard_normal((5, 3 * block)).astype(np.float32)
+    w = O.fwht_rows(v, block)
+    Hm = sylvester(block) / np.sqrt(block)
+    ref = np.concatenate([v[:, b * block:(b + 1) * block] @ Hm.T for b in range(3)], axis=1)
+    assert np.abs(w - ref).max() < 1e-5
+    assert np.abs(O.fwht_rows(w, block) - v).max() < 1e-5
+
+
+def test_fast_exp_error_profile():
+    L = O.lib()
+    xs = np.linspace(-30, 0, 2001)
+    sm = np.array([L.orc_fast_exp_softmax_biased(float(x)) for x in xs])
+    rel = (sm - np.exp(xs)) / np.exp(xs)
+    # simd_math/exponential.mojo:161-170: undershooting, max rel error ~6.88e-3
+    assert rel.max() <= 1e-6 and rel.min() > -7.5e-3
+    xf = np.linspace(-20, 0, 2001)
+    ef = np.array([L.orc_exp_f32_fast(float(x)) for x in xf])
+    assert np.abs(ef / np.exp(xf) - 1).max() < 4e-3   # simd_math/ops.mojo:76 "~0.3%"
+
+
+def test_gelu_tanh_close_to_exact():
+    L = O.lib()
+    xs = np.linspace(-8, 8, 801)
+    got = np.array([L.orc_gelu_tanh(float(x)) for x in xs])
+    exact = 0.5 * xs * (1 + np.tanh(np.sqrt(2 / np.pi) * (xs + 0.044715 * xs ** 3)))
+    assert np.abs(got - exact).max() < 1e-2
+
+
+def test_bf16_rne():
+    vals = np.array([1.0, 1.00390625, 1.0078125, 3.14159, -2.5e-3, 65504.0], np.float32)
+    b = O.f32_to_bf16(vals)
+    for v, bb in zip(vals, b):
+        assert O.lib().orc_f2bf(float(v)) == bb
+    # ties to even: 1 + 2^-8 lies halfway between 1 and 1+2^-7 -> 1
+    assert O.bf16_to_f32(O.f32_to_bf16(np.array([1.00390625], np.float32)))[0] == 1.0
+
+
+@pytest.mark.parametrize("block,gamma", [(128, True), (64, False)])
+def test_quantizer_spec_identities(block, gamma):
+    rng = np.random.default_rng(1)
+    cols = H if block == 128 else I
+    w = O.f32_to_bf16(rng.standard_normal((64, cols)).astype(np.float32) * 0.02)
+    g = O.f32_to_bf16(rng.standard_normal(cols).astype(np.float32) * 0.25 + 1.0) if gamma else None
+    q, s = O.quantize_rows(w, block, g)
+    wf = O.bf16_to_f32(w).reshape(64, cols)
+    if gamma:
+        wf = wf * np.sqrt(np.abs(O.bf16_to_f32(g)))
+    rot = O.fwht_rows(wf, block)
+    amax = np.abs(rot).max(axis=1)
+    # scale stored pre-divided by 127 (butterquant.md 2.4)
+    assert np.allclose(s, amax / 127, rtol=1e-6)
+    assert q.min() >= -128 and q.max() <= 127
+    # reconstruction error <= S/254 (butterquant.md 1.2), plus f32 slack
+    err = np.abs(q * s[:, None] - rot)
+    assert (err <= (amax / 254)[:, None] * 1.0001 + 1e-9).all()
+    # the absmax element maps to +-127
+    assert (np.abs(q).max(axis=1) == 127).all()
+
+
+def test_vnni_layout_formula_and_roundtrip():
+    rng = np.random.default_rng(2)
+    q = rng.integers(-128, 128, size=(96, 192), dtype=np.int8)
+    p = O.vnni_pack(q)
+    # offset = t*32*K + ks*2048 + half*1024 + (k%64//4)*64 + n*4 + k%4
+    ref = q.reshape(3, 2, 16, 3, 16, 4).transpose(0, 3, 1, 4, 2, 5).reshape(96, 192)
+    assert np.array_equal(p.reshape(-1), ref.reshape(-1))
+    assert np.array_equal(O.vnni_unpack(p, 96, 192), q)
+
+
+def test_colsum_layouts():
+    rng = np.random.default_rng(3)
+    q = rng.integers(-128, 128, size=(64, 704), dtype=np.int8)
+    rm = O.colsum(q, 64, True)
+    bm = O.colsum(q, 64, False)
+    ref = q.reshape(64, 11, 64).astype(np.int64).sum(axis=2)
+    assert np.array_equal(rm, ref.astype(np.float32))
+    assert np.array_equal(bm, ref.T.astype(np.float32))
+
+
+@pytest.fixture(scope="module")
+def router_inputs():
+    rng = np.random.default_rng(4)
+    T = 37
+    x = tokens_np(T, seed=5)
+    wr = O.f32_to_bf16(rng.standard_normal((E, H)).astype(np.float32) * 0.5)
+    rs = O.bake_router_scale(O.f32_to_bf16(np.ones(H, np.float32)))
+    pes = O.f32_to_bf16(np.ones(E, np.float32))
+    return x, wr, rs, pes
+
+
+def test_router_matches_softmax_argsort_renorm(router_inputs):
+    x, wr, rs, pes = router_inputs
+    idx, w, lg = O.router(x, wr, rs, pes)
+    # self-check (iv): same f32 logits -> softmax over 128 -> stable argsort -> renorm
+    p = np.exp(lg.astype(np.float64) - lg.max(axis=1, keepdims=True))
+    p /= p.sum(axis=1, keepdims=True)
+    order = np.argsort(-p, axis=1, kind="stable")[:, :TOPK]
+    assert np.array_equal(idx, order)
+    ref_w = np.take_along_axis(p, order, axis=1)
+    ref_w /= ref_w.sum(axis=1, keepdims=True)
+    assert np.abs(w - ref_w).max() < 1e-2
+    # benchmarks/benchmark_router_merge.mojo:120-135 verify_softmax
+    assert ((idx >= 0) & (idx < E)).all()
+    assert np.abs(w.sum(axis=1) - 1).max() <= 1e-3
+
+
+def test_router_logits_match_float64(router_inputs):
+    x, wr, rs, pes = router_inputs
+    _, _, lg = O.router(x, wr, rs, pes)
+    xf = O.bf16_to_f32(x).astype(np.float64)
+    inv = 1 / np.sqrt((xf ** 2).mean(axis=1) + 1e-6)
+    s = xf * O.bf16_to_f32(rs)[None, :] * inv[:, None]
+    ref = s @ O.bf16_to_f32(wr).astype(np.float64).T
+    assert np.abs(lg - ref).max() < 1e-4 * np.abs(ref).max()
+
+
+def test_router_tie_breaks_to_lower_expert():
+    # identical router rows -> identical logits -> lowest ids win, in id order
+    x = tokens_np(3, seed=6)
+    row = O.f32_to_bf16(np.random.default_rng(7).standard_normal(H).astype(np.float32))
+    wr = np.tile(row, (E, 1))
+    rs = O.f32_to_bf16(np.ones(H, np.float32))
+    pes = O.f32_to_bf16(np.ones(E, np.float32))
+    idx, w, _ = O.router(x, wr, rs, pes)
+    assert (idx == np.arange(8)[None, :]).all()
+    assert np.allclose(w, 1 / 8, atol=1e-6)
+
+
+def np_schedule(idx, w, base, epr):
+    off = np.zeros(epr + 1, np.int32)
+    recs = [[] for _ in range(epr)]
+    T = idx.shape[0]
+    for t in range(T):
+        for k in range(TOPK):
+            e = idx[t, k] - base
+            if 0 <= e < epr:
+                recs[e].append((t, w[t, k]))
+    out = []
+    for e in range(epr):
+        off[e + 1] = off[e] + len(recs[e])
+        out += recs[e]
+    return off, out
+
+
+@pytest.mark.parametrize("base,epr", [(0, 128), (32, 32), (96, 32)])
+def test_schedule_stable_order(base, epr):
+    rng = np.random.default_rng(8)
+    T = 300
+    idx = np.stack([rng.permutation(E)[:TOPK] for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, TOPK)).astype(np.float32)
+    off, routes = O.build_schedules(idx, w, base, epr)
+    roff, rrec = np_schedule(idx, w, base, epr)
+    assert np.array_equal(off, roff)
+    assert [int(t) for t in routes["token"]] == [t for t, _ in rrec]
+    assert np.array_equal(routes["weight"], np.array([x for _, x in rrec], np.float32))
+
+
+@pytest.fixture(scope="module")
+def bq_small():
+    raw = raw_layer_np(seed=11, router_std=1.0, stress=True)
+    return raw, oracle_bq_layer(raw)
+
+
+def test_bq_forward_degree_partials_close(bq_small):
+    raw, L = bq_small
+    x = tokens_np(24, seed=12)
+    out1, idx1, _, _ = O.bq_forward(x, L, degree=1)
+    out2, idx2, _, _ = O.bq_forward(x, L, degree=2)
+    assert np.array_equal(idx1, idx2)
+    # reference degree-G semantics round each rank's partial to bf16 first
+    assert rel_err(out2, out1) < 1e-2
+
+
+def test_bq_forward_tokens_independent(bq_small):
+    _, L = bq_small
+    x = tokens_np(20, seed=13)
+    full, _, _, _ = O.bq_forward(x, L)
+    part, _, _, _ = O.bq_forward(x[:7], L)
+    assert np.array_equal(full[:7], part)
+
+
+def test_bq_close_to_bf16_path(bq_small):
+    """Butterquant output approximates the unquantised model (the int8 error
+    is the only difference; FWHT rotations cancel): self-check (i)."""
+    raw, Lq = bq_small
+    Lb = oracle_bf16_layer(raw)
+    x = tokens_np(16, seed=14)
+    ob, ib, _, lgb = O.bf16_forward(x, Lb)
+    oq, iq, _, lgq = O.bq_forward(x, Lq)
+    # the centred router keeps the softmax ranking (gauge cancels)
+    keep = (ib == iq).all(axis=1)
+    assert keep.mean() > 0.9
+    assert rel_err(oq, ob, rows=keep) < 0.1
