@@ -233,14 +233,21 @@ def main():
     def step(i):
         blk.forward(0, xs[i % len(xs)], outs[i % len(xs)], T, stream)
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The clock sampler runs from the warm-up through the timed region; the
+    # warm-up lasts at least 0.5 s so that nvidia-smi sees the GPU under load.
     with ClockSampler(local) as clk:
+        t_w = time.perf_counter()
+        i = 0
+        while i < args.warmup or time.perf_counter() - t_w < 0.5:
+            step(i)
+            i += 1
+            if i % 8 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
         ev0.record(stream)
         for i in range(args.steps):
             step(i)
@@ -326,7 +333,7 @@ def roofline(blk, fmt, L, xs, T, steps, stream):
     import gmoe
     hbm, tf, src = peaks()
     x = xs[0]
-    lg = torch.empty(T, E, dtype=torch.float32, device="cuda")
+    lg = torch.empty(gmoe.lib().gm_router_workspace_bytes(T) // 4, dtype=torch.float32, device="cuda")
     idx = torch.empty(T, TOPK, dtype=torch.int32, device="cuda")
     w = torch.empty(T, TOPK, dtype=torch.float32, device="cuda")
     off = torch.empty(E + 1, dtype=torch.int32, device="cuda")

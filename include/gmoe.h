@@ -119,9 +119,13 @@ int gm_moe_forward_sync(gm_moe_t* h, int layer, const void* x, void* out, int T)
  * callers that own their scratch.  Device pointers. */
 
 /* dispatch_router_expert + dispatch_merge_router_candidates
- * (kernels/moe_router.mojo:206-244,333-389): logits_ws f32 [T][128] (also an
- * output), route_idx i32 [T][8] (logit-descending, ties to the lower id),
- * route_w f32 [T][8] (softmax over the 8, times per_expert_scale). */
+ * (kernels/moe_router.mojo:206-244,333-389): route_idx i32 [T][8]
+ * (logit-descending, ties to the lower id), route_w f32 [T][8] (softmax over
+ * the 8, times per_expert_scale).  logits_ws: f32 workspace of
+ * gm_router_workspace_bytes(T) bytes (split-K partial logits); on return its
+ * first T*128 floats hold the logits [T][128]. */
+size_t gm_router_workspace_bytes(int T);
+
 int gm_router_select(const void* x, const void* router_w, const void* router_scale,
                      const void* per_expert_scale, int T, float* logits_ws, int32_t* route_idx,
                      float* route_w, void* stream);

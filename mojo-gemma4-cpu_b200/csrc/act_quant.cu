@@ -49,7 +49,9 @@ __device__ __forceinline__ void fwht64_lane2(float& v0, float& v1, int lane) {
 
 __global__ void __launch_bounds__(256)
 bq_norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, int T,
-                     int8_t* __restrict__ xi8, float* __restrict__ xsa) {
+                     int8_t* __restrict__ xi8, float* __restrict__ xsa, float* __restrict__ inv_out) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -69,6 +71,7 @@ bq_norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
   }
   ss = warp_sum(ss);
   const float inv = inv_rms_from_sumsq(ss);
+  if (inv_out && lane == 0) inv_out[t] = inv;
   float amax = 0.0f;
 #pragma unroll
   for (int b = 0; b < NBLK; ++b) {
@@ -96,6 +99,8 @@ bq_norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
 __global__ void __launch_bounds__(256)
 block_quant_kernel(const uint16_t* __restrict__ src, long rows, int8_t* __restrict__ qi8,
                    float* __restrict__ sa) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const long r = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
@@ -115,7 +120,9 @@ block_quant_kernel(const uint16_t* __restrict__ src, long rows, int8_t* __restri
 
 __global__ void __launch_bounds__(256)
 rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, int T,
-                     uint16_t* __restrict__ out) {
+                     uint16_t* __restrict__ out, float* __restrict__ inv_out) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -135,6 +142,7 @@ rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
   }
   ss = warp_sum(ss);
   const float inv = inv_rms_from_sumsq(ss);
+  if (inv_out && lane == 0) inv_out[t] = inv;
   uint16_t* dst = out + (size_t)t * H;
 #pragma unroll
   for (int b = 0; b < NBLK; ++b) {
@@ -151,24 +159,24 @@ rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
 }
 
 cudaError_t launch_bq_norm_quant(const uint16_t* x, const uint16_t* gamma, int T, int8_t* xi8,
-                                 float* xsa, cudaStream_t s) {
+                                 float* xsa, float* inv_rms, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  bq_norm_quant_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, gamma, T, xi8, xsa);
-  return cudaGetLastError();
+  return launch_k(bq_norm_quant_kernel, dim3((T + 7) / 8), dim3(256), 0, s, x, gamma, T, xi8, xsa,
+                  inv_rms);
 }
 
 cudaError_t launch_block_quant(const uint16_t* bucket, long rows, int8_t* qi8, float* sa,
                                cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  block_quant_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(bucket, rows, qi8, sa);
-  return cudaGetLastError();
+  return launch_k(block_quant_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, s, bucket, rows,
+                  qi8, sa);
 }
 
 cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int T, uint16_t* out,
-                                 cudaStream_t s) {
+                                 float* inv_rms, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  rms_norm_bf16_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, gamma, T, out);
-  return cudaGetLastError();
+  return launch_k(rms_norm_bf16_kernel, dim3((T + 7) / 8), dim3(256), 0, s, x, gamma, T, out,
+                  inv_rms);
 }
 
 }  // namespace gm

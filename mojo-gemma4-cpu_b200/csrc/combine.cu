@@ -16,6 +16,8 @@ combine_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict_
                const float* __restrict__ ybuf, int T, uint16_t* __restrict__ out) {
   __shared__ int s_pos[TOPK];
   __shared__ int s_n;
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   if (threadIdx.x == 0) {
     int ex[TOPK], ps[TOPK], n = 0;
@@ -52,8 +54,7 @@ combine_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict_
 cudaError_t launch_combine(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
                            int T, uint16_t* out, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  combine_kernel<<<T, 352, 0, s>>>(route_idx, route_pos, ybuf, T, out);
-  return cudaGetLastError();
+  return launch_k(combine_kernel, dim3(T), dim3(352), 0, s, route_idx, route_pos, ybuf, T, out);
 }
 
 }  // namespace gm

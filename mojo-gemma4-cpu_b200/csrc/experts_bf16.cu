@@ -30,6 +30,8 @@ bf16_phase1_kernel(const uint16_t* __restrict__ xn, const int32_t* __restrict__ 
   float* red = reinterpret_cast<float*>(smem + RC_BF * XS_BF);               // (KSPLIT-1)*2*32*8
   float* dots = red + (KSPLIT - 1) * 2 * 32 * 8;                             // [2][32][RC]
 
+  pdl_wait();
+  pdl_trigger();
   const int total = __ldg(chunk_off + epr) * NTILES;
   const int task = blockIdx.x;
   if (task >= total) return;
@@ -129,6 +131,8 @@ bf16_phase2_kernel(const uint16_t* __restrict__ bucket, const int32_t* __restric
   __shared__ __align__(16) uint8_t xs[RC_BF * BS_BF];
   __shared__ float s_w[RC_BF];
 
+  pdl_wait();
+  pdl_trigger();
   const int total = __ldg(chunk_off + epr) * GROUPS;
   const int task = blockIdx.x;
   if (task >= total) return;
@@ -200,8 +204,8 @@ cudaError_t launch_bf16_phase1(const uint16_t* xn, const int32_t* expert_offset,
   const int grid = max_route_chunks(T, epr, RC_BF) * (I / 32);
   auto k = bf16_phase1_kernel<KSPLIT, DEPTH>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k<<<grid, 64 * KSPLIT, smem, s>>>(xn, expert_offset, routes, chunk_off, epr, w_gu, bucket);
-  return cudaGetLastError();
+  return launch_k(k, dim3(grid), dim3(64 * KSPLIT), smem, s, xn, expert_offset, routes, chunk_off,
+                  epr, w_gu, bucket);
 }
 
 cudaError_t launch_bf16_phase2(const uint16_t* bucket, const int32_t* expert_offset,
@@ -210,9 +214,8 @@ cudaError_t launch_bf16_phase2(const uint16_t* bucket, const int32_t* expert_off
   if (T <= 0) return cudaSuccess;
   constexpr int NTILE = 4, DEPTH = 4;
   const int grid = max_route_chunks(T, epr, RC_BF) * ((H / 32) / NTILE);
-  bf16_phase2_kernel<NTILE, DEPTH><<<grid, 32 * NTILE, 0, s>>>(bucket, expert_offset, routes,
-                                                               chunk_off, epr, w_dn, ybuf);
-  return cudaGetLastError();
+  return launch_k(bf16_phase2_kernel<NTILE, DEPTH>, dim3(grid), dim3(32 * NTILE), 0, s, bucket,
+                  expert_offset, routes, chunk_off, epr, w_dn, ybuf);
 }
 
 }  // namespace gm

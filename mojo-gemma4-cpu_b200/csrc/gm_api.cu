@@ -40,6 +40,7 @@ struct gm_moe {
   void* ws = nullptr;
   size_t ws_bytes = 0;
   float* logits = nullptr;
+  float* inv_rms = nullptr;
   int32_t* route_idx = nullptr;
   float* route_w = nullptr;
   int32_t* route_pos = nullptr;
@@ -99,7 +100,7 @@ struct Carve {
 };
 
 struct WsLayout {
-  size_t logits, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
+  size_t logits, inv_rms, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
       x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, total;
 };
 
@@ -107,7 +108,10 @@ WsLayout ws_layout(int max_tokens) {
   const size_t T = (size_t)max_tokens, R = T * TOPK;
   Carve c;
   WsLayout L;
-  L.logits = c.take<float>(T * E);
+  const int m1 = std::min(max_tokens, 64), m2 = std::min(max_tokens, 1024);
+  L.logits = c.take<float>(std::max({router_workspace_floats(m1), router_workspace_floats(m2),
+                                     router_workspace_floats(max_tokens)}));
+  L.inv_rms = c.take<float>(T);
   L.route_idx = c.take<int32_t>(R);
   L.route_w = c.take<float>(R);
   L.route_pos = c.take<int32_t>(R);
@@ -173,6 +177,10 @@ const char* gm_last_error(const gm_moe_t* h) {
   return h ? h->err.c_str() : g_tls_error.c_str();
 }
 
+size_t gm_router_workspace_bytes(int T) {
+  return T > 0 ? router_workspace_floats(T) * sizeof(float) : 0;
+}
+
 size_t gm_moe_workspace_bytes(int max_tokens) {
   return max_tokens > 0 ? ws_layout(max_tokens).total : 0;
 }
@@ -209,6 +217,7 @@ int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, in
   h->ws_bytes = L.total;
   char* b = static_cast<char*>(h->ws);
   h->logits = reinterpret_cast<float*>(b + L.logits);
+  h->inv_rms = reinterpret_cast<float*>(b + L.inv_rms);
   h->route_idx = reinterpret_cast<int32_t*>(b + L.route_idx);
   h->route_w = reinterpret_cast<float*>(b + L.route_w);
   h->route_pos = reinterpret_cast<int32_t*>(b + L.route_pos);
@@ -296,22 +305,27 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
   if (!x || !out) return set_err(h, GM_EINVAL, "NULL x/out");
   cudaStream_t s = S(stream);
   const uint16_t* xb = static_cast<const uint16_t*>(x);
-  GM_TRY(h, launch_router(xb, L.router, L.rscale, L.pes, T, h->logits, h->route_idx, h->route_w, s),
-         "router");
+  // 1. activation norm (+ inv_rms shared with the router)
+  if (L.kind == 1)
+    GM_TRY(h, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, h->inv_rms, s), "bq_norm_quant");
+  else
+    GM_TRY(h, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
+  // 2. router logits, 3. top-8 + schedule
+  GM_TRY(h, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, s), "router");
   const int rc_chunk = L.kind == 1 ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
-  GM_TRY(h, launch_build_schedule(h->route_idx, h->route_w, T, h->expert_base, h->epr, rc_chunk,
-                                  h->expert_offset, h->routes, h->route_pos, h->chunk_off, s),
-         "build_schedules");
+  GM_TRY(h, launch_topk_schedule(h->logits, L.pes, T, h->route_idx, h->route_w, h->expert_base,
+                                 h->epr, rc_chunk, h->expert_offset, h->routes, h->route_pos,
+                                 h->chunk_off, s),
+         "topk_schedule");
+  // 4. experts, 5. combine
   if (L.kind == 1) {
-    GM_TRY(h, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, s), "bq_norm_quant");
     GM_TRY(h, launch_bq_phase1(h->x_i8, h->x_sa, h->expert_offset, h->routes, h->chunk_off, h->epr,
                                T, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
            "bq_phase1");
     GM_TRY(h, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
-                               h->chunk_off, h->epr, T, L.dn_q, L.dn_scale, h->ybuf, s),
+                               h->chunk_off, h->epr, T, L.dn_q, L.dn_scale, h->ybuf, true, s),
            "bq_phase2");
   } else {
-    GM_TRY(h, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, s), "rms_norm");
     GM_TRY(h, launch_bf16_phase1(h->x_normed, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
                                  L.gu_bf16, h->bucket, s),
            "phase1_bf16");
@@ -380,14 +394,14 @@ int gm_build_expert_schedules(const int32_t* route_idx, const float* route_w, in
 
 int gm_rms_norm(const void* x, const void* gamma, int T, void* out, void* stream) {
   STAGE(launch_rms_norm_bf16(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gamma),
-                             T, static_cast<uint16_t*>(out), S(stream)),
+                             T, static_cast<uint16_t*>(out), nullptr, S(stream)),
         "rms_norm");
 }
 
 int gm_bq_norm_quant(const void* x, const void* gamma, int T, int8_t* x_i8, float* x_sa,
                      void* stream) {
   STAGE(launch_bq_norm_quant(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gamma),
-                             T, x_i8, x_sa, S(stream)),
+                             T, x_i8, x_sa, nullptr, S(stream)),
         "bq_norm_quant");
 }
 
@@ -413,7 +427,7 @@ int gm_bq_phase2_down(const int8_t* bucket_i8, const float* bucket_sa, const int
   if (epr < 1 || epr > E || T < 0) return set_err(nullptr, GM_EINVAL, "bq_phase2: epr=%d T=%d", epr, T);
   STAGE(launch_bq_phase2(bucket_i8, bucket_sa, expert_offset,
                          reinterpret_cast<const SparseRoute*>(routes), chunk_off, epr, T,
-                         static_cast<const int8_t*>(down), down_scale, y, S(stream)),
+                         static_cast<const int8_t*>(down), down_scale, y, false, S(stream)),
         "bq_phase2_down");
 }
 

@@ -134,6 +134,15 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return r;
 }
 
+// 16-byte global -> shared asynchronous copy (bypasses registers and L1).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
 // mma.sync m16n8k32 s8 x s8 -> s32 (fragment layout: PTX ISA, "Matrix
 // Fragments for mma.m16n8k32").
 __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -154,6 +163,14 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+
+// Programmatic dependent launch.  The forward's kernels are launched with
+// programmatic stream serialisation, so kernel N+1 may start while kernel N is
+// finishing; pdl_wait() blocks until the predecessor grid has completed and its
+// writes are visible (a no-op for launches without the attribute), and
+// pdl_trigger() lets the successor grid launch early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 // Locate the expert owning global route-chunk `cg` given the per-expert chunk
 // prefix `chunk_off[0..n]` (binary search; chunk_off is non-decreasing).

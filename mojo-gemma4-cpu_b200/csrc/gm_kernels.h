@@ -6,7 +6,39 @@
 
 namespace gm {
 
+// Launch with programmatic stream serialisation (see pdl_wait/pdl_trigger):
+// every kernel launched this way calls pdl_wait() before touching memory that
+// an earlier kernel of the stream writes or reads.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 int max_route_chunks(int T, int epr, int rc);
+int router_ksplit(int T);
+size_t router_workspace_floats(int T);
+
+cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
+                                 const float* inv_rms, int T, float* logits, cudaStream_t s);
+cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_t s);
+cudaError_t launch_topk(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
+                        float* route_w, cudaStream_t s);
+// top-8 + softmax followed by the expert schedule (one CTA when T <= 1024)
+cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
+                                 float* route_w, int expert_base, int epr, int route_chunk,
+                                 int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
+                                 int32_t* chunk_off, cudaStream_t s);
 
 cudaError_t launch_router(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
                           const uint16_t* pes, int T, float* logits, int32_t* route_idx,
@@ -16,11 +48,11 @@ cudaError_t launch_build_schedule(const int32_t* route_idx, const float* route_w
                                   int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
                                   int32_t* chunk_off, cudaStream_t s);
 cudaError_t launch_bq_norm_quant(const uint16_t* x, const uint16_t* gamma, int T, int8_t* xi8,
-                                 float* xsa, cudaStream_t s);
+                                 float* xsa, float* inv_rms, cudaStream_t s);
 cudaError_t launch_block_quant(const uint16_t* bucket, long rows, int8_t* qi8, float* sa,
                                cudaStream_t s);
 cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int T, uint16_t* out,
-                                 cudaStream_t s);
+                                 float* inv_rms, cudaStream_t s);
 cudaError_t launch_bq_phase1(const int8_t* xi8, const float* xsa, const int32_t* expert_offset,
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_gu, const float* gu_scale, int8_t* bucket_i8,
@@ -28,7 +60,7 @@ cudaError_t launch_bq_phase1(const int8_t* xi8, const float* xsa, const int32_t*
 cudaError_t launch_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t* expert_offset,
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_dn, const float* dn_scale, float* ybuf,
-                             cudaStream_t s);
+                             bool after_phase1, cudaStream_t s);
 cudaError_t launch_bf16_phase1(const uint16_t* xn, const int32_t* expert_offset,
                                const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                                const uint16_t* w_gu, uint16_t* bucket, cudaStream_t s);

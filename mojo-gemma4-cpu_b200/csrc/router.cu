@@ -8,44 +8,38 @@
 //
 // B200 shape: the logits are a skinny [T x 2816] x [2816 x 128] product done
 // in f32 FMA (the reference's f32-activation x bf16-weight dot, no bf16
-// rounding of the activation), tiled through shared memory; top-8 selection is
-// one warp per token with 8 rounds of warp arg-max under the reference's
+// rounding of the activation), tiled through shared memory and split along K
+// for small T so that enough CTAs stream the 720 KB projection.  inv_rms comes
+// from the activation-norm kernel that runs first (the reference computes the
+// same rms_reduce_row for both, kernels/rmsnorm.mojo:16-17).  Top-8 selection
+// is one warp per token with 8 rounds of warp arg-max under the reference's
 // ordering (logit descending, ties to the lower expert id).
 #include "gm_kernels.h"
+#include "router_dev.cuh"
 
 namespace gm {
 
 template <int TT, int EG, int MT, int ME>
 __global__ void __launch_bounds__((TT / MT) * (EG / ME))
 router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
-                     const uint16_t* __restrict__ rscale, int T, int n_experts,
-                     float* __restrict__ logits) {
+                     const uint16_t* __restrict__ rscale, const float* __restrict__ inv_rms,
+                     int T, int n_experts, int k_len, float* __restrict__ logits) {
   constexpr int NT = (TT / MT) * (EG / ME);
-  constexpr int NW = NT / 32;
   constexpr int KC = 64;
   static_assert(NT % 32 == 0, "whole warps");
   __shared__ float s_inv[TT];
   __shared__ float s_x[KC][TT + 1];
   __shared__ float s_w[KC][EG + 1];
+  pdl_wait();
+  pdl_trigger();
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const int t0 = blockIdx.x * TT, e0 = blockIdx.y * EG;
-
-  // inv_rms per token (kernels/rmsnorm.mojo:16-17,45-46)
-  for (int t = warp; t < TT; t += NW) {
-    float ss = 0.0f;
-    if (t0 + t < T) {
-      const uint16_t* xr = x + (size_t)(t0 + t) * H;
-      for (int k = lane * 2; k < H; k += 64) {
-        uint32_t v = *reinterpret_cast<const uint32_t*>(xr + k);
-        float a = bf2f(v & 0xFFFFu), b = bf2f(v >> 16);
-        ss = __fadd_rn(ss, __fmul_rn(a, a));
-        ss = __fadd_rn(ss, __fmul_rn(b, b));
-      }
-      ss = warp_sum(ss);
-    }
-    if (lane == 0) s_inv[t] = inv_rms_from_sumsq(ss);
-  }
+  // split-K: this CTA covers K range [kb, kb + k_len) and writes partial logits
+  // to slice blockIdx.z of [gridDim.z][T][n_experts]
+  const int kb = blockIdx.z * k_len;
+  logits += (size_t)blockIdx.z * T * n_experts;
+  for (int t = tid; t < TT; t += NT) s_inv[t] = t0 + t < T ? inv_rms[t0 + t] : 0.0f;
   __syncthreads();
 
   const int tx = tid % (EG / ME), ty = tid / (EG / ME);
@@ -55,7 +49,7 @@ router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
 #pragma unroll
     for (int n = 0; n < ME; ++n) acc[m][n] = 0.0f;
 
-  for (int k0 = 0; k0 < H; k0 += KC) {
+  for (int k0 = kb; k0 < kb + k_len; k0 += KC) {
     for (int i = tid; i < TT * (KC / 2); i += NT) {
       int t = i / (KC / 2), kp = (i % (KC / 2)) * 2;
       float a = 0.0f, b = 0.0f;
@@ -105,71 +99,145 @@ router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
   }
 }
 
-// One warp per token.  Lane l holds experts l, l+32, l+64, l+96.
-__global__ void __launch_bounds__(128)
-topk_softmax_kernel(const float* __restrict__ logits, const uint16_t* __restrict__ pes, int T,
-                    int32_t* __restrict__ route_idx, float* __restrict__ route_w) {
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (t >= T) return;
-  float v[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) v[j] = logits[(size_t)t * E + lane + 32 * j];
-  unsigned taken = 0;
-  int sel_e[TOPK];
-  float sel_l[TOPK];
-#pragma unroll
-  for (int k = 0; k < TOPK; ++k) {
-    float bv = -INFINITY;
-    int bi = 0x7FFFFFFF;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      int id = lane + 32 * j;
-      if (!((taken >> j) & 1u) && (v[j] > bv || (v[j] == bv && id < bi))) { bv = v[j]; bi = id; }
+// Router logits for T <= 1024.  CTA = 8 warps, tile = 8 tokens x 32 experts x
+// one 256-wide K slice (blockIdx.z).  Lane l owns k = kb+8l..8l+7 of every row
+// and reads the bf16 projection straight from global memory (one 16-byte load
+// per expert); each warp owns 4 experts.  The 32 (token, expert) lane partials
+// are combined by a reduce-scatter butterfly that leaves lane t*4+e holding
+// the slice sum of token t and expert e (a fixed, deterministic order).
+__global__ void __launch_bounds__(256)
+router_logits_small_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
+                           const uint16_t* __restrict__ rscale, const float* __restrict__ inv_rms,
+                           int T, float* __restrict__ logits) {
+  constexpr int TT = 8, KS = 256;
+  __shared__ __align__(16) float s_s[TT][KS];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0 = blockIdx.x * TT, e0 = blockIdx.y * 32, kb = blockIdx.z * KS;
+  logits += (size_t)blockIdx.z * T * E;
+  for (int i = tid; i < TT * KS / 2; i += 256) {
+    const int t = i / (KS / 2), kp = (i % (KS / 2)) * 2;
+    float a = 0.0f, b = 0.0f;
+    if (t0 + t < T) {
+      const uint32_t v = *reinterpret_cast<const uint32_t*>(x + (size_t)(t0 + t) * H + kb + kp);
+      const uint32_t rs = *reinterpret_cast<const uint32_t*>(rscale + kb + kp);
+      const float inv = inv_rms[t0 + t];
+      // `xv * sv * inv_vec` (moe_router.mojo:175-178): (x*s)*inv, f32
+      a = __fmul_rn(__fmul_rn(bf2f(v & 0xFFFFu), bf2f(rs & 0xFFFFu)), inv);
+      b = __fmul_rn(__fmul_rn(bf2f(v >> 16), bf2f(rs >> 16)), inv);
     }
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-      float ov = __shfl_xor_sync(0xffffffffu, bv, m);
-      int oi = __shfl_xor_sync(0xffffffffu, bi, m);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    if (bi >= E) bi = 0;  // only reachable with NaN logits; keeps indices in range
-    sel_e[k] = bi;
-    sel_l[k] = bv;
-    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    s_s[t][kp] = a;
+    s_s[t][kp + 1] = b;
   }
-  if (lane == 0) {
-    // moe_router.mojo:276-293
-    float maxl = sel_l[0];
-    float ev[TOPK];
-    float sum = 0.0f;
+  __syncthreads();
+  float v[TT * 4];
 #pragma unroll
-    for (int k = 0; k < TOPK; ++k) {
-      ev[k] = fast_exp_softmax_biased(__fsub_rn(sel_l[k], maxl));
-      sum = __fadd_rn(sum, ev[k]);
-    }
-    float inv_sum = __fdiv_rn(1.0f, sum);
+  for (int ee = 0; ee < 4; ++ee) {
+    const uint4 w4 = *reinterpret_cast<const uint4*>(wr + (size_t)(e0 + warp * 4 + ee) * H + kb + 8 * lane);
+    const float w[8] = {bf2f(w4.x & 0xFFFFu), bf2f(w4.x >> 16), bf2f(w4.y & 0xFFFFu), bf2f(w4.y >> 16),
+                        bf2f(w4.z & 0xFFFFu), bf2f(w4.z >> 16), bf2f(w4.w & 0xFFFFu), bf2f(w4.w >> 16)};
 #pragma unroll
-    for (int k = 0; k < TOPK; ++k) {
-      route_idx[t * TOPK + k] = sel_e[k];
-      route_w[t * TOPK + k] = __fmul_rn(__fmul_rn(ev[k], inv_sum), bf2f(pes[sel_e[k]]));
+    for (int t = 0; t < TT; ++t) {
+      const float4 s0 = *reinterpret_cast<const float4*>(&s_s[t][8 * lane]);
+      const float4 s1 = *reinterpret_cast<const float4*>(&s_s[t][8 * lane + 4]);
+      float a = __fmul_rn(s0.x, w[0]);
+      a = __fmaf_rn(s0.y, w[1], a);
+      a = __fmaf_rn(s0.z, w[2], a);
+      a = __fmaf_rn(s0.w, w[3], a);
+      a = __fmaf_rn(s1.x, w[4], a);
+      a = __fmaf_rn(s1.y, w[5], a);
+      a = __fmaf_rn(s1.z, w[6], a);
+      a = __fmaf_rn(s1.w, w[7], a);
+      v[t * 4 + ee] = a;
     }
   }
+#pragma unroll
+  for (int m = 16, n = 32; m >= 1; m >>= 1, n >>= 1) {
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const bool up = (lane & m) != 0;
+      const float send = up ? v[i] : v[i + n / 2];
+      const float keep = up ? v[i + n / 2] : v[i];
+      v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+    }
+  }
+  const int t = t0 + (lane >> 2);
+  if (t < T) logits[(size_t)t * E + e0 + warp * 4 + (lane & 3)] = v[0];
 }
 
+// inv_rms of each token (one warp per token): kernels/rmsnorm.mojo:16-17,45-46.
+__global__ void __launch_bounds__(256)
+rms_inv_kernel(const uint16_t* __restrict__ x, int T, float* __restrict__ inv_rms) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const uint16_t* xr = x + (size_t)t * H;
+  float ss = 0.0f;
+#pragma unroll
+  for (int b = 0; b < H / NORM_BLOCK; ++b) {
+    uint2 raw = *reinterpret_cast<const uint2*>(xr + b * NORM_BLOCK + 4 * lane);
+    float v[4] = {bf2f(raw.x & 0xFFFFu), bf2f(raw.x >> 16), bf2f(raw.y & 0xFFFFu), bf2f(raw.y >> 16)};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) inv_rms[t] = inv_rms_from_sumsq(ss);
+}
+
+__global__ void __launch_bounds__(128)
+topk_softmax_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __restrict__ pes,
+                    int T, int32_t* __restrict__ route_idx, float* __restrict__ route_w) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  topk_token(logits, ksplit, pes, T, t, threadIdx.x & 31, route_idx, route_w);
+}
+
+int router_ksplit(int T) {
+  return T <= 1024 ? H / 256 : 1;  // 11 K slices of 256 for the warp-level kernel
+}
+
+size_t router_workspace_floats(int T) { return (size_t)router_ksplit(T) * T * E + T; }
+
+cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
+                                 const float* inv_rms, int T, float* logits, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const int ks = router_ksplit(T);
+  if (ks > 1)
+    return launch_k(router_logits_small_kernel, dim3((T + 7) / 8, E / 32, ks), dim3(256), 0, s, x,
+                    wr, rscale, inv_rms, T, logits);
+  dim3 grid((T + 31) / 32, E / 32, 1);
+  return launch_k(router_logits_kernel<32, 32, 4, 2>, grid, dim3(128), 0, s, x, wr, rscale,
+                  inv_rms, T, (int)E, (int)H, logits);
+}
+
+cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  return launch_k(rms_inv_kernel, dim3((T + 7) / 8), dim3(256), 0, s, x, T, inv_rms);
+}
+
+cudaError_t launch_topk(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
+                        float* route_w, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  return launch_k(topk_softmax_kernel, dim3((T + 3) / 4), dim3(128), 0, s, logits,
+                  router_ksplit(T), pes, T, route_idx, route_w);
+}
+
+// Standalone router (gm_router_select): inv_rms into the tail of the workspace,
+// then logits and top-8.
 cudaError_t launch_router(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
                           const uint16_t* pes, int T, float* logits, int32_t* route_idx,
                           float* route_w, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  if (T >= 64) {
-    dim3 grid((T + 31) / 32, E / 32);
-    router_logits_kernel<32, 32, 4, 2><<<grid, 128, 0, s>>>(x, wr, rscale, T, E, logits);
-  } else {
-    dim3 grid((T + 7) / 8, E / 16);
-    router_logits_kernel<8, 16, 1, 1><<<grid, 128, 0, s>>>(x, wr, rscale, T, E, logits);
-  }
-  topk_softmax_kernel<<<(T + 3) / 4, 128, 0, s>>>(logits, pes, T, route_idx, route_w);
-  return cudaGetLastError();
+  float* inv = logits + (size_t)router_ksplit(T) * T * E;
+  cudaError_t e = launch_rms_inv(x, T, inv, s);
+  if (e == cudaSuccess) e = launch_router_logits(x, wr, rscale, inv, T, logits, s);
+  if (e == cudaSuccess) e = launch_topk(logits, pes, T, route_idx, route_w, s);
+  return e;
 }
 
 }  // namespace gm

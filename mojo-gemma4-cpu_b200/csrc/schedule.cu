@@ -13,18 +13,28 @@
 // each route, -1 if the expert is not local) and chunk_off[epr+1] (prefix of
 // ceil(n_e / route_chunk), the work decomposition of the expert kernels).
 #include "gm_kernels.h"
+#include "router_dev.cuh"
 
 namespace gm {
 
-__global__ void __launch_bounds__(1024)
-build_schedule_kernel(const int32_t* __restrict__ route_idx, const float* __restrict__ route_w,
-                      int T, int expert_base, int epr, int route_chunk,
-                      int32_t* __restrict__ expert_offset, SparseRoute* __restrict__ routes,
-                      int32_t* __restrict__ route_pos, int32_t* __restrict__ chunk_off) {
-  __shared__ int cnt[E];
-  __shared__ int base[E];
-  __shared__ uint32_t mask[E][32];
-  __shared__ int wpre[E][33];
+struct ScheduleSmem {
+  int cnt[E];
+  int base[E];
+  uint32_t mask[E][32];
+  int wpre[E][33];
+};
+
+// Body shared by the schedule kernel and the fused top-8 + schedule kernel
+// (one CTA of 1024 threads).
+__device__ void schedule_body(const int32_t* __restrict__ route_idx,
+                              const float* __restrict__ route_w, int T, int expert_base, int epr,
+                              int route_chunk, int32_t* __restrict__ expert_offset,
+                              SparseRoute* __restrict__ routes, int32_t* __restrict__ route_pos,
+                              int32_t* __restrict__ chunk_off, ScheduleSmem& sm) {
+  int* cnt = sm.cnt;
+  int* base = sm.base;
+  auto& mask = sm.mask;
+  auto& wpre = sm.wpre;
   const int tid = threadIdx.x;
   for (int e = tid; e < E; e += 1024) cnt[e] = 0;
   __syncthreads();
@@ -117,13 +127,58 @@ build_schedule_kernel(const int32_t* __restrict__ route_idx, const float* __rest
   }
 }
 
+__global__ void __launch_bounds__(1024)
+build_schedule_kernel(const int32_t* __restrict__ route_idx, const float* __restrict__ route_w,
+                      int T, int expert_base, int epr, int route_chunk,
+                      int32_t* __restrict__ expert_offset, SparseRoute* __restrict__ routes,
+                      int32_t* __restrict__ route_pos, int32_t* __restrict__ chunk_off) {
+  __shared__ ScheduleSmem sm;
+  pdl_wait();
+  pdl_trigger();
+  schedule_body(route_idx, route_w, T, expert_base, epr, route_chunk, expert_offset, routes,
+                route_pos, chunk_off, sm);
+}
+
+// Top-8 selection of every token (32 warps, one token per warp at a time) and
+// then the schedule, in one CTA: for decode-sized T this saves a launch and a
+// round trip of the routes through a separate kernel boundary.
+__global__ void __launch_bounds__(1024)
+topk_schedule_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __restrict__ pes,
+                     int T, int32_t* __restrict__ route_idx, float* __restrict__ route_w,
+                     int expert_base, int epr, int route_chunk, int32_t* __restrict__ expert_offset,
+                     SparseRoute* __restrict__ routes, int32_t* __restrict__ route_pos,
+                     int32_t* __restrict__ chunk_off) {
+  __shared__ ScheduleSmem sm;
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = warp; t < T; t += 32)
+    topk_token(logits, ksplit, pes, T, t, lane, route_idx, route_w);
+  __syncthreads();  // route_idx / route_w written by this CTA are now visible to it
+  schedule_body(route_idx, route_w, T, expert_base, epr, route_chunk, expert_offset, routes,
+                route_pos, chunk_off, sm);
+}
+
 cudaError_t launch_build_schedule(const int32_t* route_idx, const float* route_w, int T,
                                   int expert_base, int epr, int route_chunk,
                                   int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
                                   int32_t* chunk_off, cudaStream_t s) {
-  build_schedule_kernel<<<1, 1024, 0, s>>>(route_idx, route_w, T, expert_base, epr, route_chunk,
-                                           expert_offset, routes, route_pos, chunk_off);
-  return cudaGetLastError();
+  return launch_k(build_schedule_kernel, dim3(1), dim3(1024), 0, s, route_idx, route_w, T,
+                  expert_base, epr, route_chunk, expert_offset, routes, route_pos, chunk_off);
+}
+
+cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
+                                 float* route_w, int expert_base, int epr, int route_chunk,
+                                 int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
+                                 int32_t* chunk_off, cudaStream_t s) {
+  if (T <= 1024)
+    return launch_k(topk_schedule_kernel, dim3(1), dim3(1024), 0, s, logits, router_ksplit(T), pes,
+                    T, route_idx, route_w, expert_base, epr, route_chunk, expert_offset, routes,
+                    route_pos, chunk_off);
+  cudaError_t e = launch_topk(logits, pes, T, route_idx, route_w, s);
+  if (e != cudaSuccess) return e;
+  return launch_build_schedule(route_idx, route_w, T, expert_base, epr, route_chunk, expert_offset,
+                               routes, route_pos, chunk_off, s);
 }
 
 }  // namespace gm

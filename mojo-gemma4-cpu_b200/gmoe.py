@@ -32,6 +32,7 @@ SIGNATURES = {
     "gm_moe_create": (_i32, [C.POINTER(_vp), _i32, _i32, _i32, _i32, _i32]),
     "gm_moe_destroy": (_i32, [_vp]),
     "gm_moe_workspace_bytes": (_sz, [_i32]),
+    "gm_router_workspace_bytes": (_sz, [_i32]),
     "gm_moe_register_layer_bq": (_i32, [_vp, _i32] + [_vp] * 8),
     "gm_moe_register_layer_bf16": (_i32, [_vp, _i32] + [_vp] * 6),
     "gm_moe_forward": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp]),
@@ -83,6 +84,8 @@ def _addr(t):
         return None
     if isinstance(t, int):
         return t
+    if hasattr(t, "cuda_stream"):  # torch.cuda.Stream
+        return t.cuda_stream
     if hasattr(t, "data_ptr"):
         return t.data_ptr()
     if hasattr(t, "ctypes"):

@@ -84,13 +84,13 @@ def test_quantizer_and_packer_bit_exact(layer_stress):
 def run_router(g, x_np):
     T = x_np.shape[0]
     x = dev(x_np)
-    lg = torch.empty(T, E, dtype=torch.float32, device="cuda")
+    lg = torch.empty(gmoe.lib().gm_router_workspace_bytes(T) // 4, dtype=torch.float32, device="cuda")
     idx = torch.empty(T, TOPK, dtype=torch.int32, device="cuda")
     w = torch.empty(T, TOPK, dtype=torch.float32, device="cuda")
     gmoe.call("gm_router_select", x, g["router_centered"], g["router_scale"], g["per_expert_scale"],
               T, lg, idx, w, None)
     torch.cuda.synchronize()
-    return host(idx), host(w), host(lg)
+    return host(idx), host(w), host(lg)[:T * E].reshape(T, E)
 
 
 @pytest.mark.parametrize("T", [1, 16, 64, 300])
@@ -303,7 +303,7 @@ def test_forward_bf16(T, layer_default):
     blk.forward(0, dev(x_np), out, T)
     torch.cuda.synchronize()
     rout, ridx, _, rlg = O.bf16_forward(x_np, Lb)
-    lg = torch.empty(T, E, dtype=torch.float32, device="cuda")
+    lg = torch.empty(gmoe.lib().gm_router_workspace_bytes(T) // 4, dtype=torch.float32, device="cuda")
     idx = torch.empty(T, TOPK, dtype=torch.int32, device="cuda")
     w = torch.empty(T, TOPK, dtype=torch.float32, device="cuda")
     gmoe.call("gm_router_select", dev(x_np), gl["router_proj"], gl["router_scale"],
@@ -348,8 +348,8 @@ def test_forward_errors_and_edges(layer_default):
     # all-zero tokens: amax = 0 paths (inv = 0), output exactly zero
     blk.forward(0, x, out, 32)
     torch.cuda.synchronize()
-    assert not torch.isnan(out.float()).any()
-    assert (out.float() == 0).all()
+    assert not torch.isnan(out[:32].float()).any()
+    assert (out[:32].float() == 0).all()
 
 
 @pytest.mark.parametrize("degree", [2, 4])
