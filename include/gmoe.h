@@ -130,6 +130,23 @@ int gm_router_select(const void* x, const void* router_w, const void* router_sca
                      const void* per_expert_scale, int T, float* logits_ws, int32_t* route_idx,
                      float* route_w, void* stream);
 
+/* gm_router_select without the caller's scratch buffer, for callers that
+ * cannot allocate device memory (no cudaMalloc allowed where they run, fixed
+ * memory pools only, or a binding that cannot own device buffers).  No
+ * counterpart in the reference: its router scratch comes from the model's
+ * phase-scoped pool.  Same inputs and outputs as gm_router_select, minus
+ * logits_ws; the logits themselves are not returned.
+ * Limit: T <= 256 (GM_EINVAL beyond).  The scratch is a fixed 1.38 MiB array
+ * inside this library, present on every GPU that loads it until the process
+ * exits, and shared by all calls on that GPU: calls that overlap on the GPU
+ * race, so order them on one stream.  The first call on each device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device current;
+ * make that first call before any stream capture.  The call allocates
+ * nothing. */
+int gm_router_select_noalloc(const void* x, const void* router_w, const void* router_scale,
+                             const void* per_expert_scale, int T, int32_t* route_idx,
+                             float* route_w, void* stream);
+
 /* dispatch_build_expert_schedules (kernels/moe_router.mojo:109-145) for the
  * experts [expert_base, expert_base+epr): expert_offset i32 [epr+1], routes
  * [T*8] (stable, token-major).  Extra outputs: route_pos i32 [T*8] (position of

@@ -169,6 +169,10 @@ bool is_device_ptr(const void* p) {
 
 }  // namespace
 
+namespace gm {
+void set_thread_error(const char* msg) { g_tls_error = msg; }
+}  // namespace gm
+
 extern "C" {
 
 const char* gm_version(void) { return "gmoe 0.1 (sm_100a)"; }

@@ -25,6 +25,9 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// Records the text returned by gm_last_error(NULL) on the calling thread.
+void set_thread_error(const char* msg);
+
 int max_route_chunks(int T, int epr, int rc);
 int router_ksplit(int T);
 size_t router_workspace_floats(int T);

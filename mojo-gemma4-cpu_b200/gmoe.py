@@ -38,6 +38,7 @@ SIGNATURES = {
     "gm_moe_forward": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp]),
     "gm_moe_forward_sync": (_i32, [_vp, _i32, _vp, _vp, _i32]),
     "gm_router_select": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "gm_router_select_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),
     "gm_build_expert_schedules": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "gm_rms_norm": (_i32, [_vp, _vp, _i32, _vp, _vp]),
     "gm_bq_norm_quant": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
