@@ -108,6 +108,19 @@ int gm_moe_register_layer_bf16(gm_moe_t* h, int layer, const void* gate_up, cons
  * Asynchronous on `stream`; x and out are device pointers. */
 int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void* stream);
 
+/* Options (no reference counterpart: the reference picks its kernels at
+ * compile time).  GM_OPT_TC_MIN_TOKENS: calls with T >= value run the
+ * butterquant gate/up product on the tcgen05 grouped GEMM (prefill path),
+ * smaller calls on the HBM-streaming decode kernel; both give bit-identical
+ * results.  Default 1024. */
+#define GM_OPT_TC_MIN_TOKENS 1
+int gm_moe_set_option(gm_moe_t* h, int option, long value);
+
+/* Synchronises the handle's device and reports (then clears) the device-side
+ * error word that kernels with bounded waits write when a wait expires:
+ * *device_error = 0 and GM_OK when none did, GM_ETIMEOUT otherwise. */
+int gm_moe_device_status(gm_moe_t* h, int* device_error);
+
 /* Blocking form with the reference's calling convention (the reference's
  * dispatchers fan out and join before returning, kernels/helpers.mojo:295-327):
  * x and out may be host or device memory; host buffers are staged through the

@@ -1,0 +1,487 @@
+// gemm_tc.cu -- prefill gate/up expert product on the 5th-generation tensor
+// cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Same mathematics as bq_phase1_kernel (butterquant_kernels/moe.mojo:26-129
+// followed by the bucket FWHT-64 quantisation, linear.mojo:182-205), organised
+// for many routes per expert:
+//
+//   * A = the routed activation rows of one expert, in schedule order
+//     (gathered once per call into a contiguous [R][2816] int8 buffer so that a
+//     2-D TMA box covers 128 consecutive routes);
+//   * B = 64 gate rows + the matching 64 up rows of that expert, from a
+//     row-major (K-contiguous) int8 copy of the packed weights made at
+//     registration (gm_vnni_unpack: the VNNI tile order is a permutation);
+//   * D = 128 routes x 128 int32 columns in TMEM, exact signed dots
+//     (tcgen05.mma kind::i8, K = 32 per instruction, 22 blocks of 128 K bytes).
+//
+// Warp roles in a persistent CTA (one per SM): warp 0 issues TMA loads into a
+// 6-stage shared-memory ring, warp 1 allocates TMEM and issues the MMAs from
+// one elected thread, warps 2-5 drain the double-buffered accumulator
+// (tcgen05.ld, one TMEM lane = one route per thread) and run the epilogue in
+// registers: dequant (dot*(sa/127))*sw, GeGLU with the reference's gelu_tanh,
+// bf16 rounding, FWHT-64 of the thread's 64 bucket values, per-block absmax and
+// int8.  Output = bucket_i8/bucket_sa rows, bit-identical to the decode kernel.
+//
+// Every mbarrier wait is bounded (1 s of globaltimer); on expiry the kernel
+// records GM_ERR_TIMEOUT in *err, stops issuing work, still meets the final
+// barrier and frees its TMEM.
+#include <cuda.h>
+
+#include "gm_kernels.h"
+
+namespace gm {
+
+namespace tc {
+
+constexpr int BM = 128;            // routes per tile (TMEM lanes)
+constexpr int BN = 128;            // 64 gate + 64 up rows
+constexpr int BK = 128;            // K bytes per stage (one 128-byte swizzle row)
+constexpr int STAGES = 6;
+constexpr int KB1 = H / BK;        // 22 K blocks for gate/up
+constexpr int NJ1 = I / 64;        // 11 column tiles of 64 intermediate outputs
+constexpr int A_BYTES = BM * BK;   // 16 KB
+constexpr int B_BYTES = BN * BK;   // 16 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 256;  // two 128-column accumulators
+constexpr int ERR_TIMEOUT = 1;
+
+struct Smem {
+  uint8_t stage[STAGES][STAGE_BYTES];  // 1024-byte aligned (offset 0 of a 1024-aligned base)
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+  int failed;
+  int eoff[E + 1];   // expert_offset of this rank
+  int moff[E + 1];   // prefix of ceil(n_e / BM): m-tiles before expert e
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase with parity `parity` to complete.  Returns false
+// (and flags the CTA) after ~1 s.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* failed) {
+  const uint32_t a = smem_u32(b);
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (*(volatile int*)failed) return false;
+    if ((it & 63) == 0) {
+      const uint64_t t = global_ns();
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > 1000000000ull) {
+        atomicExch(failed, 1);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// K-major operand, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes
+// apart (SBO), version 1 (sm100), layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::i8, D = s32, A = B = signed int8, both K-major, N = 128, M = 128.
+constexpr uint32_t IDESC_I8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                              ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p; }"
+      ::"r"(d_tmem), "l"(da), "l"(db), "r"(IDESC_I8), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+struct TileInfo {
+  int e, row0, nvalid, nj;
+};
+
+// Tile t = (m-tile of an expert, column tile nj); m-tiles enumerated expert by
+// expert so that consecutive tiles reuse the same weights (L2-resident).
+__device__ __forceinline__ TileInfo tile_info(const Smem& s, int epr, int t) {
+  const int mg = t / NJ1;
+  TileInfo ti;
+  ti.nj = t % NJ1;
+  int lo = 0, hi = epr;  // s.moff[lo] <= mg < s.moff[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (s.moff[mid] <= mg) lo = mid; else hi = mid;
+  }
+  ti.e = lo;
+  ti.row0 = s.eoff[lo] + (mg - s.moff[lo]) * BM;
+  ti.nvalid = min(BM, s.eoff[lo + 1] - ti.row0);
+  return ti;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                 const int32_t* __restrict__ expert_offset, int epr,
+                 const float* __restrict__ xg_sa, const float* __restrict__ gu_scale,
+                 int8_t* __restrict__ bucket_i8, float* __restrict__ bucket_sa,
+                 uint16_t* __restrict__ bucket_bf16, int* __restrict__ err, int max_rows,
+                 int max_tiles) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 128);
+    }
+    s.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // m-tile prefix over this rank's experts (one warp scan, 4 experts per lane)
+  if (warp == 2) {
+    int c[4], sum = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = lane * 4 + j;
+      const int n = e < epr ? expert_offset[e + 1] - expert_offset[e] : 0;
+      c[j] = (n + BM - 1) / BM;
+      sum += c[j];
+    }
+    int inc = sum;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, inc, m);
+      if (lane >= m) inc += o;
+    }
+    int run = inc - sum;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = lane * 4 + j;
+      if (e < epr) {
+        s.moff[e] = run;
+        s.eoff[e] = expert_offset[e];
+      }
+      run += c[j];
+    }
+    if (lane == 31) {  // the end entries (e = epr, up to 128) are not covered above
+      s.moff[epr] = run;
+      s.eoff[epr] = expert_offset[epr];
+    }
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s.tmem_base)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem = s.tmem_base;
+  int total = s.moff[epr] * NJ1;
+  // Defensive bound: never more tiles than the route buffers can hold.
+  if (total < 0 || total > max_tiles || s.eoff[epr] > max_rows) {
+    if (tid == 0) atomicExch(err, 2);
+    total = 0;
+  }
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        const TileInfo ti = tile_info(s, epr, t);
+        const int brow_g = ti.e * GU + ti.nj * 64;
+        const int brow_u = ti.e * GU + I + ti.nj * 64;
+        for (int kb = 0; kb < KB1; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done;
+          uint8_t* st = s.stage[stage];
+          mbar_expect_tx(&s.full[stage], STAGE_BYTES);
+          tma_load_2d(st, &map_a, kb * BK, ti.row0, &s.full[stage]);
+          tma_load_2d(st + A_BYTES, &map_b, kb * BK, brow_g, &s.full[stage]);
+          tma_load_2d(st + A_BYTES + B_BYTES / 2, &map_b, kb * BK, brow_u, &s.full[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1, &s.failed)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < KB1; ++kb) {
+          if (!mbar_wait(&s.full[stage], phase, &s.failed)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(s.stage[stage]);
+          const uint32_t b0 = a0 + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk)
+            mma_i8(d, kmajor_sw128_desc(a0 + kk * 32), kmajor_sw128_desc(b0 + kk * 32),
+                   (kb | kk) != 0);
+          mma_commit(&s.empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&s.acc_full[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5, thread = TMEM lane = route row
+    const int quarter = warp & 3;           // TMEM lanes 32*quarter .. +31
+    const int r = quarter * 32 + lane;      // row inside the tile
+    const float inv127 = 1.0f / 127.0f;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const TileInfo ti = tile_info(s, epr, t);
+      // warp-uniform outcome: the tcgen05.ld below is .sync.aligned
+      if (!__all_sync(0xffffffffu, mbar_wait(&s.acc_full[acc], acc_phase, &s.failed))) break;
+      tc_fence_after();
+      const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      const bool valid = r < ti.nvalid;
+      const int row = ti.row0 + r;
+      const float ad = valid ? __fmul_rn(xg_sa[row], inv127) : 0.0f;
+      const float* wsg = gu_scale + (size_t)ti.e * GU + ti.nj * 64;
+      const float* wsu = wsg + I;
+      float hv[64];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        int gd[32], ud[32];
+        tmem_ld32(base + half * 32, gd);
+        tmem_ld32(base + 64 + half * 32, ud);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int col = half * 32 + c;
+          const float gv = __fmul_rn(__fmul_rn((float)gd[c], ad), __ldg(wsg + col));
+          const float uv = __fmul_rn(__fmul_rn((float)ud[c], ad), __ldg(wsu + col));
+          hv[col] = bf2f(f2bf(__fmul_rn(gelu_tanh_f32(gv), uv)));
+        }
+      }
+      // accumulator drained: hand it back to the MMA warp
+      tc_fence_before();
+      mbar_arrive(&s.acc_empty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+
+      if (valid) {
+        if (bucket_bf16) {
+          uint4* dst = reinterpret_cast<uint4*>(bucket_bf16 + (size_t)row * I + ti.nj * 64);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            uint32_t w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              w[u] = (uint32_t)f2bf(hv[v * 8 + 2 * u]) | ((uint32_t)f2bf(hv[v * 8 + 2 * u + 1]) << 16);
+            dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        // FWHT-64 in registers: stages stride 1..32, (a+b, a-b), then x0.125
+#pragma unroll
+        for (int st = 1; st < 64; st <<= 1)
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (!(i & st)) {
+              const float a = hv[i], b = hv[i + st];
+              hv[i] = __fadd_rn(a, b);
+              hv[i + st] = __fsub_rn(a, b);
+            }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          hv[i] = __fmul_rn(hv[i], fwht_scale_64());
+          amax = fmaxf(amax, fabsf(hv[i]));
+        }
+        const float qinv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        uint4* qdst = reinterpret_cast<uint4*>(bucket_i8 + (size_t)row * I + ti.nj * 64);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint32_t w[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint32_t p = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+              p |= (uint32_t)(quantize_i8(hv[v * 16 + u * 4 + b], qinv) & 0xFF) << (8 * b);
+            w[u] = p;
+          }
+          qdst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        bucket_sa[(size_t)row * NB_DOWN + ti.nj] = amax;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+  if (tid == 0 && s.failed) atomicExch(err, ERR_TIMEOUT);
+}
+
+// xg[pos] = x_i8[routes[pos].token], xg_sa[pos] = x_sa[token]: the routed
+// activation rows in schedule order (one warp per route).
+__global__ void __launch_bounds__(256)
+gather_rows_kernel(const int8_t* __restrict__ xi8, const float* __restrict__ xsa,
+                   const SparseRoute* __restrict__ routes, const int32_t* __restrict__ expert_offset,
+                   int epr, int8_t* __restrict__ xg, float* __restrict__ xg_sa) {
+  pdl_wait();
+  pdl_trigger();
+  const int R = expert_offset[epr];
+  const int lane = threadIdx.x & 31;
+  for (int pos = blockIdx.x * 8 + (threadIdx.x >> 5); pos < R; pos += gridDim.x * 8) {
+    const int tok = routes[pos].token;
+    const uint4* src = reinterpret_cast<const uint4*>(xi8 + (size_t)tok * H);
+    uint4* dst = reinterpret_cast<uint4*>(xg + (size_t)pos * H);
+    for (int c = lane; c < H / 16; c += 32) dst[c] = src[c];
+    if (lane == 0) xg_sa[pos] = xsa[tok];
+  }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------ host side
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+// 2-D int8 tensor map [rows][cols] with a box of box_rows x 128 bytes, 128-byte
+// swizzle, zero fill outside the tensor.
+bool make_tmap_i8(void* map, const void* base, long rows, int cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (cols % 16)) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols};
+  cuuint32_t box[2] = {(cuuint32_t)tc::BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(reinterpret_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t tmap_bytes() { return sizeof(CUtensorMap); }
+
+cudaError_t launch_gather_rows(const int8_t* xi8, const float* xsa, const SparseRoute* routes,
+                               const int32_t* expert_offset, int epr, int T, int8_t* xg,
+                               float* xg_sa, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const int rows = T * TOPK;
+  const int grid = std::min((rows + 7) / 8, 148 * 8);
+  return launch_k(tc::gather_rows_kernel, dim3(grid), dim3(256), 0, s, xi8, xsa, routes,
+                  expert_offset, epr, xg, xg_sa);
+}
+
+cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t* expert_offset,
+                             int epr, int T, const float* xg_sa, const float* gu_scale,
+                             int8_t* bucket_i8, float* bucket_sa, uint16_t* bucket_bf16, int* err,
+                             cudaStream_t s) {
+  const int max_rows = T * TOPK;
+  const int max_tiles = (max_rows / tc::BM + epr) * tc::NJ1;
+  const size_t smem = sizeof(tc::Smem) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(tc::tc_phase1_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return launch_k(tc::tc_phase1_kernel, dim3(sms), dim3(tc::THREADS), smem, s,
+                  *reinterpret_cast<const CUtensorMap*>(map_a),
+                  *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, xg_sa, gu_scale,
+                  bucket_i8, bucket_sa, bucket_bf16, err, max_rows, max_tiles);
+}
+
+}  // namespace gm

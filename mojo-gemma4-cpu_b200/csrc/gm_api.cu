@@ -27,6 +27,9 @@ struct Layer {
   uint16_t* rscale = nullptr;   // [H]
   uint16_t* pes = nullptr;      // [E]
   uint16_t* gamma2 = nullptr;   // [H]
+  int8_t* gu_rm = nullptr;      // bq: row-major copy of gate_up for the tcgen05 prefill path
+  alignas(64) unsigned char tmap_gu[128] = {};  // TMA descriptor over gu_rm (64-row boxes)
+  bool has_tc = false;
 };
 
 }  // namespace
@@ -56,6 +59,12 @@ struct gm_moe {
   float* ybuf = nullptr;
   uint16_t* x_stage = nullptr;
   uint16_t* out_stage = nullptr;
+  int8_t* xg = nullptr;         // routed activation rows in schedule order (tcgen05 A operand)
+  float* xg_sa = nullptr;
+  int* dev_err = nullptr;       // device-side error word (bounded waits that expired)
+  alignas(64) unsigned char tmap_xg[128] = {};
+  bool tc_ok = false;           // TMA descriptors available
+  int tc_min_tokens = 1024;     // GM_OPT_TC_MIN_TOKENS
   cudaStream_t own_stream = nullptr;
 };
 
@@ -101,7 +110,7 @@ struct Carve {
 
 struct WsLayout {
   size_t logits, inv_rms, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
-      x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, total;
+      x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, xg, xg_sa, dev_err, total;
 };
 
 WsLayout ws_layout(int max_tokens) {
@@ -127,6 +136,9 @@ WsLayout ws_layout(int max_tokens) {
   L.ybuf = c.take<float>(R * H);
   L.x_stage = c.take<uint16_t>(T * H);
   L.out_stage = c.take<uint16_t>(T * H);
+  L.xg = c.take<int8_t>(R * H);
+  L.xg_sa = c.take<float>(R);
+  L.dev_err = c.take<int>(1);
   L.total = align_up(c.off, 256);
   return L;
 }
@@ -145,7 +157,7 @@ int dev_copy(gm_moe* h, T** dst, const void* src, size_t count, const char* what
 
 void free_layer(Layer& L) {
   void* ptrs[] = {L.gu_q, L.gu_scale, L.dn_q, L.dn_scale, L.gu_bf16, L.dn_bf16,
-                  L.router, L.rscale, L.pes, L.gamma2};
+                  L.router, L.rscale, L.pes, L.gamma2, L.gu_rm};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   L = Layer{};
@@ -237,6 +249,11 @@ int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, in
   h->ybuf = reinterpret_cast<float*>(b + L.ybuf);
   h->x_stage = reinterpret_cast<uint16_t*>(b + L.x_stage);
   h->out_stage = reinterpret_cast<uint16_t*>(b + L.out_stage);
+  h->xg = reinterpret_cast<int8_t*>(b + L.xg);
+  h->xg_sa = reinterpret_cast<float*>(b + L.xg_sa);
+  h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
+  cudaMemset(h->dev_err, 0, sizeof(int));
+  h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)max_tokens * TOPK, H, 128);
   if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
     cudaFree(h->ws);
     delete h;
@@ -275,6 +292,12 @@ int gm_moe_register_layer_bq(gm_moe_t* h, int layer, const void* gate_up,
   if ((rc = dev_copy(h, &L.rscale, router_scale, (size_t)H, "router_scale"))) return rc;
   if ((rc = dev_copy(h, &L.pes, per_expert_scale, (size_t)E, "per_expert_scale"))) return rc;
   if ((rc = dev_copy(h, &L.gamma2, pre_ffn_norm_2, (size_t)H, "pre_ffn_norm_2"))) return rc;
+  // Row-major (K-contiguous) copy of gate_up for the tcgen05 prefill path: the
+  // VNNI tile order is a byte permutation, undone once here on the device.
+  GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.gu_rm), epr * GU * H), "gate_up row-major copy");
+  GM_TRY(h, launch_vnni_permute(L.gu_q, (long)(epr * GU), H, L.gu_rm, 1, h->own_stream), "vnni unpack");
+  GM_TRY(h, cudaStreamSynchronize(h->own_stream), "vnni unpack");
+  L.has_tc = make_tmap_i8(L.tmap_gu, L.gu_rm, (long)(epr * GU), H, 64);
   L.kind = 1;
   return GM_OK;
 }
@@ -323,9 +346,19 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
          "topk_schedule");
   // 4. experts, 5. combine
   if (L.kind == 1) {
-    GM_TRY(h, launch_bq_phase1(h->x_i8, h->x_sa, h->expert_offset, h->routes, h->chunk_off, h->epr,
-                               T, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
-           "bq_phase1");
+    if (L.has_tc && h->tc_ok && T >= h->tc_min_tokens) {
+      // prefill: routed rows gathered in schedule order, then the tcgen05 GEMM
+      GM_TRY(h, launch_gather_rows(h->x_i8, h->x_sa, h->routes, h->expert_offset, h->epr, T, h->xg,
+                                   h->xg_sa, s),
+             "gather_rows");
+      GM_TRY(h, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, T, h->xg_sa,
+                                 L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
+             "tc_phase1");
+    } else {
+      GM_TRY(h, launch_bq_phase1(h->x_i8, h->x_sa, h->expert_offset, h->routes, h->chunk_off,
+                                 h->epr, T, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
+             "bq_phase1");
+    }
     GM_TRY(h, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
                                h->chunk_off, h->epr, T, L.dn_q, L.dn_scale, h->ybuf, true, s),
            "bq_phase2");
@@ -339,6 +372,28 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
   }
   GM_TRY(h, launch_combine(h->route_idx, h->route_pos, h->ybuf, T, static_cast<uint16_t*>(out), s),
          "combine");
+  return GM_OK;
+}
+
+int gm_moe_set_option(gm_moe_t* h, int option, long value) {
+  if (!h) return set_err(nullptr, GM_EINVAL, "NULL handle");
+  switch (option) {
+    case GM_OPT_TC_MIN_TOKENS:
+      if (value < 1) return set_err(h, GM_EINVAL, "GM_OPT_TC_MIN_TOKENS must be >= 1");
+      h->tc_min_tokens = value > 0x7FFFFFFF ? 0x7FFFFFFF : (int)value;
+      return GM_OK;
+    default:
+      return set_err(h, GM_EINVAL, "unknown option %d", option);
+  }
+}
+
+int gm_moe_device_status(gm_moe_t* h, int* device_error) {
+  if (!h || !device_error) return set_err(h, GM_EINVAL, "NULL argument");
+  GM_TRY(h, cudaSetDevice(h->device), "device_status");
+  GM_TRY(h, cudaDeviceSynchronize(), "device_status");
+  GM_TRY(h, cudaMemcpy(device_error, h->dev_err, sizeof(int), cudaMemcpyDeviceToHost), "device_status");
+  GM_TRY(h, cudaMemset(h->dev_err, 0, sizeof(int)), "device_status");
+  if (*device_error) return set_err(h, GM_ETIMEOUT, "a kernel's bounded wait expired (code %d)", *device_error);
   return GM_OK;
 }
 

@@ -72,6 +72,17 @@ cudaError_t launch_bf16_phase2(const uint16_t* bucket, const int32_t* expert_off
                                const uint16_t* w_dn, float* ybuf, cudaStream_t s);
 cudaError_t launch_combine(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
                            int T, uint16_t* out, cudaStream_t s);
+// tcgen05 prefill path (gemm_tc.cu)
+bool make_tmap_i8(void* map, const void* base, long rows, int cols, int box_rows);
+size_t tmap_bytes();
+cudaError_t launch_gather_rows(const int8_t* xi8, const float* xsa, const SparseRoute* routes,
+                               const int32_t* expert_offset, int epr, int T, int8_t* xg,
+                               float* xg_sa, cudaStream_t s);
+cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t* expert_offset,
+                             int epr, int T, const float* xg_sa, const float* gu_scale,
+                             int8_t* bucket_i8, float* bucket_sa, uint16_t* bucket_bf16, int* err,
+                             cudaStream_t s);
+
 cudaError_t launch_quantize_rows(const uint16_t* w, long rows, int cols, const uint16_t* gamma,
                                  int block, int8_t* q, float* scale, cudaStream_t s);
 cudaError_t launch_vnni_permute(const int8_t* src, long rows, int cols, int8_t* dst, int dir,

@@ -37,6 +37,8 @@ SIGNATURES = {
     "gm_moe_register_layer_bf16": (_i32, [_vp, _i32] + [_vp] * 6),
     "gm_moe_forward": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp]),
     "gm_moe_forward_sync": (_i32, [_vp, _i32, _vp, _vp, _i32]),
+    "gm_moe_set_option": (_i32, [_vp, _i32, _i64]),
+    "gm_moe_device_status": (_i32, [_vp, C.POINTER(_i32)]),
     "gm_router_select": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "gm_router_select_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),
     "gm_build_expert_schedules": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
@@ -160,3 +162,15 @@ class MoeBlock:
     def forward_sync(self, layer, x, out, T):
         """Blocking; x/out may be host (e.g. pinned) or device buffers."""
         check(lib().gm_moe_forward_sync(self.h, layer, _addr(x), _addr(out), T), self.h)
+
+    def set_option(self, option, value):
+        check(lib().gm_moe_set_option(self.h, option, value), self.h)
+
+    def device_status(self):
+        """Synchronises; raises GmoeError(GM_ETIMEOUT) if a bounded wait expired."""
+        e = C.c_int(0)
+        check(lib().gm_moe_device_status(self.h, C.byref(e)), self.h)
+        return e.value
+
+
+OPT_TC_MIN_TOKENS = 1

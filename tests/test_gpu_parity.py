@@ -290,6 +290,24 @@ def test_forward_bq(T, which, layer_default, layer_stress):
         assert same.mean() > 0.95
 
 
+@pytest.mark.parametrize("T", [64, 300, 1100, 2048])
+def test_tc_prefill_path_bit_identical_to_decode_path(T, layer_stress):
+    """The tcgen05 grouped GEMM (prefill) and the HBM-streaming decode kernel
+    compute the same integer dots and the same epilogue: outputs must be equal
+    bit for bit, including experts with several 128-route tiles (T=2048)."""
+    raw, ref, g = layer_stress
+    blk = make_block(g, max_tokens=2048)
+    x = dev(tokens_np(T, seed=1000 + T))
+    outs = []
+    for thr in (1, 1 << 30):
+        blk.set_option(gmoe.OPT_TC_MIN_TOKENS, thr)
+        o = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        blk.forward(0, x, o, T)
+        outs.append(o)
+    assert blk.device_status() == 0
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+
+
 @pytest.mark.parametrize("T", [1, 16, 64])
 def test_forward_bf16(T, layer_default):
     raw, _, _ = layer_default
