@@ -395,6 +395,229 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   if (tid == 0 && s.failed) atomicExch(err, ERR_TIMEOUT);
 }
 
+// ---------------------------------------------------------------- phase 2
+// Down product with the reference's per-64-K-block dequantisation
+// (butterquant_kernels/moe.mojo:198-225): for every 64-wide K block b the MMA
+// warp writes the block's exact int32 dot into one of 4 TMEM regions (128
+// columns each); the epilogue threads (one route row each) fold it into
+// facc = fma(f32(dot_b), sa[b]/127, facc) in block order and release the
+// region, so the MMA warp runs up to 4 blocks ahead.  y = facc*sw*route_weight.
+constexpr int BN2 = 128;                  // hidden rows per tile
+constexpr int NT2 = H / BN2;              // 22 hidden tiles
+constexpr int KC2 = (I + BK - 1) / BK;    // 6 chunks of 128 K bytes (last half zero-filled)
+constexpr int RING = 4;
+constexpr uint32_t TMEM_COLS2 = RING * BN2;  // 512
+
+struct Smem2 {
+  uint8_t stage[STAGES][STAGE_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t reg_full[RING];
+  uint64_t reg_empty[RING];
+  uint32_t tmem_base;
+  int failed;
+  int eoff[E + 1];
+  int moff[E + 1];
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                 const int32_t* __restrict__ expert_offset, int epr,
+                 const float* __restrict__ bsa, const SparseRoute* __restrict__ routes,
+                 const float* __restrict__ dn_scale, float* __restrict__ ybuf,
+                 int* __restrict__ err, int max_rows, int max_tiles) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Smem2& s = *reinterpret_cast<Smem2*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < RING; ++i) {
+      mbar_init(&s.reg_full[i], 1);
+      mbar_init(&s.reg_empty[i], 128);
+    }
+    s.failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    int c[4], sum = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = lane * 4 + j;
+      const int n = e < epr ? expert_offset[e + 1] - expert_offset[e] : 0;
+      c[j] = (n + BM - 1) / BM;
+      sum += c[j];
+    }
+    int inc = sum;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, inc, m);
+      if (lane >= m) inc += o;
+    }
+    int run = inc - sum;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = lane * 4 + j;
+      if (e < epr) {
+        s.moff[e] = run;
+        s.eoff[e] = expert_offset[e];
+      }
+      run += c[j];
+    }
+    if (lane == 31) {
+      s.moff[epr] = run;
+      s.eoff[epr] = expert_offset[epr];
+    }
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s.tmem_base)),
+                 "r"(TMEM_COLS2));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tmem = s.tmem_base;
+  int total = s.moff[epr] * NT2;
+  if (total < 0 || total > max_tiles || s.eoff[epr] > max_rows) {
+    if (tid == 0) atomicExch(err, 2);
+    total = 0;
+  }
+
+  auto info = [&](int t, int& e, int& row0, int& nvalid, int& nt) {
+    const int mg = t / NT2;
+    nt = t % NT2;
+    int lo = 0, hi = epr;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (s.moff[mid] <= mg) lo = mid; else hi = mid;
+    }
+    e = lo;
+    row0 = s.eoff[lo] + (mg - s.moff[lo]) * BM;
+    nvalid = min(BM, s.eoff[lo + 1] - row0);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        int e, row0, nvalid, nt;
+        info(t, e, row0, nvalid, nt);
+        for (int c = 0; c < KC2; ++c) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done2;
+          uint8_t* st = s.stage[stage];
+          mbar_expect_tx(&s.full[stage], STAGE_BYTES);
+          tma_load_2d(st, &map_a, c * BK, row0, &s.full[stage]);
+          tma_load_2d(st + A_BYTES, &map_b, c * BK, e * H + nt * BN2, &s.full[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    producer_done2:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0, reg = 0;
+      uint32_t phase = 0, rphase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+        for (int c = 0; ok && c < KC2; ++c) {
+          if (!mbar_wait(&s.full[stage], phase, &s.failed)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(s.stage[stage]);
+          const uint32_t b0 = a0 + A_BYTES;
+          for (int h = 0; h < 2; ++h) {
+            if (2 * c + h >= NB_DOWN) break;  // K bytes 704..767 are padding
+            if (!mbar_wait(&s.reg_empty[reg], rphase ^ 1, &s.failed)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)(reg * BN2);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const uint32_t off = (uint32_t)((2 * h + kk) * 32);
+              mma_i8(d, kmajor_sw128_desc(a0 + off), kmajor_sw128_desc(b0 + off), kk);
+            }
+            mma_commit(&s.reg_full[reg]);
+            if (++reg == RING) { reg = 0; rphase ^= 1; }
+          }
+          if (!ok) break;
+          mma_commit(&s.empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const float inv127 = 1.0f / 127.0f;
+    int reg = 0;
+    uint32_t rphase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
+      int e, row0, nvalid, nt;
+      info(t, e, row0, nvalid, nt);
+      const bool valid = r < nvalid;
+      const int row = row0 + r;
+      float adv[NB_DOWN];
+#pragma unroll
+      for (int b = 0; b < NB_DOWN; ++b)
+        adv[b] = valid ? __fmul_rn(bsa[(size_t)row * NB_DOWN + b], inv127) : 0.0f;
+      float facc[BN2];
+#pragma unroll
+      for (int n = 0; n < BN2; ++n) facc[n] = 0.0f;
+      for (int b = 0; b < NB_DOWN; ++b) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s.reg_full[reg], rphase, &s.failed))) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(reg * BN2);
+        float a = adv[0];
+#pragma unroll
+        for (int bb = 1; bb < NB_DOWN; ++bb)
+          if (bb == b) a = adv[bb];
+#pragma unroll
+        for (int q = 0; q < BN2 / 32; ++q) {
+          int d[32];
+          tmem_ld32(base + q * 32, d);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) facc[q * 32 + i] = __fmaf_rn((float)d[i], a, facc[q * 32 + i]);
+        }
+        tc_fence_before();
+        mbar_arrive(&s.reg_empty[reg]);
+        if (++reg == RING) { reg = 0; rphase ^= 1; }
+      }
+      if (!ok) break;
+      if (valid) {
+        const float wr = routes[row].weight;
+        const float* wsc = dn_scale + (size_t)e * H + nt * BN2;
+        float4* dst = reinterpret_cast<float4*>(ybuf + (size_t)row * H + nt * BN2);
+#pragma unroll
+        for (int v = 0; v < BN2 / 4; ++v) {
+          float4 o;
+          o.x = __fmul_rn(__fmul_rn(facc[4 * v + 0], __ldg(wsc + 4 * v + 0)), wr);
+          o.y = __fmul_rn(__fmul_rn(facc[4 * v + 1], __ldg(wsc + 4 * v + 1)), wr);
+          o.z = __fmul_rn(__fmul_rn(facc[4 * v + 2], __ldg(wsc + 4 * v + 2)), wr);
+          o.w = __fmul_rn(__fmul_rn(facc[4 * v + 3], __ldg(wsc + 4 * v + 3)), wr);
+          dst[v] = o;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS2));
+  }
+  if (tid == 0 && s.failed) atomicExch(err, ERR_TIMEOUT);
+}
+
 // xg[pos] = x_i8[routes[pos].token], xg_sa[pos] = x_sa[token]: the routed
 // activation rows in schedule order (one warp per route).
 __global__ void __launch_bounds__(256)
@@ -482,6 +705,24 @@ cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t
                   *reinterpret_cast<const CUtensorMap*>(map_a),
                   *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, xg_sa, gu_scale,
                   bucket_i8, bucket_sa, bucket_bf16, err, max_rows, max_tiles);
+}
+
+cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
+                             int epr, int T, const float* bsa, const SparseRoute* routes,
+                             const float* dn_scale, float* ybuf, int* err, cudaStream_t s) {
+  const int max_rows = T * TOPK;
+  const int max_tiles = (max_rows / tc::BM + epr) * tc::NT2;
+  const size_t smem = sizeof(tc::Smem2) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(tc::tc_phase2_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return launch_k(tc::tc_phase2_kernel, dim3(sms), dim3(tc::THREADS), smem, s,
+                  *reinterpret_cast<const CUtensorMap*>(map_a),
+                  *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, bsa, routes,
+                  dn_scale, ybuf, err, max_rows, max_tiles);
 }
 
 }  // namespace gm

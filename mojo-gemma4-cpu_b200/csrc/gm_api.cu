@@ -27,8 +27,10 @@ struct Layer {
   uint16_t* rscale = nullptr;   // [H]
   uint16_t* pes = nullptr;      // [E]
   uint16_t* gamma2 = nullptr;   // [H]
-  int8_t* gu_rm = nullptr;      // bq: row-major copy of gate_up for the tcgen05 prefill path
+  int8_t* gu_rm = nullptr;      // bq: row-major copies for the tcgen05 prefill path
+  int8_t* dn_rm = nullptr;
   alignas(64) unsigned char tmap_gu[128] = {};  // TMA descriptor over gu_rm (64-row boxes)
+  alignas(64) unsigned char tmap_dn[128] = {};  // TMA descriptor over dn_rm (128-row boxes)
   bool has_tc = false;
 };
 
@@ -63,6 +65,7 @@ struct gm_moe {
   float* xg_sa = nullptr;
   int* dev_err = nullptr;       // device-side error word (bounded waits that expired)
   alignas(64) unsigned char tmap_xg[128] = {};
+  alignas(64) unsigned char tmap_bucket[128] = {};
   bool tc_ok = false;           // TMA descriptors available
   int tc_min_tokens = 1024;     // GM_OPT_TC_MIN_TOKENS
   cudaStream_t own_stream = nullptr;
@@ -157,7 +160,7 @@ int dev_copy(gm_moe* h, T** dst, const void* src, size_t count, const char* what
 
 void free_layer(Layer& L) {
   void* ptrs[] = {L.gu_q, L.gu_scale, L.dn_q, L.dn_scale, L.gu_bf16, L.dn_bf16,
-                  L.router, L.rscale, L.pes, L.gamma2, L.gu_rm};
+                  L.router, L.rscale, L.pes, L.gamma2, L.gu_rm, L.dn_rm};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   L = Layer{};
@@ -253,7 +256,8 @@ int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, in
   h->xg_sa = reinterpret_cast<float*>(b + L.xg_sa);
   h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
   cudaMemset(h->dev_err, 0, sizeof(int));
-  h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)max_tokens * TOPK, H, 128);
+  h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)max_tokens * TOPK, H, 128) &&
+             make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)max_tokens * TOPK, I, 128);
   if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
     cudaFree(h->ws);
     delete h;
@@ -296,8 +300,11 @@ int gm_moe_register_layer_bq(gm_moe_t* h, int layer, const void* gate_up,
   // VNNI tile order is a byte permutation, undone once here on the device.
   GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.gu_rm), epr * GU * H), "gate_up row-major copy");
   GM_TRY(h, launch_vnni_permute(L.gu_q, (long)(epr * GU), H, L.gu_rm, 1, h->own_stream), "vnni unpack");
+  GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.dn_rm), epr * H * I), "down row-major copy");
+  GM_TRY(h, launch_vnni_permute(L.dn_q, (long)(epr * H), I, L.dn_rm, 1, h->own_stream), "vnni unpack");
   GM_TRY(h, cudaStreamSynchronize(h->own_stream), "vnni unpack");
-  L.has_tc = make_tmap_i8(L.tmap_gu, L.gu_rm, (long)(epr * GU), H, 64);
+  L.has_tc = make_tmap_i8(L.tmap_gu, L.gu_rm, (long)(epr * GU), H, 64) &&
+             make_tmap_i8(L.tmap_dn, L.dn_rm, (long)(epr * H), I, 128);
   L.kind = 1;
   return GM_OK;
 }
@@ -354,14 +361,17 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
       GM_TRY(h, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, T, h->xg_sa,
                                  L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
              "tc_phase1");
+      GM_TRY(h, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, T,
+                                 h->bucket_sa, h->routes, L.dn_scale, h->ybuf, h->dev_err, s),
+             "tc_phase2");
     } else {
       GM_TRY(h, launch_bq_phase1(h->x_i8, h->x_sa, h->expert_offset, h->routes, h->chunk_off,
                                  h->epr, T, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
              "bq_phase1");
+      GM_TRY(h, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
+                                 h->chunk_off, h->epr, T, L.dn_q, L.dn_scale, h->ybuf, true, s),
+             "bq_phase2");
     }
-    GM_TRY(h, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
-                               h->chunk_off, h->epr, T, L.dn_q, L.dn_scale, h->ybuf, true, s),
-           "bq_phase2");
   } else {
     GM_TRY(h, launch_bf16_phase1(h->x_normed, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
                                  L.gu_bf16, h->bucket, s),

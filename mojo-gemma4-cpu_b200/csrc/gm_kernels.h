@@ -82,6 +82,9 @@ cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t
                              int epr, int T, const float* xg_sa, const float* gu_scale,
                              int8_t* bucket_i8, float* bucket_sa, uint16_t* bucket_bf16, int* err,
                              cudaStream_t s);
+cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
+                             int epr, int T, const float* bsa, const SparseRoute* routes,
+                             const float* dn_scale, float* ybuf, int* err, cudaStream_t s);
 
 cudaError_t launch_quantize_rows(const uint16_t* w, long rows, int cols, const uint16_t* gamma,
                                  int block, int8_t* q, float* scale, cudaStream_t s);
