@@ -248,11 +248,13 @@ def main():
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
+        blk.profile(False)           # profiler off; zeroes the handle's kernel launch count
         ev0.record(stream)
         for i in range(args.steps):
             step(i)
         ev1.record(stream)
         torch.cuda.synchronize()
+        _, timed_launches = blk.profile_read()
     ms = ev0.elapsed_time(ev1)
     if dist:
         t = torch.tensor([ms], device="cuda")
@@ -278,9 +280,9 @@ def main():
         e2e_s = float(t.item())
     e2e = world * T * args.steps / e2e_s
 
-    # ---- roofline of the dominant kernel (expert phase 1), CUDA events on the
-    # launching stream around the same per-stage entry points the forward uses
-    roof = roofline(blk, fmt, L, xs, T, args.steps, stream)
+    # ---- roofline of the dominant kernel: CUDA events on the forward's stream
+    # around each stage of the same forward (handle's stage profiler)
+    roof = roofline(blk, fmt, L, xs, outs, T, args.steps, stream, args.workload)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -293,7 +295,7 @@ def main():
                          % (len(xs), roof.get("weight_mb", 0))},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2},
-        "gpu_launches": 7 * args.steps,
+        "gpu_launches": timed_launches,
         "roofline": {k: roof[k] for k in ("bound", "achieved", "peak", "unit", "frac", "traffic")},
         "roofline_detail": roof["detail"],
         "clocks": clk.summary(),
@@ -326,78 +328,119 @@ def cpu_leg(fmt, T, args, raw_dev):
                       % (iters, T, args.cpu_seconds)}
 
 
-def roofline(blk, fmt, L, xs, T, steps, stream):
-    """Time the dominant kernel (phase 1 gate/up) per launch with CUDA events
-    on its stream, over `steps` launches on the same inputs the forward uses."""
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of
+# the dominant kernel, from the ncu captures summarised under profiles/
+# (bq_decode_b64.md, tc_prefill_4k.md); None where no capture of the current
+# kernel exists.
+NCU_TRAFFIC = {
+    ("bq-decode-b64", "bq_phase1_gate_up"): 500_506_880 + 4_189_184,
+}
+
+
+def stage_model(label, fmt, T, distinct):
+    """(bound, algorithmic bytes or FLOPs per launch) of one forward stage.
+    Bytes count every operand once: routed expert weights (distinct experts
+    x bytes per expert), activations read, results written."""
+    R = T * TOPK
+    ksplit = H // 256
+    if label == "bq_phase1_gate_up":
+        return "hbm", distinct * BQ_EXPERT_GU_BYTES + T * H + T * 4 + R * (I + 11 * 4)
+    if label == "bq_phase2_down":
+        return "hbm", distinct * BQ_EXPERT_DN_BYTES + R * (I + 11 * 4) + R * H * 4
+    if label in ("bq_phase1_gate_up.tc",):
+        return "tensor", 2.0 * R * GU * H
+    if label in ("bq_phase2_down.tc",):
+        return "tensor", 2.0 * R * H * I
+    if label == "phase1_gate_up":
+        if T >= 1024:
+            return "tensor", 2.0 * R * GU * H
+        return "hbm", distinct * GU * H * 2 + T * H * 2 + R * I * 2
+    if label == "phase2_down":
+        if T >= 1024:
+            return "tensor", 2.0 * R * H * I
+        return "hbm", distinct * H * I * 2 + R * I * 2 + R * H * 4
+    if label == "router_expert":
+        return "hbm", E * H * 2 + T * H * 2 + H * 2 + T * 4 + ksplit * T * E * 4
+    if label == "router_merge.schedule":
+        return "hbm", ksplit * T * E * 4 + R * (4 + 4 + 8 + 4)
+    if label in ("bq_norm_quant",):
+        return "hbm", T * H * 2 + H * 2 + T * H + T * 8
+    if label in ("rms_norm",):
+        return "hbm", T * H * 2 + H * 2 + T * H * 2 + T * 4
+    if label == "gather_rows":
+        return "hbm", R * (H + 4) * 2 + R * 8
+    if label == "combine":
+        return "hbm", R * H * 4 + T * H * 2 + R * 8
+    return "hbm", None
+
+
+def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload):
+    """Per-stage device times of the forward itself: the handle's stage
+    profiler (GM_OPT_PROFILE) records CUDA events on the forward's stream
+    around every stage; L2 is flushed (256 MB write) before each profiled
+    forward.  The dominant stage (largest share of the step) is reported
+    against its roofline; every stage is listed in the detail."""
     import torch
     import gmoe
     hbm, tf, src = peaks()
-    x = xs[0]
+    s = stream
+    # distinct experts each batch routes to (the weight bytes a launch must read)
     lg = torch.empty(gmoe.lib().gm_router_workspace_bytes(T) // 4, dtype=torch.float32, device="cuda")
     idx = torch.empty(T, TOPK, dtype=torch.int32, device="cuda")
     w = torch.empty(T, TOPK, dtype=torch.float32, device="cuda")
-    off = torch.empty(E + 1, dtype=torch.int32, device="cuda")
-    routes = torch.empty(T * TOPK, 2, dtype=torch.int32, device="cuda")
-    pos = torch.empty(T * TOPK, dtype=torch.int32, device="cuda")
-    chunk = torch.empty(E + 1, dtype=torch.int32, device="cuda")
-    R = T * TOPK
-    s = stream
-    if fmt == "bq":
-        gmoe.call("gm_router_select", x, L["router_centered"], L["router_scale"], L["per_expert_scale"],
-                  T, lg, idx, w, s)
-        gmoe.call("gm_build_expert_schedules", idx, w, T, 0, E, 16, off, routes, pos, chunk, s)
-        xq = torch.empty(T, H, dtype=torch.int8, device="cuda")
-        xsa = torch.empty(T, dtype=torch.float32, device="cuda")
-        gmoe.call("gm_bq_norm_quant", x, L["pre_ffn_norm_2"], T, xq, xsa, s)
-        bq = torch.empty(R, I, dtype=torch.int8, device="cuda")
-        bsa = torch.empty(R, 11, dtype=torch.float32, device="cuda")
-
-        def launch():
-            gmoe.call("gm_bq_phase1_gate_up", xq, xsa, off, routes, chunk, E, T, L["gate_up"],
-                      L["gate_up_scale"], bq, bsa, None, s)
-        per_expert = BQ_EXPERT_GU_BYTES
-    else:
-        gmoe.call("gm_router_select", x, L["router_proj"], L["router_scale"], L["per_expert_scale"],
-                  T, lg, idx, w, s)
-        gmoe.call("gm_build_expert_schedules", idx, w, T, 0, E, 8, off, routes, pos, chunk, s)
-        xn = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
-        gmoe.call("gm_rms_norm", x, L["pre_ffn_norm_2"], T, xn, s)
-        bucket = torch.empty(R, I, dtype=torch.bfloat16, device="cuda")
-
-        def launch():
-            gmoe.call("gm_phase1_gate_up_bf16", xn, off, routes, chunk, E, T, L["gate_up"], bucket, s)
-        per_expert = GU * H * 2
+    rw = L["router_centered"] if fmt == "bq" else L["router_proj"]
+    distinct = []
+    for x in xs:
+        gmoe.call("gm_router_select", x, rw, L["router_scale"], L["per_expert_scale"], T, lg, idx, w, s)
+        distinct.append(int(torch.unique(idx).numel()))
     torch.cuda.synchronize()
-    distinct = int(torch.unique(idx).numel())
-    for _ in range(3):
-        launch()
-    # flush L2 between timed launches: 256 MB write (> 126 MB L2)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
-    tot = 0.0
     n = max(5, min(steps, 50))
-    for _ in range(n):
+    blk.profile(True)
+    for i in range(n):
         flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(s)
-        launch()
-        b.record(s)
-        b.synchronize()
-        tot += a.elapsed_time(b)
-    avg_ms = tot / n
-    if T >= 1024:
-        flops = 2.0 * T * TOPK * GU * H
-        ach = flops / (avg_ms / 1e3) / 1e12
-        return {"bound": "tensor", "achieved": ach, "peak": tf, "unit": "TFLOP/s", "frac": ach / tf,
-                "traffic": None, "weight_mb": distinct * per_expert / 1e6,
-                "detail": {"kernel": "phase1_gate_up", "avg_launch_us": avg_ms * 1e3,
-                           "flop_per_launch": flops, "peak_source": src + " (bf16 burst)"}}
-    algo = distinct * per_expert + T * H + T * 4 + R * (I + 11 * 4)
-    ach = algo / (avg_ms / 1e3) / 1e9
-    return {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
-            "traffic": None, "weight_mb": distinct * per_expert / 1e6,
-            "detail": {"kernel": "phase1_gate_up", "avg_launch_us": avg_ms * 1e3,
-                       "distinct_experts": distinct, "bytes_per_launch": algo,
-                       "bytes_per_expert": per_expert, "peak_source": src + " (hbm copy)"}}
+        blk.forward(0, xs[i % len(xs)], outs[i % len(xs)], T, s)
+    torch.cuda.synchronize()
+    stats, launches = blk.profile_read()
+    blk.profile(False)
+    mean_distinct = sum(distinct[i % len(xs)] for i in range(n)) / n
+    step_ms = sum(v["avg_ms"] for v in stats.values())
+    stages = {}
+    for label, v in stats.items():
+        bound, amount = stage_model(label, fmt, T, mean_distinct)
+        e = {"avg_us": round(v["avg_ms"] * 1e3, 2), "share": round(v["avg_ms"] / step_ms, 4),
+             "kernels_per_call": v["kernels"] / max(v["calls"], 1)}
+        if amount is not None:
+            sec = v["avg_ms"] / 1e3
+            if bound == "tensor":
+                e["tflops"] = round(amount / sec / 1e12, 1)
+                e["frac"] = round(amount / sec / 1e12 / tf, 3)
+            else:
+                e["gbs"] = round(amount / sec / 1e9, 1)
+                e["frac"] = round(amount / sec / 1e9 / hbm, 3)
+        stages[label] = e
+    top = max(stats, key=lambda k: stats[k]["avg_ms"])
+    bound, amount = stage_model(top, fmt, T, mean_distinct)
+    sec = stats[top]["avg_ms"] / 1e3
+    traffic = NCU_TRAFFIC.get((workload, top))
+    detail = {"kernel": top, "avg_launch_us": stats[top]["avg_ms"] * 1e3, "launches_timed": n,
+              "distinct_experts": mean_distinct, "stages": stages,
+              "kernels_per_forward": launches / n}
+    if bound == "tensor":
+        ach = amount / sec / 1e12
+        detail.update({"flop_per_launch": amount, "peak_source": src + " (bf16 dense, burst)"})
+        roof = {"bound": "tensor", "achieved": ach, "peak": tf, "unit": "TFLOP/s", "frac": ach / tf}
+    else:
+        ach = amount / sec / 1e9
+        per_expert = {"bq_phase1_gate_up": BQ_EXPERT_GU_BYTES, "bq_phase2_down": BQ_EXPERT_DN_BYTES,
+                      "phase1_gate_up": GU * H * 2, "phase2_down": H * I * 2}.get(top, 0)
+        detail.update({"bytes_per_launch": amount, "bytes_per_expert": per_expert,
+                       "peak_source": src + " (hbm copy)"})
+        roof = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm}
+    roof["traffic"] = traffic
+    roof["detail"] = detail
+    roof["weight_mb"] = mean_distinct * (BQ_EXPERT_BYTES if fmt == "bq" else BF16_EXPERT_BYTES) / 1e6
+    return roof
 
 
 if __name__ == "__main__":

@@ -112,9 +112,35 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
  * compile time).  GM_OPT_TC_MIN_TOKENS: calls with T >= value run the
  * butterquant gate/up product on the tcgen05 grouped GEMM (prefill path),
  * smaller calls on the HBM-streaming decode kernel; both give bit-identical
- * results.  Default 1024. */
+ * results.  Default 1024.
+ * GM_OPT_PROFILE: 1 records a CUDA event pair around every stage that
+ * gm_moe_forward launches, 0 (default) records none; setting it (either
+ * value) clears the stage statistics and the kernel launch count. */
 #define GM_OPT_TC_MIN_TOKENS 1
+#define GM_OPT_PROFILE 2
 int gm_moe_set_option(gm_moe_t* h, int option, long value);
+
+/* Per-stage statistics of the handle's forwards.  Replaces the reference's
+ * Profiler / DispatchSpan (kernels/profiling.mojo:214-254, 366-413): one
+ * record per stage label (the reference's dispatch labels where a stage has
+ * one: "bq_norm_quant", "router_expert", "bq_phase1_gate_up",
+ * "bq_phase2_down", ...; tcgen05 variants carry a ".tc" suffix), with the
+ * device time between the events recorded on the forward's stream before and
+ * after the stage's launches. */
+typedef struct gm_stage_stat {
+  char label[32];
+  long calls;       /* stage executions recorded */
+  long kernels;     /* kernels the stage launched over those executions */
+  double total_ms, min_ms, max_ms;
+} gm_stage_stat_t;
+
+/* Waits for the recorded events, folds them into the statistics and copies up
+ * to max_stats records (first-seen order) into `stats`; *n_stats = number of
+ * records.  *kernel_launches (may be NULL) = kernels gm_moe_forward launched
+ * on this handle since creation or the last GM_OPT_PROFILE setting, counted
+ * whether or not profiling is on. */
+int gm_moe_profile_read(gm_moe_t* h, gm_stage_stat_t* stats, int max_stats, int* n_stats,
+                        long* kernel_launches);
 
 /* Synchronises the handle's device and reports (then clears) the device-side
  * error word that kernels with bounded waits write when a wait expires:

@@ -1,26 +1,31 @@
-// gemm_tc.cu -- prefill gate/up expert product on the 5th-generation tensor
-// cores (tcgen05 + TMEM + TMA), sm_100a.
+// gemm_tc.cu -- prefill expert products on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), sm_100a.
 //
-// Same mathematics as bq_phase1_kernel (butterquant_kernels/moe.mojo:26-129
-// followed by the bucket FWHT-64 quantisation, linear.mojo:182-205), organised
-// for many routes per expert:
+// Same mathematics as the decode kernels of experts_bq.cu, organised for many
+// routes per expert:
 //
-//   * A = the routed activation rows of one expert, in schedule order
-//     (gathered once per call into a contiguous [R][2816] int8 buffer so that a
-//     2-D TMA box covers 128 consecutive routes);
-//   * B = 64 gate rows + the matching 64 up rows of that expert, from a
-//     row-major (K-contiguous) int8 copy of the packed weights made at
-//     registration (gm_vnni_unpack: the VNNI tile order is a permutation);
-//   * D = 128 routes x 128 int32 columns in TMEM, exact signed dots
-//     (tcgen05.mma kind::i8, K = 32 per instruction, 22 blocks of 128 K bytes).
+//  * phase 1 (butterquant_kernels/moe.mojo:26-129, then the bucket FWHT-64
+//    quantisation of linear.mojo:182-205): A = the routed activation rows of
+//    one expert in schedule order (gathered once per call into a contiguous
+//    [R][2816] int8 buffer so that a 2-D TMA box covers 128 routes), B = 64 gate
+//    rows + the matching 64 up rows from a row-major (K-contiguous) int8 copy of
+//    the packed weights (gm_vnni_unpack: the VNNI tile order is a permutation),
+//    D = 128 routes x 128 int32 columns in TMEM, exact signed dots
+//    (tcgen05.mma kind::i8, K = 32 per instruction, 22 stages of 128 K bytes).
+//  * phase 2 (butterquant_kernels/moe.mojo:168-225): the down product with the
+//    reference's per-64-K-block dequantisation; each K block's exact int32 dot
+//    goes to one of 4 TMEM regions (128 columns), the epilogue folds it into
+//    facc = fma(f32(dot_b), sa[b]/127, facc) in block order and frees the
+//    region, so the MMA warp runs up to 4 blocks ahead.  y = facc*sw*w_route.
 //
-// Warp roles in a persistent CTA (one per SM): warp 0 issues TMA loads into a
-// 6-stage shared-memory ring, warp 1 allocates TMEM and issues the MMAs from
-// one elected thread, warps 2-5 drain the double-buffered accumulator
-// (tcgen05.ld, one TMEM lane = one route per thread) and run the epilogue in
-// registers: dequant (dot*(sa/127))*sw, GeGLU with the reference's gelu_tanh,
-// bf16 rounding, FWHT-64 of the thread's 64 bucket values, per-block absmax and
-// int8.  Output = bucket_i8/bucket_sa rows, bit-identical to the decode kernel.
+// Persistent CTAs (one per SM), warp-specialised: warp 0 issues TMA loads into
+// a shared-memory ring, warp 1 allocates TMEM and issues the MMAs from one
+// thread, warps 2..17 are the epilogue: 4 warps per TMEM lane quarter (one
+// route row per thread), each owning a quarter of the tile's columns.  In
+// phase 1 the FWHT-64 stages of stride 16 and 32 and the row absmax cross
+// those column blocks through shared memory (named barrier per quarter); in
+// phase 2 the f32 output rows are staged in shared memory and written with
+// whole-row coalesced stores.
 //
 // Every mbarrier wait is bounded (1 s of globaltimer); on expiry the kernel
 // records GM_ERR_TIMEOUT in *err, stops issuing work, still meets the final
@@ -34,28 +39,55 @@ namespace gm {
 namespace tc {
 
 constexpr int BM = 128;            // routes per tile (TMEM lanes)
-constexpr int BN = 128;            // 64 gate + 64 up rows
+constexpr int BN = 128;            // phase 1: 64 gate + 64 up rows; phase 2: 128 hidden rows
 constexpr int BK = 128;            // K bytes per stage (one 128-byte swizzle row)
-constexpr int STAGES = 6;
-constexpr int KB1 = H / BK;        // 22 K blocks for gate/up
+constexpr int KB1 = H / BK;        // 22 K stages for gate/up
 constexpr int NJ1 = I / 64;        // 11 column tiles of 64 intermediate outputs
+constexpr int NT2 = H / BN;        // 22 hidden tiles
+constexpr int KC2 = (I + BK - 1) / BK;  // 6 K stages of 128 bytes (last half zero-filled)
 constexpr int A_BYTES = BM * BK;   // 16 KB
 constexpr int B_BYTES = BN * BK;   // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 256;  // two 128-column accumulators
+constexpr int STAGES1 = 5;
+constexpr int STAGES2 = 4;
+constexpr int RING = 4;            // phase-2 TMEM regions
+constexpr int EPI_WARPS = 16;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;  // 576
+constexpr int EPI_THREADS = 32 * EPI_WARPS;
+constexpr uint32_t TMEM_COLS1 = 256;         // two 128-column accumulators
+constexpr uint32_t TMEM_COLS2 = RING * BN;   // 512
+constexpr int XSTR = 64 + 4;       // phase-1 exchange row stride (floats)
+constexpr int YSTR = BN + 4;       // phase-2 output staging row stride (floats)
 constexpr int ERR_TIMEOUT = 1;
 
-struct Smem {
-  uint8_t stage[STAGES][STAGE_BYTES];  // 1024-byte aligned (offset 0 of a 1024-aligned base)
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+struct TileTable {
+  int eoff[E + 1];   // expert_offset of this rank
+  int moff[E + 1];   // prefix of ceil(n_e / BM): m-tiles before expert e
+};
+
+struct Smem1 {
+  uint8_t stage[STAGES1][STAGE_BYTES];  // first member: 1024-byte aligned
+  float xbuf[BM][XSTR];
+  float amax[BM][4];
+  uint64_t full[STAGES1];
+  uint64_t empty[STAGES1];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint32_t tmem_base;
   int failed;
-  int eoff[E + 1];   // expert_offset of this rank
-  int moff[E + 1];   // prefix of ceil(n_e / BM): m-tiles before expert e
+  TileTable tt;
+};
+
+struct Smem2 {
+  uint8_t stage[STAGES2][STAGE_BYTES];
+  float ystage[BM][YSTR];
+  uint64_t full[STAGES2];
+  uint64_t empty[STAGES2];
+  uint64_t reg_full[RING];
+  uint64_t reg_empty[RING];
+  uint32_t tmem_base;
+  int failed;
+  TileTable tt;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -106,6 +138,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* fai
   }
 }
 
+// Named barrier for the 4 epilogue warps of one TMEM lane quarter.
+__device__ __forceinline__ void quarter_sync(int q) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + q) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
   asm volatile(
@@ -142,6 +179,15 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -155,25 +201,91 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&r)[32]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Packed two-lane f32 arithmetic of sm_100 (one instruction, two IEEE
+// round-to-nearest results; identical to the scalar operations).
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 c;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(c))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return c;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 c;
+  asm("mul.rn.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(c))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return c;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
+        "l"(reinterpret_cast<const uint64_t&>(c)));
+  return d;
+}
+
+// Exact int32 -> f32 for |d| < 2^22 (the 64-wide down-block dots are < 2^21):
+// 1.5*2^23 + d is representable, so its bits are those of 0x4B400000 + d, and
+// subtracting 1.5*2^23 is exact.  Two lanes at a time.
+__device__ __forceinline__ float2 small_ints_to_float2(int d0, int d1) {
+  const float2 biased = make_float2(__int_as_float(0x4B400000 + d0), __int_as_float(0x4B400000 + d1));
+  return add2(biased, make_float2(-12582912.0f, -12582912.0f));
+}
+
 struct TileInfo {
-  int e, row0, nvalid, nj;
+  int e, row0, nvalid, col;
 };
 
-// Tile t = (m-tile of an expert, column tile nj); m-tiles enumerated expert by
+// Tile t = (m-tile of an expert, column tile); m-tiles enumerated expert by
 // expert so that consecutive tiles reuse the same weights (L2-resident).
-__device__ __forceinline__ TileInfo tile_info(const Smem& s, int epr, int t) {
-  const int mg = t / NJ1;
+__device__ __forceinline__ TileInfo tile_info(const TileTable& tt, int epr, int ncol, int t) {
+  const int mg = t / ncol;
   TileInfo ti;
-  ti.nj = t % NJ1;
-  int lo = 0, hi = epr;  // s.moff[lo] <= mg < s.moff[hi]
+  ti.col = t % ncol;
+  int lo = 0, hi = epr;  // tt.moff[lo] <= mg < tt.moff[hi]
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (s.moff[mid] <= mg) lo = mid; else hi = mid;
+    if (tt.moff[mid] <= mg) lo = mid; else hi = mid;
   }
   ti.e = lo;
-  ti.row0 = s.eoff[lo] + (mg - s.moff[lo]) * BM;
-  ti.nvalid = min(BM, s.eoff[lo + 1] - ti.row0);
+  ti.row0 = tt.eoff[lo] + (mg - tt.moff[lo]) * BM;
+  ti.nvalid = min(BM, tt.eoff[lo + 1] - ti.row0);
   return ti;
+}
+
+// m-tile prefix over this rank's experts (one warp, 4 experts per lane).
+__device__ __forceinline__ void build_tile_table(TileTable& tt, const int32_t* expert_offset, int epr,
+                                                 int lane) {
+  int c[4], sum = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int e = lane * 4 + j;
+    const int n = e < epr ? expert_offset[e + 1] - expert_offset[e] : 0;
+    c[j] = (n + BM - 1) / BM;
+    sum += c[j];
+  }
+  int inc = sum;
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, inc, m);
+    if (lane >= m) inc += o;
+  }
+  int run = inc - sum;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int e = lane * 4 + j;
+    if (e < epr) {
+      tt.moff[e] = run;
+      tt.eoff[e] = expert_offset[e];
+    }
+    run += c[j];
+  }
+  if (lane == 31) {  // end entries (e = epr, up to 128)
+    tt.moff[epr] = run;
+    tt.eoff[epr] = expert_offset[epr];
+  }
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -184,58 +296,28 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                  uint16_t* __restrict__ bucket_bf16, int* __restrict__ err, int max_rows,
                  int max_tiles) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Smem1& s = *reinterpret_cast<Smem1*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   pdl_wait();
   pdl_trigger();
   if (tid == 0) {
-    for (int i = 0; i < STAGES; ++i) {
+    for (int i = 0; i < STAGES1; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
-      mbar_init(&s.acc_empty[i], 128);
+      mbar_init(&s.acc_empty[i], EPI_THREADS);
     }
     s.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // m-tile prefix over this rank's experts (one warp scan, 4 experts per lane)
-  if (warp == 2) {
-    int c[4], sum = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = lane * 4 + j;
-      const int n = e < epr ? expert_offset[e + 1] - expert_offset[e] : 0;
-      c[j] = (n + BM - 1) / BM;
-      sum += c[j];
-    }
-    int inc = sum;
-#pragma unroll
-    for (int m = 1; m < 32; m <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, inc, m);
-      if (lane >= m) inc += o;
-    }
-    int run = inc - sum;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = lane * 4 + j;
-      if (e < epr) {
-        s.moff[e] = run;
-        s.eoff[e] = expert_offset[e];
-      }
-      run += c[j];
-    }
-    if (lane == 31) {  // the end entries (e = epr, up to 128) are not covered above
-      s.moff[epr] = run;
-      s.eoff[epr] = expert_offset[epr];
-    }
-  }
+  if (warp == 2) build_tile_table(s.tt, expert_offset, epr, lane);
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s.tmem_base)),
-                 "r"(TMEM_COLS));
+                 "r"(TMEM_COLS1));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
   tc_fence_before();
@@ -243,9 +325,9 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   tc_fence_after();
 
   const uint32_t tmem = s.tmem_base;
-  int total = s.moff[epr] * NJ1;
+  int total = s.tt.moff[epr] * NJ1;
   // Defensive bound: never more tiles than the route buffers can hold.
-  if (total < 0 || total > max_tiles || s.eoff[epr] > max_rows) {
+  if (total < 0 || total > max_tiles || s.tt.eoff[epr] > max_rows) {
     if (tid == 0) atomicExch(err, 2);
     total = 0;
   }
@@ -256,9 +338,9 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        const TileInfo ti = tile_info(s, epr, t);
-        const int brow_g = ti.e * GU + ti.nj * 64;
-        const int brow_u = ti.e * GU + I + ti.nj * 64;
+        const TileInfo ti = tile_info(s.tt, epr, NJ1, t);
+        const int brow_g = ti.e * GU + ti.col * 64;
+        const int brow_u = ti.e * GU + I + ti.col * 64;
         for (int kb = 0; kb < KB1; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done;
           uint8_t* st = s.stage[stage];
@@ -266,7 +348,7 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           tma_load_2d(st, &map_a, kb * BK, ti.row0, &s.full[stage]);
           tma_load_2d(st + A_BYTES, &map_b, kb * BK, brow_g, &s.full[stage]);
           tma_load_2d(st + A_BYTES + B_BYTES / 2, &map_b, kb * BK, brow_u, &s.full[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == STAGES1) { stage = 0; phase ^= 1; }
         }
       }
     producer_done:;
@@ -293,7 +375,7 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             mma_i8(d, kmajor_sw128_desc(a0 + kk * 32), kmajor_sw128_desc(b0 + kk * 32),
                    (kb | kk) != 0);
           mma_commit(&s.empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == STAGES1) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
         mma_commit(&s.acc_full[acc]);
@@ -301,87 +383,116 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       }
     }
   } else {
-    // ---------------- epilogue: warps 2..5, thread = TMEM lane = route row
-    const int quarter = warp & 3;           // TMEM lanes 32*quarter .. +31
-    const int r = quarter * 32 + lane;      // row inside the tile
+    // ---------------- epilogue: warp (q, cb) owns TMEM lanes 32q..32q+31 and
+    // bucket columns 16cb..16cb+15 of the tile's 64
+    const int q = warp & 3;
+    const int cb = (warp - 2) >> 2;
+    const int r = q * 32 + lane;
     const float inv127 = 1.0f / 127.0f;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const TileInfo ti = tile_info(s, epr, t);
-      // warp-uniform outcome: the tcgen05.ld below is .sync.aligned
-      if (!__all_sync(0xffffffffu, mbar_wait(&s.acc_full[acc], acc_phase, &s.failed))) break;
-      tc_fence_after();
-      const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      const TileInfo ti = tile_info(s.tt, epr, NJ1, t);
+      // per-tile operands are loaded before the accumulator wait
       const bool valid = r < ti.nvalid;
       const int row = ti.row0 + r;
       const float ad = valid ? __fmul_rn(xg_sa[row], inv127) : 0.0f;
-      const float* wsg = gu_scale + (size_t)ti.e * GU + ti.nj * 64;
-      const float* wsu = wsg + I;
-      float hv[64];
+      const float* wsg = gu_scale + (size_t)ti.e * GU + ti.col * 64 + 16 * cb;
+      float sg[16], su[16];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        int gd[32], ud[32];
-        tmem_ld32(base + half * 32, gd);
-        tmem_ld32(base + 64 + half * 32, ud);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int col = half * 32 + c;
-          const float gv = __fmul_rn(__fmul_rn((float)gd[c], ad), __ldg(wsg + col));
-          const float uv = __fmul_rn(__fmul_rn((float)ud[c], ad), __ldg(wsu + col));
-          hv[col] = bf2f(f2bf(__fmul_rn(gelu_tanh_f32(gv), uv)));
-        }
+      for (int c = 0; c < 16; ++c) {
+        sg[c] = __ldg(wsg + c);
+        su[c] = __ldg(wsg + I + c);
       }
-      // accumulator drained: hand it back to the MMA warp
+      // On a failed (timed-out) wait the epilogue keeps walking the tiles
+      // without waiting (the CTA's failed flag makes every later wait return at
+      // once) so that the named barriers below are always met; the results are
+      // then discarded through *err.  The vote keeps the warp converged for the
+      // .sync.aligned tcgen05.ld.
+      (void)__all_sync(0xffffffffu, mbar_wait(&s.acc_full[acc], acc_phase, &s.failed));
+      tc_fence_after();
+      const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      int gd[16], ud[16];
+      tmem_ld16(base + 16 * cb, gd);
+      tmem_ld16(base + 64 + 16 * cb, ud);
+      tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(&s.acc_empty[acc]);
+      mbar_arrive(&s.acc_empty[acc]);  // accumulator drained: MMA may reuse it
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
 
-      if (valid) {
-        if (bucket_bf16) {
-          uint4* dst = reinterpret_cast<uint4*>(bucket_bf16 + (size_t)row * I + ti.nj * 64);
+      float hv[16];
 #pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            uint32_t w[4];
+      for (int c = 0; c < 16; ++c) {
+        const float gv = __fmul_rn(__fmul_rn((float)gd[c], ad), sg[c]);
+        const float uv = __fmul_rn(__fmul_rn((float)ud[c], ad), su[c]);
+        hv[c] = bf2f(f2bf(__fmul_rn(gelu_tanh_f32(gv), uv)));
+      }
+      if (bucket_bf16 && valid) {
+        uint4* dst = reinterpret_cast<uint4*>(bucket_bf16 + (size_t)row * I + ti.col * 64 + 16 * cb);
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              w[u] = (uint32_t)f2bf(hv[v * 8 + 2 * u]) | ((uint32_t)f2bf(hv[v * 8 + 2 * u + 1]) << 16);
-            dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
-          }
-        }
-        // FWHT-64 in registers: stages stride 1..32, (a+b, a-b), then x0.125
-#pragma unroll
-        for (int st = 1; st < 64; st <<= 1)
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (!(i & st)) {
-              const float a = hv[i], b = hv[i + st];
-              hv[i] = __fadd_rn(a, b);
-              hv[i + st] = __fsub_rn(a, b);
-            }
-        float amax = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          hv[i] = __fmul_rn(hv[i], fwht_scale_64());
-          amax = fmaxf(amax, fabsf(hv[i]));
-        }
-        const float qinv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-        uint4* qdst = reinterpret_cast<uint4*>(bucket_i8 + (size_t)row * I + ti.nj * 64);
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
+        for (int v = 0; v < 2; ++v) {
           uint32_t w[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint32_t p = 0;
-#pragma unroll
-            for (int b = 0; b < 4; ++b)
-              p |= (uint32_t)(quantize_i8(hv[v * 16 + u * 4 + b], qinv) & 0xFF) << (8 * b);
-            w[u] = p;
-          }
-          qdst[v] = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int u = 0; u < 4; ++u)
+            w[u] = (uint32_t)f2bf(hv[v * 8 + 2 * u]) | ((uint32_t)f2bf(hv[v * 8 + 2 * u + 1]) << 16);
+          dst[v] = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        bucket_sa[(size_t)row * NB_DOWN + ti.nj] = amax;
+      }
+      // FWHT-64 stages of stride 1..8 stay inside this thread's 16 columns
+#pragma unroll
+      for (int st = 1; st < 16; st <<= 1)
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (!(i & st)) {
+            const float a = hv[i], b = hv[i + st];
+            hv[i] = __fadd_rn(a, b);
+            hv[i + st] = __fsub_rn(a, b);
+          }
+      // strides 16 and 32 pair this block with block cb^1, then cb^2 (the lower
+      // block keeps a+b, the upper a-b with a from the lower block)
+#pragma unroll
+      for (int sx = 1; sx <= 2; sx <<= 1) {
+        float4* mine = reinterpret_cast<float4*>(&s.xbuf[r][16 * cb]);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) mine[v] = make_float4(hv[4 * v], hv[4 * v + 1], hv[4 * v + 2], hv[4 * v + 3]);
+        quarter_sync(q);
+        const float4* other = reinterpret_cast<const float4*>(&s.xbuf[r][16 * (cb ^ sx)]);
+        const bool upper = (cb & sx) != 0;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const float4 p = other[v];
+          const float pv[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int i = 4 * v + u;
+            hv[i] = upper ? __fsub_rn(pv[u], hv[i]) : __fadd_rn(hv[i], pv[u]);
+          }
+        }
+        quarter_sync(q);  // partners have read before the buffer is reused
+      }
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        hv[i] = __fmul_rn(hv[i], fwht_scale_64());
+        amax = fmaxf(amax, fabsf(hv[i]));
+      }
+      s.amax[r][cb] = amax;
+      quarter_sync(q);
+      amax = fmaxf(fmaxf(s.amax[r][0], s.amax[r][1]), fmaxf(s.amax[r][2], s.amax[r][3]));
+      if (valid) {
+        const float qinv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        uint32_t w[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint32_t p = 0;
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            p |= (uint32_t)(quantize_i8(hv[u * 4 + b], qinv) & 0xFF) << (8 * b);
+          w[u] = p;
+        }
+        *reinterpret_cast<uint4*>(bucket_i8 + (size_t)row * I + ti.col * 64 + 16 * cb) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+        if (cb == 0) bucket_sa[(size_t)row * NB_DOWN + ti.col] = amax;
       }
     }
   }
@@ -390,35 +501,10 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS1));
   }
   if (tid == 0 && s.failed) atomicExch(err, ERR_TIMEOUT);
 }
-
-// ---------------------------------------------------------------- phase 2
-// Down product with the reference's per-64-K-block dequantisation
-// (butterquant_kernels/moe.mojo:198-225): for every 64-wide K block b the MMA
-// warp writes the block's exact int32 dot into one of 4 TMEM regions (128
-// columns each); the epilogue threads (one route row each) fold it into
-// facc = fma(f32(dot_b), sa[b]/127, facc) in block order and release the
-// region, so the MMA warp runs up to 4 blocks ahead.  y = facc*sw*route_weight.
-constexpr int BN2 = 128;                  // hidden rows per tile
-constexpr int NT2 = H / BN2;              // 22 hidden tiles
-constexpr int KC2 = (I + BK - 1) / BK;    // 6 chunks of 128 K bytes (last half zero-filled)
-constexpr int RING = 4;
-constexpr uint32_t TMEM_COLS2 = RING * BN2;  // 512
-
-struct Smem2 {
-  uint8_t stage[STAGES][STAGE_BYTES];
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
-  uint64_t reg_full[RING];
-  uint64_t reg_empty[RING];
-  uint32_t tmem_base;
-  int failed;
-  int eoff[E + 1];
-  int moff[E + 1];
-};
 
 __global__ void __launch_bounds__(THREADS, 1)
 tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -433,47 +519,18 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   pdl_wait();
   pdl_trigger();
   if (tid == 0) {
-    for (int i = 0; i < STAGES; ++i) {
+    for (int i = 0; i < STAGES2; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
     for (int i = 0; i < RING; ++i) {
       mbar_init(&s.reg_full[i], 1);
-      mbar_init(&s.reg_empty[i], 128);
+      mbar_init(&s.reg_empty[i], EPI_THREADS);
     }
     s.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 2) {
-    int c[4], sum = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = lane * 4 + j;
-      const int n = e < epr ? expert_offset[e + 1] - expert_offset[e] : 0;
-      c[j] = (n + BM - 1) / BM;
-      sum += c[j];
-    }
-    int inc = sum;
-#pragma unroll
-    for (int m = 1; m < 32; m <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, inc, m);
-      if (lane >= m) inc += o;
-    }
-    int run = inc - sum;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = lane * 4 + j;
-      if (e < epr) {
-        s.moff[e] = run;
-        s.eoff[e] = expert_offset[e];
-      }
-      run += c[j];
-    }
-    if (lane == 31) {
-      s.moff[epr] = run;
-      s.eoff[epr] = expert_offset[epr];
-    }
-  }
+  if (warp == 2) build_tile_table(s.tt, expert_offset, epr, lane);
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s.tmem_base)),
@@ -485,39 +542,25 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   tc_fence_after();
 
   const uint32_t tmem = s.tmem_base;
-  int total = s.moff[epr] * NT2;
-  if (total < 0 || total > max_tiles || s.eoff[epr] > max_rows) {
+  int total = s.tt.moff[epr] * NT2;
+  if (total < 0 || total > max_tiles || s.tt.eoff[epr] > max_rows) {
     if (tid == 0) atomicExch(err, 2);
     total = 0;
   }
-
-  auto info = [&](int t, int& e, int& row0, int& nvalid, int& nt) {
-    const int mg = t / NT2;
-    nt = t % NT2;
-    int lo = 0, hi = epr;
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      if (s.moff[mid] <= mg) lo = mid; else hi = mid;
-    }
-    e = lo;
-    row0 = s.eoff[lo] + (mg - s.moff[lo]) * BM;
-    nvalid = min(BM, s.eoff[lo + 1] - row0);
-  };
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        int e, row0, nvalid, nt;
-        info(t, e, row0, nvalid, nt);
+        const TileInfo ti = tile_info(s.tt, epr, NT2, t);
         for (int c = 0; c < KC2; ++c) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done2;
           uint8_t* st = s.stage[stage];
           mbar_expect_tx(&s.full[stage], STAGE_BYTES);
-          tma_load_2d(st, &map_a, c * BK, row0, &s.full[stage]);
-          tma_load_2d(st + A_BYTES, &map_b, c * BK, e * H + nt * BN2, &s.full[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          tma_load_2d(st, &map_a, c * BK, ti.row0, &s.full[stage]);
+          tma_load_2d(st + A_BYTES, &map_b, c * BK, ti.e * H + ti.col * BN, &s.full[stage]);
+          if (++stage == STAGES2) { stage = 0; phase ^= 1; }
         }
       }
     producer_done2:;
@@ -537,7 +580,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             if (2 * c + h >= NB_DOWN) break;  // K bytes 704..767 are padding
             if (!mbar_wait(&s.reg_empty[reg], rphase ^ 1, &s.failed)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t d = tmem + (uint32_t)(reg * BN2);
+            const uint32_t d = tmem + (uint32_t)(reg * BN);
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
               const uint32_t off = (uint32_t)((2 * h + kk) * 32);
@@ -548,64 +591,70 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           }
           if (!ok) break;
           mma_commit(&s.empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == STAGES2) { stage = 0; phase ^= 1; }
         }
       }
     }
   } else {
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
+    // epilogue warp (q, cb): TMEM lanes 32q..32q+31, hidden columns 32cb..32cb+31
+    const int q = warp & 3;
+    const int cb = (warp - 2) >> 2;
+    const int r = q * 32 + lane;
     const float inv127 = 1.0f / 127.0f;
     int reg = 0;
     uint32_t rphase = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-      int e, row0, nvalid, nt;
-      info(t, e, row0, nvalid, nt);
-      const bool valid = r < nvalid;
-      const int row = row0 + r;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const TileInfo ti = tile_info(s.tt, epr, NT2, t);
+      const bool valid = r < ti.nvalid;
+      const int row = ti.row0 + r;
+      // per-tile operands are loaded before the first accumulator wait
       float adv[NB_DOWN];
 #pragma unroll
       for (int b = 0; b < NB_DOWN; ++b)
         adv[b] = valid ? __fmul_rn(bsa[(size_t)row * NB_DOWN + b], inv127) : 0.0f;
-      float facc[BN2];
+      const float wr = valid ? routes[row].weight : 0.0f;
+      const float* wsc = dn_scale + (size_t)ti.e * H + ti.col * BN + 32 * cb;
+      float2 facc[16];
 #pragma unroll
-      for (int n = 0; n < BN2; ++n) facc[n] = 0.0f;
+      for (int n = 0; n < 16; ++n) facc[n] = make_float2(0.0f, 0.0f);
+#pragma unroll
       for (int b = 0; b < NB_DOWN; ++b) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&s.reg_full[reg], rphase, &s.failed))) { ok = false; break; }
+        // as in phase 1: after a failed wait keep going without waiting, so the
+        // quarter's named barriers are always met
+        (void)__all_sync(0xffffffffu, mbar_wait(&s.reg_full[reg], rphase, &s.failed));
         tc_fence_after();
-        const uint32_t base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(reg * BN2);
-        float a = adv[0];
-#pragma unroll
-        for (int bb = 1; bb < NB_DOWN; ++bb)
-          if (bb == b) a = adv[bb];
-#pragma unroll
-        for (int q = 0; q < BN2 / 32; ++q) {
-          int d[32];
-          tmem_ld32(base + q * 32, d);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) facc[q * 32 + i] = __fmaf_rn((float)d[i], a, facc[q * 32 + i]);
-        }
+        int d[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(reg * BN + 32 * cb), d);
+        tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(&s.reg_empty[reg]);
         if (++reg == RING) { reg = 0; rphase ^= 1; }
-      }
-      if (!ok) break;
-      if (valid) {
-        const float wr = routes[row].weight;
-        const float* wsc = dn_scale + (size_t)e * H + nt * BN2;
-        float4* dst = reinterpret_cast<float4*>(ybuf + (size_t)row * H + nt * BN2);
+        const float2 a2 = make_float2(adv[b], adv[b]);
 #pragma unroll
-        for (int v = 0; v < BN2 / 4; ++v) {
-          float4 o;
-          o.x = __fmul_rn(__fmul_rn(facc[4 * v + 0], __ldg(wsc + 4 * v + 0)), wr);
-          o.y = __fmul_rn(__fmul_rn(facc[4 * v + 1], __ldg(wsc + 4 * v + 1)), wr);
-          o.z = __fmul_rn(__fmul_rn(facc[4 * v + 2], __ldg(wsc + 4 * v + 2)), wr);
-          o.w = __fmul_rn(__fmul_rn(facc[4 * v + 3], __ldg(wsc + 4 * v + 3)), wr);
-          dst[v] = o;
+        for (int i = 0; i < 16; ++i)
+          facc[i] = fma2(small_ints_to_float2(d[2 * i], d[2 * i + 1]), a2, facc[i]);
+      }
+      // y = facc * sw * w_route, staged per row then written as whole rows
+      const float2 wr2 = make_float2(wr, wr);
+      float4* ys = reinterpret_cast<float4*>(&s.ystage[r][32 * cb]);
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const float4 sw = __ldg(reinterpret_cast<const float4*>(wsc) + v);
+        const float2 lo = mul2(mul2(facc[2 * v], make_float2(sw.x, sw.y)), wr2);
+        const float2 hi = mul2(mul2(facc[2 * v + 1], make_float2(sw.z, sw.w)), wr2);
+        ys[v] = make_float4(lo.x, lo.y, hi.x, hi.y);
+      }
+      quarter_sync(q);
+      // the 4 warps of quarter q write its 32 rows: 8 rows each, one 512-byte row per warp store
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int rr = q * 32 + cb * 8 + j;
+        if (rr < ti.nvalid) {
+          const float4 v = reinterpret_cast<const float4*>(&s.ystage[rr][0])[lane];
+          reinterpret_cast<float4*>(ybuf + (size_t)(ti.row0 + rr) * H + ti.col * BN)[lane] = v;
         }
       }
+      quarter_sync(q);  // staging rows read before the next tile overwrites them
     }
   }
 
@@ -659,6 +708,13 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
 }  // namespace
 
 // 2-D int8 tensor map [rows][cols] with a box of box_rows x 128 bytes, 128-byte
@@ -694,14 +750,11 @@ cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t
                              cudaStream_t s) {
   const int max_rows = T * TOPK;
   const int max_tiles = (max_rows / tc::BM + epr) * tc::NJ1;
-  const size_t smem = sizeof(tc::Smem) + 1024;
+  const size_t smem = sizeof(tc::Smem1) + 1024;
   cudaError_t e = cudaFuncSetAttribute(tc::tc_phase1_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return launch_k(tc::tc_phase1_kernel, dim3(sms), dim3(tc::THREADS), smem, s,
+  return launch_k(tc::tc_phase1_kernel, dim3(sm_count()), dim3(tc::THREADS), smem, s,
                   *reinterpret_cast<const CUtensorMap*>(map_a),
                   *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, xg_sa, gu_scale,
                   bucket_i8, bucket_sa, bucket_bf16, err, max_rows, max_tiles);
@@ -716,10 +769,7 @@ cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t
   cudaError_t e = cudaFuncSetAttribute(tc::tc_phase2_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return launch_k(tc::tc_phase2_kernel, dim3(sms), dim3(tc::THREADS), smem, s,
+  return launch_k(tc::tc_phase2_kernel, dim3(sm_count()), dim3(tc::THREADS), smem, s,
                   *reinterpret_cast<const CUtensorMap*>(map_a),
                   *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, bsa, routes,
                   dn_scale, ybuf, err, max_rows, max_tiles);

@@ -64,11 +64,23 @@ struct gm_moe {
   int8_t* xg = nullptr;         // routed activation rows in schedule order (tcgen05 A operand)
   float* xg_sa = nullptr;
   int* dev_err = nullptr;       // device-side error word (bounded waits that expired)
+  int32_t* sched_counts = nullptr;  // per-chunk expert counts of the multi-CTA schedule
   alignas(64) unsigned char tmap_xg[128] = {};
   alignas(64) unsigned char tmap_bucket[128] = {};
   bool tc_ok = false;           // TMA descriptors available
   int tc_min_tokens = 1024;     // GM_OPT_TC_MIN_TOKENS
   cudaStream_t own_stream = nullptr;
+  // stage profiler (GM_OPT_PROFILE) and kernel launch count
+  struct PendingStage {
+    int stat;
+    long kernels;
+    cudaEvent_t a, b;
+  };
+  bool profile = false;
+  long launches = 0;
+  std::vector<PendingStage> pending;
+  std::vector<cudaEvent_t> event_pool;
+  std::vector<gm_stage_stat_t> stats;
 };
 
 namespace {
@@ -98,6 +110,14 @@ int cuda_check(gm_moe* h, cudaError_t e, const char* what) {
 
 inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// One stage of gm_moe_forward: its launches are counted and, with profiling
+// on, timed under the label (StageScope below).
+#define GM_STAGE(h, s, expr, what)              \
+  do {                                          \
+    StageScope _scope((h), (what), (s));        \
+    GM_TRY((h), (expr), (what));                \
+  } while (0)
+
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct Carve {
@@ -113,7 +133,8 @@ struct Carve {
 
 struct WsLayout {
   size_t logits, inv_rms, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
-      x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, xg, xg_sa, dev_err, total;
+      x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, xg, xg_sa, dev_err,
+      sched_counts, total;
 };
 
 WsLayout ws_layout(int max_tokens) {
@@ -142,6 +163,7 @@ WsLayout ws_layout(int max_tokens) {
   L.xg = c.take<int8_t>(R * H);
   L.xg_sa = c.take<float>(R);
   L.dev_err = c.take<int>(1);
+  L.sched_counts = c.take<int32_t>(schedule_counts_ints(max_tokens));
   L.total = align_up(c.off, 256);
   return L;
 }
@@ -181,6 +203,86 @@ bool is_device_ptr(const void* p) {
   }
   return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
+
+// ---------------------------------------------------------------- profiler
+cudaEvent_t take_event(gm_moe* h) {
+  if (!h->event_pool.empty()) {
+    cudaEvent_t e = h->event_pool.back();
+    h->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return e;
+}
+
+int stat_index(gm_moe* h, const char* label) {
+  for (size_t i = 0; i < h->stats.size(); ++i)
+    if (!strncmp(h->stats[i].label, label, sizeof(h->stats[i].label))) return (int)i;
+  gm_stage_stat_t st = {};
+  snprintf(st.label, sizeof st.label, "%s", label);
+  st.min_ms = 1e300;
+  h->stats.push_back(st);
+  return (int)h->stats.size() - 1;
+}
+
+// Waits for every recorded stage and folds its duration into the statistics.
+int drain_profile(gm_moe* h) {
+  int rc = GM_OK;
+  for (auto& p : h->pending) {
+    float ms = 0.0f;
+    cudaError_t e = cudaEventSynchronize(p.b);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, p.a, p.b);
+    if (e == cudaSuccess) {
+      gm_stage_stat_t& st = h->stats[p.stat];
+      st.calls += 1;
+      st.kernels += p.kernels;
+      st.total_ms += ms;
+      st.min_ms = std::min(st.min_ms, (double)ms);
+      st.max_ms = std::max(st.max_ms, (double)ms);
+    } else if (rc == GM_OK) {
+      rc = cuda_check(h, e, "profile event");
+    }
+    h->event_pool.push_back(p.a);
+    h->event_pool.push_back(p.b);
+  }
+  h->pending.clear();
+  return rc;
+}
+
+// Scope of one forward stage: counts the kernels launched inside it and, with
+// GM_OPT_PROFILE on, brackets them with events on the forward's stream.
+struct StageScope {
+  gm_moe* h;
+  const char* label;
+  cudaStream_t s;
+  cudaEvent_t a = nullptr;
+  long n0;
+  StageScope(gm_moe* h_, const char* label_, cudaStream_t s_)
+      : h(h_), label(label_), s(s_), n0(tls_kernel_launches) {
+    if (h->profile && (a = take_event(h)) && cudaEventRecord(a, s) != cudaSuccess) {
+      cudaGetLastError();
+      h->event_pool.push_back(a);
+      a = nullptr;
+    }
+  }
+  ~StageScope() {
+    const long k = tls_kernel_launches - n0;
+    h->launches += k;
+    if (!a) return;
+    cudaEvent_t b = take_event(h);
+    if (b && cudaEventRecord(b, s) == cudaSuccess) {
+      h->pending.push_back({stat_index(h, label), k, a, b});
+    } else {
+      cudaGetLastError();
+      h->event_pool.push_back(a);
+      if (b) h->event_pool.push_back(b);
+    }
+  }
+};
 
 }  // namespace
 
@@ -255,6 +357,7 @@ int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, in
   h->xg = reinterpret_cast<int8_t*>(b + L.xg);
   h->xg_sa = reinterpret_cast<float*>(b + L.xg_sa);
   h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
+  h->sched_counts = reinterpret_cast<int32_t*>(b + L.sched_counts);
   cudaMemset(h->dev_err, 0, sizeof(int));
   h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)max_tokens * TOPK, H, 128) &&
              make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)max_tokens * TOPK, I, 128);
@@ -271,6 +374,8 @@ int gm_moe_destroy(gm_moe_t* h) {
   if (!h) return GM_OK;
   cudaSetDevice(h->device);
   for (auto& L : h->layers) free_layer(L);
+  drain_profile(h);
+  for (cudaEvent_t e : h->event_pool) cudaEventDestroy(e);
   if (h->ws) cudaFree(h->ws);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
   delete h;
@@ -338,49 +443,50 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
   if (T == 0) return GM_OK;
   if (!x || !out) return set_err(h, GM_EINVAL, "NULL x/out");
   cudaStream_t s = S(stream);
+  if (h->pending.size() > 4096 && (rc = drain_profile(h))) return rc;  // bound the event backlog
   const uint16_t* xb = static_cast<const uint16_t*>(x);
   // 1. activation norm (+ inv_rms shared with the router)
   if (L.kind == 1)
-    GM_TRY(h, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, h->inv_rms, s), "bq_norm_quant");
+    GM_STAGE(h, s, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, h->inv_rms, s), "bq_norm_quant");
   else
-    GM_TRY(h, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
+    GM_STAGE(h, s, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
   // 2. router logits, 3. top-8 + schedule
-  GM_TRY(h, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, s), "router");
+  GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, s), "router_expert");
   const int rc_chunk = L.kind == 1 ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
-  GM_TRY(h, launch_topk_schedule(h->logits, L.pes, T, h->route_idx, h->route_w, h->expert_base,
+  GM_STAGE(h, s, launch_topk_schedule(h->logits, L.pes, T, h->route_idx, h->route_w, h->expert_base,
                                  h->epr, rc_chunk, h->expert_offset, h->routes, h->route_pos,
-                                 h->chunk_off, s),
-         "topk_schedule");
+                                 h->chunk_off, h->sched_counts, s),
+         "router_merge.schedule");
   // 4. experts, 5. combine
   if (L.kind == 1) {
     if (L.has_tc && h->tc_ok && T >= h->tc_min_tokens) {
       // prefill: routed rows gathered in schedule order, then the tcgen05 GEMM
-      GM_TRY(h, launch_gather_rows(h->x_i8, h->x_sa, h->routes, h->expert_offset, h->epr, T, h->xg,
+      GM_STAGE(h, s, launch_gather_rows(h->x_i8, h->x_sa, h->routes, h->expert_offset, h->epr, T, h->xg,
                                    h->xg_sa, s),
              "gather_rows");
-      GM_TRY(h, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, T, h->xg_sa,
+      GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, T, h->xg_sa,
                                  L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
-             "tc_phase1");
-      GM_TRY(h, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, T,
+             "bq_phase1_gate_up.tc");
+      GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, T,
                                  h->bucket_sa, h->routes, L.dn_scale, h->ybuf, h->dev_err, s),
-             "tc_phase2");
+             "bq_phase2_down.tc");
     } else {
-      GM_TRY(h, launch_bq_phase1(h->x_i8, h->x_sa, h->expert_offset, h->routes, h->chunk_off,
+      GM_STAGE(h, s, launch_bq_phase1(h->x_i8, h->x_sa, h->expert_offset, h->routes, h->chunk_off,
                                  h->epr, T, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
-             "bq_phase1");
-      GM_TRY(h, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
+             "bq_phase1_gate_up");
+      GM_STAGE(h, s, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
                                  h->chunk_off, h->epr, T, L.dn_q, L.dn_scale, h->ybuf, true, s),
-             "bq_phase2");
+             "bq_phase2_down");
     }
   } else {
-    GM_TRY(h, launch_bf16_phase1(h->x_normed, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
+    GM_STAGE(h, s, launch_bf16_phase1(h->x_normed, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
                                  L.gu_bf16, h->bucket, s),
-           "phase1_bf16");
-    GM_TRY(h, launch_bf16_phase2(h->bucket, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
+           "phase1_gate_up");
+    GM_STAGE(h, s, launch_bf16_phase2(h->bucket, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
                                  L.dn_bf16, h->ybuf, s),
-           "phase2_bf16");
+           "phase2_down");
   }
-  GM_TRY(h, launch_combine(h->route_idx, h->route_pos, h->ybuf, T, static_cast<uint16_t*>(out), s),
+  GM_STAGE(h, s, launch_combine(h->route_idx, h->route_pos, h->ybuf, T, static_cast<uint16_t*>(out), s),
          "combine");
   return GM_OK;
 }
@@ -392,9 +498,34 @@ int gm_moe_set_option(gm_moe_t* h, int option, long value) {
       if (value < 1) return set_err(h, GM_EINVAL, "GM_OPT_TC_MIN_TOKENS must be >= 1");
       h->tc_min_tokens = value > 0x7FFFFFFF ? 0x7FFFFFFF : (int)value;
       return GM_OK;
+    case GM_OPT_PROFILE: {
+      if (value != 0 && value != 1) return set_err(h, GM_EINVAL, "GM_OPT_PROFILE must be 0 or 1");
+      GM_TRY(h, cudaSetDevice(h->device), "GM_OPT_PROFILE");
+      const int rc = drain_profile(h);
+      h->stats.clear();
+      h->launches = 0;
+      h->profile = value != 0;
+      return rc;
+    }
     default:
       return set_err(h, GM_EINVAL, "unknown option %d", option);
   }
+}
+
+int gm_moe_profile_read(gm_moe_t* h, gm_stage_stat_t* stats, int max_stats, int* n_stats,
+                        long* kernel_launches) {
+  if (!h || !n_stats || max_stats < 0 || (max_stats > 0 && !stats))
+    return set_err(h, GM_EINVAL, "gm_moe_profile_read: bad arguments");
+  GM_TRY(h, cudaSetDevice(h->device), "profile_read");
+  const int rc = drain_profile(h);
+  const int n = (int)h->stats.size();
+  for (int i = 0; i < n && i < max_stats; ++i) {
+    stats[i] = h->stats[i];
+    if (stats[i].calls == 0) stats[i].min_ms = 0.0;
+  }
+  *n_stats = n;
+  if (kernel_launches) *kernel_launches = h->launches;
+  return rc;
 }
 
 int gm_moe_device_status(gm_moe_t* h, int* device_error) {

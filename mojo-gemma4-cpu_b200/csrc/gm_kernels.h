@@ -6,12 +6,17 @@
 
 namespace gm {
 
+// Kernels launched through launch_k by the calling host thread (the handle
+// takes differences around its own launches to count them).
+inline thread_local long tls_kernel_launches = 0;
+
 // Launch with programmatic stream serialisation (see pdl_wait/pdl_trigger):
 // every kernel launched this way calls pdl_wait() before touching memory that
 // an earlier kernel of the stream writes or reads.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                      Args&&... args) {
+  ++tls_kernel_launches;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -37,11 +42,18 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const ui
 cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_t s);
 cudaError_t launch_topk(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
                         float* route_w, cudaStream_t s);
-// top-8 + softmax followed by the expert schedule (one CTA when T <= 1024)
+// top-8 + softmax followed by the expert schedule (one CTA when T <= 1024;
+// otherwise a top-8 grid and, given `counts` scratch of schedule_counts_ints(T)
+// ints, the two-pass multi-CTA schedule)
 cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
                                  float* route_w, int expert_base, int epr, int route_chunk,
                                  int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
-                                 int32_t* chunk_off, cudaStream_t s);
+                                 int32_t* chunk_off, int32_t* counts, cudaStream_t s);
+int schedule_counts_ints(int T);
+cudaError_t launch_schedule_multi(const int32_t* route_idx, const float* route_w, int T,
+                                  int expert_base, int epr, int route_chunk, int32_t* counts,
+                                  int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
+                                  int32_t* chunk_off, cudaStream_t s);
 
 cudaError_t launch_router(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
                           const uint16_t* pes, int T, float* logits, int32_t* route_idx,

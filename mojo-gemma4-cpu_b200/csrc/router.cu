@@ -8,8 +8,8 @@
 //
 // B200 shape: the logits are a skinny [T x 2816] x [2816 x 128] product done
 // in f32 FMA (the reference's f32-activation x bf16-weight dot, no bf16
-// rounding of the activation), tiled through shared memory and split along K
-// for small T so that enough CTAs stream the 720 KB projection.  inv_rms comes
+// rounding of the activation), split along K into 11 slices of 256 so that
+// enough CTAs stream the 720 KB projection at every T.  inv_rms comes
 // from the activation-norm kernel that runs first (the reference computes the
 // same rms_reduce_row for both, kernels/rmsnorm.mojo:16-17).  Top-8 selection
 // is one warp per token with 8 rounds of warp arg-max under the reference's
@@ -19,87 +19,7 @@
 
 namespace gm {
 
-template <int TT, int EG, int MT, int ME>
-__global__ void __launch_bounds__((TT / MT) * (EG / ME))
-router_logits_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
-                     const uint16_t* __restrict__ rscale, const float* __restrict__ inv_rms,
-                     int T, int n_experts, int k_len, float* __restrict__ logits) {
-  constexpr int NT = (TT / MT) * (EG / ME);
-  constexpr int KC = 64;
-  static_assert(NT % 32 == 0, "whole warps");
-  __shared__ float s_inv[TT];
-  __shared__ float s_x[KC][TT + 1];
-  __shared__ float s_w[KC][EG + 1];
-  pdl_wait();
-  pdl_trigger();
-
-  const int tid = threadIdx.x;
-  const int t0 = blockIdx.x * TT, e0 = blockIdx.y * EG;
-  // split-K: this CTA covers K range [kb, kb + k_len) and writes partial logits
-  // to slice blockIdx.z of [gridDim.z][T][n_experts]
-  const int kb = blockIdx.z * k_len;
-  logits += (size_t)blockIdx.z * T * n_experts;
-  for (int t = tid; t < TT; t += NT) s_inv[t] = t0 + t < T ? inv_rms[t0 + t] : 0.0f;
-  __syncthreads();
-
-  const int tx = tid % (EG / ME), ty = tid / (EG / ME);
-  float acc[MT][ME];
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int n = 0; n < ME; ++n) acc[m][n] = 0.0f;
-
-  for (int k0 = kb; k0 < kb + k_len; k0 += KC) {
-    for (int i = tid; i < TT * (KC / 2); i += NT) {
-      int t = i / (KC / 2), kp = (i % (KC / 2)) * 2;
-      float a = 0.0f, b = 0.0f;
-      if (t0 + t < T) {
-        uint32_t v = *reinterpret_cast<const uint32_t*>(x + (size_t)(t0 + t) * H + k0 + kp);
-        uint32_t rs = *reinterpret_cast<const uint32_t*>(rscale + k0 + kp);
-        float inv = s_inv[t];
-        // `xv * sv * inv_vec` (moe_router.mojo:175-178): (x*s)*inv, f32
-        a = __fmul_rn(__fmul_rn(bf2f(v & 0xFFFFu), bf2f(rs & 0xFFFFu)), inv);
-        b = __fmul_rn(__fmul_rn(bf2f(v >> 16), bf2f(rs >> 16)), inv);
-      }
-      s_x[kp][t] = a;
-      s_x[kp + 1][t] = b;
-    }
-    for (int i = tid; i < EG * (KC / 2); i += NT) {
-      int e = i / (KC / 2), kp = (i % (KC / 2)) * 2;
-      uint32_t v = 0;
-      if (e0 + e < n_experts)
-        v = *reinterpret_cast<const uint32_t*>(wr + (size_t)(e0 + e) * H + k0 + kp);
-      s_w[kp][e] = bf2f(v & 0xFFFFu);
-      s_w[kp + 1][e] = bf2f(v >> 16);
-    }
-    __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < KC; ++k) {
-      float xv[MT], wv[ME];
-#pragma unroll
-      for (int m = 0; m < MT; ++m) xv[m] = s_x[k][ty + m * (TT / MT)];
-#pragma unroll
-      for (int n = 0; n < ME; ++n) wv[n] = s_w[k][tx + n * (EG / ME)];
-#pragma unroll
-      for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int n = 0; n < ME; ++n) acc[m][n] = __fmaf_rn(xv[m], wv[n], acc[m][n]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int m = 0; m < MT; ++m) {
-    int t = t0 + ty + m * (TT / MT);
-    if (t >= T) continue;
-#pragma unroll
-    for (int n = 0; n < ME; ++n) {
-      int e = e0 + tx + n * (EG / ME);
-      if (e < n_experts) logits[(size_t)t * n_experts + e] = acc[m][n];
-    }
-  }
-}
-
-// Router logits for T <= 1024.  CTA = 8 warps, tile = 8 tokens x 32 experts x
+// Router logits.  CTA = 8 warps, tile = 8 tokens x 32 experts x
 // one 256-wide K slice (blockIdx.z).  Lane l owns k = kb+8l..8l+7 of every row
 // and reads the bf16 projection straight from global memory (one 16-byte load
 // per expert); each warp owns 4 experts.  The 32 (token, expert) lane partials
@@ -198,7 +118,8 @@ topk_softmax_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __re
 }
 
 int router_ksplit(int T) {
-  return T <= 1024 ? H / 256 : 1;  // 11 K slices of 256 for the warp-level kernel
+  (void)T;
+  return H / 256;  // 11 K slices of 256 for the warp-level kernel
 }
 
 size_t router_workspace_floats(int T) { return (size_t)router_ksplit(T) * T * E + T; }
@@ -207,12 +128,8 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const ui
                                  const float* inv_rms, int T, float* logits, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   const int ks = router_ksplit(T);
-  if (ks > 1)
-    return launch_k(router_logits_small_kernel, dim3((T + 7) / 8, E / 32, ks), dim3(256), 0, s, x,
-                    wr, rscale, inv_rms, T, logits);
-  dim3 grid((T + 31) / 32, E / 32, 1);
-  return launch_k(router_logits_kernel<32, 32, 4, 2>, grid, dim3(128), 0, s, x, wr, rscale,
-                  inv_rms, T, (int)E, (int)H, logits);
+  return launch_k(router_logits_small_kernel, dim3((T + 7) / 8, E / 32, ks), dim3(256), 0, s, x,
+                  wr, rscale, inv_rms, T, logits);
 }
 
 cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_t s) {

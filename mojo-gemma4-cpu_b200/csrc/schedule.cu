@@ -159,6 +159,147 @@ topk_schedule_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __r
                 route_pos, chunk_off, sm);
 }
 
+// ---- multi-CTA schedule for large T: chunks of 256 tokens, one CTA each.
+// Pass 1 counts the local routes of every expert per chunk; pass 2 derives
+// each chunk's first position per expert (expert prefix + earlier chunks) and
+// places its routes with the same bitmask/popcount ranking, so the order is
+// the reference's sequential token-major order.
+constexpr int SCHED_CHUNK = 256;
+
+__global__ void __launch_bounds__(SCHED_CHUNK)
+schedule_count_kernel(const int32_t* __restrict__ route_idx, int T, int expert_base, int epr,
+                      int32_t* __restrict__ counts) {
+  __shared__ int cnt[E];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, c = blockIdx.x;
+  if (tid < E) cnt[tid] = 0;
+  __syncthreads();
+  const int t = c * SCHED_CHUNK + tid;
+  if (t < T) {
+#pragma unroll
+    for (int k = 0; k < TOPK; ++k) {
+      const int e = route_idx[t * TOPK + k] - expert_base;
+      if (e >= 0 && e < epr) atomicAdd(&cnt[e], 1);
+    }
+  }
+  __syncthreads();
+  if (tid < E) counts[(size_t)c * E + tid] = tid < epr ? cnt[tid] : 0;
+}
+
+__global__ void __launch_bounds__(SCHED_CHUNK)
+schedule_scatter_kernel(const int32_t* __restrict__ route_idx, const float* __restrict__ route_w,
+                        int T, int expert_base, int epr, int route_chunk,
+                        const int32_t* __restrict__ counts, int nchunks,
+                        int32_t* __restrict__ expert_offset, SparseRoute* __restrict__ routes,
+                        int32_t* __restrict__ route_pos, int32_t* __restrict__ chunk_off) {
+  __shared__ int tot[E], before[E], base[E];
+  __shared__ uint32_t mask[E][SCHED_CHUNK / 32];
+  __shared__ int wpre[E][SCHED_CHUNK / 32 + 1];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, c = blockIdx.x;
+  if (tid < E) {
+    int s = 0, b = 0;
+    if (tid < epr)
+      for (int cc = 0; cc < nchunks; ++cc) {
+        const int v = counts[(size_t)cc * E + tid];
+        if (cc < c) b += v;
+        s += v;
+      }
+    tot[tid] = s;
+    before[tid] = b;
+  }
+  for (int i = tid; i < E * (SCHED_CHUNK / 32); i += SCHED_CHUNK) mask[i / (SCHED_CHUNK / 32)][i % (SCHED_CHUNK / 32)] = 0u;
+  __syncthreads();
+  if (tid < 32) {
+    int cv[4], cc4[4], s = 0, sc = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = tid * 4 + j;
+      cv[j] = e < epr ? tot[e] : 0;
+      cc4[j] = e < epr ? (cv[j] + route_chunk - 1) / route_chunk : 0;
+      s += cv[j];
+      sc += cc4[j];
+    }
+    int inc = s, incc = sc;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, inc, m);
+      const int oc = __shfl_up_sync(0xffffffffu, incc, m);
+      if (tid >= m) { inc += o; incc += oc; }
+    }
+    int run = inc - s, crun = incc - sc;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = tid * 4 + j;
+      if (e < epr) {
+        base[e] = run + before[e];
+        if (c == 0) {
+          expert_offset[e] = run;
+          chunk_off[e] = crun;
+        }
+      }
+      run += cv[j];
+      crun += cc4[j];
+    }
+    if (c == 0 && tid == 31) {
+      expert_offset[epr] = run;
+      chunk_off[epr] = crun;
+    }
+  }
+  const int t = c * SCHED_CHUNK + tid;
+  int le[TOPK];
+#pragma unroll
+  for (int k = 0; k < TOPK; ++k) {
+    le[k] = -1;
+    if (t < T) {
+      const int e = route_idx[t * TOPK + k] - expert_base;
+      if (e >= 0 && e < epr) {
+        le[k] = e;
+        atomicOr(&mask[e][tid >> 5], 1u << (tid & 31));
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < epr) {
+    int s = 0;
+#pragma unroll
+    for (int w = 0; w < SCHED_CHUNK / 32; ++w) {
+      wpre[tid][w] = s;
+      s += __popc(mask[tid][w]);
+    }
+  }
+  __syncthreads();
+  if (t < T) {
+#pragma unroll
+    for (int k = 0; k < TOPK; ++k) {
+      int pos = -1;
+      const int e = le[k];
+      if (e >= 0) {
+        pos = base[e] + wpre[e][tid >> 5] + __popc(mask[e][tid >> 5] & ((1u << (tid & 31)) - 1u));
+        routes[pos] = SparseRoute{t, route_w[t * TOPK + k]};
+      }
+      route_pos[t * TOPK + k] = pos;
+    }
+  }
+}
+
+int schedule_counts_ints(int T) { return ((T + SCHED_CHUNK - 1) / SCHED_CHUNK) * E; }
+
+cudaError_t launch_schedule_multi(const int32_t* route_idx, const float* route_w, int T,
+                                  int expert_base, int epr, int route_chunk, int32_t* counts,
+                                  int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
+                                  int32_t* chunk_off, cudaStream_t s) {
+  const int nchunks = (T + SCHED_CHUNK - 1) / SCHED_CHUNK;
+  cudaError_t e = launch_k(schedule_count_kernel, dim3(nchunks), dim3(SCHED_CHUNK), 0, s, route_idx,
+                           T, expert_base, epr, counts);
+  if (e != cudaSuccess) return e;
+  return launch_k(schedule_scatter_kernel, dim3(nchunks), dim3(SCHED_CHUNK), 0, s, route_idx,
+                  route_w, T, expert_base, epr, route_chunk, (const int32_t*)counts, nchunks,
+                  expert_offset, routes, route_pos, chunk_off);
+}
+
 cudaError_t launch_build_schedule(const int32_t* route_idx, const float* route_w, int T,
                                   int expert_base, int epr, int route_chunk,
                                   int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
@@ -170,13 +311,16 @@ cudaError_t launch_build_schedule(const int32_t* route_idx, const float* route_w
 cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
                                  float* route_w, int expert_base, int epr, int route_chunk,
                                  int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
-                                 int32_t* chunk_off, cudaStream_t s) {
+                                 int32_t* chunk_off, int32_t* counts, cudaStream_t s) {
   if (T <= 1024)
     return launch_k(topk_schedule_kernel, dim3(1), dim3(1024), 0, s, logits, router_ksplit(T), pes,
                     T, route_idx, route_w, expert_base, epr, route_chunk, expert_offset, routes,
                     route_pos, chunk_off);
   cudaError_t e = launch_topk(logits, pes, T, route_idx, route_w, s);
   if (e != cudaSuccess) return e;
+  if (counts)
+    return launch_schedule_multi(route_idx, route_w, T, expert_base, epr, route_chunk, counts,
+                                 expert_offset, routes, route_pos, chunk_off, s);
   return launch_build_schedule(route_idx, route_w, T, expert_base, epr, route_chunk, expert_offset,
                                routes, route_pos, chunk_off, s);
 }

@@ -26,6 +26,14 @@ STATUS = {0: "GM_OK", -1: "GM_EINVAL", -2: "GM_ECUDA", -3: "GM_ENOMEM", -4: "GM_
 
 # Every symbol include/gmoe.h declares, with its ctypes signature.
 _vp, _i32, _i64, _sz = C.c_void_p, C.c_int, C.c_long, C.c_size_t
+
+
+class StageStat(C.Structure):
+    """gm_stage_stat_t: one stage label's statistics (times in ms)."""
+    _fields_ = [("label", C.c_char * 32), ("calls", C.c_long), ("kernels", C.c_long),
+                ("total_ms", C.c_double), ("min_ms", C.c_double), ("max_ms", C.c_double)]
+
+
 SIGNATURES = {
     "gm_version": (C.c_char_p, []),
     "gm_last_error": (C.c_char_p, [_vp]),
@@ -39,6 +47,7 @@ SIGNATURES = {
     "gm_moe_forward_sync": (_i32, [_vp, _i32, _vp, _vp, _i32]),
     "gm_moe_set_option": (_i32, [_vp, _i32, _i64]),
     "gm_moe_device_status": (_i32, [_vp, C.POINTER(_i32)]),
+    "gm_moe_profile_read": (_i32, [_vp, C.POINTER(StageStat), _i32, C.POINTER(_i32), C.POINTER(_i64)]),
     "gm_router_select": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "gm_router_select_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),
     "gm_build_expert_schedules": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
@@ -166,6 +175,25 @@ class MoeBlock:
     def set_option(self, option, value):
         check(lib().gm_moe_set_option(self.h, option, value), self.h)
 
+    def profile(self, on=True):
+        """Turns the per-stage event profiler on or off; clears the statistics
+        and the kernel launch count either way."""
+        self.set_option(OPT_PROFILE, 1 if on else 0)
+
+    def profile_read(self):
+        """(stats, kernel_launches): stats maps each stage label to a dict of
+        calls, kernels, total_ms, min_ms, max_ms, avg_ms (first-seen order)."""
+        n, launches = C.c_int(0), C.c_long(0)
+        buf = (StageStat * 64)()
+        check(lib().gm_moe_profile_read(self.h, buf, 64, C.byref(n), C.byref(launches)), self.h)
+        stats = {}
+        for st in buf[:min(n.value, 64)]:
+            stats[st.label.decode()] = {
+                "calls": st.calls, "kernels": st.kernels, "total_ms": st.total_ms,
+                "min_ms": st.min_ms, "max_ms": st.max_ms,
+                "avg_ms": st.total_ms / st.calls if st.calls else 0.0}
+        return stats, launches.value
+
     def device_status(self):
         """Synchronises; raises GmoeError(GM_ETIMEOUT) if a bounded wait expired."""
         e = C.c_int(0)
@@ -174,3 +202,4 @@ class MoeBlock:
 
 
 OPT_TC_MIN_TOKENS = 1
+OPT_PROFILE = 2

@@ -71,6 +71,19 @@ def topk_margin(logits):
     return s[:, 7] - s[:, 8]
 
 
+def routes_by_expert(idx, w=None):
+    """Top-8 lists put in expert-id order.  The MoE output depends on the
+    selected SET and the per-expert weights only (the combine sums a token's
+    routes in expert order), so two routers agree when these match; the rank
+    order inside the top 8 may differ where two survivors' logits differ in
+    their last bit (f32 summation order)."""
+    order = np.argsort(idx, axis=1, kind="stable")
+    si = np.take_along_axis(idx, order, axis=1)
+    if w is None:
+        return si
+    return si, np.take_along_axis(w, order, axis=1)
+
+
 def rel_err(out_u16, ref_u16, rows=None):
     o = O.bf16_to_f32(out_u16).astype(np.float64)
     r = O.bf16_to_f32(ref_u16).astype(np.float64)

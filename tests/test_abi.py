@@ -54,3 +54,31 @@ def test_workspace_size_grows_with_tokens():
     a, b = L.gm_moe_workspace_bytes(16), L.gm_moe_workspace_bytes(1024)
     assert 0 < a < b
     assert L.gm_moe_workspace_bytes(0) == 0
+
+
+def test_stage_stat_layout_matches_header(tmp_path):
+    """gmoe.StageStat mirrors gm_stage_stat_t byte for byte (checked by
+    compiling the header with the host C compiler)."""
+    import subprocess
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "gmoe.h"\n'
+        'int main(void) { printf("%zu %zu %zu %zu %zu %zu %zu\\n", sizeof(gm_stage_stat_t),'
+        ' offsetof(gm_stage_stat_t, label), offsetof(gm_stage_stat_t, calls),'
+        ' offsetof(gm_stage_stat_t, kernels), offsetof(gm_stage_stat_t, total_ms),'
+        ' offsetof(gm_stage_stat_t, min_ms), offsetof(gm_stage_stat_t, max_ms)); return 0; }\n')
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True,
+                                          text=True).stdout.split()]
+    S = gmoe.StageStat
+    want = [ctypes.sizeof(S)] + [getattr(S, f).offset for f in
+                                 ("label", "calls", "kernels", "total_ms", "min_ms", "max_ms")]
+    assert got == want
+
+
+def test_profile_read_rejects_null_handle():
+    L = gmoe.lib()
+    n, k = ctypes.c_int(0), ctypes.c_long(0)
+    assert L.gm_moe_profile_read(None, None, 0, ctypes.byref(n), ctypes.byref(k)) == -1
