@@ -235,11 +235,12 @@ def main():
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # The clock sampler runs from the warm-up through the timed region; the
-    # warm-up lasts at least 0.5 s so that nvidia-smi sees the GPU under load.
+    # warm-up lasts at least 1 s so that the GPU's power and clocks have settled
+    # under this load (and nvidia-smi sees it) before the timed region.
     with ClockSampler(local) as clk:
         t_w = time.perf_counter()
         i = 0
-        while i < args.warmup or time.perf_counter() - t_w < 0.5:
+        while i < args.warmup or time.perf_counter() - t_w < 1.0:
             step(i)
             i += 1
             if i % 8 == 0:

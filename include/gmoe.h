@@ -115,9 +115,13 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
  * results.  Default 1024.
  * GM_OPT_PROFILE: 1 records a CUDA event pair around every stage that
  * gm_moe_forward launches, 0 (default) records none; setting it (either
- * value) clears the stage statistics and the kernel launch count. */
+ * value) clears the stage statistics and the kernel launch count.
+ * GM_OPT_PDL: 1 (default) launches the forward's kernels with programmatic
+ * dependent launch (each kernel's prologue overlaps its predecessor's tail);
+ * 0 launches them with plain stream ordering. */
 #define GM_OPT_TC_MIN_TOKENS 1
 #define GM_OPT_PROFILE 2
+#define GM_OPT_PDL 3
 int gm_moe_set_option(gm_moe_t* h, int option, long value);
 
 /* Per-stage statistics of the handle's forwards.  Replaces the reference's

@@ -33,6 +33,7 @@
 #include <cuda.h>
 
 #include "gm_kernels.h"
+#include "tc_prims.cuh"
 
 namespace gm {
 
@@ -90,72 +91,9 @@ struct Smem2 {
   TileTable tt;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Bounded wait for the phase with parity `parity` to complete.  Returns false
-// (and flags the CTA) after ~1 s.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* failed) {
-  const uint32_t a = smem_u32(b);
-  uint64_t t0 = 0;
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if (*(volatile int*)failed) return false;
-    if ((it & 63) == 0) {
-      const uint64_t t = global_ns();
-      if (t0 == 0) t0 = t;
-      else if (t - t0 > 1000000000ull) {
-        atomicExch(failed, 1);
-        return false;
-      }
-    }
-  }
-}
-
 // Named barrier for the 4 epilogue warps of one TMEM lane quarter.
 __device__ __forceinline__ void quarter_sync(int q) {
   asm volatile("bar.sync %0, 128;" ::"r"(1 + q) : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
-// K-major operand, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes
-// apart (SBO), version 1 (sm100), layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
 // kind::i8, D = s32, A = B = signed int8, both K-major, N = 128, M = 128.
@@ -168,70 +106,6 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t da, uint64_t db
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p; }"
       ::"r"(d_tmem), "l"(da), "l"(db), "r"(IDESC_I8), "r"(accumulate), "r"(0u)
       : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
-        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Packed two-lane f32 arithmetic of sm_100 (one instruction, two IEEE
-// round-to-nearest results; identical to the scalar operations).
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  float2 c;
-  asm("add.rn.f32x2 %0, %1, %2;"
-      : "=l"(reinterpret_cast<uint64_t&>(c))
-      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
-  return c;
-}
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-  float2 c;
-  asm("mul.rn.f32x2 %0, %1, %2;"
-      : "=l"(reinterpret_cast<uint64_t&>(c))
-      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
-  return c;
-}
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(reinterpret_cast<uint64_t&>(d))
-      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
-        "l"(reinterpret_cast<const uint64_t&>(c)));
-  return d;
-}
-
-// Exact int32 -> f32 for |d| < 2^22 (the 64-wide down-block dots are < 2^21):
-// 1.5*2^23 + d is representable, so its bits are those of 0x4B400000 + d, and
-// subtracting 1.5*2^23 is exact.  Two lanes at a time.
-__device__ __forceinline__ float2 small_ints_to_float2(int d0, int d1) {
-  const float2 biased = make_float2(__int_as_float(0x4B400000 + d0), __int_as_float(0x4B400000 + d1));
-  return add2(biased, make_float2(-12582912.0f, -12582912.0f));
 }
 
 struct TileInfo {
@@ -555,7 +429,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const TileInfo ti = tile_info(s.tt, epr, NT2, t);
         for (int c = 0; c < KC2; ++c) {
-          if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done2;
+          if (!mbar_wait<false>(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done2;
           uint8_t* st = s.stage[stage];
           mbar_expect_tx(&s.full[stage], STAGE_BYTES);
           tma_load_2d(st, &map_a, c * BK, ti.row0, &s.full[stage]);
@@ -572,13 +446,13 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
         for (int c = 0; ok && c < KC2; ++c) {
-          if (!mbar_wait(&s.full[stage], phase, &s.failed)) { ok = false; break; }
+          if (!mbar_wait<false>(&s.full[stage], phase, &s.failed)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(s.stage[stage]);
           const uint32_t b0 = a0 + A_BYTES;
           for (int h = 0; h < 2; ++h) {
             if (2 * c + h >= NB_DOWN) break;  // K bytes 704..767 are padding
-            if (!mbar_wait(&s.reg_empty[reg], rphase ^ 1, &s.failed)) { ok = false; break; }
+            if (!mbar_wait<false>(&s.reg_empty[reg], rphase ^ 1, &s.failed)) { ok = false; break; }
             tc_fence_after();
             const uint32_t d = tmem + (uint32_t)(reg * BN);
 #pragma unroll
@@ -606,6 +480,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const TileInfo ti = tile_info(s.tt, epr, NT2, t);
       const bool valid = r < ti.nvalid;
+      const bool quarter_live = q * 32 < ti.nvalid;  // warp-uniform
       const int row = ti.row0 + r;
       // per-tile operands are loaded before the first accumulator wait
       float adv[NB_DOWN];
@@ -621,18 +496,21 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       for (int b = 0; b < NB_DOWN; ++b) {
         // as in phase 1: after a failed wait keep going without waiting, so the
         // quarter's named barriers are always met
-        (void)__all_sync(0xffffffffu, mbar_wait(&s.reg_full[reg], rphase, &s.failed));
+        (void)__all_sync(0xffffffffu, mbar_wait<false>(&s.reg_full[reg], rphase, &s.failed));
         tc_fence_after();
         int d[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(reg * BN + 32 * cb), d);
+        if (quarter_live)  // a quarter with no valid route rows only releases the region
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(reg * BN + 32 * cb), d);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(&s.reg_empty[reg]);
         if (++reg == RING) { reg = 0; rphase ^= 1; }
-        const float2 a2 = make_float2(adv[b], adv[b]);
+        if (quarter_live) {
+          const float2 a2 = make_float2(adv[b], adv[b]);
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          facc[i] = fma2(small_ints_to_float2(d[2 * i], d[2 * i + 1]), a2, facc[i]);
+          for (int i = 0; i < 16; ++i)
+            facc[i] = fma2(small_ints_to_float2(d[2 * i], d[2 * i + 1]), a2, facc[i]);
+        }
       }
       // y = facc * sw * w_route, staged per row then written as whole rows
       const float2 wr2 = make_float2(wr, wr);

@@ -77,6 +77,7 @@ struct gm_moe {
     cudaEvent_t a, b;
   };
   bool profile = false;
+  bool pdl = true;              // GM_OPT_PDL
   long launches = 0;
   std::vector<PendingStage> pending;
   std::vector<cudaEvent_t> event_pool;
@@ -433,6 +434,15 @@ int gm_moe_register_layer_bf16(gm_moe_t* h, int layer, const void* gate_up, cons
   return GM_OK;
 }
 
+namespace {
+// Applies the handle's GM_OPT_PDL to launch_k for the scope of one forward.
+struct PdlScope {
+  bool saved;
+  explicit PdlScope(bool on) : saved(tls_pdl) { tls_pdl = on; }
+  ~PdlScope() { tls_pdl = saved; }
+};
+}  // namespace
+
 int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void* stream) {
   int rc = check_layer(h, layer);
   if (rc) return rc;
@@ -444,6 +454,7 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
   if (!x || !out) return set_err(h, GM_EINVAL, "NULL x/out");
   cudaStream_t s = S(stream);
   if (h->pending.size() > 4096 && (rc = drain_profile(h))) return rc;  // bound the event backlog
+  PdlScope pdl_scope(h->pdl);
   const uint16_t* xb = static_cast<const uint16_t*>(x);
   // 1. activation norm (+ inv_rms shared with the router)
   if (L.kind == 1)
@@ -451,7 +462,7 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
   else
     GM_STAGE(h, s, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
   // 2. router logits, 3. top-8 + schedule
-  GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, s), "router_expert");
+  GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, s), "router_expert");
   const int rc_chunk = L.kind == 1 ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
   GM_STAGE(h, s, launch_topk_schedule(h->logits, L.pes, T, h->route_idx, h->route_w, h->expert_base,
                                  h->epr, rc_chunk, h->expert_offset, h->routes, h->route_pos,
@@ -497,6 +508,10 @@ int gm_moe_set_option(gm_moe_t* h, int option, long value) {
     case GM_OPT_TC_MIN_TOKENS:
       if (value < 1) return set_err(h, GM_EINVAL, "GM_OPT_TC_MIN_TOKENS must be >= 1");
       h->tc_min_tokens = value > 0x7FFFFFFF ? 0x7FFFFFFF : (int)value;
+      return GM_OK;
+    case GM_OPT_PDL:
+      if (value != 0 && value != 1) return set_err(h, GM_EINVAL, "GM_OPT_PDL must be 0 or 1");
+      h->pdl = value != 0;
       return GM_OK;
     case GM_OPT_PROFILE: {
       if (value != 0 && value != 1) return set_err(h, GM_EINVAL, "GM_OPT_PROFILE must be 0 or 1");

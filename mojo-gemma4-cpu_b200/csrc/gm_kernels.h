@@ -9,6 +9,9 @@ namespace gm {
 // Kernels launched through launch_k by the calling host thread (the handle
 // takes differences around its own launches to count them).
 inline thread_local long tls_kernel_launches = 0;
+// Programmatic dependent launch for launch_k on the calling thread (the
+// handle sets it from GM_OPT_PDL for the duration of a forward).
+inline thread_local bool tls_pdl = true;
 
 // Launch with programmatic stream serialisation (see pdl_wait/pdl_trigger):
 // every kernel launched this way calls pdl_wait() before touching memory that
@@ -26,7 +29,7 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = tls_pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
@@ -37,8 +40,16 @@ int max_route_chunks(int T, int epr, int rc);
 int router_ksplit(int T);
 size_t router_workspace_floats(int T);
 
+// Router logits as split-K partials [ksplit][T][E].  With a device error word
+// and T >= ROUTER_TC_MIN_TOKENS the tcgen05 kernel (router_tc.cu) runs,
+// otherwise the FMA kernel.
+constexpr int ROUTER_TC_MIN_TOKENS = 512;
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
-                                 const float* inv_rms, int T, float* logits, cudaStream_t s);
+                                 const float* inv_rms, int T, float* logits, int* err,
+                                 cudaStream_t s);
+cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
+                                    const float* inv_rms, int T, float* logits, int* err,
+                                    cudaStream_t s);
 cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_t s);
 cudaError_t launch_topk(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
                         float* route_w, cudaStream_t s);

@@ -122,11 +122,15 @@ int router_ksplit(int T) {
   return H / 256;  // 11 K slices of 256 for the warp-level kernel
 }
 
-size_t router_workspace_floats(int T) { return (size_t)router_ksplit(T) * T * E + T; }
+// partials [11][T][E], then inv_rms [T], then one device error word
+size_t router_workspace_floats(int T) { return (size_t)router_ksplit(T) * T * E + T + 1; }
 
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
-                                 const float* inv_rms, int T, float* logits, cudaStream_t s) {
+                                 const float* inv_rms, int T, float* logits, int* err,
+                                 cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
+  if (err && T >= ROUTER_TC_MIN_TOKENS)
+    return launch_router_logits_tc(x, wr, rscale, inv_rms, T, logits, err, s);
   const int ks = router_ksplit(T);
   return launch_k(router_logits_small_kernel, dim3((T + 7) / 8, E / 32, ks), dim3(256), 0, s, x,
                   wr, rscale, inv_rms, T, logits);
@@ -144,15 +148,17 @@ cudaError_t launch_topk(float* logits, const uint16_t* pes, int T, int32_t* rout
                   router_ksplit(T), pes, T, route_idx, route_w);
 }
 
-// Standalone router (gm_router_select): inv_rms into the tail of the workspace,
-// then logits and top-8.
+// Standalone router (gm_router_select): inv_rms and a device error word in
+// the tail of the workspace, then logits and top-8.
 cudaError_t launch_router(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
                           const uint16_t* pes, int T, float* logits, int32_t* route_idx,
                           float* route_w, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   float* inv = logits + (size_t)router_ksplit(T) * T * E;
-  cudaError_t e = launch_rms_inv(x, T, inv, s);
-  if (e == cudaSuccess) e = launch_router_logits(x, wr, rscale, inv, T, logits, s);
+  int* err = reinterpret_cast<int*>(inv + T);
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), s);
+  if (e == cudaSuccess) e = launch_rms_inv(x, T, inv, s);
+  if (e == cudaSuccess) e = launch_router_logits(x, wr, rscale, inv, T, logits, err, s);
   if (e == cudaSuccess) e = launch_topk(logits, pes, T, route_idx, route_w, s);
   return e;
 }

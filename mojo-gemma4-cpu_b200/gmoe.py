@@ -203,3 +203,4 @@ class MoeBlock:
 
 OPT_TC_MIN_TOKENS = 1
 OPT_PROFILE = 2
+OPT_PDL = 3

@@ -91,10 +91,14 @@ def run_router(g, x_np):
     gmoe.call("gm_router_select", x, g["router_centered"], g["router_scale"], g["per_expert_scale"],
               T, lg, idx, w, None)
     torch.cuda.synchronize()
-    return host(idx), host(w), host(lg)[:T * E].reshape(T, E)
+    ws = host(lg)
+    assert ws[-1:].view(np.int32)[0] == 0  # device error word (bounded waits)
+    return host(idx), host(w), ws[:T * E].reshape(T, E)
 
 
-@pytest.mark.parametrize("T", [1, 16, 64, 300])
+# T >= 512 runs the tcgen05 router (three-way exact bf16 split of the f32
+# activations), smaller T the FMA kernel
+@pytest.mark.parametrize("T", [1, 16, 64, 300, 600, 2000])
 @pytest.mark.parametrize("which", ["default", "stress"])
 def test_router_parity(T, which, layer_default, layer_stress):
     raw, ref, g = layer_default if which == "default" else layer_stress
