@@ -32,13 +32,18 @@ BF16_EXPERT_BYTES = (GU * H + H * I) * 2                     # 11,894,784
 FLOP_PER_TOKEN = TOPK * (2 * GU * H + 2 * H * I)              # 95,158,272
 
 WORKLOADS = {
-    # name: (tokens per step per GPU, weight format)
-    "bq-decode-b64": (64, "bq"),
-    "bq-decode-b8": (8, "bq"),
-    "bq-decode-b1": (1, "bq"),
-    "bf16-decode-b16": (16, "bf16"),
-    "bq-prefill-4k": (4096, "bq"),
-    "bf16-prefill-4k": (4096, "bf16"),
+    # name: (tokens per step, weight format, parallelism)
+    #   replicas:  N independent copies, tokens per GPU fixed (weak scaling)
+    #   ep-weak:   expert parallel over the N GPUs, tokens per GPU fixed
+    #   ep-strong: expert parallel, tokens per step fixed in total (split over N)
+    "bq-decode-b64": (64, "bq", "replicas"),
+    "bq-decode-b8": (8, "bq", "replicas"),
+    "bq-decode-b1": (1, "bq", "replicas"),
+    "bf16-decode-b16": (16, "bf16", "replicas"),
+    "bq-prefill-4k": (4096, "bq", "replicas"),
+    "bf16-prefill-4k": (4096, "bf16", "replicas"),
+    "ep-decode-b64": (64, "bq", "ep-weak"),
+    "ep-prefill-16k": (16384, "bq", "ep-strong"),
 }
 METRIC = "MoE-block tokens/s at 1/2/4/8 B200 (decode b=64, prefill 4k); % of roofline"
 
@@ -129,14 +134,18 @@ def build_layer(fmt, seed, device_rank):
     return synth.bf16_layer(raw), raw
 
 
-def register(blk, fmt, L):
+def register(blk, fmt, L, rank=0, degree=1):
+    """Registers this rank's experts [rank*128/degree, (rank+1)*128/degree)."""
+    epr = E // degree
+    lo, hi = rank * epr, (rank + 1) * epr
     if fmt == "bq":
-        blk.register_bq(0, L["gate_up"], L["gate_up_scale"], L["down"], L["down_scale"],
+        blk.register_bq(0, L["gate_up"][lo * GU:hi * GU], L["gate_up_scale"][lo * GU:hi * GU],
+                        L["down"][lo * H:hi * H], L["down_scale"][lo * H:hi * H],
                         L["router_centered"], L["router_scale"], L["per_expert_scale"],
                         L["pre_ffn_norm_2"])
     else:
-        blk.register_bf16(0, L["gate_up"], L["down"], L["router_proj"], L["router_scale"],
-                          L["per_expert_scale"], L["pre_ffn_norm_2"])
+        blk.register_bf16(0, L["gate_up"][lo:hi], L["down"][lo:hi], L["router_proj"],
+                          L["router_scale"], L["per_expert_scale"], L["pre_ffn_norm_2"])
 
 
 def cpu_baseline_sample(fmt, T, seconds, raw_cpu, xs_cpu):
@@ -185,7 +194,7 @@ def run_reference(args):
     except Exception:
         os.environ["GMOE_ORACLE_VARIANT"] = "portable"
     import synth
-    T, fmt = WORKLOADS[args.workload]
+    T, fmt, _ = WORKLOADS[args.workload]
     raw = {k: synth.to_numpy(v) for k, v in synth.make_layer(seed=0x6E6D6F45, device="cpu").items()}
     xs = [synth.to_numpy(synth.make_tokens(T, seed=s)) for s in range(2)]
     # each step is one forward of T tokens; the run is bounded by --cpu-seconds
@@ -218,12 +227,23 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    T, fmt = WORKLOADS[args.workload]
+    T, fmt, mode = WORKLOADS[args.workload]
     assert args.warmup >= 3, "at least 3 warm-up steps"
+    ep = mode.startswith("ep")
+    if mode == "ep-strong":
+        assert T % world == 0, "tokens per step must split evenly over the GPUs"
+        T //= world
+    degree = world if ep else 1
 
     L, raw = build_layer(fmt, 0x6E6D6F45, local)
-    blk = gmoe.MoeBlock(T, 1, device=local)
-    register(blk, fmt, L)
+    blk = gmoe.MoeBlock(T, 1, device=local, rank=rank if ep else 0, degree=degree)
+    register(blk, fmt, L, rank if ep else 0, degree)
+    if ep and world > 1:
+        # the NCCL id of the library's communicator, made on rank 0
+        uid = torch.tensor(list(gmoe.ep_unique_id()) if rank == 0 else [0] * gmoe.EP_UNIQUE_ID_BYTES,
+                           dtype=torch.uint8, device="cuda")
+        dist.broadcast(uid, 0)
+        blk.ep_init(bytes(uid.cpu().tolist()), world)
     g = torch.Generator(device="cuda")
     g.manual_seed(1000 + rank)
     xs = [torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16) for _ in range(args.batches)]
@@ -238,13 +258,31 @@ def main():
     # warm-up lasts at least 1 s so that the GPU's power and clocks have settled
     # under this load (and nvidia-smi sees it) before the timed region.
     with ClockSampler(local) as clk:
-        t_w = time.perf_counter()
-        i = 0
-        while i < args.warmup or time.perf_counter() - t_w < 1.0:
-            step(i)
-            i += 1
-            if i % 8 == 0:
-                torch.cuda.synchronize()
+        if dist:
+            # every rank must run the same forwards (the expert-parallel forward
+            # holds collectives): the warm-up length comes from the slowest rank
+            for i in range(3):
+                step(i)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for i in range(3):
+                step(i)
+            torch.cuda.synchronize()
+            per = torch.tensor([(time.perf_counter() - t0) / 3], device="cuda")
+            dist.all_reduce(per, op=dist.ReduceOp.MAX)
+            n_warm = max(args.warmup, int(1.0 / max(float(per.item()), 1e-6)) + 1)
+            for i in range(n_warm):
+                step(i)
+                if i % 8 == 7:
+                    torch.cuda.synchronize()
+        else:
+            t_w = time.perf_counter()
+            i = 0
+            while i < args.warmup or time.perf_counter() - t_w < 1.0:
+                step(i)
+                i += 1
+                if i % 8 == 0:
+                    torch.cuda.synchronize()
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
@@ -283,15 +321,17 @@ def main():
 
     # ---- roofline of the dominant kernel: CUDA events on the forward's stream
     # around each stage of the same forward (handle's stage profiler)
-    roof = roofline(blk, fmt, L, xs, outs, T, args.steps, stream, args.workload)
+    roof = roofline(blk, fmt, L, xs, outs, T, args.steps, stream, args.workload, rank, world, ep, dist)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "i8" if fmt == "bq" else "bf16",
+        "scaling": "strong" if mode == "ep-strong" else "weak", "vs_baseline": None,
+        "dtype": "i8" if fmt == "bq" else "bf16",
         "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights; random-init, no checkpoint)",
-        "config": {"workload": args.workload, "tokens_per_step": T, "weights": fmt,
-                   "parallelism": "replicas" if world > 1 else "single",
+        "config": {"workload": args.workload, "tokens_per_step": T * world, "tokens_per_gpu": T,
+                   "weights": fmt,
+                   "parallelism": ("ep%d" % world) if ep and world > 1 else ("replicas" if world > 1 else "single"),
                    "l2": "inputs larger than L2: %d distinct token batches, routed expert weights %.0f MB per step"
                          % (len(xs), roof.get("weight_mb", 0))},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
@@ -338,62 +378,72 @@ NCU_TRAFFIC = {
 }
 
 
-def stage_model(label, fmt, T, distinct):
+def stage_model(label, fmt, T, distinct, R):
     """(bound, algorithmic bytes or FLOPs per launch) of one forward stage.
+    T: this GPU's tokens; R: routes into this GPU's experts (T*8 without
+    expert parallelism); distinct: this GPU's experts that receive a route.
     Bytes count every operand once: routed expert weights (distinct experts
     x bytes per expert), activations read, results written."""
-    R = T * TOPK
     ksplit = H // 256
     if label == "bq_phase1_gate_up":
-        return "hbm", distinct * BQ_EXPERT_GU_BYTES + T * H + T * 4 + R * (I + 11 * 4)
+        return "hbm", distinct * BQ_EXPERT_GU_BYTES + R * (H + 4) // TOPK + R * (I + 11 * 4)
     if label == "bq_phase2_down":
         return "hbm", distinct * BQ_EXPERT_DN_BYTES + R * (I + 11 * 4) + R * H * 4
-    if label in ("bq_phase1_gate_up.tc",):
+    if label == "bq_phase1_gate_up.tc":
         return "tensor", 2.0 * R * GU * H
-    if label in ("bq_phase2_down.tc",):
+    if label == "bq_phase2_down.tc":
         return "tensor", 2.0 * R * H * I
     if label == "phase1_gate_up":
-        if T >= 1024:
+        if R >= 8 * 1024:
             return "tensor", 2.0 * R * GU * H
-        return "hbm", distinct * GU * H * 2 + T * H * 2 + R * I * 2
+        return "hbm", distinct * GU * H * 2 + R * H * 2 // TOPK + R * I * 2
     if label == "phase2_down":
-        if T >= 1024:
+        if R >= 8 * 1024:
             return "tensor", 2.0 * R * H * I
         return "hbm", distinct * H * I * 2 + R * I * 2 + R * H * 4
     if label == "router_expert":
         return "hbm", E * H * 2 + T * H * 2 + H * 2 + T * 4 + ksplit * T * E * 4
-    if label == "router_merge.schedule":
-        return "hbm", ksplit * T * E * 4 + R * (4 + 4 + 8 + 4)
-    if label in ("bq_norm_quant",):
+    if label in ("router_merge.schedule", "router_merge"):
+        return "hbm", ksplit * T * E * 4 + T * TOPK * (4 + 4 + 8 + 4)
+    if label == "bq_norm_quant":
         return "hbm", T * H * 2 + H * 2 + T * H + T * 8
-    if label in ("rms_norm",):
+    if label == "rms_norm":
         return "hbm", T * H * 2 + H * 2 + T * H * 2 + T * 4
     if label == "gather_rows":
         return "hbm", R * (H + 4) * 2 + R * 8
     if label == "combine":
-        return "hbm", R * H * 4 + T * H * 2 + R * 8
+        return "hbm", R * H * 4 + (R // TOPK) * H * 2 + R * 8
     return "hbm", None
 
 
-def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload):
+def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1, ep=False, dist=None):
     """Per-stage device times of the forward itself: the handle's stage
     profiler (GM_OPT_PROFILE) records CUDA events on the forward's stream
     around every stage; L2 is flushed (256 MB write) before each profiled
-    forward.  The dominant stage (largest share of the step) is reported
-    against its roofline; every stage is listed in the detail."""
+    forward.  The dominant kernel stage (largest share of the step among the
+    stages that launch this library's kernels) is reported against its
+    roofline; every stage is listed in the detail, the expert-parallel
+    exchanges with their NVLink bytes per second."""
     import torch
     import gmoe
     hbm, tf, src = peaks()
     s = stream
-    # distinct experts each batch routes to (the weight bytes a launch must read)
+    epr = E // world if ep else E
+    base = rank * epr if ep else 0
+    # routes into this GPU's experts and the distinct experts they reach, per
+    # batch (with expert parallelism: over every rank's tokens)
     lg = torch.empty(gmoe.lib().gm_router_workspace_bytes(T) // 4, dtype=torch.float32, device="cuda")
     idx = torch.empty(T, TOPK, dtype=torch.int32, device="cuda")
     w = torch.empty(T, TOPK, dtype=torch.float32, device="cuda")
     rw = L["router_centered"] if fmt == "bq" else L["router_proj"]
-    distinct = []
+    per_batch = []
     for x in xs:
         gmoe.call("gm_router_select", x, rw, L["router_scale"], L["per_expert_scale"], T, lg, idx, w, s)
-        distinct.append(int(torch.unique(idx).numel()))
+        hist = torch.bincount(idx.reshape(-1).long(), minlength=E)
+        if ep and dist is not None:
+            dist.all_reduce(hist)
+        mine = hist[base:base + epr]
+        per_batch.append((int((mine > 0).sum()), int(mine.sum())))
     torch.cuda.synchronize()
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
     n = max(5, min(steps, 50))
@@ -404,28 +454,36 @@ def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload):
     torch.cuda.synchronize()
     stats, launches = blk.profile_read()
     blk.profile(False)
-    mean_distinct = sum(distinct[i % len(xs)] for i in range(n)) / n
+    mean_distinct = sum(per_batch[i % len(xs)][0] for i in range(n)) / n
+    mean_R = sum(per_batch[i % len(xs)][1] for i in range(n)) / n
     step_ms = sum(v["avg_ms"] for v in stats.values())
+    row_bytes = (H + 4 + 64) if fmt == "bq" else (2 * H + 64)
     stages = {}
     for label, v in stats.items():
-        bound, amount = stage_model(label, fmt, T, mean_distinct)
+        bound, amount = stage_model(label, fmt, T, mean_distinct, mean_R)
+        sec = v["avg_ms"] / 1e3
         e = {"avg_us": round(v["avg_ms"] * 1e3, 2), "share": round(v["avg_ms"] / step_ms, 4),
              "kernels_per_call": v["kernels"] / max(v["calls"], 1)}
         if amount is not None:
-            sec = v["avg_ms"] / 1e3
             if bound == "tensor":
                 e["tflops"] = round(amount / sec / 1e12, 1)
                 e["frac"] = round(amount / sec / 1e12 / tf, 3)
             else:
                 e["gbs"] = round(amount / sec / 1e9, 1)
                 e["frac"] = round(amount / sec / 1e9 / hbm, 3)
+        if label in ("ep_dispatch", "ep_combine") and world > 1:
+            # bytes this GPU sends over NVLink (blocks of T rows to every peer)
+            per_row = row_bytes if label == "ep_dispatch" else 2 * H
+            e["nvlink_bytes_sent"] = (world - 1) * T * per_row
+            e["nvlink_gbs"] = round((world - 1) * T * per_row / sec / 1e9, 1)
         stages[label] = e
-    top = max(stats, key=lambda k: stats[k]["avg_ms"])
-    bound, amount = stage_model(top, fmt, T, mean_distinct)
+    cand = [k for k in stats if stats[k]["kernels"] > 0 and stage_model(k, fmt, T, 1, 1)[1] is not None]
+    top = max(cand, key=lambda k: stats[k]["avg_ms"])
+    bound, amount = stage_model(top, fmt, T, mean_distinct, mean_R)
     sec = stats[top]["avg_ms"] / 1e3
     traffic = NCU_TRAFFIC.get((workload, top))
     detail = {"kernel": top, "avg_launch_us": stats[top]["avg_ms"] * 1e3, "launches_timed": n,
-              "distinct_experts": mean_distinct, "stages": stages,
+              "distinct_experts": mean_distinct, "routes_to_this_gpu": mean_R, "stages": stages,
               "kernels_per_forward": launches / n}
     if bound == "tensor":
         ach = amount / sec / 1e12

@@ -146,6 +146,25 @@ typedef struct gm_stage_stat {
 int gm_moe_profile_read(gm_moe_t* h, gm_stage_stat_t* stats, int max_stats, int* n_stats,
                         long* kernel_launches);
 
+/* ------------------------------------------------------ expert parallelism --
+ * One process (and one handle) per GPU.  Replaces the reference's expert
+ * sharding by rank with replicated activations and the all-reduce of bf16
+ * partials (modeling/gemma4_topology.mojo:109-114, modeling/gemma_4_moe_bq.mojo:
+ * 711-713, kernels/reductions.mojo:186-204) by token-parallel dispatch and
+ * combine over NCCL: each rank passes only its own tokens to gm_moe_forward.
+ *
+ * gm_ep_unique_id: writes an NCCL unique id (GM_EP_UNIQUE_ID_BYTES bytes) on
+ * one rank; the caller distributes it to every rank.
+ * gm_moe_ep_init: joins the group (collective: every rank calls it with the
+ * same id; world == the handle's degree, rank == its rank).  Afterwards
+ * gm_moe_forward(h, layer, x, out, T, stream) takes this rank's T tokens
+ * (T <= max_tokens; every rank calls it for every layer, T may differ) and
+ * writes their complete MoE output: bf16(sum over ranks in rank order of each
+ * rank's bf16 partial), the value the reference's all-reduce produces. */
+#define GM_EP_UNIQUE_ID_BYTES 128
+int gm_ep_unique_id(void* out, size_t bytes);
+int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world);
+
 /* Synchronises the handle's device and reports (then clears) the device-side
  * error word that kernels with bounded waits write when a wait expires:
  * *device_error = 0 and GM_OK when none did, GM_ETIMEOUT otherwise. */

@@ -1,0 +1,38 @@
+// ep.h -- expert-parallel exchange (ep.cu): NCCL entry points, loaded at run
+// time so that single-GPU use needs no NCCL, and the plan/pack/final kernels.
+#pragma once
+#include <nccl.h>
+
+#include "gm_kernels.h"
+
+namespace gm {
+
+struct NcclApi {
+  bool loaded = false;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*group_start)() = nullptr;
+  ncclResult_t (*group_end)() = nullptr;
+  ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  const char* (*get_error_string)(ncclResult_t) = nullptr;
+};
+
+// NCCL loaded on first use (nullptr and *err set when it cannot be).
+const NcclApi* nccl_api(const char** err);
+
+// pos[t][d]: row of token t in destination d's send block, or -1; count[d].
+cudaError_t launch_ep_plan(const int32_t* route_idx, int T, int G, int epr, int32_t* pos,
+                           int32_t* count, cudaStream_t s);
+// Pack the send blocks [G][cap] (rows of row_bytes; x_sa may be null).
+cudaError_t launch_ep_pack(const void* x_rows, int row_bytes, const float* x_sa,
+                           const int32_t* route_idx, const float* route_w, int T, int G, int cap,
+                           const int32_t* pos, const int32_t* count, void* send_x, float* send_sa,
+                           int32_t* send_idx, float* send_w, cudaStream_t s);
+// out[t] = bf16(sum_d f32(contrib[d*cap + pos[t][d]])), d ascending.
+cudaError_t launch_ep_final(const uint16_t* contrib, const int32_t* pos, int T, int G, int cap,
+                            uint16_t* out, cudaStream_t s);
+
+}  // namespace gm

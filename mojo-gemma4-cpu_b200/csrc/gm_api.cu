@@ -7,6 +7,7 @@
 #include <vector>
 
 #include "../../include/gmoe.h"
+#include "ep.h"
 #include "gm_kernels.h"
 
 using namespace gm;
@@ -82,6 +83,22 @@ struct gm_moe {
   std::vector<PendingStage> pending;
   std::vector<cudaEvent_t> event_pool;
   std::vector<gm_stage_stat_t> stats;
+  // expert parallelism (gm_moe_ep_init): NCCL communicator and exchange buffers
+  int ws_tokens = 0;            // activation rows the workspace holds
+  ncclComm_t ep_comm = nullptr;
+  void* ep_buf = nullptr;
+  int32_t* ep_pos = nullptr;    // [max_tokens][degree]
+  int32_t* ep_count = nullptr;  // [degree]
+  uint8_t* ep_send_x = nullptr; // [degree*max_tokens][2*H] (int8 rows use the first H bytes)
+  float* ep_send_sa = nullptr;
+  int32_t* ep_send_idx = nullptr;
+  float* ep_send_w = nullptr;
+  uint8_t* ep_recv_x = nullptr;
+  float* ep_recv_sa = nullptr;
+  int32_t* ep_recv_idx = nullptr;
+  float* ep_recv_w = nullptr;
+  uint16_t* ep_partial = nullptr;  // [degree*max_tokens][H]
+  uint16_t* ep_contrib = nullptr;
 };
 
 namespace {
@@ -205,6 +222,48 @@ bool is_device_ptr(const void* p) {
   return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
+// (Re)allocates the workspace for `tokens` activation rows and carves it.
+int carve_workspace(gm_moe* h, int tokens) {
+  if (h->ws) {
+    cudaFree(h->ws);
+    h->ws = nullptr;
+  }
+  WsLayout L = ws_layout(tokens);
+  cudaError_t e = cudaMalloc(&h->ws, L.total);
+  if (e != cudaSuccess) {
+    h->ws = nullptr;
+    return set_err(h, GM_ENOMEM, "workspace of %zu bytes: %s", L.total, cudaGetErrorString(e));
+  }
+  h->ws_bytes = L.total;
+  h->ws_tokens = tokens;
+  char* b = static_cast<char*>(h->ws);
+  h->logits = reinterpret_cast<float*>(b + L.logits);
+  h->inv_rms = reinterpret_cast<float*>(b + L.inv_rms);
+  h->route_idx = reinterpret_cast<int32_t*>(b + L.route_idx);
+  h->route_w = reinterpret_cast<float*>(b + L.route_w);
+  h->route_pos = reinterpret_cast<int32_t*>(b + L.route_pos);
+  h->expert_offset = reinterpret_cast<int32_t*>(b + L.expert_offset);
+  h->chunk_off = reinterpret_cast<int32_t*>(b + L.chunk_off);
+  h->routes = reinterpret_cast<SparseRoute*>(b + L.routes);
+  h->x_i8 = reinterpret_cast<int8_t*>(b + L.x_i8);
+  h->x_sa = reinterpret_cast<float*>(b + L.x_sa);
+  h->x_normed = reinterpret_cast<uint16_t*>(b + L.x_normed);
+  h->bucket = reinterpret_cast<uint16_t*>(b + L.bucket);
+  h->bucket_i8 = reinterpret_cast<int8_t*>(b + L.bucket_i8);
+  h->bucket_sa = reinterpret_cast<float*>(b + L.bucket_sa);
+  h->ybuf = reinterpret_cast<float*>(b + L.ybuf);
+  h->x_stage = reinterpret_cast<uint16_t*>(b + L.x_stage);
+  h->out_stage = reinterpret_cast<uint16_t*>(b + L.out_stage);
+  h->xg = reinterpret_cast<int8_t*>(b + L.xg);
+  h->xg_sa = reinterpret_cast<float*>(b + L.xg_sa);
+  h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
+  h->sched_counts = reinterpret_cast<int32_t*>(b + L.sched_counts);
+  cudaMemset(h->dev_err, 0, sizeof(int));
+  h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)tokens * TOPK, H, 128) &&
+             make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)tokens * TOPK, I, 128);
+  return GM_OK;
+}
+
 // ---------------------------------------------------------------- profiler
 cudaEvent_t take_event(gm_moe* h) {
   if (!h->event_pool.empty()) {
@@ -285,6 +344,130 @@ struct StageScope {
   }
 };
 
+// Expert products and combine for Tn activation rows whose schedule
+// (expert_offset, routes, route_pos, chunk_off) is in the workspace: rows are
+// x_i8/x_sa (butterquant) or x_normed (bf16), route_idx their top-8.
+int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, const float* x_sa,
+                        const uint16_t* x_normed, const int32_t* route_idx, uint16_t* out,
+                        cudaStream_t s) {
+  if (L.kind == 1) {
+    if (L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
+      // prefill: routed rows gathered in schedule order, then the tcgen05 GEMM
+      GM_STAGE(h, s, launch_gather_rows(x_i8, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
+                                        h->xg_sa, s),
+               "gather_rows");
+      GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, Tn, h->xg_sa,
+                                      L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
+               "bq_phase1_gate_up.tc");
+      GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, Tn,
+                                      h->bucket_sa, h->routes, L.dn_scale, h->ybuf, h->dev_err, s),
+               "bq_phase2_down.tc");
+    } else {
+      GM_STAGE(h, s, launch_bq_phase1(x_i8, x_sa, h->expert_offset, h->routes, h->chunk_off, h->epr,
+                                      Tn, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
+               "bq_phase1_gate_up");
+      GM_STAGE(h, s, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
+                                      h->chunk_off, h->epr, Tn, L.dn_q, L.dn_scale, h->ybuf, true, s),
+               "bq_phase2_down");
+    }
+  } else {
+    GM_STAGE(h, s, launch_bf16_phase1(x_normed, h->expert_offset, h->routes, h->chunk_off, h->epr, Tn,
+                                      L.gu_bf16, h->bucket, s),
+             "phase1_gate_up");
+    GM_STAGE(h, s, launch_bf16_phase2(h->bucket, h->expert_offset, h->routes, h->chunk_off, h->epr, Tn,
+                                      L.dn_bf16, h->ybuf, s),
+             "phase2_down");
+  }
+  GM_STAGE(h, s, launch_combine(route_idx, h->route_pos, h->ybuf, Tn, out, s), "combine");
+  return GM_OK;
+}
+
+int nccl_check(gm_moe* h, ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return GM_OK;
+  const NcclApi* nc = nccl_api(nullptr);
+  return set_err(h, GM_ENCCL, "%s: %s", what, nc ? nc->get_error_string(r) : "NCCL error");
+}
+
+#define GM_NCCL(h, expr, what)                         \
+  do {                                                 \
+    int _rc = nccl_check((h), (expr), (what));         \
+    if (_rc != GM_OK) return _rc;                      \
+  } while (0)
+
+// Expert-parallel forward (after gm_moe_ep_init): this rank's T tokens in,
+// their full MoE output out; see ep.cu for the exchange.
+int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int T, cudaStream_t s) {
+  const NcclApi* nc = nccl_api(nullptr);
+  const int G = h->degree, cap = h->max_tokens, n = G * cap;
+  const bool bq = L.kind == 1;
+  const int row_bytes = bq ? H : 2 * H;
+  // 1. local activation prep, router logits and top-8 of this rank's tokens
+  if (T > 0) {
+    if (bq)
+      GM_STAGE(h, s, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, h->inv_rms, s), "bq_norm_quant");
+    else
+      GM_STAGE(h, s, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
+    GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, s),
+             "router_expert");
+    GM_STAGE(h, s, launch_topk(h->logits, L.pes, T, h->route_idx, h->route_w, s), "router_merge");
+  }
+  // 2. destinations and send blocks
+  GM_STAGE(h, s, launch_ep_plan(h->route_idx, T, G, h->epr, h->ep_pos, h->ep_count, s), "ep_plan");
+  GM_STAGE(h, s, launch_ep_pack(bq ? static_cast<const void*>(h->x_i8) : static_cast<const void*>(h->x_normed),
+                                row_bytes, bq ? h->x_sa : nullptr, h->route_idx, h->route_w, T, G, cap,
+                                h->ep_pos, h->ep_count, h->ep_send_x, h->ep_send_sa, h->ep_send_idx,
+                                h->ep_send_w, s),
+           "ep_pack");
+  // 3. dispatch: block p of every array goes to rank p
+  {
+    StageScope scope(h, "ep_dispatch", s);
+    GM_NCCL(h, nc->group_start(), "ep dispatch");
+    for (int p = 0; p < G; ++p) {
+      const size_t r0 = (size_t)p * cap;
+      GM_NCCL(h, nc->send(h->ep_send_x + r0 * row_bytes, (size_t)cap * row_bytes, ncclUint8, p, h->ep_comm, s), "send x");
+      GM_NCCL(h, nc->recv(h->ep_recv_x + r0 * row_bytes, (size_t)cap * row_bytes, ncclUint8, p, h->ep_comm, s), "recv x");
+      if (bq) {
+        GM_NCCL(h, nc->send(h->ep_send_sa + r0, (size_t)cap, ncclFloat32, p, h->ep_comm, s), "send sa");
+        GM_NCCL(h, nc->recv(h->ep_recv_sa + r0, (size_t)cap, ncclFloat32, p, h->ep_comm, s), "recv sa");
+      }
+      GM_NCCL(h, nc->send(h->ep_send_idx + r0 * TOPK, (size_t)cap * TOPK, ncclInt32, p, h->ep_comm, s), "send idx");
+      GM_NCCL(h, nc->recv(h->ep_recv_idx + r0 * TOPK, (size_t)cap * TOPK, ncclInt32, p, h->ep_comm, s), "recv idx");
+      GM_NCCL(h, nc->send(h->ep_send_w + r0 * TOPK, (size_t)cap * TOPK, ncclFloat32, p, h->ep_comm, s), "send w");
+      GM_NCCL(h, nc->recv(h->ep_recv_w + r0 * TOPK, (size_t)cap * TOPK, ncclFloat32, p, h->ep_comm, s), "recv w");
+    }
+    GM_NCCL(h, nc->group_end(), "ep dispatch");
+  }
+  // 4. this rank's experts over the n received rows (unused rows route nowhere)
+  const int rc_chunk = bq ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
+  if (n <= 1024)
+    GM_STAGE(h, s, launch_build_schedule(h->ep_recv_idx, h->ep_recv_w, n, h->expert_base, h->epr, rc_chunk,
+                                         h->expert_offset, h->routes, h->route_pos, h->chunk_off, s),
+             "ep_schedule");
+  else
+    GM_STAGE(h, s, launch_schedule_multi(h->ep_recv_idx, h->ep_recv_w, n, h->expert_base, h->epr, rc_chunk,
+                                         h->sched_counts, h->expert_offset, h->routes, h->route_pos,
+                                         h->chunk_off, s),
+             "ep_schedule");
+  int rc = experts_and_combine(h, L, n, reinterpret_cast<const int8_t*>(h->ep_recv_x), h->ep_recv_sa,
+                               reinterpret_cast<const uint16_t*>(h->ep_recv_x), h->ep_recv_idx,
+                               h->ep_partial, s);
+  if (rc) return rc;
+  // 5. combine exchange: partial rows go back to the rank they came from
+  {
+    StageScope scope(h, "ep_combine", s);
+    GM_NCCL(h, nc->group_start(), "ep combine");
+    for (int p = 0; p < G; ++p) {
+      const size_t r0 = (size_t)p * cap * H;
+      GM_NCCL(h, nc->send(h->ep_partial + r0, (size_t)cap * H, ncclBfloat16, p, h->ep_comm, s), "send partial");
+      GM_NCCL(h, nc->recv(h->ep_contrib + r0, (size_t)cap * H, ncclBfloat16, p, h->ep_comm, s), "recv partial");
+    }
+    GM_NCCL(h, nc->group_end(), "ep combine");
+  }
+  // 6. sum of the ranks' partials in rank order
+  GM_STAGE(h, s, launch_ep_final(h->ep_contrib, h->ep_pos, T, G, cap, out, s), "ep_final");
+  return GM_OK;
+}
+
 }  // namespace
 
 namespace gm {
@@ -328,40 +511,11 @@ int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, in
   h->epr = E / degree;
   h->expert_base = rank * h->epr;
   h->layers.resize(num_layers);
-  WsLayout L = ws_layout(max_tokens);
-  cudaError_t e = cudaMalloc(&h->ws, L.total);
-  if (e != cudaSuccess) {
-    int rc = set_err(nullptr, GM_ENOMEM, "gm_moe_create: workspace of %zu bytes: %s", L.total,
-                     cudaGetErrorString(e));
+  int rc = carve_workspace(h, max_tokens);
+  if (rc != GM_OK) {
     delete h;
     return rc;
   }
-  h->ws_bytes = L.total;
-  char* b = static_cast<char*>(h->ws);
-  h->logits = reinterpret_cast<float*>(b + L.logits);
-  h->inv_rms = reinterpret_cast<float*>(b + L.inv_rms);
-  h->route_idx = reinterpret_cast<int32_t*>(b + L.route_idx);
-  h->route_w = reinterpret_cast<float*>(b + L.route_w);
-  h->route_pos = reinterpret_cast<int32_t*>(b + L.route_pos);
-  h->expert_offset = reinterpret_cast<int32_t*>(b + L.expert_offset);
-  h->chunk_off = reinterpret_cast<int32_t*>(b + L.chunk_off);
-  h->routes = reinterpret_cast<SparseRoute*>(b + L.routes);
-  h->x_i8 = reinterpret_cast<int8_t*>(b + L.x_i8);
-  h->x_sa = reinterpret_cast<float*>(b + L.x_sa);
-  h->x_normed = reinterpret_cast<uint16_t*>(b + L.x_normed);
-  h->bucket = reinterpret_cast<uint16_t*>(b + L.bucket);
-  h->bucket_i8 = reinterpret_cast<int8_t*>(b + L.bucket_i8);
-  h->bucket_sa = reinterpret_cast<float*>(b + L.bucket_sa);
-  h->ybuf = reinterpret_cast<float*>(b + L.ybuf);
-  h->x_stage = reinterpret_cast<uint16_t*>(b + L.x_stage);
-  h->out_stage = reinterpret_cast<uint16_t*>(b + L.out_stage);
-  h->xg = reinterpret_cast<int8_t*>(b + L.xg);
-  h->xg_sa = reinterpret_cast<float*>(b + L.xg_sa);
-  h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
-  h->sched_counts = reinterpret_cast<int32_t*>(b + L.sched_counts);
-  cudaMemset(h->dev_err, 0, sizeof(int));
-  h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)max_tokens * TOPK, H, 128) &&
-             make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)max_tokens * TOPK, I, 128);
   if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
     cudaFree(h->ws);
     delete h;
@@ -377,6 +531,11 @@ int gm_moe_destroy(gm_moe_t* h) {
   for (auto& L : h->layers) free_layer(L);
   drain_profile(h);
   for (cudaEvent_t e : h->event_pool) cudaEventDestroy(e);
+  if (h->ep_comm) {
+    cudaDeviceSynchronize();
+    if (const NcclApi* nc = nccl_api(nullptr)) nc->comm_destroy(h->ep_comm);
+  }
+  if (h->ep_buf) cudaFree(h->ep_buf);
   if (h->ws) cudaFree(h->ws);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
   delete h;
@@ -450,11 +609,12 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
   if (L.kind == 0) return set_err(h, GM_ESTATE, "layer %d has no registered weights", layer);
   if (T < 0 || T > h->max_tokens)
     return set_err(h, GM_EINVAL, "T=%d outside [0, max_tokens=%d]", T, h->max_tokens);
-  if (T == 0) return GM_OK;
   if (!x || !out) return set_err(h, GM_EINVAL, "NULL x/out");
   cudaStream_t s = S(stream);
   if (h->pending.size() > 4096 && (rc = drain_profile(h))) return rc;  // bound the event backlog
   PdlScope pdl_scope(h->pdl);
+  if (h->ep_comm) return ep_forward(h, L, static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), T, s);
+  if (T == 0) return GM_OK;
   const uint16_t* xb = static_cast<const uint16_t*>(x);
   // 1. activation norm (+ inv_rms shared with the router)
   if (L.kind == 1)
@@ -469,37 +629,8 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
                                  h->chunk_off, h->sched_counts, s),
          "router_merge.schedule");
   // 4. experts, 5. combine
-  if (L.kind == 1) {
-    if (L.has_tc && h->tc_ok && T >= h->tc_min_tokens) {
-      // prefill: routed rows gathered in schedule order, then the tcgen05 GEMM
-      GM_STAGE(h, s, launch_gather_rows(h->x_i8, h->x_sa, h->routes, h->expert_offset, h->epr, T, h->xg,
-                                   h->xg_sa, s),
-             "gather_rows");
-      GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, T, h->xg_sa,
-                                 L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
-             "bq_phase1_gate_up.tc");
-      GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, T,
-                                 h->bucket_sa, h->routes, L.dn_scale, h->ybuf, h->dev_err, s),
-             "bq_phase2_down.tc");
-    } else {
-      GM_STAGE(h, s, launch_bq_phase1(h->x_i8, h->x_sa, h->expert_offset, h->routes, h->chunk_off,
-                                 h->epr, T, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
-             "bq_phase1_gate_up");
-      GM_STAGE(h, s, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
-                                 h->chunk_off, h->epr, T, L.dn_q, L.dn_scale, h->ybuf, true, s),
-             "bq_phase2_down");
-    }
-  } else {
-    GM_STAGE(h, s, launch_bf16_phase1(h->x_normed, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
-                                 L.gu_bf16, h->bucket, s),
-           "phase1_gate_up");
-    GM_STAGE(h, s, launch_bf16_phase2(h->bucket, h->expert_offset, h->routes, h->chunk_off, h->epr, T,
-                                 L.dn_bf16, h->ybuf, s),
-           "phase2_down");
-  }
-  GM_STAGE(h, s, launch_combine(h->route_idx, h->route_pos, h->ybuf, T, static_cast<uint16_t*>(out), s),
-         "combine");
-  return GM_OK;
+  return experts_and_combine(h, L, T, h->x_i8, h->x_sa, h->x_normed, h->route_idx,
+                             static_cast<uint16_t*>(out), s);
 }
 
 int gm_moe_set_option(gm_moe_t* h, int option, long value) {
@@ -541,6 +672,64 @@ int gm_moe_profile_read(gm_moe_t* h, gm_stage_stat_t* stats, int max_stats, int*
   *n_stats = n;
   if (kernel_launches) *kernel_launches = h->launches;
   return rc;
+}
+
+int gm_ep_unique_id(void* out, size_t bytes) {
+  if (!out || bytes < sizeof(ncclUniqueId))
+    return set_err(nullptr, GM_EINVAL, "gm_ep_unique_id: need %zu bytes", sizeof(ncclUniqueId));
+  const char* why = nullptr;
+  const NcclApi* nc = nccl_api(&why);
+  if (!nc) return set_err(nullptr, GM_ENCCL, "%s", why ? why : "NCCL unavailable");
+  ncclUniqueId id;
+  const ncclResult_t r = nc->get_unique_id(&id);
+  if (r != ncclSuccess) return set_err(nullptr, GM_ENCCL, "ncclGetUniqueId: %s", nc->get_error_string(r));
+  memcpy(out, &id, sizeof id);
+  return GM_OK;
+}
+
+int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
+  if (!h || !unique_id) return set_err(h, GM_EINVAL, "gm_moe_ep_init: NULL argument");
+  if (h->ep_comm) return set_err(h, GM_ESTATE, "gm_moe_ep_init: already initialised");
+  if (world != h->degree || world < 1 || world > 8)
+    return set_err(h, GM_EINVAL, "gm_moe_ep_init: world=%d must equal the handle's degree (%d), 1..8",
+                   world, h->degree);
+  const char* why = nullptr;
+  const NcclApi* nc = nccl_api(&why);
+  if (!nc) return set_err(h, GM_ENCCL, "%s", why ? why : "NCCL unavailable");
+  GM_TRY(h, cudaSetDevice(h->device), "ep_init");
+  // the expert stage sees world * max_tokens received rows
+  int rc = carve_workspace(h, world * h->max_tokens);
+  if (rc) return rc;
+  const size_t cap = (size_t)h->max_tokens, n = (size_t)world * cap;
+  Carve c;
+  const size_t o_pos = c.take<int32_t>(cap * world), o_cnt = c.take<int32_t>(8);
+  const size_t o_sx = c.take<uint8_t>(n * 2 * H), o_ssa = c.take<float>(n),
+               o_sidx = c.take<int32_t>(n * TOPK), o_sw = c.take<float>(n * TOPK);
+  const size_t o_rx = c.take<uint8_t>(n * 2 * H), o_rsa = c.take<float>(n),
+               o_ridx = c.take<int32_t>(n * TOPK), o_rw = c.take<float>(n * TOPK);
+  const size_t o_part = c.take<uint16_t>(n * H), o_con = c.take<uint16_t>(n * H);
+  GM_TRY(h, cudaMalloc(&h->ep_buf, align_up(c.off, 256)), "ep buffers");
+  char* b = static_cast<char*>(h->ep_buf);
+  h->ep_pos = reinterpret_cast<int32_t*>(b + o_pos);
+  h->ep_count = reinterpret_cast<int32_t*>(b + o_cnt);
+  h->ep_send_x = reinterpret_cast<uint8_t*>(b + o_sx);
+  h->ep_send_sa = reinterpret_cast<float*>(b + o_ssa);
+  h->ep_send_idx = reinterpret_cast<int32_t*>(b + o_sidx);
+  h->ep_send_w = reinterpret_cast<float*>(b + o_sw);
+  h->ep_recv_x = reinterpret_cast<uint8_t*>(b + o_rx);
+  h->ep_recv_sa = reinterpret_cast<float*>(b + o_rsa);
+  h->ep_recv_idx = reinterpret_cast<int32_t*>(b + o_ridx);
+  h->ep_recv_w = reinterpret_cast<float*>(b + o_rw);
+  h->ep_partial = reinterpret_cast<uint16_t*>(b + o_part);
+  h->ep_contrib = reinterpret_cast<uint16_t*>(b + o_con);
+  GM_TRY(h, cudaMemset(h->ep_buf, 0, align_up(c.off, 256)), "ep buffers");
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof id);
+  ncclComm_t comm = nullptr;
+  const ncclResult_t r = nc->comm_init_rank(&comm, world, id, h->rank);
+  if (r != ncclSuccess) return set_err(h, GM_ENCCL, "ncclCommInitRank: %s", nc->get_error_string(r));
+  h->ep_comm = comm;
+  return GM_OK;
 }
 
 int gm_moe_device_status(gm_moe_t* h, int* device_error) {

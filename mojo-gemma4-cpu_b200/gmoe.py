@@ -47,6 +47,8 @@ SIGNATURES = {
     "gm_moe_forward_sync": (_i32, [_vp, _i32, _vp, _vp, _i32]),
     "gm_moe_set_option": (_i32, [_vp, _i32, _i64]),
     "gm_moe_device_status": (_i32, [_vp, C.POINTER(_i32)]),
+    "gm_ep_unique_id": (_i32, [_vp, _sz]),
+    "gm_moe_ep_init": (_i32, [_vp, _vp, _i32]),
     "gm_moe_profile_read": (_i32, [_vp, C.POINTER(StageStat), _i32, C.POINTER(_i32), C.POINTER(_i64)]),
     "gm_router_select": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "gm_router_select_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),
@@ -194,6 +196,11 @@ class MoeBlock:
                 "avg_ms": st.total_ms / st.calls if st.calls else 0.0}
         return stats, launches.value
 
+    def ep_init(self, unique_id, world):
+        """Join the expert-parallel group (collective over `world` processes)."""
+        buf = C.create_string_buffer(bytes(unique_id), len(unique_id))
+        check(lib().gm_moe_ep_init(self.h, buf, world), self.h)
+
     def device_status(self):
         """Synchronises; raises GmoeError(GM_ETIMEOUT) if a bounded wait expired."""
         e = C.c_int(0)
@@ -204,3 +211,12 @@ class MoeBlock:
 OPT_TC_MIN_TOKENS = 1
 OPT_PROFILE = 2
 OPT_PDL = 3
+EP_UNIQUE_ID_BYTES = 128
+
+
+def ep_unique_id():
+    """A fresh NCCL unique id (bytes) for gm_moe_ep_init; made on one rank and
+    sent to the others by the caller."""
+    buf = C.create_string_buffer(EP_UNIQUE_ID_BYTES)
+    check(lib().gm_ep_unique_id(buf, EP_UNIQUE_ID_BYTES))
+    return buf.raw
