@@ -43,8 +43,16 @@ WORKLOADS = {
     "bq-prefill-4k": (4096, "bq", "replicas"),
     "bf16-prefill-4k": (4096, "bf16", "replicas"),
     "ep-decode-b64": (64, "bq", "ep-weak"),
+    # Zipf(1.1) routing (expert i-1 receives 8T*i^-1.1/sum of the routes, capped at T)
+    "bq-prefill-4k-zipf": (4096, "bq", "replicas"),
+    "bf16-prefill-4k-zipf": (4096, "bf16", "replicas"),
     "ep-prefill-16k": (16384, "bq", "ep-strong"),
 }
+ZIPF = {"bq-prefill-4k-zipf", "bf16-prefill-4k-zipf", "ep-prefill-16k"}
+# config 5: one decode step of 64 sequences through 30 MoE layers (distinct
+# weights per layer, the attention block between layers is an identity stand-in)
+WORKLOADS["bq-decode-b64-30L"] = (64, "bq", "replicas")
+LAYERS = {"bq-decode-b64-30L": 30}
 METRIC = "MoE-block tokens/s at 1/2/4/8 B200 (decode b=64, prefill 4k); % of roofline"
 
 
@@ -126,31 +134,51 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def build_layer(fmt, seed, device_rank):
+def build_layer(fmt, seed, device_rank, zipf=False):
     import synth
     raw = synth.make_layer(seed=seed, device="cuda")
+    if zipf:
+        raw = synth.apply_zipf(raw)
     if fmt == "bq":
         return synth.bq_layer(raw), raw
     return synth.bf16_layer(raw), raw
 
 
-def register(blk, fmt, L, rank=0, degree=1):
+def register(blk, fmt, L, rank=0, degree=1, layer=0):
     """Registers this rank's experts [rank*128/degree, (rank+1)*128/degree)."""
     epr = E // degree
     lo, hi = rank * epr, (rank + 1) * epr
     if fmt == "bq":
-        blk.register_bq(0, L["gate_up"][lo * GU:hi * GU], L["gate_up_scale"][lo * GU:hi * GU],
+        blk.register_bq(layer, L["gate_up"][lo * GU:hi * GU], L["gate_up_scale"][lo * GU:hi * GU],
                         L["down"][lo * H:hi * H], L["down_scale"][lo * H:hi * H],
                         L["router_centered"], L["router_scale"], L["per_expert_scale"],
                         L["pre_ffn_norm_2"])
     else:
-        blk.register_bf16(0, L["gate_up"][lo:hi], L["down"][lo:hi], L["router_proj"],
+        blk.register_bf16(layer, L["gate_up"][lo:hi], L["down"][lo:hi], L["router_proj"],
                           L["router_scale"], L["per_expert_scale"], L["pre_ffn_norm_2"])
+
+
+def host_info():
+    """nproc, CPU model and NUMA node count of this host."""
+    model = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    try:
+        numa = len([d for d in os.listdir("/sys/devices/system/node") if d.startswith("node")])
+    except OSError:
+        numa = None
+    return {"nproc": os.cpu_count(), "cpu_model": model, "numa_nodes": numa}
 
 
 def cpu_baseline_sample(fmt, T, seconds, raw_cpu, xs_cpu):
     """Time the oracle (CPU restatement of the reference path, all host cores)
-    on repeated forwards of the same workload until `seconds` have elapsed."""
+    on forwards of the workload; returns (tokens/s at the median sample,
+    samples, warm-up forwards, threads)."""
     from oracle import oracle as O
     import numpy as np
     import synth
@@ -169,17 +197,22 @@ def cpu_baseline_sample(fmt, T, seconds, raw_cpu, xs_cpu):
              "pes": raw_cpu["per_expert_scale"], "gamma2": raw_cpu["pre_ffn_norm_2"],
              "w_gu": raw_cpu["gate_up"], "w_dn": raw_cpu["down"]}
         fwd = O.bf16_forward
-    fwd(xs_cpu[0][:min(T, 4)], L)  # warm (page in weights)
-    n_tok, t0, i = 0, time.perf_counter(), 0
-    while True:
-        x = xs_cpu[i % len(xs_cpu)]
+    # the reference harness protocol (benchmarks/bench_harness.mojo:7,62-84):
+    # up to 30 warm-up forwards, then up to 600 timed samples, rate from the
+    # median sample -- bounded here by `seconds` (a fifth for the warm-up)
+    fwd(xs_cpu[0][:min(T, 4)], L)  # page the weights in
+    t0, warm = time.perf_counter(), 0
+    while warm < 30 and time.perf_counter() - t0 < 0.2 * seconds:
+        fwd(xs_cpu[warm % len(xs_cpu)], L)
+        warm += 1
+    samples, t1 = [], time.perf_counter()
+    while len(samples) < 600 and (time.perf_counter() - t1 < 0.8 * seconds or len(samples) < 3):
+        x = xs_cpu[len(samples) % len(xs_cpu)]
+        ts = time.perf_counter()
         fwd(x, L)
-        n_tok += x.shape[0]
-        i += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    return n_tok / el, i, O.lib().orc_num_threads()
+        samples.append(time.perf_counter() - ts)
+    p50 = float(np.median(samples))
+    return T / p50, len(samples), warm, O.lib().orc_num_threads()
 
 
 def run_reference(args):
@@ -195,17 +228,24 @@ def run_reference(args):
         os.environ["GMOE_ORACLE_VARIANT"] = "portable"
     import synth
     T, fmt, _ = WORKLOADS[args.workload]
-    raw = {k: synth.to_numpy(v) for k, v in synth.make_layer(seed=0x6E6D6F45, device="cpu").items()}
-    xs = [synth.to_numpy(synth.make_tokens(T, seed=s)) for s in range(2)]
+    zipf = args.workload in ZIPF
+    layer = synth.make_layer(seed=0x6E6D6F45, device="cpu")
+    if zipf:
+        layer = synth.apply_zipf(layer)
+    raw = {k: synth.to_numpy(v) for k, v in layer.items()}
+    xs = [synth.to_numpy(synth.zipf_tokens(T, seed=s) if zipf else synth.make_tokens(T, seed=s))
+          for s in range(2)]
     # each step is one forward of T tokens; the run is bounded by --cpu-seconds
-    rate, iters, cores = cpu_baseline_sample(fmt, T, max(1.0, args.cpu_seconds), raw, xs)
+    rate, iters, warm, cores = cpu_baseline_sample(fmt, T, max(1.0, args.cpu_seconds), raw, xs)
+    rate /= LAYERS.get(args.workload, 1)
     line = {"metric": METRIC, "value": rate, "unit": "tokens/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": iters, "warmup": 1, "ms_per_step": 1e3 * T / rate,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "i8" if fmt == "bq" else "bf16", "data": "synthetic",
             "config": {"workload": args.workload, "tokens_per_step": T, "weights": fmt},
-            "cpu_baseline": {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": "%d forwards of %d tokens (%.0f s) of the C++ restatement" % (iters, T, args.cpu_seconds)},
+            "cpu_baseline": dict({"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                  "sample": "%d warm-up + %d timed forwards of %d tokens, median, of the C++ "
+                                            "restatement" % (warm, iters, T)}, **host_info()),
             "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -235,9 +275,16 @@ def main():
         T //= world
     degree = world if ep else 1
 
-    L, raw = build_layer(fmt, 0x6E6D6F45, local)
-    blk = gmoe.MoeBlock(T, 1, device=local, rank=rank if ep else 0, degree=degree)
+    zipf = args.workload in ZIPF
+    nl = LAYERS.get(args.workload, 1)
+    L, raw = build_layer(fmt, 0x6E6D6F45, local, zipf)
+    blk = gmoe.MoeBlock(T, nl, device=local, rank=rank if ep else 0, degree=degree)
     register(blk, fmt, L, rank if ep else 0, degree)
+    for layer in range(1, nl):
+        Ll, _ = build_layer(fmt, 0x6E6D6F45 + 7919 * layer, local, zipf)
+        register(blk, fmt, Ll, rank if ep else 0, degree, layer=layer)
+        del Ll
+    torch.cuda.empty_cache()
     if ep and world > 1:
         # the NCCL id of the library's communicator, made on rank 0
         uid = torch.tensor(list(gmoe.ep_unique_id()) if rank == 0 else [0] * gmoe.EP_UNIQUE_ID_BYTES,
@@ -246,12 +293,25 @@ def main():
         blk.ep_init(bytes(uid.cpu().tolist()), world)
     g = torch.Generator(device="cuda")
     g.manual_seed(1000 + rank)
-    xs = [torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16) for _ in range(args.batches)]
+    if zipf:
+        import synth
+        xs = [synth.zipf_tokens(T, seed=1000 + 97 * rank + b, device="cuda") for b in range(args.batches)]
+    else:
+        xs = [torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16) for _ in range(args.batches)]
     outs = [torch.empty(T, H, dtype=torch.bfloat16, device="cuda") for _ in range(args.batches)]
     stream = torch.cuda.current_stream()
 
-    def step(i):
-        blk.forward(0, xs[i % len(xs)], outs[i % len(xs)], T, stream)
+    tmp = [torch.empty(T, H, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+
+    def step(i, x=None, out=None):
+        """One step: the MoE block of every layer, each layer's output the next
+        layer's input."""
+        x = xs[i % len(xs)] if x is None else x
+        out = outs[i % len(xs)] if out is None else out
+        for layer in range(nl):
+            dst = out if layer == nl - 1 else tmp[layer % 2]
+            blk.forward(layer, x, dst, T, stream)
+            x = dst
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     # The clock sampler runs from the warm-up through the timed region; the
@@ -302,16 +362,30 @@ def main():
         dist.barrier()
     value = world * T * args.steps / (ms / 1e3)
 
-    # ---- end to end through the blocking entry point with pinned host buffers
+    # ---- end to end through the public API with pinned host buffers: the
+    # blocking entry point for one layer; with several layers the host batch is
+    # copied in, every layer runs on the device and the result is copied out
     xh = [x.cpu().pin_memory() for x in xs]
     oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xin = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    yout = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+
+    def e2e_step(i):
+        if nl == 1:
+            blk.forward_sync(0, xh[i % len(xh)], oh, T)
+        else:
+            xin.copy_(xh[i % len(xh)], non_blocking=True)
+            step(i, xin, yout)
+            oh.copy_(yout, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
     for i in range(3):
-        blk.forward_sync(0, xh[i % len(xh)], oh, T)
+        e2e_step(i)
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
     for i in range(args.steps):
-        blk.forward_sync(0, xh[i % len(xh)], oh, T)
+        e2e_step(i)
     e2e_s = time.perf_counter() - t0
     if dist:
         t = torch.tensor([e2e_s], device="cuda")
@@ -330,7 +404,7 @@ def main():
         "dtype": "i8" if fmt == "bq" else "bf16",
         "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights; random-init, no checkpoint)",
         "config": {"workload": args.workload, "tokens_per_step": T * world, "tokens_per_gpu": T,
-                   "weights": fmt,
+                   "weights": fmt, "layers": nl,
                    "parallelism": ("ep%d" % world) if ep and world > 1 else ("replicas" if world > 1 else "single"),
                    "l2": "inputs larger than L2: %d distinct token batches, routed expert weights %.0f MB per step"
                          % (len(xs), roof.get("weight_mb", 0))},
@@ -339,6 +413,7 @@ def main():
         "gpu_launches": timed_launches,
         "roofline": {k: roof[k] for k in ("bound", "achieved", "peak", "unit", "frac", "traffic")},
         "roofline_detail": roof["detail"],
+        "routing": dict(roof["routing"], kind="zipf(1.1)" if zipf else "uniform"),
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -362,11 +437,17 @@ def cpu_leg(fmt, T, args, raw_dev):
     import torch
     g = torch.Generator(device="cpu")
     g.manual_seed(7)
-    xs = [synth.to_numpy(torch.randn(T, H, generator=g).to(torch.bfloat16)) for _ in range(2)]
-    rate, iters, cores = cpu_baseline_sample(fmt, T, args.cpu_seconds, raw_cpu, xs)
-    return {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": "%d forwards of %d tokens over %.0f s (C++ restatement of the reference path, OpenMP)"
-                      % (iters, T, args.cpu_seconds)}
+    if args.workload in ZIPF:
+        xs = [synth.to_numpy(synth.zipf_tokens(T, seed=7 + b)) for b in range(2)]
+    else:
+        xs = [synth.to_numpy(torch.randn(T, H, generator=g).to(torch.bfloat16)) for _ in range(2)]
+    rate, n, warm, cores = cpu_baseline_sample(fmt, T, args.cpu_seconds, raw_cpu, xs)
+    nl = LAYERS.get(args.workload, 1)
+    return dict({"value": rate / nl, "unit": "tokens/s", "cores": cores, "kind": "port",
+                 "sample": "%d warm-up + %d timed forwards of %d tokens, median (C++ restatement of "
+                           "the reference path, OpenMP)%s" % (warm, n, T, (
+                               "; one layer timed, rate divided by %d layers" % nl) if nl > 1 else "")},
+                **host_info())
 
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of
@@ -392,6 +473,10 @@ def stage_model(label, fmt, T, distinct, R):
     if label == "bq_phase1_gate_up.tc":
         return "tensor", 2.0 * R * GU * H
     if label == "bq_phase2_down.tc":
+        return "tensor", 2.0 * R * H * I
+    if label == "phase1_gate_up.tc":
+        return "tensor", 2.0 * R * GU * H
+    if label == "phase2_down.tc":
         return "tensor", 2.0 * R * H * I
     if label == "phase1_gate_up":
         if R >= 8 * 1024:
@@ -437,11 +522,13 @@ def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1,
     w = torch.empty(T, TOPK, dtype=torch.float32, device="cuda")
     rw = L["router_centered"] if fmt == "bq" else L["router_proj"]
     per_batch = []
+    hist_sum = torch.zeros(E, dtype=torch.long, device="cuda")
     for x in xs:
         gmoe.call("gm_router_select", x, rw, L["router_scale"], L["per_expert_scale"], T, lg, idx, w, s)
         hist = torch.bincount(idx.reshape(-1).long(), minlength=E)
         if ep and dist is not None:
             dist.all_reduce(hist)
+        hist_sum += hist
         mine = hist[base:base + epr]
         per_batch.append((int((mine > 0).sum()), int(mine.sum())))
     torch.cuda.synchronize()
@@ -499,6 +586,18 @@ def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1,
     roof["traffic"] = traffic
     roof["detail"] = detail
     roof["weight_mb"] = mean_distinct * (BQ_EXPERT_BYTES if fmt == "bq" else BF16_EXPERT_BYTES) / 1e6
+    # realised routing of the timed batches (all ranks' tokens with expert parallelism)
+    h = (hist_sum.double() / len(xs)).cpu().numpy()
+    tokens = T * (world if ep else 1)
+    load = {"max_expert_share": round(float(h.max() / h.sum()), 4),
+            "expert_routes_top8": [int(v) for v in h[:8]],
+            "expert_routes_last4": [int(v) for v in h[-4:]]}
+    if ep and world > 1:
+        load["routes_per_gpu"] = [int(h[r * epr:(r + 1) * epr].sum()) for r in range(world)]
+    if workload in ZIPF:
+        import synth
+        load["zipf_target_top8"] = [int(round(v)) for v in synth.zipf_targets(tokens)[:8]]
+    roof["routing"] = load
     return roof
 
 

@@ -61,11 +61,6 @@ constexpr int XSTR = 64 + 4;       // phase-1 exchange row stride (floats)
 constexpr int YSTR = BN + 4;       // phase-2 output staging row stride (floats)
 constexpr int ERR_TIMEOUT = 1;
 
-struct TileTable {
-  int eoff[E + 1];   // expert_offset of this rank
-  int moff[E + 1];   // prefix of ceil(n_e / BM): m-tiles before expert e
-};
-
 struct Smem1 {
   uint8_t stage[STAGES1][STAGE_BYTES];  // first member: 1024-byte aligned
   float xbuf[BM][XSTR];
@@ -91,11 +86,6 @@ struct Smem2 {
   TileTable tt;
 };
 
-// Named barrier for the 4 epilogue warps of one TMEM lane quarter.
-__device__ __forceinline__ void quarter_sync(int q) {
-  asm volatile("bar.sync %0, 128;" ::"r"(1 + q) : "memory");
-}
-
 // kind::i8, D = s32, A = B = signed int8, both K-major, N = 128, M = 128.
 constexpr uint32_t IDESC_I8 = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                               ((uint32_t)(BM >> 4) << 24);
@@ -106,60 +96,6 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t da, uint64_t db
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p; }"
       ::"r"(d_tmem), "l"(da), "l"(db), "r"(IDESC_I8), "r"(accumulate), "r"(0u)
       : "memory");
-}
-
-struct TileInfo {
-  int e, row0, nvalid, col;
-};
-
-// Tile t = (m-tile of an expert, column tile); m-tiles enumerated expert by
-// expert so that consecutive tiles reuse the same weights (L2-resident).
-__device__ __forceinline__ TileInfo tile_info(const TileTable& tt, int epr, int ncol, int t) {
-  const int mg = t / ncol;
-  TileInfo ti;
-  ti.col = t % ncol;
-  int lo = 0, hi = epr;  // tt.moff[lo] <= mg < tt.moff[hi]
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (tt.moff[mid] <= mg) lo = mid; else hi = mid;
-  }
-  ti.e = lo;
-  ti.row0 = tt.eoff[lo] + (mg - tt.moff[lo]) * BM;
-  ti.nvalid = min(BM, tt.eoff[lo + 1] - ti.row0);
-  return ti;
-}
-
-// m-tile prefix over this rank's experts (one warp, 4 experts per lane).
-__device__ __forceinline__ void build_tile_table(TileTable& tt, const int32_t* expert_offset, int epr,
-                                                 int lane) {
-  int c[4], sum = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int e = lane * 4 + j;
-    const int n = e < epr ? expert_offset[e + 1] - expert_offset[e] : 0;
-    c[j] = (n + BM - 1) / BM;
-    sum += c[j];
-  }
-  int inc = sum;
-#pragma unroll
-  for (int m = 1; m < 32; m <<= 1) {
-    const int o = __shfl_up_sync(0xffffffffu, inc, m);
-    if (lane >= m) inc += o;
-  }
-  int run = inc - sum;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int e = lane * 4 + j;
-    if (e < epr) {
-      tt.moff[e] = run;
-      tt.eoff[e] = expert_offset[e];
-    }
-    run += c[j];
-  }
-  if (lane == 31) {  // end entries (e = epr, up to 128)
-    tt.moff[epr] = run;
-    tt.eoff[epr] = expert_offset[epr];
-  }
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -548,19 +484,19 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 // xg[pos] = x_i8[routes[pos].token], xg_sa[pos] = x_sa[token]: the routed
 // activation rows in schedule order (one warp per route).
 __global__ void __launch_bounds__(256)
-gather_rows_kernel(const int8_t* __restrict__ xi8, const float* __restrict__ xsa,
+gather_rows_kernel(const uint8_t* __restrict__ x, int row_bytes, const float* __restrict__ xsa,
                    const SparseRoute* __restrict__ routes, const int32_t* __restrict__ expert_offset,
-                   int epr, int8_t* __restrict__ xg, float* __restrict__ xg_sa) {
+                   int epr, uint8_t* __restrict__ xg, float* __restrict__ xg_sa) {
   pdl_wait();
   pdl_trigger();
   const int R = expert_offset[epr];
   const int lane = threadIdx.x & 31;
   for (int pos = blockIdx.x * 8 + (threadIdx.x >> 5); pos < R; pos += gridDim.x * 8) {
     const int tok = routes[pos].token;
-    const uint4* src = reinterpret_cast<const uint4*>(xi8 + (size_t)tok * H);
-    uint4* dst = reinterpret_cast<uint4*>(xg + (size_t)pos * H);
-    for (int c = lane; c < H / 16; c += 32) dst[c] = src[c];
-    if (lane == 0) xg_sa[pos] = xsa[tok];
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok * row_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(xg + (size_t)pos * row_bytes);
+    for (int c = lane; c < row_bytes / 16; c += 32) dst[c] = src[c];
+    if (lane == 0 && xsa) xg_sa[pos] = xsa[tok];
   }
 }
 
@@ -597,29 +533,36 @@ int sm_count() {
 
 // 2-D int8 tensor map [rows][cols] with a box of box_rows x 128 bytes, 128-byte
 // swizzle, zero fill outside the tensor.
-bool make_tmap_i8(void* map, const void* base, long rows, int cols, int box_rows) {
+bool make_tmap_2d(void* map, const void* base, long rows, int cols, int elem_bytes, int box_rows) {
   EncodeTiledFn fn = encode_fn();
-  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (cols % 16)) return false;
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || ((long)cols * elem_bytes) % 16) return false;
+  // boxes of 128 bytes (one 128-byte swizzle row) by box_rows rows
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols};
-  cuuint32_t box[2] = {(cuuint32_t)tc::BK, (cuuint32_t)box_rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * elem_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return fn(reinterpret_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+  return fn(reinterpret_cast<CUtensorMap*>(map),
+            elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_tmap_i8(void* map, const void* base, long rows, int cols, int box_rows) {
+  return make_tmap_2d(map, base, rows, cols, 1, box_rows);
+}
+
 size_t tmap_bytes() { return sizeof(CUtensorMap); }
 
-cudaError_t launch_gather_rows(const int8_t* xi8, const float* xsa, const SparseRoute* routes,
-                               const int32_t* expert_offset, int epr, int T, int8_t* xg,
-                               float* xg_sa, cudaStream_t s) {
+cudaError_t launch_gather_rows(const void* x, int row_bytes, const float* xsa,
+                               const SparseRoute* routes, const int32_t* expert_offset, int epr,
+                               int T, void* xg, float* xg_sa, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   const int rows = T * TOPK;
   const int grid = std::min((rows + 7) / 8, 148 * 8);
-  return launch_k(tc::gather_rows_kernel, dim3(grid), dim3(256), 0, s, xi8, xsa, routes,
-                  expert_offset, epr, xg, xg_sa);
+  return launch_k(tc::gather_rows_kernel, dim3(grid), dim3(256), 0, s,
+                  static_cast<const uint8_t*>(x), row_bytes, xsa, routes, expert_offset, epr,
+                  static_cast<uint8_t*>(xg), xg_sa);
 }
 
 cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t* expert_offset,

@@ -30,8 +30,11 @@ struct Layer {
   uint16_t* gamma2 = nullptr;   // [H]
   int8_t* gu_rm = nullptr;      // bq: row-major copies for the tcgen05 prefill path
   int8_t* dn_rm = nullptr;
-  alignas(64) unsigned char tmap_gu[128] = {};  // TMA descriptor over gu_rm (64-row boxes)
-  alignas(64) unsigned char tmap_dn[128] = {};  // TMA descriptor over dn_rm (128-row boxes)
+  // TMA descriptors of the tcgen05 prefill path: butterquant, over the
+  // row-major int8 copies gu_rm (64-row boxes) / dn_rm (128-row boxes); bf16,
+  // over the registered gate_up (64-row boxes) / down (128-row boxes)
+  alignas(64) unsigned char tmap_gu[128] = {};
+  alignas(64) unsigned char tmap_dn[128] = {};
   bool has_tc = false;
 };
 
@@ -68,7 +71,10 @@ struct gm_moe {
   int32_t* sched_counts = nullptr;  // per-chunk expert counts of the multi-CTA schedule
   alignas(64) unsigned char tmap_xg[128] = {};
   alignas(64) unsigned char tmap_bucket[128] = {};
+  alignas(64) unsigned char tmap_xgb[128] = {};      // bf16 gathered rows (in ybuf's memory)
+  alignas(64) unsigned char tmap_bucketb[128] = {};  // bf16 bucket
   bool tc_ok = false;           // TMA descriptors available
+  bool tcb_ok = false;
   int tc_min_tokens = 1024;     // GM_OPT_TC_MIN_TOKENS
   cudaStream_t own_stream = nullptr;
   // stage profiler (GM_OPT_PROFILE) and kernel launch count
@@ -261,6 +267,10 @@ int carve_workspace(gm_moe* h, int tokens) {
   cudaMemset(h->dev_err, 0, sizeof(int));
   h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)tokens * TOPK, H, 128) &&
              make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)tokens * TOPK, I, 128);
+  // bf16 prefill: the gathered activation rows live in ybuf, which is idle
+  // until the down product writes it
+  h->tcb_ok = make_tmap_2d(h->tmap_xgb, h->ybuf, (long)tokens * TOPK, H, 2, 128) &&
+              make_tmap_2d(h->tmap_bucketb, h->bucket, (long)tokens * TOPK, I, 2, 128);
   return GM_OK;
 }
 
@@ -353,7 +363,7 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
   if (L.kind == 1) {
     if (L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
       // prefill: routed rows gathered in schedule order, then the tcgen05 GEMM
-      GM_STAGE(h, s, launch_gather_rows(x_i8, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
+      GM_STAGE(h, s, launch_gather_rows(x_i8, H, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
                                         h->xg_sa, s),
                "gather_rows");
       GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, Tn, h->xg_sa,
@@ -370,6 +380,16 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
                                       h->chunk_off, h->epr, Tn, L.dn_q, L.dn_scale, h->ybuf, true, s),
                "bq_phase2_down");
     }
+  } else if (L.has_tc && h->tcb_ok && Tn >= h->tc_min_tokens) {
+    GM_STAGE(h, s, launch_gather_rows(x_normed, 2 * H, nullptr, h->routes, h->expert_offset, h->epr, Tn,
+                                      h->ybuf, nullptr, s),
+             "gather_rows");
+    GM_STAGE(h, s, launch_tcb_phase1(h->tmap_xgb, L.tmap_gu, h->expert_offset, h->epr, Tn, h->bucket,
+                                     h->dev_err, s),
+             "phase1_gate_up.tc");
+    GM_STAGE(h, s, launch_tcb_phase2(h->tmap_bucketb, L.tmap_dn, h->expert_offset, h->epr, Tn, h->routes,
+                                     h->ybuf, h->dev_err, s),
+             "phase2_down.tc");
   } else {
     GM_STAGE(h, s, launch_bf16_phase1(x_normed, h->expert_offset, h->routes, h->chunk_off, h->epr, Tn,
                                       L.gu_bf16, h->bucket, s),
@@ -589,6 +609,8 @@ int gm_moe_register_layer_bf16(gm_moe_t* h, int layer, const void* gate_up, cons
   if ((rc = dev_copy(h, &L.rscale, router_scale, (size_t)H, "router_scale"))) return rc;
   if ((rc = dev_copy(h, &L.pes, per_expert_scale, (size_t)E, "per_expert_scale"))) return rc;
   if ((rc = dev_copy(h, &L.gamma2, pre_ffn_norm_2, (size_t)H, "pre_ffn_norm_2"))) return rc;
+  L.has_tc = make_tmap_2d(L.tmap_gu, L.gu_bf16, (long)(epr * GU), H, 2, 64) &&
+             make_tmap_2d(L.tmap_dn, L.dn_bf16, (long)(epr * H), I, 2, 128);
   L.kind = 2;
   return GM_OK;
 }

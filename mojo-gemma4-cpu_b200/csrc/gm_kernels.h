@@ -96,11 +96,15 @@ cudaError_t launch_bf16_phase2(const uint16_t* bucket, const int32_t* expert_off
 cudaError_t launch_combine(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
                            int T, uint16_t* out, cudaStream_t s);
 // tcgen05 prefill path (gemm_tc.cu)
+// 2-D TMA descriptor (128-byte swizzle, boxes of 128 bytes x box_rows rows)
+// over a row-major [rows][cols] tensor of 1-byte (int8) or 2-byte (bf16) elements
+bool make_tmap_2d(void* map, const void* base, long rows, int cols, int elem_bytes, int box_rows);
 bool make_tmap_i8(void* map, const void* base, long rows, int cols, int box_rows);
 size_t tmap_bytes();
-cudaError_t launch_gather_rows(const int8_t* xi8, const float* xsa, const SparseRoute* routes,
-                               const int32_t* expert_offset, int epr, int T, int8_t* xg,
-                               float* xg_sa, cudaStream_t s);
+// rows of row_bytes gathered in schedule order (xsa/xg_sa optional)
+cudaError_t launch_gather_rows(const void* x, int row_bytes, const float* xsa,
+                               const SparseRoute* routes, const int32_t* expert_offset, int epr,
+                               int T, void* xg, float* xg_sa, cudaStream_t s);
 cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t* expert_offset,
                              int epr, int T, const float* xg_sa, const float* gu_scale,
                              int8_t* bucket_i8, float* bucket_sa, uint16_t* bucket_bf16, int* err,
@@ -108,6 +112,12 @@ cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t
 cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
                              int epr, int T, const float* bsa, const SparseRoute* routes,
                              const float* dn_scale, float* ybuf, int* err, cudaStream_t s);
+// tcgen05 prefill path for bf16 layers (gemm_tc_bf16.cu)
+cudaError_t launch_tcb_phase1(const void* map_a, const void* map_b, const int32_t* expert_offset,
+                              int epr, int T, uint16_t* bucket, int* err, cudaStream_t s);
+cudaError_t launch_tcb_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
+                              int epr, int T, const SparseRoute* routes, float* ybuf, int* err,
+                              cudaStream_t s);
 
 cudaError_t launch_quantize_rows(const uint16_t* w, long rows, int cols, const uint16_t* gamma,
                                  int block, int8_t* q, float* scale, cudaStream_t s);

@@ -154,5 +154,74 @@ __device__ __forceinline__ float2 small_ints_to_float2(int d0, int d1) {
   return add2(biased, make_float2(-12582912.0f, -12582912.0f));
 }
 
+// ------------------------------------------------ grouped-GEMM tile tables
+// Routes of one expert are contiguous (schedule order); an expert with n
+// routes spans ceil(n / TILE_M) m-tiles of TILE_M routes.
+constexpr int TILE_M = 128;
+
+struct TileTable {
+  int eoff[E + 1];   // expert_offset of this rank
+  int moff[E + 1];   // prefix of ceil(n_e / TILE_M): m-tiles before expert e
+};
+
+// Named barrier for the 4 epilogue warps of one TMEM lane quarter.
+__device__ __forceinline__ void quarter_sync(int q) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + q) : "memory");
+}
+
+struct TileInfo {
+  int e, row0, nvalid, col;
+};
+
+// Tile t = (m-tile of an expert, column tile); m-tiles enumerated expert by
+// expert so that consecutive tiles reuse the same weights (L2-resident).
+__device__ __forceinline__ TileInfo tile_info(const TileTable& tt, int epr, int ncol, int t) {
+  const int mg = t / ncol;
+  TileInfo ti;
+  ti.col = t % ncol;
+  int lo = 0, hi = epr;  // tt.moff[lo] <= mg < tt.moff[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (tt.moff[mid] <= mg) lo = mid; else hi = mid;
+  }
+  ti.e = lo;
+  ti.row0 = tt.eoff[lo] + (mg - tt.moff[lo]) * TILE_M;
+  ti.nvalid = min(TILE_M, tt.eoff[lo + 1] - ti.row0);
+  return ti;
+}
+
+// m-tile prefix over this rank's experts (one warp, 4 experts per lane).
+__device__ __forceinline__ void build_tile_table(TileTable& tt, const int32_t* expert_offset, int epr,
+                                                 int lane) {
+  int c[4], sum = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int e = lane * 4 + j;
+    const int n = e < epr ? expert_offset[e + 1] - expert_offset[e] : 0;
+    c[j] = (n + TILE_M - 1) / TILE_M;
+    sum += c[j];
+  }
+  int inc = sum;
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, inc, m);
+    if (lane >= m) inc += o;
+  }
+  int run = inc - sum;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int e = lane * 4 + j;
+    if (e < epr) {
+      tt.moff[e] = run;
+      tt.eoff[e] = expert_offset[e];
+    }
+    run += c[j];
+  }
+  if (lane == 31) {  // end entries (e = epr, up to 128)
+    tt.moff[epr] = run;
+    tt.eoff[epr] = expert_offset[epr];
+  }
+}
+
 }  // namespace tc
 }  // namespace gm

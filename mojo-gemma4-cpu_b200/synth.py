@@ -19,6 +19,7 @@ import torch
 import gmoe
 
 H, E, I, GU = gmoe.HIDDEN, gmoe.NUM_EXPERTS, gmoe.INTERMEDIATE, gmoe.GATE_UP
+TOPK_K = gmoe.TOP_K
 
 
 def _gen(seed, device):
@@ -55,6 +56,80 @@ def make_layer(seed=0x6E6D6F45, device="cpu", weight_std=0.02, router_std=0.02,
         L["per_expert_scale"] = torch.ones(E, dtype=torch.bfloat16, device=device)
         L["pre_ffn_norm_2"] = torch.ones(H, dtype=torch.bfloat16, device=device)
     return L
+
+
+# ---------------------------------------------------------------- Zipf routing
+ZIPF_S = 1.1
+ZIPF_C = 16.0   # token shift along u (|x| is about sqrt(2816) = 53)
+
+
+def zipf_targets(T, s=ZIPF_S):
+    """Per-expert route counts for T tokens: 8T * i^-s / sum_j j^-s for the
+    expert of rank i (expert i-1), capped at T (an expert is picked at most
+    once per token); the overflow is re-spread over the uncapped experts in
+    proportion to their shares."""
+    w = np.arange(1, E + 1, dtype=np.float64) ** -s
+    tgt = 8.0 * T * w / w.sum()
+    capped = np.zeros(E, bool)
+    for _ in range(E):
+        over = tgt > T
+        if not over.any():
+            break
+        capped |= over
+        excess = float((tgt[over] - T).sum())
+        tgt[over] = T
+        free = ~capped
+        tgt[free] += excess * w[free] / w[free].sum()
+    return tgt
+
+
+def zipf_direction(seed=0x6E6D6F45):
+    """The fixed unit vector u of the skew (host f32)."""
+    g = _gen(seed + 7, "cpu")
+    u = torch.randn(H, generator=g, dtype=torch.float64)
+    return (u / u.norm()).to(torch.float32)
+
+
+def zipf_tokens(T, seed=0x6E6D6F45, device="cpu", c=ZIPF_C, u=None):
+    """x + c*u (bf16) for x ~ N(0,1)."""
+    u = zipf_direction() if u is None else u
+    g = _gen(seed + 1, device)
+    x = torch.randn(T, H, generator=g, device=device, dtype=torch.float32)
+    return (x + c * u.to(device)).to(torch.bfloat16)
+
+
+def apply_zipf(raw, T_cal=4096, iters=80, c=ZIPF_C, cal_seed=0x5A1F):
+    """Adds beta_e * u to router row e so that the top-8 route counts of
+    tokens x + c*u track zipf_targets (the skew direction of the synthetic
+    Zipf(1.1) configs).  beta is calibrated on the host side from routed
+    counts of T_cal calibration tokens: each round moves every expert's logit
+    bias by a damped step of log(target) - log(count) until the counts track
+    the targets.  Routing ranks are invariant to a common logit shift, so the
+    butterquant router's centring (which removes the mean of beta) keeps the
+    skew.  Returns the new raw dict (router_proj replaced)."""
+    # computed on the host CPU so that every process derives identical weights
+    dev = raw["router_proj"].device
+    u = zipf_direction()
+    x = zipf_tokens(T_cal, seed=cal_seed, device="cpu", c=c, u=u).float()
+    inv = torch.rsqrt((x * x).mean(dim=1, keepdim=True) + 1e-6)
+    rs = raw["router_scale"].float().cpu() * (H ** -0.5)
+    sv = x * rs * inv                                  # router input, as the kernels form it
+    W = raw["router_proj"].float().cpu()
+    base = sv @ W.t()                                  # [T, E]
+    us = sv @ u                                        # [T]: per-token weight of the bias
+    tgt = torch.tensor(zipf_targets(T_cal), dtype=torch.float32)
+    sigma = float(base.std())
+    b = torch.zeros(E)
+    for it in range(iters):
+        lg = base + us[:, None] * (b / us.mean())[None, :]
+        top = lg.topk(TOPK_K, dim=1).indices
+        cnt = torch.bincount(top.reshape(-1), minlength=E).float()
+        step = sigma * (0.5 if it < iters // 2 else 0.2)
+        b = b + step * (torch.log(tgt + 1.0) - torch.log(cnt + 1.0))
+    beta = b / us.mean()
+    out = dict(raw)
+    out["router_proj"] = (W + beta[:, None] * u[None, :]).to(torch.bfloat16).to(dev)
+    return out
 
 
 def bake_router_scale(rs, stream=None):

@@ -337,6 +337,36 @@ def test_forward_bf16(T, layer_default):
     check_forward(host(out), host(idx), rout, ridx, rlg, TOL_BF16)
 
 
+@pytest.mark.parametrize("T", [1100, 2048])
+def test_forward_bf16_tc_prefill(T, layer_stress):
+    """bf16 layers at prefill size run the tcgen05 grouped GEMM (kind::f16):
+    within the bf16 tolerance of the oracle, and close to the decode kernels
+    (the same products summed in a different order)."""
+    raw, _, _ = layer_stress
+    Lb = oracle_bf16_layer(raw)
+    gl = synth.bf16_layer(raw_to_torch(raw))
+    blk = gmoe.MoeBlock(T, 1)
+    blk.register_bf16(0, gl["gate_up"], gl["down"], gl["router_proj"], gl["router_scale"],
+                      gl["per_expert_scale"], gl["pre_ffn_norm_2"])
+    x_np = tokens_np(T, seed=710 + T)
+    x = dev(x_np)
+    out_tc = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    blk.profile(True)
+    blk.forward(0, x, out_tc, T)
+    stats, _ = blk.profile_read()
+    assert "phase1_gate_up.tc" in stats and "phase2_down.tc" in stats
+    blk.set_option(gmoe.OPT_TC_MIN_TOKENS, 1 << 30)  # force the decode kernels
+    out_dec = torch.empty_like(out_tc)
+    blk.forward(0, x, out_dec, T)
+    torch.cuda.synchronize()
+    assert blk.device_status() == 0
+    rout, ridx, _, rlg = O.bf16_forward(x_np, Lb)
+    checked = topk_margin(rlg) > MARGIN
+    assert checked.mean() > 0.95
+    assert rel_err(host(out_tc), rout, rows=checked) < TOL_BF16
+    assert rel_err(host(out_tc), host(out_dec)) < 1e-2
+
+
 def test_forward_deterministic_and_sync_host_path(layer_stress):
     raw, ref, g = layer_stress
     blk = make_block(g, max_tokens=128)
