@@ -451,11 +451,14 @@ def cpu_leg(fmt, T, args, raw_dev):
 
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of
-# the dominant kernel, from the ncu captures summarised under profiles/
-# (bq_decode_b64.md, tc_prefill_4k.md); None where no capture of the current
-# kernel exists.
+# the dominant kernel, from the ncu captures of the same bench command
+# summarised under profiles/ (bq_decode_b64.md, bq_prefill_4k_zipf_tcgen05.md,
+# bf16_prefill_4k_tcgen05.md); None where no capture of the current kernel
+# and workload exists.
 NCU_TRAFFIC = {
-    ("bq-decode-b64", "bq_phase1_gate_up"): 500_506_880 + 4_189_184,
+    ("bq-decode-b64", "bq_phase1_gate_up"): 505_800_000 + 500_000,
+    ("bq-prefill-4k-zipf", "bq_phase2_down.tc"): 280_055_808 + 353_800_192,
+    ("bf16-prefill-4k", "phase1_gate_up.tc"): 1_229_532_000 + 45_981_184,
 }
 
 
