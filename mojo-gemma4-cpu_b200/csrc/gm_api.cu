@@ -69,6 +69,7 @@ struct gm_moe {
   float* xg_sa = nullptr;
   int* dev_err = nullptr;       // device-side error word (bounded waits that expired)
   int32_t* sched_counts = nullptr;  // per-chunk expert counts of the multi-CTA schedule
+  int* router_counts = nullptr;     // router tile counters (zero between calls)
   alignas(64) unsigned char tmap_xg[128] = {};
   alignas(64) unsigned char tmap_bucket[128] = {};
   alignas(64) unsigned char tmap_xgb[128] = {};      // bf16 gathered rows (in ybuf's memory)
@@ -77,6 +78,8 @@ struct gm_moe {
   bool tcb_ok = false;
   int tc_min_tokens = 1024;     // GM_OPT_TC_MIN_TOKENS
   cudaStream_t own_stream = nullptr;
+  cudaStream_t side_stream = nullptr;  // L2 prefetches forked off the forward's stream
+  cudaEvent_t fork_event = nullptr;
   // stage profiler (GM_OPT_PROFILE) and kernel launch count
   struct PendingStage {
     int stat;
@@ -108,6 +111,8 @@ struct gm_moe {
 };
 
 namespace {
+
+constexpr int L2_PREFETCH_EXPERTS = 20;  // 20 x 3.97 MB of gate/up weights (L2 is 126 MB)
 
 int set_err(gm_moe* h, int code, const char* fmt, ...) {
   char buf[512];
@@ -158,7 +163,7 @@ struct Carve {
 struct WsLayout {
   size_t logits, inv_rms, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
       x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, xg, xg_sa, dev_err,
-      sched_counts, total;
+      sched_counts, router_counts, total;
 };
 
 WsLayout ws_layout(int max_tokens) {
@@ -188,6 +193,7 @@ WsLayout ws_layout(int max_tokens) {
   L.xg_sa = c.take<float>(R);
   L.dev_err = c.take<int>(1);
   L.sched_counts = c.take<int32_t>(schedule_counts_ints(max_tokens));
+  L.router_counts = c.take<int>(router_tile_counters(max_tokens));
   L.total = align_up(c.off, 256);
   return L;
 }
@@ -264,7 +270,9 @@ int carve_workspace(gm_moe* h, int tokens) {
   h->xg_sa = reinterpret_cast<float*>(b + L.xg_sa);
   h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
   h->sched_counts = reinterpret_cast<int32_t*>(b + L.sched_counts);
+  h->router_counts = reinterpret_cast<int*>(b + L.router_counts);
   cudaMemset(h->dev_err, 0, sizeof(int));
+  cudaMemset(h->router_counts, 0, sizeof(int) * router_tile_counters(tokens));
   h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)tokens * TOPK, H, 128) &&
              make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)tokens * TOPK, I, 128);
   // bf16 prefill: the gathered activation rows live in ybuf, which is idle
@@ -427,7 +435,7 @@ int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int
       GM_STAGE(h, s, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, h->inv_rms, s), "bq_norm_quant");
     else
       GM_STAGE(h, s, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
-    GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, s),
+    GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, h->router_counts, s),
              "router_expert");
     GM_STAGE(h, s, launch_topk(h->logits, L.pes, T, h->route_idx, h->route_w, s), "router_merge");
   }
@@ -536,6 +544,11 @@ int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, in
     delete h;
     return rc;
   }
+  if (cudaStreamCreateWithFlags(&h->side_stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&h->fork_event, cudaEventDisableTiming) != cudaSuccess) {
+    cudaGetLastError();
+    h->side_stream = nullptr;  // prefetch disabled; everything else works
+  }
   if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
     cudaFree(h->ws);
     delete h;
@@ -558,6 +571,8 @@ int gm_moe_destroy(gm_moe_t* h) {
   if (h->ep_buf) cudaFree(h->ep_buf);
   if (h->ws) cudaFree(h->ws);
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
+  if (h->side_stream) cudaStreamDestroy(h->side_stream);
+  if (h->fork_event) cudaEventDestroy(h->fork_event);
   delete h;
   return GM_OK;
 }
@@ -638,13 +653,28 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
   if (h->ep_comm) return ep_forward(h, L, static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), T, s);
   if (T == 0) return GM_OK;
   const uint16_t* xb = static_cast<const uint16_t*>(x);
+  // 0. decode batches route to nearly every expert: pull the gate/up weights
+  // phase 1 reads first into L2 while the router runs (HBM is idle then).  The
+  // prefetch runs on a side stream forked from `s`: nothing waits for it.
+  if (L.kind == 1 && T >= 32 && !(L.has_tc && h->tc_ok && T >= h->tc_min_tokens) && h->side_stream) {
+    GM_TRY(h, cudaEventRecord(h->fork_event, s), "prefetch fork");
+    GM_TRY(h, cudaStreamWaitEvent(h->side_stream, h->fork_event, 0), "prefetch fork");
+    const bool pdl = tls_pdl;
+    tls_pdl = false;
+    const long n0 = tls_kernel_launches;
+    const cudaError_t pe =
+        launch_l2_prefetch(L.gu_q, (size_t)std::min(h->epr, L2_PREFETCH_EXPERTS) * GU * H, h->side_stream);
+    h->launches += tls_kernel_launches - n0;
+    tls_pdl = pdl;
+    GM_TRY(h, pe, "l2_prefetch");
+  }
   // 1. activation norm (+ inv_rms shared with the router)
   if (L.kind == 1)
     GM_STAGE(h, s, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, h->inv_rms, s), "bq_norm_quant");
   else
     GM_STAGE(h, s, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
   // 2. router logits, 3. top-8 + schedule
-  GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, s), "router_expert");
+  GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, h->router_counts, s), "router_expert");
   const int rc_chunk = L.kind == 1 ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
   GM_STAGE(h, s, launch_topk_schedule(h->logits, L.pes, T, h->route_idx, h->route_w, h->expert_base,
                                  h->epr, rc_chunk, h->expert_offset, h->routes, h->route_pos,

@@ -37,7 +37,15 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
 void set_thread_error(const char* msg);
 
 int max_route_chunks(int T, int epr, int rc);
+// The router writes ROUTER_SLICES split-K partial logit slices [slice][T][E];
+// router_ksplit(T) is how many of them the top-8 kernels sum: below
+// ROUTER_TC_MIN_TOKENS the FMA kernel reduces them itself into slice 0 (1),
+// at and above it the partials stay separate (ROUTER_SLICES).
+constexpr int ROUTER_SLICES = H / 256;
 int router_ksplit(int T);
+// Tile counters of the FMA kernel's in-kernel reduction (ints, zero between calls).
+int router_tile_counters(int T);
+// Router workspace: partials, inv_rms [T], an error word, tile counters.
 size_t router_workspace_floats(int T);
 
 // Router logits as split-K partials [ksplit][T][E].  With a device error word
@@ -46,7 +54,7 @@ size_t router_workspace_floats(int T);
 constexpr int ROUTER_TC_MIN_TOKENS = 512;
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
                                  const float* inv_rms, int T, float* logits, int* err,
-                                 cudaStream_t s);
+                                 int* tile_counters, cudaStream_t s);
 cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
                                     const float* inv_rms, int T, float* logits, int* err,
                                     cudaStream_t s);
@@ -83,6 +91,8 @@ cudaError_t launch_bq_phase1(const int8_t* xi8, const float* xsa, const int32_t*
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_gu, const float* gu_scale, int8_t* bucket_i8,
                              float* bucket_sa, uint16_t* bucket_bf16, cudaStream_t s);
+// bulk L2 prefetch of [base, base + bytes) (16-byte aligned base)
+cudaError_t launch_l2_prefetch(const void* base, size_t bytes, cudaStream_t s);
 cudaError_t launch_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t* expert_offset,
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_dn, const float* dn_scale, float* ybuf,

@@ -25,17 +25,23 @@ namespace gm {
 // per expert); each warp owns 4 experts.  The 32 (token, expert) lane partials
 // are combined by a reduce-scatter butterfly that leaves lane t*4+e holding
 // the slice sum of token t and expert e (a fixed, deterministic order).
+//
+// With tile_count, the K slices of a tile are also reduced here: every CTA
+// publishes its partial, and the last of the tile's CTAs to finish (a counter
+// per tile, re-armed by that CTA) sums the slices in slice order into slice 0,
+// so the top-8 kernel reads T*E logits instead of 11*T*E partials.
 __global__ void __launch_bounds__(256)
 router_logits_small_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
                            const uint16_t* __restrict__ rscale, const float* __restrict__ inv_rms,
-                           int T, float* __restrict__ logits) {
+                           int T, float* __restrict__ logits_base, int* __restrict__ tile_count) {
   constexpr int TT = 8, KS = 256;
   __shared__ __align__(16) float s_s[TT][KS];
+  __shared__ int s_last;
   pdl_wait();
   pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t0 = blockIdx.x * TT, e0 = blockIdx.y * 32, kb = blockIdx.z * KS;
-  logits += (size_t)blockIdx.z * T * E;
+  float* logits = logits_base + (size_t)blockIdx.z * T * E;
   for (int i = tid; i < TT * KS / 2; i += 256) {
     const int t = i / (KS / 2), kp = (i % (KS / 2)) * 2;
     float a = 0.0f, b = 0.0f;
@@ -84,6 +90,24 @@ router_logits_small_kernel(const uint16_t* __restrict__ x, const uint16_t* __res
   }
   const int t = t0 + (lane >> 2);
   if (t < T) logits[(size_t)t * E + e0 + warp * 4 + (lane & 3)] = v[0];
+  if (tile_count) {
+    __threadfence();  // this CTA's partial is visible before it is counted
+    __syncthreads();
+    int* ctr = tile_count + blockIdx.x * gridDim.y + blockIdx.y;
+    if (tid == 0) s_last = atomicAdd(ctr, 1) == (int)gridDim.z - 1;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      const int tt = t0 + (tid >> 5), ee = e0 + (tid & 31);
+      if (tt < T) {
+        float* p = logits_base + (size_t)tt * E + ee;
+        float a = __ldcg(p);
+        for (int z = 1; z < (int)gridDim.z; ++z) a = __fadd_rn(a, __ldcg(p + (size_t)z * T * E));
+        *p = a;
+      }
+      if (tid == 0) *ctr = 0;  // re-armed for the next call on this stream
+    }
+  }
 }
 
 // inv_rms of each token (one warp per token): kernels/rmsnorm.mojo:16-17,45-46.
@@ -117,23 +141,27 @@ topk_softmax_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __re
   topk_token(logits, ksplit, pes, T, t, threadIdx.x & 31, route_idx, route_w);
 }
 
-int router_ksplit(int T) {
-  (void)T;
-  return H / 256;  // 11 K slices of 256 for the warp-level kernel
-}
+int router_ksplit(int T) { return T >= ROUTER_TC_MIN_TOKENS ? ROUTER_SLICES : 1; }
 
-// partials [11][T][E], then inv_rms [T], then one device error word
-size_t router_workspace_floats(int T) { return (size_t)router_ksplit(T) * T * E + T + 1; }
+int router_tile_counters(int T) { return (T + 7) / 8 * (E / 32); }
+
+// partials [11][T][E], inv_rms [T], one device error word, tile counters
+size_t router_workspace_floats(int T) {
+  return (size_t)ROUTER_SLICES * T * E + T + 1 + router_tile_counters(T);
+}
 
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
                                  const float* inv_rms, int T, float* logits, int* err,
-                                 cudaStream_t s) {
+                                 int* tile_counters, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  if (err && T >= ROUTER_TC_MIN_TOKENS)
-    return launch_router_logits_tc(x, wr, rscale, inv_rms, T, logits, err, s);
-  const int ks = router_ksplit(T);
-  return launch_k(router_logits_small_kernel, dim3((T + 7) / 8, E / 32, ks), dim3(256), 0, s, x,
-                  wr, rscale, inv_rms, T, logits);
+  if (T >= ROUTER_TC_MIN_TOKENS) {
+    if (err) return launch_router_logits_tc(x, wr, rscale, inv_rms, T, logits, err, s);
+    tile_counters = nullptr;  // ROUTER_SLICES separate partials, as the tcgen05 kernel leaves them
+  } else if (!tile_counters) {
+    return cudaErrorInvalidValue;
+  }
+  return launch_k(router_logits_small_kernel, dim3((T + 7) / 8, E / 32, ROUTER_SLICES), dim3(256), 0,
+                  s, x, wr, rscale, inv_rms, T, logits, tile_counters);
 }
 
 cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_t s) {
@@ -148,17 +176,19 @@ cudaError_t launch_topk(float* logits, const uint16_t* pes, int T, int32_t* rout
                   router_ksplit(T), pes, T, route_idx, route_w);
 }
 
-// Standalone router (gm_router_select): inv_rms and a device error word in
-// the tail of the workspace, then logits and top-8.
+// Standalone router (gm_router_select): inv_rms, a device error word and the
+// tile counters in the tail of the workspace (cleared here: the caller's
+// workspace may hold anything), then logits and top-8.
 cudaError_t launch_router(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
                           const uint16_t* pes, int T, float* logits, int32_t* route_idx,
                           float* route_w, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  float* inv = logits + (size_t)router_ksplit(T) * T * E;
+  float* inv = logits + (size_t)ROUTER_SLICES * T * E;
   int* err = reinterpret_cast<int*>(inv + T);
-  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), s);
+  int* counters = err + 1;
+  cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int) * (1 + router_tile_counters(T)), s);
   if (e == cudaSuccess) e = launch_rms_inv(x, T, inv, s);
-  if (e == cudaSuccess) e = launch_router_logits(x, wr, rscale, inv, T, logits, err, s);
+  if (e == cudaSuccess) e = launch_router_logits(x, wr, rscale, inv, T, logits, err, counters, s);
   if (e == cudaSuccess) e = launch_topk(logits, pes, T, route_idx, route_w, s);
   return e;
 }

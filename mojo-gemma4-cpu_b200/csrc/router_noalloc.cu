@@ -24,7 +24,7 @@ namespace gm {
 // partial logits plus 256 inv_rms values = 360,704 floats (1.38 MiB).
 constexpr int NOALLOC_MAX_TOKENS = 256;
 constexpr size_t NOALLOC_SCRATCH_FLOATS =
-    (size_t)(H / 256) * NOALLOC_MAX_TOKENS * E + NOALLOC_MAX_TOKENS;
+    (size_t)(H / 256) * NOALLOC_MAX_TOKENS * E + NOALLOC_MAX_TOKENS + NOALLOC_MAX_TOKENS / 8 * (E / 32);
 
 static __device__ __align__(256) float g_router_scratch[NOALLOC_SCRATCH_FLOATS];
 
@@ -81,14 +81,18 @@ int gm_router_select_noalloc(const void* x, const void* router_w, const void* ro
   if (e != cudaSuccess)
     return fail(GM_ECUDA, "gm_router_select_noalloc: cudaGetSymbolAddress of the scratch failed", e);
   // Every scratch element a later kernel reads is written earlier in the same
-  // call (inv_rms, then all K-slice partials), so nothing needs clearing.
+  // call (inv_rms, then all K-slice partials); the logit kernel's tile
+  // counters (after inv_rms) are cleared here.
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const uint16_t* xb = static_cast<const uint16_t*>(x);
-  float* inv = scratch + (size_t)router_ksplit(T) * T * E;
-  e = launch_rms_inv(xb, T, inv, s);
+  float* inv = scratch + (size_t)ROUTER_SLICES * T * E;
+  int* counters = reinterpret_cast<int*>(inv + T);
+  e = cudaMemsetAsync(counters, 0, sizeof(int) * router_tile_counters(T), s);
+  if (e == cudaSuccess) e = launch_rms_inv(xb, T, inv, s);
   if (e == cudaSuccess)
     e = launch_router_logits(xb, static_cast<const uint16_t*>(router_w),
-                             static_cast<const uint16_t*>(router_scale), inv, T, scratch, nullptr, s);
+                             static_cast<const uint16_t*>(router_scale), inv, T, scratch, nullptr,
+                             counters, s);
   if (e == cudaSuccess)
     e = launch_topk(scratch, static_cast<const uint16_t*>(per_expert_scale), T, route_idx, route_w, s);
   if (e != cudaSuccess) return fail(GM_ECUDA, "gm_router_select_noalloc: launch failed", e);

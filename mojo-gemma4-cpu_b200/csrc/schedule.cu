@@ -20,7 +20,7 @@ namespace gm {
 struct ScheduleSmem {
   int cnt[E];
   int base[E];
-  uint32_t mask[E][32];
+  uint32_t mask[E][33];  // padded: thread e scans row e without bank conflicts
   int wpre[E][33];
 };
 
@@ -312,7 +312,9 @@ cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, int T, int3
                                  float* route_w, int expert_base, int epr, int route_chunk,
                                  int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
                                  int32_t* chunk_off, int32_t* counts, cudaStream_t s) {
-  if (T <= 1024)
+  // one CTA when the logits arrive reduced (small T); otherwise the top-8 is
+  // spread over T/4 CTAs first
+  if (T <= 1024 && router_ksplit(T) == 1)
     return launch_k(topk_schedule_kernel, dim3(1), dim3(1024), 0, s, logits, router_ksplit(T), pes,
                     T, route_idx, route_w, expert_base, epr, route_chunk, expert_offset, routes,
                     route_pos, chunk_off);

@@ -92,7 +92,10 @@ def run_router(g, x_np):
               T, lg, idx, w, None)
     torch.cuda.synchronize()
     ws = host(lg)
-    assert ws[-1:].view(np.int32)[0] == 0  # device error word (bounded waits)
+    # workspace tail: 11 partial slices, inv_rms [T], the device error word of
+    # the bounded waits, then the router's tile counters (re-armed to zero)
+    tail = ws[11 * T * E + T:].view(np.int32)
+    assert tail[0] == 0 and (tail[1:] == 0).all()
     return host(idx), host(w), ws[:T * E].reshape(T, E)
 
 
@@ -441,6 +444,8 @@ def test_stage_profiler_labels_and_launch_count(layer_stress):
     for T in (64, 64, 1100):
         blk.forward(0, dev(tokens_np(T, seed=T)), out, T)
     stats, launches = blk.profile_read()
+    # decode batches (32 <= T < 1024) also launch an L2 prefetch on a side
+    # stream (counted as a launch, not a stage of the forward's stream)
     assert list(stats) == ["bq_norm_quant", "router_expert", "router_merge.schedule",
                            "bq_phase1_gate_up", "bq_phase2_down", "combine", "gather_rows",
                            "bq_phase1_gate_up.tc", "bq_phase2_down.tc"]
@@ -448,12 +453,12 @@ def test_stage_profiler_labels_and_launch_count(layer_stress):
     assert stats["combine"]["calls"] == 3
     # T <= 1024: one fused top-8+schedule kernel; T > 1024: top-8, count, scatter
     assert stats["router_merge.schedule"]["kernels"] == 2 * 1 + 3
-    assert launches == 2 * 6 + 9
+    assert launches == 2 * 7 + 9
     for v in stats.values():
         assert 0 < v["min_ms"] <= v["avg_ms"] <= v["max_ms"] < 1e3
     # profiling off: launches still counted, no new stage records
     blk.profile(False)
     blk.forward(0, dev(tokens_np(64, seed=1)), out, 64)
     stats, launches = blk.profile_read()
-    assert stats == {} and launches == 6
+    assert stats == {} and launches == 7
     blk.close()
