@@ -108,6 +108,23 @@ int gm_moe_register_layer_bf16(gm_moe_t* h, int layer, const void* gate_up, cons
  * Asynchronous on `stream`; x and out are device pointers. */
 int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void* stream);
 
+/* Post-MoE tail of dispatch_bq_ffn (modeling/gemma_4_moe_bq.mojo:785-805),
+ * fused into the MoE's final kernel so the MoE output never goes to memory:
+ *   dense' = rms_norm(dense_out) * post_ffn_norm_1
+ *   dense' = dense' + rms_norm(moe_out) * post_ffn_norm_2
+ *   x_main = (x_main + rms_norm(dense') * post_ffn_norm) * layer_scalar
+ * with the reference's bf16 rounding after each step (kernels/rmsnorm.mojo:
+ * 21-67, kernels/elementwise.mojo:75-83).  gm_moe_register_post stores the
+ * three bf16 [2816] gains (host or device pointers) and the layer scalar;
+ * gm_moe_forward_ffn(h, layer, x_main, dense_out, T, stream) runs the MoE on
+ * x_main (its input, as dispatch_bq_ffn passes x_main) and overwrites x_main
+ * with the layer's post-FFN value.  dense_out is the dense MLP's output after
+ * its all-reduce (bf16 [T][2816], device pointer, read only). */
+int gm_moe_register_post(gm_moe_t* h, int layer, const void* post_ffn_norm_1,
+                         const void* post_ffn_norm_2, const void* post_ffn_norm, float layer_scalar);
+int gm_moe_forward_ffn(gm_moe_t* h, int layer, void* x_main, const void* dense_out, int T,
+                       void* stream);
+
 /* Options (no reference counterpart: the reference picks its kernels at
  * compile time).  GM_OPT_TC_MIN_TOKENS: calls with T >= value run the
  * butterquant gate/up product on the tcgen05 grouped GEMM (prefill path),

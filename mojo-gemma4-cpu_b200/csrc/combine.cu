@@ -8,6 +8,7 @@
 // <=8 local routes are sorted by expert id and added left to right starting
 // from 0.0f, then rounded to bf16 with RNE (butterquant/convert.mojo:13-17).
 #include "gm_kernels.h"
+#include "post_moe.cuh"
 
 namespace gm {
 
@@ -49,6 +50,60 @@ combine_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict_
     o.y = (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16);
     *reinterpret_cast<uint2*>(out + (size_t)t * H + c4 * 4) = o;
   }
+}
+
+// The combine followed by the post-MoE tail (post_moe.cuh) on the same row:
+// the bf16 MoE row stays in registers.
+__global__ void __launch_bounds__(POST_THREADS)
+combine_post_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict__ route_pos,
+                    const float* __restrict__ ybuf, int T, PostParams p) {
+  __shared__ int s_pos[TOPK];
+  __shared__ int s_n;
+  __shared__ float red[POST_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int ex[TOPK], ps[TOPK], n = 0;
+    for (int k = 0; k < TOPK; ++k) {
+      const int q = route_pos[t * TOPK + k];
+      if (q < 0) continue;
+      const int e = route_idx[t * TOPK + k];
+      int j = n++;
+      while (j > 0 && ex[j - 1] > e) { ex[j] = ex[j - 1]; ps[j] = ps[j - 1]; --j; }
+      ex[j] = e;
+      ps[j] = q;
+    }
+    for (int k = 0; k < n; ++k) s_pos[k] = ps[k];
+    s_n = n;
+  }
+  __syncthreads();
+  const int n = s_n;
+  float m[8];
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int c4 = threadIdx.x + g * POST_THREADS;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int k = 0; k < n; ++k) {
+      const float4 y = *reinterpret_cast<const float4*>(ybuf + (size_t)s_pos[k] * H + c4 * 4);
+      acc.x = __fadd_rn(acc.x, y.x);
+      acc.y = __fadd_rn(acc.y, y.y);
+      acc.z = __fadd_rn(acc.z, y.z);
+      acc.w = __fadd_rn(acc.w, y.w);
+    }
+    m[4 * g] = bf2f(f2bf(acc.x));
+    m[4 * g + 1] = bf2f(f2bf(acc.y));
+    m[4 * g + 2] = bf2f(f2bf(acc.z));
+    m[4 * g + 3] = bf2f(f2bf(acc.w));
+  }
+  post_moe_row(m, t, p, red);
+}
+
+cudaError_t launch_combine_post(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
+                                int T, const PostParams& p, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  return launch_k(combine_post_kernel, dim3(T), dim3(POST_THREADS), 0, s, route_idx, route_pos, ybuf,
+                  T, p);
 }
 
 cudaError_t launch_combine(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,

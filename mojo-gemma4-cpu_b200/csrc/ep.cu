@@ -33,6 +33,7 @@
 #include <string>
 
 #include "ep.h"
+#include "post_moe.cuh"
 
 namespace gm {
 
@@ -196,6 +197,49 @@ ep_final_kernel(const uint16_t* __restrict__ contrib, const int32_t* __restrict_
     o.y = (uint32_t)f2bf(a2) | ((uint32_t)f2bf(a3) << 16);
     *reinterpret_cast<uint2*>(out + (size_t)t * H + c4 * 4) = o;
   }
+}
+
+// ep_final followed by the post-MoE tail (post_moe.cuh) on the same row.
+__global__ void __launch_bounds__(POST_THREADS)
+ep_final_post_kernel(const uint16_t* __restrict__ contrib, const int32_t* __restrict__ pos, int T,
+                     int G, int cap, PostParams p) {
+  __shared__ int s_row[8];
+  __shared__ float red[POST_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  if (threadIdx.x < 8) {
+    const int d = threadIdx.x;
+    const int q = d < G ? pos[(size_t)t * G + d] : -1;
+    s_row[d] = q < 0 ? -1 : d * cap + q;
+  }
+  __syncthreads();
+  float m[8];
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int c4 = threadIdx.x + g * POST_THREADS;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    for (int d = 0; d < G; ++d) {
+      const int r = s_row[d];
+      if (r < 0) continue;
+      const uint2 v = *reinterpret_cast<const uint2*>(contrib + (size_t)r * H + c4 * 4);
+      a0 = __fadd_rn(a0, bf2f(v.x & 0xFFFFu));
+      a1 = __fadd_rn(a1, bf2f(v.x >> 16));
+      a2 = __fadd_rn(a2, bf2f(v.y & 0xFFFFu));
+      a3 = __fadd_rn(a3, bf2f(v.y >> 16));
+    }
+    m[4 * g] = bf2f(f2bf(a0));
+    m[4 * g + 1] = bf2f(f2bf(a1));
+    m[4 * g + 2] = bf2f(f2bf(a2));
+    m[4 * g + 3] = bf2f(f2bf(a3));
+  }
+  post_moe_row(m, t, p, red);
+}
+
+cudaError_t launch_ep_final_post(const uint16_t* contrib, const int32_t* pos, int T, int G, int cap,
+                                 const PostParams& p, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  return launch_k(ep_final_post_kernel, dim3(T), dim3(POST_THREADS), 0, s, contrib, pos, T, G, cap, p);
 }
 
 cudaError_t launch_ep_plan(const int32_t* route_idx, int T, int G, int epr, int32_t* pos,

@@ -4,6 +4,7 @@
 #include <nccl.h>
 
 #include "gm_kernels.h"
+#include "post_moe.cuh"
 
 namespace gm {
 
@@ -34,5 +35,8 @@ cudaError_t launch_ep_pack(const void* x_rows, int row_bytes, const float* x_sa,
 // out[t] = bf16(sum_d f32(contrib[d*cap + pos[t][d]])), d ascending.
 cudaError_t launch_ep_final(const uint16_t* contrib, const int32_t* pos, int T, int G, int cap,
                             uint16_t* out, cudaStream_t s);
+// the same sum, then the post-MoE tail updating p.x_main
+cudaError_t launch_ep_final_post(const uint16_t* contrib, const int32_t* pos, int T, int G, int cap,
+                                 const PostParams& p, cudaStream_t s);
 
 }  // namespace gm

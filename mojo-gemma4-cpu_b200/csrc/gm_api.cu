@@ -36,6 +36,11 @@ struct Layer {
   alignas(64) unsigned char tmap_gu[128] = {};
   alignas(64) unsigned char tmap_dn[128] = {};
   bool has_tc = false;
+  // post-MoE tail (gm_moe_register_post)
+  uint16_t* post_w1 = nullptr;  // post_feedforward_layernorm_1 [H]
+  uint16_t* post_w2 = nullptr;  // post_feedforward_layernorm_2 [H]
+  uint16_t* post_w = nullptr;   // post_feedforward_layernorm [H]
+  float layer_scalar = 1.0f;
 };
 
 }  // namespace
@@ -211,8 +216,8 @@ int dev_copy(gm_moe* h, T** dst, const void* src, size_t count, const char* what
 }
 
 void free_layer(Layer& L) {
-  void* ptrs[] = {L.gu_q, L.gu_scale, L.dn_q, L.dn_scale, L.gu_bf16, L.dn_bf16,
-                  L.router, L.rscale, L.pes, L.gamma2, L.gu_rm, L.dn_rm};
+  void* ptrs[] = {L.gu_q, L.gu_scale, L.dn_q, L.dn_scale, L.gu_bf16, L.dn_bf16, L.router, L.rscale,
+                  L.pes, L.gamma2, L.gu_rm, L.dn_rm, L.post_w1, L.post_w2, L.post_w};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   L = Layer{};
@@ -367,7 +372,7 @@ struct StageScope {
 // x_i8/x_sa (butterquant) or x_normed (bf16), route_idx their top-8.
 int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, const float* x_sa,
                         const uint16_t* x_normed, const int32_t* route_idx, uint16_t* out,
-                        cudaStream_t s) {
+                        cudaStream_t s, const PostParams* post = nullptr) {
   if (L.kind == 1) {
     if (L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
       // prefill: routed rows gathered in schedule order, then the tcgen05 GEMM
@@ -406,7 +411,10 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
                                       L.dn_bf16, h->ybuf, s),
              "phase2_down");
   }
-  GM_STAGE(h, s, launch_combine(route_idx, h->route_pos, h->ybuf, Tn, out, s), "combine");
+  if (post)
+    GM_STAGE(h, s, launch_combine_post(route_idx, h->route_pos, h->ybuf, Tn, *post, s), "combine.post");
+  else
+    GM_STAGE(h, s, launch_combine(route_idx, h->route_pos, h->ybuf, Tn, out, s), "combine");
   return GM_OK;
 }
 
@@ -424,7 +432,8 @@ int nccl_check(gm_moe* h, ncclResult_t r, const char* what) {
 
 // Expert-parallel forward (after gm_moe_ep_init): this rank's T tokens in,
 // their full MoE output out; see ep.cu for the exchange.
-int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int T, cudaStream_t s) {
+int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int T, cudaStream_t s,
+               const PostParams* post) {
   const NcclApi* nc = nccl_api(nullptr);
   const int G = h->degree, cap = h->max_tokens, n = G * cap;
   const bool bq = L.kind == 1;
@@ -491,8 +500,11 @@ int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int
     }
     GM_NCCL(h, nc->group_end(), "ep combine");
   }
-  // 6. sum of the ranks' partials in rank order
-  GM_STAGE(h, s, launch_ep_final(h->ep_contrib, h->ep_pos, T, G, cap, out, s), "ep_final");
+  // 6. sum of the ranks' partials in rank order (then the post-MoE tail)
+  if (post)
+    GM_STAGE(h, s, launch_ep_final_post(h->ep_contrib, h->ep_pos, T, G, cap, *post, s), "ep_final.post");
+  else
+    GM_STAGE(h, s, launch_ep_final(h->ep_contrib, h->ep_pos, T, G, cap, out, s), "ep_final");
   return GM_OK;
 }
 
@@ -639,7 +651,11 @@ struct PdlScope {
 };
 }  // namespace
 
-int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void* stream) {
+namespace {
+// gm_moe_forward (post == NULL) and gm_moe_forward_ffn (post-MoE tail fused
+// into the final kernel, x_main updated in place).
+int forward_impl(gm_moe* h, int layer, const void* x, void* out, int T, void* stream,
+                 const PostParams* post) {
   int rc = check_layer(h, layer);
   if (rc) return rc;
   const Layer& L = h->layers[layer];
@@ -650,7 +666,8 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
   cudaStream_t s = S(stream);
   if (h->pending.size() > 4096 && (rc = drain_profile(h))) return rc;  // bound the event backlog
   PdlScope pdl_scope(h->pdl);
-  if (h->ep_comm) return ep_forward(h, L, static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), T, s);
+  if (h->ep_comm)
+    return ep_forward(h, L, static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), T, s, post);
   if (T == 0) return GM_OK;
   const uint16_t* xb = static_cast<const uint16_t*>(x);
   // 0. decode batches route to nearly every expert: pull the gate/up weights
@@ -680,9 +697,39 @@ int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void
                                  h->epr, rc_chunk, h->expert_offset, h->routes, h->route_pos,
                                  h->chunk_off, h->sched_counts, s),
          "router_merge.schedule");
-  // 4. experts, 5. combine
+  // 4. experts, 5. combine (+ post-MoE tail)
   return experts_and_combine(h, L, T, h->x_i8, h->x_sa, h->x_normed, h->route_idx,
-                             static_cast<uint16_t*>(out), s);
+                             static_cast<uint16_t*>(out), s, post);
+}
+}  // namespace
+
+int gm_moe_forward(gm_moe_t* h, int layer, const void* x, void* out, int T, void* stream) {
+  return forward_impl(h, layer, x, out, T, stream, nullptr);
+}
+
+int gm_moe_register_post(gm_moe_t* h, int layer, const void* post_ffn_norm_1,
+                         const void* post_ffn_norm_2, const void* post_ffn_norm, float layer_scalar) {
+  int rc = check_layer(h, layer);
+  if (rc) return rc;
+  GM_TRY(h, cudaSetDevice(h->device), "register_post");
+  Layer& L = h->layers[layer];
+  if ((rc = dev_copy(h, &L.post_w1, post_ffn_norm_1, (size_t)H, "post_ffn_norm_1"))) return rc;
+  if ((rc = dev_copy(h, &L.post_w2, post_ffn_norm_2, (size_t)H, "post_ffn_norm_2"))) return rc;
+  if ((rc = dev_copy(h, &L.post_w, post_ffn_norm, (size_t)H, "post_ffn_norm"))) return rc;
+  L.layer_scalar = layer_scalar;
+  return GM_OK;
+}
+
+int gm_moe_forward_ffn(gm_moe_t* h, int layer, void* x_main, const void* dense_out, int T,
+                       void* stream) {
+  int rc = check_layer(h, layer);
+  if (rc) return rc;
+  const Layer& L = h->layers[layer];
+  if (!L.post_w1) return set_err(h, GM_ESTATE, "layer %d: gm_moe_register_post not called", layer);
+  if (!x_main || !dense_out) return set_err(h, GM_EINVAL, "NULL x_main/dense_out");
+  PostParams p{static_cast<const uint16_t*>(dense_out), static_cast<uint16_t*>(x_main), L.post_w1,
+               L.post_w2, L.post_w, L.layer_scalar};
+  return forward_impl(h, layer, x_main, x_main, T, stream, &p);
 }
 
 int gm_moe_set_option(gm_moe_t* h, int option, long value) {

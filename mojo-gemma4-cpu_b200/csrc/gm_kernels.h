@@ -105,6 +105,10 @@ cudaError_t launch_bf16_phase2(const uint16_t* bucket, const int32_t* expert_off
                                const uint16_t* w_dn, float* ybuf, cudaStream_t s);
 cudaError_t launch_combine(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
                            int T, uint16_t* out, cudaStream_t s);
+struct PostParams;
+// the combine, then the post-MoE tail updating p.x_main (post_moe.cuh)
+cudaError_t launch_combine_post(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
+                                int T, const PostParams& p, cudaStream_t s);
 // tcgen05 prefill path (gemm_tc.cu)
 // 2-D TMA descriptor (128-byte swizzle, boxes of 128 bytes x box_rows rows)
 // over a row-major [rows][cols] tensor of 1-byte (int8) or 2-byte (bf16) elements

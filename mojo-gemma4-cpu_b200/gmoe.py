@@ -46,6 +46,8 @@ SIGNATURES = {
     "gm_moe_forward": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp]),
     "gm_moe_forward_sync": (_i32, [_vp, _i32, _vp, _vp, _i32]),
     "gm_moe_set_option": (_i32, [_vp, _i32, _i64]),
+    "gm_moe_register_post": (_i32, [_vp, _i32, _vp, _vp, _vp, C.c_float]),
+    "gm_moe_forward_ffn": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp]),
     "gm_moe_device_status": (_i32, [_vp, C.POINTER(_i32)]),
     "gm_ep_unique_id": (_i32, [_vp, _sz]),
     "gm_moe_ep_init": (_i32, [_vp, _vp, _i32]),
@@ -169,6 +171,15 @@ class MoeBlock:
     def forward(self, layer, x, out, T, stream=None):
         """Asynchronous on `stream`: x, out device bf16 [T][2816]."""
         check(lib().gm_moe_forward(self.h, layer, _addr(x), _addr(out), T, _stream(stream)), self.h)
+
+    def register_post(self, layer, post_ffn_norm_1, post_ffn_norm_2, post_ffn_norm, layer_scalar):
+        check(lib().gm_moe_register_post(self.h, layer, _addr(post_ffn_norm_1), _addr(post_ffn_norm_2),
+                                         _addr(post_ffn_norm), float(layer_scalar)), self.h)
+
+    def forward_ffn(self, layer, x_main, dense_out, T, stream=None):
+        """MoE on x_main, then the post-MoE tail; x_main is updated in place."""
+        check(lib().gm_moe_forward_ffn(self.h, layer, _addr(x_main), _addr(dense_out), T,
+                                       _stream(stream)), self.h)
 
     def forward_sync(self, layer, x, out, T):
         """Blocking; x/out may be host (e.g. pinned) or device buffers."""

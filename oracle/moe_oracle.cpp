@@ -391,6 +391,32 @@ void orc_rms_norm(const uint16_t* x, const uint16_t* gamma, int T, uint16_t* out
   }
 }
 
+// The tail of dispatch_bq_ffn after the MoE (modeling/gemma_4_moe_bq.mojo:
+// 785-805), per token:
+//   dense = rms_norm(dense, post_ffn_norm_1)                 (kernels/rmsnorm.mojo:21-47)
+//   dense = norm_residual_add(src=moe, residual=dense, w=post_ffn_norm_2)
+//   x     = norm_residual_add(src=dense, residual=x,  w=post_ffn_norm)
+//   x     = x * layer_scalar                              (kernels/elementwise.mojo:75-83)
+// norm_residual_add_row (kernels/rmsnorm.mojo:51-67): bf16(r + (s*inv_rms(s))*w).
+void orc_post_moe(const uint16_t* moe, const uint16_t* dense, const uint16_t* x_main,
+                  const uint16_t* w1, const uint16_t* w2, const uint16_t* w, float layer_scalar,
+                  int T, uint16_t* out) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    const uint16_t* m = moe + (long)t * H;
+    const uint16_t* d = dense + (long)t * H;
+    const uint16_t* x = x_main + (long)t * H;
+    std::vector<uint16_t> d1(H), d2(H), xm(H);
+    const float inv_d = inv_rms_row(d);
+    for (int k = 0; k < H; ++k) d1[k] = f2bf(bf2f(d[k]) * inv_d * bf2f(w1[k]));
+    const float inv_m = inv_rms_row(m);
+    for (int k = 0; k < H; ++k) d2[k] = f2bf(bf2f(d1[k]) + bf2f(m[k]) * inv_m * bf2f(w2[k]));
+    const float inv_2 = inv_rms_row(d2.data());
+    for (int k = 0; k < H; ++k) xm[k] = f2bf(bf2f(x[k]) + bf2f(d2[k]) * inv_2 * bf2f(w[k]));
+    for (int k = 0; k < H; ++k) out[(long)t * H + k] = f2bf(bf2f(xm[k]) * layer_scalar);
+  }
+}
+
 // kernels/moe_experts.mojo:16-54,82-154 Phase1GateUpKernel: per routed record
 // g = x.Wgu[e][j], u = x.Wgu[e][I+j] (bf16 dots, PU=4), bucket = bf16(gelu(g)*u)
 void orc_phase1_bf16(const uint16_t* x_normed, const int32_t* expert_offset,

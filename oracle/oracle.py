@@ -65,6 +65,7 @@ def _declare(L):
         "orc_router": (None, [vp, i32, vp, vp, vp, vp, vp, vp]),
         "orc_build_schedules": (None, [vp, vp, i32, i32, i32, vp, vp]),
         "orc_rms_norm": (None, [vp, vp, i32, vp]),
+        "orc_post_moe": (None, [vp, vp, vp, vp, vp, vp, C.c_float, i32, vp]),
         "orc_phase1_bf16": (None, [vp, vp, vp, vp, i32, vp]),
         "orc_phase2_bf16": (None, [vp, vp, vp, vp, i32, i32, vp]),
         "orc_bq_norm_quant": (None, [vp, vp, i32, vp, vp]),
@@ -179,6 +180,15 @@ def build_schedules(idx, w, expert_base, epr):
 def rms_norm(x, gamma):
     out = np.empty_like(x)
     lib().orc_rms_norm(_p(x), _p(gamma), x.shape[0], _p(out))
+    return out
+
+
+def post_moe(moe, dense, x_main, w1, w2, w, layer_scalar):
+    """The post-MoE tail of dispatch_bq_ffn (post norms, residual, layer scalar)."""
+    T = moe.shape[0]
+    out = np.empty((T, H), np.uint16)
+    a = [np.ascontiguousarray(v) for v in (moe, dense, x_main, w1, w2, w)]
+    lib().orc_post_moe(*[_p(v) for v in a], float(layer_scalar), T, _p(out))
     return out
 
 

@@ -370,6 +370,34 @@ def test_forward_bf16_tc_prefill(T, layer_stress):
     assert rel_err(host(out_tc), host(out_dec)) < 1e-2
 
 
+@pytest.mark.parametrize("T", [16, 1100])
+def test_forward_ffn_post_moe_tail(T, layer_stress):
+    """gm_moe_forward_ffn: the post-MoE tail fused into the combine equals the
+    oracle's tail applied to the same handle's MoE output (up to the order of
+    the three row reductions), for the decode and the tcgen05 path."""
+    raw, ref, g = layer_stress
+    blk = make_block(g, max_tokens=T)
+    rng = np.random.default_rng(T)
+    bf = lambda a: O.f32_to_bf16(np.asarray(a, np.float32))
+    w1, w2, w = (bf(1.0 + 0.2 * rng.standard_normal(H)) for _ in range(3))
+    blk.register_post(0, dev(w1), dev(w2), dev(w), 0.875)
+    x_np = tokens_np(T, seed=900 + T)
+    dense_np = bf(rng.standard_normal((T, H)) * 3.0)
+    moe = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    blk.forward(0, dev(x_np), moe, T)
+    x_main = dev(x_np)
+    blk.profile(True)
+    blk.forward_ffn(0, x_main, dev(dense_np), T)
+    stats, _ = blk.profile_read()
+    torch.cuda.synchronize()
+    assert blk.device_status() == 0
+    assert "combine.post" in stats and "combine" not in stats
+    want = O.post_moe(host(moe), dense_np, x_np, w1, w2, w, 0.875)
+    got = host(x_main)
+    assert rel_err(got, want) < 1e-2
+    assert (got == want).mean() > 0.97
+
+
 def test_forward_deterministic_and_sync_host_path(layer_stress):
     raw, ref, g = layer_stress
     blk = make_block(g, max_tokens=128)

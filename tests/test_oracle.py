@@ -219,3 +219,28 @@ def test_bq_close_to_bf16_path(bq_small):
     keep = (ib == iq).all(axis=1)
     assert keep.mean() > 0.9
     assert rel_err(oq, ob, rows=keep) < 0.1
+
+
+def test_post_moe_tail():
+    """orc_post_moe (modeling/gemma_4_moe_bq.mojo:785-805): identities, and a
+    float64 restatement of the three norms within bf16 rounding."""
+    rng = np.random.default_rng(5)
+    T = 6
+    bf = lambda a: O.f32_to_bf16(np.asarray(a, np.float32))
+    moe, dense, x = (bf(rng.standard_normal((T, H)) * s) for s in (0.3, 2.0, 1.0))
+    w1, w2, w = (bf(1.0 + 0.2 * rng.standard_normal(H)) for _ in range(3))
+    zero = np.zeros(H, np.uint16)
+    # all gains zero: x_main * layer_scalar
+    out = O.post_moe(moe, dense, x, zero, zero, zero, 0.5)
+    assert np.array_equal(out, bf(O.bf16_to_f32(x) * np.float32(0.5)))
+
+    def inv(v):
+        v = v.astype(np.float64)
+        return np.sqrt(H) / np.sqrt((v * v).sum(axis=1, keepdims=True) + H * 1e-6)
+
+    f = lambda a: O.bf16_to_f32(a).astype(np.float64)
+    d1 = f(dense) * inv(f(dense)) * f(w1)
+    d2 = d1 + f(moe) * inv(f(moe)) * f(w2)
+    ref = (f(x) + d2 * inv(d2) * f(w)) * 0.75
+    got = f(O.post_moe(moe, dense, x, w1, w2, w, 0.75))
+    assert np.abs(got - ref).max() <= 0.02 * np.abs(ref).max()
