@@ -36,13 +36,15 @@ WORKLOADS = {
     #   replicas:  N independent copies, tokens per GPU fixed (weak scaling)
     #   ep-weak:   expert parallel over the N GPUs, tokens per GPU fixed
     #   ep-strong: expert parallel, tokens per step fixed in total (split over N)
-    "bq-decode-b64": (64, "bq", "replicas"),
+    # the default: on one GPU the plain forward; on N GPUs expert parallel
+    # (each GPU holds 128/N experts and 64 tokens, dispatch/combine over NCCL)
+    "bq-decode-b64": (64, "bq", "ep-weak"),
     "bq-decode-b8": (8, "bq", "replicas"),
     "bq-decode-b1": (1, "bq", "replicas"),
     "bf16-decode-b16": (16, "bf16", "replicas"),
     "bq-prefill-4k": (4096, "bq", "replicas"),
     "bf16-prefill-4k": (4096, "bf16", "replicas"),
-    "ep-decode-b64": (64, "bq", "ep-weak"),
+    "bq-decode-b64-replicas": (64, "bq", "replicas"),
     # Zipf(1.1) routing (expert i-1 receives 8T*i^-1.1/sum of the routes, capped at T)
     "bq-prefill-4k-zipf": (4096, "bq", "replicas"),
     "bf16-prefill-4k-zipf": (4096, "bf16", "replicas"),
@@ -67,6 +69,8 @@ def parse():
                    help="bounded CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--batches", type=int, default=8, help="distinct token batches cycled")
+    p.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                   help="expert placement of Zipf expert-parallel workloads")
     return p.parse_args()
 
 
@@ -291,6 +295,14 @@ def main():
                            dtype=torch.uint8, device="cuda")
         dist.broadcast(uid, 0)
         blk.ep_init(bytes(uid.cpu().tolist()), world)
+    placement, rank_of = "contiguous", None
+    if ep and world > 1 and zipf and args.placement == "balanced":
+        # experts spread by their expected Zipf load (the C ABI still takes the
+        # reference's contiguous blocks; the library moves the weights)
+        import synth
+        rank_of = gmoe.balanced_placement(synth.zipf_targets(T * world), world)
+        blk.ep_set_placement(rank_of)
+        placement = "balanced (Zipf target load, longest-processing-time first)"
     g = torch.Generator(device="cuda")
     g.manual_seed(1000 + rank)
     if zipf:
@@ -395,7 +407,8 @@ def main():
 
     # ---- roofline of the dominant kernel: CUDA events on the forward's stream
     # around each stage of the same forward (handle's stage profiler)
-    roof = roofline(blk, fmt, L, xs, outs, T, args.steps, stream, args.workload, rank, world, ep, dist)
+    roof = roofline(blk, fmt, L, xs, outs, T, args.steps, stream, args.workload, rank, world, ep, dist,
+                    rank_of)
 
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -404,7 +417,7 @@ def main():
         "dtype": "i8" if fmt == "bq" else "bf16",
         "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights; random-init, no checkpoint)",
         "config": {"workload": args.workload, "tokens_per_step": T * world, "tokens_per_gpu": T,
-                   "weights": fmt, "layers": nl,
+                   "weights": fmt, "layers": nl, "expert_placement": placement if ep and world > 1 else None,
                    "parallelism": ("ep%d" % world) if ep and world > 1 else ("replicas" if world > 1 else "single"),
                    "l2": "inputs larger than L2: %d distinct token batches, routed expert weights %.0f MB per step"
                          % (len(xs), roof.get("weight_mb", 0))},
@@ -504,7 +517,8 @@ def stage_model(label, fmt, T, distinct, R):
     return "hbm", None
 
 
-def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1, ep=False, dist=None):
+def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1, ep=False, dist=None,
+             rank_of=None):
     """Per-stage device times of the forward itself: the handle's stage
     profiler (GM_OPT_PROFILE) records CUDA events on the forward's stream
     around every stage; L2 is flushed (256 MB write) before each profiled
@@ -516,8 +530,12 @@ def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1,
     import gmoe
     hbm, tf, src = peaks()
     s = stream
+    import numpy as np
     epr = E // world if ep else E
-    base = rank * epr if ep else 0
+    if rank_of is None:
+        rank_of = [e // epr for e in range(E)] if ep else [0] * E
+    owner = np.asarray(rank_of)
+    mine_idx = torch.tensor(np.nonzero(owner == (rank if ep else 0))[0], device="cuda")
     # routes into this GPU's experts and the distinct experts they reach, per
     # batch (with expert parallelism: over every rank's tokens)
     lg = torch.empty(gmoe.lib().gm_router_workspace_bytes(T) // 4, dtype=torch.float32, device="cuda")
@@ -532,7 +550,7 @@ def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1,
         if ep and dist is not None:
             dist.all_reduce(hist)
         hist_sum += hist
-        mine = hist[base:base + epr]
+        mine = hist[mine_idx]
         per_batch.append((int((mine > 0).sum()), int(mine.sum())))
     torch.cuda.synchronize()
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
@@ -596,7 +614,7 @@ def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1,
             "expert_routes_top8": [int(v) for v in h[:8]],
             "expert_routes_last4": [int(v) for v in h[-4:]]}
     if ep and world > 1:
-        load["routes_per_gpu"] = [int(h[r * epr:(r + 1) * epr].sum()) for r in range(world)]
+        load["routes_per_gpu"] = [int(h[owner == r].sum()) for r in range(world)]
     if workload in ZIPF:
         import synth
         load["zipf_target_top8"] = [int(round(v)) for v in synth.zipf_targets(tokens)[:8]]

@@ -182,6 +182,17 @@ int gm_moe_profile_read(gm_moe_t* h, gm_stage_stat_t* stats, int max_stats, int*
 int gm_ep_unique_id(void* out, size_t bytes);
 int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world);
 
+/* Optional load-based placement (no reference counterpart; the reference keeps
+ * contiguous blocks).  expert_rank[128] (host) names the rank that holds each
+ * expert, every rank exactly 128/world of them.  Collective (same map on every
+ * rank), after gm_moe_ep_init and after every layer is registered: the layers
+ * are still registered as the reference's contiguous blocks, and the library
+ * exchanges expert weights (NCCL all-gather) so that each rank keeps its
+ * assigned experts.  The per-rank partials are then sums over each rank's
+ * placed experts, so results match the contiguous placement within rounding,
+ * not bit for bit. */
+int gm_moe_ep_set_placement(gm_moe_t* h, const int32_t* expert_rank);
+
 /* Synchronises the handle's device and reports (then clears) the device-side
  * error word that kernels with bounded waits write when a wait expires:
  * *device_error = 0 and GM_OK when none did, GM_ETIMEOUT otherwise. */

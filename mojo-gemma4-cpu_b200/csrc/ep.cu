@@ -65,7 +65,7 @@ const NcclApi* nccl_api(const char** err) {
               sym(lib, "ncclCommGetAsyncError", g_nccl.comm_get_async_error) &&
               sym(lib, "ncclGroupStart", g_nccl.group_start) &&
               sym(lib, "ncclGroupEnd", g_nccl.group_end) && sym(lib, "ncclSend", g_nccl.send) &&
-              sym(lib, "ncclRecv", g_nccl.recv) &&
+              sym(lib, "ncclRecv", g_nccl.recv) && sym(lib, "ncclAllGather", g_nccl.all_gather) &&
               sym(lib, "ncclGetErrorString", g_nccl.get_error_string);
     g_nccl.loaded = ok;
   });
@@ -82,7 +82,8 @@ const NcclApi* nccl_api(const char** err) {
 // token's row in that destination's block (token order).
 __global__ void __launch_bounds__(1024)
 ep_plan_kernel(const int32_t* __restrict__ route_idx, int T, int G, int epr,
-               int32_t* __restrict__ pos, int32_t* __restrict__ count) {
+               const int32_t* __restrict__ rank_of, int32_t* __restrict__ pos,
+               int32_t* __restrict__ count) {
   __shared__ int s_cnt[32];   // per-warp counts of the current destination
   __shared__ int s_pre[32];   // their exclusive prefix
   __shared__ int s_tot;       // chunk total
@@ -99,7 +100,7 @@ ep_plan_kernel(const int32_t* __restrict__ route_idx, int T, int G, int epr,
 #pragma unroll
       for (int k = 0; k < TOPK; ++k) {
         const int e = route_idx[t * TOPK + k];
-        if (e >= 0 && e < E) mask |= 1u << (e / epr);
+        if (e >= 0 && e < E) mask |= 1u << (rank_of ? __ldg(rank_of + e) : e / epr);
       }
     }
     for (int d = 0; d < G; ++d) {
@@ -134,9 +135,11 @@ ep_plan_kernel(const int32_t* __restrict__ route_idx, int T, int G, int epr,
 __global__ void __launch_bounds__(256)
 ep_pack_kernel(const uint8_t* __restrict__ x_rows, int row_bytes, const float* __restrict__ x_sa,
                const int32_t* __restrict__ route_idx, const float* __restrict__ route_w, int T,
-               int G, int cap, const int32_t* __restrict__ pos, const int32_t* __restrict__ count,
-               uint8_t* __restrict__ send_x, float* __restrict__ send_sa,
-               int32_t* __restrict__ send_idx, float* __restrict__ send_w) {
+               int G, int cap, int epr, const int32_t* __restrict__ rank_of,
+               const int32_t* __restrict__ local_of, const int32_t* __restrict__ pos,
+               const int32_t* __restrict__ count, uint8_t* __restrict__ send_x,
+               float* __restrict__ send_sa, int32_t* __restrict__ send_idx,
+               float* __restrict__ send_w) {
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
@@ -150,7 +153,10 @@ ep_pack_kernel(const uint8_t* __restrict__ x_rows, int row_bytes, const float* _
       uint4* dst = reinterpret_cast<uint4*>(send_x + row * row_bytes);
       for (int i = lane; i < row_bytes / 16; i += 32) dst[i] = src[i];
       if (lane < TOPK) {
-        send_idx[row * TOPK + lane] = route_idx[t * TOPK + lane];
+        int e = route_idx[t * TOPK + lane];
+        if (rank_of && e >= 0 && e < E)
+          e = __ldg(rank_of + e) == d ? d * epr + __ldg(local_of + e) : -1;
+        send_idx[row * TOPK + lane] = e;
         send_w[row * TOPK + lane] = route_w[t * TOPK + lane];
       }
       if (lane == 0 && x_sa) send_sa[row] = x_sa[t];
@@ -242,19 +248,22 @@ cudaError_t launch_ep_final_post(const uint16_t* contrib, const int32_t* pos, in
   return launch_k(ep_final_post_kernel, dim3(T), dim3(POST_THREADS), 0, s, contrib, pos, T, G, cap, p);
 }
 
-cudaError_t launch_ep_plan(const int32_t* route_idx, int T, int G, int epr, int32_t* pos,
-                           int32_t* count, cudaStream_t s) {
-  return launch_k(ep_plan_kernel, dim3(1), dim3(1024), 0, s, route_idx, T, G, epr, pos, count);
+cudaError_t launch_ep_plan(const int32_t* route_idx, int T, int G, int epr, EpPlacement pl,
+                           int32_t* pos, int32_t* count, cudaStream_t s) {
+  return launch_k(ep_plan_kernel, dim3(1), dim3(1024), 0, s, route_idx, T, G, epr, pl.rank_of, pos,
+                  count);
 }
 
 cudaError_t launch_ep_pack(const void* x_rows, int row_bytes, const float* x_sa,
                            const int32_t* route_idx, const float* route_w, int T, int G, int cap,
-                           const int32_t* pos, const int32_t* count, void* send_x, float* send_sa,
-                           int32_t* send_idx, float* send_w, cudaStream_t s) {
+                           int epr, EpPlacement pl, const int32_t* pos, const int32_t* count,
+                           void* send_x, float* send_sa, int32_t* send_idx, float* send_w,
+                           cudaStream_t s) {
   const int blocks = std::max(1, std::min(1184, (std::max(T, G * cap) + 7) / 8));
   return launch_k(ep_pack_kernel, dim3(blocks), dim3(256), 0, s,
                   static_cast<const uint8_t*>(x_rows), row_bytes, x_sa, route_idx, route_w, T, G, cap,
-                  pos, count, static_cast<uint8_t*>(send_x), send_sa, send_idx, send_w);
+                  epr, pl.rank_of, pl.local_of, pos, count, static_cast<uint8_t*>(send_x), send_sa,
+                  send_idx, send_w);
 }
 
 cudaError_t launch_ep_final(const uint16_t* contrib, const int32_t* pos, int T, int G, int cap,

@@ -18,20 +18,32 @@ struct NcclApi {
   ncclResult_t (*group_end)() = nullptr;
   ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*get_error_string)(ncclResult_t) = nullptr;
 };
 
 // NCCL loaded on first use (nullptr and *err set when it cannot be).
 const NcclApi* nccl_api(const char** err);
 
+// Expert placement (device tables, E entries each): rank_of[e] = the rank
+// holding expert e, local_of[e] = its index among that rank's experts.  Null
+// tables mean the reference's contiguous blocks (rank e / epr, index e % epr).
+struct EpPlacement {
+  const int32_t* rank_of = nullptr;
+  const int32_t* local_of = nullptr;
+};
 // pos[t][d]: row of token t in destination d's send block, or -1; count[d].
-cudaError_t launch_ep_plan(const int32_t* route_idx, int T, int G, int epr, int32_t* pos,
-                           int32_t* count, cudaStream_t s);
-// Pack the send blocks [G][cap] (rows of row_bytes; x_sa may be null).
+cudaError_t launch_ep_plan(const int32_t* route_idx, int T, int G, int epr, EpPlacement pl,
+                           int32_t* pos, int32_t* count, cudaStream_t s);
+// Pack the send blocks [G][cap] (rows of row_bytes; x_sa may be null).  With
+// a placement, the ids sent to rank d are rewritten to d*epr + local index
+// for d's experts and -1 for the others, so the receiver's contiguous
+// schedule applies unchanged.
 cudaError_t launch_ep_pack(const void* x_rows, int row_bytes, const float* x_sa,
                            const int32_t* route_idx, const float* route_w, int T, int G, int cap,
-                           const int32_t* pos, const int32_t* count, void* send_x, float* send_sa,
-                           int32_t* send_idx, float* send_w, cudaStream_t s);
+                           int epr, EpPlacement pl, const int32_t* pos, const int32_t* count,
+                           void* send_x, float* send_sa, int32_t* send_idx, float* send_w,
+                           cudaStream_t s);
 // out[t] = bf16(sum_d f32(contrib[d*cap + pos[t][d]])), d ascending.
 cudaError_t launch_ep_final(const uint16_t* contrib, const int32_t* pos, int T, int G, int cap,
                             uint16_t* out, cudaStream_t s);

@@ -113,6 +113,9 @@ struct gm_moe {
   float* ep_recv_w = nullptr;
   uint16_t* ep_partial = nullptr;  // [degree*max_tokens][H]
   uint16_t* ep_contrib = nullptr;
+  int32_t* ep_rank_of = nullptr;   // [E] placement tables (device), used once placed
+  int32_t* ep_local_of = nullptr;
+  bool ep_placed = false;          // gm_moe_ep_set_placement done
 };
 
 namespace {
@@ -449,11 +452,16 @@ int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int
     GM_STAGE(h, s, launch_topk(h->logits, L.pes, T, h->route_idx, h->route_w, s), "router_merge");
   }
   // 2. destinations and send blocks
-  GM_STAGE(h, s, launch_ep_plan(h->route_idx, T, G, h->epr, h->ep_pos, h->ep_count, s), "ep_plan");
+  EpPlacement pl;
+  if (h->ep_placed) {
+    pl.rank_of = h->ep_rank_of;
+    pl.local_of = h->ep_local_of;
+  }
+  GM_STAGE(h, s, launch_ep_plan(h->route_idx, T, G, h->epr, pl, h->ep_pos, h->ep_count, s), "ep_plan");
   GM_STAGE(h, s, launch_ep_pack(bq ? static_cast<const void*>(h->x_i8) : static_cast<const void*>(h->x_normed),
                                 row_bytes, bq ? h->x_sa : nullptr, h->route_idx, h->route_w, T, G, cap,
-                                h->ep_pos, h->ep_count, h->ep_send_x, h->ep_send_sa, h->ep_send_idx,
-                                h->ep_send_w, s),
+                                h->epr, pl, h->ep_pos, h->ep_count, h->ep_send_x, h->ep_send_sa,
+                                h->ep_send_idx, h->ep_send_w, s),
            "ep_pack");
   // 3. dispatch: block p of every array goes to rank p
   {
@@ -596,6 +604,8 @@ int gm_moe_register_layer_bq(gm_moe_t* h, int layer, const void* gate_up,
                              const void* pre_ffn_norm_2) {
   int rc = check_layer(h, layer);
   if (rc) return rc;
+  if (h->ep_placed)
+    return set_err(h, GM_ESTATE, "layers are registered before gm_moe_ep_set_placement");
   GM_TRY(h, cudaSetDevice(h->device), "register_layer_bq");
   Layer& L = h->layers[layer];
   free_layer(L);
@@ -626,6 +636,8 @@ int gm_moe_register_layer_bf16(gm_moe_t* h, int layer, const void* gate_up, cons
                                const void* per_expert_scale, const void* pre_ffn_norm_2) {
   int rc = check_layer(h, layer);
   if (rc) return rc;
+  if (h->ep_placed)
+    return set_err(h, GM_ESTATE, "layers are registered before gm_moe_ep_set_placement");
   GM_TRY(h, cudaSetDevice(h->device), "register_layer_bf16");
   Layer& L = h->layers[layer];
   free_layer(L);
@@ -807,6 +819,7 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
   const size_t o_rx = c.take<uint8_t>(n * 2 * H), o_rsa = c.take<float>(n),
                o_ridx = c.take<int32_t>(n * TOPK), o_rw = c.take<float>(n * TOPK);
   const size_t o_part = c.take<uint16_t>(n * H), o_con = c.take<uint16_t>(n * H);
+  const size_t o_rank = c.take<int32_t>(E), o_local = c.take<int32_t>(E);
   GM_TRY(h, cudaMalloc(&h->ep_buf, align_up(c.off, 256)), "ep buffers");
   char* b = static_cast<char*>(h->ep_buf);
   h->ep_pos = reinterpret_cast<int32_t*>(b + o_pos);
@@ -821,6 +834,8 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
   h->ep_recv_w = reinterpret_cast<float*>(b + o_rw);
   h->ep_partial = reinterpret_cast<uint16_t*>(b + o_part);
   h->ep_contrib = reinterpret_cast<uint16_t*>(b + o_con);
+  h->ep_rank_of = reinterpret_cast<int32_t*>(b + o_rank);
+  h->ep_local_of = reinterpret_cast<int32_t*>(b + o_local);
   GM_TRY(h, cudaMemset(h->ep_buf, 0, align_up(c.off, 256)), "ep buffers");
   ncclUniqueId id;
   memcpy(&id, unique_id, sizeof id);
@@ -828,6 +843,65 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
   const ncclResult_t r = nc->comm_init_rank(&comm, world, id, h->rank);
   if (r != ncclSuccess) return set_err(h, GM_ENCCL, "ncclCommInitRank: %s", nc->get_error_string(r));
   h->ep_comm = comm;
+  return GM_OK;
+}
+
+int gm_moe_ep_set_placement(gm_moe_t* h, const int32_t* expert_rank) {
+  if (!h || !expert_rank) return set_err(h, GM_EINVAL, "gm_moe_ep_set_placement: NULL argument");
+  if (!h->ep_comm) return set_err(h, GM_ESTATE, "gm_moe_ep_set_placement: gm_moe_ep_init first");
+  if (h->ep_placed) return set_err(h, GM_ESTATE, "gm_moe_ep_set_placement: placement already set");
+  const int G = h->degree, epr = h->epr;
+  std::vector<int32_t> rank_of(E), local_of(E), mine;
+  std::vector<int> per(G, 0);
+  for (int e = 0; e < E; ++e) {
+    const int r = expert_rank[e];
+    if (r < 0 || r >= G) return set_err(h, GM_EINVAL, "expert %d placed on rank %d of %d", e, r, G);
+    rank_of[e] = r;
+    local_of[e] = per[r]++;  // experts of a rank keep ascending id order
+    if (r == h->rank) mine.push_back(e);
+  }
+  for (int r = 0; r < G; ++r)
+    if (per[r] != epr)
+      return set_err(h, GM_EINVAL, "rank %d holds %d experts; every rank must hold %d", r, per[r], epr);
+  const NcclApi* nc = nccl_api(nullptr);
+  GM_TRY(h, cudaSetDevice(h->device), "ep_set_placement");
+  cudaStream_t s = h->own_stream;
+  // Every registered layer arrived as the reference's contiguous block of this
+  // rank: gather all blocks (global expert order) and keep this rank's experts.
+  auto redistribute = [&](void* local, size_t per_expert) -> int {
+    void* full = nullptr;
+    GM_TRY(h, cudaMalloc(&full, per_expert * E), "ep placement gather buffer");
+    int rc = nccl_check(h, nc->all_gather(local, full, per_expert * epr, ncclUint8, h->ep_comm, s),
+                        "ep placement all-gather");
+    for (int i = 0; rc == GM_OK && i < epr; ++i)
+      rc = cuda_check(h, cudaMemcpyAsync(static_cast<char*>(local) + i * per_expert,
+                                         static_cast<char*>(full) + mine[i] * per_expert, per_expert,
+                                         cudaMemcpyDeviceToDevice, s),
+                      "ep placement copy");
+    if (rc == GM_OK) rc = cuda_check(h, cudaStreamSynchronize(s), "ep placement");
+    cudaFree(full);
+    return rc;
+  };
+  for (auto& L : h->layers) {
+    int rc = GM_OK;
+    if (L.kind == 1) {
+      if ((rc = redistribute(L.gu_q, (size_t)GU * H)) || (rc = redistribute(L.gu_scale, GU * sizeof(float))) ||
+          (rc = redistribute(L.dn_q, (size_t)H * I)) || (rc = redistribute(L.dn_scale, H * sizeof(float))))
+        return rc;
+      // the tcgen05 path's row-major copies (same buffers, so the TMA descriptors stay valid)
+      GM_TRY(h, launch_vnni_permute(L.gu_q, (long)epr * GU, H, L.gu_rm, 1, s), "vnni unpack");
+      GM_TRY(h, launch_vnni_permute(L.dn_q, (long)epr * H, I, L.dn_rm, 1, s), "vnni unpack");
+    } else if (L.kind == 2) {
+      if ((rc = redistribute(L.gu_bf16, (size_t)GU * H * 2)) || (rc = redistribute(L.dn_bf16, (size_t)H * I * 2)))
+        return rc;
+    }
+  }
+  GM_TRY(h, cudaMemcpyAsync(h->ep_rank_of, rank_of.data(), E * sizeof(int32_t), cudaMemcpyHostToDevice, s),
+         "placement tables");
+  GM_TRY(h, cudaMemcpyAsync(h->ep_local_of, local_of.data(), E * sizeof(int32_t), cudaMemcpyHostToDevice, s),
+         "placement tables");
+  GM_TRY(h, cudaStreamSynchronize(s), "placement tables");
+  h->ep_placed = true;
   return GM_OK;
 }
 

@@ -51,6 +51,7 @@ SIGNATURES = {
     "gm_moe_device_status": (_i32, [_vp, C.POINTER(_i32)]),
     "gm_ep_unique_id": (_i32, [_vp, _sz]),
     "gm_moe_ep_init": (_i32, [_vp, _vp, _i32]),
+    "gm_moe_ep_set_placement": (_i32, [_vp, C.POINTER(_i32)]),
     "gm_moe_profile_read": (_i32, [_vp, C.POINTER(StageStat), _i32, C.POINTER(_i32), C.POINTER(_i64)]),
     "gm_router_select": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "gm_router_select_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),
@@ -212,6 +213,11 @@ class MoeBlock:
         buf = C.create_string_buffer(bytes(unique_id), len(unique_id))
         check(lib().gm_moe_ep_init(self.h, buf, world), self.h)
 
+    def ep_set_placement(self, expert_rank):
+        """Collective: expert e moves to rank expert_rank[e] (128/world each)."""
+        arr = (C.c_int * NUM_EXPERTS)(*[int(r) for r in expert_rank])
+        check(lib().gm_moe_ep_set_placement(self.h, arr), self.h)
+
     def device_status(self):
         """Synchronises; raises GmoeError(GM_ETIMEOUT) if a bounded wait expired."""
         e = C.c_int(0)
@@ -223,6 +229,23 @@ OPT_TC_MIN_TOKENS = 1
 OPT_PROFILE = 2
 OPT_PDL = 3
 EP_UNIQUE_ID_BYTES = 128
+
+
+def balanced_placement(load, world):
+    """Expert -> rank map with 128/world experts per rank that evens out the
+    given per-expert load: experts in descending load, each to the least-loaded
+    rank that still has room (longest-processing-time first)."""
+    epr = NUM_EXPERTS // world
+    order = sorted(range(NUM_EXPERTS), key=lambda e: (-float(load[e]), e))
+    total = [0.0] * world
+    count = [0] * world
+    rank = [0] * NUM_EXPERTS
+    for e in order:
+        r = min((r for r in range(world) if count[r] < epr), key=lambda r: (total[r], r))
+        rank[e] = r
+        total[r] += float(load[e])
+        count[r] += 1
+    return rank
 
 
 def ep_unique_id():

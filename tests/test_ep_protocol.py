@@ -20,14 +20,38 @@ H, E, I, GU, TOPK = O.H, O.E, O.I, O.GU, O.TOPK
 WORLD, T_RANK = 2, 24
 
 
-def plan(idx, G, epr):
+def placement_tables(rank_of, G):
+    """local_of[e]: index of e among its rank's experts (ascending ids)."""
+    local_of = np.zeros(E, np.int32)
+    cnt = [0] * G
+    for e in range(E):
+        local_of[e] = cnt[rank_of[e]]
+        cnt[rank_of[e]] += 1
+    return local_of
+
+
+def plan(idx, G, epr, rank_of):
     """pos[t][d]: row of token t in destination d's block (token order) or -1."""
     T = idx.shape[0]
+    owner = rank_of[idx]
     mask = np.zeros((T, G), bool)
     for d in range(G):
-        mask[:, d] = ((idx // epr) == d).any(axis=1)
+        mask[:, d] = (owner == d).any(axis=1)
     pos = np.where(mask, np.cumsum(mask, axis=0) - 1, -1).astype(np.int32)
     return pos, mask.sum(axis=0)
+
+
+def rank_weights(ref, experts):
+    """This rank's experts' weights in local order (contiguous, as the handle
+    holds them after placement)."""
+    ex = np.asarray(experts)
+    gu_rows = (ex[:, None] * GU + np.arange(GU)[None, :]).reshape(-1)
+    dn_rows = (ex[:, None] * H + np.arange(H)[None, :]).reshape(-1)
+    nb = ref["dn_cs"].reshape(-1).size // (E * H)
+    return {"gu_q": ref["gu_q"][gu_rows], "gu_scale": ref["gu_scale"][gu_rows],
+            "gu_cs": ref["gu_cs"][gu_rows], "dn_q": ref["dn_q"][dn_rows],
+            "dn_scale": ref["dn_scale"][dn_rows],
+            "dn_cs": ref["dn_cs"].reshape(nb, E * H)[:, dn_rows].copy()}
 
 
 def a2a(t, world):
@@ -36,20 +60,18 @@ def a2a(t, world):
     return out
 
 
-def rank_partial(rx, rsa, ridx, rw, ref, rank, epr):
-    """This rank's experts over the received rows: bf16(sum over its experts)."""
+def rank_partial(rx, rsa, ridx, rw, W, rank, epr):
+    """This rank's experts (weights W in local order, ids rank*epr + local)
+    over the received rows: bf16(sum over its experts in local order)."""
     n = rx.shape[0]
     off, routes = O.build_schedules(ridx, rw, rank * epr, epr)
-    g0, d0 = rank * epr * GU, rank * epr * H
-    bucket = O.bq_phase1(rx, rsa, off, routes, ref["gu_q"][g0:], ref["gu_scale"][g0:],
-                         ref["gu_cs"][g0:], epr)
+    bucket = O.bq_phase1(rx, rsa, off, routes, W["gu_q"], W["gu_scale"], W["gu_cs"], epr)
     bi8, bsa = O.bq_block_quant(bucket)
-    dn_cs = ref["dn_cs"].reshape(-1)
-    return O.bq_phase2(bi8, bsa, off, routes, ref["dn_q"][d0:], ref["dn_scale"][d0:], dn_cs[d0:],
-                       E * H, epr, n)
+    return O.bq_phase2(bi8, bsa, off, routes, W["dn_q"], W["dn_scale"], W["dn_cs"].reshape(-1),
+                       epr * H, epr, n)
 
 
-def worker(rank, world, port, tmp):
+def worker(rank, world, port, tmp, placed):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -58,11 +80,15 @@ def worker(rank, world, port, tmp):
         ref = {k: z[k] for k in z.files}
     x = tokens_np(WORLD * T_RANK, seed=77)[rank * T_RANK:(rank + 1) * T_RANK]
     epr, cap = E // world, T_RANK
+    rank_of = np.load(os.path.join(tmp, "placement.npy")) if placed else np.arange(E) // epr
+    local_of = placement_tables(rank_of, world)
+    W = rank_weights(ref, [e for e in range(E) if rank_of[e] == rank])
     # 1. local prep and routing
     xi8, xsa = O.bq_norm_quant(x, ref["gamma2"])
     idx, w, _ = O.router(x, ref["router_centered"], ref["router_scale"], ref["pes"])
-    # 2. plan and pack blocks of `cap` rows per destination
-    pos, count = plan(idx, world, epr)
+    # 2. plan and pack blocks of `cap` rows per destination; ids sent to rank
+    #    d are rewritten to d*epr + local index (-1 for other ranks' experts)
+    pos, count = plan(idx, world, epr, rank_of)
     sx = np.zeros((world, cap, H), np.int8)
     ssa = np.zeros((world, cap), np.float32)
     sidx = np.full((world, cap, TOPK), -1, np.int32)
@@ -71,14 +97,15 @@ def worker(rank, world, port, tmp):
         for d in range(world):
             p = pos[t, d]
             if p >= 0:
-                sx[d, p], ssa[d, p], sidx[d, p], sw[d, p] = xi8[t], xsa[t], idx[t], w[t]
+                sx[d, p], ssa[d, p], sw[d, p] = xi8[t], xsa[t], w[t]
+                sidx[d, p] = np.where(rank_of[idx[t]] == d, d * epr + local_of[idx[t]], -1)
     # 3. dispatch
     rx = a2a(torch.from_numpy(sx), world).numpy().reshape(world * cap, H)
     rsa = a2a(torch.from_numpy(ssa), world).numpy().reshape(world * cap)
     ridx = a2a(torch.from_numpy(sidx), world).numpy().reshape(world * cap, TOPK)
     rw = a2a(torch.from_numpy(sw), world).numpy().reshape(world * cap, TOPK)
     # 4. experts, 5. combine exchange
-    part = rank_partial(rx, rsa, ridx, rw, ref, rank, epr)
+    part = rank_partial(rx, rsa, ridx, rw, W, rank, epr)
     # bf16 rows travel as int32 pairs (gloo has no 16-bit integer type)
     contrib = a2a(torch.from_numpy(np.ascontiguousarray(part).view(np.int32).reshape(world, cap, H // 2)),
                   world).numpy().view(np.uint16).reshape(world, cap, H)
@@ -102,11 +129,16 @@ def free_port():
         return s.getsockname()[1]
 
 
-def test_ep_protocol_matches_degree2_oracle(tmp_path):
+@pytest.fixture(scope="module")
+def layer_ref():
     raw = raw_layer_np(seed=4321, router_std=1.0, stress=True)
-    ref = oracle_bq_layer(raw)
+    return oracle_bq_layer(raw)
+
+
+def test_ep_protocol_matches_degree2_oracle(tmp_path, layer_ref):
+    ref = layer_ref
     np.savez(tmp_path / "layer.npz", **ref)
-    mp.spawn(worker, args=(WORLD, free_port(), str(tmp_path)), nprocs=WORLD, join=True)
+    mp.spawn(worker, args=(WORLD, free_port(), str(tmp_path), False), nprocs=WORLD, join=True)
     x = tokens_np(WORLD * T_RANK, seed=77)
     rout, _, _, _ = O.bq_forward(x, ref, degree=WORLD)
     got = np.concatenate([np.load(tmp_path / ("out%d.npy" % r)) for r in range(WORLD)])
@@ -114,3 +146,34 @@ def test_ep_protocol_matches_degree2_oracle(tmp_path):
     # every token reaches at least one rank, and some reach both
     counts = np.stack([np.load(tmp_path / ("count%d.npy" % r)) for r in range(WORLD)])
     assert counts.sum(axis=1).min() >= T_RANK and counts.max() <= T_RANK
+
+
+def test_ep_protocol_with_placement(tmp_path, layer_ref):
+    """A load-based placement (experts moved between ranks, 64 each): the
+    protocol equals each rank's partial over its placed experts (ascending
+    ids) summed in rank order, bit for bit, and stays within the bq tolerance
+    of the contiguous degree-2 result."""
+    import gmoe
+    from helpers import rel_err
+    ref = layer_ref
+    np.savez(tmp_path / "layer.npz", **ref)
+    load = np.arange(E, 0, -1).astype(float) ** 1.1     # a skewed load: expert 0 hottest
+    rank_of = np.array(gmoe.balanced_placement(load, WORLD), np.int32)
+    assert (np.bincount(rank_of, minlength=WORLD) == E // WORLD).all()
+    assert (rank_of != np.arange(E) // (E // WORLD)).any()
+    np.save(tmp_path / "placement.npy", rank_of)
+    mp.spawn(worker, args=(WORLD, free_port(), str(tmp_path), True), nprocs=WORLD, join=True)
+    got = np.concatenate([np.load(tmp_path / ("out%d.npy" % r)) for r in range(WORLD)])
+    x = tokens_np(WORLD * T_RANK, seed=77)
+    idx, w, _ = O.router(x, ref["router_centered"], ref["router_scale"], ref["pes"])
+    xi8, xsa = O.bq_norm_quant(x, ref["gamma2"])
+    epr = E // WORLD
+    local_of = placement_tables(rank_of, WORLD)
+    acc = np.zeros((x.shape[0], H), np.float32)
+    for r in range(WORLD):
+        Wr = rank_weights(ref, [e for e in range(E) if rank_of[e] == r])
+        ridx = np.where(rank_of[idx] == r, r * epr + local_of[idx], -1).astype(np.int32)
+        acc = acc + O.bf16_to_f32(rank_partial(xi8, xsa, ridx, w, Wr, r, epr))
+    assert np.array_equal(got, O.f32_to_bf16(acc))
+    rout, _, _, _ = O.bq_forward(x, ref, degree=WORLD)
+    assert rel_err(got, rout) < 3e-2

@@ -41,7 +41,7 @@ def register(blk, fmt, g, rank, degree):
                           g["router_scale"], g["per_expert_scale"], g["pre_ffn_norm_2"])
 
 
-def worker(rank, fmt, T, uid, tmp):
+def worker(rank, fmt, T, uid, tmp, placement=None):
     torch.cuda.set_device(rank)
     raw = raw_layer_np(seed=4321, router_std=1.0, stress=True)
     g = synth.bq_layer(raw_to_torch(raw)) if fmt == "bq" else synth.bf16_layer(raw_to_torch(raw))
@@ -50,11 +50,25 @@ def worker(rank, fmt, T, uid, tmp):
     ep = gmoe.MoeBlock(T, 1, device=rank, rank=rank, degree=WORLD)
     register(ep, fmt, g, rank, WORLD)
     ep.ep_init(uid, WORLD)
+    if placement is not None:
+        ep.ep_set_placement(placement)
     out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
     for _ in range(2):  # the second call reuses every buffer
         ep.forward(0, x_all[rank * T:(rank + 1) * T], out, T)
+    # the fused post-MoE tail on the expert-parallel path (rank-order sum,
+    # then the three norms and the residual on the same row)
+    rng = np.random.default_rng(7)
+    bf = lambda a: torch.from_numpy(O.f32_to_bf16(np.asarray(a, np.float32)).view(np.int16)).view(torch.bfloat16).cuda()
+    gains = [bf(1.0 + 0.2 * rng.standard_normal(H)) for _ in range(3)]
+    dense_all = bf(rng.standard_normal((WORLD * T, H)) * 2.0)
+    ep.register_post(0, gains[0], gains[1], gains[2], 0.75)
+    x_main = x_all[rank * T:(rank + 1) * T].clone()
+    ep.forward_ffn(0, x_main, dense_all[rank * T:(rank + 1) * T].contiguous(), T)
     torch.cuda.synchronize()
     assert ep.device_status() == 0
+    np.save(os.path.join(tmp, "ffn%d.npy" % rank), synth.to_numpy(x_main))
+    np.save(os.path.join(tmp, "dense.npy"), synth.to_numpy(dense_all))
+    np.save(os.path.join(tmp, "gains.npy"), np.stack([synth.to_numpy(g_) for g_ in gains]))
     # plain degree-2 handle: this rank's partial over all tokens
     part = gmoe.MoeBlock(WORLD * T, 1, device=rank, rank=rank, degree=WORLD)
     register(part, fmt, g, rank, WORLD)
@@ -77,6 +91,12 @@ def test_ep_forward_two_gpus(fmt, T, tmp_path):
     for p in parts:  # rank order, from +0.0, as the all-reduce of the reference
         acc = acc + O.bf16_to_f32(p)
     assert np.array_equal(got, O.f32_to_bf16(acc))
+    # fused post-MoE tail: the oracle's tail applied to the EP output
+    ffn = np.concatenate([np.load(tmp_path / ("ffn%d.npy" % r)) for r in range(WORLD)])
+    g3 = np.load(tmp_path / "gains.npy")
+    want = O.post_moe(got, np.load(tmp_path / "dense.npy"), tokens_np(WORLD * T, seed=500 + T),
+                      g3[0], g3[1], g3[2], 0.75)
+    assert rel_err(ffn, want) < 1e-2 and (ffn == want).mean() > 0.97
     # against the oracle's degree-2 forward, on tokens whose top-8 margin
     # guarantees the device picks the same experts
     raw = raw_layer_np(seed=4321, router_std=1.0, stress=True)
@@ -90,3 +110,34 @@ def test_ep_forward_two_gpus(fmt, T, tmp_path):
     checked = topk_margin(rlg) > MARGIN
     assert checked.mean() > 0.9
     assert rel_err(got, rout, rows=checked) < tol
+
+
+def test_ep_forward_two_gpus_with_placement(tmp_path):
+    """gm_moe_ep_set_placement: experts moved between the ranks (load-based);
+    the output equals each rank's bf16 partial over its placed experts summed
+    in rank order (the oracle's stages, on the tokens whose top-8 margin
+    guarantees the device routes like the oracle) within the bq tolerance."""
+    from test_ep_protocol import placement_tables, rank_weights, rank_partial
+    T = 200
+    load = np.arange(E, 0, -1).astype(float) ** 1.1
+    rank_of = np.array(gmoe.balanced_placement(load, WORLD), np.int32)
+    uid = gmoe.ep_unique_id()
+    mp.spawn(worker, args=("bq", T, uid, str(tmp_path), [int(r) for r in rank_of]), nprocs=WORLD,
+             join=True)
+    got = np.concatenate([np.load(tmp_path / ("ep%d.npy" % r)) for r in range(WORLD)])
+    raw = raw_layer_np(seed=4321, router_std=1.0, stress=True)
+    ref = oracle_bq_layer(raw)
+    x = tokens_np(WORLD * T, seed=500 + T)
+    idx, w, lg = O.router(x, ref["router_centered"], ref["router_scale"], ref["pes"])
+    xi8, xsa = O.bq_norm_quant(x, ref["gamma2"])
+    epr = E // WORLD
+    local_of = placement_tables(rank_of, WORLD)
+    acc = np.zeros((x.shape[0], H), np.float32)
+    for r in range(WORLD):
+        Wr = rank_weights(ref, [e for e in range(E) if rank_of[e] == r])
+        ridx = np.where(rank_of[idx] == r, r * epr + local_of[idx], -1).astype(np.int32)
+        acc = acc + O.bf16_to_f32(rank_partial(xi8, xsa, ridx, w, Wr, r, epr))
+    want = O.f32_to_bf16(acc)
+    checked = topk_margin(lg) > MARGIN
+    assert checked.mean() > 0.9
+    assert rel_err(got, want, rows=checked) < TOL_BQ
