@@ -135,10 +135,16 @@ int gm_moe_forward_ffn(gm_moe_t* h, int layer, void* x_main, const void* dense_o
  * value) clears the stage statistics and the kernel launch count.
  * GM_OPT_PDL: 1 (default) launches the forward's kernels with programmatic
  * dependent launch (each kernel's prologue overlaps its predecessor's tail);
- * 0 launches them with plain stream ordering. */
+ * 0 launches them with plain stream ordering.
+ * GM_OPT_EP_TRANSPORT (expert parallelism): 1 = the dispatch and combine
+ * exchanges are stores into the peers' memory (CUDA IPC mappings over
+ * NVLink) made by the pack and combine kernels themselves, ordered by flags;
+ * the default whenever every rank could map every peer at gm_moe_ep_init.
+ * 0 = NCCL send/recv.  Every rank must use the same value. */
 #define GM_OPT_TC_MIN_TOKENS 1
 #define GM_OPT_PROFILE 2
 #define GM_OPT_PDL 3
+#define GM_OPT_EP_TRANSPORT 4
 int gm_moe_set_option(gm_moe_t* h, int option, long value);
 
 /* Per-stage statistics of the handle's forwards.  Replaces the reference's

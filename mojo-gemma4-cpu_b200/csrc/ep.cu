@@ -248,6 +248,167 @@ cudaError_t launch_ep_final_post(const uint16_t* contrib, const int32_t* pos, in
   return launch_k(ep_final_post_kernel, dim3(T), dim3(POST_THREADS), 0, s, contrib, pos, T, G, cap, p);
 }
 
+// ------------------------------------------------- peer-memory exchange
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ep_global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Called by every thread of a CTA after its peer stores: the last CTA of the
+// grid (done_counter) publishes `epoch` into flag[d][my_rank] of every rank d.
+__device__ __forceinline__ void publish_when_last(int* done_counter, uint32_t* const* flags, int G,
+                                                  int my_rank, uint32_t epoch) {
+  __shared__ int s_last;
+  __threadfence_system();  // this thread's peer stores are visible system-wide
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(done_counter, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (s_last && threadIdx.x < G) {
+    __threadfence_system();
+    st_release_sys(flags[threadIdx.x] + my_rank, epoch);
+    if (threadIdx.x == 0) *done_counter = 0;  // re-armed for the next forward
+  }
+}
+
+__global__ void __launch_bounds__(256)
+ep_pack_p2p_kernel(const uint8_t* __restrict__ x_rows, int row_bytes, const float* __restrict__ x_sa,
+                   const int32_t* __restrict__ route_idx, const float* __restrict__ route_w, int T,
+                   int G, int cap, int epr, const int32_t* __restrict__ rank_of,
+                   const int32_t* __restrict__ local_of, const int32_t* __restrict__ pos,
+                   const int32_t* __restrict__ count, EpPeers peers, int my_rank, uint32_t epoch,
+                   int* __restrict__ done_counter) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const size_t src_row0 = (size_t)my_rank * cap;  // this source's block in every receiver
+  for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < T; t += warps) {
+    for (int d = 0; d < G; ++d) {
+      const int p = pos[(size_t)t * G + d];
+      if (p < 0) continue;
+      const size_t row = src_row0 + p;
+      const uint4* src = reinterpret_cast<const uint4*>(x_rows + (size_t)t * row_bytes);
+      uint4* dst = reinterpret_cast<uint4*>(peers.recv_x[d] + row * row_bytes);
+      for (int i = lane; i < row_bytes / 16; i += 32) dst[i] = src[i];
+      if (lane < TOPK) {
+        int e = route_idx[t * TOPK + lane];
+        if (rank_of && e >= 0 && e < E)
+          e = __ldg(rank_of + e) == d ? d * epr + __ldg(local_of + e) : -1;
+        peers.recv_idx[d][row * TOPK + lane] = e;
+        peers.recv_w[d][row * TOPK + lane] = route_w[t * TOPK + lane];
+      }
+      if (lane == 0 && x_sa) peers.recv_sa[d][row] = x_sa[t];
+    }
+  }
+  // rows beyond each destination's count route nowhere
+  const size_t n = (size_t)G * cap;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int d = (int)(i / cap), p = (int)(i % cap);
+    if (p >= count[d]) {
+#pragma unroll
+      for (int k = 0; k < TOPK; ++k) peers.recv_idx[d][(src_row0 + p) * TOPK + k] = -1;
+    }
+  }
+  publish_when_last(done_counter, peers.dflag, G, my_rank, epoch);
+}
+
+__global__ void ep_wait_kernel(const uint32_t* __restrict__ flags, int G, uint32_t epoch,
+                               int* __restrict__ err) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x >= G) return;
+  const uint64_t t0 = ep_global_ns();
+  uint32_t it = 0;
+  while ((int32_t)(ld_acquire_sys(flags + threadIdx.x) - epoch) < 0) {
+    if ((++it & 255) == 0 && ep_global_ns() - t0 > 1000000000ull) {
+      atomicExch(err, 3);  // a peer did not publish within ~1 s
+      return;
+    }
+  }
+  __threadfence_system();
+}
+
+__global__ void __launch_bounds__(352)
+combine_p2p_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict__ route_pos,
+                   const float* __restrict__ ybuf, int n, int cap, EpPeers peers, int G, int my_rank,
+                   uint32_t epoch, int* __restrict__ done_counter) {
+  __shared__ int s_pos[TOPK];
+  __shared__ int s_n;
+  pdl_wait();
+  pdl_trigger();
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+    if (threadIdx.x == 0) {
+      int ex[TOPK], ps[TOPK], m = 0;
+      for (int k = 0; k < TOPK; ++k) {
+        const int q = route_pos[(size_t)r * TOPK + k];
+        if (q < 0) continue;
+        const int e = route_idx[(size_t)r * TOPK + k];
+        int j = m++;
+        while (j > 0 && ex[j - 1] > e) { ex[j] = ex[j - 1]; ps[j] = ps[j - 1]; --j; }
+        ex[j] = e;
+        ps[j] = q;
+      }
+      for (int k = 0; k < m; ++k) s_pos[k] = ps[k];
+      s_n = m;
+    }
+    __syncthreads();
+    const int m = s_n;
+    if (m > 0) {  // rows with no route here were never sent (or are unused)
+      const int src = r / cap;
+      uint16_t* dst = peers.contrib[src] + ((size_t)my_rank * cap + (r % cap)) * H;
+      for (int c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int k = 0; k < m; ++k) {
+          const float4 y = *reinterpret_cast<const float4*>(ybuf + (size_t)s_pos[k] * H + c4 * 4);
+          acc.x = __fadd_rn(acc.x, y.x);
+          acc.y = __fadd_rn(acc.y, y.y);
+          acc.z = __fadd_rn(acc.z, y.z);
+          acc.w = __fadd_rn(acc.w, y.w);
+        }
+        uint2 o;
+        o.x = (uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16);
+        o.y = (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16);
+        *reinterpret_cast<uint2*>(dst + c4 * 4) = o;
+      }
+    }
+    __syncthreads();  // s_pos / s_n reused by the next row
+  }
+  publish_when_last(done_counter, peers.cflag, G, my_rank, epoch);
+}
+
+cudaError_t launch_ep_pack_p2p(const void* x_rows, int row_bytes, const float* x_sa,
+                               const int32_t* route_idx, const float* route_w, int T, int G, int cap,
+                               int epr, EpPlacement pl, const int32_t* pos, const int32_t* count,
+                               const EpPeers& peers, int my_rank, uint32_t epoch, int* done_counter,
+                               cudaStream_t s) {
+  const int blocks = std::max(1, std::min(1184, (std::max(T, G * cap) + 7) / 8));
+  return launch_k(ep_pack_p2p_kernel, dim3(blocks), dim3(256), 0, s,
+                  static_cast<const uint8_t*>(x_rows), row_bytes, x_sa, route_idx, route_w, T, G, cap,
+                  epr, pl.rank_of, pl.local_of, pos, count, peers, my_rank, epoch, done_counter);
+}
+
+cudaError_t launch_ep_wait(const uint32_t* flags, int G, uint32_t epoch, int* err, cudaStream_t s) {
+  return launch_k(ep_wait_kernel, dim3(1), dim3(32), 0, s, flags, G, epoch, err);
+}
+
+cudaError_t launch_combine_p2p(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
+                               int n, int cap, const EpPeers& peers, int G, int my_rank, uint32_t epoch,
+                               int* done_counter, cudaStream_t s) {
+  const int blocks = std::max(1, std::min(n, 148 * 8));
+  return launch_k(combine_p2p_kernel, dim3(blocks), dim3(352), 0, s, route_idx, route_pos, ybuf, n, cap,
+                  peers, G, my_rank, epoch, done_counter);
+}
+
 cudaError_t launch_ep_plan(const int32_t* route_idx, int T, int G, int epr, EpPlacement pl,
                            int32_t* pos, int32_t* count, cudaStream_t s) {
   return launch_k(ep_plan_kernel, dim3(1), dim3(1024), 0, s, route_idx, T, G, epr, pl.rank_of, pos,

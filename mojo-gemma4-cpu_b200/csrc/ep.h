@@ -51,4 +51,36 @@ cudaError_t launch_ep_final(const uint16_t* contrib, const int32_t* pos, int T, 
 cudaError_t launch_ep_final_post(const uint16_t* contrib, const int32_t* pos, int T, int G, int cap,
                                  const PostParams& p, cudaStream_t s);
 
+// Peer-memory exchange: the buffers of every rank (this rank's own at index
+// rank), mapped into this process by CUDA IPC, for the current forward's
+// parity.  dflag[r] / cflag[r] point at rank r's dispatch / combine flag
+// arrays (one slot per source rank).
+struct EpPeers {
+  uint8_t* recv_x[8];
+  float* recv_sa[8];
+  int32_t* recv_idx[8];
+  float* recv_w[8];
+  uint16_t* contrib[8];
+  uint32_t* dflag[8];
+  uint32_t* cflag[8];
+};
+
+// Pack with peer stores: rows go straight into rank d's receive block of this
+// source; the last CTA to finish (done_counter) publishes dflag[d][my_rank] =
+// epoch on every rank d (release, system scope).
+cudaError_t launch_ep_pack_p2p(const void* x_rows, int row_bytes, const float* x_sa,
+                               const int32_t* route_idx, const float* route_w, int T, int G, int cap,
+                               int epr, EpPlacement pl, const int32_t* pos, const int32_t* count,
+                               const EpPeers& peers, int my_rank, uint32_t epoch, int* done_counter,
+                               cudaStream_t s);
+// Waits (bounded, ~1 s) until flags[0..G) all reach epoch; on expiry writes 3
+// to *err and returns.
+cudaError_t launch_ep_wait(const uint32_t* flags, int G, uint32_t epoch, int* err, cudaStream_t s);
+// Combine with peer stores: received row r = (src, p) is summed over this
+// rank's experts (ascending id, from 0.0, bf16) and written into rank src's
+// contrib block of this rank; then cflag[src][my_rank] = epoch on every rank.
+cudaError_t launch_combine_p2p(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
+                               int n, int cap, const EpPeers& peers, int G, int my_rank, uint32_t epoch,
+                               int* done_counter, cudaStream_t s);
+
 }  // namespace gm

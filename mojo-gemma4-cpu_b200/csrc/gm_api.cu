@@ -116,6 +116,17 @@ struct gm_moe {
   int32_t* ep_rank_of = nullptr;   // [E] placement tables (device), used once placed
   int32_t* ep_local_of = nullptr;
   bool ep_placed = false;          // gm_moe_ep_set_placement done
+  // peer-memory exchange (GM_OPT_EP_TRANSPORT 1): receive and contrib regions
+  // in two parities, flags written by the peers, the exchange allocation of
+  // every rank mapped into this process, the forward counter
+  bool ep_p2p_ok = false;          // peers mapped
+  bool ep_use_p2p = false;         // transport chosen
+  EpPeers ep_peers[2];             // per parity
+  uint32_t* ep_dflag = nullptr;    // [8] this rank's dispatch flags (slot per source)
+  uint32_t* ep_cflag = nullptr;    // [8] combine flags
+  int* ep_counters = nullptr;      // [2] last-CTA counters of the pack and the combine
+  void* ep_peer_base[8] = {};      // IPC mappings (own base at this rank's index)
+  uint32_t ep_epoch = 0;
 };
 
 namespace {
@@ -375,7 +386,7 @@ struct StageScope {
 // x_i8/x_sa (butterquant) or x_normed (bf16), route_idx their top-8.
 int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, const float* x_sa,
                         const uint16_t* x_normed, const int32_t* route_idx, uint16_t* out,
-                        cudaStream_t s, const PostParams* post = nullptr) {
+                        cudaStream_t s, const PostParams* post = nullptr, bool skip_combine = false) {
   if (L.kind == 1) {
     if (L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
       // prefill: routed rows gathered in schedule order, then the tcgen05 GEMM
@@ -414,6 +425,7 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
                                       L.dn_bf16, h->ybuf, s),
              "phase2_down");
   }
+  if (skip_combine) return GM_OK;
   if (post)
     GM_STAGE(h, s, launch_combine_post(route_idx, h->route_pos, h->ybuf, Tn, *post, s), "combine.post");
   else
@@ -432,6 +444,53 @@ int nccl_check(gm_moe* h, ncclResult_t r, const char* what) {
     int _rc = nccl_check((h), (expr), (what));         \
     if (_rc != GM_OK) return _rc;                      \
   } while (0)
+
+// Expert-parallel forward, peer-memory transport (after routing and the plan):
+// the pack kernel stores rows into the receivers' buffers, the combine kernel
+// stores partial rows into the sources' buffers, and flags stamped with the
+// forward counter order the two sides (ep.cu).
+int ep_forward_p2p(gm_moe* h, const Layer& L, uint16_t* out, int T, cudaStream_t s,
+                   const PostParams* post, const EpPlacement& pl) {
+  const int G = h->degree, cap = h->max_tokens, n = G * cap;
+  const bool bq = L.kind == 1;
+  const int row_bytes = bq ? H : 2 * H;
+  const uint32_t epoch = ++h->ep_epoch;
+  const EpPeers& P = h->ep_peers[epoch & 1];
+  GM_STAGE(h, s, launch_ep_pack_p2p(bq ? static_cast<const void*>(h->x_i8) : static_cast<const void*>(h->x_normed),
+                                    row_bytes, bq ? h->x_sa : nullptr, h->route_idx, h->route_w, T, G, cap,
+                                    h->epr, pl, h->ep_pos, h->ep_count, P, h->rank, epoch,
+                                    h->ep_counters, s),
+           "ep_pack.p2p");
+  GM_STAGE(h, s, launch_ep_wait(h->ep_dflag, G, epoch, h->dev_err, s), "ep_dispatch.wait");
+  // this rank's experts over the rows every source stored here
+  const uint8_t* rx = P.recv_x[h->rank];
+  const int32_t* ridx = P.recv_idx[h->rank];
+  const int rc_chunk = bq ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
+  if (n <= 1024)
+    GM_STAGE(h, s, launch_build_schedule(ridx, P.recv_w[h->rank], n, h->expert_base, h->epr, rc_chunk,
+                                         h->expert_offset, h->routes, h->route_pos, h->chunk_off, s),
+             "ep_schedule");
+  else
+    GM_STAGE(h, s, launch_schedule_multi(ridx, P.recv_w[h->rank], n, h->expert_base, h->epr, rc_chunk,
+                                         h->sched_counts, h->expert_offset, h->routes, h->route_pos,
+                                         h->chunk_off, s),
+             "ep_schedule");
+  // expert products only; the combine below stores into the sources' buffers
+  int rc = experts_and_combine(h, L, n, reinterpret_cast<const int8_t*>(rx), P.recv_sa[h->rank],
+                               reinterpret_cast<const uint16_t*>(rx), ridx, nullptr, s, nullptr,
+                               /*skip_combine=*/true);
+  if (rc) return rc;
+  GM_STAGE(h, s, launch_combine_p2p(ridx, h->route_pos, h->ybuf, n, cap, P, G, h->rank, epoch,
+                                    h->ep_counters + 1, s),
+           "combine.p2p");
+  GM_STAGE(h, s, launch_ep_wait(h->ep_cflag, G, epoch, h->dev_err, s), "ep_combine.wait");
+  const uint16_t* contrib = P.contrib[h->rank];
+  if (post)
+    GM_STAGE(h, s, launch_ep_final_post(contrib, h->ep_pos, T, G, cap, *post, s), "ep_final.post");
+  else
+    GM_STAGE(h, s, launch_ep_final(contrib, h->ep_pos, T, G, cap, out, s), "ep_final");
+  return GM_OK;
+}
 
 // Expert-parallel forward (after gm_moe_ep_init): this rank's T tokens in,
 // their full MoE output out; see ep.cu for the exchange.
@@ -458,6 +517,7 @@ int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int
     pl.local_of = h->ep_local_of;
   }
   GM_STAGE(h, s, launch_ep_plan(h->route_idx, T, G, h->epr, pl, h->ep_pos, h->ep_count, s), "ep_plan");
+  if (h->ep_use_p2p) return ep_forward_p2p(h, L, out, T, s, post, pl);
   GM_STAGE(h, s, launch_ep_pack(bq ? static_cast<const void*>(h->x_i8) : static_cast<const void*>(h->x_normed),
                                 row_bytes, bq ? h->x_sa : nullptr, h->route_idx, h->route_w, T, G, cap,
                                 h->epr, pl, h->ep_pos, h->ep_count, h->ep_send_x, h->ep_send_sa,
@@ -586,6 +646,8 @@ int gm_moe_destroy(gm_moe_t* h) {
   for (cudaEvent_t e : h->event_pool) cudaEventDestroy(e);
   if (h->ep_comm) {
     cudaDeviceSynchronize();
+    for (int q = 0; q < 8; ++q)
+      if (h->ep_peer_base[q] && q != h->rank) cudaIpcCloseMemHandle(h->ep_peer_base[q]);
     if (const NcclApi* nc = nccl_api(nullptr)) nc->comm_destroy(h->ep_comm);
   }
   if (h->ep_buf) cudaFree(h->ep_buf);
@@ -751,6 +813,12 @@ int gm_moe_set_option(gm_moe_t* h, int option, long value) {
       if (value < 1) return set_err(h, GM_EINVAL, "GM_OPT_TC_MIN_TOKENS must be >= 1");
       h->tc_min_tokens = value > 0x7FFFFFFF ? 0x7FFFFFFF : (int)value;
       return GM_OK;
+    case GM_OPT_EP_TRANSPORT:
+      if (value != 0 && value != 1) return set_err(h, GM_EINVAL, "GM_OPT_EP_TRANSPORT must be 0 or 1");
+      if (value == 1 && !h->ep_p2p_ok)
+        return set_err(h, GM_ESTATE, "peer-memory transport unavailable (not initialised or not mapped)");
+      h->ep_use_p2p = value == 1;
+      return GM_OK;
     case GM_OPT_PDL:
       if (value != 0 && value != 1) return set_err(h, GM_EINVAL, "GM_OPT_PDL must be 0 or 1");
       h->pdl = value != 0;
@@ -820,6 +888,11 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
                o_ridx = c.take<int32_t>(n * TOPK), o_rw = c.take<float>(n * TOPK);
   const size_t o_part = c.take<uint16_t>(n * H), o_con = c.take<uint16_t>(n * H);
   const size_t o_rank = c.take<int32_t>(E), o_local = c.take<int32_t>(E);
+  // second parity of the regions peers write (peer-memory transport)
+  const size_t o_rx1 = c.take<uint8_t>(n * 2 * H), o_rsa1 = c.take<float>(n),
+               o_ridx1 = c.take<int32_t>(n * TOPK), o_rw1 = c.take<float>(n * TOPK),
+               o_con1 = c.take<uint16_t>(n * H);
+  const size_t o_dflag = c.take<uint32_t>(8), o_cflag = c.take<uint32_t>(8), o_ctr = c.take<int>(2);
   GM_TRY(h, cudaMalloc(&h->ep_buf, align_up(c.off, 256)), "ep buffers");
   char* b = static_cast<char*>(h->ep_buf);
   h->ep_pos = reinterpret_cast<int32_t*>(b + o_pos);
@@ -836,6 +909,9 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
   h->ep_contrib = reinterpret_cast<uint16_t*>(b + o_con);
   h->ep_rank_of = reinterpret_cast<int32_t*>(b + o_rank);
   h->ep_local_of = reinterpret_cast<int32_t*>(b + o_local);
+  h->ep_dflag = reinterpret_cast<uint32_t*>(b + o_dflag);
+  h->ep_cflag = reinterpret_cast<uint32_t*>(b + o_cflag);
+  h->ep_counters = reinterpret_cast<int*>(b + o_ctr);
   GM_TRY(h, cudaMemset(h->ep_buf, 0, align_up(c.off, 256)), "ep buffers");
   ncclUniqueId id;
   memcpy(&id, unique_id, sizeof id);
@@ -843,6 +919,69 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
   const ncclResult_t r = nc->comm_init_rank(&comm, world, id, h->rank);
   if (r != ncclSuccess) return set_err(h, GM_ENCCL, "ncclCommInitRank: %s", nc->get_error_string(r));
   h->ep_comm = comm;
+  // Peer-memory transport: map every rank's exchange allocation (the carve
+  // offsets are the same on every rank: same max_tokens and world).
+  bool ok = true;
+  cudaIpcMemHandle_t mine_h;
+  if (cudaIpcGetMemHandle(&mine_h, h->ep_buf) != cudaSuccess) ok = false;
+  std::vector<cudaIpcMemHandle_t> all(world);
+  void* dev_h = nullptr;
+  if (ok && cudaMalloc(&dev_h, sizeof(cudaIpcMemHandle_t) * (world + 1)) != cudaSuccess) ok = false;
+  // every rank takes part in the all-gather (a rank that failed sends zeros)
+  if (dev_h) {
+    cudaMemcpy(dev_h, &mine_h, sizeof mine_h, cudaMemcpyHostToDevice);
+    char* dh = static_cast<char*>(dev_h);
+    ncclResult_t gr = nc->all_gather(dh, dh + sizeof(cudaIpcMemHandle_t), sizeof(cudaIpcMemHandle_t),
+                                     ncclUint8, comm, h->own_stream);
+    if (gr != ncclSuccess || cudaStreamSynchronize(h->own_stream) != cudaSuccess) ok = false;
+    if (ok) cudaMemcpy(all.data(), dh + sizeof(cudaIpcMemHandle_t), sizeof(cudaIpcMemHandle_t) * world,
+                       cudaMemcpyDeviceToHost);
+    cudaFree(dev_h);
+  }
+  for (int q = 0; ok && q < world; ++q) {
+    if (q == h->rank) {
+      h->ep_peer_base[q] = h->ep_buf;
+    } else if (cudaIpcOpenMemHandle(&h->ep_peer_base[q], all[q], cudaIpcMemLazyEnablePeerAccess) !=
+               cudaSuccess) {
+      h->ep_peer_base[q] = nullptr;
+      ok = false;
+    }
+  }
+  cudaGetLastError();
+  if (ok) {
+    const size_t rx[2] = {o_rx, o_rx1}, rsa[2] = {o_rsa, o_rsa1}, ridx[2] = {o_ridx, o_ridx1},
+                 rw[2] = {o_rw, o_rw1}, con[2] = {o_con, o_con1};
+    for (int par = 0; par < 2; ++par)
+      for (int q = 0; q < world; ++q) {
+        char* pb = static_cast<char*>(h->ep_peer_base[q]);
+        EpPeers& P = h->ep_peers[par];
+        P.recv_x[q] = reinterpret_cast<uint8_t*>(pb + rx[par]);
+        P.recv_sa[q] = reinterpret_cast<float*>(pb + rsa[par]);
+        P.recv_idx[q] = reinterpret_cast<int32_t*>(pb + ridx[par]);
+        P.recv_w[q] = reinterpret_cast<float*>(pb + rw[par]);
+        P.contrib[q] = reinterpret_cast<uint16_t*>(pb + con[par]);
+        P.dflag[q] = reinterpret_cast<uint32_t*>(pb + o_dflag);
+        P.cflag[q] = reinterpret_cast<uint32_t*>(pb + o_cflag);
+      }
+  }
+  // every rank must choose the same transport: agree on "all ranks mapped"
+  int* dflag_ok = nullptr;
+  bool all_ok = false;
+  if (cudaMalloc(&dflag_ok, sizeof(int) * (world + 1)) == cudaSuccess) {
+    const int v = ok ? 1 : 0;
+    cudaMemcpy(dflag_ok, &v, sizeof v, cudaMemcpyHostToDevice);
+    if (nc->all_gather(dflag_ok, dflag_ok + 1, 1, ncclInt32, comm, h->own_stream) == ncclSuccess &&
+        cudaStreamSynchronize(h->own_stream) == cudaSuccess) {
+      std::vector<int> v_all(world);
+      cudaMemcpy(v_all.data(), dflag_ok + 1, sizeof(int) * world, cudaMemcpyDeviceToHost);
+      all_ok = true;
+      for (int x : v_all) all_ok = all_ok && x == 1;
+    }
+    cudaFree(dflag_ok);
+  }
+  cudaGetLastError();
+  h->ep_p2p_ok = all_ok;
+  h->ep_use_p2p = all_ok;
   return GM_OK;
 }
 

@@ -228,6 +228,7 @@ class MoeBlock:
 OPT_TC_MIN_TOKENS = 1
 OPT_PROFILE = 2
 OPT_PDL = 3
+OPT_EP_TRANSPORT = 4
 EP_UNIQUE_ID_BYTES = 128
 
 

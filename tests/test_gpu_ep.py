@@ -53,8 +53,20 @@ def worker(rank, fmt, T, uid, tmp, placement=None):
     if placement is not None:
         ep.ep_set_placement(placement)
     out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
-    for _ in range(2):  # the second call reuses every buffer
-        ep.forward(0, x_all[rank * T:(rank + 1) * T], out, T)
+    x_loc = x_all[rank * T:(rank + 1) * T]
+    ep.profile(True)
+    for _ in range(3):  # later calls reuse every buffer (both parities)
+        ep.forward(0, x_loc, out, T)
+    stats, _ = ep.profile_read()
+    ep.profile(False)
+    assert "ep_pack.p2p" in stats, sorted(stats)  # peer-memory transport by default
+    # the NCCL transport computes the same result bit for bit
+    out_nccl = torch.empty_like(out)
+    ep.set_option(gmoe.OPT_EP_TRANSPORT, 0)
+    ep.forward(0, x_loc, out_nccl, T)
+    ep.set_option(gmoe.OPT_EP_TRANSPORT, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out_nccl)
     # the fused post-MoE tail on the expert-parallel path (rank-order sum,
     # then the three norms and the residual on the same row)
     rng = np.random.default_rng(7)
