@@ -125,6 +125,68 @@ int gm_moe_register_post(gm_moe_t* h, int layer, const void* post_ffn_norm_1,
 int gm_moe_forward_ffn(gm_moe_t* h, int layer, void* x_main, const void* dense_out, int T,
                        void* stream);
 
+/* ------------------------------------------------------------ checkpoints --
+ * Safetensors checkpoints as the reference reads and writes them
+ * (safetensors/parser.mojo, safetensors/writer.mojo:39-75): an 8-byte
+ * little-endian header length, a JSON header {name: {dtype, shape,
+ * data_offsets}} ("__metadata__" ignored), then the data.  `path` is one file
+ * or a directory whose *.safetensors shards are merged (the reference's
+ * source checkpoints are sharded; its butterquant output is one
+ * model.safetensors, quant/quantizer.mojo:383-446).  Opening parses and
+ * checks every header (offsets inside the file, byte counts equal to the
+ * shapes); tensors are read on demand.  These calls need no GPU; failures
+ * leave their text in gm_last_error(NULL). */
+typedef struct gm_checkpoint gm_checkpoint_t;
+
+#define GM_DTYPE_BOOL 1
+#define GM_DTYPE_U8 2
+#define GM_DTYPE_I8 3
+#define GM_DTYPE_I16 4
+#define GM_DTYPE_U16 5
+#define GM_DTYPE_F16 6
+#define GM_DTYPE_BF16 7
+#define GM_DTYPE_I32 8
+#define GM_DTYPE_U32 9
+#define GM_DTYPE_F32 10
+#define GM_DTYPE_I64 11
+#define GM_DTYPE_U64 12
+#define GM_DTYPE_F64 13
+#define GM_DTYPE_F8_E4M3 14
+#define GM_DTYPE_F8_E5M2 15
+#define GM_CKPT_MAX_DIMS 8
+
+int gm_checkpoint_open(gm_checkpoint_t** out, const char* path);
+int gm_checkpoint_close(gm_checkpoint_t* ck);
+/* Tensors in name order: count, and the name at `index` (NULL if out of range). */
+int gm_checkpoint_tensor_count(const gm_checkpoint_t* ck);
+const char* gm_checkpoint_tensor_name(const gm_checkpoint_t* ck, int index);
+/* dtype (GM_DTYPE_*), rank and shape[GM_CKPT_MAX_DIMS] of a tensor. */
+int gm_checkpoint_tensor_info(const gm_checkpoint_t* ck, const char* name, int* dtype, int* ndim,
+                              int64_t* shape);
+/* Rows [row0, row0+nrows) of a tensor seen as 2-D (all leading dimensions
+ * folded into rows, quant/quantizer.mojo:62-71; a 1-D tensor is a column),
+ * into host memory dst of dst_bytes. */
+int gm_checkpoint_read_rows(const gm_checkpoint_t* ck, const char* name, int64_t row0,
+                            int64_t nrows, void* dst, size_t dst_bytes);
+
+/* One MoE layer from a checkpoint into the handle: replaces the reference's
+ * weight load (modeling/loader.mojo:95-150, this rank's row block of the
+ * expert tensors) plus its load-time transforms (VNNI packing,
+ * modeling/slot.mojo:263-300; router scale bake,
+ * modeling/gemma4_topology.mojo:362-388; split-gain bake of
+ * pre_feedforward_layernorm_2, modeling/gemma_4_moe_bq.mojo:905-910), then
+ * registers the layer as gm_moe_register_layer_bq / _bf16 would.  The format
+ * follows the dtype of experts.gate_up_proj: I8 is the butterquant file
+ * (members ".scale", quant/manifest.mojo:10-13,93-120), BF16 the original
+ * checkpoint ([128][1408][2816] or folded).  Tensor names are `prefix` +
+ * modeling/gemma4_topology.mojo:143-158 names; prefix NULL means
+ * "model.language_model.layers.%d." with %d = ckpt_layer.  With
+ * GM_LOAD_POST the post-MoE gains and layer_scalar are registered too
+ * (gm_moe_register_post).  Synchronous. */
+#define GM_LOAD_POST 1
+int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* ck, int ckpt_layer,
+                      const char* prefix, int flags);
+
 /* Options (no reference counterpart: the reference picks its kernels at
  * compile time).  GM_OPT_TC_MIN_TOKENS: calls with T >= value run the
  * butterquant gate/up product on the tcgen05 grouped GEMM (prefill path),

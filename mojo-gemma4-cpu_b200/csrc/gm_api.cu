@@ -580,6 +580,17 @@ int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int
 
 namespace gm {
 void set_thread_error(const char* msg) { g_tls_error = msg; }
+
+int handle_shard(const gm_moe* h, int* device, int* expert_base, int* epr, int* num_layers) {
+  if (!h) return set_err(nullptr, GM_EINVAL, "NULL handle");
+  *device = h->device;
+  *expert_base = h->expert_base;
+  *epr = h->epr;
+  *num_layers = h->num_layers;
+  return GM_OK;
+}
+
+int handle_fail(gm_moe* h, int code, const char* msg) { return set_err(h, code, "%s", msg); }
 }  // namespace gm
 
 extern "C" {

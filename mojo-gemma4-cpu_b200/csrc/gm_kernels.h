@@ -4,6 +4,8 @@
 #include <algorithm>
 #include "gm_common.cuh"
 
+struct gm_moe;
+
 namespace gm {
 
 // Kernels launched through launch_k by the calling host thread (the handle
@@ -35,6 +37,10 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
 
 // Records the text returned by gm_last_error(NULL) on the calling thread.
 void set_thread_error(const char* msg);
+// Shard of a handle (device, first expert held, experts held, layers) and a
+// failure recorded on it, for code outside gm_api.cu (the checkpoint loader).
+int handle_shard(const ::gm_moe* h, int* device, int* expert_base, int* epr, int* num_layers);
+int handle_fail(::gm_moe* h, int code, const char* msg);
 
 int max_route_chunks(int T, int epr, int rc);
 // The router writes ROUTER_SLICES split-K partial logit slices [slice][T][E];

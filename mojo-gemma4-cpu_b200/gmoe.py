@@ -70,6 +70,14 @@ SIGNATURES = {
     "gm_router_center": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "gm_bake_split_gain": (_i32, [_vp, _vp, _i32, _vp]),
     "gm_bake_router_scale": (_i32, [_vp, _vp, _i32, _vp]),
+    "gm_checkpoint_open": (_i32, [C.POINTER(_vp), C.c_char_p]),
+    "gm_checkpoint_close": (_i32, [_vp]),
+    "gm_checkpoint_tensor_count": (_i32, [_vp]),
+    "gm_checkpoint_tensor_name": (C.c_char_p, [_vp, _i32]),
+    "gm_checkpoint_tensor_info": (_i32, [_vp, C.c_char_p, C.POINTER(_i32), C.POINTER(_i32),
+                                         C.POINTER(C.c_int64)]),
+    "gm_checkpoint_read_rows": (_i32, [_vp, C.c_char_p, C.c_int64, C.c_int64, _vp, _sz]),
+    "gm_moe_load_layer": (_i32, [_vp, _i32, _vp, _i32, C.c_char_p, _i32]),
 }
 
 
@@ -223,6 +231,69 @@ class MoeBlock:
         e = C.c_int(0)
         check(lib().gm_moe_device_status(self.h, C.byref(e)), self.h)
         return e.value
+
+    def load_layer(self, layer, ckpt, ckpt_layer=None, prefix=None, post=False):
+        """One MoE layer from a Checkpoint (this handle's experts, load-time
+        bakes and packing included); the format follows the file's
+        experts.gate_up_proj dtype.  prefix None: the reference's
+        "model.language_model.layers.%d." with %d = ckpt_layer (default: layer)."""
+        if ckpt_layer is None:
+            ckpt_layer = layer
+        check(lib().gm_moe_load_layer(self.h, layer, ckpt.h, ckpt_layer,
+                                      prefix.encode() if prefix is not None else None,
+                                      LOAD_POST if post else 0), self.h)
+
+
+DTYPES = {1: "BOOL", 2: "U8", 3: "I8", 4: "I16", 5: "U16", 6: "F16", 7: "BF16", 8: "I32", 9: "U32",
+          10: "F32", 11: "I64", 12: "U64", 13: "F64", 14: "F8_E4M3", 15: "F8_E5M2"}
+LOAD_POST = 1
+CKPT_MAX_DIMS = 8
+
+
+class Checkpoint:
+    """A gm_checkpoint_t: one .safetensors file or a directory of shards,
+    headers parsed and checked at open, tensors read on demand (no GPU)."""
+
+    def __init__(self, path):
+        h = C.c_void_p()
+        check(lib().gm_checkpoint_open(C.byref(h), os.fsencode(path)))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            lib().gm_checkpoint_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def names(self):
+        L = lib()
+        return [L.gm_checkpoint_tensor_name(self.h, i).decode()
+                for i in range(L.gm_checkpoint_tensor_count(self.h))]
+
+    def info(self, name):
+        """(dtype tag, shape tuple)."""
+        dt, nd = C.c_int(0), C.c_int(0)
+        shape = (C.c_int64 * CKPT_MAX_DIMS)()
+        check(lib().gm_checkpoint_tensor_info(self.h, name.encode(), C.byref(dt), C.byref(nd), shape))
+        return DTYPES[dt.value], tuple(shape[:nd.value])
+
+    def read_rows(self, name, row0, nrows, out):
+        """Rows [row0, row0+nrows) of the tensor folded to 2-D into `out`
+        (a writable host buffer: numpy array or address with its size)."""
+        nbytes = out.nbytes if hasattr(out, "nbytes") else out.numel() * out.element_size()
+        check(lib().gm_checkpoint_read_rows(self.h, name.encode(), row0, nrows, _addr(out), nbytes))
+        return out
 
 
 OPT_TC_MIN_TOKENS = 1

@@ -92,3 +92,35 @@ def rel_err(out_u16, ref_u16, rows=None):
     if r.size == 0:
         return 0.0
     return float(np.abs(o - r).max() / max(np.abs(r).max(), 1e-30))
+
+
+NP_TAG = {np.dtype(np.int8): "I8", np.dtype(np.uint8): "U8", np.dtype(np.float32): "F32",
+          np.dtype(np.int32): "I32", np.dtype(np.int64): "I64", np.dtype(np.float64): "F64",
+          np.dtype(np.int16): "I16"}
+
+
+def write_safetensors(path, entries):
+    """A safetensors file laid out as the reference's writer makes it
+    (safetensors/writer.mojo:39-75, entries in plan order with tightly packed
+    data, quant/quantizer.mojo:674-683): 8-byte little-endian header length,
+    the JSON header padded with spaces to a multiple of 8, then the data.
+    entries: list of (name, array, tag or None, shape or None); uint16 arrays
+    are bf16 bit patterns unless a tag says otherwise."""
+    import json
+    head, blobs, off = {}, [], 0
+    for name, arr, tag, shape in entries:
+        a = np.ascontiguousarray(arr)
+        tag = tag or ("BF16" if a.dtype == np.uint16 else NP_TAG[a.dtype])
+        shape = list(a.shape if shape is None else shape)
+        b = a.tobytes()
+        head[name] = {"dtype": tag, "shape": shape, "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    js = json.dumps(head, separators=(",", ":")).encode()
+    js += b" " * (-len(js) % 8)
+    with open(path, "wb") as f:
+        f.write(len(js).to_bytes(8, "little"))
+        f.write(js)
+        for b in blobs:
+            f.write(b)
+    return path
