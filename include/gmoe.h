@@ -125,6 +125,28 @@ int gm_moe_register_post(gm_moe_t* h, int layer, const void* post_ffn_norm_1,
 int gm_moe_forward_ffn(gm_moe_t* h, int layer, void* x_main, const void* dense_out, int T,
                        void* stream);
 
+/* The dense butterquant MLP of the same FFN (dispatch_bq_ffn,
+ * modeling/gemma_4_moe_bq.mojo:749-783), weights replicated on every handle
+ * (17.8 MB per layer; tokens stay on their GPU):
+ *   gate_proj, up_proj  int8 VNNI-packed [2112][2816], FWHT-128 rotated,
+ *                       split gain of pre_feedforward_layernorm folded in
+ *                       (SplitGainPerRowCs, modeling/gemma_4_moe_bq.mojo:113-114)
+ *   gate_scale, up_scale f32 [2112]
+ *   down_proj           int8 VNNI-packed [2816][2112], FWHT-64 rotated
+ *                       (PlainPerRowBlockCs[64]), down_scale f32 [2816]
+ *   pre_ffn_norm        bf16 [2816], split-gain baked
+ * gm_dense_forward: x [T][2816] -> dense_out [T][2816] (device, async): the
+ * reference's dispatch_bq_norm_quant, two dispatch_bq_linear,
+ * dispatch_gelu_gate_up, dispatch_bq_block_quant and dispatch_bq_block_linear.
+ * gm_ffn_forward: the whole FFN on x_main in place -- the dense MLP on a
+ * forked stream beside the MoE, then the MoE's combine with the post-MoE tail
+ * (needs gm_moe_register_post; at degree > 1 only with expert parallelism). */
+int gm_moe_register_dense_bq(gm_moe_t* h, int layer, const void* gate_proj, const float* gate_scale,
+                             const void* up_proj, const float* up_scale, const void* down_proj,
+                             const float* down_scale, const void* pre_ffn_norm);
+int gm_dense_forward(gm_moe_t* h, int layer, const void* x, void* dense_out, int T, void* stream);
+int gm_ffn_forward(gm_moe_t* h, int layer, void* x_main, int T, void* stream);
+
 /* ------------------------------------------------------------ checkpoints --
  * Safetensors checkpoints as the reference reads and writes them
  * (safetensors/parser.mojo, safetensors/writer.mojo:39-75): an 8-byte
@@ -202,11 +224,15 @@ int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* ck, int ckp
  * exchanges are stores into the peers' memory (CUDA IPC mappings over
  * NVLink) made by the pack and combine kernels themselves, ordered by flags;
  * the default whenever every rank could map every peer at gm_moe_ep_init.
- * 0 = NCCL send/recv.  Every rank must use the same value. */
+ * 0 = NCCL send/recv.  Every rank must use the same value.
+ * GM_OPT_DENSE_TC_MIN_TOKENS: calls with T >= value run the dense MLP's
+ * products on tcgen05 GEMMs, smaller calls on its HBM-streaming kernels;
+ * both give bit-identical results.  Default 128. */
 #define GM_OPT_TC_MIN_TOKENS 1
 #define GM_OPT_PROFILE 2
 #define GM_OPT_PDL 3
 #define GM_OPT_EP_TRANSPORT 4
+#define GM_OPT_DENSE_TC_MIN_TOKENS 5
 int gm_moe_set_option(gm_moe_t* h, int option, long value);
 
 /* Per-stage statistics of the handle's forwards.  Replaces the reference's
@@ -369,9 +395,24 @@ int gm_combine(const int32_t* route_idx, const int32_t* route_pos, const float* 
  * 963-1051 do_quant with butterquant/kernels.mojo:148-168 rotate_and_quant),
  * bit-identical to it: w bf16 [rows][cols] (* sqrt|gamma| if gamma != NULL),
  * FWHT-`fwht_block` along K, per-row absmax int8 q [rows][cols] row-major,
- * scale f32 [rows] = amax/127.  cols/block: 2816/128 or 704/64. */
+ * scale f32 [rows] = amax/127.  cols/block: 2816/128, 2816/64, 704/64 or
+ * 2112/64 (the dense MLP's down_proj). */
 int gm_bq_quantize_rows(const void* w, long rows, int cols, const void* gamma, int fwht_block,
                         int8_t* q, float* scale, void* stream);
+
+/* Stages of the dense MLP on explicit buffers.  gm_bq_dense_gate_up:
+ * dispatch_bq_linear on gate_proj and up_proj (butterquant_kernels/linear.mojo:
+ * 85-130), dispatch_gelu_gate_up (kernels/elementwise.mojo:17-60) and
+ * dispatch_bq_block_quant[64, fwht] (linear.mojo:159-205) in one pass:
+ * x_i8 [T][2816], x_sa [T] -> h_i8 [T][2112], h_sa [T][33] (h_bf16
+ * [T][2112], the GeGLU output, also written when non-NULL).
+ * gm_bq_block_linear: dispatch_bq_block_linear (linear.mojo:208-270) with
+ * n_rows 2816, k_dim 2112: h_i8, h_sa -> out bf16 [T][2816]. */
+int gm_bq_dense_gate_up(const int8_t* x_i8, const float* x_sa, int T, const void* gate_proj,
+                        const float* gate_scale, const void* up_proj, const float* up_scale,
+                        int8_t* h_i8, float* h_sa, void* h_bf16, void* stream);
+int gm_bq_block_linear(const int8_t* h_i8, const float* h_sa, int T, const void* down_proj,
+                       const float* down_scale, void* out, void* stream);
 
 /* butterquant/vnni.mojo:31-83 pack (and its inverse). rows%32 == 0, cols%64 == 0. */
 int gm_vnni_pack(const int8_t* q, long rows, int cols, int8_t* packed, void* stream);

@@ -33,25 +33,14 @@
 // Phase 2 writes per-route f32 rows y = facc*sw*w; combine.cu sums them per
 // token in ascending expert order (the reference's accumulation order).
 #include "gm_kernels.h"
+#include "vnni_stream.cuh"
 
 namespace gm {
 
 constexpr int RC_BQ = 16;                 // routes per work item
 constexpr int XSTRIDE = H + 16;           // staged activation row (bytes)
 constexpr int BSTRIDE = I + 16;           // staged bucket row (bytes)
-constexpr float INV127 = 1.0f / 127.0f;   // f32(1)/f32(127)
 constexpr int DSTRIDE = 33;               // padded row stride of the phase-1 dot tile
-
-// Byte offset of lane (g,q)'s first 16-byte load inside a 2048-byte K-step
-// tile, for K chunk cc (0/1) of that step.  The second load is +256 bytes.
-__device__ __forceinline__ int vnni_lane_off(int g, int q, int cc) {
-  return (g >> 2) * 1024 + (8 * cc + q) * 64 + (g & 3) * 16;
-}
-
-// Row (0..31) inside the N-tile of accumulator element i of MMA m for lane g.
-__device__ __forceinline__ int acc_row(int g, int m, int i) {
-  return 16 * (g >> 2) + 4 * (g & 3) + 2 * m + (i >> 1);
-}
 
 struct Task {
   int e, rbeg, nr, blk;
@@ -75,18 +64,6 @@ __device__ __forceinline__ bool decode_task(int task, int total, int per_chunk,
 __device__ __forceinline__ const int8_t* p1_tile(const int8_t* w_gu, const Task& t, int nt) {
   const int tile = (nt < 2) ? (2 * t.blk + nt) : (I / 32 + 2 * t.blk + (nt - 2));
   return w_gu + (size_t)t.e * GU * H + (size_t)tile * 32 * H;
-}
-
-template <int DEPTH>
-__device__ __forceinline__ void prefetch_chunks(uint4 (&buf)[DEPTH][2], const int8_t* wt, int c0,
-                                                int g, int q) {
-#pragma unroll
-  for (int d = 0; d < DEPTH; ++d) {
-    const int gc = c0 + d;
-    const int8_t* p = wt + (gc >> 1) * 2048 + vnni_lane_off(g, q, gc & 1);
-    buf[d][0] = ldg_stream(p);
-    buf[d][1] = ldg_stream(p + 256);
-  }
 }
 
 template <int KSPLIT, int DEPTH, bool WRITE_BF16>

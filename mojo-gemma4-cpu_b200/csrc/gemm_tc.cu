@@ -98,13 +98,20 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t da, uint64_t db
       : "memory");
 }
 
+// DENSE: the dense MLP's gate/up product (dense_bq.cu's mathematics, gate and
+// up rounded to bf16 before GeGLU) over dense_rows token rows in order, as one
+// "expert" with 2112 intermediate columns: B rows [0, 2112) gate, [2112, 4224) up.
+template <bool DENSE>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                 const int32_t* __restrict__ expert_offset, int epr,
+                 const int32_t* __restrict__ expert_offset, int epr, int dense_rows,
                  const float* __restrict__ xg_sa, const float* __restrict__ gu_scale,
                  int8_t* __restrict__ bucket_i8, float* __restrict__ bucket_sa,
                  uint16_t* __restrict__ bucket_bf16, int* __restrict__ err, int max_rows,
                  int max_tiles) {
+  constexpr int IW = DENSE ? DENSE_I : I;  // intermediate columns per expert
+  constexpr int GUW = 2 * IW;               // gate + up rows per expert
+  constexpr int NJ = IW / 64;               // column tiles
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem1& s = *reinterpret_cast<Smem1*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -123,7 +130,18 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     s.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 2) build_tile_table(s.tt, expert_offset, epr, lane);
+  if (warp == 2) {
+    if constexpr (DENSE) {
+      if (lane == 0) {
+        s.tt.eoff[0] = 0;
+        s.tt.eoff[1] = dense_rows;
+        s.tt.moff[0] = 0;
+        s.tt.moff[1] = (dense_rows + TILE_M - 1) / TILE_M;
+      }
+    } else {
+      build_tile_table(s.tt, expert_offset, epr, lane);
+    }
+  }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s.tmem_base)),
@@ -135,7 +153,7 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   tc_fence_after();
 
   const uint32_t tmem = s.tmem_base;
-  int total = s.tt.moff[epr] * NJ1;
+  int total = s.tt.moff[epr] * NJ;
   // Defensive bound: never more tiles than the route buffers can hold.
   if (total < 0 || total > max_tiles || s.tt.eoff[epr] > max_rows) {
     if (tid == 0) atomicExch(err, 2);
@@ -148,9 +166,9 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        const TileInfo ti = tile_info(s.tt, epr, NJ1, t);
-        const int brow_g = ti.e * GU + ti.col * 64;
-        const int brow_u = ti.e * GU + I + ti.col * 64;
+        const TileInfo ti = tile_info(s.tt, epr, NJ, t);
+        const int brow_g = ti.e * GUW + ti.col * 64;
+        const int brow_u = ti.e * GUW + IW + ti.col * 64;
         for (int kb = 0; kb < KB1; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done;
           uint8_t* st = s.stage[stage];
@@ -202,17 +220,17 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const TileInfo ti = tile_info(s.tt, epr, NJ1, t);
+      const TileInfo ti = tile_info(s.tt, epr, NJ, t);
       // per-tile operands are loaded before the accumulator wait
       const bool valid = r < ti.nvalid;
       const int row = ti.row0 + r;
       const float ad = valid ? __fmul_rn(xg_sa[row], inv127) : 0.0f;
-      const float* wsg = gu_scale + (size_t)ti.e * GU + ti.col * 64 + 16 * cb;
+      const float* wsg = gu_scale + (size_t)ti.e * GUW + ti.col * 64 + 16 * cb;
       float sg[16], su[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         sg[c] = __ldg(wsg + c);
-        su[c] = __ldg(wsg + I + c);
+        su[c] = __ldg(wsg + IW + c);
       }
       // On a failed (timed-out) wait the epilogue keeps walking the tiles
       // without waiting (the CTA's failed flag makes every later wait return at
@@ -233,12 +251,16 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       float hv[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
-        const float gv = __fmul_rn(__fmul_rn((float)gd[c], ad), sg[c]);
-        const float uv = __fmul_rn(__fmul_rn((float)ud[c], ad), su[c]);
+        float gv = __fmul_rn(__fmul_rn((float)gd[c], ad), sg[c]);
+        float uv = __fmul_rn(__fmul_rn((float)ud[c], ad), su[c]);
+        if constexpr (DENSE) {  // bq_linear stores gate and up as bf16 before GeGLU
+          gv = bf2f(f2bf(gv));
+          uv = bf2f(f2bf(uv));
+        }
         hv[c] = bf2f(f2bf(__fmul_rn(gelu_tanh_f32(gv), uv)));
       }
       if (bucket_bf16 && valid) {
-        uint4* dst = reinterpret_cast<uint4*>(bucket_bf16 + (size_t)row * I + ti.col * 64 + 16 * cb);
+        uint4* dst = reinterpret_cast<uint4*>(bucket_bf16 + (size_t)row * IW + ti.col * 64 + 16 * cb);
 #pragma unroll
         for (int v = 0; v < 2; ++v) {
           uint32_t w[4];
@@ -300,9 +322,9 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             p |= (uint32_t)(quantize_i8(hv[u * 4 + b], qinv) & 0xFF) << (8 * b);
           w[u] = p;
         }
-        *reinterpret_cast<uint4*>(bucket_i8 + (size_t)row * I + ti.col * 64 + 16 * cb) =
+        *reinterpret_cast<uint4*>(bucket_i8 + (size_t)row * IW + ti.col * 64 + 16 * cb) =
             make_uint4(w[0], w[1], w[2], w[3]);
-        if (cb == 0) bucket_sa[(size_t)row * NB_DOWN + ti.col] = amax;
+        if (cb == 0) bucket_sa[(size_t)row * NJ + ti.col] = amax;
       }
     }
   }
@@ -316,12 +338,18 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   if (tid == 0 && s.failed) atomicExch(err, ERR_TIMEOUT);
 }
 
+// DENSE: the dense MLP's down product (K = 2112, 33 blocks) over dense_rows
+// token rows in order, out = bf16(facc * sw) into a bf16 [rows][2816] `yout`.
+template <bool DENSE>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                 const int32_t* __restrict__ expert_offset, int epr,
+                 const int32_t* __restrict__ expert_offset, int epr, int dense_rows,
                  const float* __restrict__ bsa, const SparseRoute* __restrict__ routes,
-                 const float* __restrict__ dn_scale, float* __restrict__ ybuf,
+                 const float* __restrict__ dn_scale, void* __restrict__ yout,
                  int* __restrict__ err, int max_rows, int max_tiles) {
+  constexpr int KW = DENSE ? DENSE_I : I;   // K bytes per row
+  constexpr int NB = KW / 64;               // dequantisation blocks
+  constexpr int KC = (KW + BK - 1) / BK;    // K stages (last half zero-filled)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem2& s = *reinterpret_cast<Smem2*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -340,7 +368,18 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     s.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 2) build_tile_table(s.tt, expert_offset, epr, lane);
+  if (warp == 2) {
+    if constexpr (DENSE) {
+      if (lane == 0) {
+        s.tt.eoff[0] = 0;
+        s.tt.eoff[1] = dense_rows;
+        s.tt.moff[0] = 0;
+        s.tt.moff[1] = (dense_rows + TILE_M - 1) / TILE_M;
+      }
+    } else {
+      build_tile_table(s.tt, expert_offset, epr, lane);
+    }
+  }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s.tmem_base)),
@@ -364,7 +403,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         const TileInfo ti = tile_info(s.tt, epr, NT2, t);
-        for (int c = 0; c < KC2; ++c) {
+        for (int c = 0; c < KC; ++c) {
           if (!mbar_wait<false>(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done2;
           uint8_t* st = s.stage[stage];
           mbar_expect_tx(&s.full[stage], STAGE_BYTES);
@@ -381,13 +420,13 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       uint32_t phase = 0, rphase = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < total; t += gridDim.x) {
-        for (int c = 0; ok && c < KC2; ++c) {
+        for (int c = 0; ok && c < KC; ++c) {
           if (!mbar_wait<false>(&s.full[stage], phase, &s.failed)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(s.stage[stage]);
           const uint32_t b0 = a0 + A_BYTES;
           for (int h = 0; h < 2; ++h) {
-            if (2 * c + h >= NB_DOWN) break;  // K bytes 704..767 are padding
+            if (2 * c + h >= NB) break;  // K bytes beyond KW are padding
             if (!mbar_wait<false>(&s.reg_empty[reg], rphase ^ 1, &s.failed)) { ok = false; break; }
             tc_fence_after();
             const uint32_t d = tmem + (uint32_t)(reg * BN);
@@ -419,17 +458,26 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       const bool quarter_live = q * 32 < ti.nvalid;  // warp-uniform
       const int row = ti.row0 + r;
       // per-tile operands are loaded before the first accumulator wait
-      float adv[NB_DOWN];
+      // the 11 expert block scales are held in registers; the dense MLP's 33
+      // are read per block (issued before that block's accumulator wait)
+      float adv[DENSE ? 1 : NB];
+      if constexpr (!DENSE) {
 #pragma unroll
-      for (int b = 0; b < NB_DOWN; ++b)
-        adv[b] = valid ? __fmul_rn(bsa[(size_t)row * NB_DOWN + b], inv127) : 0.0f;
-      const float wr = valid ? routes[row].weight : 0.0f;
+        for (int b = 0; b < NB; ++b)
+          adv[b] = valid ? __fmul_rn(bsa[(size_t)row * NB + b], inv127) : 0.0f;
+      }
+      const float wr = (!DENSE && valid) ? routes[row].weight : 0.0f;
       const float* wsc = dn_scale + (size_t)ti.e * H + ti.col * BN + 32 * cb;
       float2 facc[16];
 #pragma unroll
       for (int n = 0; n < 16; ++n) facc[n] = make_float2(0.0f, 0.0f);
 #pragma unroll
-      for (int b = 0; b < NB_DOWN; ++b) {
+      for (int b = 0; b < NB; ++b) {
+        float adv_b;
+        if constexpr (DENSE)
+          adv_b = valid ? __fmul_rn(__ldg(bsa + (size_t)row * NB + b), inv127) : 0.0f;
+        else
+          adv_b = adv[b];
         // as in phase 1: after a failed wait keep going without waiting, so the
         // quarter's named barriers are always met
         (void)__all_sync(0xffffffffu, mbar_wait<false>(&s.reg_full[reg], rphase, &s.failed));
@@ -442,30 +490,43 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         mbar_arrive(&s.reg_empty[reg]);
         if (++reg == RING) { reg = 0; rphase ^= 1; }
         if (quarter_live) {
-          const float2 a2 = make_float2(adv[b], adv[b]);
+          const float2 a2 = make_float2(adv_b, adv_b);
 #pragma unroll
           for (int i = 0; i < 16; ++i)
             facc[i] = fma2(small_ints_to_float2(d[2 * i], d[2 * i + 1]), a2, facc[i]);
         }
       }
-      // y = facc * sw * w_route, staged per row then written as whole rows
+      // y = facc * sw * w_route (dense: facc * sw), staged per row then
+      // written as whole rows
       const float2 wr2 = make_float2(wr, wr);
       float4* ys = reinterpret_cast<float4*>(&s.ystage[r][32 * cb]);
 #pragma unroll
       for (int v = 0; v < 8; ++v) {
         const float4 sw = __ldg(reinterpret_cast<const float4*>(wsc) + v);
-        const float2 lo = mul2(mul2(facc[2 * v], make_float2(sw.x, sw.y)), wr2);
-        const float2 hi = mul2(mul2(facc[2 * v + 1], make_float2(sw.z, sw.w)), wr2);
+        float2 lo = mul2(facc[2 * v], make_float2(sw.x, sw.y));
+        float2 hi = mul2(facc[2 * v + 1], make_float2(sw.z, sw.w));
+        if constexpr (!DENSE) {
+          lo = mul2(lo, wr2);
+          hi = mul2(hi, wr2);
+        }
         ys[v] = make_float4(lo.x, lo.y, hi.x, hi.y);
       }
       quarter_sync(q);
-      // the 4 warps of quarter q write its 32 rows: 8 rows each, one 512-byte row per warp store
+      // the 4 warps of quarter q write its 32 rows: 8 rows each, one whole row per warp store
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int rr = q * 32 + cb * 8 + j;
         if (rr < ti.nvalid) {
           const float4 v = reinterpret_cast<const float4*>(&s.ystage[rr][0])[lane];
-          reinterpret_cast<float4*>(ybuf + (size_t)(ti.row0 + rr) * H + ti.col * BN)[lane] = v;
+          if constexpr (DENSE) {
+            const uint2 o = make_uint2((uint32_t)f2bf(v.x) | ((uint32_t)f2bf(v.y) << 16),
+                                       (uint32_t)f2bf(v.z) | ((uint32_t)f2bf(v.w) << 16));
+            reinterpret_cast<uint2*>(static_cast<uint16_t*>(yout) + (size_t)(ti.row0 + rr) * H +
+                                     ti.col * BN)[lane] = o;
+          } else {
+            reinterpret_cast<float4*>(static_cast<float*>(yout) + (size_t)(ti.row0 + rr) * H +
+                                      ti.col * BN)[lane] = v;
+          }
         }
       }
       quarter_sync(q);  // staging rows read before the next tile overwrites them
@@ -572,13 +633,28 @@ cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t
   const int max_rows = T * TOPK;
   const int max_tiles = (max_rows / tc::BM + epr) * tc::NJ1;
   const size_t smem = sizeof(tc::Smem1) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(tc::tc_phase1_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto k = tc::tc_phase1_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_k(tc::tc_phase1_kernel, dim3(sm_count()), dim3(tc::THREADS), smem, s,
+  return launch_k(k, dim3(sm_count()), dim3(tc::THREADS), smem, s,
                   *reinterpret_cast<const CUtensorMap*>(map_a),
-                  *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, xg_sa, gu_scale,
+                  *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, 0, xg_sa, gu_scale,
                   bucket_i8, bucket_sa, bucket_bf16, err, max_rows, max_tiles);
+}
+
+cudaError_t launch_tc_dense_gate_up(const void* map_x, const void* map_w, int T, const float* xsa,
+                                    const float* gu_scale, int8_t* h_i8, float* h_sa,
+                                    uint16_t* h_bf16, int* err, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const int tiles = (T + tc::BM - 1) / tc::BM * (DENSE_I / 64);
+  const size_t smem = sizeof(tc::Smem1) + 1024;
+  auto k = tc::tc_phase1_kernel<true>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_k(k, dim3(std::min(sm_count(), tiles)), dim3(tc::THREADS), smem, s,
+                  *reinterpret_cast<const CUtensorMap*>(map_x),
+                  *reinterpret_cast<const CUtensorMap*>(map_w), nullptr, 1, T, xsa, gu_scale, h_i8,
+                  h_sa, h_bf16, err, T, tiles);
 }
 
 cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
@@ -587,13 +663,27 @@ cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t
   const int max_rows = T * TOPK;
   const int max_tiles = (max_rows / tc::BM + epr) * tc::NT2;
   const size_t smem = sizeof(tc::Smem2) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(tc::tc_phase2_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto k = tc::tc_phase2_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_k(tc::tc_phase2_kernel, dim3(sm_count()), dim3(tc::THREADS), smem, s,
+  return launch_k(k, dim3(sm_count()), dim3(tc::THREADS), smem, s,
                   *reinterpret_cast<const CUtensorMap*>(map_a),
-                  *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, bsa, routes,
-                  dn_scale, ybuf, err, max_rows, max_tiles);
+                  *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, 0, bsa, routes,
+                  dn_scale, static_cast<void*>(ybuf), err, max_rows, max_tiles);
+}
+
+cudaError_t launch_tc_dense_down(const void* map_h, const void* map_w, int T, const float* hsa,
+                                 const float* dn_scale, uint16_t* out, int* err, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const int tiles = (T + tc::BM - 1) / tc::BM * tc::NT2;
+  const size_t smem = sizeof(tc::Smem2) + 1024;
+  auto k = tc::tc_phase2_kernel<true>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_k(k, dim3(std::min(sm_count(), tiles)), dim3(tc::THREADS), smem, s,
+                  *reinterpret_cast<const CUtensorMap*>(map_h),
+                  *reinterpret_cast<const CUtensorMap*>(map_w), nullptr, 1, T, hsa, nullptr, dn_scale,
+                  static_cast<void*>(out), err, T, tiles);
 }
 
 }  // namespace gm

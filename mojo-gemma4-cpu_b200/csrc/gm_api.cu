@@ -41,6 +41,22 @@ struct Layer {
   uint16_t* post_w2 = nullptr;  // post_feedforward_layernorm_2 [H]
   uint16_t* post_w = nullptr;   // post_feedforward_layernorm [H]
   float layer_scalar = 1.0f;
+  // dense butterquant MLP (gm_moe_register_dense_bq), VNNI-packed
+  int8_t* dg_q = nullptr;       // gate_proj [2112][H]
+  float* dg_scale = nullptr;
+  int8_t* du_q = nullptr;       // up_proj [2112][H]
+  float* du_scale = nullptr;
+  int8_t* dd_q = nullptr;       // down_proj [H][2112]
+  float* dd_scale = nullptr;
+  uint16_t* dgamma = nullptr;   // pre_feedforward_layernorm, split-gain baked
+  // row-major copies for the dense tcgen05 path: gate rows then up rows, and
+  // their scales in the same order; down
+  int8_t* dgu_rm = nullptr;     // [4224][H]
+  float* dgu_scale = nullptr;   // [4224]
+  int8_t* dd_rm = nullptr;      // [H][2112]
+  alignas(64) unsigned char tmap_dgu[128] = {};
+  alignas(64) unsigned char tmap_ddn[128] = {};
+  bool has_dense_tc = false;
 };
 
 }  // namespace
@@ -85,6 +101,21 @@ struct gm_moe {
   cudaStream_t own_stream = nullptr;
   cudaStream_t side_stream = nullptr;  // L2 prefetches forked off the forward's stream
   cudaEvent_t fork_event = nullptr;
+  // dense MLP of gm_ffn_forward, forked off the forward's stream and joined
+  // before the post-MoE tail
+  cudaStream_t dense_stream = nullptr;
+  cudaEvent_t dense_fork = nullptr, dense_done = nullptr;
+  bool dense_pending = false;
+  int8_t* d_xi8 = nullptr;      // [T][H]
+  float* d_xsa = nullptr;       // [T]
+  float* d_inv = nullptr;       // [T]
+  int8_t* d_hi8 = nullptr;      // [T][2112]
+  float* d_hsa = nullptr;       // [T][33]
+  uint16_t* d_out = nullptr;    // [T][H] dense_out
+  alignas(64) unsigned char tmap_dx[128] = {};  // over d_xi8 (tcgen05 A operand)
+  alignas(64) unsigned char tmap_dh[128] = {};  // over d_hi8
+  bool dense_tc_ok = false;
+  int dense_tc_min = 128;       // GM_OPT_DENSE_TC_MIN_TOKENS
   // stage profiler (GM_OPT_PROFILE) and kernel launch count
   struct PendingStage {
     int stat;
@@ -182,7 +213,7 @@ struct Carve {
 struct WsLayout {
   size_t logits, inv_rms, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
       x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, xg, xg_sa, dev_err,
-      sched_counts, router_counts, total;
+      sched_counts, router_counts, d_xi8, d_xsa, d_inv, d_hi8, d_hsa, d_out, total;
 };
 
 WsLayout ws_layout(int max_tokens) {
@@ -213,6 +244,12 @@ WsLayout ws_layout(int max_tokens) {
   L.dev_err = c.take<int>(1);
   L.sched_counts = c.take<int32_t>(schedule_counts_ints(max_tokens));
   L.router_counts = c.take<int>(router_tile_counters(max_tokens));
+  L.d_xi8 = c.take<int8_t>(T * H);
+  L.d_xsa = c.take<float>(T);
+  L.d_inv = c.take<float>(T);
+  L.d_hi8 = c.take<int8_t>(T * DENSE_I);
+  L.d_hsa = c.take<float>(T * NB_DENSE);
+  L.d_out = c.take<uint16_t>(T * H);
   L.total = align_up(c.off, 256);
   return L;
 }
@@ -231,10 +268,34 @@ int dev_copy(gm_moe* h, T** dst, const void* src, size_t count, const char* what
 
 void free_layer(Layer& L) {
   void* ptrs[] = {L.gu_q, L.gu_scale, L.dn_q, L.dn_scale, L.gu_bf16, L.dn_bf16, L.router, L.rscale,
-                  L.pes, L.gamma2, L.gu_rm, L.dn_rm, L.post_w1, L.post_w2, L.post_w};
+                  L.pes, L.gamma2, L.gu_rm, L.dn_rm, L.post_w1, L.post_w2, L.post_w,
+                  L.dg_q, L.dg_scale, L.du_q, L.du_scale, L.dd_q, L.dd_scale, L.dgamma,
+                  L.dgu_rm, L.dgu_scale, L.dd_rm};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   L = Layer{};
+}
+
+// Frees a layer's expert weights only: the post-MoE gains and the dense MLP
+// stay registered across a re-registration of the experts.
+void free_moe(Layer& L) {
+  Layer keep;
+  keep.post_w1 = L.post_w1; keep.post_w2 = L.post_w2; keep.post_w = L.post_w;
+  keep.layer_scalar = L.layer_scalar;
+  keep.dg_q = L.dg_q; keep.dg_scale = L.dg_scale; keep.du_q = L.du_q; keep.du_scale = L.du_scale;
+  keep.dd_q = L.dd_q; keep.dd_scale = L.dd_scale; keep.dgamma = L.dgamma;
+  keep.dgu_rm = L.dgu_rm; keep.dgu_scale = L.dgu_scale; keep.dd_rm = L.dd_rm;
+  memcpy(keep.tmap_dgu, L.tmap_dgu, sizeof keep.tmap_dgu);
+  memcpy(keep.tmap_ddn, L.tmap_ddn, sizeof keep.tmap_ddn);
+  keep.has_dense_tc = L.has_dense_tc;
+  L.post_w1 = L.post_w2 = L.post_w = nullptr;
+  L.dg_q = L.du_q = L.dd_q = nullptr;
+  L.dg_scale = L.du_scale = L.dd_scale = nullptr;
+  L.dgamma = nullptr;
+  L.dgu_rm = L.dd_rm = nullptr;
+  L.dgu_scale = nullptr;
+  free_layer(L);
+  L = keep;
 }
 
 int check_layer(gm_moe* h, int layer) {
@@ -290,6 +351,14 @@ int carve_workspace(gm_moe* h, int tokens) {
   h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
   h->sched_counts = reinterpret_cast<int32_t*>(b + L.sched_counts);
   h->router_counts = reinterpret_cast<int*>(b + L.router_counts);
+  h->d_xi8 = reinterpret_cast<int8_t*>(b + L.d_xi8);
+  h->d_xsa = reinterpret_cast<float*>(b + L.d_xsa);
+  h->d_inv = reinterpret_cast<float*>(b + L.d_inv);
+  h->d_hi8 = reinterpret_cast<int8_t*>(b + L.d_hi8);
+  h->d_hsa = reinterpret_cast<float*>(b + L.d_hsa);
+  h->d_out = reinterpret_cast<uint16_t*>(b + L.d_out);
+  h->dense_tc_ok = make_tmap_i8(h->tmap_dx, h->d_xi8, (long)tokens, H, 128) &&
+                   make_tmap_i8(h->tmap_dh, h->d_hi8, (long)tokens, DENSE_I, 128);
   cudaMemset(h->dev_err, 0, sizeof(int));
   cudaMemset(h->router_counts, 0, sizeof(int) * router_tile_counters(tokens));
   h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)tokens * TOPK, H, 128) &&
@@ -381,6 +450,14 @@ struct StageScope {
   }
 };
 
+// The post-MoE tail reads dense_out: wait for the dense MLP forked by
+// gm_ffn_forward (no-op otherwise).
+int join_dense(gm_moe* h, cudaStream_t s) {
+  if (!h->dense_pending) return GM_OK;
+  h->dense_pending = false;
+  return cuda_check(h, cudaStreamWaitEvent(s, h->dense_done, 0), "dense join");
+}
+
 // Expert products and combine for Tn activation rows whose schedule
 // (expert_offset, routes, route_pos, chunk_off) is in the workspace: rows are
 // x_i8/x_sa (butterquant) or x_normed (bf16), route_idx their top-8.
@@ -426,6 +503,7 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
              "phase2_down");
   }
   if (skip_combine) return GM_OK;
+  if (post && join_dense(h, s)) return GM_ECUDA;
   if (post)
     GM_STAGE(h, s, launch_combine_post(route_idx, h->route_pos, h->ybuf, Tn, *post, s), "combine.post");
   else
@@ -485,6 +563,7 @@ int ep_forward_p2p(gm_moe* h, const Layer& L, uint16_t* out, int T, cudaStream_t
            "combine.p2p");
   GM_STAGE(h, s, launch_ep_wait(h->ep_cflag, G, epoch, h->dev_err, s), "ep_combine.wait");
   const uint16_t* contrib = P.contrib[h->rank];
+  if (post && join_dense(h, s)) return GM_ECUDA;
   if (post)
     GM_STAGE(h, s, launch_ep_final_post(contrib, h->ep_pos, T, G, cap, *post, s), "ep_final.post");
   else
@@ -569,6 +648,7 @@ int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int
     GM_NCCL(h, nc->group_end(), "ep combine");
   }
   // 6. sum of the ranks' partials in rank order (then the post-MoE tail)
+  if (post && join_dense(h, s)) return GM_ECUDA;
   if (post)
     GM_STAGE(h, s, launch_ep_final_post(h->ep_contrib, h->ep_pos, T, G, cap, *post, s), "ep_final.post");
   else
@@ -640,6 +720,12 @@ int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, in
     cudaGetLastError();
     h->side_stream = nullptr;  // prefetch disabled; everything else works
   }
+  if (cudaStreamCreateWithFlags(&h->dense_stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&h->dense_fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&h->dense_done, cudaEventDisableTiming) != cudaSuccess) {
+    cudaGetLastError();
+    h->dense_stream = nullptr;  // the dense MLP then runs on the forward's stream
+  }
   if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
     cudaFree(h->ws);
     delete h;
@@ -666,6 +752,9 @@ int gm_moe_destroy(gm_moe_t* h) {
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
   if (h->side_stream) cudaStreamDestroy(h->side_stream);
   if (h->fork_event) cudaEventDestroy(h->fork_event);
+  if (h->dense_stream) cudaStreamDestroy(h->dense_stream);
+  if (h->dense_fork) cudaEventDestroy(h->dense_fork);
+  if (h->dense_done) cudaEventDestroy(h->dense_done);
   delete h;
   return GM_OK;
 }
@@ -681,7 +770,7 @@ int gm_moe_register_layer_bq(gm_moe_t* h, int layer, const void* gate_up,
     return set_err(h, GM_ESTATE, "layers are registered before gm_moe_ep_set_placement");
   GM_TRY(h, cudaSetDevice(h->device), "register_layer_bq");
   Layer& L = h->layers[layer];
-  free_layer(L);
+  free_moe(L);
   const size_t epr = (size_t)h->epr;
   if ((rc = dev_copy(h, &L.gu_q, gate_up, epr * GU * H, "gate_up"))) return rc;
   if ((rc = dev_copy(h, &L.gu_scale, gate_up_scale, epr * GU, "gate_up_scale"))) return rc;
@@ -713,7 +802,7 @@ int gm_moe_register_layer_bf16(gm_moe_t* h, int layer, const void* gate_up, cons
     return set_err(h, GM_ESTATE, "layers are registered before gm_moe_ep_set_placement");
   GM_TRY(h, cudaSetDevice(h->device), "register_layer_bf16");
   Layer& L = h->layers[layer];
-  free_layer(L);
+  free_moe(L);
   const size_t epr = (size_t)h->epr;
   if ((rc = dev_copy(h, &L.gu_bf16, gate_up, epr * GU * H, "gate_up"))) return rc;
   if ((rc = dev_copy(h, &L.dn_bf16, down, epr * H * I, "down"))) return rc;
@@ -812,9 +901,122 @@ int gm_moe_forward_ffn(gm_moe_t* h, int layer, void* x_main, const void* dense_o
   const Layer& L = h->layers[layer];
   if (!L.post_w1) return set_err(h, GM_ESTATE, "layer %d: gm_moe_register_post not called", layer);
   if (!x_main || !dense_out) return set_err(h, GM_EINVAL, "NULL x_main/dense_out");
+  if (h->degree > 1 && !h->ep_comm)
+    return set_err(h, GM_ESTATE, "the post-MoE tail needs the complete MoE output: degree %d "
+                   "without gm_moe_ep_init yields partials", h->degree);
   PostParams p{static_cast<const uint16_t*>(dense_out), static_cast<uint16_t*>(x_main), L.post_w1,
                L.post_w2, L.post_w, L.layer_scalar};
   return forward_impl(h, layer, x_main, x_main, T, stream, &p);
+}
+
+namespace {
+// The dense MLP of dispatch_bq_ffn (modeling/gemma_4_moe_bq.mojo:749-783)
+// on stream s: norm+quant with pre_feedforward_layernorm, gate/up + GeGLU +
+// block quant, down -> out bf16 [T][H].
+int run_dense(gm_moe* h, const Layer& L, const uint16_t* x, uint16_t* out, int T, cudaStream_t s) {
+  if (T == 0) return GM_OK;
+  GM_STAGE(h, s, launch_bq_norm_quant(x, L.dgamma, T, h->d_xi8, h->d_xsa, h->d_inv, s),
+           "dense.bq_norm_quant");
+  if (L.has_dense_tc && h->dense_tc_ok && T >= h->dense_tc_min) {
+    GM_STAGE(h, s, launch_tc_dense_gate_up(h->tmap_dx, L.tmap_dgu, T, h->d_xsa, L.dgu_scale, h->d_hi8,
+                                           h->d_hsa, nullptr, h->dev_err, s),
+             "bq_linear.gate_up.tc");
+    GM_STAGE(h, s, launch_tc_dense_down(h->tmap_dh, L.tmap_ddn, T, h->d_hsa, L.dd_scale, out,
+                                        h->dev_err, s),
+             "bq_block_linear.tc");
+    return GM_OK;
+  }
+  GM_STAGE(h, s, launch_dense_gate_up(h->d_xi8, h->d_xsa, T, L.dg_q, L.dg_scale, L.du_q, L.du_scale,
+                                      h->d_hi8, h->d_hsa, nullptr, s),
+           "bq_linear.gate_up");
+  GM_STAGE(h, s, launch_dense_down(h->d_hi8, h->d_hsa, T, L.dd_q, L.dd_scale, out, s), "bq_block_linear");
+  return GM_OK;
+}
+
+int check_dense(gm_moe* h, int layer, const void* x, int T) {
+  int rc = check_layer(h, layer);
+  if (rc) return rc;
+  if (!h->layers[layer].dg_q)
+    return set_err(h, GM_ESTATE, "layer %d: gm_moe_register_dense_bq not called", layer);
+  if (T < 0 || T > h->max_tokens)
+    return set_err(h, GM_EINVAL, "T=%d outside [0, max_tokens=%d]", T, h->max_tokens);
+  if (!x) return set_err(h, GM_EINVAL, "NULL activation");
+  return GM_OK;
+}
+}  // namespace
+
+int gm_moe_register_dense_bq(gm_moe_t* h, int layer, const void* gate_proj, const float* gate_scale,
+                             const void* up_proj, const float* up_scale, const void* down_proj,
+                             const float* down_scale, const void* pre_ffn_norm) {
+  int rc = check_layer(h, layer);
+  if (rc) return rc;
+  GM_TRY(h, cudaSetDevice(h->device), "register_dense_bq");
+  Layer& L = h->layers[layer];
+  if ((rc = dev_copy(h, &L.dg_q, gate_proj, (size_t)DENSE_I * H, "gate_proj"))) return rc;
+  if ((rc = dev_copy(h, &L.dg_scale, gate_scale, (size_t)DENSE_I, "gate_proj scale"))) return rc;
+  if ((rc = dev_copy(h, &L.du_q, up_proj, (size_t)DENSE_I * H, "up_proj"))) return rc;
+  if ((rc = dev_copy(h, &L.du_scale, up_scale, (size_t)DENSE_I, "up_proj scale"))) return rc;
+  if ((rc = dev_copy(h, &L.dd_q, down_proj, (size_t)H * DENSE_I, "down_proj"))) return rc;
+  if ((rc = dev_copy(h, &L.dd_scale, down_scale, (size_t)H, "down_proj scale"))) return rc;
+  if ((rc = dev_copy(h, &L.dgamma, pre_ffn_norm, (size_t)H, "pre_ffn_norm"))) return rc;
+  // row-major copies and tensor maps for the tcgen05 path
+  for (void* p : {(void*)L.dgu_rm, (void*)L.dgu_scale, (void*)L.dd_rm})
+    if (p) cudaFree(p);
+  L.dgu_rm = L.dd_rm = nullptr;
+  L.dgu_scale = nullptr;
+  GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.dgu_rm), (size_t)2 * DENSE_I * H), "dense gate|up copy");
+  GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.dgu_scale), (size_t)2 * DENSE_I * 4), "dense scales");
+  GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.dd_rm), (size_t)H * DENSE_I), "dense down copy");
+  GM_TRY(h, launch_vnni_permute(L.dg_q, DENSE_I, H, L.dgu_rm, 1, h->own_stream), "vnni unpack");
+  GM_TRY(h, launch_vnni_permute(L.du_q, DENSE_I, H, L.dgu_rm + (size_t)DENSE_I * H, 1, h->own_stream),
+         "vnni unpack");
+  GM_TRY(h, launch_vnni_permute(L.dd_q, H, DENSE_I, L.dd_rm, 1, h->own_stream), "vnni unpack");
+  GM_TRY(h, cudaMemcpyAsync(L.dgu_scale, L.dg_scale, DENSE_I * 4, cudaMemcpyDeviceToDevice, h->own_stream),
+         "dense scales");
+  GM_TRY(h, cudaMemcpyAsync(L.dgu_scale + DENSE_I, L.du_scale, DENSE_I * 4, cudaMemcpyDeviceToDevice,
+                            h->own_stream),
+         "dense scales");
+  GM_TRY(h, cudaStreamSynchronize(h->own_stream), "dense copies");
+  L.has_dense_tc = make_tmap_i8(L.tmap_dgu, L.dgu_rm, 2L * DENSE_I, H, 64) &&
+                   make_tmap_i8(L.tmap_ddn, L.dd_rm, (long)H, DENSE_I, 128);
+  return GM_OK;
+}
+
+int gm_dense_forward(gm_moe_t* h, int layer, const void* x, void* dense_out, int T, void* stream) {
+  int rc = check_dense(h, layer, x, T);
+  if (rc) return rc;
+  if (!dense_out) return set_err(h, GM_EINVAL, "NULL dense_out");
+  PdlScope pdl_scope(h->pdl);
+  return run_dense(h, h->layers[layer], static_cast<const uint16_t*>(x),
+                   static_cast<uint16_t*>(dense_out), T, S(stream));
+}
+
+int gm_ffn_forward(gm_moe_t* h, int layer, void* x_main, int T, void* stream) {
+  int rc = check_dense(h, layer, x_main, T);
+  if (rc) return rc;
+  const Layer& L = h->layers[layer];
+  if (L.kind == 0) return set_err(h, GM_ESTATE, "layer %d has no registered experts", layer);
+  if (!L.post_w1) return set_err(h, GM_ESTATE, "layer %d: gm_moe_register_post not called", layer);
+  if (h->degree > 1 && !h->ep_comm)
+    return set_err(h, GM_ESTATE, "the post-MoE tail needs the complete MoE output: degree %d "
+                   "without gm_moe_ep_init yields partials", h->degree);
+  cudaStream_t s = S(stream);
+  const uint16_t* x = static_cast<const uint16_t*>(x_main);
+  {
+    PdlScope pdl_scope(h->pdl);
+    if (h->dense_stream && T > 0) {
+      // the dense MLP runs beside the MoE on the same input; the tail joins it
+      GM_TRY(h, cudaEventRecord(h->dense_fork, s), "dense fork");
+      GM_TRY(h, cudaStreamWaitEvent(h->dense_stream, h->dense_fork, 0), "dense fork");
+      if ((rc = run_dense(h, L, x, h->d_out, T, h->dense_stream))) return rc;
+      GM_TRY(h, cudaEventRecord(h->dense_done, h->dense_stream), "dense done");
+      h->dense_pending = true;
+    } else if ((rc = run_dense(h, L, x, h->d_out, T, s))) {
+      return rc;
+    }
+  }
+  PostParams p{h->d_out, static_cast<uint16_t*>(x_main), L.post_w1, L.post_w2, L.post_w, L.layer_scalar};
+  return forward_impl(h, layer, x_main, x_main, T, s, &p);
 }
 
 int gm_moe_set_option(gm_moe_t* h, int option, long value) {
@@ -823,6 +1025,10 @@ int gm_moe_set_option(gm_moe_t* h, int option, long value) {
     case GM_OPT_TC_MIN_TOKENS:
       if (value < 1) return set_err(h, GM_EINVAL, "GM_OPT_TC_MIN_TOKENS must be >= 1");
       h->tc_min_tokens = value > 0x7FFFFFFF ? 0x7FFFFFFF : (int)value;
+      return GM_OK;
+    case GM_OPT_DENSE_TC_MIN_TOKENS:
+      if (value < 1) return set_err(h, GM_EINVAL, "GM_OPT_DENSE_TC_MIN_TOKENS must be >= 1");
+      h->dense_tc_min = value > 0x7FFFFFFF ? 0x7FFFFFFF : (int)value;
       return GM_OK;
     case GM_OPT_EP_TRANSPORT:
       if (value != 0 && value != 1) return set_err(h, GM_EINVAL, "GM_OPT_EP_TRANSPORT must be 0 or 1");
@@ -1156,6 +1362,24 @@ int gm_bq_phase2_down(const int8_t* bucket_i8, const float* bucket_sa, const int
                          reinterpret_cast<const SparseRoute*>(routes), chunk_off, epr, T,
                          static_cast<const int8_t*>(down), down_scale, y, false, S(stream)),
         "bq_phase2_down");
+}
+
+int gm_bq_dense_gate_up(const int8_t* x_i8, const float* x_sa, int T, const void* gate_proj,
+                        const float* gate_scale, const void* up_proj, const float* up_scale,
+                        int8_t* h_i8, float* h_sa, void* h_bf16, void* stream) {
+  if (T < 0) return set_err(nullptr, GM_EINVAL, "bq_dense_gate_up: T=%d", T);
+  STAGE(launch_dense_gate_up(x_i8, x_sa, T, static_cast<const int8_t*>(gate_proj), gate_scale,
+                             static_cast<const int8_t*>(up_proj), up_scale, h_i8, h_sa,
+                             static_cast<uint16_t*>(h_bf16), S(stream)),
+        "bq_dense_gate_up");
+}
+
+int gm_bq_block_linear(const int8_t* h_i8, const float* h_sa, int T, const void* down_proj,
+                       const float* down_scale, void* out, void* stream) {
+  if (T < 0) return set_err(nullptr, GM_EINVAL, "bq_block_linear: T=%d", T);
+  STAGE(launch_dense_down(h_i8, h_sa, T, static_cast<const int8_t*>(down_proj), down_scale,
+                          static_cast<uint16_t*>(out), S(stream)),
+        "bq_block_linear");
 }
 
 int gm_phase1_gate_up_bf16(const void* x_normed, const int32_t* expert_offset,

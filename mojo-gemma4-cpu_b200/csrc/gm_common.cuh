@@ -21,6 +21,8 @@ constexpr int GU = 1408;         // fused gate|up rows (:23)
 constexpr int DOWN_BLOCK = 64;   // DOWN_FWHT_BLOCK (:25)
 constexpr int NB_DOWN = I / DOWN_BLOCK;  // 11
 constexpr int NORM_BLOCK = 128;  // FWHT block of the gate/up activation
+constexpr int DENSE_I = 2112;    // dense MLP intermediate (modeling/gemma4_common.mojo:22)
+constexpr int NB_DENSE = DENSE_I / DOWN_BLOCK;  // 33
 constexpr int VNNI_N = 32;       // rows per packed N-tile (butterquant/vnni.mojo:13)
 constexpr int VNNI_K = 64;       // cols per packed K-step (vnni.mojo:14)
 

@@ -97,6 +97,13 @@ cudaError_t launch_bq_phase1(const int8_t* xi8, const float* xsa, const int32_t*
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_gu, const float* gu_scale, int8_t* bucket_i8,
                              float* bucket_sa, uint16_t* bucket_bf16, cudaStream_t s);
+// dense butterquant MLP (dense_bq.cu): gate/up products + GeGLU + FWHT-64
+// block quant of h (h_bf16 optional), then the down product to bf16 [T][H]
+cudaError_t launch_dense_gate_up(const int8_t* xi8, const float* xsa, int T, const int8_t* wg,
+                                 const float* gsc, const int8_t* wu, const float* usc,
+                                 int8_t* h_i8, float* h_sa, uint16_t* h_bf16, cudaStream_t s);
+cudaError_t launch_dense_down(const int8_t* hi8, const float* hsa, int T, const int8_t* wd,
+                              const float* dsc, uint16_t* out, cudaStream_t s);
 // bulk L2 prefetch of [base, base + bytes) (16-byte aligned base)
 cudaError_t launch_l2_prefetch(const void* base, size_t bytes, cudaStream_t s);
 cudaError_t launch_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t* expert_offset,
@@ -132,6 +139,15 @@ cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t
 cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
                              int epr, int T, const float* bsa, const SparseRoute* routes,
                              const float* dn_scale, float* ybuf, int* err, cudaStream_t s);
+// tcgen05 path of the dense MLP (gemm_tc.cu): maps over the activation rows
+// (int8 [rows][2816], 128-row boxes), the row-major gate|up weight ([4224][2816],
+// 64-row boxes), h (int8 [rows][2112], 128-row boxes) and the row-major down
+// weight ([2816][2112], 128-row boxes); gu_scale is gate scales then up scales
+cudaError_t launch_tc_dense_gate_up(const void* map_x, const void* map_w, int T, const float* xsa,
+                                    const float* gu_scale, int8_t* h_i8, float* h_sa,
+                                    uint16_t* h_bf16, int* err, cudaStream_t s);
+cudaError_t launch_tc_dense_down(const void* map_h, const void* map_w, int T, const float* hsa,
+                                 const float* dn_scale, uint16_t* out, int* err, cudaStream_t s);
 // tcgen05 prefill path for bf16 layers (gemm_tc_bf16.cu)
 cudaError_t launch_tcb_phase1(const void* map_a, const void* map_b, const int32_t* expert_offset,
                               int epr, int T, uint16_t* bucket, int* err, cudaStream_t s);

@@ -125,6 +125,8 @@ cudaError_t launch_quantize_rows(const uint16_t* w, long rows, int cols, const u
     quantize_rows_kernel<I, 64><<<grid, 256, 0, s>>>(w, rows, gamma, q, scale);
   else if (cols == H && block == 64)
     quantize_rows_kernel<H, 64><<<grid, 256, 0, s>>>(w, rows, gamma, q, scale);
+  else if (cols == DENSE_I && block == 64)
+    quantize_rows_kernel<DENSE_I, 64><<<grid, 256, 0, s>>>(w, rows, gamma, q, scale);
   else
     return cudaErrorInvalidValue;
   return cudaGetLastError();

@@ -70,6 +70,11 @@ SIGNATURES = {
     "gm_router_center": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "gm_bake_split_gain": (_i32, [_vp, _vp, _i32, _vp]),
     "gm_bake_router_scale": (_i32, [_vp, _vp, _i32, _vp]),
+    "gm_moe_register_dense_bq": (_i32, [_vp, _i32] + [_vp] * 7),
+    "gm_dense_forward": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp]),
+    "gm_ffn_forward": (_i32, [_vp, _i32, _vp, _i32, _vp]),
+    "gm_bq_dense_gate_up": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "gm_bq_block_linear": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "gm_checkpoint_open": (_i32, [C.POINTER(_vp), C.c_char_p]),
     "gm_checkpoint_close": (_i32, [_vp]),
     "gm_checkpoint_tensor_count": (_i32, [_vp]),
@@ -190,6 +195,22 @@ class MoeBlock:
         check(lib().gm_moe_forward_ffn(self.h, layer, _addr(x_main), _addr(dense_out), T,
                                        _stream(stream)), self.h)
 
+    def register_dense(self, layer, gate_proj, gate_scale, up_proj, up_scale, down_proj,
+                       down_scale, pre_ffn_norm):
+        """The layer's dense butterquant MLP (VNNI-packed weights, baked gain)."""
+        check(lib().gm_moe_register_dense_bq(
+            self.h, layer, _addr(gate_proj), _addr(gate_scale), _addr(up_proj), _addr(up_scale),
+            _addr(down_proj), _addr(down_scale), _addr(pre_ffn_norm)), self.h)
+
+    def dense_forward(self, layer, x, dense_out, T, stream=None):
+        """The dense MLP alone: x -> dense_out (device bf16 [T][2816])."""
+        check(lib().gm_dense_forward(self.h, layer, _addr(x), _addr(dense_out), T, _stream(stream)),
+              self.h)
+
+    def ffn_forward(self, layer, x_main, T, stream=None):
+        """Dense MLP beside the MoE, then the post-MoE tail; x_main in place."""
+        check(lib().gm_ffn_forward(self.h, layer, _addr(x_main), T, _stream(stream)), self.h)
+
     def forward_sync(self, layer, x, out, T):
         """Blocking; x/out may be host (e.g. pinned) or device buffers."""
         check(lib().gm_moe_forward_sync(self.h, layer, _addr(x), _addr(out), T), self.h)
@@ -300,6 +321,7 @@ OPT_TC_MIN_TOKENS = 1
 OPT_PROFILE = 2
 OPT_PDL = 3
 OPT_EP_TRANSPORT = 4
+OPT_DENSE_TC_MIN_TOKENS = 5
 EP_UNIQUE_ID_BYTES = 128
 
 

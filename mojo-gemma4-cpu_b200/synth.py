@@ -184,6 +184,46 @@ def bq_layer(raw, keep_rowmajor=False):
     return out
 
 
+DENSE_I = 2112
+
+
+def make_dense(seed=0x0D3E, device="cpu", weight_std=0.02, stress_gains=True):
+    """Raw bf16 tensors of one layer's dense MLP (gate/up [2112][2816], down
+    [2816][2112], pre_feedforward_layernorm gain)."""
+    g = _gen(seed, device)
+
+    def normal(*shape, std=1.0, mean=0.0):
+        t = torch.randn(*shape, generator=g, device=device, dtype=torch.float32)
+        return (t * std + mean).to(torch.bfloat16)
+
+    return {"gate": normal(DENSE_I, H, std=weight_std), "up": normal(DENSE_I, H, std=weight_std),
+            "down": normal(H, DENSE_I, std=weight_std),
+            "pre_ffn_norm": normal(H, std=0.25 if stress_gains else 0.0, mean=1.0)}
+
+
+def dense_layer(raw, keep_rowmajor=False):
+    """Device tensors for gm_moe_register_dense_bq: the reference's DenseGateUp
+    (PerRowQuant(128, SplitGamma(pre_feedforward_layernorm))) and DenseDown
+    (PerRowQuant(64, NoGamma)) recipes, VNNI-packed, split gain baked."""
+    d = {k: v.cuda().contiguous() for k, v in raw.items()}
+    out = {}
+    for name, rows, cols, gamma, block in (("gate", DENSE_I, H, d["pre_ffn_norm"], 128),
+                                           ("up", DENSE_I, H, d["pre_ffn_norm"], 128),
+                                           ("down", H, DENSE_I, None, 64)):
+        q = torch.empty(rows, cols, dtype=torch.int8, device="cuda")
+        sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+        gmoe.call("gm_bq_quantize_rows", d[name], rows, cols, gamma, block, q, sc, None)
+        p = torch.empty_like(q)
+        gmoe.call("gm_vnni_pack", q, rows, cols, p, None)
+        out[name], out[name + "_scale"] = p, sc
+        if keep_rowmajor:
+            out[name + "_rowmajor"] = q
+    g = torch.empty_like(d["pre_ffn_norm"])
+    gmoe.call("gm_bake_split_gain", d["pre_ffn_norm"], g, H, None)
+    out["pre_ffn_norm"] = g
+    return out
+
+
 def to_numpy_u16(t):
     """bf16 torch tensor -> uint16 numpy bit patterns (host)."""
     return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)

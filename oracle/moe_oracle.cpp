@@ -573,6 +573,84 @@ void orc_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t* expert_of
   for (size_t i = 0; i < (size_t)T * H; ++i) out[i] = f2bf(acc[i]);
 }
 
+// ------------------------------------------------------------ dense MLP
+// butterquant/gemm.mojo:115-143 gemm_i8_per_row_panel (u8 x s8 vpdpbusd,
+// dot_products.mojo:70-73 correction), stored as bf16 (convert.mojo:8-28):
+// out[t][n] = bf16((f32(iacc) - 128*cs[n]) * (sa[t]*(1/127)) * ws[n]).
+// w row-major int8 [n_rows][k] (the VNNI pack is a pure permutation).
+void orc_bq_linear(const int8_t* xi8, const float* xsa, int T, const int8_t* w, const float* ws,
+                   const float* cs, int n_rows, int k, uint16_t* out) {
+  const float inv127 = 1.0f / 127.0f;
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    const uint8_t* xr = reinterpret_cast<const uint8_t*>(xi8 + (long)t * k);
+    const float ad = xsa[t] * inv127;
+    for (int n = 0; n < n_rows; ++n) {
+      const int8_t* wr = w + (long)n * k;
+      int32_t ia = 0;
+      for (int j = 0; j < k; ++j) ia += (int32_t)(uint8_t)(xr[j] ^ 0x80u) * (int32_t)wr[j];
+      const float corr = (float)ia - 128.0f * cs[n];
+      out[(long)t * n_rows + n] = f2bf(corr * ad * ws[n]);
+    }
+  }
+}
+
+// kernels/elementwise.mojo:17-24 gelu_gate_up_row: bf16(gelu_tanh(g) * u).
+void orc_gelu_gate_up(const uint16_t* gate, const uint16_t* up, long n, uint16_t* out) {
+  for (long i = 0; i < n; ++i) out[i] = f2bf(gelu_tanh_f32(bf2f(gate[i])) * bf2f(up[i]));
+}
+
+// butterquant/gemm.mojo:174-216 gemm_i8_per_block_panel: per output row n,
+// facc = fma(f32(iacc_b) - 128*cs[b][n], sa[t][b]*(1/127), facc) over the k/64
+// blocks in order, out = bf16(facc * ws[n]).  cs block-major [nb][n_rows].
+void orc_bq_block_linear(const int8_t* hi8, const float* hsa, int T, int k, const int8_t* w,
+                         const float* ws, const float* cs, int n_rows, uint16_t* out) {
+  const float inv127 = 1.0f / 127.0f;
+  const int nb = k / DOWN_BLOCK;
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    const uint8_t* ar = reinterpret_cast<const uint8_t*>(hi8 + (long)t * k);
+    for (int n = 0; n < n_rows; ++n) {
+      const int8_t* wr = w + (long)n * k;
+      float facc = 0.0f;
+      for (int b = 0; b < nb; ++b) {
+        int32_t ia = 0;
+        for (int j = b * DOWN_BLOCK; j < (b + 1) * DOWN_BLOCK; ++j)
+          ia += (int32_t)(uint8_t)(ar[j] ^ 0x80u) * (int32_t)wr[j];
+        const float corr = (float)ia - 128.0f * cs[(long)b * n_rows + n];
+        facc = std::fmaf(corr, hsa[(long)t * nb + b] * inv127, facc);
+      }
+      out[(long)t * n_rows + n] = f2bf(facc * ws[n]);
+    }
+  }
+}
+
+// modeling/gemma_4_moe_bq.mojo:749-783 the dense half of dispatch_bq_ffn:
+// norm+quant (pre_feedforward_layernorm, split-gain baked), gate and up
+// bq_linear, GeGLU, FWHT-64 block quant of h, bq_block_linear with down.
+// h_bf16/h_i8/h_sa (optional) receive the intermediates.
+void orc_dense_mlp(const uint16_t* x, int T, const uint16_t* gamma, int inter,
+                   const int8_t* wg, const float* wgs, const float* wgcs,
+                   const int8_t* wu, const float* wus, const float* wucs,
+                   const int8_t* wd, const float* wds, const float* wdcs, uint16_t* out,
+                   uint16_t* h_bf16, int8_t* h_i8, float* h_sa) {
+  std::vector<int8_t> xi8((size_t)T * H);
+  std::vector<float> xsa(T);
+  orc_bq_norm_quant(x, gamma, T, xi8.data(), xsa.data());
+  std::vector<uint16_t> g((size_t)T * inter), u((size_t)T * inter), hh((size_t)T * inter);
+  orc_bq_linear(xi8.data(), xsa.data(), T, wg, wgs, wgcs, inter, H, g.data());
+  orc_bq_linear(xi8.data(), xsa.data(), T, wu, wus, wucs, inter, H, u.data());
+  orc_gelu_gate_up(g.data(), u.data(), (long)T * inter, hh.data());
+  const int nb = inter / DOWN_BLOCK;
+  std::vector<int8_t> qi((size_t)T * inter);
+  std::vector<float> qs((size_t)T * nb);
+  orc_bq_block_quant(hh.data(), T, inter, DOWN_BLOCK, qi.data(), qs.data());
+  orc_bq_block_linear(qi.data(), qs.data(), T, inter, wd, wds, wdcs, H, out);
+  if (h_bf16) std::memcpy(h_bf16, hh.data(), hh.size() * 2);
+  if (h_i8) std::memcpy(h_i8, qi.data(), qi.size());
+  if (h_sa) std::memcpy(h_sa, qs.data(), qs.size() * 4);
+}
+
 // ------------------------------------------------------------ whole block
 struct OrcBqLayer {
   const uint16_t* router_centered;  // [E][H] bf16 (router_center_softmax)

@@ -72,6 +72,10 @@ def _declare(L):
         "orc_bq_phase1": (None, [vp, vp, vp, vp, vp, vp, vp, i32, vp]),
         "orc_bq_block_quant": (None, [vp, i64, i32, i32, vp, vp]),
         "orc_bq_phase2": (None, [vp, vp, vp, vp, vp, vp, vp, i64, i32, i32, vp]),
+        "orc_bq_linear": (None, [vp, vp, i32, vp, vp, vp, i32, i32, vp]),
+        "orc_gelu_gate_up": (None, [vp, vp, i64, vp]),
+        "orc_bq_block_linear": (None, [vp, vp, i32, i32, vp, vp, vp, i32, vp]),
+        "orc_dense_mlp": (None, [vp, i32, vp, i32] + [vp] * 9 + [vp, vp, vp, vp]),
         "orc_bq_moe_forward": (i32, [vp, i32, vp, i32, vp, vp, vp, vp]),
         "orc_bf16_moe_forward": (i32, [vp, i32, vp, i32, vp, vp, vp, vp]),
         "orc_num_threads": (i32, []),
@@ -224,6 +228,53 @@ def bq_phase2(bi8, bsa, off, routes, dn_q, dn_scale, dn_cs, cs_stride, epr, T):
     lib().orc_bq_phase2(_p(bi8), _p(bsa), _p(off), _p(routes), _p(dn_q), _p(dn_scale),
                         _p(dn_cs), cs_stride, epr, T, _p(out))
     return out
+
+
+# ------------------------------------------------------------ dense MLP
+DENSE_I = 2112
+
+
+def bq_linear(xi8, xsa, w, ws, cs):
+    """dispatch_bq_linear: bf16 [T][n_rows] from x_i8/x_sa and a row-major int8 weight."""
+    T, k = xi8.shape
+    n = w.shape[0]
+    out = np.empty((T, n), np.uint16)
+    lib().orc_bq_linear(_p(np.ascontiguousarray(xi8)), _p(np.ascontiguousarray(xsa)), T,
+                        _p(np.ascontiguousarray(w)), _p(ws), _p(cs), n, k, _p(out))
+    return out
+
+
+def gelu_gate_up(g, u):
+    out = np.empty_like(g)
+    lib().orc_gelu_gate_up(_p(np.ascontiguousarray(g)), _p(np.ascontiguousarray(u)), g.size, _p(out))
+    return out
+
+
+def bq_block_linear(hi8, hsa, w, ws, cs_block_major):
+    """dispatch_bq_block_linear: bf16 [T][n_rows]; cs block-major [k/64][n_rows]."""
+    T, k = hi8.shape
+    n = w.shape[0]
+    out = np.empty((T, n), np.uint16)
+    lib().orc_bq_block_linear(_p(np.ascontiguousarray(hi8)), _p(np.ascontiguousarray(hsa)), T, k,
+                              _p(np.ascontiguousarray(w)), _p(ws), _p(cs_block_major), n, _p(out))
+    return out
+
+
+def dense_mlp(x, d):
+    """The dense MLP of dispatch_bq_ffn on layer dict d (row-major int8 weights
+    wg/wu [2112][2816], wd [2816][2112], scales, colsums, gamma baked).
+    Returns (dense_out, h_bf16, h_i8, h_sa)."""
+    T = x.shape[0]
+    inter = d["wg"].shape[0]
+    out = np.empty((T, H), np.uint16)
+    hb = np.empty((T, inter), np.uint16)
+    hq = np.empty((T, inter), np.int8)
+    hs = np.empty((T, inter // DOWN_BLOCK), np.float32)
+    a = [np.ascontiguousarray(d[k]) for k in ("wg", "wgs", "wgcs", "wu", "wus", "wucs", "wd", "wds",
+                                              "wdcs")]
+    lib().orc_dense_mlp(_p(np.ascontiguousarray(x)), T, _p(np.ascontiguousarray(d["gamma"])), inter,
+                        *[_p(v) for v in a], _p(out), _p(hb), _p(hq), _p(hs))
+    return out, hb, hq, hs
 
 
 def phase1_bf16(xn, off, routes, w_gu, epr):

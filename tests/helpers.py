@@ -54,6 +54,37 @@ def oracle_bq_layer(raw):
     }
 
 
+DI = 2112  # dense MLP intermediate
+
+
+def raw_dense_np(seed=2112, weight_std=0.02, stress=True):
+    """Seeded raw bf16 dense MLP (gate/up [2112][2816], down [2816][2112],
+    pre_feedforward_layernorm gain) as uint16 numpy arrays."""
+    rng = np.random.default_rng(seed)
+
+    def normal(shape, std=1.0, mean=0.0):
+        a = rng.standard_normal(size=shape, dtype=np.float32)
+        a *= np.float32(std)
+        a += np.float32(mean)
+        return O.f32_to_bf16(a)
+
+    return {"gate": normal((DI, H), weight_std), "up": normal((DI, H), weight_std),
+            "down": normal((H, DI), weight_std),
+            "pre_ffn_norm": normal((H,), 0.25 if stress else 0.0, 1.0)}
+
+
+def oracle_dense_layer(raw):
+    """Quantize as the reference's DenseGateUp / DenseDown recipes
+    (modeling/gemma_4_moe_bq.mojo:113-116) and bake the split gain."""
+    wg, wgs = O.quantize_rows(raw["gate"], 128, raw["pre_ffn_norm"])
+    wu, wus = O.quantize_rows(raw["up"], 128, raw["pre_ffn_norm"])
+    wd, wds = O.quantize_rows(raw["down"], 64)
+    return {"wg": wg, "wgs": wgs, "wgcs": O.colsum(wg, H, True).reshape(-1),
+            "wu": wu, "wus": wus, "wucs": O.colsum(wu, H, True).reshape(-1),
+            "wd": wd, "wds": wds, "wdcs": O.colsum(wd, 64, False),
+            "gamma": O.bake_split_gain(raw["pre_ffn_norm"])}
+
+
 def oracle_bf16_layer(raw):
     return {
         "router_proj": raw["router_proj"],

@@ -244,3 +244,36 @@ def test_post_moe_tail():
     ref = (f(x) + d2 * inv(d2) * f(w)) * 0.75
     got = f(O.post_moe(moe, dense, x, w1, w2, w, 0.75))
     assert np.abs(got - ref).max() <= 0.02 * np.abs(ref).max()
+
+
+def test_dense_mlp_oracle():
+    """orc_dense_mlp (modeling/gemma_4_moe_bq.mojo:749-783): equals its own
+    stages composed, the signed-dot form of bq_linear (the u8 x s8 - 128*colsum
+    identity, exact here), and a float64 restatement of the unquantised MLP
+    within the int8 quantisation tolerance."""
+    from helpers import raw_dense_np, oracle_dense_layer
+    raw = raw_dense_np(seed=31)
+    d = oracle_dense_layer(raw)
+    x = tokens_np(5, seed=8)
+    out, hb, hq, hs = O.dense_mlp(x, d)
+    xi8, xsa = O.bq_norm_quant(x, d["gamma"])
+    g = O.bq_linear(xi8, xsa, d["wg"], d["wgs"], d["wgcs"])
+    u = O.bq_linear(xi8, xsa, d["wu"], d["wus"], d["wucs"])
+    assert np.array_equal(O.gelu_gate_up(g, u), hb)
+    q, s = O.bq_block_quant(hb)
+    assert np.array_equal(q, hq) and np.array_equal(s, hs)
+    assert np.array_equal(O.bq_block_linear(hq, hs, d["wd"], d["wds"], d["wdcs"]), out)
+    # signed dots: f32(dot) * (sa/127) * sw, rounded to bf16
+    dot = xi8.astype(np.int64) @ d["wg"].astype(np.int64).T
+    ad = (xsa * np.float32(1.0 / 127.0)).astype(np.float32)
+    ref_g = O.f32_to_bf16((dot.astype(np.float32) * ad[:, None]) * d["wgs"][None, :])
+    assert np.array_equal(ref_g, g)
+    # float64 MLP on the raw weights
+    f = lambda a: O.bf16_to_f32(a).astype(np.float64)
+    xf = f(x)
+    xn = xf * (np.sqrt(H) / np.sqrt((xf * xf).sum(1, keepdims=True) + H * 1e-6)) * f(raw["pre_ffn_norm"])
+    gg, uu = xn @ f(raw["gate"]).T, xn @ f(raw["up"]).T
+    gel = 0.5 * gg * (1 + np.tanh(np.sqrt(2 / np.pi) * (gg + 0.044715 * gg ** 3)))
+    ref = (gel * uu) @ f(raw["down"]).T
+    got = f(out)
+    assert np.abs(got - ref).max() <= 0.03 * np.abs(ref).max()
