@@ -202,10 +202,17 @@ int gm_checkpoint_read_rows(const gm_checkpoint_t* ck, const char* name, int64_t
  * (members ".scale", quant/manifest.mojo:10-13,93-120), BF16 the original
  * checkpoint ([128][1408][2816] or folded).  Tensor names are `prefix` +
  * modeling/gemma4_topology.mojo:143-158 names; prefix NULL means
- * "model.language_model.layers.%d." with %d = ckpt_layer.  With
- * GM_LOAD_POST the post-MoE gains and layer_scalar are registered too
- * (gm_moe_register_post).  Synchronous. */
+ * "model.language_model.layers.%d." with %d = ckpt_layer.  Flags:
+ * GM_LOAD_POST also registers the post-MoE gains and layer_scalar
+ * (gm_moe_register_post); GM_LOAD_DENSE also registers the dense MLP
+ * (mlp.{gate,up,down}_proj.weight + pre_feedforward_layernorm.weight,
+ * gm_moe_register_dense_bq); GM_LOAD_QUANTIZE turns a BF16 checkpoint into
+ * the butterquant layer on the device, as the reference quantizer would
+ * (quant/quantizer.mojo:963-1114: per-row FWHT + int8 with the split gains,
+ * router centring), instead of registering bf16 experts.  Synchronous. */
 #define GM_LOAD_POST 1
+#define GM_LOAD_DENSE 2
+#define GM_LOAD_QUANTIZE 4
 int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* ck, int ckpt_layer,
                       const char* prefix, int flags);
 

@@ -590,8 +590,10 @@ struct Stager {
 // Device allocations of one load, freed on every exit path.
 struct DevTemps {
   std::vector<void*> ptrs;
-  ~DevTemps() {
+  ~DevTemps() { release(); }
+  void release() {
     for (void* p : ptrs) cudaFree(p);
+    ptrs.clear();
   }
   template <typename T>
   cudaError_t alloc(T** p, size_t count) {
@@ -674,6 +676,12 @@ struct Loader {
   int whole(const Tensor& t, T** dev, const char* what) {
     return to_device(t, 0, t.rows * t.cols, dev, what);
   }
+  // row-major int8 [rows][cols] -> a new VNNI-packed copy (butterquant/vnni.mojo:31-83)
+  int pack(const uint8_t* rm, int64_t rows, int cols, int8_t** packed, const char* what) {
+    int rc;
+    if ((rc = cuda(tmp.alloc(packed, (size_t)rows * cols), what))) return rc;
+    return cuda(launch_vnni_permute(reinterpret_cast<const int8_t*>(rm), rows, cols, *packed, 0, s), what);
+  }
 };
 
 }  // namespace
@@ -686,7 +694,8 @@ extern "C" int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* 
   if (layer < 0 || layer >= num_layers)
     return handle_fail(h, GM_EINVAL, "layer out of range");
   if (!ck) return handle_fail(h, GM_EINVAL, "NULL checkpoint");
-  if (flags & ~GM_LOAD_POST) return handle_fail(h, GM_EINVAL, "unknown load flags");
+  if (flags & ~(GM_LOAD_POST | GM_LOAD_DENSE | GM_LOAD_QUANTIZE))
+    return handle_fail(h, GM_EINVAL, "unknown load flags");
   Loader ld{h, ck, {}};
   {
     char buf[512];
@@ -711,6 +720,13 @@ extern "C" int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* 
   if (!bq && gu->dtype != GM_DTYPE_BF16)
     return ld.fail(GM_EINVAL, "%sexperts.gate_up_proj: dtype %s, expected I8 (butterquant) or BF16",
                    ld.prefix.c_str(), dtype_name(gu->dtype));
+  const bool quantize = (flags & GM_LOAD_QUANTIZE) != 0;
+  if (quantize && bq)
+    return ld.fail(GM_EINVAL, "GM_LOAD_QUANTIZE needs a BF16 checkpoint; this one is butterquant");
+  if ((flags & GM_LOAD_DENSE) && !bq && !quantize)
+    return ld.fail(GM_EINVAL, "the dense MLP runs in butterquant only: load a BF16 checkpoint's "
+                   "dense MLP with GM_LOAD_QUANTIZE");
+  // ---- every tensor is looked up (dtype and shape checked) before any transfer
   const Tensor *t_gu, *t_dn, *t_gus = nullptr, *t_dns = nullptr, *t_r, *t_rs, *t_pes, *t_g2;
   const int wdt = bq ? GM_DTYPE_I8 : GM_DTYPE_BF16;
   if ((rc = ld.lookup("experts.gate_up_proj", wdt, (int64_t)E * GU, H, &t_gu)) ||
@@ -730,6 +746,19 @@ extern "C" int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* 
        (rc = ld.lookup("post_feedforward_layernorm.weight", GM_DTYPE_BF16, H, 0, &t_p)) ||
        (rc = ld.lookup("layer_scalar", GM_DTYPE_BF16, 1, 0, &t_ls))))
     return rc;
+  const Tensor *t_dg = nullptr, *t_du = nullptr, *t_dd = nullptr, *t_dgs = nullptr, *t_dus = nullptr,
+               *t_dds = nullptr, *t_pf = nullptr;
+  if (flags & GM_LOAD_DENSE) {
+    if ((rc = ld.lookup("mlp.gate_proj.weight", wdt, DENSE_I, H, &t_dg)) ||
+        (rc = ld.lookup("mlp.up_proj.weight", wdt, DENSE_I, H, &t_du)) ||
+        (rc = ld.lookup("mlp.down_proj.weight", wdt, H, DENSE_I, &t_dd)) ||
+        (rc = ld.lookup("pre_feedforward_layernorm.weight", GM_DTYPE_BF16, H, 0, &t_pf)))
+      return rc;
+    if (bq && ((rc = ld.lookup("mlp.gate_proj.weight.scale", GM_DTYPE_F32, DENSE_I, 0, &t_dgs)) ||
+               (rc = ld.lookup("mlp.up_proj.weight.scale", GM_DTYPE_F32, DENSE_I, 0, &t_dus)) ||
+               (rc = ld.lookup("mlp.down_proj.weight.scale", GM_DTYPE_F32, H, 0, &t_dds))))
+      return rc;
+  }
 
   if ((rc = ld.cuda(cudaStreamCreateWithFlags(&ld.s, cudaStreamNonBlocking), "stream"))) return rc;
   struct StreamGuard {
@@ -743,7 +772,7 @@ extern "C" int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* 
   } sg{ld.s};
   if ((rc = ld.cuda(ld.st.init(), "pinned staging"))) return rc;
 
-  // this rank's row block of the expert tensors (modeling/loader.mojo:113-125)
+  // ---- experts: this rank's row block (modeling/loader.mojo:113-125)
   const int64_t gu_rows = (int64_t)epr * GU, dn_rows = (int64_t)epr * H;
   uint8_t *gu_w, *dn_w;  // int8 (bq) or bf16 bytes
   float *gu_s = nullptr, *dn_s = nullptr;
@@ -758,25 +787,47 @@ extern "C" int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* 
   if (bq && ((rc = ld.to_device(*t_gus, (int64_t)base * GU, gu_rows, &gu_s, "gate_up.scale")) ||
              (rc = ld.to_device(*t_dns, (int64_t)base * H, dn_rows, &dn_s, "down.scale"))))
     return rc;
-  // load-time transforms
+  // load-time transforms (router scale bake for every format)
   if ((rc = ld.cuda(ld.tmp.alloc(&rs_baked, H), "router scale")) ||
       (rc = ld.cuda(launch_bake(rs_raw, rs_baked, H, 1, ld.s), "router scale bake")))
     return rc;
   g2_use = g2_raw;
   int8_t *gu_p = nullptr, *dn_p = nullptr;
-  if (bq) {
+  uint16_t* router_use = router;
+  if (quantize) {
+    // the reference quantizer on the device (quant/quantizer.mojo:963-1051):
+    // MoeGateUp = PerRowQuant(128, SplitGamma(pre_feedforward_layernorm_2)),
+    // MoeDown = PerRowQuant(64), Router = SoftmaxRouterCenter
+    int8_t *gq, *dq;
+    if ((rc = ld.cuda(ld.tmp.alloc(&gq, (size_t)gu_rows * H), "gate_up quantize")) ||
+        (rc = ld.cuda(ld.tmp.alloc(&gu_s, (size_t)gu_rows), "gate_up quantize")) ||
+        (rc = ld.cuda(launch_quantize_rows(reinterpret_cast<const uint16_t*>(gu_w), gu_rows, H, g2_raw,
+                                           128, gq, gu_s, ld.s), "gate_up quantize")) ||
+        (rc = ld.cuda(ld.tmp.alloc(&dq, (size_t)dn_rows * I), "down quantize")) ||
+        (rc = ld.cuda(ld.tmp.alloc(&dn_s, (size_t)dn_rows), "down quantize")) ||
+        (rc = ld.cuda(launch_quantize_rows(reinterpret_cast<const uint16_t*>(dn_w), dn_rows, I, nullptr,
+                                           64, dq, dn_s, ld.s), "down quantize")) ||
+        (rc = ld.cuda(ld.tmp.alloc(&router_use, (size_t)E * H), "router center")) ||
+        (rc = ld.cuda(launch_router_center(router, E, H, router_use, ld.s), "router center")))
+      return rc;
+    gu_w = reinterpret_cast<uint8_t*>(gq);
+    dn_w = reinterpret_cast<uint8_t*>(dq);
+  }
+  if (bq || quantize) {
     if ((rc = ld.cuda(ld.tmp.alloc(&g2_use, H), "split gain")) ||
         (rc = ld.cuda(launch_bake(g2_raw, g2_use, H, 0, ld.s), "split gain bake")) ||
-        (rc = ld.cuda(ld.tmp.alloc(&gu_p, (size_t)gu_rows * H), "gate_up pack")) ||
-        (rc = ld.cuda(launch_vnni_permute(reinterpret_cast<const int8_t*>(gu_w), gu_rows, H, gu_p, 0, ld.s), "gate_up pack")) ||
-        (rc = ld.cuda(ld.tmp.alloc(&dn_p, (size_t)dn_rows * I), "down pack")) ||
-        (rc = ld.cuda(launch_vnni_permute(reinterpret_cast<const int8_t*>(dn_w), dn_rows, I, dn_p, 0, ld.s), "down pack")))
+        (rc = ld.pack(gu_w, gu_rows, H, &gu_p, "gate_up pack")) ||
+        (rc = ld.pack(dn_w, dn_rows, I, &dn_p, "down pack")))
       return rc;
   }
   if ((rc = ld.cuda(cudaStreamSynchronize(ld.s), "load"))) return rc;
-  rc = bq ? gm_moe_register_layer_bq(h, layer, gu_p, gu_s, dn_p, dn_s, router, rs_baked, pes, g2_use)
-          : gm_moe_register_layer_bf16(h, layer, gu_w, dn_w, router, rs_baked, pes, g2_use);
+  rc = (bq || quantize)
+           ? gm_moe_register_layer_bq(h, layer, gu_p, gu_s, dn_p, dn_s, router_use, rs_baked, pes, g2_use)
+           : gm_moe_register_layer_bf16(h, layer, gu_w, dn_w, router, rs_baked, pes, g2_use);
   if (rc) return rc;
+  ld.tmp.release();  // the expert temporaries are no longer needed
+
+  // ---- post-MoE gains
   if (flags & GM_LOAD_POST) {
     uint16_t *p1, *p2, *p;
     uint16_t ls_bits = 0;
@@ -789,6 +840,51 @@ extern "C" int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* 
     float ls;
     memcpy(&ls, &fbits, sizeof ls);
     if ((rc = gm_moe_register_post(h, layer, p1, p2, p, ls))) return rc;
+  }
+
+  // ---- dense MLP (modeling/gemma_4_moe_bq.mojo:749-783; DenseGateUp =
+  // PerRowQuant(128, SplitGamma(pre_feedforward_layernorm)), DenseDown =
+  // PerRowQuant(64), :113-116), replicated on every rank
+  if (flags & GM_LOAD_DENSE) {
+    uint8_t *dg, *du, *dd;
+    float *dgs = nullptr, *dus = nullptr, *dds = nullptr;
+    uint16_t *pf_raw, *pf;
+    if ((rc = ld.whole(*t_dg, &dg, "mlp.gate_proj")) || (rc = ld.whole(*t_du, &du, "mlp.up_proj")) ||
+        (rc = ld.whole(*t_dd, &dd, "mlp.down_proj")) ||
+        (rc = ld.whole(*t_pf, &pf_raw, "pre_feedforward_layernorm")))
+      return rc;
+    if (bq && ((rc = ld.whole(*t_dgs, &dgs, "mlp.gate_proj.scale")) ||
+               (rc = ld.whole(*t_dus, &dus, "mlp.up_proj.scale")) ||
+               (rc = ld.whole(*t_dds, &dds, "mlp.down_proj.scale"))))
+      return rc;
+    if (quantize) {
+      int8_t *gq, *uq, *dq;
+      if ((rc = ld.cuda(ld.tmp.alloc(&gq, (size_t)DENSE_I * H), "dense quantize")) ||
+          (rc = ld.cuda(ld.tmp.alloc(&dgs, DENSE_I), "dense quantize")) ||
+          (rc = ld.cuda(launch_quantize_rows(reinterpret_cast<const uint16_t*>(dg), DENSE_I, H, pf_raw,
+                                             128, gq, dgs, ld.s), "dense quantize")) ||
+          (rc = ld.cuda(ld.tmp.alloc(&uq, (size_t)DENSE_I * H), "dense quantize")) ||
+          (rc = ld.cuda(ld.tmp.alloc(&dus, DENSE_I), "dense quantize")) ||
+          (rc = ld.cuda(launch_quantize_rows(reinterpret_cast<const uint16_t*>(du), DENSE_I, H, pf_raw,
+                                             128, uq, dus, ld.s), "dense quantize")) ||
+          (rc = ld.cuda(ld.tmp.alloc(&dq, (size_t)H * DENSE_I), "dense quantize")) ||
+          (rc = ld.cuda(ld.tmp.alloc(&dds, H), "dense quantize")) ||
+          (rc = ld.cuda(launch_quantize_rows(reinterpret_cast<const uint16_t*>(dd), H, DENSE_I, nullptr,
+                                             64, dq, dds, ld.s), "dense quantize")))
+        return rc;
+      dg = reinterpret_cast<uint8_t*>(gq);
+      du = reinterpret_cast<uint8_t*>(uq);
+      dd = reinterpret_cast<uint8_t*>(dq);
+    }
+    int8_t *dgp, *dup, *ddp;
+    if ((rc = ld.cuda(ld.tmp.alloc(&pf, H), "split gain")) ||
+        (rc = ld.cuda(launch_bake(pf_raw, pf, H, 0, ld.s), "split gain bake")) ||
+        (rc = ld.pack(dg, DENSE_I, H, &dgp, "gate_proj pack")) ||
+        (rc = ld.pack(du, DENSE_I, H, &dup, "up_proj pack")) ||
+        (rc = ld.pack(dd, H, DENSE_I, &ddp, "down_proj pack")))
+      return rc;
+    if ((rc = ld.cuda(cudaStreamSynchronize(ld.s), "load"))) return rc;
+    if ((rc = gm_moe_register_dense_bq(h, layer, dgp, dgs, dup, dus, ddp, dds, pf))) return rc;
   }
   return GM_OK;
 }

@@ -253,21 +253,28 @@ class MoeBlock:
         check(lib().gm_moe_device_status(self.h, C.byref(e)), self.h)
         return e.value
 
-    def load_layer(self, layer, ckpt, ckpt_layer=None, prefix=None, post=False):
+    def load_layer(self, layer, ckpt, ckpt_layer=None, prefix=None, post=False, dense=False,
+                   quantize=False):
         """One MoE layer from a Checkpoint (this handle's experts, load-time
         bakes and packing included); the format follows the file's
         experts.gate_up_proj dtype.  prefix None: the reference's
-        "model.language_model.layers.%d." with %d = ckpt_layer (default: layer)."""
+        "model.language_model.layers.%d." with %d = ckpt_layer (default: layer).
+        post / dense: also the post-MoE gains / the dense MLP; quantize: a BF16
+        checkpoint becomes the butterquant layer on the device."""
         if ckpt_layer is None:
             ckpt_layer = layer
+        flags = (LOAD_POST if post else 0) | (LOAD_DENSE if dense else 0) | \
+                (LOAD_QUANTIZE if quantize else 0)
         check(lib().gm_moe_load_layer(self.h, layer, ckpt.h, ckpt_layer,
-                                      prefix.encode() if prefix is not None else None,
-                                      LOAD_POST if post else 0), self.h)
+                                      prefix.encode() if prefix is not None else None, flags),
+              self.h)
 
 
 DTYPES = {1: "BOOL", 2: "U8", 3: "I8", 4: "I16", 5: "U16", 6: "F16", 7: "BF16", 8: "I32", 9: "U32",
           10: "F32", 11: "I64", 12: "U64", 13: "F64", 14: "F8_E4M3", 15: "F8_E5M2"}
 LOAD_POST = 1
+LOAD_DENSE = 2
+LOAD_QUANTIZE = 4
 CKPT_MAX_DIMS = 8
 
 

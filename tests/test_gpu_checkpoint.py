@@ -127,3 +127,97 @@ def test_load_bf16_layer_matches_register(tmp_path):
     ref.close()
     got.close()
     ck.close()
+
+
+def dense_entries(rawd, Ld, layer, quantized):
+    p = PFX % layer
+    if quantized:
+        return [
+            (p + "mlp.gate_proj.weight", host(Ld["gate_rowmajor"]), None, None),
+            (p + "mlp.gate_proj.weight.scale", host(Ld["gate_scale"]), None, None),
+            (p + "mlp.up_proj.weight", host(Ld["up_rowmajor"]), None, None),
+            (p + "mlp.up_proj.weight.scale", host(Ld["up_scale"]), None, None),
+            (p + "mlp.down_proj.weight", host(Ld["down_rowmajor"]), None, None),
+            (p + "mlp.down_proj.weight.scale", host(Ld["down_scale"]), None, None),
+            (p + "pre_feedforward_layernorm.weight", host(rawd["pre_ffn_norm"]), None, [H, 1]),
+        ]
+    return [
+        (p + "mlp.gate_proj.weight", host(rawd["gate"]), None, None),
+        (p + "mlp.up_proj.weight", host(rawd["up"]), None, None),
+        (p + "mlp.down_proj.weight", host(rawd["down"]), None, None),
+        (p + "pre_feedforward_layernorm.weight", host(rawd["pre_ffn_norm"]), None, None),
+    ]
+
+
+def register_all(blk, L, Ld, gains, ls):
+    blk.register_bq(0, L["gate_up"], L["gate_up_scale"], L["down"], L["down_scale"],
+                    L["router_centered"], L["router_scale"], L["per_expert_scale"], L["pre_ffn_norm_2"])
+    blk.register_post(0, gains[0].cuda(), gains[1].cuda(), gains[2].cuda(), float(ls.float()))
+    blk.register_dense(0, Ld["gate"], Ld["gate_scale"], Ld["up"], Ld["up_scale"], Ld["down"],
+                       Ld["down_scale"], Ld["pre_ffn_norm"])
+
+
+def ffn(blk, T, seed):
+    x = synth.make_tokens(T, seed=seed, device="cuda")
+    blk.ffn_forward(0, x, T)
+    torch.cuda.synchronize()
+    return host(x)
+
+
+def test_load_bq_ffn_with_dense_matches_register(tmp_path):
+    """A butterquant file with the dense MLP: GM_LOAD_POST | GM_LOAD_DENSE
+    gives the same whole-FFN output as registering the same tensors."""
+    raw = synth.make_layer(seed=808, device="cuda", router_std=1.0, stress_gains=True)
+    L = synth.bq_layer(raw, keep_rowmajor=True)
+    rawd = synth.make_dense(seed=909, device="cuda")
+    Ld = synth.dense_layer(rawd, keep_rowmajor=True)
+    gains, ls = post_gains(12)
+    path = write_safetensors(tmp_path / "model.safetensors",
+                             bq_entries(raw, L, 2, gains, ls) + dense_entries(rawd, Ld, 2, True))
+    ck = gmoe.Checkpoint(path)
+    ref, got = gmoe.MoeBlock(700, 1), gmoe.MoeBlock(700, 1)
+    register_all(ref, L, Ld, gains, ls)
+    got.load_layer(0, ck, ckpt_layer=2, post=True, dense=True)
+    for T in (12, 700):
+        assert np.array_equal(ffn(ref, T, T), ffn(got, T, T))
+    with pytest.raises(gmoe.GmoeError, match="BF16 checkpoint"):
+        got.load_layer(0, ck, ckpt_layer=2, quantize=True)
+    ref.close()
+    got.close()
+    ck.close()
+
+
+def test_load_bf16_checkpoint_quantized_on_device(tmp_path):
+    """GM_LOAD_QUANTIZE: a BF16 checkpoint (experts, router, norms, dense MLP)
+    becomes the butterquant layer on the device, bit-identical to the layer
+    the on-device restatement of the reference quantizer produces."""
+    raw = synth.make_layer(seed=1001, device="cuda", router_std=1.0, stress_gains=True)
+    rawd = synth.make_dense(seed=1002, device="cuda")
+    gains, ls = post_gains(13)
+    p = PFX % 0
+    entries = [
+        (p + "experts.gate_up_proj", host(raw["gate_up"]), None, None),
+        (p + "experts.down_proj", host(raw["down"]), None, None),
+        (p + "router.proj.weight", host(raw["router_proj"]), None, None),
+        (p + "router.scale", host(raw["router_scale"]), None, None),
+        (p + "router.per_expert_scale", host(raw["per_expert_scale"]), None, None),
+        (p + "pre_feedforward_layernorm_2.weight", host(raw["pre_ffn_norm_2"]), None, None),
+        (p + "post_feedforward_layernorm_1.weight", host(gains[0]), None, None),
+        (p + "post_feedforward_layernorm_2.weight", host(gains[1]), None, None),
+        (p + "post_feedforward_layernorm.weight", host(gains[2]), None, None),
+        (p + "layer_scalar", host(ls), None, None),
+    ] + dense_entries(rawd, None, 0, False)
+    path = write_safetensors(tmp_path / "bf16.safetensors", entries)
+    ck = gmoe.Checkpoint(path)
+    L = synth.bq_layer(raw)
+    Ld = synth.dense_layer(rawd)
+    ref, got = gmoe.MoeBlock(640, 1), gmoe.MoeBlock(640, 1)
+    register_all(ref, L, Ld, gains, ls)
+    got.load_layer(0, ck, post=True, dense=True, quantize=True)
+    for T in (7, 640):
+        assert np.array_equal(ffn(ref, T, 50 + T), ffn(got, T, 50 + T))
+    with pytest.raises(gmoe.GmoeError, match="GM_LOAD_QUANTIZE"):
+        got.load_layer(0, ck, dense=True)
+    ref.close()
+    got.close()
+    ck.close()
