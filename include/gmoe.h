@@ -421,6 +421,56 @@ int gm_bq_dense_gate_up(const int8_t* x_i8, const float* x_sa, int T, const void
 int gm_bq_block_linear(const int8_t* h_i8, const float* h_sa, int T, const void* down_proj,
                        const float* down_scale, void* out, void* stream);
 
+/* ------------------------------------------------------ bq attention --
+ * Decode attention of the butterquant model over its int8, FWHT-rotated,
+ * paged KV cache.  Cache layout as the reference's (modeling/
+ * gemma_4_moe_bq.mojo:123-160 KV slot groups): k/v int8 [rows][num_kv *
+ * head_dim], k/v scales f32 [rows][num_kv] (the head's absmax).  Row of
+ * position p (kernels/attention_ops.mojo:41-52 PagedKV):
+ *   base_rows[run.rows_off + ((p >> page_shift) & page_mask)] + (p & row_mask)
+ * with page_mask = pages-1 for the sliding ring and -1 for full layers.
+ * Head geometries (modeling/gemma4_common.mojo:9-20): sliding head_dim 256,
+ * rope_half 128, pair_stride 128; full head_dim 512, rope_half 64,
+ * pair_stride 256 (others are refused).  All pointers are device memory. */
+typedef struct gm_kv_run { /* kernels/attention_ops.mojo:55-60 KVRun */
+  int32_t buf_start;  /* first token of the run in the batch */
+  int32_t base_pos;   /* position of that token */
+  int32_t rows_off;   /* first entry of the run's page list in base_rows */
+  int32_t page_count;
+} gm_kv_run_t;
+
+/* dispatch_bq_attn_prep (butterquant_kernels/attention.mojo:474-610): T
+ * tokens of q_src bf16 [T][num_q*head_dim], k_src / v_src bf16
+ * [T][num_kv*head_dim] (v_src = k_src for the full layers) -> q_i8 [T][num_q *
+ * head_dim], qi_bias = 128*sum(q_i8) and f_q = absmax [T][num_q], and the K/V
+ * cache rows of the positions this rank holds (pos % cache_degree == rank).
+ * cos/sin f32 [positions][rope_half].  Bit-identical to the reference's
+ * 16-lane arithmetic. */
+int gm_bq_attn_prep(const void* q_src, const void* k_src, const void* v_src, const void* q_norm,
+                    const void* k_norm, int8_t* q_i8, float* qi_bias, float* f_q, int8_t* k_cache,
+                    float* k_scale, int8_t* v_cache, float* v_scale, const float* cos_table,
+                    const float* sin_table, const gm_kv_run_t* runs, int num_runs,
+                    const int32_t* base_rows, int T, int head_dim, int num_q, int num_kv,
+                    int rope_half, int pair_stride, int cache_degree, int rank, int page_shift,
+                    int row_mask, int page_mask, void* stream);
+
+/* The decode path of dispatch_bq_sliding_attention / dispatch_bq_full_attention
+ * (attention.mojo:333-472, kernels/attention_dispatch_kernels.mojo:36-130):
+ * T tokens, token t the newest position of run t (runs[t].buf_start = t).
+ * Sliding (window > 0): the last min(pos+1, window) positions; full (window =
+ * 0): this rank's positions 0..pos.  The KV range is split over CTAs and the
+ * splits merged as kernels/logsum_merge.mojo does; out bf16 [T][num_q *
+ * head_dim], in the rotated domain as the reference's.  The signed int8 dot
+ * needs no qi_bias.  max_kv_len bounds the KV length of any token (sizes the
+ * split count); workspace of gm_bq_attention_workspace_bytes. */
+int gm_bq_attention_decode(const int8_t* q_i8, const float* f_q, const int8_t* k_cache,
+                           const float* k_scale, const int8_t* v_cache, const float* v_scale,
+                           const gm_kv_run_t* runs, const int32_t* base_rows, int T, int head_dim,
+                           int num_q, int num_kv, int window, int cache_degree, int rank,
+                           int page_shift, int row_mask, int page_mask, int max_kv_len, void* out,
+                           float* workspace, size_t workspace_bytes, void* stream);
+size_t gm_bq_attention_workspace_bytes(int T, int head_dim, int num_q, int num_kv, int max_kv_len);
+
 /* butterquant/vnni.mojo:31-83 pack (and its inverse). rows%32 == 0, cols%64 == 0. */
 int gm_vnni_pack(const int8_t* q, long rows, int cols, int8_t* packed, void* stream);
 int gm_vnni_unpack(const int8_t* packed, long rows, int cols, int8_t* q, void* stream);

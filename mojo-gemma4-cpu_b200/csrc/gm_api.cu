@@ -1382,6 +1382,68 @@ int gm_bq_block_linear(const int8_t* h_i8, const float* h_sa, int T, const void*
         "bq_block_linear");
 }
 
+namespace {
+int check_attn_geometry(int head_dim, int num_q, int num_kv, int cache_degree, int rank) {
+  if (head_dim != 256 && head_dim != 512)
+    return set_err(nullptr, GM_EINVAL, "attention: head_dim %d (256 or 512)", head_dim);
+  if (num_q < 1 || num_kv < 1 || num_q % num_kv || (num_q / num_kv) % 2 || (num_q / num_kv) > 8)
+    return set_err(nullptr, GM_EINVAL, "attention: num_q %d / num_kv %d (an even ratio <= 8)", num_q,
+                   num_kv);
+  if (cache_degree < 1 || rank < 0 || rank >= cache_degree)
+    return set_err(nullptr, GM_EINVAL, "attention: cache_degree %d rank %d", cache_degree, rank);
+  return GM_OK;
+}
+}  // namespace
+
+int gm_bq_attn_prep(const void* q_src, const void* k_src, const void* v_src, const void* q_norm,
+                    const void* k_norm, int8_t* q_i8, float* qi_bias, float* f_q, int8_t* k_cache,
+                    float* k_scale, int8_t* v_cache, float* v_scale, const float* cos_table,
+                    const float* sin_table, const gm_kv_run_t* runs, int num_runs,
+                    const int32_t* base_rows, int T, int head_dim, int num_q, int num_kv,
+                    int rope_half, int pair_stride, int cache_degree, int rank, int page_shift,
+                    int row_mask, int page_mask, void* stream) {
+  int rc = check_attn_geometry(head_dim, num_q, num_kv, cache_degree, rank);
+  if (rc) return rc;
+  if (T < 0 || (T > 0 && num_runs < 1)) return set_err(nullptr, GM_EINVAL, "attn_prep: T=%d runs=%d", T, num_runs);
+  if (!((head_dim == 256 && rope_half == 128 && pair_stride == 128) ||
+        (head_dim == 512 && rope_half == 64 && pair_stride == 256)))
+    return set_err(nullptr, GM_EINVAL, "attn_prep: head_dim %d rope_half %d pair_stride %d is not a "
+                   "Gemma-4 geometry", head_dim, rope_half, pair_stride);
+  STAGE(launch_attn_prep(static_cast<const uint16_t*>(q_src), static_cast<const uint16_t*>(k_src),
+                         static_cast<const uint16_t*>(v_src), static_cast<const uint16_t*>(q_norm),
+                         static_cast<const uint16_t*>(k_norm), q_i8, qi_bias, f_q, k_cache, k_scale, v_cache,
+                         v_scale, cos_table, sin_table, runs, num_runs, base_rows, T, head_dim, num_q, num_kv,
+                         rope_half, pair_stride, cache_degree, rank, page_shift, row_mask, page_mask,
+                         S(stream)),
+        "bq_attn_prep");
+}
+
+size_t gm_bq_attention_workspace_bytes(int T, int head_dim, int num_q, int num_kv, int max_kv_len) {
+  if (T <= 0 || num_kv <= 0) return 0;
+  return attention_workspace_floats(T, head_dim, num_q, num_kv, max_kv_len) * sizeof(float);
+}
+
+int gm_bq_attention_decode(const int8_t* q_i8, const float* f_q, const int8_t* k_cache,
+                           const float* k_scale, const int8_t* v_cache, const float* v_scale,
+                           const gm_kv_run_t* runs, const int32_t* base_rows, int T, int head_dim,
+                           int num_q, int num_kv, int window, int cache_degree, int rank,
+                           int page_shift, int row_mask, int page_mask, int max_kv_len, void* out,
+                           float* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_attn_geometry(head_dim, num_q, num_kv, cache_degree, rank);
+  if (rc) return rc;
+  if (T < 0 || window < 0 || max_kv_len < 0)
+    return set_err(nullptr, GM_EINVAL, "attention_decode: T=%d window=%d max_kv_len=%d", T, window,
+                   max_kv_len);
+  const size_t need = gm_bq_attention_workspace_bytes(T, head_dim, num_q, num_kv, max_kv_len);
+  if (workspace_bytes < need)
+    return set_err(nullptr, GM_EINVAL, "attention_decode: workspace %zu bytes, %zu needed", workspace_bytes,
+                   need);
+  STAGE(launch_attn_decode(q_i8, f_q, k_cache, k_scale, v_cache, v_scale, runs, base_rows, T, head_dim, num_q,
+                           num_kv, window, cache_degree, rank, page_shift, row_mask, page_mask, max_kv_len,
+                           workspace, static_cast<uint16_t*>(out), S(stream)),
+        "bq_attention_decode");
+}
+
 int gm_phase1_gate_up_bf16(const void* x_normed, const int32_t* expert_offset,
                            const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr,
                            int T, const void* gate_up, void* bucket, void* stream) {

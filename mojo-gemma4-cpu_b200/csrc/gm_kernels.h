@@ -139,6 +139,22 @@ cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t
 cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
                              int epr, int T, const float* bsa, const SparseRoute* routes,
                              const float* dn_scale, float* ybuf, int* err, cudaStream_t s);
+// butterquant attention (attention_bq.cu).  runs: device array of
+// {buf_start, base_pos, rows_off, page_count} (gm_kv_run_t)
+cudaError_t launch_attn_prep(const uint16_t* q_src, const uint16_t* k_src, const uint16_t* v_src,
+                             const uint16_t* q_norm, const uint16_t* k_norm, int8_t* q_i8, float* qi_bias,
+                             float* f_q, int8_t* k_cache, float* k_scale, int8_t* v_cache, float* v_scale,
+                             const float* cos_table, const float* sin_table, const void* runs, int num_runs,
+                             const int32_t* base_rows, int T, int head_dim, int num_q, int num_kv,
+                             int rope_half, int pair_stride, int cache_degree, int rank, int shift,
+                             int row_mask, int page_mask, cudaStream_t s);
+cudaError_t launch_attn_decode(const int8_t* q_i8, const float* f_q, const int8_t* k_cache,
+                               const float* k_scale, const int8_t* v_cache, const float* v_scale,
+                               const void* runs, const int32_t* base_rows, int T, int head_dim, int num_q,
+                               int num_kv, int window, int cache_degree, int rank, int shift, int row_mask,
+                               int page_mask, int max_kv_len, float* partials, uint16_t* out, cudaStream_t s);
+int attention_splits(int T, int num_kv, int max_kv_len);
+size_t attention_workspace_floats(int T, int head_dim, int num_q, int num_kv, int max_kv_len);
 // tcgen05 path of the dense MLP (gemm_tc.cu): maps over the activation rows
 // (int8 [rows][2816], 128-row boxes), the row-major gate|up weight ([4224][2816],
 // 64-row boxes), h (int8 [rows][2112], 128-row boxes) and the row-major down

@@ -651,6 +651,202 @@ void orc_dense_mlp(const uint16_t* x, int T, const uint16_t* gamma, int inter,
   if (h_sa) std::memcpy(h_sa, qs.data(), qs.size() * 4);
 }
 
+// ------------------------------------------------------------ bq attention
+// The reference's SIMD width on its AVX-512 hosts (W = 16 f32 lanes) fixes
+// the order of its per-head reductions; the restatement keeps it: element e
+// lives in lane e % 16 of register e / 16.
+constexpr int ATT_W = 16;
+
+// SIMD.reduce_add / reduce_max of 16 lanes: halving tree v[i] op v[i + w/2].
+inline float lane_tree_sum(float* v) {
+  for (int w = ATT_W / 2; w >= 1; w >>= 1)
+    for (int i = 0; i < w; ++i) v[i] = v[i] + v[i + w];
+  return v[0];
+}
+
+// butterquant/head_prep.mojo:9-37 head_inv_rms (sqrt_n = sqrt_f32(head_dim),
+// n_eps = f32(head_dim) * f32(1e-6)) and absmax_quantize_head.
+inline float head_inv_rms(const float* r, int head_dim) {
+  float lanes[ATT_W];
+  const int regs = head_dim / ATT_W;
+  for (int l = 0; l < ATT_W; ++l) {
+    float s = r[l] * r[l];
+    for (int ri = 1; ri < regs; ++ri) s = std::fmaf(r[ri * ATT_W + l], r[ri * ATT_W + l], s);
+    lanes[l] = s;
+  }
+  const float sqrt_n = std::sqrt((float)head_dim);
+  const float n_eps = (float)head_dim * 1e-6f;
+  return sqrt_n / std::sqrt(lane_tree_sum(lanes) + n_eps);
+}
+
+inline float absmax_quantize_head(const float* r, int head_dim, int8_t* q, int32_t* qsum) {
+  float amax = 0.0f;
+  for (int e = 0; e < head_dim; ++e) amax = std::max(amax, std::fabs(r[e]));
+  if (amax < 1e-10f) amax = 1e-10f;
+  const float inv = 127.0f / amax;
+  int32_t s = 0;
+  for (int e = 0; e < head_dim; ++e) {
+    q[e] = quantize_i8(r[e], inv);
+    s += q[e];
+  }
+  if (qsum) *qsum = s;
+  return amax;
+}
+
+// butterquant/head_prep.mojo:40-75 prep_head_qk_i8 (gamma != NULL, rope over
+// rope_half lanes pairing e with e + pair_stride) and :78-97 prep_head_v_i8
+// (gamma == NULL: no gain, no rope): RMSNorm, RoPE, FWHT over the head, int8.
+float orc_prep_head(const uint16_t* src, const uint16_t* gamma, const float* cos, const float* sin,
+                    int head_dim, int rope_half, int pair_stride, int8_t* q_out, int32_t* qsum) {
+  std::vector<float> r(head_dim);
+  for (int e = 0; e < head_dim; ++e) r[e] = bf2f(src[e]);
+  const float inv = head_inv_rms(r.data(), head_dim);
+  for (int e = 0; e < head_dim; ++e) r[e] = gamma ? (r[e] * inv) * bf2f(gamma[e]) : r[e] * inv;
+  if (gamma) {
+    for (int e = 0; e < rope_half; ++e) {
+      const float lo = r[e], hi = r[pair_stride + e];
+      r[e] = lo * cos[e] - hi * sin[e];
+      r[pair_stride + e] = hi * cos[e] + lo * sin[e];
+    }
+  }
+  fwht_block(r.data(), head_dim);
+  return absmax_quantize_head(r.data(), head_dim, q_out, qsum);
+}
+
+// butterquant_kernels/attention.mojo:474-560 BqAttnPrepKernel for tokens at
+// positions pos[t]: q heads -> q_i8, qi_bias = 128*sum(q), f_q = amax; k and
+// v heads into cache row slot[t] (skipped when slot[t] < 0).  v_src may equal
+// k_src (the full layers' shared K/V projection).
+void orc_bq_attn_prep(const uint16_t* q_src, const uint16_t* k_src, const uint16_t* v_src,
+                      const uint16_t* q_norm, const uint16_t* k_norm, int T, const int32_t* pos,
+                      const int32_t* slot, int head_dim, int num_q, int num_kv, int rope_half,
+                      int pair_stride, const float* cos_table, const float* sin_table, int8_t* q_i8,
+                      float* qi_bias, float* f_q, int8_t* k_cache, float* k_scale, int8_t* v_cache,
+                      float* v_scale) {
+  const long qs = (long)num_q * head_dim, kvs = (long)num_kv * head_dim;
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    const float* c = cos_table + (long)pos[t] * rope_half;
+    const float* sn = sin_table + (long)pos[t] * rope_half;
+    for (int h = 0; h < num_q; ++h) {
+      int32_t qsum = 0;
+      f_q[(long)t * num_q + h] = orc_prep_head(q_src + t * qs + (long)h * head_dim, q_norm, c, sn,
+                                               head_dim, rope_half, pair_stride,
+                                               q_i8 + t * qs + (long)h * head_dim, &qsum);
+      qi_bias[(long)t * num_q + h] = (float)qsum * 128.0f;
+    }
+    if (slot[t] < 0) continue;
+    const long row = slot[t];
+    for (int h = 0; h < num_kv; ++h) {
+      k_scale[row * num_kv + h] = orc_prep_head(k_src + t * kvs + (long)h * head_dim, k_norm, c, sn,
+                                                head_dim, rope_half, pair_stride,
+                                                k_cache + row * kvs + (long)h * head_dim, nullptr);
+      v_scale[row * num_kv + h] = orc_prep_head(v_src + t * kvs + (long)h * head_dim, nullptr, c, sn,
+                                                head_dim, 0, 0, v_cache + row * kvs + (long)h * head_dim,
+                                                nullptr);
+    }
+  }
+}
+
+// Flash decode over int8 K/V (butterquant_kernels/attention.mojo:33-146
+// bq_process_kv_tile + BqFlashAttentionKernel, kernels/attention_ops.mojo:
+// 196-212 online_softmax_tile with TILE = 16), the KV range of each token
+// split into n_splits worker ranges (kernels/helpers.mojo:182-190
+// worker_range), then kernels/logsum_merge.mojo:29-117 merge_segments /
+// write_finalized_head.  slots: per token, kv_len[t] cache rows in position
+// order (row-major [T][max_kv]).  out bf16 [T][num_q*head_dim].
+void orc_bq_flash_decode(const int8_t* q_i8, const float* qi_bias, const float* f_q,
+                         const int8_t* k_cache, const float* k_scale, const int8_t* v_cache,
+                         const float* v_scale, int T, const int32_t* slots, const int32_t* kv_len,
+                         int max_kv, int head_dim, int num_q, int num_kv, int n_splits, uint16_t* out) {
+  const float inv127 = 1.0f / 127.0f;
+  const float inv127sq = inv127 * inv127;
+  const int gqa = num_q / num_kv;
+  const long kvs = (long)num_kv * head_dim;
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+  for (int t = 0; t < T; ++t) {
+    for (int h = 0; h < num_q; ++h) {
+      const int g = h / gqa;
+      const int8_t* q = q_i8 + ((long)t * num_q + h) * head_dim;
+      const float qb = qi_bias[(long)t * num_q + h], fq = f_q[(long)t * num_q + h];
+      const int32_t* sl = slots + (long)t * max_kv;
+      std::vector<float> pm(n_splits), pl(n_splits), pacc((size_t)n_splits * head_dim);
+      for (int s = 0; s < n_splits; ++s) {
+        const int per = (kv_len[t] + n_splits - 1) / n_splits;
+        int b = s * per, e = std::min(b + per, kv_len[t]);
+        if (b >= kv_len[t]) b = e = kv_len[t];
+        float m = -1e30f, l = 0.0f;
+        float* acc = pacc.data() + (size_t)s * head_dim;
+        for (int i = 0; i < head_dim; ++i) acc[i] = 0.0f;
+        for (int p = b; p < e; p += ATT_W) {
+          const int tl = std::min(ATT_W, e - p);
+          float sc[ATT_W];
+          for (int j = 0; j < ATT_W; ++j) sc[j] = -1e30f;
+          for (int j = 0; j < tl; ++j) {
+            const long row = sl[p + j];
+            const int8_t* k = k_cache + row * kvs + (long)g * head_dim;
+            int32_t r = 0;  // u8(k ^ 0x80) x s8(q): the shifted VNNI dot
+            for (int i = 0; i < head_dim; ++i) r += (int32_t)(uint8_t)(k[i] ^ 0x80u) * (int32_t)q[i];
+            const float ks = k_scale[row * num_kv + g];
+            sc[j] = ((((float)r - qb) * fq) * ks) * inv127sq;
+          }
+          float tmax = sc[0];
+          for (int j = 1; j < ATT_W; ++j) tmax = std::max(tmax, sc[j]);
+          const float m_new = tmax > m ? tmax : m;
+          const float corr = fast_exp_softmax_biased(std::max(-87.0f, m - m_new));
+          float w[ATT_W], wsum[ATT_W];
+          for (int j = 0; j < ATT_W; ++j) {
+            w[j] = fast_exp_softmax_biased(std::max(-87.0f, sc[j] - m_new));
+            wsum[j] = w[j];
+          }
+          for (int i = 0; i < head_dim; ++i) acc[i] = acc[i] * corr;
+          l = l * corr + lane_tree_sum(wsum);
+          m = m_new;
+          for (int j = 0; j < tl; ++j) {
+            const long row = sl[p + j];
+            const int8_t* v = v_cache + row * kvs + (long)g * head_dim;
+            const float wv = (w[j] * v_scale[row * num_kv + g]) * inv127;
+            for (int i = 0; i < head_dim; ++i) acc[i] = std::fmaf((float)v[i], wv, acc[i]);
+          }
+        }
+        pm[s] = m;
+        pl[s] = l;
+      }
+      // merge (batches of 16 partials)
+      float gm = -1e30f;
+      for (int s = 0; s < n_splits; ++s) gm = pm[s] > gm ? pm[s] : gm;
+      float gl = 0.0f;
+      bool first = true;
+      std::vector<float> acc(head_dim, 0.0f);
+      for (int b0 = 0; b0 < n_splits; b0 += ATT_W) {
+        const int bl = std::min(ATT_W, n_splits - b0);
+        float c[ATT_W], lc[ATT_W];
+        for (int j = 0; j < ATT_W; ++j) {
+          const float d = j < bl ? pm[b0 + j] - gm : -1e30f;
+          const float ls = j < bl ? pl[b0 + j] : 0.0f;
+          c[j] = fast_exp_softmax_biased(std::max(-87.0f, d));
+          if (!(ls > 0.0f)) c[j] = 0.0f;
+          lc[j] = ls * c[j];
+        }
+        gl += lane_tree_sum(lc);
+        for (int j = 0; j < bl; ++j) {
+          if (c[j] <= 0.0f) continue;
+          const float* src = pacc.data() + (size_t)(b0 + j) * head_dim;
+          for (int i = 0; i < head_dim; ++i) acc[i] = first ? src[i] * c[j] : std::fmaf(src[i], c[j], acc[i]);
+          first = false;
+        }
+      }
+      uint16_t* o = out + ((long)t * num_q + h) * head_dim;
+      if (!(gl > 0.0f)) {
+        for (int i = 0; i < head_dim; ++i) o[i] = 0;
+      } else {
+        const float il = 1.0f / gl;
+        for (int i = 0; i < head_dim; ++i) o[i] = f2bf(acc[i] * il);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------ whole block
 struct OrcBqLayer {
   const uint16_t* router_centered;  // [E][H] bf16 (router_center_softmax)

@@ -76,6 +76,10 @@ def _declare(L):
         "orc_gelu_gate_up": (None, [vp, vp, i64, vp]),
         "orc_bq_block_linear": (None, [vp, vp, i32, i32, vp, vp, vp, i32, vp]),
         "orc_dense_mlp": (None, [vp, i32, vp, i32] + [vp] * 9 + [vp, vp, vp, vp]),
+        "orc_prep_head": (f32, [vp, vp, vp, vp, i32, i32, i32, vp, vp]),
+        "orc_bq_attn_prep": (None, [vp, vp, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, i32, vp, vp]
+                             + [vp] * 7),
+        "orc_bq_flash_decode": (None, [vp] * 7 + [i32, vp, vp, i32, i32, i32, i32, i32, vp]),
         "orc_bq_moe_forward": (i32, [vp, i32, vp, i32, vp, vp, vp, vp]),
         "orc_bf16_moe_forward": (i32, [vp, i32, vp, i32, vp, vp, vp, vp]),
         "orc_num_threads": (i32, []),
@@ -325,3 +329,40 @@ def bf16_forward(x, layer, degree=1):
                                     _p(out), _p(idx), _p(w), _p(lg))
     assert rc == 0
     return out, idx, w, lg
+
+
+# ------------------------------------------------------------ bq attention
+def bq_attn_prep(q_src, k_src, v_src, q_norm, k_norm, pos, slot, head_dim, num_q, num_kv,
+                 rope_half, pair_stride, cos_table, sin_table, n_slots):
+    """BqAttnPrepKernel for T tokens: returns q_i8, qi_bias, f_q and the K/V
+    cache rows (int8 [n_slots][num_kv*head_dim], scales [n_slots][num_kv]) with
+    the tokens' rows written at slot[t] (rows not written stay zero)."""
+    T = q_src.shape[0]
+    q_i8 = np.zeros((T, num_q * head_dim), np.int8)
+    qb = np.zeros((T, num_q), np.float32)
+    fq = np.zeros((T, num_q), np.float32)
+    kc = np.zeros((n_slots, num_kv * head_dim), np.int8)
+    ks = np.zeros((n_slots, num_kv), np.float32)
+    vc = np.zeros_like(kc)
+    vs = np.zeros_like(ks)
+    a = [np.ascontiguousarray(v) for v in (q_src, k_src, v_src, q_norm, k_norm)]
+    lib().orc_bq_attn_prep(*[_p(v) for v in a], T, _p(np.ascontiguousarray(pos, np.int32)),
+                           _p(np.ascontiguousarray(slot, np.int32)), head_dim, num_q, num_kv,
+                           rope_half, pair_stride, _p(np.ascontiguousarray(cos_table, np.float32)),
+                           _p(np.ascontiguousarray(sin_table, np.float32)), _p(q_i8), _p(qb), _p(fq),
+                           _p(kc), _p(ks), _p(vc), _p(vs))
+    return q_i8, qb, fq, kc, ks, vc, vs
+
+
+def bq_flash_decode(q_i8, qi_bias, f_q, k_cache, k_scale, v_cache, v_scale, slots, kv_len,
+                    head_dim, num_q, num_kv, n_splits=1):
+    """Flash decode of T query tokens over their cache rows `slots`
+    ([T][max_kv], position order, kv_len[t] valid) with n_splits worker
+    ranges merged as the reference does; bf16 [T][num_q*head_dim]."""
+    T = q_i8.shape[0]
+    slots = np.ascontiguousarray(slots, np.int32)
+    out = np.empty((T, num_q * head_dim), np.uint16)
+    a = [np.ascontiguousarray(v) for v in (q_i8, qi_bias, f_q, k_cache, k_scale, v_cache, v_scale)]
+    lib().orc_bq_flash_decode(*[_p(v) for v in a], T, _p(slots), _p(np.ascontiguousarray(kv_len, np.int32)),
+                              slots.shape[1], head_dim, num_q, num_kv, n_splits, _p(out))
+    return out

@@ -1,0 +1,148 @@
+"""Butterquant decode attention on the GPU (gm_bq_attn_prep,
+gm_bq_attention_decode) against the oracle's restatement of the reference's
+attention (butterquant_kernels/attention.mojo, kernels/attention_ops.mojo,
+kernels/logsum_merge.mojo).
+
+The prep (RMSNorm, RoPE, FWHT, int8 into the paged cache) is bit-identical.
+The decode output is a sum of exponentially weighted V rows whose order of
+accumulation differs from the reference's 16-position tiles (as the
+reference's own output differs between worker counts), so it is checked
+within 1e-2 of max|ref| against the oracle and against a float64 softmax."""
+import numpy as np
+import pytest
+import torch
+
+import gmoe
+from oracle import oracle as O
+from test_attention_oracle import SLIDING, FULL, bf, rope_tables, random_cache, decode_f64
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")]
+
+PAGE = 64
+SHIFT = 6
+
+
+def dev(a):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16)).cuda().view(torch.bfloat16)
+    return torch.from_numpy(a).cuda()
+
+
+def host(t):
+    t = t.detach().cpu()
+    return t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+
+
+def runs_array(runs):
+    return np.array(runs, np.int32).reshape(-1, 4)
+
+
+def slot_of(base_rows, run, p, page_mask):
+    return base_rows[run[2] + ((p >> SHIFT) & page_mask)] + (p & (PAGE - 1))
+
+
+@pytest.mark.parametrize("cfg,page_mask", [(SLIDING, 1), (FULL, -1)], ids=["sliding", "full"])
+def test_attn_prep_bit_exact(cfg, page_mask):
+    rng = np.random.default_rng(11)
+    hd, nq, nkv = cfg["head_dim"], cfg["num_q"], cfg["num_kv"]
+    # two runs (sequences): 3 prefill-chunk tokens at positions 62..64 (crossing
+    # a page) and one decode token at position 200 (ring wraps for sliding)
+    runs = [(0, 62, 0, 2), (3, 200, 2, 4)]
+    base_rows = np.array([128, 0, 320, 192, 64, 256], np.int32)
+    T = 4
+    q = bf(rng.standard_normal((T, nq * hd)) * 1.5)
+    k = bf(rng.standard_normal((T, nkv * hd)))
+    v = k.copy() if cfg is FULL else bf(rng.standard_normal((T, nkv * hd)) * 0.7)
+    qn, kn = bf(1.0 + 0.3 * rng.standard_normal(hd)), bf(1.0 + 0.3 * rng.standard_normal(hd))
+    cos, sin = rope_tables(256, cfg["rope_half"], 10000.0)
+    pos = np.array([62, 63, 64, 200], np.int32)
+    run_of = [0, 0, 0, 1]
+    slot = np.array([slot_of(base_rows, runs[run_of[t]], pos[t], page_mask) for t in range(T)], np.int32)
+    n_slots = 384
+    want = O.bq_attn_prep(q, k, v, qn, kn, pos, slot, hd, nq, nkv, cfg["rope_half"],
+                          cfg["pair_stride"], cos, sin, n_slots)
+    q_i8 = torch.zeros(T, nq * hd, dtype=torch.int8, device="cuda")
+    qb = torch.zeros(T, nq, dtype=torch.float32, device="cuda")
+    fq = torch.zeros_like(qb)
+    kc = torch.zeros(n_slots, nkv * hd, dtype=torch.int8, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks = torch.zeros(n_slots, nkv, dtype=torch.float32, device="cuda")
+    vs = torch.zeros_like(ks)
+    dq, dk = dev(q), dev(k)
+    dv = dk if cfg is FULL else dev(v)
+    gmoe.call("gm_bq_attn_prep", dq, dk, dv, dev(qn), dev(kn), q_i8, qb, fq, kc, ks, vc, vs,
+              dev(cos), dev(sin), dev(runs_array(runs)), len(runs), dev(base_rows), T, hd, nq, nkv,
+              cfg["rope_half"], cfg["pair_stride"], 1, 0, SHIFT, PAGE - 1, page_mask, None)
+    torch.cuda.synchronize()
+    for got, exp in zip((q_i8, qb, fq, kc, ks, vc, vs), want):
+        assert np.array_equal(host(got), exp)
+    # degree 2, rank 1: only odd positions reach this rank's cache (row pos // 2)
+    kc.zero_()
+    slot2 = np.array([slot_of(base_rows, runs[run_of[t]], pos[t] // 2, page_mask)
+                      if pos[t] % 2 == 1 else -1 for t in range(T)], np.int32)
+    want2 = O.bq_attn_prep(q, k, v, qn, kn, pos, slot2, hd, nq, nkv, cfg["rope_half"],
+                           cfg["pair_stride"], cos, sin, n_slots)
+    gmoe.call("gm_bq_attn_prep", dq, dk, dv, dev(qn), dev(kn), q_i8, qb, fq, kc, ks, vc, vs,
+              dev(cos), dev(sin), dev(runs_array(runs)), len(runs), dev(base_rows), T, hd, nq, nkv,
+              cfg["rope_half"], cfg["pair_stride"], 2, 1, SHIFT, PAGE - 1, page_mask, None)
+    torch.cuda.synchronize()
+    assert np.array_equal(host(kc), want2[3])
+
+
+def decode_case(cfg, window, page_mask, positions, rng):
+    hd, nq, nkv = cfg["head_dim"], cfg["num_q"], cfg["num_kv"]
+    T = len(positions)
+    pages_per_run = 2 if page_mask == 1 else (max(positions) >> SHIFT) + 1
+    n_slots = T * pages_per_run * PAGE
+    perm = rng.permutation(T * pages_per_run)
+    base_rows = (perm * PAGE).astype(np.int32)
+    runs = [(t, positions[t], t * pages_per_run, pages_per_run) for t in range(T)]
+    kc, ks, vc, vs = random_cache(rng, n_slots, cfg)
+    ks *= 0.03
+    q_i8 = rng.integers(-127, 128, size=(T, nq * hd), dtype=np.int8)
+    fq = (rng.random((T, nq)) + 0.5).astype(np.float32)
+    qb = (q_i8.reshape(T, nq, hd).astype(np.int64).sum(-1) * 128).astype(np.float32)
+    max_kv = max(min(p + 1, window) if window else p + 1 for p in positions)
+    slots = np.zeros((T, max_kv), np.int32)
+    kv_len = np.zeros(T, np.int32)
+    for t, p in enumerate(positions):
+        valid = min(p + 1, window) if window else p + 1
+        start = p - valid + 1 if window else 0
+        kv_len[t] = valid
+        for i in range(valid):
+            slots[t, i] = slot_of(base_rows, runs[t], start + i, page_mask)
+    return dict(q_i8=q_i8, fq=fq, qb=qb, kc=kc, ks=ks, vc=vc, vs=vs, slots=slots, kv_len=kv_len,
+                runs=runs, base_rows=base_rows, max_kv=max_kv)
+
+
+@pytest.mark.parametrize("cfg,window,page_mask,positions", [
+    (SLIDING, 64, 1, [0, 5, 63, 64, 100, 127, 128, 300]),
+    (FULL, 0, -1, [0, 1, 31, 64, 200, 511]),
+    (SLIDING, 64, 1, [90]),
+], ids=["sliding", "full", "sliding-b1"])
+def test_attention_decode_matches_oracle(cfg, window, page_mask, positions):
+    rng = np.random.default_rng(len(positions) + cfg["head_dim"])
+    hd, nq, nkv = cfg["head_dim"], cfg["num_q"], cfg["num_kv"]
+    c = decode_case(cfg, window, page_mask, positions, rng)
+    T = len(positions)
+    want = O.bf16_to_f32(O.bq_flash_decode(c["q_i8"], c["qb"], c["fq"], c["kc"], c["ks"], c["vc"], c["vs"],
+                                           c["slots"], c["kv_len"], hd, nq, nkv, 1)).astype(np.float64)
+    ref = decode_f64(c["q_i8"], c["fq"], c["kc"], c["ks"], c["vc"], c["vs"], c["slots"], c["kv_len"], cfg)
+    ws_bytes = gmoe.lib().gm_bq_attention_workspace_bytes(T, hd, nq, nkv, c["max_kv"])
+    ws = torch.empty(ws_bytes // 4, dtype=torch.float32, device="cuda")
+    out = torch.empty(T, nq * hd, dtype=torch.bfloat16, device="cuda")
+    gmoe.call("gm_bq_attention_decode", dev(c["q_i8"]), dev(c["fq"]), dev(c["kc"]), dev(c["ks"]),
+              dev(c["vc"]), dev(c["vs"]), dev(runs_array(c["runs"])), dev(c["base_rows"]), T, hd, nq, nkv,
+              window, 1, 0, SHIFT, PAGE - 1, page_mask, c["max_kv"], out, ws, ws_bytes, None)
+    torch.cuda.synchronize()
+    got = O.bf16_to_f32(host(out)).astype(np.float64)
+    scale = np.abs(ref).max()
+    assert np.abs(got - want).max() <= 1e-2 * scale
+    assert np.abs(got - ref).max() <= 1e-2 * scale
+    # a too-small workspace is refused
+    with pytest.raises(gmoe.GmoeError, match="workspace"):
+        gmoe.call("gm_bq_attention_decode", dev(c["q_i8"]), dev(c["fq"]), dev(c["kc"]), dev(c["ks"]),
+                  dev(c["vc"]), dev(c["vs"]), dev(runs_array(c["runs"])), dev(c["base_rows"]), T, hd, nq,
+                  nkv, window, 1, 0, SHIFT, PAGE - 1, page_mask, c["max_kv"], out, ws, ws_bytes - 4, None)
