@@ -19,12 +19,11 @@
 // B200 shape.  Prep: a half-warp per head, element e in lane e % 16 of
 // register e / 16 -- the reference's 16-lane SIMD layout, so the
 // sum-of-squares chains and their lane tree are the reference's and the prep
-// is bit-exact.  Decode: CTA = (token, KV head, KV split), 4 warps; a warp
-// owns two query heads of the GQA group and a stripe of 32-position tiles:
-// lane j scores position j of the tile from its own K row (dp4a against the
-// query in shared memory), then all lanes stream each V row once (coalesced)
-// into per-lane accumulators of head_dim/32 columns.  Warps that share heads
-// merge in shared memory; the CTA writes one partial (m, l, acc) per head.
+// is bit-exact.  Decode: CTA = (token, KV head, KV split), 256 threads,
+// tiles of 32 positions; each K and V row of the split is read once and
+// serves every query head of the GQA group (see attn_decode_kernel); the CTA
+// writes one partial (m, l, acc) per head and a merge kernel combines the
+// splits.
 #include "gm_kernels.h"
 
 namespace gm {
@@ -32,8 +31,6 @@ namespace gm {
 namespace {
 
 constexpr int AW = 16;                 // reference SIMD lanes (AVX-512 f32)
-constexpr int DEC_WARPS = 4;
-constexpr int QW = 2;                  // query heads per warp
 constexpr float NEG_BIG = -1e30f;      // the reference's initial running max
 
 struct KvRun {
@@ -208,31 +205,74 @@ __device__ __forceinline__ void split_range(int total, int n, int s, int& b, int
   if (b >= total) b = e = total;
 }
 
+// CTA = (split, KV head g, token t), 256 threads, tiles of DEC_TP positions.  The
+// K and V rows of a tile (and their scales) are copied into shared memory
+// with cp.async one tile ahead (double buffer), then:
+//  A. scores: mma.m16n8k32 s8 with the tile's positions as M and the
+//     group's heads as N; the eight warps split K and their integer
+//     partials are summed exactly;
+//  B. softmax: the warp owning head h (h % 8) keeps its running max / sum and
+//     turns the tile's scores into weights w*vs/127;
+//  C. V: thread i owns columns [i*CPT, (i+1)*CPT) of every head: each V row is
+//     converted once and used for all G heads.
+constexpr int DEC_TP = 16;  // positions per tile
+
 template <int HD>
-__global__ void __launch_bounds__(32 * DEC_WARPS)
+struct DecodeSmem {
+  static constexpr int TP = DEC_TP;
+  static constexpr int RS = HD + 16;  // padded row: the 32 lanes of phase A hit distinct banks
+  int8_t k[2][TP][RS];  // RS padding: lanes reading rows at one column hit distinct banks
+  int8_t v[2][TP][RS];
+  float ks[2][TP];
+  float vs[2][TP];
+};
+
+constexpr int DEC_THREADS = 256;
+constexpr int DEC_WARPS = DEC_THREADS / 32;
+
+template <int HD, int G>
+__global__ void __launch_bounds__(DEC_THREADS)
 attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_q,
                    const int8_t* __restrict__ k_cache, const float* __restrict__ k_scale,
                    const int8_t* __restrict__ v_cache, const float* __restrict__ v_scale,
                    const KvRun* __restrict__ runs, const int32_t* __restrict__ base_rows, int num_q,
                    int num_kv, int window, int cache_degree, int rank, int shift, int row_mask,
                    int page_mask, int n_splits, float* __restrict__ partials) {
-  constexpr int VPL = HD / 32;       // V columns per lane
-  constexpr int QWORDS = HD / 4;     // int32 words per query head
+  using Sm = DecodeSmem<HD>;
+  constexpr int TP = Sm::TP;
+  constexpr int NW = DEC_WARPS;
+  constexpr int CPT = HD / DEC_THREADS;           // V columns per thread
+  constexpr int HPW = (G + NW - 1) / NW;          // heads whose softmax state a warp keeps
+  constexpr int TPR = DEC_THREADS / TP;           // copying threads per row
+  constexpr int CHUNKS = HD / (16 * TPR);         // 16-byte chunks per copying thread
+  constexpr int KSW = HD / 32 / NW;               // 32-wide K steps per warp
+  static_assert(KSW >= 1 && CPT >= 1 && CHUNKS >= 1, "tile geometry");
+  static_assert(G <= 8, "heads of a group fit the N = 8 tile");
   const int s = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
-  const int G = num_q / num_kv;      // query heads per KV head (even)
-  const int n_hs = G / QW, wph = DEC_WARPS / n_hs;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hs = warp % n_hs, stripe = warp / n_hs;
-  const int h0 = g * G + hs * QW;
-  extern __shared__ __align__(16) uint8_t smem[];
-  int* qs = reinterpret_cast<int*>(smem);                               // [G][QWORDS]
-  float* red = reinterpret_cast<float*>(qs + G * QWORDS);               // [DEC_WARPS][QW][HD + 2]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grp = lane >> 2, tig = lane & 3;
+  extern __shared__ __align__(16) uint8_t dsm[];
+  Sm& sm = *reinterpret_cast<Sm*>(dsm);
+  __shared__ __align__(16) int8_t qs[G * HD];
+  __shared__ int part[DEC_WARPS][G][TP];
+  __shared__ __align__(16) float wv[TP][G];
+  __shared__ float corr_s[G];
 
   pdl_wait();
   pdl_trigger();
-  for (int i = threadIdx.x; i < G * QWORDS; i += blockDim.x)
-    qs[i] = __ldg(reinterpret_cast<const int*>(q_i8 + ((size_t)t * num_q + g * G) * HD) + i);
+  for (int i = tid; i < G * HD / 16; i += DEC_THREADS)
+    reinterpret_cast<int4*>(qs)[i] =
+        __ldg(reinterpret_cast<const int4*>(q_i8 + ((size_t)t * num_q + g * G) * HD) + i);
   __syncthreads();
+  // B fragments of the query (k = 4*tig.., head = grp; heads past G are zero),
+  // held for the whole split
+  uint32_t bq[KSW][2];
+#pragma unroll
+  for (int ks = 0; ks < KSW; ++ks) {
+    const int k0 = (warp * KSW + ks) * 32 + 4 * tig;
+    bq[ks][0] = grp < G ? *reinterpret_cast<const uint32_t*>(qs + grp * HD + k0) : 0u;
+    bq[ks][1] = grp < G ? *reinterpret_cast<const uint32_t*>(qs + grp * HD + k0 + 16) : 0u;
+  }
 
   const KvRun run = runs[t];
   const int pos = run.base_pos;
@@ -247,122 +287,162 @@ attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_
   const int32_t* rows = base_rows + run.rows_off;
   int b, e;
   split_range(valid, n_splits, s, b, e);
+  const size_t kvs = (size_t)num_kv * HD;
+  // copy rows [p0, p0 + TP) of the split into buffer `buf`: thread tid copies
+  // part tid % TPR of row tid / TPR (and one of its two scales)
+  const int crow = tid / TPR, cpart = tid % TPR;
+  auto issue = [&](int p0, int buf) {
+    const int p = p0 + crow;
+    if (p < e) {
+      const long slot = kv_slot(rows, shift, row_mask, page_mask, start + p);
+      const int8_t* kr = k_cache + slot * kvs + (size_t)g * HD + cpart * (HD / TPR);
+      const int8_t* vr = v_cache + slot * kvs + (size_t)g * HD + cpart * (HD / TPR);
+#pragma unroll
+      for (int c = 0; c < CHUNKS; ++c) {
+        cp_async16(&sm.k[buf][crow][cpart * (HD / TPR) + 16 * c], kr + 16 * c);
+        cp_async16(&sm.v[buf][crow][cpart * (HD / TPR) + 16 * c], vr + 16 * c);
+      }
+      if (cpart == 0) cp_async4(&sm.ks[buf][crow], k_scale + slot * num_kv + g);
+      if (cpart == 1) cp_async4(&sm.vs[buf][crow], v_scale + slot * num_kv + g);
+    }
+    cp_async_commit();
+  };
+
   const float inv127 = 1.0f / 127.0f;
   const float inv127sq = __fmul_rn(inv127, inv127);
-  const float fq0 = __ldg(f_q + (size_t)t * num_q + h0), fq1 = __ldg(f_q + (size_t)t * num_q + h0 + 1);
-  const size_t kvs = (size_t)num_kv * HD;
-
-  float m[QW] = {NEG_BIG, NEG_BIG}, l[QW] = {0.0f, 0.0f};
-  float acc[QW][VPL];
+  float fq[HPW], m[HPW], l[HPW];
 #pragma unroll
-  for (int a = 0; a < QW; ++a)
+  for (int j = 0; j < HPW; ++j) {
+    const int h = warp + NW * j;
+    fq[j] = h < G ? __ldg(f_q + (size_t)t * num_q + g * G + h) : 0.0f;
+    m[j] = NEG_BIG;
+    l[j] = 0.0f;
+  }
+  float acc[G][CPT];
 #pragma unroll
-    for (int c = 0; c < VPL; ++c) acc[a][c] = 0.0f;
-  const int* q0 = qs + (hs * QW) * QWORDS;
-  const int* q1 = q0 + QWORDS;
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int c = 0; c < CPT; ++c) acc[h][c] = 0.0f;
 
-  for (int p0 = b + stripe * 32; p0 < e; p0 += wph * 32) {
-    const int i = p0 + lane;
-    const bool ok = i < e;
-    const long slot = ok ? kv_slot(rows, shift, row_mask, page_mask, start + i) : 0;
-    float sc0 = NEG_BIG, sc1 = NEG_BIG, vs = 0.0f;
-    if (ok) {
-      const int4* kr = reinterpret_cast<const int4*>(k_cache + slot * kvs + (size_t)g * HD);
-      int d0 = 0, d1 = 0;
-#pragma unroll 4
-      for (int c = 0; c < HD / 16; ++c) {
-        const int4 kw = __ldg(kr + c);
-        d0 = __dp4a(kw.x, q0[4 * c], d0);
-        d0 = __dp4a(kw.y, q0[4 * c + 1], d0);
-        d0 = __dp4a(kw.z, q0[4 * c + 2], d0);
-        d0 = __dp4a(kw.w, q0[4 * c + 3], d0);
-        d1 = __dp4a(kw.x, q1[4 * c], d1);
-        d1 = __dp4a(kw.y, q1[4 * c + 1], d1);
-        d1 = __dp4a(kw.z, q1[4 * c + 2], d1);
-        d1 = __dp4a(kw.w, q1[4 * c + 3], d1);
-      }
-      const float ks = __ldg(k_scale + slot * num_kv + g);
-      sc0 = __fmul_rn(__fmul_rn(__fmul_rn((float)d0, fq0), ks), inv127sq);
-      sc1 = __fmul_rn(__fmul_rn(__fmul_rn((float)d1, fq1), ks), inv127sq);
-      vs = __ldg(v_scale + slot * num_kv + g);
+  if (b < e) issue(b, 0);
+  int buf = 0;
+  for (int p0 = b; p0 < e; p0 += TP, buf ^= 1) {
+    const int n = min(TP, e - p0);
+    if (p0 + TP < e) {
+      issue(p0 + TP, buf ^ 1);  // next tile in flight during this one
+      cp_async_wait_group<1>();
+    } else {
+      cp_async_wait_group<0>();
     }
-    float w0, w1;
+    __syncthreads();
+    // ---- A: QK on the tensor cores (mma.m16n8k32 s8): positions are M (TP/16
+    // 16-row tiles), the group's heads N (8, zero-padded), K split over the warps
+    constexpr int MT = TP / 16;
+    const bool ok = lane < n;  // n <= TP
     {
-      const float mn0 = fmaxf(m[0], warp_max(sc0)), mn1 = fmaxf(m[1], warp_max(sc1));
-      const float c0 = fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(m[0], mn0)));
-      const float c1 = fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(m[1], mn1)));
-      w0 = ok ? fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(sc0, mn0))) : 0.0f;
-      w1 = ok ? fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(sc1, mn1))) : 0.0f;
-      l[0] = __fadd_rn(__fmul_rn(l[0], c0), warp_sum(w0));
-      l[1] = __fadd_rn(__fmul_rn(l[1], c1), warp_sum(w1));
-      m[0] = mn0;
-      m[1] = mn1;
+      int c[MT][4];
 #pragma unroll
-      for (int c = 0; c < VPL; ++c) {
-        acc[0][c] = __fmul_rn(acc[0][c], c0);
-        acc[1][c] = __fmul_rn(acc[1][c], c1);
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c[mt][i] = 0;
+#pragma unroll
+      for (int ks = 0; ks < KSW; ++ks) {
+        const int k0 = (warp * KSW + ks) * 32 + 4 * tig;
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const int8_t* r0 = &sm.k[buf][mt * 16 + grp][k0];
+          const int8_t* r1 = &sm.k[buf][mt * 16 + grp + 8][k0];
+          mma_s8(c[mt], *reinterpret_cast<const uint32_t*>(r0), *reinterpret_cast<const uint32_t*>(r1),
+                 *reinterpret_cast<const uint32_t*>(r0 + 16), *reinterpret_cast<const uint32_t*>(r1 + 16),
+                 bq[ks][0], bq[ks][1]);
+        }
+      }
+      // c[mt][0..1]: position mt*16 + grp, heads 2*tig, 2*tig+1; [2..3]: position + 8
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int h = 2 * tig + (i & 1);
+          if (h < G) part[warp][h][mt * 16 + grp + 8 * (i >> 1)] = c[mt][i];
+        }
+    }
+    __syncthreads();
+    // ---- B: online softmax of the heads this warp owns
+    {
+      const float ks = ok ? sm.ks[buf][lane] : 0.0f;
+      const float vs = ok ? sm.vs[buf][lane] : 0.0f;
+      const int pl = ok ? lane : 0;  // lanes past the tile read row 0 and are masked
+#pragma unroll
+      for (int j = 0; j < HPW; ++j) {
+        const int h = warp + NW * j;
+        if (h < G) {
+          int dot = 0;
+#pragma unroll
+          for (int w = 0; w < NW; ++w) dot += part[w][h][pl];
+          const float sc = ok ? __fmul_rn(__fmul_rn(__fmul_rn((float)dot, fq[j]), ks), inv127sq) : NEG_BIG;
+          const float mn = fmaxf(m[j], warp_max(sc));
+          const float cr = fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(m[j], mn)));
+          const float w = ok ? fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(sc, mn))) : 0.0f;
+          l[j] = __fadd_rn(__fmul_rn(l[j], cr), warp_sum(w));
+          m[j] = mn;
+          if (lane < TP) wv[lane][h] = __fmul_rn(__fmul_rn(w, vs), inv127);
+          if (lane == 0) corr_s[h] = cr;
+        }
       }
     }
-    const float wv0 = __fmul_rn(__fmul_rn(w0, vs), inv127), wv1 = __fmul_rn(__fmul_rn(w1, vs), inv127);
-    const int n = min(32, e - p0);
-    for (int j = 0; j < n; ++j) {
-      const long sj = (long)__shfl_sync(0xffffffffu, (int)slot, j);
-      const float a0 = __shfl_sync(0xffffffffu, wv0, j), a1 = __shfl_sync(0xffffffffu, wv1, j);
-      const int8_t* vr = v_cache + sj * kvs + (size_t)g * HD + lane * VPL;
-      uint32_t vw[VPL / 4];
-      if constexpr (VPL == 8) {
-        const int2 x = __ldg(reinterpret_cast<const int2*>(vr));
-        vw[0] = (uint32_t)x.x;
-        vw[1] = (uint32_t)x.y;
+    __syncthreads();
+    // ---- C: acc = acc*corr + sum_p v[p] * wv[p]
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float cr = corr_s[h];
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) acc[h][c] = __fmul_rn(acc[h][c], cr);
+    }
+#pragma unroll 4
+    for (int p = 0; p < n; ++p) {
+      uint32_t vw;
+      if constexpr (CPT == 2) vw = *reinterpret_cast<const uint16_t*>(&sm.v[buf][p][tid * CPT]);
+      else vw = (uint32_t)(uint8_t)sm.v[buf][p][tid * CPT];
+      float v[CPT];
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) v[c] = (float)(int8_t)((vw >> (8 * c)) & 0xFFu);
+      float a[G];
+      if constexpr (G % 4 == 0) {
+#pragma unroll
+        for (int h4 = 0; h4 < G / 4; ++h4) {
+          const float4 w4 = reinterpret_cast<const float4*>(&wv[p][0])[h4];
+          a[4 * h4] = w4.x;
+          a[4 * h4 + 1] = w4.y;
+          a[4 * h4 + 2] = w4.z;
+          a[4 * h4 + 3] = w4.w;
+        }
       } else {
-        const int4 x = __ldg(reinterpret_cast<const int4*>(vr));
-        vw[0] = (uint32_t)x.x;
-        vw[1] = (uint32_t)x.y;
-        vw[2] = (uint32_t)x.z;
-        vw[3] = (uint32_t)x.w;
+#pragma unroll
+        for (int h = 0; h < G; ++h) a[h] = wv[p][h];
       }
 #pragma unroll
-      for (int c = 0; c < VPL; ++c) {
-        const float v = (float)(int8_t)((vw[c >> 2] >> (8 * (c & 3))) & 0xFFu);
-        acc[0][c] = __fmaf_rn(v, a0, acc[0][c]);
-        acc[1][c] = __fmaf_rn(v, a1, acc[1][c]);
-      }
+      for (int h = 0; h < G; ++h)
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) acc[h][c] = __fmaf_rn(v[c], a[h], acc[h][c]);
     }
+    __syncthreads();  // this buffer and part / wv / corr_s are reused
   }
 
-  // merge the stripes of each head set in shared memory, then one partial per head
-  float* mine = red + (size_t)warp * QW * (HD + 2);
+  // one partial (m, l, acc) per head of the group
 #pragma unroll
-  for (int a = 0; a < QW; ++a) {
+  for (int h = 0; h < G; ++h) {
+    float* dst = partials + (((size_t)t * num_q + g * G + h) * n_splits + s) * (HD + 2);
 #pragma unroll
-    for (int c = 0; c < VPL; ++c) mine[a * (HD + 2) + 2 + lane * VPL + c] = acc[a][c];
-    if (lane == 0) {
-      mine[a * (HD + 2)] = m[a];
-      mine[a * (HD + 2) + 1] = l[a];
-    }
+    for (int c = 0; c < CPT; ++c) dst[2 + tid * CPT + c] = acc[h][c];
   }
-  __syncthreads();
-  if (stripe == 0) {
-    for (int a = 0; a < QW; ++a) {
-      float M = NEG_BIG;
-      for (int w = hs; w < DEC_WARPS; w += n_hs) M = fmaxf(M, red[((size_t)w * QW + a) * (HD + 2)]);
-      float L = 0.0f;
-      float o[VPL];
+  if (lane == 0) {
 #pragma unroll
-      for (int c = 0; c < VPL; ++c) o[c] = 0.0f;
-      for (int w = hs; w < DEC_WARPS; w += n_hs) {
-        const float* src = red + ((size_t)w * QW + a) * (HD + 2);
-        const float cw = src[1] > 0.0f ? fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(src[0], M))) : 0.0f;
-        L = __fmaf_rn(src[1], cw, L);
-#pragma unroll
-        for (int c = 0; c < VPL; ++c) o[c] = __fmaf_rn(src[2 + lane * VPL + c], cw, o[c]);
-      }
-      float* dst = partials + (((size_t)t * num_q + h0 + a) * n_splits + s) * (HD + 2);
-#pragma unroll
-      for (int c = 0; c < VPL; ++c) dst[2 + lane * VPL + c] = o[c];
-      if (lane == 0) {
-        dst[0] = M;
-        dst[1] = L;
+    for (int j = 0; j < HPW; ++j) {
+      const int h = warp + NW * j;
+      if (h < G) {
+        float* dst = partials + (((size_t)t * num_q + g * G + h) * n_splits + s) * (HD + 2);
+        dst[0] = m[j];
+        dst[1] = l[j];
       }
     }
   }
@@ -392,10 +472,12 @@ attn_merge_kernel(const float* __restrict__ partials, int n_splits, uint16_t* __
 
 }  // namespace
 
+// KV splits per (token, KV head): enough CTAs for every SM several times
+// over, at least 64 positions per split, at most 64 splits.
 int attention_splits(int T, int num_kv, int max_kv_len) {
   const int want = (148 * 8 + T * num_kv - 1) / (T * num_kv);
   const int cap = std::max(1, (max_kv_len + 63) / 64);
-  return std::max(1, std::min({want, cap, 32}));
+  return std::max(1, std::min({want, cap, 64}));
 }
 
 size_t attention_workspace_floats(int T, int head_dim, int num_q, int num_kv, int max_kv_len) {
@@ -434,22 +516,30 @@ cudaError_t launch_attn_decode(const int8_t* q_i8, const float* f_q, const int8_
   if (T <= 0) return cudaSuccess;
   const int n_splits = attention_splits(T, num_kv, max_kv_len);
   const int G = num_q / num_kv;
-  const size_t smem = (size_t)G * head_dim + (size_t)DEC_WARPS * QW * (head_dim + 2) * 4;
   const KvRun* r = static_cast<const KvRun*>(runs);
   const dim3 grid(n_splits, num_kv, T);
-  cudaError_t e;
+  void (*k)(const int8_t*, const float*, const int8_t*, const float*, const int8_t*, const float*,
+            const KvRun*, const int32_t*, int, int, int, int, int, int, int, int, int, float*) = nullptr;
   if (head_dim == 256) {
-    e = launch_k(attn_decode_kernel<256>, grid, dim3(32 * DEC_WARPS), smem, s, q_i8, f_q, k_cache, k_scale,
-                 v_cache, v_scale, r, base_rows, num_q, num_kv, window, cache_degree, rank, shift, row_mask,
-                 page_mask, n_splits, partials);
-    if (e != cudaSuccess) return e;
+    if (G == 2) k = attn_decode_kernel<256, 2>;
+    else if (G == 4) k = attn_decode_kernel<256, 4>;
+    else if (G == 8) k = attn_decode_kernel<256, 8>;
+  } else {
+    if (G == 2) k = attn_decode_kernel<512, 2>;
+    else if (G == 4) k = attn_decode_kernel<512, 4>;
+    else if (G == 8) k = attn_decode_kernel<512, 8>;
+  }
+  if (!k) return cudaErrorInvalidValue;
+  const size_t smem = head_dim == 256 ? sizeof(DecodeSmem<256>) : sizeof(DecodeSmem<512>);
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  e = launch_k(k, grid, dim3(DEC_THREADS), smem, s, q_i8, f_q, k_cache, k_scale, v_cache, v_scale, r, base_rows,
+                           num_q, num_kv, window, cache_degree, rank, shift, row_mask, page_mask, n_splits,
+                           partials);
+  if (e != cudaSuccess) return e;
+  if (head_dim == 256)
     return launch_k(attn_merge_kernel<256>, dim3(T * num_q), dim3(256), 0, s, (const float*)partials,
                     n_splits, out);
-  }
-  e = launch_k(attn_decode_kernel<512>, grid, dim3(32 * DEC_WARPS), smem, s, q_i8, f_q, k_cache, k_scale,
-               v_cache, v_scale, r, base_rows, num_q, num_kv, window, cache_degree, rank, shift, row_mask,
-               page_mask, n_splits, partials);
-  if (e != cudaSuccess) return e;
   return launch_k(attn_merge_kernel<512>, dim3(T * num_q), dim3(512), 0, s, (const float*)partials, n_splits,
                   out);
 }
