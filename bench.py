@@ -56,6 +56,21 @@ ZIPF = {"bq-prefill-4k-zipf", "bf16-prefill-4k-zipf", "ep-prefill-16k"}
 WORKLOADS["bq-decode-b64-30L"] = (64, "bq", "replicas")
 LAYERS = {"bq-decode-b64-30L": 30}
 METRIC = "MoE-block tokens/s at 1/2/4/8 B200 (decode b=64, prefill 4k); % of roofline"
+# Workloads of the rows widened beyond the MoE block (one GPU): the whole FFN
+# (dense MLP beside the MoE, post-FFN tail; gm_ffn_forward) and butterquant
+# decode attention over a full KV window (gm_bq_attention_decode).
+EXTRA = {
+    "ffn-decode-b64": ("ffn", 64),
+    "ffn-prefill-4k": ("ffn", 4096),
+    "attn-decode-sliding-b64": ("attn-sliding", 64),
+    "attn-decode-full-b64": ("attn-full", 64),
+}
+DENSE_I = 2112
+DENSE_BYTES = 3 * DENSE_I * H + 2 * DENSE_I * 4 + H * 4       # int8 weights + row scales
+ATTN = {  # head_dim, query heads, KV heads, window (0 = full), KV positions, pages per sequence
+    "attn-sliding": (256, 16, 8, 1024, 1024, 2),
+    "attn-full": (512, 16, 2, 0, 4096, 4),
+}
 
 
 def parse():
@@ -63,7 +78,7 @@ def parse():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--workload", default="bq-decode-b64", choices=sorted(WORKLOADS))
+    p.add_argument("--workload", default="bq-decode-b64", choices=sorted(WORKLOADS) + sorted(EXTRA))
     p.add_argument("--impl", default="gmoe", choices=["gmoe", "reference"])
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="bounded CPU-baseline sample length")
@@ -179,22 +194,37 @@ def host_info():
     return {"nproc": os.cpu_count(), "cpu_model": model, "numa_nodes": numa}
 
 
+def oracle_bq_layer(O, raw_cpu):
+    """The reference quantizer and load-time bakes, run by the oracle on the host."""
+    gu_q, gu_s = O.quantize_rows(raw_cpu["gate_up"].reshape(E * GU, H), 128, raw_cpu["pre_ffn_norm_2"])
+    dn_q, dn_s = O.quantize_rows(raw_cpu["down"].reshape(E * H, I), 64)
+    return {"router_centered": O.router_center(raw_cpu["router_proj"]),
+            "router_scale": O.bake_router_scale(raw_cpu["router_scale"]),
+            "pes": raw_cpu["per_expert_scale"], "gamma2": O.bake_split_gain(raw_cpu["pre_ffn_norm_2"]),
+            "gu_q": gu_q, "gu_scale": gu_s, "gu_cs": O.colsum(gu_q, H, True).reshape(-1),
+            "dn_q": dn_q, "dn_scale": dn_s, "dn_cs": O.colsum(dn_q, 64, False)}
+
+
+def oracle_dense_layer(O, rawd_cpu):
+    """DenseGateUp / DenseDown recipes on the host (row-major int8, colsums)."""
+    wg, wgs = O.quantize_rows(rawd_cpu["gate"], 128, rawd_cpu["pre_ffn_norm"])
+    wu, wus = O.quantize_rows(rawd_cpu["up"], 128, rawd_cpu["pre_ffn_norm"])
+    wd, wds = O.quantize_rows(rawd_cpu["down"], 64)
+    return {"wg": wg, "wgs": wgs, "wgcs": O.colsum(wg, H, True).reshape(-1),
+            "wu": wu, "wus": wus, "wucs": O.colsum(wu, H, True).reshape(-1),
+            "wd": wd, "wds": wds, "wdcs": O.colsum(wd, 64, False),
+            "gamma": O.bake_split_gain(rawd_cpu["pre_ffn_norm"])}
+
+
 def cpu_baseline_sample(fmt, T, seconds, raw_cpu, xs_cpu):
     """Time the oracle (CPU restatement of the reference path, all host cores)
     on forwards of the workload; returns (tokens/s at the median sample,
     samples, warm-up forwards, threads)."""
     from oracle import oracle as O
     import numpy as np
-    import synth
     L = {}
     if fmt == "bq":
-        gu_q, gu_s = O.quantize_rows(raw_cpu["gate_up"].reshape(E * GU, H), 128, raw_cpu["pre_ffn_norm_2"])
-        dn_q, dn_s = O.quantize_rows(raw_cpu["down"].reshape(E * H, I), 64)
-        L = {"router_centered": O.router_center(raw_cpu["router_proj"]),
-             "router_scale": O.bake_router_scale(raw_cpu["router_scale"]),
-             "pes": raw_cpu["per_expert_scale"], "gamma2": O.bake_split_gain(raw_cpu["pre_ffn_norm_2"]),
-             "gu_q": gu_q, "gu_scale": gu_s, "gu_cs": O.colsum(gu_q, H, True).reshape(-1),
-             "dn_q": dn_q, "dn_scale": dn_s, "dn_cs": O.colsum(dn_q, 64, False)}
+        L = oracle_bq_layer(O, raw_cpu)
         fwd = O.bq_forward
     else:
         L = {"router_proj": raw_cpu["router_proj"], "router_scale": O.bake_router_scale(raw_cpu["router_scale"]),
@@ -254,8 +284,238 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def timed(fn, steps, warmup, stream):
+    """CUDA-event time of `steps` calls after a warm-up of >= 1 s."""
+    import torch
+    t_w, i = time.perf_counter(), 0
+    while i < warmup or time.perf_counter() - t_w < 1.0:
+        fn(i)
+        i += 1
+        if i % 8 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(steps):
+        fn(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    return ev0.elapsed_time(ev1)
+
+
+def oracle_native():
+    os.environ.setdefault("GMOE_ORACLE_VARIANT", "native")
+    from oracle import build as ob
+    try:
+        ob.build("native")
+    except Exception:
+        os.environ["GMOE_ORACLE_VARIANT"] = "portable"
+    from oracle import oracle as O
+    return O
+
+
+def median_rate(fn, units, seconds):
+    """The reference harness protocol, bounded: warm-up, then samples; units
+    per second at the median sample."""
+    import numpy as np
+    fn()
+    t0, warm = time.perf_counter(), 0
+    while warm < 30 and time.perf_counter() - t0 < 0.2 * seconds:
+        fn()
+        warm += 1
+    samples, t1 = [], time.perf_counter()
+    while len(samples) < 600 and (time.perf_counter() - t1 < 0.8 * seconds or len(samples) < 3):
+        ts = time.perf_counter()
+        fn()
+        samples.append(time.perf_counter() - ts)
+    return units / float(np.median(samples)), len(samples), warm
+
+
+def run_extra(args):
+    """The FFN and attention workloads (one GPU; see EXTRA)."""
+    import numpy as np
+    import torch
+    import gmoe
+    import synth
+    assert int(os.environ.get("WORLD_SIZE", "1")) == 1, "the FFN / attention workloads run on one GPU"
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    kind, T = EXTRA[args.workload]
+    torch.cuda.set_device(0)
+    hbm, tflops, peak_kind = peaks()
+    stream = torch.cuda.current_stream()
+    line = {"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "data": "synthetic (seeded; random-init, no checkpoint)"}
+    with ClockSampler(0) as clk:
+        if kind == "ffn":
+            raw = synth.make_layer(seed=0x6E6D6F45, device="cuda")
+            L = synth.bq_layer(raw)
+            rawd = synth.make_dense(seed=0x0D3E, device="cuda")
+            D = synth.dense_layer(rawd)
+            g = torch.Generator(device="cpu").manual_seed(5)
+            gains = [(1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).cuda() for _ in range(3)]
+            blk = gmoe.MoeBlock(T, 1)
+            register(blk, "bq", L)
+            blk.register_post(0, gains[0], gains[1], gains[2], 1.0)
+            blk.register_dense(0, D["gate"], D["gate_scale"], D["up"], D["up_scale"], D["down"],
+                               D["down_scale"], D["pre_ffn_norm"])
+            xs = [synth.make_tokens(T, seed=100 + b, device="cuda") for b in range(args.batches)]
+            work = [x.clone() for x in xs]
+
+            def step(i):
+                w = work[i % len(work)]
+                w.copy_(xs[i % len(xs)])          # fresh input (the FFN updates x_main in place)
+                blk.ffn_forward(0, w, T, stream)
+            ms = timed(step, args.steps, args.warmup, stream)
+            blk.profile(False)               # zeroes the handle's launch count
+            step(0)
+            torch.cuda.synchronize()
+            launches = blk.profile_read()[1] * args.steps   # kernels per step x timed steps
+            per_step = ms / args.steps
+            if T <= 256:
+                moe_bytes = min(E, T * TOPK) * BQ_EXPERT_BYTES
+                algo = moe_bytes + DENSE_BYTES + 4 * T * H * 2
+                roof = {"bound": "hbm", "achieved": algo / (per_step * 1e-3) / 1e9, "peak": hbm,
+                        "unit": "GB/s"}
+            else:
+                algo = T * (FLOP_PER_TOKEN + 2 * (2 * DENSE_I * H + H * DENSE_I))
+                roof = {"bound": "tensor", "achieved": algo / (per_step * 1e-3) / 1e12, "peak": tflops,
+                        "unit": "TFLOP/s"}
+            # e2e: pinned host batch in, FFN, result out
+            xh = [x.cpu().pin_memory() for x in xs]
+            oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+            w = work[0]
+
+            def e2e_step(i):
+                w.copy_(xh[i % len(xh)], non_blocking=True)
+                blk.ffn_forward(0, w, T, stream)
+                oh.copy_(w, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+            for i in range(3):
+                e2e_step(i)
+            t0 = time.perf_counter()
+            for i in range(args.steps):
+                e2e_step(i)
+            e2e = T * args.steps / (time.perf_counter() - t0)
+            e2e_io = (T * H * 2, T * H * 2)
+            cpu = None
+            if not args.no_cpu_baseline:
+                O = oracle_native()
+                Lo = oracle_bq_layer(O, {k: synth.to_numpy(v) for k, v in raw.items()})
+                Do = oracle_dense_layer(O, {k: synth.to_numpy(v) for k, v in rawd.items()})
+                gn = [synth.to_numpy(v) for v in gains]
+                Tc = min(T, 64)   # a bounded sample: at most 64 tokens per timed FFN
+                xc = synth.to_numpy(xs[0][:Tc])
+
+                def ffn_once():
+                    moe = O.bq_forward(xc, Lo)[0]
+                    dense = O.dense_mlp(xc, Do)[0]
+                    O.post_moe(moe, dense, xc, gn[0], gn[1], gn[2], 1.0)
+                rate, n, warm = median_rate(ffn_once, Tc, args.cpu_seconds)
+                cpu = dict({"value": rate, "unit": "tokens/s", "cores": O.lib().orc_num_threads(),
+                            "kind": "port",
+                            "sample": "%d warm-up + %d timed FFNs of %d tokens (MoE + dense MLP + post tail), "
+                                      "median (C++ restatement, OpenMP)" % (warm, n, Tc)}, **host_info())
+            line.update({"metric": "FFN tokens/s (dense MLP + MoE + post-FFN tail, gm_ffn_forward)",
+                         "dtype": "i8", "config": {"workload": args.workload, "tokens_per_step": T,
+                                                   "weights": "bq", "layers": 1, "parallelism": "single"}})
+            blk.close()
+        else:
+            hd, nq, nkv, window, kv, ppr = ATTN[kind]
+            PAGE, SHIFT = 1024, 10
+            g = torch.Generator(device="cuda").manual_seed(9)
+            n_slots = T * ppr * PAGE
+            kc = torch.randint(-127, 128, (n_slots, nkv * hd), dtype=torch.int8, device="cuda", generator=g)
+            vc = torch.randint(-127, 128, (n_slots, nkv * hd), dtype=torch.int8, device="cuda", generator=g)
+            ks = torch.rand(n_slots, nkv, device="cuda", generator=g) * 0.03
+            vs = torch.rand(n_slots, nkv, device="cuda", generator=g) + 0.5
+            qs = [torch.randint(-127, 128, (T, nq * hd), dtype=torch.int8, device="cuda", generator=g)
+                  for _ in range(args.batches)]
+            fq = torch.rand(T, nq, device="cuda", generator=g) + 0.5
+            pos = (5000 if window else kv - 1)
+            base = (torch.randperm(T * ppr, device="cuda", generator=g).int() * PAGE).contiguous()
+            runs = torch.tensor([[t, pos, t * ppr, ppr] for t in range(T)], dtype=torch.int32, device="cuda")
+            pmask = ppr - 1 if window else -1
+            wsb = gmoe.lib().gm_bq_attention_workspace_bytes(T, hd, nq, nkv, kv)
+            ws = torch.empty(wsb // 4 + 1, device="cuda")
+            out = torch.empty(T, nq * hd, dtype=torch.bfloat16, device="cuda")
+
+            def call(q, o):
+                gmoe.call("gm_bq_attention_decode", q, fq, kc, ks, vc, vs, runs, base, T, hd, nq, nkv,
+                          window, 1, 0, SHIFT, PAGE - 1, pmask, kv, o, ws, wsb, stream)
+
+            def step(i):
+                call(qs[i % len(qs)], out)
+            ms = timed(step, args.steps, args.warmup, stream)
+            launches = 2 * args.steps  # decode + merge kernels per call
+            per_step = ms / args.steps
+            algo = T * kv * nkv * (2 * hd + 8) + T * nq * hd * 3
+            roof = {"bound": "hbm", "achieved": algo / (per_step * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s"}
+            qh = [q.cpu().pin_memory() for q in qs]
+            oh = torch.empty(T, nq * hd, dtype=torch.bfloat16).pin_memory()
+            qd = torch.empty_like(qs[0])
+
+            def e2e_step(i):
+                qd.copy_(qh[i % len(qh)], non_blocking=True)
+                call(qd, out)
+                oh.copy_(out, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+            for i in range(3):
+                e2e_step(i)
+            t0 = time.perf_counter()
+            for i in range(args.steps):
+                e2e_step(i)
+            e2e = T * args.steps / (time.perf_counter() - t0)
+            e2e_io = (T * nq * hd, T * nq * hd * 2)
+            cpu = None
+            if not args.no_cpu_baseline:
+                O = oracle_native()
+                # a bounded sample: the oracle's flash decode of 4 of the tokens
+                Tc = 4
+                slots = np.zeros((Tc, kv), np.int32)
+                bh = base.cpu().numpy()
+                start = pos - kv + 1 if window else 0
+                for t in range(Tc):
+                    p = np.arange(start, start + kv)
+                    slots[t] = bh[t * ppr + ((p >> SHIFT) & (pmask if window else 0x7FFFFFFF))] + (p & (PAGE - 1))
+                kch, ksh, vch, vsh = kc.cpu().numpy(), ks.cpu().numpy(), vc.cpu().numpy(), vs.cpu().numpy()
+                qc = qs[0][:Tc].cpu().numpy()
+                fqc = fq[:Tc].cpu().numpy()
+                qbc = (qc.reshape(Tc, nq, hd).astype(np.int64).sum(-1) * 128).astype(np.float32)
+                kvl = np.full(Tc, kv, np.int32)
+                rate, n, warm = median_rate(
+                    lambda: O.bq_flash_decode(qc, qbc, fqc, kch, ksh, vch, vsh, slots, kvl, hd, nq, nkv,
+                                              O.lib().orc_num_threads()),
+                    Tc, args.cpu_seconds)
+                cpu = dict({"value": rate, "unit": "tokens/s", "cores": O.lib().orc_num_threads(),
+                            "kind": "port",
+                            "sample": "%d warm-up + %d timed decode calls of %d tokens x %d KV positions, "
+                                      "median (C++ restatement, OpenMP)" % (warm, n, Tc, kv)}, **host_info())
+            line.update({"metric": "decode attention tokens/s (%s layer, %d KV positions)" % (kind[5:], kv),
+                         "dtype": "i8", "config": {"workload": args.workload, "tokens_per_step": T,
+                                                   "head_dim": hd, "q_heads": nq, "kv_heads": nkv,
+                                                   "kv_positions": kv, "parallelism": "single",
+                                                   "l2": "KV cache %.0f MB per step (larger than L2)"
+                                                         % (T * kv * nkv * 2 * hd / 1e6)}})
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = None
+    line.update({"value": T * args.steps / (ms / 1e3), "unit": "tokens/s", "ms_per_step": per_step,
+                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": e2e_io[0],
+                         "d2h_bytes_per_step": e2e_io[1]},
+                 "gpu_launches": launches, "roofline": roof, "peak_source": peak_kind,
+                 "clocks": clk.summary()})
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.workload in EXTRA:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm covers the MoE-block "
+                              "workloads; this workload's CPU leg is its cpu_baseline"}))
+            return
+        return run_extra(args)
     if args.impl == "reference":
         return run_reference(args)
     import torch
