@@ -53,7 +53,7 @@ bq_norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
   constexpr int NBLK = H / NORM_BLOCK;  // 22
   const uint16_t* xr = x + (size_t)t * H;
@@ -124,7 +124,7 @@ rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
   constexpr int NBLK = H / NORM_BLOCK;
   const uint16_t* xr = x + (size_t)t * H;
@@ -161,8 +161,10 @@ rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
 cudaError_t launch_bq_norm_quant(const uint16_t* x, const uint16_t* gamma, int T, int8_t* xi8,
                                  float* xsa, float* inv_rms, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  return launch_k(bq_norm_quant_kernel, dim3((T + 7) / 8), dim3(256), 0, s, x, gamma, T, xi8, xsa,
-                  inv_rms);
+  // a warp per token; small batches spread over more SMs (2 warps per CTA)
+  const int wpb = T <= 512 ? 2 : 8;
+  return launch_k(bq_norm_quant_kernel, dim3((T + wpb - 1) / wpb), dim3(32 * wpb), 0, s, x, gamma, T, xi8,
+                  xsa, inv_rms);
 }
 
 cudaError_t launch_block_quant(const uint16_t* bucket, long rows, int8_t* qi8, float* sa,
@@ -175,7 +177,8 @@ cudaError_t launch_block_quant(const uint16_t* bucket, long rows, int8_t* qi8, f
 cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int T, uint16_t* out,
                                  float* inv_rms, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  return launch_k(rms_norm_bf16_kernel, dim3((T + 7) / 8), dim3(256), 0, s, x, gamma, T, out,
+  const int wpb = T <= 512 ? 2 : 8;
+  return launch_k(rms_norm_bf16_kernel, dim3((T + wpb - 1) / wpb), dim3(32 * wpb), 0, s, x, gamma, T, out,
                   inv_rms);
 }
 

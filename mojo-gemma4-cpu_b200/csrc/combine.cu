@@ -36,7 +36,9 @@ combine_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict_
   }
   __syncthreads();
   const int n = s_n;
-  for (int c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
+  // gridDim.y CTAs share the token's row (column slices)
+  const int per = (H / 4) / gridDim.y;
+  for (int c4 = blockIdx.y * per + threadIdx.x; c4 < (blockIdx.y + 1) * per; c4 += blockDim.x) {
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     for (int k = 0; k < n; ++k) {
       const float4 y = *reinterpret_cast<const float4*>(ybuf + (size_t)s_pos[k] * H + c4 * 4);
@@ -109,7 +111,9 @@ cudaError_t launch_combine_post(const int32_t* route_idx, const int32_t* route_p
 cudaError_t launch_combine(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
                            int T, uint16_t* out, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  return launch_k(combine_kernel, dim3(T), dim3(352), 0, s, route_idx, route_pos, ybuf, T, out);
+  // small batches: two CTAs per token (half a row each) to spread the reads
+  const int split = T < 256 ? 2 : 1;
+  return launch_k(combine_kernel, dim3(T, split), dim3(352), 0, s, route_idx, route_pos, ybuf, T, out);
 }
 
 }  // namespace gm

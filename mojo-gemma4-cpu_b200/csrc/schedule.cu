@@ -83,6 +83,7 @@ __device__ void schedule_body(const int32_t* __restrict__ route_idx,
   __syncthreads();
 
   for (int c0 = 0; c0 < T; c0 += 1024) {
+    const int nw = min(32, (T - c0 + 31) >> 5);  // mask words holding this chunk's tokens
     for (int i = tid; i < epr * 32; i += 1024) mask[i >> 5][i & 31] = 0u;
     __syncthreads();
     const int t = c0 + tid;
@@ -101,7 +102,7 @@ __device__ void schedule_body(const int32_t* __restrict__ route_idx,
     __syncthreads();
     if (tid < epr) {
       int s = 0;
-      for (int w = 0; w < 32; ++w) {
+      for (int w = 0; w < nw; ++w) {
         wpre[tid][w] = s;
         s += __popc(mask[tid][w]);
       }
@@ -314,13 +315,13 @@ cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, int T, int3
                                  int32_t* chunk_off, int32_t* counts, cudaStream_t s) {
   // one CTA when the logits arrive reduced (small T); otherwise the top-8 is
   // spread over T/4 CTAs first
-  if (T <= 1024 && router_ksplit(T) == 1)
+  if (T <= 32 && router_ksplit(T) == 1)
     return launch_k(topk_schedule_kernel, dim3(1), dim3(1024), 0, s, logits, router_ksplit(T), pes,
                     T, route_idx, route_w, expert_base, epr, route_chunk, expert_offset, routes,
                     route_pos, chunk_off);
   cudaError_t e = launch_topk(logits, pes, T, route_idx, route_w, s);
   if (e != cudaSuccess) return e;
-  if (counts)
+  if (counts && T > 1024)
     return launch_schedule_multi(route_idx, route_w, T, expert_base, epr, route_chunk, counts,
                                  expert_offset, routes, route_pos, chunk_off, s);
   return launch_build_schedule(route_idx, route_w, T, expert_base, epr, route_chunk, expert_offset,
