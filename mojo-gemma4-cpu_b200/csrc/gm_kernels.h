@@ -44,9 +44,9 @@ int handle_fail(::gm_moe* h, int code, const char* msg);
 
 int max_route_chunks(int T, int epr, int rc);
 // The router writes ROUTER_SLICES split-K partial logit slices [slice][T][E];
-// router_ksplit(T) is how many of them the top-8 kernels sum: below
-// ROUTER_TC_MIN_TOKENS the FMA kernel reduces them itself into slice 0 (1),
-// at and above it the partials stay separate (ROUTER_SLICES).
+// router_ksplit(T) is how many of them the top-8 kernels sum: up to 32 tokens
+// the FMA kernel reduces them itself into slice 0 (1), above the partials stay
+// separate (ROUTER_SLICES) and the top-8 kernel sums them in slice order.
 constexpr int ROUTER_SLICES = H / 256;
 int router_ksplit(int T);
 // Tile counters of the FMA kernel's in-kernel reduction (ints, zero between calls).

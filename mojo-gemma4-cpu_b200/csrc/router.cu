@@ -141,7 +141,10 @@ topk_softmax_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __re
   topk_token(logits, ksplit, pes, T, t, threadIdx.x & 31, route_idx, route_w);
 }
 
-int router_ksplit(int T) { return T >= ROUTER_TC_MIN_TOKENS ? ROUTER_SLICES : 1; }
+// Up to 32 tokens the one-CTA top-8 + schedule kernel runs, so the router
+// reduces its K slices itself (tile counters); above, the top-8 kernel (T/4
+// CTAs) sums the slices while it loads them.
+int router_ksplit(int T) { return T > 32 ? ROUTER_SLICES : 1; }
 
 int router_tile_counters(int T) { return (T + 7) / 8 * (E / 32); }
 
@@ -154,9 +157,9 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const ui
                                  const float* inv_rms, int T, float* logits, int* err,
                                  int* tile_counters, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  if (T >= ROUTER_TC_MIN_TOKENS) {
-    if (err) return launch_router_logits_tc(x, wr, rscale, inv_rms, T, logits, err, s);
-    tile_counters = nullptr;  // ROUTER_SLICES separate partials, as the tcgen05 kernel leaves them
+  if (T >= ROUTER_TC_MIN_TOKENS && err) return launch_router_logits_tc(x, wr, rscale, inv_rms, T, logits, err, s);
+  if (router_ksplit(T) > 1) {
+    tile_counters = nullptr;  // ROUTER_SLICES separate partials, summed by the top-8 kernel
   } else if (!tile_counters) {
     return cudaErrorInvalidValue;
   }
