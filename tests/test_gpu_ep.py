@@ -79,6 +79,22 @@ def worker(rank, fmt, T, uid, tmp, placement=None):
     torch.cuda.synchronize()
     assert ep.device_status() == 0
     np.save(os.path.join(tmp, "ffn%d.npy" % rank), synth.to_numpy(x_main))
+    if fmt == "bq":
+        # the whole FFN under expert parallelism: the dense MLP (replicated) on
+        # the dense stream, joined before the EP final sum's post tail, equals
+        # the MoE tail given that dense MLP's output
+        D = synth.dense_layer(synth.make_dense(seed=77, device="cuda"))
+        ep.register_dense(0, D["gate"], D["gate_scale"], D["up"], D["up_scale"], D["down"],
+                          D["down_scale"], D["pre_ffn_norm"])
+        x0 = x_all[rank * T:(rank + 1) * T]
+        dense_loc = torch.empty(T, gmoe.HIDDEN, dtype=torch.bfloat16, device="cuda")
+        ep.dense_forward(0, x0, dense_loc, T)
+        a = x0.clone()
+        ep.forward_ffn(0, a, dense_loc, T)
+        b = x0.clone()
+        ep.ffn_forward(0, b, T)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b)
     np.save(os.path.join(tmp, "dense.npy"), synth.to_numpy(dense_all))
     np.save(os.path.join(tmp, "gains.npy"), np.stack([synth.to_numpy(g_) for g_ in gains]))
     # plain degree-2 handle: this rank's partial over all tokens
