@@ -138,3 +138,52 @@ def test_flash_decode_matches_float64(cfg):
         outs.append(got)
     # the split count changes only rounding
     assert np.abs(outs[0] - outs[2]).max() <= 1e-2 * np.abs(ref).max()
+
+
+def run_scenario_oracle(n_splits=4):
+    """The reference test's ten steps through the oracle (prep into the
+    paged cache, then the flash decode of every token of the step); returns
+    per step (tokens, q_i8, f_q, output) and the final cache."""
+    import attention_scenario as S
+    n_slots = S.NUM_PAGES * S.PAGE_LEN
+    kvs = S.NUM_KV * S.HEAD_DIM
+    kc = np.zeros((n_slots, kvs), np.int8)
+    vc = np.zeros_like(kc)
+    ks = np.zeros((n_slots, S.NUM_KV), np.float32)
+    vs = np.zeros_like(ks)
+    cos, sin = S.identity_rope()
+    g = S.unit_gain()
+    steps = []
+    for step in range(len(S.STEPS)):
+        toks, _ = S.step_tokens(step)
+        q, k, v = S.step_inputs(step)
+        pos = np.array([p for _, p in toks], np.int32)
+        slot = np.array([S.ring_slot(p, seq) for seq, p in toks], np.int32)
+        q_i8, qb, fq, kc1, ks1, vc1, vs1 = O.bq_attn_prep(
+            q, k, v, g, g, pos, slot, S.HEAD_DIM, S.NUM_Q, S.NUM_KV, 128, 128, cos, sin, n_slots)
+        kc[slot], ks[slot], vc[slot], vs[slot] = kc1[slot], ks1[slot], vc1[slot], vs1[slot]
+        lists = [S.window_slots(seq, p) for seq, p in toks]
+        kv_len = np.array([len(x) for x in lists], np.int32)
+        slots = np.zeros((len(toks), S.WINDOW), np.int32)
+        for t, x in enumerate(lists):
+            slots[t, :len(x)] = x
+        out = O.bq_flash_decode(q_i8, qb, fq, kc, ks, vc, vs, slots, kv_len, S.HEAD_DIM, S.NUM_Q,
+                                S.NUM_KV, n_splits)
+        steps.append((toks, q_i8, fq, out, (kc.copy(), ks.copy(), vc.copy(), vs.copy())))
+    return steps
+
+
+def test_reference_sliding_attention_scenario():
+    """The scenario and acceptance bound of the reference's own test
+    (tests/test_sliding_attention_degree_parity.mojo): every token of every
+    step within 0.05 of its f32 exact-exp reference_head."""
+    import attention_scenario as S
+    worst = 0.0
+    for toks, q_i8, fq, out, (kc, ks, vc, vs) in run_scenario_oracle():
+        got = O.bf16_to_f32(out)
+        for t, (seq, p) in enumerate(toks):
+            for h in range(S.NUM_Q):
+                ref = S.reference_head(kc, ks, vc, vs, seq, p, q_i8[t, h * S.HEAD_DIM:(h + 1) * S.HEAD_DIM],
+                                       fq[t, h], h)
+                worst = max(worst, float(np.abs(got[t, h * S.HEAD_DIM:(h + 1) * S.HEAD_DIM] - ref).max()))
+    assert worst <= S.TOL, worst

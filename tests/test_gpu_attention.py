@@ -146,3 +146,57 @@ def test_attention_decode_matches_oracle(cfg, window, page_mask, positions):
         gmoe.call("gm_bq_attention_decode", dev(c["q_i8"]), dev(c["fq"]), dev(c["kc"]), dev(c["ks"]),
                   dev(c["vc"]), dev(c["vs"]), dev(runs_array(c["runs"])), dev(c["base_rows"]), T, hd, nq,
                   nkv, window, 1, 0, SHIFT, PAGE - 1, page_mask, c["max_kv"], out, ws, ws_bytes - 4, None)
+
+
+def test_reference_sliding_attention_scenario_on_gpu():
+    """The reference's own sliding-attention test scenario
+    (tests/test_sliding_attention_degree_parity.mojo: three sequences on
+    two-page rings, ten steps of prefill chunks and decode tokens) through the
+    C ABI: the prep of every step (multi-token runs) writes the same cache and
+    q_i8 as the oracle, bit for bit, and every token's attention output is
+    within the reference test's bound (0.05) of its f32 reference_head."""
+    import attention_scenario as S
+    from test_attention_oracle import run_scenario_oracle
+    oracle_steps = run_scenario_oracle()
+    n_slots = S.NUM_PAGES * S.PAGE_LEN
+    kvs = S.NUM_KV * S.HEAD_DIM
+    kc = torch.zeros(n_slots, kvs, dtype=torch.int8, device="cuda")
+    vc = torch.zeros_like(kc)
+    ks = torch.zeros(n_slots, S.NUM_KV, dtype=torch.float32, device="cuda")
+    vs = torch.zeros_like(ks)
+    cos, sin = S.identity_rope()
+    g = dev(S.unit_gain())
+    base_rows = dev(np.concatenate([S.base_rows(q) for q in range(3)]))
+    worst = 0.0
+    for step, (toks, q_o, fq_o, out_o, cache_o) in enumerate(oracle_steps):
+        T = len(toks)
+        _, runs = S.step_tokens(step)
+        q, k, v = S.step_inputs(step)
+        prep_runs = runs_array([(b, p, 2 * seq, 2) for b, p, seq in runs])
+        q_i8 = torch.empty(T, S.NUM_Q * S.HEAD_DIM, dtype=torch.int8, device="cuda")
+        qb = torch.empty(T, S.NUM_Q, dtype=torch.float32, device="cuda")
+        fq = torch.empty_like(qb)
+        gmoe.call("gm_bq_attn_prep", dev(q), dev(k), dev(v), g, g, q_i8, qb, fq, kc, ks, vc, vs,
+                  dev(cos), dev(sin), dev(prep_runs), len(runs), base_rows, T, S.HEAD_DIM, S.NUM_Q,
+                  S.NUM_KV, 128, 128, 1, 0, 6, S.PAGE_LEN - 1, S.RING_PAGES - 1, None)
+        # every token (prefill chunks too) as the newest position of its own run
+        tok_runs = runs_array([(t, p, 2 * seq, 2) for t, (seq, p) in enumerate(toks)])
+        wsb = gmoe.lib().gm_bq_attention_workspace_bytes(T, S.HEAD_DIM, S.NUM_Q, S.NUM_KV, S.WINDOW)
+        ws = torch.empty(wsb // 4 + 1, dtype=torch.float32, device="cuda")
+        out = torch.empty(T, S.NUM_Q * S.HEAD_DIM, dtype=torch.bfloat16, device="cuda")
+        gmoe.call("gm_bq_attention_decode", q_i8, fq, kc, ks, vc, vs, dev(tok_runs), base_rows, T,
+                  S.HEAD_DIM, S.NUM_Q, S.NUM_KV, S.WINDOW, 1, 0, 6, S.PAGE_LEN - 1, S.RING_PAGES - 1,
+                  S.WINDOW, out, ws, wsb, None)
+        torch.cuda.synchronize()
+        assert np.array_equal(host(q_i8), q_o) and np.array_equal(host(fq), fq_o)
+        kc_o, ks_o, vc_o, vs_o = cache_o
+        assert np.array_equal(host(kc), kc_o) and np.array_equal(host(vc), vc_o)
+        assert np.array_equal(host(ks), ks_o) and np.array_equal(host(vs), vs_o)
+        got = O.bf16_to_f32(host(out))
+        assert np.abs(got - O.bf16_to_f32(out_o)).max() <= 2e-2
+        for t, (seq, p) in enumerate(toks):
+            for h in range(S.NUM_Q):
+                ref = S.reference_head(kc_o, ks_o, vc_o, vs_o, seq, p,
+                                       q_o[t, h * S.HEAD_DIM:(h + 1) * S.HEAD_DIM], fq_o[t, h], h)
+                worst = max(worst, float(np.abs(got[t, h * S.HEAD_DIM:(h + 1) * S.HEAD_DIM] - ref).max()))
+    assert worst <= S.TOL, worst
