@@ -140,50 +140,57 @@ def test_flash_decode_matches_float64(cfg):
     assert np.abs(outs[0] - outs[2]).max() <= 1e-2 * np.abs(ref).max()
 
 
-def run_scenario_oracle(n_splits=4):
-    """The reference test's ten steps through the oracle (prep into the
-    paged cache, then the flash decode of every token of the step); returns
-    per step (tokens, q_i8, f_q, output) and the final cache."""
+def run_scenario_oracle(n_splits=4, full=False):
+    """A reference test's ten steps through the oracle (prep into the paged
+    cache, then the flash decode of every token of the step); per step
+    (tokens, q_i8, f_q, output, cache after the step)."""
     import attention_scenario as S
-    n_slots = S.NUM_PAGES * S.PAGE_LEN
-    kvs = S.NUM_KV * S.HEAD_DIM
+    if full:
+        hd, nq, nkv, rh, ps = S.FULL_HEAD_DIM, S.FULL_NUM_Q, S.FULL_NUM_KV, 64, 256
+        n_slots, slot_of, slots_of = S.FULL_NUM_PAGES * S.PAGE_LEN, S.full_slot, S.full_slots
+    else:
+        hd, nq, nkv, rh, ps = S.HEAD_DIM, S.NUM_Q, S.NUM_KV, 128, 128
+        n_slots, slot_of, slots_of = S.NUM_PAGES * S.PAGE_LEN, S.ring_slot, S.window_slots
+    kvs = nkv * hd
     kc = np.zeros((n_slots, kvs), np.int8)
     vc = np.zeros_like(kc)
-    ks = np.zeros((n_slots, S.NUM_KV), np.float32)
+    ks = np.zeros((n_slots, nkv), np.float32)
     vs = np.zeros_like(ks)
-    cos, sin = S.identity_rope()
-    g = S.unit_gain()
+    cos, sin = S.identity_rope(rh)
+    g = S.unit_gain(hd)
     steps = []
     for step in range(len(S.STEPS)):
         toks, _ = S.step_tokens(step)
-        q, k, v = S.step_inputs(step)
+        q, k, v = S.step_inputs(step, hd, nq, nkv)
         pos = np.array([p for _, p in toks], np.int32)
-        slot = np.array([S.ring_slot(p, seq) for seq, p in toks], np.int32)
+        slot = np.array([slot_of(p, seq) for seq, p in toks], np.int32)
         q_i8, qb, fq, kc1, ks1, vc1, vs1 = O.bq_attn_prep(
-            q, k, v, g, g, pos, slot, S.HEAD_DIM, S.NUM_Q, S.NUM_KV, 128, 128, cos, sin, n_slots)
+            q, k, v, g, g, pos, slot, hd, nq, nkv, rh, ps, cos, sin, n_slots)
         kc[slot], ks[slot], vc[slot], vs[slot] = kc1[slot], ks1[slot], vc1[slot], vs1[slot]
-        lists = [S.window_slots(seq, p) for seq, p in toks]
+        lists = [slots_of(seq, p) for seq, p in toks]
         kv_len = np.array([len(x) for x in lists], np.int32)
-        slots = np.zeros((len(toks), S.WINDOW), np.int32)
+        slots = np.zeros((len(toks), max(kv_len)), np.int32)
         for t, x in enumerate(lists):
             slots[t, :len(x)] = x
-        out = O.bq_flash_decode(q_i8, qb, fq, kc, ks, vc, vs, slots, kv_len, S.HEAD_DIM, S.NUM_Q,
-                                S.NUM_KV, n_splits)
+        out = O.bq_flash_decode(q_i8, qb, fq, kc, ks, vc, vs, slots, kv_len, hd, nq, nkv, n_splits)
         steps.append((toks, q_i8, fq, out, (kc.copy(), ks.copy(), vc.copy(), vs.copy())))
     return steps
 
 
-def test_reference_sliding_attention_scenario():
-    """The scenario and acceptance bound of the reference's own test
-    (tests/test_sliding_attention_degree_parity.mojo): every token of every
-    step within 0.05 of its f32 exact-exp reference_head."""
+@pytest.mark.parametrize("full", [False, True], ids=["sliding", "full"])
+def test_reference_attention_scenario(full):
+    """The scenarios and acceptance bound of the reference's own tests
+    (tests/test_sliding_attention_degree_parity.mojo,
+    tests/test_full_attention_degree_parity.mojo at degree 1): every token of
+    every step within 0.05 of its f32 exact-exp reference_head."""
     import attention_scenario as S
+    hd, nq = (S.FULL_HEAD_DIM, S.FULL_NUM_Q) if full else (S.HEAD_DIM, S.NUM_Q)
     worst = 0.0
-    for toks, q_i8, fq, out, (kc, ks, vc, vs) in run_scenario_oracle():
+    for toks, q_i8, fq, out, (kc, ks, vc, vs) in run_scenario_oracle(full=full):
         got = O.bf16_to_f32(out)
         for t, (seq, p) in enumerate(toks):
-            for h in range(S.NUM_Q):
-                ref = S.reference_head(kc, ks, vc, vs, seq, p, q_i8[t, h * S.HEAD_DIM:(h + 1) * S.HEAD_DIM],
-                                       fq[t, h], h)
-                worst = max(worst, float(np.abs(got[t, h * S.HEAD_DIM:(h + 1) * S.HEAD_DIM] - ref).max()))
+            for h in range(nq):
+                ref = S.reference_head(kc, ks, vc, vs, seq, p, q_i8[t, h * hd:(h + 1) * hd], fq[t, h], h,
+                                       full=full)
+                worst = max(worst, float(np.abs(got[t, h * hd:(h + 1) * hd] - ref).max()))
     assert worst <= S.TOL, worst

@@ -148,45 +148,54 @@ def test_attention_decode_matches_oracle(cfg, window, page_mask, positions):
                   nkv, window, 1, 0, SHIFT, PAGE - 1, page_mask, c["max_kv"], out, ws, ws_bytes - 4, None)
 
 
-def test_reference_sliding_attention_scenario_on_gpu():
-    """The reference's own sliding-attention test scenario
-    (tests/test_sliding_attention_degree_parity.mojo: three sequences on
-    two-page rings, ten steps of prefill chunks and decode tokens) through the
+@pytest.mark.parametrize("full", [False, True], ids=["sliding", "full"])
+def test_reference_attention_scenario_on_gpu(full):
+    """The reference's own attention test scenarios
+    (tests/test_sliding_attention_degree_parity.mojo,
+    tests/test_full_attention_degree_parity.mojo at degree 1: three sequences
+    on paged caches, ten steps of prefill chunks and decode tokens) through the
     C ABI: the prep of every step (multi-token runs) writes the same cache and
     q_i8 as the oracle, bit for bit, and every token's attention output is
-    within the reference test's bound (0.05) of its f32 reference_head."""
+    within the reference tests' bound (0.05) of their f32 reference_head."""
     import attention_scenario as S
     from test_attention_oracle import run_scenario_oracle
-    oracle_steps = run_scenario_oracle()
-    n_slots = S.NUM_PAGES * S.PAGE_LEN
-    kvs = S.NUM_KV * S.HEAD_DIM
+    oracle_steps = run_scenario_oracle(full=full)
+    if full:
+        hd, nq, nkv, rh, ps = S.FULL_HEAD_DIM, S.FULL_NUM_Q, S.FULL_NUM_KV, 64, 256
+        n_slots, window, page_mask, max_kv = S.FULL_NUM_PAGES * S.PAGE_LEN, 0, -1, 256
+        lists = [S.full_base_rows(q) for q in range(3)]
+    else:
+        hd, nq, nkv, rh, ps = S.HEAD_DIM, S.NUM_Q, S.NUM_KV, 128, 128
+        n_slots, window, page_mask, max_kv = S.NUM_PAGES * S.PAGE_LEN, S.WINDOW, S.RING_PAGES - 1, S.WINDOW
+        lists = [S.base_rows(q) for q in range(3)]
+    rows_off = np.cumsum([0] + [len(x) for x in lists])[:3]
+    kvs = nkv * hd
     kc = torch.zeros(n_slots, kvs, dtype=torch.int8, device="cuda")
     vc = torch.zeros_like(kc)
-    ks = torch.zeros(n_slots, S.NUM_KV, dtype=torch.float32, device="cuda")
+    ks = torch.zeros(n_slots, nkv, dtype=torch.float32, device="cuda")
     vs = torch.zeros_like(ks)
-    cos, sin = S.identity_rope()
-    g = dev(S.unit_gain())
-    base_rows = dev(np.concatenate([S.base_rows(q) for q in range(3)]))
+    cos, sin = S.identity_rope(rh)
+    g = dev(S.unit_gain(hd))
+    base_rows = dev(np.concatenate(lists))
     worst = 0.0
     for step, (toks, q_o, fq_o, out_o, cache_o) in enumerate(oracle_steps):
         T = len(toks)
         _, runs = S.step_tokens(step)
-        q, k, v = S.step_inputs(step)
-        prep_runs = runs_array([(b, p, 2 * seq, 2) for b, p, seq in runs])
-        q_i8 = torch.empty(T, S.NUM_Q * S.HEAD_DIM, dtype=torch.int8, device="cuda")
-        qb = torch.empty(T, S.NUM_Q, dtype=torch.float32, device="cuda")
+        q, k, v = S.step_inputs(step, hd, nq, nkv)
+        prep_runs = runs_array([(b, p, rows_off[seq], len(lists[seq])) for b, p, seq in runs])
+        q_i8 = torch.empty(T, nq * hd, dtype=torch.int8, device="cuda")
+        qb = torch.empty(T, nq, dtype=torch.float32, device="cuda")
         fq = torch.empty_like(qb)
         gmoe.call("gm_bq_attn_prep", dev(q), dev(k), dev(v), g, g, q_i8, qb, fq, kc, ks, vc, vs,
-                  dev(cos), dev(sin), dev(prep_runs), len(runs), base_rows, T, S.HEAD_DIM, S.NUM_Q,
-                  S.NUM_KV, 128, 128, 1, 0, 6, S.PAGE_LEN - 1, S.RING_PAGES - 1, None)
+                  dev(cos), dev(sin), dev(prep_runs), len(runs), base_rows, T, hd, nq, nkv, rh, ps,
+                  1, 0, 6, S.PAGE_LEN - 1, page_mask, None)
         # every token (prefill chunks too) as the newest position of its own run
-        tok_runs = runs_array([(t, p, 2 * seq, 2) for t, (seq, p) in enumerate(toks)])
-        wsb = gmoe.lib().gm_bq_attention_workspace_bytes(T, S.HEAD_DIM, S.NUM_Q, S.NUM_KV, S.WINDOW)
+        tok_runs = runs_array([(t, p, rows_off[seq], len(lists[seq])) for t, (seq, p) in enumerate(toks)])
+        wsb = gmoe.lib().gm_bq_attention_workspace_bytes(T, hd, nq, nkv, max_kv)
         ws = torch.empty(wsb // 4 + 1, dtype=torch.float32, device="cuda")
-        out = torch.empty(T, S.NUM_Q * S.HEAD_DIM, dtype=torch.bfloat16, device="cuda")
+        out = torch.empty(T, nq * hd, dtype=torch.bfloat16, device="cuda")
         gmoe.call("gm_bq_attention_decode", q_i8, fq, kc, ks, vc, vs, dev(tok_runs), base_rows, T,
-                  S.HEAD_DIM, S.NUM_Q, S.NUM_KV, S.WINDOW, 1, 0, 6, S.PAGE_LEN - 1, S.RING_PAGES - 1,
-                  S.WINDOW, out, ws, wsb, None)
+                  hd, nq, nkv, window, 1, 0, 6, S.PAGE_LEN - 1, page_mask, max_kv, out, ws, wsb, None)
         torch.cuda.synchronize()
         assert np.array_equal(host(q_i8), q_o) and np.array_equal(host(fq), fq_o)
         kc_o, ks_o, vc_o, vs_o = cache_o
@@ -195,8 +204,8 @@ def test_reference_sliding_attention_scenario_on_gpu():
         got = O.bf16_to_f32(host(out))
         assert np.abs(got - O.bf16_to_f32(out_o)).max() <= 2e-2
         for t, (seq, p) in enumerate(toks):
-            for h in range(S.NUM_Q):
-                ref = S.reference_head(kc_o, ks_o, vc_o, vs_o, seq, p,
-                                       q_o[t, h * S.HEAD_DIM:(h + 1) * S.HEAD_DIM], fq_o[t, h], h)
-                worst = max(worst, float(np.abs(got[t, h * S.HEAD_DIM:(h + 1) * S.HEAD_DIM] - ref).max()))
+            for h in range(nq):
+                ref = S.reference_head(kc_o, ks_o, vc_o, vs_o, seq, p, q_o[t, h * hd:(h + 1) * hd],
+                                       fq_o[t, h], h, full=full)
+                worst = max(worst, float(np.abs(got[t, h * hd:(h + 1) * hd] - ref).max()))
     assert worst <= S.TOL, worst
