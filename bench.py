@@ -65,6 +65,7 @@ EXTRA = {
     "attn-decode-sliding-b64": ("attn-sliding", 64),
     "attn-decode-full-b64": ("attn-full", 64),
 }
+EXTRA_TRAFFIC = {"attn-decode-full-b64": 541_900_000 + 14_200_000}
 DENSE_I = 2112
 DENSE_BYTES = 3 * DENSE_I * H + 2 * DENSE_I * 4 + H * 4       # int8 weights + row scales
 ATTN = {  # head_dim, query heads, KV heads, window (0 = full), KV positions, pages per sequence
@@ -497,7 +498,9 @@ def run_extra(args):
                                                    "l2": "KV cache %.0f MB per step (larger than L2)"
                                                          % (T * kv * nkv * 2 * hd / 1e6)}})
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = None
+    # DRAM bytes per call of the dominant kernel from the ncu capture of the
+    # same command (profiles/attn_decode_full_b64.md); None elsewhere
+    roof["traffic"] = EXTRA_TRAFFIC.get(args.workload)
     line.update({"value": T * args.steps / (ms / 1e3), "unit": "tokens/s", "ms_per_step": per_step,
                  "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": e2e_io[0],
                          "d2h_bytes_per_step": e2e_io[1]},
