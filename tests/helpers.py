@@ -1,5 +1,9 @@
 """Shared test helpers: seeded raw layers and the oracle-side preparation of
 the butterquant / bf16 layer (the checker's own copy of every tensor)."""
+import hashlib
+import json
+import os
+
 import numpy as np
 
 from oracle import oracle as O
@@ -32,6 +36,41 @@ def raw_layer_np(seed=1234, weight_std=0.02, router_std=0.02, stress=False):
         L["per_expert_scale"] = np.full(E, one, np.uint16)
         L["pre_ffn_norm_2"] = np.full(H, one, np.uint16)
     return L
+
+
+_STRESS = []
+
+
+def stress_layer():
+    """The stress layer of the parity tests (seed 4321, router std 1.0, gains
+    ~ N(1, 0.25) with negatives) and its oracle preparation, generated once
+    per process (about 40 s of numpy normals); callers must not modify it."""
+    if not _STRESS:
+        raw = raw_layer_np(seed=4321, router_std=1.0, stress=True)
+        _STRESS.append((raw, oracle_bq_layer(raw)))
+    return _STRESS[0]
+
+
+GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def digest(a):
+    """SHA-256 of an array's bytes, with its dtype and shape."""
+    a = np.ascontiguousarray(a)
+    return {"sha256": hashlib.sha256(a.tobytes()).hexdigest(), "dtype": a.dtype.str,
+            "shape": list(a.shape)}
+
+
+def golden(name):
+    """Arrays of the golden fixture tests/golden/<name>.npz."""
+    with np.load(os.path.join(GOLDEN_DIR, name + ".npz")) as z:
+        return {k: z[k] for k in z.files}
+
+
+def golden_digests():
+    """The digests of tests/golden/digests.json, keyed "<fixture>/<name>"."""
+    with open(os.path.join(GOLDEN_DIR, "digests.json")) as f:
+        return json.load(f)
 
 
 def tokens_np(T, seed=99, std=1.0):
@@ -137,7 +176,6 @@ def write_safetensors(path, entries):
     the JSON header padded with spaces to a multiple of 8, then the data.
     entries: list of (name, array, tag or None, shape or None); uint16 arrays
     are bf16 bit patterns unless a tag says otherwise."""
-    import json
     head, blobs, off = {}, [], 0
     for name, arr, tag, shape in entries:
         a = np.ascontiguousarray(arr)

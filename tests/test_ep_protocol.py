@@ -14,7 +14,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from oracle import oracle as O
-from helpers import raw_layer_np, tokens_np, oracle_bq_layer
+from helpers import stress_layer, tokens_np
 
 H, E, I, GU, TOPK = O.H, O.E, O.I, O.GU, O.TOPK
 WORLD, T_RANK = 2, 24
@@ -131,8 +131,7 @@ def free_port():
 
 @pytest.fixture(scope="module")
 def layer_ref():
-    raw = raw_layer_np(seed=4321, router_std=1.0, stress=True)
-    return oracle_bq_layer(raw)
+    return stress_layer()[1]
 
 
 def test_ep_protocol_matches_degree2_oracle(tmp_path, layer_ref):

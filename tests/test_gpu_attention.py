@@ -15,6 +15,8 @@ import torch
 import gmoe
 from oracle import oracle as O
 from test_attention_oracle import SLIDING, FULL, bf, rope_tables, random_cache, decode_f64
+import golden_cases as G
+from helpers import golden
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")]
@@ -203,6 +205,12 @@ def test_reference_attention_scenario_on_gpu(full):
         assert np.array_equal(host(ks), ks_o) and np.array_equal(host(vs), vs_o)
         got = O.bf16_to_f32(host(out))
         assert np.abs(got - O.bf16_to_f32(out_o)).max() <= 2e-2
+        if step in G.ATTN_STEPS:
+            # the committed golden vectors of the same step
+            name = "full" if full else "sliding"
+            ga = golden("attention")
+            assert np.array_equal(host(fq), ga[f"{name}_fq_s{step}"])
+            assert np.abs(got - O.bf16_to_f32(ga[f"{name}_out_s{step}"])).max() <= 2e-2
         for t, (seq, p) in enumerate(toks):
             for h in range(nq):
                 ref = S.reference_head(kc_o, ks_o, vc_o, vs_o, seq, p, q_o[t, h * hd:(h + 1) * hd],

@@ -13,7 +13,8 @@ import torch
 import gmoe
 import synth
 from oracle import oracle as O
-from helpers import raw_dense_np, oracle_dense_layer, raw_layer_np, tokens_np, rel_err
+import golden_cases as G
+from helpers import raw_dense_np, oracle_dense_layer, raw_layer_np, tokens_np, rel_err, golden
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")]
@@ -65,6 +66,13 @@ def test_dense_stages_bit_exact(dense, T):
     assert np.array_equal(host(h_sa), hs)
     want = O.bq_block_linear(hq, hs, d["wd"], d["wds"], d["wdcs"])
     assert np.array_equal(host(out), want)
+    if T == G.DENSE_T:
+        # the committed golden vectors of the same inputs
+        gd = golden("dense_mlp")
+        assert np.array_equal(host(h_bf), gd["bucket"])
+        assert np.array_equal(host(h_i8), gd["bucket_q"])
+        assert np.array_equal(host(h_sa), gd["bucket_sa"])
+        assert np.array_equal(host(out), gd["out"])
 
 
 @pytest.mark.parametrize("T", [3, 64, 700])

@@ -14,8 +14,9 @@ import torch
 import gmoe
 import synth
 from oracle import oracle as O
+import golden_cases as G
 from helpers import (raw_layer_np, tokens_np, oracle_bq_layer, oracle_bf16_layer, rel_err,
-                     topk_margin, routes_by_expert)
+                     topk_margin, routes_by_expert, stress_layer, golden, golden_digests, digest)
 
 pytestmark = pytest.mark.gpu
 
@@ -46,8 +47,8 @@ def layer_default():
 
 @pytest.fixture(scope="module")
 def layer_stress():
-    raw = raw_layer_np(seed=4321, router_std=1.0, stress=True)
-    return raw, oracle_bq_layer(raw), synth.bq_layer(raw_to_torch(raw), keep_rowmajor=True)
+    raw, ref = stress_layer()
+    return raw, ref, synth.bq_layer(raw_to_torch(raw), keep_rowmajor=True)
 
 
 def make_block(gpu_layer, max_tokens=2560, rank=0, degree=1):
@@ -122,6 +123,15 @@ def test_router_parity(T, which, layer_default, layer_stress):
         assert np.abs(w.sum(1) - 1).max() <= 1e-3
     if which == "stress":
         assert checked.mean() > 0.95
+    if which == "stress" and T == G.ROUTER_T:
+        # the committed golden vectors of the same inputs, by the same criteria
+        gs = golden("moe_stages")
+        assert np.abs(lg - gs["router_logits"]).max() <= 1e-5 * np.abs(gs["router_logits"]).max()
+        gchecked = topk_margin(gs["router_logits"]) > MARGIN
+        gi, gw = routes_by_expert(gs["router_idx"], gs["router_w"])
+        assert np.array_equal(si[gchecked], gi[gchecked])
+        gsame = (si == gi).all(axis=1)
+        assert np.abs(sw[gsame] - gw[gsame]).max(initial=0) < 1e-4
 
 
 # ----------------------------------------------------------- schedules
@@ -159,6 +169,11 @@ def test_schedule_bit_exact(T, base, epr):
     p = pos[local]
     assert np.array_equal(np.sort(p), np.arange(n))
     assert np.array_equal(routes[p, 0], np.nonzero(local)[0] // TOPK)
+    if (T, base, epr) == (G.SCHED_T, G.SCHED_BASE, G.SCHED_EPR):
+        gs = golden("moe_stages")
+        assert np.array_equal(off, gs["sched_offset"])
+        assert np.array_equal(routes[:n, 0], gs["sched_token"])
+        assert np.array_equal(routes[:n, 1].view(np.float32), gs["sched_weight"])
 
 
 # ----------------------------------------------------------- activations
@@ -175,6 +190,8 @@ def test_norm_quant_parity(T, layer_stress):
     d = np.abs(host(q).astype(np.int32) - rq.astype(np.int32))
     assert d.max() <= 1 and (d == 0).mean() > 0.999
     assert np.abs(host(sa) / rsa - 1).max() < 1e-5
+    if T == G.NORM_T:
+        assert np.abs(host(sa) / golden("moe_stages")["norm_sa"] - 1).max() < 1e-5
 
 
 def test_rms_norm_parity():
@@ -200,6 +217,9 @@ def test_block_quant_bit_exact(rows):
     rq, rsa = O.bq_block_quant(b_np)
     assert np.array_equal(host(q), rq)
     assert np.array_equal(host(sa), rsa)
+    if rows == G.BLOCK_ROWS:
+        assert digest(host(q)) == golden_digests()["moe_stages/block_q"]
+        assert np.array_equal(host(sa), golden("moe_stages")["block_sa"])
 
 
 # ----------------------------------------------------------- expert stages
@@ -298,6 +318,10 @@ def test_forward_bq(T, which, layer_default, layer_stress):
         # except where an activation scale differs in its last bit (inv_rms
         # reduction order) -- bounded by the bq tolerance above
         assert same.mean() > 0.95
+    if which == "stress" and T == G.FWD_T:
+        # the committed golden vectors of the same inputs, by the same criteria
+        gf = golden("moe_forward")
+        check_forward(host(out), gidx, gf["out"], gf["idx"], gf["logits"], TOL_BQ)
 
 
 @pytest.mark.parametrize("T", [64, 300, 1100, 2048])

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from helpers import raw_layer_np, tokens_np, oracle_bq_layer, oracle_bf16_layer, rel_err, topk_margin
+from helpers import stress_layer, tokens_np, oracle_bf16_layer, rel_err, topk_margin, routes_by_expert
 
 H, E, I, GU, TOPK = O.H, O.E, O.I, O.GU, O.TOPK
 
@@ -185,8 +185,7 @@ def test_schedule_stable_order(base, epr):
 
 @pytest.fixture(scope="module")
 def bq_small():
-    raw = raw_layer_np(seed=11, router_std=1.0, stress=True)
-    return raw, oracle_bq_layer(raw)
+    return stress_layer()
 
 
 def test_bq_forward_degree_partials_close(bq_small):
@@ -212,11 +211,14 @@ def test_bq_close_to_bf16_path(bq_small):
     is the only difference; FWHT rotations cancel): self-check (i)."""
     raw, Lq = bq_small
     Lb = oracle_bf16_layer(raw)
-    x = tokens_np(16, seed=14)
+    x = tokens_np(64, seed=14)
     ob, ib, _, lgb = O.bf16_forward(x, Lb)
     oq, iq, _, lgq = O.bq_forward(x, Lq)
-    # the centred router keeps the softmax ranking (gauge cancels)
-    keep = (ib == iq).all(axis=1)
+    # the centred router keeps the selected set (the gauge x.mean(W) shifts
+    # every logit of a token alike); only tokens whose 8th/9th margin is below
+    # the bf16 rounding of the centred weights may select differently
+    keep = (routes_by_expert(ib) == routes_by_expert(iq)).all(axis=1)
+    assert keep[topk_margin(lgb) > 1e-3].all()
     assert keep.mean() > 0.9
     assert rel_err(oq, ob, rows=keep) < 0.1
 
