@@ -55,6 +55,7 @@ ZIPF = {"bq-prefill-4k-zipf", "bf16-prefill-4k-zipf", "ep-prefill-16k"}
 # weights per layer, the attention block between layers is an identity stand-in)
 WORKLOADS["bq-decode-b64-30L"] = (64, "bq", "replicas")
 LAYERS = {"bq-decode-b64-30L": 30}
+REF_SAMPLE_TOKENS = 512   # tokens per step of the --impl reference arm (CPU)
 METRIC = "MoE-block tokens/s at 1/2/4/8 B200 (decode b=64, prefill 4k); % of roofline"
 # Workloads of the rows widened beyond the MoE block (one GPU): the whole FFN
 # (dense MLP beside the MoE, post-FFN tail; gm_ffn_forward) and butterquant
@@ -217,21 +218,24 @@ def oracle_dense_layer(O, rawd_cpu):
             "gamma": O.bake_split_gain(rawd_cpu["pre_ffn_norm"])}
 
 
+def oracle_layer(fmt, raw_cpu):
+    """The oracle's layer and forward for the workload's weight format."""
+    from oracle import oracle as O
+    if fmt == "bq":
+        return oracle_bq_layer(O, raw_cpu), O.bq_forward
+    L = {"router_proj": raw_cpu["router_proj"], "router_scale": O.bake_router_scale(raw_cpu["router_scale"]),
+         "pes": raw_cpu["per_expert_scale"], "gamma2": raw_cpu["pre_ffn_norm_2"],
+         "w_gu": raw_cpu["gate_up"], "w_dn": raw_cpu["down"]}
+    return L, O.bf16_forward
+
+
 def cpu_baseline_sample(fmt, T, seconds, raw_cpu, xs_cpu):
     """Time the oracle (CPU restatement of the reference path, all host cores)
     on forwards of the workload; returns (tokens/s at the median sample,
     samples, warm-up forwards, threads)."""
     from oracle import oracle as O
     import numpy as np
-    L = {}
-    if fmt == "bq":
-        L = oracle_bq_layer(O, raw_cpu)
-        fwd = O.bq_forward
-    else:
-        L = {"router_proj": raw_cpu["router_proj"], "router_scale": O.bake_router_scale(raw_cpu["router_scale"]),
-             "pes": raw_cpu["per_expert_scale"], "gamma2": raw_cpu["pre_ffn_norm_2"],
-             "w_gu": raw_cpu["gate_up"], "w_dn": raw_cpu["down"]}
-        fwd = O.bf16_forward
+    L, fwd = oracle_layer(fmt, raw_cpu)
     # the reference harness protocol (benchmarks/bench_harness.mojo:7,62-84):
     # up to 30 warm-up forwards, then up to 600 timed samples, rate from the
     # median sample -- bounded here by `seconds` (a fifth for the warm-up)
@@ -268,19 +272,34 @@ def run_reference(args):
     if zipf:
         layer = synth.apply_zipf(layer)
     raw = {k: synth.to_numpy(v) for k, v in layer.items()}
-    xs = [synth.to_numpy(synth.zipf_tokens(T, seed=s) if zipf else synth.make_tokens(T, seed=s))
+    # each step is one forward of a bounded sample of the workload's tokens
+    # (all of them up to REF_SAMPLE_TOKENS: the CPU's per-token rate is flat
+    # beyond a few hundred tokens), so that --steps K --warmup W ends within
+    # minutes even for the prefill workloads
+    Ts = min(T, REF_SAMPLE_TOKENS)
+    xs = [synth.to_numpy(synth.zipf_tokens(T, seed=s) if zipf else synth.make_tokens(T, seed=s))[:Ts]
           for s in range(2)]
-    # each step is one forward of T tokens; the run is bounded by --cpu-seconds
-    rate, iters, warm, cores = cpu_baseline_sample(fmt, T, max(1.0, args.cpu_seconds), raw, xs)
-    rate /= LAYERS.get(args.workload, 1)
+    from oracle import oracle as O
+    L, fwd = oracle_layer(fmt, raw)
+    fwd(xs[0][:min(Ts, 4)], L)  # page the weights in
+    for i in range(args.warmup):
+        fwd(xs[i % 2], L)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        fwd(xs[i % 2], L)
+    dt = time.perf_counter() - t0
+    cores = O.lib().orc_num_threads()
+    rate = args.steps * Ts / dt / LAYERS.get(args.workload, 1)
+    sample = ("%d warm-up + %d timed forwards of %d of the workload's %d tokens (one per step), "
+              "of the C++ restatement" % (args.warmup, args.steps, Ts, T))
     line = {"metric": METRIC, "value": rate, "unit": "tokens/s", "impl": "reference",
-            "n_gpus": args.gpus, "steps": iters, "warmup": 1, "ms_per_step": 1e3 * T / rate,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "i8" if fmt == "bq" else "bf16", "data": "synthetic",
-            "config": {"workload": args.workload, "tokens_per_step": T, "weights": fmt},
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "i8" if fmt == "bq" else "bf16", "data": "synthetic",
+            "config": {"workload": args.workload, "tokens_per_step": T, "weights": fmt,
+                       "reference_tokens_per_step": Ts},
             "cpu_baseline": dict({"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port",
-                                  "sample": "%d warm-up + %d timed forwards of %d tokens, median, of the C++ "
-                                            "restatement" % (warm, iters, T)}, **host_info()),
+                                  "sample": sample}, **host_info()),
             "e2e": {"value": rate, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
