@@ -149,6 +149,26 @@ struct Json {
     while (p < e && *p != '"') {
       const unsigned char c = (unsigned char)*p++;
       if (c < 0x20) return fail("control character in a string");
+      if (c >= 0x80) {  // a UTF-8 sequence (RFC 3629): well formed, or the header is refused
+        int n;
+        uint32_t cp;
+        if (c >= 0xC2 && c <= 0xDF) n = 1, cp = c & 0x1Fu;
+        else if (c >= 0xE0 && c <= 0xEF) n = 2, cp = c & 0x0Fu;
+        else if (c >= 0xF0 && c <= 0xF4) n = 3, cp = c & 0x07u;
+        else return fail("invalid UTF-8 in a string");
+        if (e - p < n) return fail("invalid UTF-8 in a string");
+        out.push_back((char)c);
+        for (int i = 0; i < n; ++i) {
+          const unsigned char t = (unsigned char)*p++;
+          if ((t & 0xC0) != 0x80) return fail("invalid UTF-8 in a string");
+          cp = (cp << 6) | (t & 0x3Fu);
+          out.push_back((char)t);
+        }
+        if ((n == 2 && cp < 0x800) || (n == 3 && (cp < 0x10000 || cp > 0x10FFFF)) ||
+            (cp >= 0xD800 && cp <= 0xDFFF))
+          return fail("invalid UTF-8 in a string");
+        continue;
+      }
       if (c != '\\') {
         out.push_back((char)c);
         continue;

@@ -137,7 +137,8 @@ def _stream(s):
 def check(rc, handle=None):
     if rc != 0:
         msg = lib().gm_last_error(handle)
-        raise GmoeError("%s: %s" % (STATUS.get(rc, rc), msg.decode() if msg else ""))
+        text = msg.decode(errors="backslashreplace") if msg else ""
+        raise GmoeError("%s: %s" % (STATUS.get(rc, rc), text))
     return rc
 
 

@@ -197,3 +197,64 @@ def test_large_tensor_threaded_read(tmp_path):
         ck.read_rows("big", 333, 700, part)
         assert np.array_equal(part, big[333:1033])
     os.remove(p)
+
+
+def test_utf8_names(tmp_path):
+    """Header strings are UTF-8 (the safetensors format): raw multi-byte
+    sequences are kept as they are, malformed ones (a stray continuation
+    byte, an overlong form, an encoded surrogate, a truncated sequence)
+    refuse the file."""
+    name = "exp\u00e9rt.\U0001F600"
+    hdr = ('{"%s":{"dtype":"U8","shape":[1],"data_offsets":[0,1]}}' % name).encode()
+    with gmoe.Checkpoint(_raw_file(tmp_path / "ok.safetensors", hdr, b"\x07")) as ck:
+        assert ck.names() == [name]
+        out = np.empty((1, 1), np.uint8)
+        ck.read_rows(name, 0, 1, out)
+        assert out[0, 0] == 7
+    for bad in (b"\xff", b"\x80", b"\xc0\xaf", b"\xed\xa0\x80", b"\xf4\x90\x80\x80", b"\xe2\x82"):
+        hdr = b'{"a' + bad + b'":{"dtype":"U8","shape":[1],"data_offsets":[0,1]}}'
+        with pytest.raises(gmoe.GmoeError, match="UTF-8"):
+            gmoe.Checkpoint(_raw_file(tmp_path / "bad.safetensors", hdr, b"\x07"))
+
+
+def test_mutated_headers_never_crash(tmp_path):
+    """Seeded mutations of a valid header (byte swaps, insertions, deletions,
+    deep nesting, short data, wrong header lengths): every open either
+    succeeds with readable tensors or fails with an error status."""
+    import random
+    good = (b'{"__metadata__":{"format":"pt"},"a":{"dtype":"BF16","shape":[2,3],"data_offsets":[0,12]},'
+            b'"b":{"dtype":"F32","shape":[4],"data_offsets":[12,28]}}')
+    data = bytes(range(28))
+    rng = random.Random(1234)
+    alphabet = b'{}[]":,0123456789-+.eE \\u\x00\x01\x80\xc3\xa9\xffabcdefghFBIU'
+    p = tmp_path / "f.safetensors"
+    opened = refused = 0
+    for _ in range(3000):
+        h = bytearray(good)
+        for _ in range(rng.randint(1, 6)):
+            op, i = rng.random(), rng.randrange(len(h) + 1)
+            if op < 0.4 and h:
+                h[min(i, len(h) - 1)] = rng.choice(alphabet)
+            elif op < 0.6:
+                h[i:i] = bytes(rng.choice(alphabet) for _ in range(rng.randint(1, 8)))
+            elif op < 0.8:
+                del h[i:i + rng.randint(1, 8)]
+            else:
+                h[i:i] = b"[" * rng.randint(1, 200)
+        d = data[:rng.randint(0, len(data))] if rng.random() < 0.2 else data
+        n = len(h) if rng.random() < 0.9 else rng.randint(0, 1 << 20)
+        p.write_bytes(n.to_bytes(8, "little") + bytes(h) + d)
+        try:
+            with gmoe.Checkpoint(p) as ck:
+                for nm in ck.names():
+                    _, shape = ck.info(nm)
+                    rows = shape[0] if shape else 1
+                    buf = np.zeros(max(int(np.prod(shape)) * 8, 64), np.uint8)
+                    try:
+                        ck.read_rows(nm, 0, rows, buf)
+                    except gmoe.GmoeError:
+                        pass
+            opened += 1
+        except gmoe.GmoeError:
+            refused += 1
+    assert opened > 10 and refused > 1000
