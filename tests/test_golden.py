@@ -60,3 +60,22 @@ def test_fixture_invariants():
     g = sm["gelu_x"].astype(np.float64)
     exact = 0.5 * g * (1 + np.tanh(np.sqrt(2 / np.pi) * (g + 0.044715 * g ** 3)))
     assert np.abs(sm["gelu"] - exact).max() < 1e-2
+
+
+@pytest.mark.parametrize("case", ["moe_stages", "moe_forward", "dense_mlp"])
+def test_oracle_bits_independent_of_thread_count(case):
+    """The fixtures hold on any host: the oracle's OpenMP loops split work
+    over tokens, rows or experts, never inside one sum, so 1 and 3 threads
+    give the bits of the default thread count."""
+    from oracle import oracle as O
+    L = O.lib()
+    n = L.orc_num_threads()
+    stored = golden(case)
+    try:
+        for threads in (1, 3):
+            L.orc_set_num_threads(threads)
+            _, arrays, _ = getattr(golden_cases, case)()
+            for k, a in arrays.items():
+                assert same_bits(a, stored[k]), (threads, k)
+    finally:
+        L.orc_set_num_threads(n)
