@@ -826,8 +826,13 @@ def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1,
     rw = L["router_centered"] if fmt == "bq" else L["router_proj"]
     per_batch = []
     hist_sum = torch.zeros(E, dtype=torch.long, device="cuda")
+    covered = torch.zeros((), dtype=torch.long, device="cuda")
     for x in xs:
         gmoe.call("gm_router_select", x, rw, L["router_scale"], L["per_expert_scale"], T, lg, idx, w, s)
+        # tokens whose 8th/9th logit margin exceeds 1e-3 (the parity tests'
+        # rule for a selection that must match the reference bit for bit)
+        top9 = torch.topk(lg[:T * E].view(T, E), 9, dim=1).values
+        covered += ((top9[:, 7] - top9[:, 8]) > 1e-3).sum()
         hist = torch.bincount(idx.reshape(-1).long(), minlength=E)
         if ep and dist is not None:
             dist.all_reduce(hist)
@@ -894,7 +899,8 @@ def roofline(blk, fmt, L, xs, outs, T, steps, stream, workload, rank=0, world=1,
     tokens = T * (world if ep else 1)
     load = {"max_expert_share": round(float(h.max() / h.sum()), 4),
             "expert_routes_top8": [int(v) for v in h[:8]],
-            "expert_routes_last4": [int(v) for v in h[-4:]]}
+            "expert_routes_last4": [int(v) for v in h[-4:]],
+            "top8_margin_above_1e-3": round(float(covered.item()) / (T * len(xs)), 4)}
     if ep and world > 1:
         load["routes_per_gpu"] = [int(h[owner == r].sum()) for r in range(world)]
     if workload in ZIPF:
