@@ -206,6 +206,20 @@ def test_bq_forward_tokens_independent(bq_small):
     assert np.array_equal(full[:7], part)
 
 
+def test_bq_forward_chunked_equals_unchunked(bq_small):
+    """Self-check (ii): the reference runs prefill in chunks of at most 1024
+    tokens (its scratch plan, modeling/gemma_4_moe_bq.mojo:275-360); the
+    block's output does not depend on the chunking, bit for bit."""
+    _, L = bq_small
+    x = tokens_np(1100, seed=15)
+    full, idx, w, _ = O.bq_forward(x, L)
+    a = O.bq_forward(x[:1024], L)
+    b = O.bq_forward(x[1024:], L)
+    assert np.array_equal(full, np.concatenate([a[0], b[0]]))
+    assert np.array_equal(idx, np.concatenate([a[1], b[1]]))
+    assert np.array_equal(w, np.concatenate([a[2], b[2]]))
+
+
 def test_bq_close_to_bf16_path(bq_small):
     """Butterquant output approximates the unquantised model (the int8 error
     is the only difference; FWHT rotations cancel): self-check (i)."""
