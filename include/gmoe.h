@@ -458,7 +458,9 @@ int gm_bq_attn_prep(const void* q_src, const void* k_src, const void* v_src, con
  * (attention.mojo:333-472, kernels/attention_dispatch_kernels.mojo:36-130):
  * T tokens, token t the newest position of run t (runs[t].buf_start = t).
  * Sliding (window > 0): the last min(pos+1, window) positions; full (window =
- * 0): this rank's positions 0..pos.  The KV range is split over CTAs and the
+ * 0): positions 0..pos.  cache_degree must be 1 (rank 0): a cache sharded by
+ * position over ranks would need each rank's unnormalised partials merged
+ * across ranks, which this call does not return.  The KV range is split over CTAs and the
  * splits merged as kernels/logsum_merge.mojo does; out bf16 [T][num_q *
  * head_dim], in the rotated domain as the reference's.  The signed int8 dot
  * needs no qi_bias.  max_kv_len bounds the KV length of any token (sizes the

@@ -20,7 +20,7 @@
 // register e / 16 -- the reference's 16-lane SIMD layout, so the
 // sum-of-squares chains and their lane tree are the reference's and the prep
 // is bit-exact.  Decode: CTA = (token, KV head, KV split), 256 threads,
-// tiles of 32 positions; each K and V row of the split is read once and
+// tiles of 16 positions; each K and V row of the split is read once and
 // serves every query head of the GQA group (see attn_decode_kernel); the CTA
 // writes one partial (m, l, acc) per head and a merge kernel combines the
 // splits.

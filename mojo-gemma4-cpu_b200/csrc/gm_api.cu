@@ -1434,6 +1434,13 @@ int gm_bq_attention_decode(const int8_t* q_i8, const float* f_q, const int8_t* k
   if (T < 0 || window < 0 || max_kv_len < 0)
     return set_err(nullptr, GM_EINVAL, "attention_decode: T=%d window=%d max_kv_len=%d", T, window,
                    max_kv_len);
+  // One GPU holds every position of its sequences.  A cache sharded by
+  // position (the reference's full layers at degree > 1) would need each
+  // rank's unnormalised partials (m, l, acc) merged across ranks, which this
+  // entry point does not return, so it takes the whole cache only.
+  if (cache_degree != 1)
+    return set_err(nullptr, GM_EINVAL, "attention_decode: cache_degree %d (the decode takes an "
+                   "unsharded cache: cache_degree 1)", cache_degree);
   const size_t need = gm_bq_attention_workspace_bytes(T, head_dim, num_q, num_kv, max_kv_len);
   if (workspace_bytes < need)
     return set_err(nullptr, GM_EINVAL, "attention_decode: workspace %zu bytes, %zu needed", workspace_bytes,

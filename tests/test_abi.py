@@ -82,3 +82,24 @@ def test_profile_read_rejects_null_handle():
     L = gmoe.lib()
     n, k = ctypes.c_int(0), ctypes.c_long(0)
     assert L.gm_moe_profile_read(None, None, 0, ctypes.byref(n), ctypes.byref(k)) == -1
+
+
+def test_attention_entry_points_validate_before_any_launch():
+    """Geometry and sharding checks of the stateless attention calls run on
+    the host before any CUDA call, so they answer without a GPU."""
+    L = gmoe.lib()
+    z = ctypes.c_void_p(0)
+
+    def decode(head_dim=256, num_q=16, num_kv=8, window=1024, degree=1, rank=0, T=1):
+        return L.gm_bq_attention_decode(z, z, z, z, z, z, z, z, T, head_dim, num_q, num_kv, window,
+                                        degree, rank, 6, 63, 1, 1024, z, z, ctypes.c_size_t(0), z)
+
+    assert decode(head_dim=128) == -1 and b"head_dim" in L.gm_last_error(None)
+    assert decode(num_q=12, num_kv=8) == -1 and b"num_q" in L.gm_last_error(None)
+    assert decode(degree=2, rank=1) == -1 and b"cache_degree" in L.gm_last_error(None)
+    assert decode(window=0, degree=2, rank=0) == -1 and b"cache_degree" in L.gm_last_error(None)
+    assert decode(T=1) == -1 and b"workspace" in L.gm_last_error(None)
+    assert L.gm_bq_attention_workspace_bytes(0, 256, 16, 8, 1024) == 0
+    assert L.gm_bq_attn_prep(z, z, z, z, z, z, z, z, z, z, z, z, z, z, z, 1, z, 1, 512, 16, 2, 128,
+                             128, 1, 0, 6, 63, -1, z) == -1
+    assert b"geometry" in L.gm_last_error(None)
