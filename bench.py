@@ -232,7 +232,8 @@ def oracle_layer(fmt, raw_cpu):
 def cpu_baseline_sample(fmt, T, seconds, raw_cpu, xs_cpu):
     """Time the oracle (CPU restatement of the reference path, all host cores)
     on forwards of the workload; returns (tokens/s at the median sample,
-    samples, warm-up forwards, threads)."""
+    samples, warm-up forwards, threads, per-forward ms at min / p50 / p90 /
+    p99 as the reference harness reports them)."""
     from oracle import oracle as O
     import numpy as np
     L, fwd = oracle_layer(fmt, raw_cpu)
@@ -251,7 +252,10 @@ def cpu_baseline_sample(fmt, T, seconds, raw_cpu, xs_cpu):
         fwd(x, L)
         samples.append(time.perf_counter() - ts)
     p50 = float(np.median(samples))
-    return T / p50, len(samples), warm, O.lib().orc_num_threads()
+    ms = np.asarray(samples) * 1e3
+    pct = {"min": round(float(ms.min()), 3), "p50": round(p50 * 1e3, 3),
+           "p90": round(float(np.percentile(ms, 90)), 3), "p99": round(float(np.percentile(ms, 99)), 3)}
+    return T / p50, len(samples), warm, O.lib().orc_num_threads(), pct
 
 
 def run_reference(args):
@@ -736,9 +740,10 @@ def cpu_leg(fmt, T, args, raw_dev):
         xs = [synth.to_numpy(synth.zipf_tokens(T, seed=7 + b)) for b in range(2)]
     else:
         xs = [synth.to_numpy(torch.randn(T, H, generator=g).to(torch.bfloat16)) for _ in range(2)]
-    rate, n, warm, cores = cpu_baseline_sample(fmt, T, args.cpu_seconds, raw_cpu, xs)
+    rate, n, warm, cores, pct = cpu_baseline_sample(fmt, T, args.cpu_seconds, raw_cpu, xs)
     nl = LAYERS.get(args.workload, 1)
     return dict({"value": rate / nl, "unit": "tokens/s", "cores": cores, "kind": "port",
+                 "forward_ms": pct,
                  "sample": "%d warm-up + %d timed forwards of %d tokens, median (C++ restatement of "
                            "the reference path, OpenMP)%s" % (warm, n, T, (
                                "; one layer timed, rate divided by %d layers" % nl) if nl > 1 else "")},
