@@ -103,3 +103,47 @@ def test_attention_entry_points_validate_before_any_launch():
     assert L.gm_bq_attn_prep(z, z, z, z, z, z, z, z, z, z, z, z, z, z, z, 1, z, 1, 512, 16, 2, 128,
                              128, 1, 0, 6, 63, -1, z) == -1
     assert b"geometry" in L.gm_last_error(None)
+
+
+def test_header_compiles_as_c_and_cxx_and_links(tmp_path):
+    """A C99 consumer (what Mojo's external_call, cgo or a ctypes user sees):
+    the header compiles warning-free as C99 and C++17, every declared entry
+    point links from libgmoe.so, and host-only calls answer without a GPU."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        import pytest
+        pytest.skip("no C compiler")
+    names = declared_functions()
+    table = ",\n    ".join("(fn)%s" % n for n in names)
+    src = tmp_path / "consumer.c"
+    src.write_text('''#include "gmoe.h"
+#include <stdio.h>
+#include <string.h>
+typedef void (*fn)(void);
+static fn every_entry_point[] = {
+    %s
+};
+int main(void) {
+  gm_moe_t* h = NULL;
+  const char* v = gm_version();
+  if (!v || !strstr(v, "sm_100a")) return 1;
+  if (gm_moe_workspace_bytes(0) != 0) return 2;
+  if (gm_moe_create(&h, 0, 0, 1, 0, 1) != GM_EINVAL || h != NULL) return 3;
+  if (!strstr(gm_last_error(NULL), "max_tokens")) return 4;
+  printf("%%s %%d\\n", v, (int)(sizeof every_entry_point / sizeof every_entry_point[0]));
+  return 0;
+}
+''' % table)
+    inc = os.path.join(ROOT, "include")
+    libdir = os.path.dirname(gmoe.LIB_PATH)
+    exe = tmp_path / "consumer"
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-I", inc, str(src), "-o", str(exe),
+                    "-L", libdir, "-lgmoe", "-Wl,-rpath," + libdir], check=True)
+    gxx = shutil.which("g++")
+    if gxx:
+        subprocess.run([gxx, "-std=c++17", "-Wall", "-Wextra", "-Werror", "-fsyntax-only", "-x", "c++",
+                        "-I", inc, str(src)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    assert "sm_100a" in " ".join(out) and int(out[-1]) == len(names)
