@@ -1,8 +1,8 @@
-"""Expert-parallel exchange protocol on CPU: two gloo processes run the same
+"""Expert-parallel exchange protocol on CPU: two (and four) gloo processes run the same
 steps as the library's EP forward (ep.cu: plan -> pack -> dispatch all-to-all
 -> this rank's experts over the received rows -> combine all-to-all -> sum in
 rank order), with the oracle's stages as the expert arithmetic, and must
-reproduce the oracle's degree-2 forward (the reference's sharded experts plus
+reproduce the oracle's degree-G forward (the reference's sharded experts plus
 all-reduce) bit for bit."""
 import os
 import socket
@@ -78,7 +78,7 @@ def worker(rank, world, port, tmp, placed):
     O.lib().orc_set_num_threads(4)
     with np.load(os.path.join(tmp, "layer.npz")) as z:
         ref = {k: z[k] for k in z.files}
-    x = tokens_np(WORLD * T_RANK, seed=77)[rank * T_RANK:(rank + 1) * T_RANK]
+    x = tokens_np(world * T_RANK, seed=77)[rank * T_RANK:(rank + 1) * T_RANK]
     epr, cap = E // world, T_RANK
     rank_of = np.load(os.path.join(tmp, "placement.npy")) if placed else np.arange(E) // epr
     local_of = placement_tables(rank_of, world)
@@ -134,16 +134,17 @@ def layer_ref():
     return stress_layer()[1]
 
 
-def test_ep_protocol_matches_degree2_oracle(tmp_path, layer_ref):
+@pytest.mark.parametrize("world", [WORLD, 4])
+def test_ep_protocol_matches_degree_g_oracle(tmp_path, layer_ref, world):
     ref = layer_ref
     np.savez(tmp_path / "layer.npz", **ref)
-    mp.spawn(worker, args=(WORLD, free_port(), str(tmp_path), False), nprocs=WORLD, join=True)
-    x = tokens_np(WORLD * T_RANK, seed=77)
-    rout, _, _, _ = O.bq_forward(x, ref, degree=WORLD)
-    got = np.concatenate([np.load(tmp_path / ("out%d.npy" % r)) for r in range(WORLD)])
+    mp.spawn(worker, args=(world, free_port(), str(tmp_path), False), nprocs=world, join=True)
+    x = tokens_np(world * T_RANK, seed=77)
+    rout, _, _, _ = O.bq_forward(x, ref, degree=world)
+    got = np.concatenate([np.load(tmp_path / ("out%d.npy" % r)) for r in range(world)])
     assert np.array_equal(got, rout)
-    # every token reaches at least one rank, and some reach both
-    counts = np.stack([np.load(tmp_path / ("count%d.npy" % r)) for r in range(WORLD)])
+    # every token reaches at least one rank, and none more than its rows
+    counts = np.stack([np.load(tmp_path / ("count%d.npy" % r)) for r in range(world)])
     assert counts.sum(axis=1).min() >= T_RANK and counts.max() <= T_RANK
 
 
