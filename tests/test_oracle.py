@@ -220,6 +220,87 @@ def test_bq_forward_chunked_equals_unchunked(bq_small):
     assert np.array_equal(w, np.concatenate([a[2], b[2]]))
 
 
+def _f64(a):
+    return O.bf16_to_f32(a).astype(np.float64)
+
+
+def _bf16_round(a):
+    return _f64(O.f32_to_bf16(np.asarray(a, np.float32)))
+
+
+def _gelu_tanh64(g):
+    return 0.5 * g * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (g + 0.044715 * g ** 3)))
+
+
+def _fwht64_blocks(v, block):
+    """Orthonormal FWHT in blocks along the last axis (float64)."""
+    v = v.reshape(-1, block).copy()
+    h = 1
+    while h < block:
+        a = v.reshape(v.shape[0], block // (2 * h), 2, h)
+        x, y = a[:, :, 0, :].copy(), a[:, :, 1, :].copy()
+        a[:, :, 0, :], a[:, :, 1, :] = x + y, x - y
+        h *= 2
+    return (v / np.sqrt(block)).reshape(-1)
+
+
+def test_bf16_forward_matches_float64(bq_small):
+    """The oracle's bf16 block against an independent float64 restatement of
+    its specification (RMSNorm with the gain rounded to
+    bf16, softmax top-8 renormalised times the per-expert scale, GeGLU bucket
+    rounded to bf16, down product, weighted sum): routing weights within the
+    reference's fast-exp error (1e-2), output within 1e-2 of max|ref| (half
+    the bf16 tolerance; 4e-3 measured).  The experts are the oracle's own
+    selection."""
+    raw, _ = bq_small
+    T = 6
+    x = tokens_np(T, seed=16)
+    out, idx, w, lg = O.bf16_forward(x, oracle_bf16_layer(raw))
+    p = np.exp(lg.astype(np.float64) - lg.max(axis=1, keepdims=True))
+    ref_w = np.take_along_axis(p, idx, axis=1)
+    ref_w = ref_w / ref_w.sum(axis=1, keepdims=True) * _f64(raw["per_expert_scale"])[idx]
+    assert (np.abs(w - ref_w) <= 1e-2 * np.abs(ref_w)).all()
+    xf = _f64(x)
+    inv = np.sqrt(H) / np.sqrt((xf * xf).sum(axis=1, keepdims=True) + H * 1e-6)
+    xn = _bf16_round(xf * inv * _f64(raw["pre_ffn_norm_2"]))
+    ref = np.zeros((T, H))
+    for t in range(T):
+        for k in range(TOPK):
+            e = idx[t, k]
+            gu = _f64(raw["gate_up"][e]) @ xn[t]
+            h = _bf16_round(_gelu_tanh64(gu[:I]) * gu[I:])
+            ref[t] += ref_w[t, k] * (_f64(raw["down"][e]) @ h)
+    got = _f64(out)
+    assert np.abs(got - ref).max() <= 1e-2 * np.abs(ref).max()
+
+
+def test_bq_forward_matches_float64_dequantized(bq_small):
+    """The oracle's butterquant expert arithmetic against float64 on the same
+    int8 operands: dequantised dots (x_i8 * sa/127) . (W_i8 * scale) in the
+    rotated domain, exact GeGLU, the bucket rounded to bf16 and rotated by
+    FWHT64 (unquantised here), the dequantised down product, the oracle's
+    routing weights: within 1.5e-2 of max|ref| (half the butterquant
+    tolerance; 6e-3 measured)."""
+    _, L = bq_small
+    T = 6
+    x = tokens_np(T, seed=17)
+    out, idx, w, _ = O.bq_forward(x, L)
+    xq, xsa = O.bq_norm_quant(x, L["gamma2"])
+    ref = np.zeros((T, H))
+    for t in range(T):
+        a = xq[t].astype(np.float64) * (float(xsa[t]) / 127.0)
+        for k in range(TOPK):
+            e = idx[t, k]
+            rows = slice(e * GU, (e + 1) * GU)
+            gu = (L["gu_q"][rows].astype(np.float64) * L["gu_scale"][rows, None].astype(np.float64)) @ a
+            h = _fwht64_blocks(_bf16_round(_gelu_tanh64(gu[:I]) * gu[I:]), 64)
+            drows = slice(e * H, (e + 1) * H)
+            wd = L["dn_q"][drows].astype(np.float64) * L["dn_scale"][drows, None].astype(np.float64)
+            ref[t] += float(w[t, k]) * (wd @ h)
+    got = _f64(out)
+    assert np.abs(got - ref).max() <= 1.5e-2 * np.abs(ref).max()
+
+
 def test_bq_close_to_bf16_path(bq_small):
     """Butterquant output approximates the unquantised model (the int8 error
     is the only difference; FWHT rotations cancel): self-check (i)."""
