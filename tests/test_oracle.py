@@ -5,8 +5,10 @@ oracle against mathematics and against independent numpy restatements:
 FWHT orthonormality, the quantizer's spec identities
 (quantization_docs/butterquant.md 1.1-1.4, 2.4-2.5), the VNNI layout
 formula, the router against softmax->argsort->renorm on the same logits, the
-router-merge invariant of benchmarks/benchmark_router_merge.mojo:120-135, and
-the stable schedule order of kernels/moe_router.mojo:72-101."""
+router-merge invariant of benchmarks/benchmark_router_merge.mojo:120-135,
+the stable schedule order of kernels/moe_router.mojo:72-101, float64
+restatements of the whole bf16 block and of the butterquant expert
+arithmetic, degree-G partial sums, token independence and chunking."""
 import numpy as np
 import pytest
 
