@@ -107,9 +107,12 @@ class ClockSampler:
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
+        import tempfile
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", "clocks_bench_%d.csv" % os.getpid())
+        # raw samples: GMOE_CLOCKS_DIR if set (to keep them), else a temp dir
+        folder = os.environ.get("GMOE_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(folder, "clocks_bench_%d.csv" % os.getpid())
 
     def __enter__(self):
         try:

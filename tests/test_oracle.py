@@ -248,7 +248,8 @@ def _fwht64_blocks(v, block):
 
 def test_bf16_forward_matches_float64(bq_small):
     """The oracle's bf16 block against an independent float64 restatement of
-    its specification (RMSNorm with the gain rounded to
+    its specification (kernels/rmsnorm.mojo:21-47, kernels/moe_router.mojo:
+    164-293, kernels/moe_experts.mojo:16-319: RMSNorm with the gain rounded to
     bf16, softmax top-8 renormalised times the per-expert scale, GeGLU bucket
     rounded to bf16, down product, weighted sum): routing weights within the
     reference's fast-exp error (1e-2), output within 1e-2 of max|ref| (half
