@@ -147,3 +147,17 @@ int main(void) {
                         "-I", inc, str(src)], check=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
     assert "sm_100a" in " ".join(out) and int(out[-1]) == len(names)
+
+
+def test_no_gpu_means_an_error_not_a_fallback():
+    """Without a GPU the product path fails with a CUDA status and text; there
+    is no CPU path behind it."""
+    import pytest
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(gmoe.GmoeError, match="GM_ECUDA"):
+        gmoe.MoeBlock(16, 1)
+    h = ctypes.c_void_p()
+    assert gmoe.lib().gm_moe_create(ctypes.byref(h), 0, 16, 1, 0, 1) == -2   # GM_ECUDA
+    assert not h.value
