@@ -266,12 +266,7 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    os.environ.setdefault("GMOE_ORACLE_VARIANT", "native")
-    from oracle import build as ob
-    try:
-        ob.build("native")
-    except Exception:
-        os.environ["GMOE_ORACLE_VARIANT"] = "portable"
+    O = oracle_native()
     import synth
     T, fmt, _ = WORKLOADS[args.workload]
     zipf = args.workload in ZIPF
@@ -286,7 +281,6 @@ def run_reference(args):
     Ts = min(T, REF_SAMPLE_TOKENS)
     xs = [synth.to_numpy(synth.zipf_tokens(T, seed=s) if zipf else synth.make_tokens(T, seed=s))[:Ts]
           for s in range(2)]
-    from oracle import oracle as O
     L, fwd = oracle_layer(fmt, raw)
     fwd(xs[0][:min(Ts, 4)], L)  # page the weights in
     for i in range(args.warmup):
@@ -331,6 +325,9 @@ def timed(fn, steps, warmup, stream):
 
 
 def oracle_native():
+    """The oracle built for this host's instruction set (-march=native; the
+    portable build if that fails), set to run on every host thread: the CPU
+    legs run on rank 0 alone, and torchrun sets OMP_NUM_THREADS=1 per rank."""
     os.environ.setdefault("GMOE_ORACLE_VARIANT", "native")
     from oracle import build as ob
     try:
@@ -338,6 +335,7 @@ def oracle_native():
     except Exception:
         os.environ["GMOE_ORACLE_VARIANT"] = "portable"
     from oracle import oracle as O
+    O.lib().orc_set_num_threads(len(os.sched_getaffinity(0)))
     return O
 
 
@@ -729,12 +727,7 @@ def main():
 
 def cpu_leg(fmt, T, args, raw_dev):
     import synth
-    os.environ.setdefault("GMOE_ORACLE_VARIANT", "native")
-    from oracle import build as ob
-    try:
-        ob.build("native")
-    except Exception:
-        os.environ["GMOE_ORACLE_VARIANT"] = "portable"
+    oracle_native()
     raw_cpu = {k: synth.to_numpy(v) for k, v in raw_dev.items()}
     import torch
     g = torch.Generator(device="cpu")
