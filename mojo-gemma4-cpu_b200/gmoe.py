@@ -145,6 +145,8 @@ def check(rc, handle=None):
 def call(name, *args):
     """Call a stateless entry point; addresses/streams are converted."""
     fn = getattr(lib(), name)
+    if len(args) != len(fn.argtypes):
+        raise TypeError("%s takes %d arguments, %d given" % (name, len(fn.argtypes), len(args)))
     conv = []
     for a, ty in zip(args, fn.argtypes):
         conv.append(_addr(a) if ty is _vp else a)

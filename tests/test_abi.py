@@ -161,3 +161,11 @@ def test_no_gpu_means_an_error_not_a_fallback():
     h = ctypes.c_void_p()
     assert gmoe.lib().gm_moe_create(ctypes.byref(h), 0, 16, 1, 0, 1) == -2   # GM_ECUDA
     assert not h.value
+
+
+def test_call_checks_the_argument_count():
+    import pytest
+    with pytest.raises(TypeError, match="takes 5 arguments, 4 given"):
+        gmoe.call("gm_rms_norm", 0, 0, 1, 0)
+    with pytest.raises(TypeError, match="takes 5 arguments, 6 given"):
+        gmoe.call("gm_rms_norm", 0, 0, 1, 0, None, None)
