@@ -169,3 +169,14 @@ def test_call_checks_the_argument_count():
         gmoe.call("gm_rms_norm", 0, 0, 1, 0)
     with pytest.raises(TypeError, match="takes 5 arguments, 6 given"):
         gmoe.call("gm_rms_norm", 0, 0, 1, 0, None, None)
+
+
+def test_missing_library_raises(monkeypatch):
+    """No libgmoe.so: the binding raises on first use (no fallback)."""
+    import pytest
+    monkeypatch.setattr(gmoe, "_LIB", None)
+    monkeypatch.setattr(gmoe, "LIB_PATH", os.path.join(ROOT, "no-such-dir", "libgmoe.so"))
+    with pytest.raises(gmoe.GmoeError, match="not built"):
+        gmoe.lib()
+    with pytest.raises(gmoe.GmoeError, match="not built"):
+        gmoe.call("gm_rms_norm", 0, 0, 1, 0, None)
