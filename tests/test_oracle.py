@@ -185,6 +185,36 @@ def test_schedule_stable_order(base, epr):
     assert np.array_equal(routes["weight"], np.array([x for _, x in rrec], np.float32))
 
 
+def _edge_routes(kind, T):
+    rng = np.random.default_rng(len(kind) + T)
+    if kind == "hot":        # every token picks experts 0..7
+        idx = np.tile(np.arange(TOPK, dtype=np.int32), (T, 1))
+    elif kind == "remote":   # nothing lands in the rank's block (experts 64..127)
+        idx = np.stack([rng.permutation(64)[:TOPK] for _ in range(T)]).astype(np.int32)
+    else:                    # reversed ids: the schedule order is by token, not by rank in the top 8
+        idx = np.stack([np.sort(rng.permutation(E)[:TOPK])[::-1] for _ in range(T)]).astype(np.int32)
+    return idx, rng.random((T, TOPK)).astype(np.float32)
+
+
+@pytest.mark.parametrize("kind,T,base,epr", [("hot", 0, 0, 128), ("hot", 1, 0, 128), ("hot", 1024, 0, 1),
+                                             ("remote", 50, 64, 64), ("reversed", 97, 0, 128),
+                                             ("reversed", 97, 120, 8)])
+def test_schedule_edge_cases(kind, T, base, epr):
+    """The stable schedule (kernels/moe_router.mojo:72-101) on the edge cases
+    its GPU restatement must handle: an empty batch, one token, one expert
+    taking every route, a rank receiving no route, reversed top-8 order."""
+    idx, w = _edge_routes(kind, T)
+    off, routes = O.build_schedules(idx, w, base, epr)
+    roff, rrec = np_schedule(idx, w, base, epr)
+    assert np.array_equal(off, roff)
+    assert [int(t) for t in routes["token"]] == [t for t, _ in rrec]
+    assert np.array_equal(routes["weight"], np.array([x for _, x in rrec], np.float32))
+    if kind == "remote":
+        assert off[-1] == 0
+    if kind == "hot" and epr == 1:
+        assert off.tolist() == [0, T]
+
+
 @pytest.fixture(scope="module")
 def bq_small():
     return stress_layer()
