@@ -156,6 +156,30 @@ def test_router_tie_breaks_to_lower_expert():
     assert np.allclose(w, 1 / 8, atol=1e-6)
 
 
+def test_zero_tokens_and_empty_batches():
+    """Edge rows of the front end: an all-zero token (RMSNorm with only the
+    epsilon, butterquant_kernels/linear.mojo:58-82: scale 0, int8 0; every logit
+    0, so the top 8 are experts 0..7 with weights pes/8), an all-zero bucket row
+    (block scales 0, int8 0), and empty batches."""
+    rng = np.random.default_rng(9)
+    zero = np.zeros((2, H), np.uint16)
+    wr = O.f32_to_bf16(rng.standard_normal((E, H)).astype(np.float32))
+    rs = O.bake_router_scale(O.f32_to_bf16(np.ones(H, np.float32)))
+    pes = O.f32_to_bf16((1.0 + 0.25 * rng.standard_normal(E)).astype(np.float32))
+    idx, w, lg = O.router(zero, wr, rs, pes)
+    assert (lg == 0).all() and (idx == np.arange(8)[None, :]).all()
+    assert np.allclose(w, O.bf16_to_f32(pes)[:8][None, :] / 8, rtol=1e-5)
+    g2 = O.bake_split_gain(O.f32_to_bf16(np.ones(H, np.float32)))
+    q, sa = O.bq_norm_quant(zero, g2)
+    assert not q.any() and not sa.any()
+    bq, bsa = O.bq_block_quant(np.zeros((3, I), np.uint16))
+    assert not bq.any() and not bsa.any()
+    idx0, w0, lg0 = O.router(np.zeros((0, H), np.uint16), wr, rs, pes)
+    assert idx0.shape == (0, TOPK) and lg0.shape == (0, E)
+    q0, sa0 = O.bq_norm_quant(np.zeros((0, H), np.uint16), g2)
+    assert q0.shape == (0, H) and sa0.shape == (0,)
+
+
 def np_schedule(idx, w, base, epr):
     off = np.zeros(epr + 1, np.int32)
     recs = [[] for _ in range(epr)]
