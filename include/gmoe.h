@@ -234,12 +234,22 @@ int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* ck, int ckp
  * 0 = NCCL send/recv.  Every rank must use the same value.
  * GM_OPT_DENSE_TC_MIN_TOKENS: calls with T >= value run the dense MLP's
  * products on tcgen05 GEMMs, smaller calls on its HBM-streaming kernels;
- * both give bit-identical results.  Default 128. */
+ * both give bit-identical results.  Default 128.
+ * GM_OPT_EP_TIMEOUT_MS (expert parallelism, peer-memory transport): bound in
+ * milliseconds of each exchange wait on the GPU, counted from the moment the
+ * wait kernel starts.  Default 1000; every rank must enter each forward within
+ * that time of its peers (raise it for a first forward that follows slow
+ * host-side work on one rank).  On expiry the forward completes with
+ * undefined output and gm_moe_device_status reports GM_ETIMEOUT.
+ * GM_OPT_EP_INIT_TIMEOUT_MS: bound of gm_moe_ep_init's communicator set-up on
+ * the host (default 120000); set it before gm_moe_ep_init. */
 #define GM_OPT_TC_MIN_TOKENS 1
 #define GM_OPT_PROFILE 2
 #define GM_OPT_PDL 3
 #define GM_OPT_EP_TRANSPORT 4
 #define GM_OPT_DENSE_TC_MIN_TOKENS 5
+#define GM_OPT_EP_TIMEOUT_MS 6
+#define GM_OPT_EP_INIT_TIMEOUT_MS 7
 int gm_moe_set_option(gm_moe_t* h, int option, long value);
 
 /* Per-stage statistics of the handle's forwards.  Replaces the reference's
@@ -278,10 +288,41 @@ int gm_moe_profile_read(gm_moe_t* h, gm_stage_stat_t* stats, int max_stats, int*
  * gm_moe_forward(h, layer, x, out, T, stream) takes this rank's T tokens
  * (T <= max_tokens; every rank calls it for every layer, T may differ) and
  * writes their complete MoE output: bf16(sum over ranks in rank order of each
- * rank's bf16 partial), the value the reference's all-reduce produces. */
+ * rank's bf16 partial), the value the reference's all-reduce produces.
+ * The communicator is set up non-blocking and polled against
+ * GM_OPT_EP_INIT_TIMEOUT_MS: if a rank never joins, the call aborts the
+ * communicator and returns GM_ETIMEOUT instead of blocking.
+ * The output of an expert-parallel forward is valid once the stream has
+ * reached it AND gm_moe_device_status returns GM_OK: when a peer misses the
+ * exchange (GM_OPT_EP_TIMEOUT_MS), the forward still completes, with
+ * undefined output, and the status reports GM_ETIMEOUT. */
 #define GM_EP_UNIQUE_ID_BYTES 128
 int gm_ep_unique_id(void* out, size_t bytes);
 int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world);
+
+/* Expert parallelism inside one process (the reference's ranks as handles of
+ * one process, e.g. several handles sharing one GPU, or one handle per GPU
+ * driven by one host thread).  gm_moe_ep_init_group joins `world` handles,
+ * handles[g] created with rank g and degree world, all with the same
+ * max_tokens; the exchange uses the members' buffers as plain pointers of
+ * this process (peer access is enabled between their devices), no NCCL.
+ * gm_moe_ep_forward_group runs one layer on every member: member g's T[g]
+ * tokens x[g] -> out[g], on streams[g]; it issues the three phases of the
+ * exchange (route and pack; experts and combine; final sum) for every member
+ * before the next phase, so that members sharing a GPU never wait on a kernel
+ * that has not been issued before them.  Members on one device must be given
+ * the same stream (GM_EINVAL otherwise).  The result equals the multi-process
+ * forward's bit for bit.  A lone gm_moe_forward on a member of a group that
+ * shares a device has no peer running beside it: its exchange waits expire
+ * (GM_OPT_EP_TIMEOUT_MS) and gm_moe_device_status reports GM_ETIMEOUT.
+ * Destroy the members after their last forward; destroying one dissolves
+ * the group (the others then return GM_ESTATE).
+ * gm_moe_ep_set_placement_group: gm_moe_ep_set_placement for such a group
+ * (one call for all members; expert weights move by device copies). */
+int gm_moe_ep_init_group(gm_moe_t* const* handles, int world);
+int gm_moe_ep_forward_group(gm_moe_t* const* handles, int world, int layer, const void* const* x,
+                            void* const* out, const int* T, void* const* streams);
+int gm_moe_ep_set_placement_group(gm_moe_t* const* handles, int world, const int32_t* expert_rank);
 
 /* Optional load-based placement (no reference counterpart; the reference keeps
  * contiguous blocks).  expert_rank[128] (host) names the rank that holds each
@@ -332,8 +373,10 @@ int gm_router_select(const void* x, const void* router_w, const void* router_sca
  * exits, and shared by all calls on that GPU: calls that overlap on the GPU
  * race, so order them on one stream.  The first call on each device looks up
  * the array's device address (cudaGetSymbolAddress) with that device current;
- * make that first call before any stream capture.  The call allocates
- * nothing. */
+ * make that first call before any stream capture.  That address is cached for
+ * the life of the process: after cudaDeviceReset on a device, do not call this
+ * entry point there again.  The call allocates nothing, but it does call the
+ * CUDA runtime, so it cannot run inside a stream's host function. */
 int gm_router_select_noalloc(const void* x, const void* router_w, const void* router_scale,
                              const void* per_expert_scale, int T, int32_t* route_idx,
                              float* route_w, void* stream);

@@ -60,8 +60,9 @@ const NcclApi* nccl_api(const char** err) {
       return;
     }
     bool ok = sym(lib, "ncclGetUniqueId", g_nccl.get_unique_id) &&
-              sym(lib, "ncclCommInitRank", g_nccl.comm_init_rank) &&
+              sym(lib, "ncclCommInitRankConfig", g_nccl.comm_init_rank_config) &&
               sym(lib, "ncclCommDestroy", g_nccl.comm_destroy) &&
+              sym(lib, "ncclCommAbort", g_nccl.comm_abort) &&
               sym(lib, "ncclCommGetAsyncError", g_nccl.comm_get_async_error) &&
               sym(lib, "ncclGroupStart", g_nccl.group_start) &&
               sym(lib, "ncclGroupEnd", g_nccl.group_end) && sym(lib, "ncclSend", g_nccl.send) &&
@@ -323,15 +324,15 @@ ep_pack_p2p_kernel(const uint8_t* __restrict__ x_rows, int row_bytes, const floa
 }
 
 __global__ void ep_wait_kernel(const uint32_t* __restrict__ flags, int G, uint32_t epoch,
-                               int* __restrict__ err) {
+                               uint64_t limit_ns, int* __restrict__ err) {
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x >= G) return;
   const uint64_t t0 = ep_global_ns();
   uint32_t it = 0;
   while ((int32_t)(ld_acquire_sys(flags + threadIdx.x) - epoch) < 0) {
-    if ((++it & 255) == 0 && ep_global_ns() - t0 > 1000000000ull) {
-      atomicExch(err, 3);  // a peer did not publish within ~1 s
+    if ((++it & 255) == 0 && ep_global_ns() - t0 > limit_ns) {
+      atomicExch(err, 3);  // a peer did not publish within the limit
       return;
     }
   }
@@ -397,8 +398,9 @@ cudaError_t launch_ep_pack_p2p(const void* x_rows, int row_bytes, const float* x
                   epr, pl.rank_of, pl.local_of, pos, count, peers, my_rank, epoch, done_counter);
 }
 
-cudaError_t launch_ep_wait(const uint32_t* flags, int G, uint32_t epoch, int* err, cudaStream_t s) {
-  return launch_k(ep_wait_kernel, dim3(1), dim3(32), 0, s, flags, G, epoch, err);
+cudaError_t launch_ep_wait(const uint32_t* flags, int G, uint32_t epoch, uint64_t limit_ns, int* err,
+                           cudaStream_t s) {
+  return launch_k(ep_wait_kernel, dim3(1), dim3(32), 0, s, flags, G, epoch, limit_ns, err);
 }
 
 cudaError_t launch_combine_p2p(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,

@@ -11,8 +11,9 @@ namespace gm {
 struct NcclApi {
   bool loaded = false;
   ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
-  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
   ncclResult_t (*group_start)() = nullptr;
   ncclResult_t (*group_end)() = nullptr;
@@ -73,9 +74,10 @@ cudaError_t launch_ep_pack_p2p(const void* x_rows, int row_bytes, const float* x
                                int epr, EpPlacement pl, const int32_t* pos, const int32_t* count,
                                const EpPeers& peers, int my_rank, uint32_t epoch, int* done_counter,
                                cudaStream_t s);
-// Waits (bounded, ~1 s) until flags[0..G) all reach epoch; on expiry writes 3
-// to *err and returns.
-cudaError_t launch_ep_wait(const uint32_t* flags, int G, uint32_t epoch, int* err, cudaStream_t s);
+// Waits (bounded: limit_ns of the GPU's global timer) until flags[0..G) all
+// reach epoch; on expiry writes 3 to *err and returns.
+cudaError_t launch_ep_wait(const uint32_t* flags, int G, uint32_t epoch, uint64_t limit_ns, int* err,
+                           cudaStream_t s);
 // Combine with peer stores: received row r = (src, p) is summed over this
 // rank's experts (ascending id, from 0.0, bf16) and written into rank src's
 // contrib block of this rank; then cflag[src][my_rank] = epoch on every rank.

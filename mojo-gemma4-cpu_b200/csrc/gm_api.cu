@@ -1,9 +1,11 @@
 // gm_api.cu -- the C ABI of include/gmoe.h: handle, weight registration, the
 // MoE operator and the per-stage entry points.
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/gmoe.h"
@@ -158,6 +160,14 @@ struct gm_moe {
   int* ep_counters = nullptr;      // [2] last-CTA counters of the pack and the combine
   void* ep_peer_base[8] = {};      // IPC mappings (own base at this rank's index)
   uint32_t ep_epoch = 0;
+  uint32_t ep_cur = 0;             // epoch of the forward whose phases are being issued
+  bool ep_on = false;              // expert-parallel forward (either kind of group)
+  // in-process group (gm_moe_ep_init_group): every member by rank; the peers'
+  // exchange buffers are plain pointers of this process, no NCCL communicator
+  bool ep_group = false;
+  gm_moe* ep_members[8] = {};
+  int ep_timeout_ms = 1000;        // GM_OPT_EP_TIMEOUT_MS: bound of each exchange wait
+  int ep_init_timeout_ms = 120000; // GM_OPT_EP_INIT_TIMEOUT_MS: bound of gm_moe_ep_init
 };
 
 namespace {
@@ -370,6 +380,94 @@ int carve_workspace(gm_moe* h, int tokens) {
   return GM_OK;
 }
 
+// Exchange allocation of an expert-parallel handle: one cudaMalloc, the same
+// offsets on every rank (same max_tokens and world), so a peer's buffer is
+// its base plus these offsets.
+struct EpLayout {
+  size_t pos, cnt, sx, ssa, sidx, sw, rx, rsa, ridx, rw, part, con, rank, local;
+  size_t rx1, rsa1, ridx1, rw1, con1;  // second parity of the regions peers write
+  size_t dflag, cflag, ctr, total;
+};
+
+EpLayout ep_layout(int max_tokens, int world) {
+  const size_t cap = (size_t)max_tokens, n = (size_t)world * cap;
+  Carve c;
+  EpLayout o;
+  o.pos = c.take<int32_t>(cap * world);
+  o.cnt = c.take<int32_t>(8);
+  o.sx = c.take<uint8_t>(n * 2 * H);
+  o.ssa = c.take<float>(n);
+  o.sidx = c.take<int32_t>(n * TOPK);
+  o.sw = c.take<float>(n * TOPK);
+  o.rx = c.take<uint8_t>(n * 2 * H);
+  o.rsa = c.take<float>(n);
+  o.ridx = c.take<int32_t>(n * TOPK);
+  o.rw = c.take<float>(n * TOPK);
+  o.part = c.take<uint16_t>(n * H);
+  o.con = c.take<uint16_t>(n * H);
+  o.rank = c.take<int32_t>(E);
+  o.local = c.take<int32_t>(E);
+  o.rx1 = c.take<uint8_t>(n * 2 * H);
+  o.rsa1 = c.take<float>(n);
+  o.ridx1 = c.take<int32_t>(n * TOPK);
+  o.rw1 = c.take<float>(n * TOPK);
+  o.con1 = c.take<uint16_t>(n * H);
+  o.dflag = c.take<uint32_t>(8);
+  o.cflag = c.take<uint32_t>(8);
+  o.ctr = c.take<int>(2);
+  o.total = align_up(c.off, 256);
+  return o;
+}
+
+// Workspace for world*max_tokens received rows plus the exchange allocation
+// (zeroed: flags at epoch 0, counters re-armed), carved into the handle.
+int ep_alloc(gm_moe* h, int world, EpLayout* out) {
+  int rc = carve_workspace(h, world * h->max_tokens);
+  if (rc) return rc;
+  const EpLayout o = ep_layout(h->max_tokens, world);
+  GM_TRY(h, cudaMalloc(&h->ep_buf, o.total), "ep buffers");
+  GM_TRY(h, cudaMemset(h->ep_buf, 0, o.total), "ep buffers");
+  char* b = static_cast<char*>(h->ep_buf);
+  h->ep_pos = reinterpret_cast<int32_t*>(b + o.pos);
+  h->ep_count = reinterpret_cast<int32_t*>(b + o.cnt);
+  h->ep_send_x = reinterpret_cast<uint8_t*>(b + o.sx);
+  h->ep_send_sa = reinterpret_cast<float*>(b + o.ssa);
+  h->ep_send_idx = reinterpret_cast<int32_t*>(b + o.sidx);
+  h->ep_send_w = reinterpret_cast<float*>(b + o.sw);
+  h->ep_recv_x = reinterpret_cast<uint8_t*>(b + o.rx);
+  h->ep_recv_sa = reinterpret_cast<float*>(b + o.rsa);
+  h->ep_recv_idx = reinterpret_cast<int32_t*>(b + o.ridx);
+  h->ep_recv_w = reinterpret_cast<float*>(b + o.rw);
+  h->ep_partial = reinterpret_cast<uint16_t*>(b + o.part);
+  h->ep_contrib = reinterpret_cast<uint16_t*>(b + o.con);
+  h->ep_rank_of = reinterpret_cast<int32_t*>(b + o.rank);
+  h->ep_local_of = reinterpret_cast<int32_t*>(b + o.local);
+  h->ep_dflag = reinterpret_cast<uint32_t*>(b + o.dflag);
+  h->ep_cflag = reinterpret_cast<uint32_t*>(b + o.cflag);
+  h->ep_counters = reinterpret_cast<int*>(b + o.ctr);
+  *out = o;
+  return GM_OK;
+}
+
+// Peer tables of both parities from every rank's exchange base (IPC mappings
+// across processes, plain pointers inside one process).
+void ep_wire(gm_moe* h, int world, void* const* bases, const EpLayout& o) {
+  const size_t rx[2] = {o.rx, o.rx1}, rsa[2] = {o.rsa, o.rsa1}, ridx[2] = {o.ridx, o.ridx1},
+               rw[2] = {o.rw, o.rw1}, con[2] = {o.con, o.con1};
+  for (int par = 0; par < 2; ++par)
+    for (int q = 0; q < world; ++q) {
+      char* pb = static_cast<char*>(bases[q]);
+      EpPeers& P = h->ep_peers[par];
+      P.recv_x[q] = reinterpret_cast<uint8_t*>(pb + rx[par]);
+      P.recv_sa[q] = reinterpret_cast<float*>(pb + rsa[par]);
+      P.recv_idx[q] = reinterpret_cast<int32_t*>(pb + ridx[par]);
+      P.recv_w[q] = reinterpret_cast<float*>(pb + rw[par]);
+      P.contrib[q] = reinterpret_cast<uint16_t*>(pb + con[par]);
+      P.dflag[q] = reinterpret_cast<uint32_t*>(pb + o.dflag);
+      P.cflag[q] = reinterpret_cast<uint32_t*>(pb + o.cflag);
+    }
+}
+
 // ---------------------------------------------------------------- profiler
 cudaEvent_t take_event(gm_moe* h) {
   if (!h->event_pool.empty()) {
@@ -511,8 +609,25 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
   return GM_OK;
 }
 
+// With a non-blocking communicator every NCCL call may return
+// ncclInProgress; the call is complete once the communicator's state leaves
+// that value (polled for at most `limit_ms`).
+ncclResult_t nccl_settle(ncclComm_t comm, ncclResult_t r, int limit_ms) {
+  if (r != ncclInProgress || !comm) return r;
+  const NcclApi* nc = nccl_api(nullptr);
+  const auto t0 = std::chrono::steady_clock::now();
+  ncclResult_t st = ncclInProgress;
+  while (nc->comm_get_async_error(comm, &st) == ncclSuccess && st == ncclInProgress) {
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(limit_ms)) return ncclInProgress;
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  return st;
+}
+
 int nccl_check(gm_moe* h, ncclResult_t r, const char* what) {
+  r = nccl_settle(h ? h->ep_comm : nullptr, r, 60000);
   if (r == ncclSuccess) return GM_OK;
+  if (r == ncclInProgress) return set_err(h, GM_ETIMEOUT, "%s: NCCL call did not complete in 60 s", what);
   const NcclApi* nc = nccl_api(nullptr);
   return set_err(h, GM_ENCCL, "%s: %s", what, nc ? nc->get_error_string(r) : "NCCL error");
 }
@@ -523,24 +638,67 @@ int nccl_check(gm_moe* h, ncclResult_t r, const char* what) {
     if (_rc != GM_OK) return _rc;                      \
   } while (0)
 
-// Expert-parallel forward, peer-memory transport (after routing and the plan):
-// the pack kernel stores rows into the receivers' buffers, the combine kernel
-// stores partial rows into the sources' buffers, and flags stamped with the
-// forward counter order the two sides (ep.cu).
-int ep_forward_p2p(gm_moe* h, const Layer& L, uint16_t* out, int T, cudaStream_t s,
-                   const PostParams* post, const EpPlacement& pl) {
-  const int G = h->degree, cap = h->max_tokens, n = G * cap;
+// A member of an in-process group whose peer was destroyed has no exchange.
+int ep_group_intact(gm_moe* h) {
+  if (!h->ep_group) return GM_OK;
+  for (int q = 0; q < h->degree; ++q)
+    if (!h->ep_members[q])
+      return set_err(h, GM_ESTATE, "member %d of this handle's expert-parallel group was destroyed", q);
+  return GM_OK;
+}
+
+uint64_t ep_limit_ns(const gm_moe* h) { return (uint64_t)h->ep_timeout_ms * 1000000ull; }
+
+EpPlacement ep_placement(const gm_moe* h) {
+  EpPlacement pl;
+  if (h->ep_placed) {
+    pl.rank_of = h->ep_rank_of;
+    pl.local_of = h->ep_local_of;
+  }
+  return pl;
+}
+
+// Expert-parallel forward in three phases, so that an in-process group can
+// issue each phase for every member before the next one (the waits of phase
+// B and C then find their flags already published, see
+// gm_moe_ep_forward_group).  A one-handle-per-process forward runs A, B, C.
+//
+// Phase A: local activation prep, router logits and top-8 of this rank's T
+// tokens, the destination plan and, with the peer-memory transport, the pack
+// that stores each row into its receivers' buffers.
+int ep_phase_a(gm_moe* h, const Layer& L, const uint16_t* xb, int T, cudaStream_t s) {
+  const int G = h->degree, cap = h->max_tokens;
   const bool bq = L.kind == 1;
-  const int row_bytes = bq ? H : 2 * H;
-  const uint32_t epoch = ++h->ep_epoch;
-  const EpPeers& P = h->ep_peers[epoch & 1];
+  if (T > 0) {
+    if (bq)
+      GM_STAGE(h, s, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, h->inv_rms, s), "bq_norm_quant");
+    else
+      GM_STAGE(h, s, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
+    GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, h->router_counts, s),
+             "router_expert");
+    GM_STAGE(h, s, launch_topk(h->logits, L.pes, T, h->route_idx, h->route_w, s), "router_merge");
+  }
+  const EpPlacement pl = ep_placement(h);
+  GM_STAGE(h, s, launch_ep_plan(h->route_idx, T, G, h->epr, pl, h->ep_pos, h->ep_count, s), "ep_plan");
+  if (!h->ep_use_p2p) return GM_OK;
+  h->ep_cur = ++h->ep_epoch;
+  const EpPeers& P = h->ep_peers[h->ep_cur & 1];
   GM_STAGE(h, s, launch_ep_pack_p2p(bq ? static_cast<const void*>(h->x_i8) : static_cast<const void*>(h->x_normed),
-                                    row_bytes, bq ? h->x_sa : nullptr, h->route_idx, h->route_w, T, G, cap,
-                                    h->epr, pl, h->ep_pos, h->ep_count, P, h->rank, epoch,
+                                    bq ? H : 2 * H, bq ? h->x_sa : nullptr, h->route_idx, h->route_w, T, G, cap,
+                                    h->epr, pl, h->ep_pos, h->ep_count, P, h->rank, h->ep_cur,
                                     h->ep_counters, s),
            "ep_pack.p2p");
-  GM_STAGE(h, s, launch_ep_wait(h->ep_dflag, G, epoch, h->dev_err, s), "ep_dispatch.wait");
-  // this rank's experts over the rows every source stored here
+  return GM_OK;
+}
+
+// Phase B (peer memory): wait until every source stored its rows here, run
+// this rank's experts over them, and store each row's partial into its
+// source's contribution block.
+int ep_phase_b(gm_moe* h, const Layer& L, cudaStream_t s) {
+  const int G = h->degree, cap = h->max_tokens, n = G * cap;
+  const bool bq = L.kind == 1;
+  const EpPeers& P = h->ep_peers[h->ep_cur & 1];
+  GM_STAGE(h, s, launch_ep_wait(h->ep_dflag, G, h->ep_cur, ep_limit_ns(h), h->dev_err, s), "ep_dispatch.wait");
   const uint8_t* rx = P.recv_x[h->rank];
   const int32_t* ridx = P.recv_idx[h->rank];
   const int rc_chunk = bq ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
@@ -558,10 +716,18 @@ int ep_forward_p2p(gm_moe* h, const Layer& L, uint16_t* out, int T, cudaStream_t
                                reinterpret_cast<const uint16_t*>(rx), ridx, nullptr, s, nullptr,
                                /*skip_combine=*/true);
   if (rc) return rc;
-  GM_STAGE(h, s, launch_combine_p2p(ridx, h->route_pos, h->ybuf, n, cap, P, G, h->rank, epoch,
+  GM_STAGE(h, s, launch_combine_p2p(ridx, h->route_pos, h->ybuf, n, cap, P, G, h->rank, h->ep_cur,
                                     h->ep_counters + 1, s),
            "combine.p2p");
-  GM_STAGE(h, s, launch_ep_wait(h->ep_cflag, G, epoch, h->dev_err, s), "ep_combine.wait");
+  return GM_OK;
+}
+
+// Phase C (peer memory): wait for every destination's partial rows, then sum
+// them in rank order (and run the post-MoE tail when asked).
+int ep_phase_c(gm_moe* h, uint16_t* out, int T, cudaStream_t s, const PostParams* post) {
+  const int G = h->degree, cap = h->max_tokens;
+  const EpPeers& P = h->ep_peers[h->ep_cur & 1];
+  GM_STAGE(h, s, launch_ep_wait(h->ep_cflag, G, h->ep_cur, ep_limit_ns(h), h->dev_err, s), "ep_combine.wait");
   const uint16_t* contrib = P.contrib[h->rank];
   if (post && join_dense(h, s)) return GM_ECUDA;
   if (post)
@@ -571,38 +737,22 @@ int ep_forward_p2p(gm_moe* h, const Layer& L, uint16_t* out, int T, cudaStream_t
   return GM_OK;
 }
 
-// Expert-parallel forward (after gm_moe_ep_init): this rank's T tokens in,
-// their full MoE output out; see ep.cu for the exchange.
-int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int T, cudaStream_t s,
-               const PostParams* post) {
+// Expert-parallel forward, NCCL transport (after phase A): send/recv of the
+// packed blocks, the experts, send/recv of the partial rows, the rank-order sum.
+int ep_forward_nccl(gm_moe* h, const Layer& L, uint16_t* out, int T, cudaStream_t s,
+                    const PostParams* post) {
   const NcclApi* nc = nccl_api(nullptr);
+  if (!h->ep_comm || !nc) return set_err(h, GM_ESTATE, "the NCCL transport needs gm_moe_ep_init");
   const int G = h->degree, cap = h->max_tokens, n = G * cap;
   const bool bq = L.kind == 1;
   const int row_bytes = bq ? H : 2 * H;
-  // 1. local activation prep, router logits and top-8 of this rank's tokens
-  if (T > 0) {
-    if (bq)
-      GM_STAGE(h, s, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, h->inv_rms, s), "bq_norm_quant");
-    else
-      GM_STAGE(h, s, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
-    GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, h->router_counts, s),
-             "router_expert");
-    GM_STAGE(h, s, launch_topk(h->logits, L.pes, T, h->route_idx, h->route_w, s), "router_merge");
-  }
-  // 2. destinations and send blocks
-  EpPlacement pl;
-  if (h->ep_placed) {
-    pl.rank_of = h->ep_rank_of;
-    pl.local_of = h->ep_local_of;
-  }
-  GM_STAGE(h, s, launch_ep_plan(h->route_idx, T, G, h->epr, pl, h->ep_pos, h->ep_count, s), "ep_plan");
-  if (h->ep_use_p2p) return ep_forward_p2p(h, L, out, T, s, post, pl);
+  const EpPlacement pl = ep_placement(h);
   GM_STAGE(h, s, launch_ep_pack(bq ? static_cast<const void*>(h->x_i8) : static_cast<const void*>(h->x_normed),
                                 row_bytes, bq ? h->x_sa : nullptr, h->route_idx, h->route_w, T, G, cap,
                                 h->epr, pl, h->ep_pos, h->ep_count, h->ep_send_x, h->ep_send_sa,
                                 h->ep_send_idx, h->ep_send_w, s),
            "ep_pack");
-  // 3. dispatch: block p of every array goes to rank p
+  // dispatch: block p of every array goes to rank p
   {
     StageScope scope(h, "ep_dispatch", s);
     GM_NCCL(h, nc->group_start(), "ep dispatch");
@@ -621,7 +771,7 @@ int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int
     }
     GM_NCCL(h, nc->group_end(), "ep dispatch");
   }
-  // 4. this rank's experts over the n received rows (unused rows route nowhere)
+  // this rank's experts over the n received rows (unused rows route nowhere)
   const int rc_chunk = bq ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
   if (n <= 1024)
     GM_STAGE(h, s, launch_build_schedule(h->ep_recv_idx, h->ep_recv_w, n, h->expert_base, h->epr, rc_chunk,
@@ -636,7 +786,7 @@ int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int
                                reinterpret_cast<const uint16_t*>(h->ep_recv_x), h->ep_recv_idx,
                                h->ep_partial, s);
   if (rc) return rc;
-  // 5. combine exchange: partial rows go back to the rank they came from
+  // combine exchange: partial rows go back to the rank they came from
   {
     StageScope scope(h, "ep_combine", s);
     GM_NCCL(h, nc->group_start(), "ep combine");
@@ -647,13 +797,24 @@ int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int
     }
     GM_NCCL(h, nc->group_end(), "ep combine");
   }
-  // 6. sum of the ranks' partials in rank order (then the post-MoE tail)
+  // sum of the ranks' partials in rank order (then the post-MoE tail)
   if (post && join_dense(h, s)) return GM_ECUDA;
   if (post)
     GM_STAGE(h, s, launch_ep_final_post(h->ep_contrib, h->ep_pos, T, G, cap, *post, s), "ep_final.post");
   else
     GM_STAGE(h, s, launch_ep_final(h->ep_contrib, h->ep_pos, T, G, cap, out, s), "ep_final");
   return GM_OK;
+}
+
+// Expert-parallel forward of one handle (after gm_moe_ep_init or
+// gm_moe_ep_init_group): this rank's T tokens in, their full MoE output out.
+int ep_forward(gm_moe* h, const Layer& L, const uint16_t* xb, uint16_t* out, int T, cudaStream_t s,
+               const PostParams* post) {
+  int rc = ep_phase_a(h, L, xb, T, s);
+  if (rc) return rc;
+  if (!h->ep_use_p2p) return ep_forward_nccl(h, L, out, T, s, post);
+  if ((rc = ep_phase_b(h, L, s))) return rc;
+  return ep_phase_c(h, out, T, s, post);
 }
 
 }  // namespace
@@ -746,6 +907,19 @@ int gm_moe_destroy(gm_moe_t* h) {
     for (int q = 0; q < 8; ++q)
       if (h->ep_peer_base[q] && q != h->rank) cudaIpcCloseMemHandle(h->ep_peer_base[q]);
     if (const NcclApi* nc = nccl_api(nullptr)) nc->comm_destroy(h->ep_comm);
+  }
+  if (h->ep_group) {
+    // no member may still be storing into this handle's exchange buffers, and
+    // none may use them afterwards: the group is dissolved
+    for (int q = 0; q < h->degree; ++q)
+      if (gm_moe* m = h->ep_members[q]) {
+        cudaSetDevice(m->device);
+        cudaDeviceSynchronize();
+      }
+    for (int q = 0; q < h->degree; ++q)
+      if (gm_moe* m = h->ep_members[q])
+        if (m != h) m->ep_members[h->rank] = nullptr;
+    cudaSetDevice(h->device);
   }
   if (h->ep_buf) cudaFree(h->ep_buf);
   if (h->ws) cudaFree(h->ws);
@@ -840,8 +1014,10 @@ int forward_impl(gm_moe* h, int layer, const void* x, void* out, int T, void* st
   cudaStream_t s = S(stream);
   if (h->pending.size() > 4096 && (rc = drain_profile(h))) return rc;  // bound the event backlog
   PdlScope pdl_scope(h->pdl);
-  if (h->ep_comm)
+  if (h->ep_on) {
+    if ((rc = ep_group_intact(h))) return rc;
     return ep_forward(h, L, static_cast<const uint16_t*>(x), static_cast<uint16_t*>(out), T, s, post);
+  }
   if (T == 0) return GM_OK;
   const uint16_t* xb = static_cast<const uint16_t*>(x);
   // 0. decode batches route to nearly every expert: pull the gate/up weights
@@ -901,7 +1077,7 @@ int gm_moe_forward_ffn(gm_moe_t* h, int layer, void* x_main, const void* dense_o
   const Layer& L = h->layers[layer];
   if (!L.post_w1) return set_err(h, GM_ESTATE, "layer %d: gm_moe_register_post not called", layer);
   if (!x_main || !dense_out) return set_err(h, GM_EINVAL, "NULL x_main/dense_out");
-  if (h->degree > 1 && !h->ep_comm)
+  if (h->degree > 1 && !h->ep_on)
     return set_err(h, GM_ESTATE, "the post-MoE tail needs the complete MoE output: degree %d "
                    "without gm_moe_ep_init yields partials", h->degree);
   PostParams p{static_cast<const uint16_t*>(dense_out), static_cast<uint16_t*>(x_main), L.post_w1,
@@ -997,7 +1173,7 @@ int gm_ffn_forward(gm_moe_t* h, int layer, void* x_main, int T, void* stream) {
   const Layer& L = h->layers[layer];
   if (L.kind == 0) return set_err(h, GM_ESTATE, "layer %d has no registered experts", layer);
   if (!L.post_w1) return set_err(h, GM_ESTATE, "layer %d: gm_moe_register_post not called", layer);
-  if (h->degree > 1 && !h->ep_comm)
+  if (h->degree > 1 && !h->ep_on)
     return set_err(h, GM_ESTATE, "the post-MoE tail needs the complete MoE output: degree %d "
                    "without gm_moe_ep_init yields partials", h->degree);
   cudaStream_t s = S(stream);
@@ -1034,7 +1210,20 @@ int gm_moe_set_option(gm_moe_t* h, int option, long value) {
       if (value != 0 && value != 1) return set_err(h, GM_EINVAL, "GM_OPT_EP_TRANSPORT must be 0 or 1");
       if (value == 1 && !h->ep_p2p_ok)
         return set_err(h, GM_ESTATE, "peer-memory transport unavailable (not initialised or not mapped)");
+      if (value == 0 && !h->ep_comm)
+        return set_err(h, GM_ESTATE, "the NCCL transport needs gm_moe_ep_init (an in-process group has "
+                       "no communicator)");
       h->ep_use_p2p = value == 1;
+      return GM_OK;
+    case GM_OPT_EP_TIMEOUT_MS:
+      if (value < 1 || value > 600000)
+        return set_err(h, GM_EINVAL, "GM_OPT_EP_TIMEOUT_MS must be in [1, 600000]");
+      h->ep_timeout_ms = (int)value;
+      return GM_OK;
+    case GM_OPT_EP_INIT_TIMEOUT_MS:
+      if (value < 1 || value > 3600000)
+        return set_err(h, GM_EINVAL, "GM_OPT_EP_INIT_TIMEOUT_MS must be in [1, 3600000]");
+      h->ep_init_timeout_ms = (int)value;
       return GM_OK;
     case GM_OPT_PDL:
       if (value != 0 && value != 1) return set_err(h, GM_EINVAL, "GM_OPT_PDL must be 0 or 1");
@@ -1085,7 +1274,7 @@ int gm_ep_unique_id(void* out, size_t bytes) {
 
 int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
   if (!h || !unique_id) return set_err(h, GM_EINVAL, "gm_moe_ep_init: NULL argument");
-  if (h->ep_comm) return set_err(h, GM_ESTATE, "gm_moe_ep_init: already initialised");
+  if (h->ep_on) return set_err(h, GM_ESTATE, "gm_moe_ep_init: already initialised");
   if (world != h->degree || world < 1 || world > 8)
     return set_err(h, GM_EINVAL, "gm_moe_ep_init: world=%d must equal the handle's degree (%d), 1..8",
                    world, h->degree);
@@ -1093,49 +1282,28 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
   const NcclApi* nc = nccl_api(&why);
   if (!nc) return set_err(h, GM_ENCCL, "%s", why ? why : "NCCL unavailable");
   GM_TRY(h, cudaSetDevice(h->device), "ep_init");
-  // the expert stage sees world * max_tokens received rows
-  int rc = carve_workspace(h, world * h->max_tokens);
+  EpLayout o;
+  int rc = ep_alloc(h, world, &o);
   if (rc) return rc;
-  const size_t cap = (size_t)h->max_tokens, n = (size_t)world * cap;
-  Carve c;
-  const size_t o_pos = c.take<int32_t>(cap * world), o_cnt = c.take<int32_t>(8);
-  const size_t o_sx = c.take<uint8_t>(n * 2 * H), o_ssa = c.take<float>(n),
-               o_sidx = c.take<int32_t>(n * TOPK), o_sw = c.take<float>(n * TOPK);
-  const size_t o_rx = c.take<uint8_t>(n * 2 * H), o_rsa = c.take<float>(n),
-               o_ridx = c.take<int32_t>(n * TOPK), o_rw = c.take<float>(n * TOPK);
-  const size_t o_part = c.take<uint16_t>(n * H), o_con = c.take<uint16_t>(n * H);
-  const size_t o_rank = c.take<int32_t>(E), o_local = c.take<int32_t>(E);
-  // second parity of the regions peers write (peer-memory transport)
-  const size_t o_rx1 = c.take<uint8_t>(n * 2 * H), o_rsa1 = c.take<float>(n),
-               o_ridx1 = c.take<int32_t>(n * TOPK), o_rw1 = c.take<float>(n * TOPK),
-               o_con1 = c.take<uint16_t>(n * H);
-  const size_t o_dflag = c.take<uint32_t>(8), o_cflag = c.take<uint32_t>(8), o_ctr = c.take<int>(2);
-  GM_TRY(h, cudaMalloc(&h->ep_buf, align_up(c.off, 256)), "ep buffers");
-  char* b = static_cast<char*>(h->ep_buf);
-  h->ep_pos = reinterpret_cast<int32_t*>(b + o_pos);
-  h->ep_count = reinterpret_cast<int32_t*>(b + o_cnt);
-  h->ep_send_x = reinterpret_cast<uint8_t*>(b + o_sx);
-  h->ep_send_sa = reinterpret_cast<float*>(b + o_ssa);
-  h->ep_send_idx = reinterpret_cast<int32_t*>(b + o_sidx);
-  h->ep_send_w = reinterpret_cast<float*>(b + o_sw);
-  h->ep_recv_x = reinterpret_cast<uint8_t*>(b + o_rx);
-  h->ep_recv_sa = reinterpret_cast<float*>(b + o_rsa);
-  h->ep_recv_idx = reinterpret_cast<int32_t*>(b + o_ridx);
-  h->ep_recv_w = reinterpret_cast<float*>(b + o_rw);
-  h->ep_partial = reinterpret_cast<uint16_t*>(b + o_part);
-  h->ep_contrib = reinterpret_cast<uint16_t*>(b + o_con);
-  h->ep_rank_of = reinterpret_cast<int32_t*>(b + o_rank);
-  h->ep_local_of = reinterpret_cast<int32_t*>(b + o_local);
-  h->ep_dflag = reinterpret_cast<uint32_t*>(b + o_dflag);
-  h->ep_cflag = reinterpret_cast<uint32_t*>(b + o_cflag);
-  h->ep_counters = reinterpret_cast<int*>(b + o_ctr);
-  GM_TRY(h, cudaMemset(h->ep_buf, 0, align_up(c.off, 256)), "ep buffers");
+  // Non-blocking communicator: the initialisation is polled against a host
+  // deadline (GM_OPT_EP_INIT_TIMEOUT_MS) and aborted when a rank never
+  // arrives, instead of blocking the caller for good.
   ncclUniqueId id;
   memcpy(&id, unique_id, sizeof id);
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
   ncclComm_t comm = nullptr;
-  const ncclResult_t r = nc->comm_init_rank(&comm, world, id, h->rank);
-  if (r != ncclSuccess) return set_err(h, GM_ENCCL, "ncclCommInitRank: %s", nc->get_error_string(r));
+  ncclResult_t r = nc->comm_init_rank_config(&comm, world, id, h->rank, &cfg);
+  if (r == ncclInProgress) r = nccl_settle(comm, r, h->ep_init_timeout_ms);
+  if (r != ncclSuccess) {
+    if (comm) nc->comm_abort(comm);
+    if (r == ncclInProgress)
+      return set_err(h, GM_ETIMEOUT, "ncclCommInitRankConfig: the group of %d ranks did not form within "
+                     "%d ms (a rank never joined); communicator aborted", world, h->ep_init_timeout_ms);
+    return set_err(h, GM_ENCCL, "ncclCommInitRankConfig: %s", nc->get_error_string(r));
+  }
   h->ep_comm = comm;
+  h->ep_on = true;
   // Peer-memory transport: map every rank's exchange allocation (the carve
   // offsets are the same on every rank: same max_tokens and world).
   bool ok = true;
@@ -1148,8 +1316,8 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
   if (dev_h) {
     cudaMemcpy(dev_h, &mine_h, sizeof mine_h, cudaMemcpyHostToDevice);
     char* dh = static_cast<char*>(dev_h);
-    ncclResult_t gr = nc->all_gather(dh, dh + sizeof(cudaIpcMemHandle_t), sizeof(cudaIpcMemHandle_t),
-                                     ncclUint8, comm, h->own_stream);
+    ncclResult_t gr = nccl_settle(comm, nc->all_gather(dh, dh + sizeof(cudaIpcMemHandle_t), sizeof(cudaIpcMemHandle_t),
+                                                       ncclUint8, comm, h->own_stream), 60000);
     if (gr != ncclSuccess || cudaStreamSynchronize(h->own_stream) != cudaSuccess) ok = false;
     if (ok) cudaMemcpy(all.data(), dh + sizeof(cudaIpcMemHandle_t), sizeof(cudaIpcMemHandle_t) * world,
                        cudaMemcpyDeviceToHost);
@@ -1165,29 +1333,15 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
     }
   }
   cudaGetLastError();
-  if (ok) {
-    const size_t rx[2] = {o_rx, o_rx1}, rsa[2] = {o_rsa, o_rsa1}, ridx[2] = {o_ridx, o_ridx1},
-                 rw[2] = {o_rw, o_rw1}, con[2] = {o_con, o_con1};
-    for (int par = 0; par < 2; ++par)
-      for (int q = 0; q < world; ++q) {
-        char* pb = static_cast<char*>(h->ep_peer_base[q]);
-        EpPeers& P = h->ep_peers[par];
-        P.recv_x[q] = reinterpret_cast<uint8_t*>(pb + rx[par]);
-        P.recv_sa[q] = reinterpret_cast<float*>(pb + rsa[par]);
-        P.recv_idx[q] = reinterpret_cast<int32_t*>(pb + ridx[par]);
-        P.recv_w[q] = reinterpret_cast<float*>(pb + rw[par]);
-        P.contrib[q] = reinterpret_cast<uint16_t*>(pb + con[par]);
-        P.dflag[q] = reinterpret_cast<uint32_t*>(pb + o_dflag);
-        P.cflag[q] = reinterpret_cast<uint32_t*>(pb + o_cflag);
-      }
-  }
+  if (ok) ep_wire(h, world, h->ep_peer_base, o);
   // every rank must choose the same transport: agree on "all ranks mapped"
   int* dflag_ok = nullptr;
   bool all_ok = false;
   if (cudaMalloc(&dflag_ok, sizeof(int) * (world + 1)) == cudaSuccess) {
     const int v = ok ? 1 : 0;
     cudaMemcpy(dflag_ok, &v, sizeof v, cudaMemcpyHostToDevice);
-    if (nc->all_gather(dflag_ok, dflag_ok + 1, 1, ncclInt32, comm, h->own_stream) == ncclSuccess &&
+    if (nccl_settle(comm, nc->all_gather(dflag_ok, dflag_ok + 1, 1, ncclInt32, comm, h->own_stream), 60000) ==
+            ncclSuccess &&
         cudaStreamSynchronize(h->own_stream) == cudaSuccess) {
       std::vector<int> v_all(world);
       cudaMemcpy(v_all.data(), dflag_ok + 1, sizeof(int) * world, cudaMemcpyDeviceToHost);
@@ -1202,62 +1356,238 @@ int gm_moe_ep_init(gm_moe_t* h, const void* unique_id, int world) {
   return GM_OK;
 }
 
-int gm_moe_ep_set_placement(gm_moe_t* h, const int32_t* expert_rank) {
-  if (!h || !expert_rank) return set_err(h, GM_EINVAL, "gm_moe_ep_set_placement: NULL argument");
-  if (!h->ep_comm) return set_err(h, GM_ESTATE, "gm_moe_ep_set_placement: gm_moe_ep_init first");
-  if (h->ep_placed) return set_err(h, GM_ESTATE, "gm_moe_ep_set_placement: placement already set");
+int gm_moe_ep_init_group(gm_moe_t* const* handles, int world) {
+  if (!handles || world < 1 || world > 8)
+    return set_err(nullptr, GM_EINVAL, "gm_moe_ep_init_group: world=%d (1..8) or NULL handles", world);
+  for (int g = 0; g < world; ++g) {
+    gm_moe* h = handles[g];
+    if (!h) return set_err(nullptr, GM_EINVAL, "gm_moe_ep_init_group: handle %d is NULL", g);
+    if (h->ep_on) return set_err(h, GM_ESTATE, "gm_moe_ep_init_group: handle %d already initialised", g);
+    if (h->degree != world || h->rank != g)
+      return set_err(h, GM_EINVAL, "gm_moe_ep_init_group: handle %d has rank %d of degree %d (want %d of %d)",
+                     g, h->rank, h->degree, g, world);
+    if (h->max_tokens != handles[0]->max_tokens)
+      return set_err(h, GM_EINVAL, "gm_moe_ep_init_group: every handle needs the same max_tokens");
+    for (int q = 0; q < g; ++q)
+      if (handles[q] == h) return set_err(h, GM_EINVAL, "gm_moe_ep_init_group: handle %d repeated", g);
+  }
+  // members on different devices store into each other's memory directly
+  for (int g = 0; g < world; ++g)
+    for (int q = 0; q < world; ++q) {
+      const int dg = handles[g]->device, dq = handles[q]->device;
+      if (dg == dq) continue;
+      int can = 0;
+      if (cudaDeviceCanAccessPeer(&can, dg, dq) != cudaSuccess || !can)
+        return set_err(handles[g], GM_ECUDA, "gm_moe_ep_init_group: device %d cannot access device %d", dg, dq);
+      GM_TRY(handles[g], cudaSetDevice(dg), "ep_init_group");
+      const cudaError_t e = cudaDeviceEnablePeerAccess(dq, 0);
+      if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+        return cuda_check(handles[g], e, "cudaDeviceEnablePeerAccess");
+      cudaGetLastError();
+    }
+  EpLayout o;
+  void* bases[8] = {};
+  for (int g = 0; g < world; ++g) {
+    GM_TRY(handles[g], cudaSetDevice(handles[g]->device), "ep_init_group");
+    int rc = ep_alloc(handles[g], world, &o);
+    if (rc) return rc;
+    bases[g] = handles[g]->ep_buf;
+  }
+  for (int g = 0; g < world; ++g) {
+    gm_moe* h = handles[g];
+    ep_wire(h, world, bases, o);
+    for (int q = 0; q < world; ++q) {
+      h->ep_members[q] = handles[q];
+      h->ep_peer_base[q] = bases[q];
+    }
+    h->ep_group = true;
+    h->ep_on = true;
+    h->ep_p2p_ok = h->ep_use_p2p = true;
+  }
+  return GM_OK;
+}
+
+int gm_moe_ep_forward_group(gm_moe_t* const* handles, int world, int layer, const void* const* x,
+                            void* const* out, const int* T, void* const* streams) {
+  if (!handles || !x || !out || !T || !streams || world < 1 || world > 8)
+    return set_err(nullptr, GM_EINVAL, "gm_moe_ep_forward_group: NULL argument or world=%d", world);
+  for (int g = 0; g < world; ++g) {
+    gm_moe* h = handles[g];
+    if (!h || !h->ep_group || h->degree != world || h->ep_members[g] != h || h->ep_members[0] != handles[0])
+      return set_err(h, GM_EINVAL, "gm_moe_ep_forward_group: handle %d is not member %d of one group "
+                     "(gm_moe_ep_init_group)", g, g);
+    int rc = ep_group_intact(h);
+    if (rc) return rc;
+    rc = check_layer(h, layer);
+    if (rc) return rc;
+    if (h->layers[layer].kind == 0) return set_err(h, GM_ESTATE, "layer %d has no registered weights", layer);
+    if (T[g] < 0 || T[g] > h->max_tokens)
+      return set_err(h, GM_EINVAL, "member %d: T=%d outside [0, max_tokens=%d]", g, T[g], h->max_tokens);
+    if (!x[g] || !out[g]) return set_err(h, GM_EINVAL, "member %d: NULL x/out", g);
+    // members sharing a GPU run their phases on one stream, in issue order: a
+    // wait kernel then never spins on a kernel that has not yet run
+    for (int q = 0; q < g; ++q)
+      if (handles[q]->device == h->device && streams[q] != streams[g])
+        return set_err(h, GM_EINVAL, "members %d and %d share device %d: pass them the same stream", q, g,
+                       h->device);
+  }
+  for (int phase = 0; phase < 3; ++phase)
+    for (int g = 0; g < world; ++g) {
+      gm_moe* h = handles[g];
+      GM_TRY(h, cudaSetDevice(h->device), "ep_forward_group");
+      if (h->pending.size() > 4096) {
+        int rc = drain_profile(h);
+        if (rc) return rc;
+      }
+      PdlScope pdl_scope(h->pdl);
+      const Layer& L = h->layers[layer];
+      cudaStream_t s = S(streams[g]);
+      int rc = phase == 0 ? ep_phase_a(h, L, static_cast<const uint16_t*>(x[g]), T[g], s)
+             : phase == 1 ? ep_phase_b(h, L, s)
+                          : ep_phase_c(h, static_cast<uint16_t*>(out[g]), T[g], s, nullptr);
+      if (rc) return rc;
+    }
+  return GM_OK;
+}
+
+namespace {
+// Checks an expert -> rank map (every rank exactly 128/world experts) and
+// derives the device tables: rank_of[e], local_of[e] (index among its rank's
+// experts, ascending id order) and, per rank, its experts in ascending order.
+int placement_tables(gm_moe* h, const int32_t* expert_rank, std::vector<int32_t>& rank_of,
+                     std::vector<int32_t>& local_of, std::vector<std::vector<int>>& mine) {
   const int G = h->degree, epr = h->epr;
-  std::vector<int32_t> rank_of(E), local_of(E), mine;
-  std::vector<int> per(G, 0);
+  rank_of.assign(E, 0);
+  local_of.assign(E, 0);
+  mine.assign(G, {});
   for (int e = 0; e < E; ++e) {
     const int r = expert_rank[e];
     if (r < 0 || r >= G) return set_err(h, GM_EINVAL, "expert %d placed on rank %d of %d", e, r, G);
     rank_of[e] = r;
-    local_of[e] = per[r]++;  // experts of a rank keep ascending id order
-    if (r == h->rank) mine.push_back(e);
+    local_of[e] = (int32_t)mine[r].size();
+    mine[r].push_back(e);
   }
   for (int r = 0; r < G; ++r)
-    if (per[r] != epr)
-      return set_err(h, GM_EINVAL, "rank %d holds %d experts; every rank must hold %d", r, per[r], epr);
-  const NcclApi* nc = nccl_api(nullptr);
-  GM_TRY(h, cudaSetDevice(h->device), "ep_set_placement");
+    if ((int)mine[r].size() != epr)
+      return set_err(h, GM_EINVAL, "rank %d holds %zu experts; every rank must hold %d", r, mine[r].size(), epr);
+  return GM_OK;
+}
+
+// The per-expert tensors of a layer, with their bytes per expert.
+std::vector<std::pair<void*, size_t>> expert_tensors(Layer& L) {
+  if (L.kind == 1)
+    return {{L.gu_q, (size_t)GU * H}, {L.gu_scale, GU * sizeof(float)}, {L.dn_q, (size_t)H * I},
+            {L.dn_scale, H * sizeof(float)}};
+  if (L.kind == 2) return {{L.gu_bf16, (size_t)GU * H * 2}, {L.dn_bf16, (size_t)H * I * 2}};
+  return {};
+}
+
+// After the expert tensors moved: the tcgen05 path's row-major copies (same
+// buffers, so the TMA descriptors stay valid) and the placement tables.
+int finish_placement(gm_moe* h, const std::vector<int32_t>& rank_of, const std::vector<int32_t>& local_of) {
   cudaStream_t s = h->own_stream;
-  // Every registered layer arrived as the reference's contiguous block of this
-  // rank: gather all blocks (global expert order) and keep this rank's experts.
-  auto redistribute = [&](void* local, size_t per_expert) -> int {
-    void* full = nullptr;
-    GM_TRY(h, cudaMalloc(&full, per_expert * E), "ep placement gather buffer");
-    int rc = nccl_check(h, nc->all_gather(local, full, per_expert * epr, ncclUint8, h->ep_comm, s),
-                        "ep placement all-gather");
-    for (int i = 0; rc == GM_OK && i < epr; ++i)
-      rc = cuda_check(h, cudaMemcpyAsync(static_cast<char*>(local) + i * per_expert,
-                                         static_cast<char*>(full) + mine[i] * per_expert, per_expert,
-                                         cudaMemcpyDeviceToDevice, s),
-                      "ep placement copy");
-    if (rc == GM_OK) rc = cuda_check(h, cudaStreamSynchronize(s), "ep placement");
-    cudaFree(full);
-    return rc;
-  };
-  for (auto& L : h->layers) {
-    int rc = GM_OK;
+  for (auto& L : h->layers)
     if (L.kind == 1) {
-      if ((rc = redistribute(L.gu_q, (size_t)GU * H)) || (rc = redistribute(L.gu_scale, GU * sizeof(float))) ||
-          (rc = redistribute(L.dn_q, (size_t)H * I)) || (rc = redistribute(L.dn_scale, H * sizeof(float))))
-        return rc;
-      // the tcgen05 path's row-major copies (same buffers, so the TMA descriptors stay valid)
-      GM_TRY(h, launch_vnni_permute(L.gu_q, (long)epr * GU, H, L.gu_rm, 1, s), "vnni unpack");
-      GM_TRY(h, launch_vnni_permute(L.dn_q, (long)epr * H, I, L.dn_rm, 1, s), "vnni unpack");
-    } else if (L.kind == 2) {
-      if ((rc = redistribute(L.gu_bf16, (size_t)GU * H * 2)) || (rc = redistribute(L.dn_bf16, (size_t)H * I * 2)))
-        return rc;
+      GM_TRY(h, launch_vnni_permute(L.gu_q, (long)h->epr * GU, H, L.gu_rm, 1, s), "vnni unpack");
+      GM_TRY(h, launch_vnni_permute(L.dn_q, (long)h->epr * H, I, L.dn_rm, 1, s), "vnni unpack");
     }
-  }
   GM_TRY(h, cudaMemcpyAsync(h->ep_rank_of, rank_of.data(), E * sizeof(int32_t), cudaMemcpyHostToDevice, s),
          "placement tables");
   GM_TRY(h, cudaMemcpyAsync(h->ep_local_of, local_of.data(), E * sizeof(int32_t), cudaMemcpyHostToDevice, s),
          "placement tables");
   GM_TRY(h, cudaStreamSynchronize(s), "placement tables");
   h->ep_placed = true;
+  return GM_OK;
+}
+}  // namespace
+
+int gm_moe_ep_set_placement(gm_moe_t* h, const int32_t* expert_rank) {
+  if (!h || !expert_rank) return set_err(h, GM_EINVAL, "gm_moe_ep_set_placement: NULL argument");
+  if (!h->ep_comm)
+    return set_err(h, GM_ESTATE, "gm_moe_ep_set_placement: gm_moe_ep_init first (an in-process group "
+                   "uses gm_moe_ep_set_placement_group)");
+  if (h->ep_placed) return set_err(h, GM_ESTATE, "gm_moe_ep_set_placement: placement already set");
+  const int epr = h->epr;
+  std::vector<int32_t> rank_of, local_of;
+  std::vector<std::vector<int>> mine;
+  int rc = placement_tables(h, expert_rank, rank_of, local_of, mine);
+  if (rc) return rc;
+  const NcclApi* nc = nccl_api(nullptr);
+  GM_TRY(h, cudaSetDevice(h->device), "ep_set_placement");
+  cudaStream_t s = h->own_stream;
+  // Every registered layer arrived as the reference's contiguous block of this
+  // rank: gather all blocks (global expert order) and keep this rank's experts.
+  for (auto& L : h->layers)
+    for (auto& t : expert_tensors(L)) {
+      void* full = nullptr;
+      GM_TRY(h, cudaMalloc(&full, t.second * E), "ep placement gather buffer");
+      rc = nccl_check(h, nc->all_gather(t.first, full, t.second * epr, ncclUint8, h->ep_comm, s),
+                      "ep placement all-gather");
+      for (int i = 0; rc == GM_OK && i < epr; ++i)
+        rc = cuda_check(h, cudaMemcpyAsync(static_cast<char*>(t.first) + i * t.second,
+                                           static_cast<char*>(full) + mine[h->rank][i] * t.second, t.second,
+                                           cudaMemcpyDeviceToDevice, s),
+                        "ep placement copy");
+      if (rc == GM_OK) rc = cuda_check(h, cudaStreamSynchronize(s), "ep placement");
+      cudaFree(full);
+      if (rc) return rc;
+    }
+  return finish_placement(h, rank_of, local_of);
+}
+
+int gm_moe_ep_set_placement_group(gm_moe_t* const* handles, int world, const int32_t* expert_rank) {
+  if (!handles || !expert_rank || world < 1 || world > 8)
+    return set_err(nullptr, GM_EINVAL, "gm_moe_ep_set_placement_group: NULL argument or world=%d", world);
+  for (int g = 0; g < world; ++g) {
+    gm_moe* h = handles[g];
+    if (!h || !h->ep_group || h->degree != world || h->ep_members[g] != h || h->ep_members[0] != handles[0])
+      return set_err(h, GM_EINVAL, "gm_moe_ep_set_placement_group: handle %d is not member %d of one group", g, g);
+    if (int rc = ep_group_intact(h)) return rc;
+    if (h->ep_placed) return set_err(h, GM_ESTATE, "gm_moe_ep_set_placement_group: placement already set");
+    if (h->num_layers != handles[0]->num_layers)
+      return set_err(h, GM_EINVAL, "gm_moe_ep_set_placement_group: members differ in their layer count");
+    for (int l = 0; l < h->num_layers; ++l)
+      if (h->layers[l].kind != handles[0]->layers[l].kind)
+        return set_err(h, GM_ESTATE, "layer %d is not registered alike on every member", l);
+  }
+  gm_moe* h0 = handles[0];
+  const int epr = h0->epr;
+  std::vector<int32_t> rank_of, local_of;
+  std::vector<std::vector<int>> mine;
+  int rc = placement_tables(h0, expert_rank, rank_of, local_of, mine);
+  if (rc) return rc;
+  // every member's contiguous block, in global expert order, on member 0's
+  // device; then each member copies out its placed experts
+  GM_TRY(h0, cudaSetDevice(h0->device), "ep_set_placement_group");
+  for (int l = 0; l < h0->num_layers; ++l) {
+    const size_t nt = expert_tensors(h0->layers[l]).size();
+    for (size_t ti = 0; ti < nt; ++ti) {
+      const size_t per = expert_tensors(h0->layers[l])[ti].second;
+      void* full = nullptr;
+      GM_TRY(h0, cudaSetDevice(h0->device), "ep_set_placement_group");
+      GM_TRY(h0, cudaMalloc(&full, per * E), "ep placement gather buffer");
+      for (int g = 0; rc == GM_OK && g < world; ++g) {
+        void* src = expert_tensors(handles[g]->layers[l])[ti].first;
+        rc = cuda_check(h0, cudaMemcpyPeer(static_cast<char*>(full) + (size_t)g * epr * per, h0->device, src,
+                                           handles[g]->device, per * epr),
+                        "ep placement gather");
+      }
+      for (int g = 0; rc == GM_OK && g < world; ++g) {
+        void* dst = expert_tensors(handles[g]->layers[l])[ti].first;
+        for (int i = 0; rc == GM_OK && i < epr; ++i)
+          rc = cuda_check(h0, cudaMemcpyPeer(static_cast<char*>(dst) + (size_t)i * per, handles[g]->device,
+                                             static_cast<char*>(full) + (size_t)mine[g][i] * per, h0->device, per),
+                          "ep placement copy");
+      }
+      cudaSetDevice(h0->device);
+      cudaFree(full);
+      if (rc) return rc;
+    }
+  }
+  for (int g = 0; g < world; ++g) {
+    GM_TRY(handles[g], cudaSetDevice(handles[g]->device), "ep_set_placement_group");
+    if ((rc = finish_placement(handles[g], rank_of, local_of))) return rc;
+  }
   return GM_OK;
 }
 

@@ -2,16 +2,22 @@
 //
 // gm_router_select needs a caller-provided scratch buffer (split-K partial
 // logits and the per-token inv_rms).  Some callers cannot produce one: code
-// running where cudaMalloc is not allowed or not wanted (inside a host
-// function of a stream, under an allocator that forbids device allocations,
-// a runtime that hands out fixed memory pools only, or a foreign-language
-// binding with no way to own device memory).  gm_router_select_noalloc keeps
-// that scratch in a fixed array compiled into this library instead.
+// running where cudaMalloc is not allowed or not wanted (under an allocator
+// that forbids device allocations, a runtime that hands out fixed memory
+// pools only, or a foreign-language binding with no way to own device
+// memory).  gm_router_select_noalloc keeps that scratch in a fixed array
+// compiled into this library instead.  It still calls the CUDA runtime
+// (symbol lookup, a memset, kernel launches), so it cannot be called where
+// CUDA calls are forbidden, such as inside a stream's host function.
 //
 // The array lives in every GPU's memory once the library is loaded and stays
 // there until the process exits.  All calls on one GPU share it and the last
 // call's contents stay in it; calls that overlap on the GPU (different streams
-// without ordering between them) race on it and must not be issued.
+// without ordering between them) race on it and must not be issued.  The
+// array's device address is cached per device for the life of the process;
+// cudaDeviceReset (or any teardown of the device's primary context) makes
+// that cached address stale, so this entry point must not be called on a
+// device after such a reset.
 #include <cstdio>
 #include <mutex>
 

@@ -52,6 +52,10 @@ SIGNATURES = {
     "gm_ep_unique_id": (_i32, [_vp, _sz]),
     "gm_moe_ep_init": (_i32, [_vp, _vp, _i32]),
     "gm_moe_ep_set_placement": (_i32, [_vp, C.POINTER(_i32)]),
+    "gm_moe_ep_init_group": (_i32, [C.POINTER(_vp), _i32]),
+    "gm_moe_ep_forward_group": (_i32, [C.POINTER(_vp), _i32, _i32, C.POINTER(_vp), C.POINTER(_vp),
+                                        C.POINTER(_i32), C.POINTER(_vp)]),
+    "gm_moe_ep_set_placement_group": (_i32, [C.POINTER(_vp), _i32, C.POINTER(_i32)]),
     "gm_moe_profile_read": (_i32, [_vp, C.POINTER(StageStat), _i32, C.POINTER(_i32), C.POINTER(_i64)]),
     "gm_router_select": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
     "gm_router_select_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),
@@ -335,7 +339,39 @@ OPT_PROFILE = 2
 OPT_PDL = 3
 OPT_EP_TRANSPORT = 4
 OPT_DENSE_TC_MIN_TOKENS = 5
+OPT_EP_TIMEOUT_MS = 6
+OPT_EP_INIT_TIMEOUT_MS = 7
 EP_UNIQUE_ID_BYTES = 128
+
+
+def _handles(blocks):
+    arr = (C.c_void_p * len(blocks))(*[b.h.value for b in blocks])
+    return arr
+
+
+def ep_init_group(blocks):
+    """Joins the MoeBlocks (rank g of degree len(blocks) at index g) into one
+    in-process expert-parallel group (no NCCL; members may share a GPU)."""
+    check(lib().gm_moe_ep_init_group(_handles(blocks), len(blocks)))
+
+
+def ep_forward_group(blocks, layer, xs, outs, Ts, streams=None):
+    """One layer on every member of an in-process group: member g's Ts[g]
+    tokens xs[g] -> outs[g] on streams[g] (members sharing a GPU need the same
+    stream; None = the default stream for every member)."""
+    n = len(blocks)
+    streams = [None] * n if streams is None else streams
+    xa = (C.c_void_p * n)(*[_addr(x) for x in xs])
+    oa = (C.c_void_p * n)(*[_addr(o) for o in outs])
+    ta = (C.c_int * n)(*[int(t) for t in Ts])
+    sa = (C.c_void_p * n)(*[_stream(s) for s in streams])
+    check(lib().gm_moe_ep_forward_group(_handles(blocks), n, layer, xa, oa, ta, sa))
+
+
+def ep_set_placement_group(blocks, expert_rank):
+    """gm_moe_ep_set_placement for an in-process group (one call for all)."""
+    arr = (C.c_int * NUM_EXPERTS)(*[int(r) for r in expert_rank])
+    check(lib().gm_moe_ep_set_placement_group(_handles(blocks), len(blocks), arr))
 
 
 def balanced_placement(load, world):
