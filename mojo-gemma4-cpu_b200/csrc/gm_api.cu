@@ -93,6 +93,7 @@ struct gm_moe {
   int* dev_err = nullptr;       // device-side error word (bounded waits that expired)
   int32_t* sched_counts = nullptr;  // per-chunk expert counts of the multi-CTA schedule
   int* router_counts = nullptr;     // router tile counters (zero between calls)
+  int* comb_counts = nullptr;       // arrival counters of the fused combine [rows][H/128] (zero between calls)
   alignas(64) unsigned char tmap_xg[128] = {};
   alignas(64) unsigned char tmap_bucket[128] = {};
   alignas(64) unsigned char tmap_xgb[128] = {};      // bf16 gathered rows (in ybuf's memory)
@@ -223,7 +224,7 @@ struct Carve {
 struct WsLayout {
   size_t logits, inv_rms, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
       x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, xg, xg_sa, dev_err,
-      sched_counts, router_counts, d_xi8, d_xsa, d_inv, d_hi8, d_hsa, d_out, total;
+      sched_counts, router_counts, comb_counts, d_xi8, d_xsa, d_inv, d_hi8, d_hsa, d_out, total;
 };
 
 WsLayout ws_layout(int max_tokens) {
@@ -254,6 +255,7 @@ WsLayout ws_layout(int max_tokens) {
   L.dev_err = c.take<int>(1);
   L.sched_counts = c.take<int32_t>(schedule_counts_ints(max_tokens));
   L.router_counts = c.take<int>(router_tile_counters(max_tokens));
+  L.comb_counts = c.take<int>(T * TC_COLS2);
   L.d_xi8 = c.take<int8_t>(T * H);
   L.d_xsa = c.take<float>(T);
   L.d_inv = c.take<float>(T);
@@ -361,6 +363,7 @@ int carve_workspace(gm_moe* h, int tokens) {
   h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
   h->sched_counts = reinterpret_cast<int32_t*>(b + L.sched_counts);
   h->router_counts = reinterpret_cast<int*>(b + L.router_counts);
+  h->comb_counts = reinterpret_cast<int*>(b + L.comb_counts);
   h->d_xi8 = reinterpret_cast<int8_t*>(b + L.d_xi8);
   h->d_xsa = reinterpret_cast<float*>(b + L.d_xsa);
   h->d_inv = reinterpret_cast<float*>(b + L.d_inv);
@@ -371,6 +374,7 @@ int carve_workspace(gm_moe* h, int tokens) {
                    make_tmap_i8(h->tmap_dh, h->d_hi8, (long)tokens, DENSE_I, 128);
   cudaMemset(h->dev_err, 0, sizeof(int));
   cudaMemset(h->router_counts, 0, sizeof(int) * router_tile_counters(tokens));
+  cudaMemset(h->comb_counts, 0, sizeof(int) * (size_t)tokens * TC_COLS2);
   h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)tokens * TOPK, H, 128) &&
              make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)tokens * TOPK, I, 128);
   // bf16 prefill: the gathered activation rows live in ybuf, which is idle
@@ -556,32 +560,69 @@ int join_dense(gm_moe* h, cudaStream_t s) {
   return cuda_check(h, cudaStreamWaitEvent(s, h->dense_done, 0), "dense join");
 }
 
+// Where experts_and_combine puts each row's finished MoE value: a local bf16
+// output, the post-MoE tail (x_main updated in place), or -- expert-parallel
+// forward over peer memory -- the partial row stored into its source rank's
+// contribution block, followed by the combine flags.
+struct CombineTarget {
+  uint16_t* out = nullptr;
+  const PostParams* post = nullptr;
+  const EpPeers* peers = nullptr;
+  uint32_t epoch = 0;
+};
+
 // Expert products and combine for Tn activation rows whose schedule
 // (expert_offset, routes, route_pos, chunk_off) is in the workspace: rows are
 // x_i8/x_sa (butterquant) or x_normed (bf16), route_idx their top-8.
 int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, const float* x_sa,
-                        const uint16_t* x_normed, const int32_t* route_idx, uint16_t* out,
-                        cudaStream_t s, const PostParams* post = nullptr, bool skip_combine = false) {
-  if (L.kind == 1) {
-    if (L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
-      // prefill: routed rows gathered in schedule order, then the tcgen05 GEMM
-      GM_STAGE(h, s, launch_gather_rows(x_i8, H, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
-                                        h->xg_sa, s),
-               "gather_rows");
-      GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, Tn, h->xg_sa,
-                                      L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
-               "bq_phase1_gate_up.tc");
-      GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, Tn,
-                                      h->bucket_sa, h->routes, L.dn_scale, h->ybuf, h->dev_err, s),
-               "bq_phase2_down.tc");
+                        const uint16_t* x_normed, const int32_t* route_idx, const CombineTarget& ct,
+                        cudaStream_t s) {
+  if (L.kind == 1 && L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
+    // prefill: routed rows gathered in schedule order, then the tcgen05 GEMMs;
+    // the down product's epilogue finishes each token's row (fused combine)
+    GM_STAGE(h, s, launch_gather_rows(x_i8, H, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
+                                      h->xg_sa, s),
+             "gather_rows");
+    GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, Tn, h->xg_sa,
+                                    L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
+             "bq_phase1_gate_up.tc");
+    TcCombine c;
+    c.route_idx = route_idx;
+    c.route_pos = h->route_pos;
+    c.counts = h->comb_counts;
+    if (ct.peers) {
+      for (int q = 0; q < h->degree; ++q) {
+        c.contrib[q] = ct.peers->contrib[q];
+        c.cflag[q] = ct.peers->cflag[q];
+      }
+      c.cap = h->max_tokens;
+      c.my_rank = h->rank;
+      c.G = h->degree;
+      c.epoch = ct.epoch;
+      c.done_counter = h->ep_counters + 1;
     } else {
-      GM_STAGE(h, s, launch_bq_phase1(x_i8, x_sa, h->expert_offset, h->routes, h->chunk_off, h->epr,
-                                      Tn, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
-               "bq_phase1_gate_up");
-      GM_STAGE(h, s, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
-                                      h->chunk_off, h->epr, Tn, L.dn_q, L.dn_scale, h->ybuf, true, s),
-               "bq_phase2_down");
+      c.out = ct.post ? h->out_stage : ct.out;
+      // a partial handle (degree > 1, no exchange) outputs zero for tokens
+      // with no route here; the fused combine writes only routed tokens
+      if (h->degree > 1 && !h->ep_on)
+        GM_TRY(h, cudaMemsetAsync(c.out, 0, (size_t)Tn * H * sizeof(uint16_t), s), "partial rows");
     }
+    GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, Tn,
+                                    h->bucket_sa, h->routes, L.dn_scale, h->ybuf, c, h->dev_err, s),
+             ct.peers ? "bq_phase2_down.tc.p2p" : "bq_phase2_down.tc");
+    if (ct.post) {
+      if (join_dense(h, s)) return GM_ECUDA;
+      GM_STAGE(h, s, launch_post_tail(h->out_stage, Tn, *ct.post, s), "post_tail");
+    }
+    return GM_OK;
+  }
+  if (L.kind == 1) {
+    GM_STAGE(h, s, launch_bq_phase1(x_i8, x_sa, h->expert_offset, h->routes, h->chunk_off, h->epr,
+                                    Tn, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
+             "bq_phase1_gate_up");
+    GM_STAGE(h, s, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
+                                    h->chunk_off, h->epr, Tn, L.dn_q, L.dn_scale, h->ybuf, true, s),
+             "bq_phase2_down");
   } else if (L.has_tc && h->tcb_ok && Tn >= h->tc_min_tokens) {
     GM_STAGE(h, s, launch_gather_rows(x_normed, 2 * H, nullptr, h->routes, h->expert_offset, h->epr, Tn,
                                       h->ybuf, nullptr, s),
@@ -600,12 +641,17 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
                                       L.dn_bf16, h->ybuf, s),
              "phase2_down");
   }
-  if (skip_combine) return GM_OK;
-  if (post && join_dense(h, s)) return GM_ECUDA;
-  if (post)
-    GM_STAGE(h, s, launch_combine_post(route_idx, h->route_pos, h->ybuf, Tn, *post, s), "combine.post");
+  if (ct.peers) {
+    GM_STAGE(h, s, launch_combine_p2p(route_idx, h->route_pos, h->ybuf, Tn, h->max_tokens, *ct.peers,
+                                      h->degree, h->rank, ct.epoch, h->ep_counters + 1, s),
+             "combine.p2p");
+    return GM_OK;
+  }
+  if (ct.post && join_dense(h, s)) return GM_ECUDA;
+  if (ct.post)
+    GM_STAGE(h, s, launch_combine_post(route_idx, h->route_pos, h->ybuf, Tn, *ct.post, s), "combine.post");
   else
-    GM_STAGE(h, s, launch_combine(route_idx, h->route_pos, h->ybuf, Tn, out, s), "combine");
+    GM_STAGE(h, s, launch_combine(route_idx, h->route_pos, h->ybuf, Tn, ct.out, s), "combine");
   return GM_OK;
 }
 
@@ -711,15 +757,12 @@ int ep_phase_b(gm_moe* h, const Layer& L, cudaStream_t s) {
                                          h->sched_counts, h->expert_offset, h->routes, h->route_pos,
                                          h->chunk_off, s),
              "ep_schedule");
-  // expert products only; the combine below stores into the sources' buffers
-  int rc = experts_and_combine(h, L, n, reinterpret_cast<const int8_t*>(rx), P.recv_sa[h->rank],
-                               reinterpret_cast<const uint16_t*>(rx), ridx, nullptr, s, nullptr,
-                               /*skip_combine=*/true);
-  if (rc) return rc;
-  GM_STAGE(h, s, launch_combine_p2p(ridx, h->route_pos, h->ybuf, n, cap, P, G, h->rank, h->ep_cur,
-                                    h->ep_counters + 1, s),
-           "combine.p2p");
-  return GM_OK;
+  // the experts; each row's partial goes into its source's contribution block
+  CombineTarget ct;
+  ct.peers = &P;
+  ct.epoch = h->ep_cur;
+  return experts_and_combine(h, L, n, reinterpret_cast<const int8_t*>(rx), P.recv_sa[h->rank],
+                             reinterpret_cast<const uint16_t*>(rx), ridx, ct, s);
 }
 
 // Phase C (peer memory): wait for every destination's partial rows, then sum
@@ -782,9 +825,10 @@ int ep_forward_nccl(gm_moe* h, const Layer& L, uint16_t* out, int T, cudaStream_
                                          h->sched_counts, h->expert_offset, h->routes, h->route_pos,
                                          h->chunk_off, s),
              "ep_schedule");
+  CombineTarget ct;
+  ct.out = h->ep_partial;
   int rc = experts_and_combine(h, L, n, reinterpret_cast<const int8_t*>(h->ep_recv_x), h->ep_recv_sa,
-                               reinterpret_cast<const uint16_t*>(h->ep_recv_x), h->ep_recv_idx,
-                               h->ep_partial, s);
+                               reinterpret_cast<const uint16_t*>(h->ep_recv_x), h->ep_recv_idx, ct, s);
   if (rc) return rc;
   // combine exchange: partial rows go back to the rank they came from
   {
@@ -1048,8 +1092,10 @@ int forward_impl(gm_moe* h, int layer, const void* x, void* out, int T, void* st
                                  h->chunk_off, h->sched_counts, s),
          "router_merge.schedule");
   // 4. experts, 5. combine (+ post-MoE tail)
-  return experts_and_combine(h, L, T, h->x_i8, h->x_sa, h->x_normed, h->route_idx,
-                             static_cast<uint16_t*>(out), s, post);
+  CombineTarget ct;
+  ct.out = static_cast<uint16_t*>(out);
+  ct.post = post;
+  return experts_and_combine(h, L, T, h->x_i8, h->x_sa, h->x_normed, h->route_idx, ct, s);
 }
 }  // namespace
 
@@ -1597,7 +1643,14 @@ int gm_moe_device_status(gm_moe_t* h, int* device_error) {
   GM_TRY(h, cudaDeviceSynchronize(), "device_status");
   GM_TRY(h, cudaMemcpy(device_error, h->dev_err, sizeof(int), cudaMemcpyDeviceToHost), "device_status");
   GM_TRY(h, cudaMemset(h->dev_err, 0, sizeof(int)), "device_status");
-  if (*device_error) return set_err(h, GM_ETIMEOUT, "a kernel's bounded wait expired (code %d)", *device_error);
+  if (*device_error) {
+    // a kernel that gave up may have left self-re-arming counters mid-count
+    cudaMemset(h->router_counts, 0, sizeof(int) * router_tile_counters(h->ws_tokens));
+    cudaMemset(h->comb_counts, 0, sizeof(int) * (size_t)h->ws_tokens * TC_COLS2);
+    if (h->ep_counters) cudaMemset(h->ep_counters, 0, 2 * sizeof(int));
+    cudaDeviceSynchronize();
+    return set_err(h, GM_ETIMEOUT, "a kernel's bounded wait expired (code %d)", *device_error);
+  }
   return GM_OK;
 }
 
