@@ -766,8 +766,8 @@ def stage_model(label, fmt, T, distinct, R):
     ksplit = H // 256
     if label == "bq_phase1_gate_up":
         return "hbm", distinct * BQ_EXPERT_GU_BYTES + R * (H + 4) // TOPK + R * (I + 11 * 4)
-    if label == "bq_phase2_down":
-        return "hbm", distinct * BQ_EXPERT_DN_BYTES + R * (I + 11 * 4) + R * H * 4
+    if label in ("bq_phase2_down", "bq_phase2_down.p2p"):  # + the fused combine's bf16 rows
+        return "hbm", distinct * BQ_EXPERT_DN_BYTES + R * (I + 11 * 4) + (R // TOPK) * H * 2
     if label == "bq_phase1_gate_up.tc":
         return "tensor", 2.0 * R * GU * H
     if label in ("bq_phase2_down.tc", "bq_phase2_down.tc.p2p"):  # + the fused combine

@@ -577,15 +577,9 @@ struct CombineTarget {
 int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, const float* x_sa,
                         const uint16_t* x_normed, const int32_t* route_idx, const CombineTarget& ct,
                         cudaStream_t s) {
-  if (L.kind == 1 && L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
-    // prefill: routed rows gathered in schedule order, then the tcgen05 GEMMs;
-    // the down product's epilogue finishes each token's row (fused combine)
-    GM_STAGE(h, s, launch_gather_rows(x_i8, H, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
-                                      h->xg_sa, s),
-             "gather_rows");
-    GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, Tn, h->xg_sa,
-                                    L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
-             "bq_phase1_gate_up.tc");
+  if (L.kind == 1) {
+    // butterquant: the down product's epilogue finishes each token's row
+    // (fused weighted combine), on the tcgen05 kernel and on the decode kernel
     TcCombine c;
     c.route_idx = route_idx;
     c.route_pos = h->route_pos;
@@ -607,23 +601,32 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
       if (h->degree > 1 && !h->ep_on)
         GM_TRY(h, cudaMemsetAsync(c.out, 0, (size_t)Tn * H * sizeof(uint16_t), s), "partial rows");
     }
-    GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, Tn,
-                                    h->bucket_sa, h->routes, L.dn_scale, h->ybuf, c, h->dev_err, s),
-             ct.peers ? "bq_phase2_down.tc.p2p" : "bq_phase2_down.tc");
+    if (L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
+      // prefill: routed rows gathered in schedule order, then the tcgen05 GEMMs
+      GM_STAGE(h, s, launch_gather_rows(x_i8, H, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
+                                        h->xg_sa, s),
+               "gather_rows");
+      GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, Tn, h->xg_sa,
+                                      L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
+               "bq_phase1_gate_up.tc");
+      GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, Tn,
+                                      h->bucket_sa, h->routes, L.dn_scale, h->ybuf, c, h->dev_err, s),
+               ct.peers ? "bq_phase2_down.tc.p2p" : "bq_phase2_down.tc");
+    } else {
+      GM_STAGE(h, s, launch_bq_phase1(x_i8, x_sa, h->expert_offset, h->routes, h->chunk_off, h->epr,
+                                      Tn, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
+               "bq_phase1_gate_up");
+      GM_STAGE(h, s, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
+                                      h->chunk_off, h->epr, Tn, L.dn_q, L.dn_scale, h->ybuf, true, s, &c),
+               ct.peers ? "bq_phase2_down.p2p" : "bq_phase2_down");
+    }
     if (ct.post) {
       if (join_dense(h, s)) return GM_ECUDA;
       GM_STAGE(h, s, launch_post_tail(h->out_stage, Tn, *ct.post, s), "post_tail");
     }
     return GM_OK;
   }
-  if (L.kind == 1) {
-    GM_STAGE(h, s, launch_bq_phase1(x_i8, x_sa, h->expert_offset, h->routes, h->chunk_off, h->epr,
-                                    Tn, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
-             "bq_phase1_gate_up");
-    GM_STAGE(h, s, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
-                                    h->chunk_off, h->epr, Tn, L.dn_q, L.dn_scale, h->ybuf, true, s),
-             "bq_phase2_down");
-  } else if (L.has_tc && h->tcb_ok && Tn >= h->tc_min_tokens) {
+  if (L.has_tc && h->tcb_ok && Tn >= h->tc_min_tokens) {
     GM_STAGE(h, s, launch_gather_rows(x_normed, 2 * H, nullptr, h->routes, h->expert_offset, h->epr, Tn,
                                       h->ybuf, nullptr, s),
              "gather_rows");

@@ -106,10 +106,13 @@ cudaError_t launch_dense_down(const int8_t* hi8, const float* hsa, int T, const 
                               const float* dsc, uint16_t* out, cudaStream_t s);
 // bulk L2 prefetch of [base, base + bytes) (16-byte aligned base)
 cudaError_t launch_l2_prefetch(const void* base, size_t bytes, cudaStream_t s);
+struct TcCombine;
+// comb (may be null): the fused weighted combine of the tcgen05 kernel
+// (TcCombine below), on the decode kernel's 128-column groups
 cudaError_t launch_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t* expert_offset,
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_dn, const float* dn_scale, float* ybuf,
-                             bool after_phase1, cudaStream_t s);
+                             bool after_phase1, cudaStream_t s, const TcCombine* comb = nullptr);
 cudaError_t launch_bf16_phase1(const uint16_t* xn, const int32_t* expert_offset,
                                const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                                const uint16_t* w_gu, uint16_t* bucket, cudaStream_t s);
