@@ -250,8 +250,8 @@ bq_phase1_kernel(const int8_t* __restrict__ xi8, const float* __restrict__ xsa,
 // token whose last route this was: the token's <= 8 slices in ascending
 // expert order, added from 0.0f and rounded to bf16 (the reference's order,
 // butterquant_kernels/moe.mojo:252-290), stored to the output or, expert-
-// parallel, into the source rank's contribution block; the consumed L2 lines
-// are dropped and the counter re-armed.  Same counters and the same sum as
+// parallel, into the source rank's contribution block, and the counter is
+// re-armed.  Same counters and the same sum as
 // the tcgen05 kernel's combine (gemm_tc.cu).
 __device__ __forceinline__ void finish_token_slice(const TcCombine& comb, const float* ybuf, int tok,
                                                    int col, int lane) {
@@ -286,12 +286,6 @@ __device__ __forceinline__ void finish_token_slice(const TcCombine& comb, const 
                            : comb.contrib[tok / comb.cap] + ((size_t)comb.my_rank * comb.cap + tok % comb.cap) * H;
   *reinterpret_cast<uint2*>(dst + c0) = make_uint2((uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16),
                                                    (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16));
-  __syncwarp();
-  // lanes 0..31 drop the 4 lines (512 bytes) of each of the token's slices
-  const int k = lane >> 2;
-  if (k < TOPK && ps[k] >= 0)
-    asm volatile("discard.global.L2 [%0], 128;" ::"l"(ybuf + (size_t)ps[k] * H + (size_t)col * 128 + 32 * (lane & 3))
-                 : "memory");
   if (lane == 0) comb.counts[(size_t)tok * TC_COLS2 + col] = 0;  // re-armed for the next call
 }
 

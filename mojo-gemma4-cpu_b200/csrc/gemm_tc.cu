@@ -338,12 +338,6 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   if (tid == 0 && s.failed) atomicExch(err, ERR_TIMEOUT);
 }
 
-// L2 line of a finished route slice: dropped without a write-back (its only
-// reader has consumed it).
-__device__ __forceinline__ void discard_l2_line(const void* p) {
-  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
-}
-
 // Phase 2: the down product with the reference's per-64-K-block fma chain,
 // followed (MoE) by the fused weighted combine or (DENSE) by the dense MLP's
 // bf16 output rows.
@@ -362,9 +356,10 @@ __device__ __forceinline__ void discard_l2_line(const void* p) {
 // from 0.0f (the reference's accumulation order, butterquant_kernels/
 // moe.mojo:252-290), round to bf16 (butterquant/convert.mojo:13-17), store
 // the 128 columns to the output (or, expert-parallel, into the source rank's
-// contribution block in peer memory), drop the consumed lines from L2 and
-// re-arm the counter.  Column-major order keeps a column's slices L2-resident
-// between their store and that read.
+// contribution block in peer memory) and re-arm the counter.  Column-major
+// order keeps a column's slices L2-resident between their store and that
+// read.  (Dropping the consumed lines with discard.global.L2 was measured:
+// it made the kernel ten times slower.)
 template <bool DENSE>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -637,9 +632,6 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                              (uint32_t)f2bf(acc[2 * u + 1].x) | ((uint32_t)f2bf(acc[2 * u + 1].y) << 16),
                              (uint32_t)f2bf(acc[2 * u + 1].z) | ((uint32_t)f2bf(acc[2 * u + 1].w) << 16));
           }
-#pragma unroll
-          for (int k = 0; k < TOPK; ++k)
-            if (ps[k] >= 0) discard_l2_line(ybuf + (size_t)ps[k] * H + col0);
           if (cb == 0) comb.counts[(size_t)lt * NT2 + ti.col] = 0;  // re-armed for the next call
         }
       }
