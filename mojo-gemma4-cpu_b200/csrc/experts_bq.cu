@@ -33,6 +33,7 @@
 // Phase 2 writes per-route f32 rows y = facc*sw*w; in the forward the token's
 // last route sums them in ascending expert order (the reference's
 // accumulation order) inside the same kernel, otherwise combine.cu does.
+#include "combine_dev.cuh"
 #include "ep_dev.cuh"
 #include "gm_kernels.h"
 #include "vnni_stream.cuh"
@@ -243,52 +244,12 @@ bq_phase1_kernel(const int8_t* __restrict__ xi8, const float* __restrict__ xsa,
   }
 }
 
-// The weighted combine fused into the decode down product (comb.counts
+// The weighted combine is fused into the decode down product (comb.counts
 // non-null): a work item's routes have just stored their slices of hidden
 // columns [128*blk, 128*blk+128) (f32, L2); one thread per route bumps the
 // (token, column group) arrival counter, and the CTA then finishes every
-// token whose last route this was: the token's <= 8 slices in ascending
-// expert order, added from 0.0f and rounded to bf16 (the reference's order,
-// butterquant_kernels/moe.mojo:252-290), stored to the output or, expert-
-// parallel, into the source rank's contribution block, and the counter is
-// re-armed.  Same counters and the same sum as
-// the tcgen05 kernel's combine (gemm_tc.cu).
-__device__ __forceinline__ void finish_token_slice(const TcCombine& comb, const float* ybuf, int tok,
-                                                   int col, int lane) {
-  int ex[TOPK], pp[TOPK], ps[TOPK];
-#pragma unroll
-  for (int k = 0; k < TOPK; ++k) {
-    pp[k] = __ldg(comb.route_pos + (size_t)tok * TOPK + k);
-    ex[k] = __ldg(comb.route_idx + (size_t)tok * TOPK + k);
-    ps[k] = -1;
-  }
-#pragma unroll
-  for (int k = 0; k < TOPK; ++k) {
-    int rank = 0;
-#pragma unroll
-    for (int j = 0; j < TOPK; ++j) rank += (pp[j] >= 0 && ex[j] < ex[k]) ? 1 : 0;
-#pragma unroll
-    for (int j = 0; j < TOPK; ++j)
-      if (pp[k] >= 0 && rank == j) ps[j] = pp[k];
-  }
-  const size_t c0 = (size_t)col * 128 + 4 * lane;  // this lane's 4 columns
-  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-  for (int k = 0; k < TOPK; ++k) {
-    if (ps[k] < 0) break;
-    const float4 y = __ldcg(reinterpret_cast<const float4*>(ybuf + (size_t)ps[k] * H + c0));
-    acc.x = __fadd_rn(acc.x, y.x);
-    acc.y = __fadd_rn(acc.y, y.y);
-    acc.z = __fadd_rn(acc.z, y.z);
-    acc.w = __fadd_rn(acc.w, y.w);
-  }
-  uint16_t* dst = comb.out ? comb.out + (size_t)tok * H
-                           : comb.contrib[tok / comb.cap] + ((size_t)comb.my_rank * comb.cap + tok % comb.cap) * H;
-  *reinterpret_cast<uint2*>(dst + c0) = make_uint2((uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16),
-                                                   (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16));
-  if (lane == 0) comb.counts[(size_t)tok * TC_COLS2 + col] = 0;  // re-armed for the next call
-}
-
+// token whose last route this was (finish_token_slice, combine_dev.cuh) --
+// the same counters and sum as the tcgen05 kernel's combine (gemm_tc.cu).
 // `prologue_prefetch`: the schedule (two launches back) is complete when the
 // kernel starts, so the first weight chunks are issued before waiting for
 // phase 1's bucket.  Only the fused forward sets it (it always runs phase 1

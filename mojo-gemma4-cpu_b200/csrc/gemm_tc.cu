@@ -32,6 +32,7 @@
 // barrier and frees its TMEM.
 #include <cuda.h>
 
+#include "combine_dev.cuh"
 #include "ep_dev.cuh"
 #include "gm_kernels.h"
 #include "tc_prims.cuh"
@@ -51,7 +52,7 @@ constexpr int A_BYTES = BM * BK;   // 16 KB
 constexpr int B_BYTES = BN * BK;   // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int STAGES1 = 5;
-constexpr int STAGES2 = 6;
+constexpr int STAGES2 = 4;
 constexpr int RING = 4;            // phase-2 TMEM regions
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;  // 576
@@ -59,6 +60,7 @@ constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr uint32_t TMEM_COLS1 = 256;         // two 128-column accumulators
 constexpr uint32_t TMEM_COLS2 = RING * BN;   // 512
 constexpr int XSTR = 64 + 4;       // phase-1 exchange row stride (floats)
+constexpr int YSTR = BN + 4;       // phase-2 output staging row stride (floats)
 constexpr int ERR_TIMEOUT = 1;
 
 struct Smem1 {
@@ -76,13 +78,14 @@ struct Smem1 {
 
 struct Smem2 {
   uint8_t stage[STAGES2][STAGE_BYTES];
+  float ystage[BM][YSTR];
   uint64_t full[STAGES2];
   uint64_t empty[STAGES2];
   uint64_t reg_full[RING];
   uint64_t reg_empty[RING];
   uint32_t tmem_base;
   int failed;
-  int last_tok[BM];  // fused combine: the token a tile row completes, or -1
+  int row_tok[BM];   // fused combine: token of each tile row (-1 past the routes)
   TileTable tt;
 };
 
@@ -345,21 +348,18 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 // Tiles are walked column-major (tile_info_colmajor): all m-tiles of hidden
 // columns [128c, 128c+128) before column c+1.  Epilogue warp (q, cb) owns
 // TMEM lanes 32q..32q+31 (one route row per thread) and columns 32cb..32cb+31
-// of the tile; the TMEM load of block b+1 is issued before block b's
-// arithmetic so that its latency overlaps it.
+// of the tile; the tile's outputs are staged in shared memory and written as
+// whole 128-column rows, 8 rows per warp.
 //
-// Fused combine (MoE): each thread stores its weighted slice
-// y = facc*sw*w_route (f32, 128 bytes: one L2 line) and, per (token, column
-// tile), an arrival counter is bumped once per route row.  The row that
-// brings it to the token's number of local routes is the token's last: its 4
-// threads re-read the token's <= 8 slices in ascending expert order, add them
-// from 0.0f (the reference's accumulation order, butterquant_kernels/
-// moe.mojo:252-290), round to bf16 (butterquant/convert.mojo:13-17), store
-// the 128 columns to the output (or, expert-parallel, into the source rank's
-// contribution block in peer memory) and re-arm the counter.  Column-major
-// order keeps a column's slices L2-resident between their store and that
-// read.  (Dropping the consumed lines with discard.global.L2 was measured:
-// it made the kernel ten times slower.)
+// Fused combine (MoE): the rows are the routes' weighted outputs
+// y = facc*sw*w_route (f32).  After storing its 8 rows a warp bumps each
+// row's (token, column tile) arrival counter; the row that brings it to the
+// token's number of local routes is the token's last, and the warp finishes
+// that token's 128 columns (finish_token_slice: the <= 8 slices summed in
+// ascending expert order from 0.0f, bf16) into the output or, expert-
+// parallel, into the source rank's contribution block in peer memory.
+// Column-major order keeps a column's slices L2-resident between their store
+// and that read.
 template <bool DENSE>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -478,163 +478,112 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       const bool valid = r < ti.nvalid;
       const bool quarter_live = q * 32 < ti.nvalid;  // warp-uniform
       const int row = ti.row0 + r;
+      // per-tile operands are loaded before the first accumulator wait
+      // the 11 expert block scales are held in registers; the dense MLP's 33
+      // are read per block (issued before that block's accumulator wait)
       float adv[DENSE ? 1 : NB];
       if constexpr (!DENSE) {
 #pragma unroll
         for (int b = 0; b < NB; ++b)
           adv[b] = valid ? __fmul_rn(bsa[(size_t)row * NB + b], inv127) : 0.0f;
       }
-      SparseRoute rt = {0, 0.0f};
+      SparseRoute rt = {-1, 0.0f};
       if (!DENSE && valid) rt = routes[row];
       const float* wsc = dn_scale + (size_t)ti.e * H + ti.col * BN + 32 * cb;
-      const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(32 * cb);
       float2 facc[16];
 #pragma unroll
       for (int n = 0; n < 16; ++n) facc[n] = make_float2(0.0f, 0.0f);
-      // The thread's 32 columns of a block are read as two 16-column segments;
-      // segment i+1's TMEM load is issued before segment i's arithmetic, and a
-      // block's region is released once both of its segments are in registers.
-      int d[2][16];
-      // as in phase 1: after a failed wait keep going without waiting, so the
-      // quarter's named barriers are always met; the vote keeps the warp
-      // converged for the .sync.aligned TMEM loads
-      (void)__all_sync(0xffffffffu, mbar_wait<false>(&s.reg_full[reg], rphase, &s.failed));
-      tc_fence_after();
-      if (quarter_live) tmem_ld16(lane_base + (uint32_t)(reg * BN), d[0]);
 #pragma unroll
-      for (int i = 0; i < 2 * NB; ++i) {
-        const int b = i >> 1, hh = i & 1;
+      for (int b = 0; b < NB; ++b) {
         float adv_b;
         if constexpr (DENSE)
           adv_b = valid ? __fmul_rn(__ldg(bsa + (size_t)row * NB + b), inv127) : 0.0f;
         else
           adv_b = adv[b];
-        tmem_ld_wait();  // segment i is in d[i & 1]
-        if (hh == 1) {   // both segments of block b read: release its region
-          tc_fence_before();
-          mbar_arrive(&s.reg_empty[reg]);
-          if (++reg == RING) { reg = 0; rphase ^= 1; }
-        }
-        if (i + 1 < 2 * NB) {
-          if (hh == 1) {
-            (void)__all_sync(0xffffffffu, mbar_wait<false>(&s.reg_full[reg], rphase, &s.failed));
-            tc_fence_after();
-          }
-          if (quarter_live)
-            tmem_ld16(lane_base + (uint32_t)(reg * BN + 16 * ((i + 1) & 1)), d[(i + 1) & 1]);
-        }
+        // as in phase 1: after a failed wait keep going without waiting, so the
+        // quarter's named barriers are always met
+        (void)__all_sync(0xffffffffu, mbar_wait<false>(&s.reg_full[reg], rphase, &s.failed));
+        tc_fence_after();
+        int d[32];
+        if (quarter_live)  // a quarter with no valid route rows only releases the region
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(reg * BN + 32 * cb), d);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&s.reg_empty[reg]);
+        if (++reg == RING) { reg = 0; rphase ^= 1; }
         if (quarter_live) {
           const float2 a2 = make_float2(adv_b, adv_b);
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            facc[8 * hh + j] =
-                fma2(small_ints_to_float2(d[i & 1][2 * j], d[i & 1][2 * j + 1]), a2, facc[8 * hh + j]);
+          for (int i = 0; i < 16; ++i)
+            facc[i] = fma2(small_ints_to_float2(d[2 * i], d[2 * i + 1]), a2, facc[i]);
         }
       }
-      if constexpr (DENSE) {
-        // out = bf16(facc * sw): 32 columns (64 bytes) of the row
-        if (valid) {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(yout) + (size_t)row * H +
-                                                ti.col * BN + 32 * cb);
+      // y = facc * sw * w_route (dense: facc * sw), staged per row then
+      // written as whole rows
+      const float2 wr2 = make_float2(rt.weight, rt.weight);
+      float4* ys = reinterpret_cast<float4*>(&s.ystage[r][32 * cb]);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const float4 s0 = __ldg(reinterpret_cast<const float4*>(wsc) + 2 * v);
-            const float4 s1 = __ldg(reinterpret_cast<const float4*>(wsc) + 2 * v + 1);
-            const float2 a = mul2(facc[4 * v], make_float2(s0.x, s0.y));
-            const float2 b2 = mul2(facc[4 * v + 1], make_float2(s0.z, s0.w));
-            const float2 c2 = mul2(facc[4 * v + 2], make_float2(s1.x, s1.y));
-            const float2 e2 = mul2(facc[4 * v + 3], make_float2(s1.z, s1.w));
-            dst[v] = make_uint4((uint32_t)f2bf(a.x) | ((uint32_t)f2bf(a.y) << 16),
-                                (uint32_t)f2bf(b2.x) | ((uint32_t)f2bf(b2.y) << 16),
-                                (uint32_t)f2bf(c2.x) | ((uint32_t)f2bf(c2.y) << 16),
-                                (uint32_t)f2bf(e2.x) | ((uint32_t)f2bf(e2.y) << 16));
+      for (int v = 0; v < 8; ++v) {
+        const float4 sw = __ldg(reinterpret_cast<const float4*>(wsc) + v);
+        float2 lo = mul2(facc[2 * v], make_float2(sw.x, sw.y));
+        float2 hi = mul2(facc[2 * v + 1], make_float2(sw.z, sw.w));
+        if constexpr (!DENSE) {
+          lo = mul2(lo, wr2);
+          hi = mul2(hi, wr2);
+        }
+        ys[v] = make_float4(lo.x, lo.y, hi.x, hi.y);
+      }
+      if (!DENSE && cb == 0) s.row_tok[r] = rt.token;
+      quarter_sync(q);
+      // the 4 warps of quarter q write its 32 rows: 8 rows each, one whole row
+      // (128 columns) per warp store
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int rr = q * 32 + cb * 8 + j;
+        if (rr < ti.nvalid) {
+          const float4 v = reinterpret_cast<const float4*>(&s.ystage[rr][0])[lane];
+          if constexpr (DENSE) {
+            const uint2 o = make_uint2((uint32_t)f2bf(v.x) | ((uint32_t)f2bf(v.y) << 16),
+                                       (uint32_t)f2bf(v.z) | ((uint32_t)f2bf(v.w) << 16));
+            reinterpret_cast<uint2*>(static_cast<uint16_t*>(yout) + (size_t)(ti.row0 + rr) * H +
+                                     ti.col * BN)[lane] = o;
+          } else {
+            __stcg(reinterpret_cast<float4*>(static_cast<float*>(yout) + (size_t)(ti.row0 + rr) * H +
+                                             ti.col * BN) + lane, v);
           }
         }
-      } else {
-        float* ybuf = static_cast<float*>(yout);
-        const size_t col0 = (size_t)ti.col * BN + 32 * cb;
-        // y = facc * sw * w_route: one 128-byte line of the route's row
-        if (valid) {
-          const float2 wr2 = make_float2(rt.weight, rt.weight);
-          float4* yp = reinterpret_cast<float4*>(ybuf + (size_t)row * H + col0);
-#pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            const float4 sw = __ldg(reinterpret_cast<const float4*>(wsc) + v);
-            const float2 lo = mul2(mul2(facc[2 * v], make_float2(sw.x, sw.y)), wr2);
-            const float2 hi = mul2(mul2(facc[2 * v + 1], make_float2(sw.z, sw.w)), wr2);
-            __stcg(yp + v, make_float4(lo.x, lo.y, hi.x, hi.y));
-          }
-        }
-        quarter_sync(q);  // the quarter's 4 slices of every row are stored
-        if (cb == 0) {
-          int lt = -1;
-          if (valid) {
-            const int4 p0 = __ldg(reinterpret_cast<const int4*>(comb.route_pos) + 2 * rt.token);
-            const int4 p1 = __ldg(reinterpret_cast<const int4*>(comb.route_pos) + 2 * rt.token + 1);
+      }
+      if constexpr (!DENSE) {
+        // Fused combine: this warp's 8 rows are stored; one arrival per row
+        // on its (token, column tile) counter.  The warp then finishes every
+        // token whose last route one of these rows was.
+        __syncwarp();  // the lanes' row stores are ordered before the arrivals
+        int lt = -1;
+        if (lane < 8) {
+          const int rr = q * 32 + cb * 8 + lane;
+          const int tok = rr < ti.nvalid ? s.row_tok[rr] : -1;
+          if (tok >= 0) {
+            const int4 p0 = __ldg(reinterpret_cast<const int4*>(comb.route_pos) + 2 * tok);
+            const int4 p1 = __ldg(reinterpret_cast<const int4*>(comb.route_pos) + 2 * tok + 1);
             const int nloc = (p0.x >= 0) + (p0.y >= 0) + (p0.z >= 0) + (p0.w >= 0) + (p1.x >= 0) +
                              (p1.y >= 0) + (p1.z >= 0) + (p1.w >= 0);
-            __threadfence();  // the slices stored above, before the arrival
-            const int old = atomicAdd(comb.counts + (size_t)rt.token * NT2 + ti.col, 1);
-            if (old == nloc - 1) {
+            __threadfence();
+            if (atomicAdd(comb.counts + (size_t)tok * NT2 + ti.col, 1) == nloc - 1) {
               __threadfence();  // every other route's slice, before the re-read
-              lt = rt.token;
+              lt = tok;
             }
           }
-          s.last_tok[r] = lt;
         }
-        quarter_sync(q);
-        const int lt = s.last_tok[r];
-        if (lt >= 0) {
-          // the token's local routes in ascending expert order (its expert ids
-          // are distinct): ps[j] = position of the route of rank j, -1 past the end
-          int ex[TOPK], pp[TOPK], ps[TOPK];
-#pragma unroll
-          for (int k = 0; k < TOPK; ++k) {
-            pp[k] = __ldg(comb.route_pos + (size_t)lt * TOPK + k);
-            ex[k] = __ldg(comb.route_idx + (size_t)lt * TOPK + k);
-            ps[k] = -1;
-          }
-#pragma unroll
-          for (int k = 0; k < TOPK; ++k) {
-            int rank = 0;
-#pragma unroll
-            for (int j = 0; j < TOPK; ++j) rank += (pp[j] >= 0 && ex[j] < ex[k]) ? 1 : 0;
-#pragma unroll
-            for (int j = 0; j < TOPK; ++j)
-              if (pp[k] >= 0 && rank == j) ps[j] = pp[k];
-          }
-          uint16_t* dst = comb.out ? comb.out + (size_t)lt * H
-                                   : comb.contrib[lt / comb.cap] + ((size_t)comb.my_rank * comb.cap + lt % comb.cap) * H;
-          uint4* d4 = reinterpret_cast<uint4*>(dst + col0);
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {  // 16 columns at a time
-            float4 acc[4];
-#pragma unroll
-            for (int v = 0; v < 4; ++v) acc[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-            for (int k = 0; k < TOPK; ++k) {
-              if (ps[k] < 0) break;
-              const float4* yp = reinterpret_cast<const float4*>(ybuf + (size_t)ps[k] * H + col0) + 4 * half;
-#pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                const float4 y = __ldcg(yp + v);
-                acc[v].x = __fadd_rn(acc[v].x, y.x);
-                acc[v].y = __fadd_rn(acc[v].y, y.y);
-                acc[v].z = __fadd_rn(acc[v].z, y.z);
-                acc[v].w = __fadd_rn(acc[v].w, y.w);
-              }
-            }
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-              d4[2 * half + u] =
-                  make_uint4((uint32_t)f2bf(acc[2 * u].x) | ((uint32_t)f2bf(acc[2 * u].y) << 16),
-                             (uint32_t)f2bf(acc[2 * u].z) | ((uint32_t)f2bf(acc[2 * u].w) << 16),
-                             (uint32_t)f2bf(acc[2 * u + 1].x) | ((uint32_t)f2bf(acc[2 * u + 1].y) << 16),
-                             (uint32_t)f2bf(acc[2 * u + 1].z) | ((uint32_t)f2bf(acc[2 * u + 1].w) << 16));
-          }
-          if (cb == 0) comb.counts[(size_t)lt * NT2 + ti.col] = 0;  // re-armed for the next call
+        unsigned last = __ballot_sync(0xffffffffu, lt >= 0);
+        __syncwarp();
+        while (last) {
+          const int src = __ffs(last) - 1;
+          last &= last - 1;
+          finish_token_slice(comb, static_cast<const float*>(yout), __shfl_sync(0xffffffffu, lt, src),
+                             ti.col, lane);
         }
       }
+      quarter_sync(q);  // staging rows read before the next tile overwrites them
     }
   }
 
