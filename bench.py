@@ -753,6 +753,7 @@ def cpu_leg(fmt, T, args, raw_dev):
 # and workload exists.
 NCU_TRAFFIC = {
     ("bq-decode-b64", "bq_phase1_gate_up"): 505_800_000 + 500_000,
+    ("bq-prefill-4k-zipf", "bq_phase2_down.tc"): 280_055_808 + 353_800_192,
     ("bf16-prefill-4k", "phase1_gate_up.tc"): 1_229_532_000 + 45_981_184,
 }
 
@@ -766,14 +767,12 @@ def stage_model(label, fmt, T, distinct, R):
     ksplit = H // 256
     if label == "bq_phase1_gate_up":
         return "hbm", distinct * BQ_EXPERT_GU_BYTES + R * (H + 4) // TOPK + R * (I + 11 * 4)
-    if label in ("bq_phase2_down", "bq_phase2_down.p2p"):  # + the fused combine's bf16 rows
-        return "hbm", distinct * BQ_EXPERT_DN_BYTES + R * (I + 11 * 4) + (R // TOPK) * H * 2
+    if label == "bq_phase2_down":
+        return "hbm", distinct * BQ_EXPERT_DN_BYTES + R * (I + 11 * 4) + R * H * 4
     if label == "bq_phase1_gate_up.tc":
         return "tensor", 2.0 * R * GU * H
-    if label in ("bq_phase2_down.tc", "bq_phase2_down.tc.p2p"):  # + the fused combine
+    if label == "bq_phase2_down.tc":
         return "tensor", 2.0 * R * H * I
-    if label == "post_tail":
-        return "hbm", T * H * 2 * 5 + 3 * H * 2
     if label == "phase1_gate_up.tc":
         return "tensor", 2.0 * R * GU * H
     if label == "phase2_down.tc":

@@ -101,25 +101,6 @@ combine_post_kernel(const int32_t* __restrict__ route_idx, const int32_t* __rest
   post_moe_row(m, t, p, red);
 }
 
-// The post-MoE tail over finished bf16 MoE rows (the fused combine of the
-// tcgen05 down product wrote them).
-__global__ void __launch_bounds__(POST_THREADS)
-post_tail_kernel(const uint16_t* __restrict__ moe, int T, PostParams p) {
-  __shared__ float red[POST_THREADS / 32];
-  pdl_wait();
-  pdl_trigger();
-  const int t = blockIdx.x;
-  float m[8];
-  load_bf16x4(moe + (size_t)t * H + 4 * threadIdx.x, *reinterpret_cast<float(*)[4]>(m));
-  load_bf16x4(moe + (size_t)t * H + 4 * (threadIdx.x + POST_THREADS), *reinterpret_cast<float(*)[4]>(m + 4));
-  post_moe_row(m, t, p, red);
-}
-
-cudaError_t launch_post_tail(const uint16_t* moe, int T, const PostParams& p, cudaStream_t s) {
-  if (T <= 0) return cudaSuccess;
-  return launch_k(post_tail_kernel, dim3(T), dim3(POST_THREADS), 0, s, moe, T, p);
-}
-
 cudaError_t launch_combine_post(const int32_t* route_idx, const int32_t* route_pos, const float* ybuf,
                                 int T, const PostParams& p, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;

@@ -30,11 +30,8 @@
 // holds the 64 gate and 64 up outputs of one FWHT-64 block for every route, so
 // GeGLU, the bf16 rounding of the bucket, FWHT-64 and the per-block int8
 // quantisation run in registers and only bucket_i8/bucket_sa reach HBM.
-// Phase 2 writes per-route f32 rows y = facc*sw*w; in the forward the token's
-// last route sums them in ascending expert order (the reference's
-// accumulation order) inside the same kernel, otherwise combine.cu does.
-#include "combine_dev.cuh"
-#include "ep_dev.cuh"
+// Phase 2 writes per-route f32 rows y = facc*sw*w; combine.cu sums them per
+// token in ascending expert order (the reference's accumulation order).
 #include "gm_kernels.h"
 #include "vnni_stream.cuh"
 
@@ -244,12 +241,6 @@ bq_phase1_kernel(const int8_t* __restrict__ xi8, const float* __restrict__ xsa,
   }
 }
 
-// The weighted combine is fused into the decode down product (comb.counts
-// non-null): a work item's routes have just stored their slices of hidden
-// columns [128*blk, 128*blk+128) (f32, L2); one thread per route bumps the
-// (token, column group) arrival counter, and the CTA then finishes every
-// token whose last route this was (finish_token_slice, combine_dev.cuh) --
-// the same counters and sum as the tcgen05 kernel's combine (gemm_tc.cu).
 // `prologue_prefetch`: the schedule (two launches back) is complete when the
 // kernel starts, so the first weight chunks are issued before waiting for
 // phase 1's bucket.  Only the fused forward sets it (it always runs phase 1
@@ -260,15 +251,12 @@ bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
                  const int32_t* __restrict__ expert_offset, const SparseRoute* __restrict__ routes,
                  const int32_t* __restrict__ chunk_off, int epr,
                  const int8_t* __restrict__ w_dn, const float* __restrict__ dn_scale,
-                 float* __restrict__ ybuf, int prologue_prefetch, const __grid_constant__ TcCombine comb) {
+                 float* __restrict__ ybuf, int prologue_prefetch) {
   constexpr int GROUPS = (H / 32) / NTILE;  // hidden tile groups per expert
   constexpr int KCH = I / 32;               // 22 K chunks, 2 per K-block
-  static_assert(GROUPS == TC_COLS2, "one arrival counter per 128-column group");
   __shared__ __align__(16) int8_t xs[RC_BQ * BSTRIDE];
   __shared__ float s_adv[RC_BQ * NB_DOWN];
   __shared__ float s_w[RC_BQ];
-  __shared__ int s_tok[RC_BQ];
-  __shared__ int s_last[RC_BQ];
 
   if (!prologue_prefetch) pdl_wait();
   const int total = __ldg(chunk_off + epr) * GROUPS;
@@ -284,8 +272,9 @@ bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
   }
   if (prologue_prefetch) pdl_wait();
   pdl_trigger();
+  if (!any) return;
 
-  while (any) {
+  while (true) {
     const int nr = cur.nr, rbeg = cur.rbeg;
     const int tile = cur.blk * NTILE + warp;
     const int8_t* wt = w_dn + (size_t)cur.e * H * I + (size_t)tile * 32 * I;
@@ -297,11 +286,7 @@ bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
     }
     for (int i = tid; i < nr * NB_DOWN; i += blockDim.x)
       s_adv[i] = __fmul_rn(bsa[(size_t)rbeg * NB_DOWN + i], INV127);
-    if (tid < nr) {
-      const SparseRoute rt = routes[rbeg + tid];
-      s_w[tid] = rt.weight;
-      s_tok[tid] = rt.token;
-    }
+    if (tid < nr) s_w[tid] = routes[rbeg + tid].weight;
     cp_async_wait_all();
     __syncthreads();
 
@@ -381,37 +366,15 @@ bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
           o.y = __fmul_rn(__fmul_rn(facc[a][0][2 + h], sw[1]), wr);
           o.z = __fmul_rn(__fmul_rn(facc[a][1][h], sw[2]), wr);
           o.w = __fmul_rn(__fmul_rn(facc[a][1][2 + h], sw[3]), wr);
-          __stcg(reinterpret_cast<float4*>(ybuf + (size_t)(rbeg + r) * H + tile * 32 + rbase), o);
+          *reinterpret_cast<float4*>(ybuf + (size_t)(rbeg + r) * H + tile * 32 + rbase) = o;
         }
       }
     }
     __syncthreads();
-    if (comb.counts) {
-      // one arrival per route of the item; then the CTA finishes the tokens
-      // whose last route this was, one warp per token
-      if (tid < nr) {
-        const int tok = s_tok[tid];
-        const int4 p0 = __ldg(reinterpret_cast<const int4*>(comb.route_pos) + 2 * tok);
-        const int4 p1 = __ldg(reinterpret_cast<const int4*>(comb.route_pos) + 2 * tok + 1);
-        const int nloc = (p0.x >= 0) + (p0.y >= 0) + (p0.z >= 0) + (p0.w >= 0) + (p1.x >= 0) +
-                         (p1.y >= 0) + (p1.z >= 0) + (p1.w >= 0);
-        __threadfence();  // the item's slices (stored before the barrier), before the arrival
-        const int old = atomicAdd(comb.counts + (size_t)tok * TC_COLS2 + cur.blk, 1);
-        if (old == nloc - 1) __threadfence();
-        s_last[tid] = old == nloc - 1 ? tok : -1;
-      }
-      __syncthreads();
-      for (int r = warp; r < nr; r += NTILE)
-        if (s_last[r] >= 0) finish_token_slice(comb, ybuf, s_last[r], cur.blk, lane);
-      __syncthreads();
-    }
     if (!has_next) break;
     cur = nxt;
     task += gridDim.x;
   }
-  // expert parallel: the partial rows went straight into the sources' memory;
-  // the last CTA to finish tells every source
-  if (comb.done_counter) publish_when_last(comb.done_counter, comb.cflag, comb.G, comb.my_rank, comb.epoch);
 }
 
 static size_t phase1_smem(int ksplit) {
@@ -485,20 +448,19 @@ cudaError_t launch_bq_phase1(const int8_t* xi8, const float* xsa, const int32_t*
 cudaError_t launch_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t* expert_offset,
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_dn, const float* dn_scale, float* ybuf,
-                             bool after_phase1, cudaStream_t s, const TcCombine* comb) {
+                             bool after_phase1, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   constexpr int NTILE = 4, DEPTH = 4;
   const int items = max_route_chunks(T, epr, RC_BQ) * ((H / 32) / NTILE);
   auto k = bq_phase2_kernel<NTILE, DEPTH>;
   const int grid = resident_grid(k, 32 * NTILE, 0, items);
-  const TcCombine c = comb ? *comb : TcCombine{};
   if (after_phase1)
     return launch_k(k, dim3(grid), dim3(32 * NTILE), 0, s, bi8, bsa, expert_offset, routes,
-                    chunk_off, epr, w_dn, dn_scale, ybuf, 1, c);
+                    chunk_off, epr, w_dn, dn_scale, ybuf, 1);
   // standalone: an ordinary stream-ordered launch (the prologue may then read
   // the schedule before any wait)
   k<<<grid, 32 * NTILE, 0, s>>>(bi8, bsa, expert_offset, routes, chunk_off, epr, w_dn, dn_scale,
-                                ybuf, 0, c);
+                                ybuf, 0);
   return cudaGetLastError();
 }
 

@@ -32,8 +32,6 @@
 // barrier and frees its TMEM.
 #include <cuda.h>
 
-#include "combine_dev.cuh"
-#include "ep_dev.cuh"
 #include "gm_kernels.h"
 #include "tc_prims.cuh"
 
@@ -85,7 +83,6 @@ struct Smem2 {
   uint64_t reg_empty[RING];
   uint32_t tmem_base;
   int failed;
-  int row_tok[BM];   // fused combine: token of each tile row (-1 past the routes)
   TileTable tt;
 };
 
@@ -341,33 +338,15 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   if (tid == 0 && s.failed) atomicExch(err, ERR_TIMEOUT);
 }
 
-// Phase 2: the down product with the reference's per-64-K-block fma chain,
-// followed (MoE) by the fused weighted combine or (DENSE) by the dense MLP's
-// bf16 output rows.
-//
-// Tiles are walked column-major (tile_info_colmajor): all m-tiles of hidden
-// columns [128c, 128c+128) before column c+1.  Epilogue warp (q, cb) owns
-// TMEM lanes 32q..32q+31 (one route row per thread) and columns 32cb..32cb+31
-// of the tile; the tile's outputs are staged in shared memory and written as
-// whole 128-column rows, 8 rows per warp.
-//
-// Fused combine (MoE): the rows are the routes' weighted outputs
-// y = facc*sw*w_route (f32).  After storing its 8 rows a warp bumps each
-// row's (token, column tile) arrival counter; the row that brings it to the
-// token's number of local routes is the token's last, and the warp finishes
-// that token's 128 columns (finish_token_slice: the <= 8 slices summed in
-// ascending expert order from 0.0f, bf16) into the output or, expert-
-// parallel, into the source rank's contribution block in peer memory.
-// Column-major order keeps a column's slices L2-resident between their store
-// and that read.
+// DENSE: the dense MLP's down product (K = 2112, 33 blocks) over dense_rows
+// token rows in order, out = bf16(facc * sw) into a bf16 [rows][2816] `yout`.
 template <bool DENSE>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                  const int32_t* __restrict__ expert_offset, int epr, int dense_rows,
                  const float* __restrict__ bsa, const SparseRoute* __restrict__ routes,
                  const float* __restrict__ dn_scale, void* __restrict__ yout,
-                 const __grid_constant__ TcCombine comb, int* __restrict__ err, int max_rows,
-                 int max_tiles) {
+                 int* __restrict__ err, int max_rows, int max_tiles) {
   constexpr int KW = DENSE ? DENSE_I : I;   // K bytes per row
   constexpr int NB = KW / 64;               // dequantisation blocks
   constexpr int KC = (KW + BK - 1) / BK;    // K stages (last half zero-filled)
@@ -423,7 +402,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
-        const TileInfo ti = tile_info_colmajor(s.tt, epr, t);
+        const TileInfo ti = tile_info(s.tt, epr, NT2, t);
         for (int c = 0; c < KC; ++c) {
           if (!mbar_wait<false>(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done2;
           uint8_t* st = s.stage[stage];
@@ -474,7 +453,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     int reg = 0;
     uint32_t rphase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const TileInfo ti = tile_info_colmajor(s.tt, epr, t);
+      const TileInfo ti = tile_info(s.tt, epr, NT2, t);
       const bool valid = r < ti.nvalid;
       const bool quarter_live = q * 32 < ti.nvalid;  // warp-uniform
       const int row = ti.row0 + r;
@@ -487,8 +466,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         for (int b = 0; b < NB; ++b)
           adv[b] = valid ? __fmul_rn(bsa[(size_t)row * NB + b], inv127) : 0.0f;
       }
-      SparseRoute rt = {-1, 0.0f};
-      if (!DENSE && valid) rt = routes[row];
+      const float wr = (!DENSE && valid) ? routes[row].weight : 0.0f;
       const float* wsc = dn_scale + (size_t)ti.e * H + ti.col * BN + 32 * cb;
       float2 facc[16];
 #pragma unroll
@@ -520,7 +498,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       }
       // y = facc * sw * w_route (dense: facc * sw), staged per row then
       // written as whole rows
-      const float2 wr2 = make_float2(rt.weight, rt.weight);
+      const float2 wr2 = make_float2(wr, wr);
       float4* ys = reinterpret_cast<float4*>(&s.ystage[r][32 * cb]);
 #pragma unroll
       for (int v = 0; v < 8; ++v) {
@@ -533,10 +511,8 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         }
         ys[v] = make_float4(lo.x, lo.y, hi.x, hi.y);
       }
-      if (!DENSE && cb == 0) s.row_tok[r] = rt.token;
       quarter_sync(q);
-      // the 4 warps of quarter q write its 32 rows: 8 rows each, one whole row
-      // (128 columns) per warp store
+      // the 4 warps of quarter q write its 32 rows: 8 rows each, one whole row per warp store
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int rr = q * 32 + cb * 8 + j;
@@ -548,39 +524,9 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             reinterpret_cast<uint2*>(static_cast<uint16_t*>(yout) + (size_t)(ti.row0 + rr) * H +
                                      ti.col * BN)[lane] = o;
           } else {
-            __stcg(reinterpret_cast<float4*>(static_cast<float*>(yout) + (size_t)(ti.row0 + rr) * H +
-                                             ti.col * BN) + lane, v);
+            reinterpret_cast<float4*>(static_cast<float*>(yout) + (size_t)(ti.row0 + rr) * H +
+                                      ti.col * BN)[lane] = v;
           }
-        }
-      }
-      if constexpr (!DENSE) {
-        // Fused combine: this warp's 8 rows are stored; one arrival per row
-        // on its (token, column tile) counter.  The warp then finishes every
-        // token whose last route one of these rows was.
-        __syncwarp();  // the lanes' row stores are ordered before the arrivals
-        int lt = -1;
-        if (lane < 8) {
-          const int rr = q * 32 + cb * 8 + lane;
-          const int tok = rr < ti.nvalid ? s.row_tok[rr] : -1;
-          if (tok >= 0) {
-            const int4 p0 = __ldg(reinterpret_cast<const int4*>(comb.route_pos) + 2 * tok);
-            const int4 p1 = __ldg(reinterpret_cast<const int4*>(comb.route_pos) + 2 * tok + 1);
-            const int nloc = (p0.x >= 0) + (p0.y >= 0) + (p0.z >= 0) + (p0.w >= 0) + (p1.x >= 0) +
-                             (p1.y >= 0) + (p1.z >= 0) + (p1.w >= 0);
-            __threadfence();
-            if (atomicAdd(comb.counts + (size_t)tok * NT2 + ti.col, 1) == nloc - 1) {
-              __threadfence();  // every other route's slice, before the re-read
-              lt = tok;
-            }
-          }
-        }
-        unsigned last = __ballot_sync(0xffffffffu, lt >= 0);
-        __syncwarp();
-        while (last) {
-          const int src = __ffs(last) - 1;
-          last &= last - 1;
-          finish_token_slice(comb, static_cast<const float*>(yout), __shfl_sync(0xffffffffu, lt, src),
-                             ti.col, lane);
         }
       }
       quarter_sync(q);  // staging rows read before the next tile overwrites them
@@ -594,9 +540,6 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS2));
   }
   if (tid == 0 && s.failed) atomicExch(err, ERR_TIMEOUT);
-  // expert parallel: the partial rows went straight into the sources' memory;
-  // the last CTA to finish tells every source
-  if (!DENSE && comb.done_counter) publish_when_last(comb.done_counter, comb.cflag, comb.G, comb.my_rank, comb.epoch);
 }
 
 // xg[pos] = x_i8[routes[pos].token], xg_sa[pos] = x_sa[token]: the routed
@@ -716,8 +659,7 @@ cudaError_t launch_tc_dense_gate_up(const void* map_x, const void* map_w, int T,
 
 cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
                              int epr, int T, const float* bsa, const SparseRoute* routes,
-                             const float* dn_scale, float* ybuf, const TcCombine& comb, int* err,
-                             cudaStream_t s) {
+                             const float* dn_scale, float* ybuf, int* err, cudaStream_t s) {
   const int max_rows = T * TOPK;
   const int max_tiles = (max_rows / tc::BM + epr) * tc::NT2;
   const size_t smem = sizeof(tc::Smem2) + 1024;
@@ -727,7 +669,7 @@ cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t
   return launch_k(k, dim3(sm_count()), dim3(tc::THREADS), smem, s,
                   *reinterpret_cast<const CUtensorMap*>(map_a),
                   *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, 0, bsa, routes,
-                  dn_scale, static_cast<void*>(ybuf), comb, err, max_rows, max_tiles);
+                  dn_scale, static_cast<void*>(ybuf), err, max_rows, max_tiles);
 }
 
 cudaError_t launch_tc_dense_down(const void* map_h, const void* map_w, int T, const float* hsa,
@@ -741,7 +683,7 @@ cudaError_t launch_tc_dense_down(const void* map_h, const void* map_w, int T, co
   return launch_k(k, dim3(std::min(sm_count(), tiles)), dim3(tc::THREADS), smem, s,
                   *reinterpret_cast<const CUtensorMap*>(map_h),
                   *reinterpret_cast<const CUtensorMap*>(map_w), nullptr, 1, T, hsa, nullptr, dn_scale,
-                  static_cast<void*>(out), TcCombine{}, err, T, tiles);
+                  static_cast<void*>(out), err, T, tiles);
 }
 
 }  // namespace gm

@@ -93,7 +93,6 @@ struct gm_moe {
   int* dev_err = nullptr;       // device-side error word (bounded waits that expired)
   int32_t* sched_counts = nullptr;  // per-chunk expert counts of the multi-CTA schedule
   int* router_counts = nullptr;     // router tile counters (zero between calls)
-  int* comb_counts = nullptr;       // arrival counters of the fused combine [rows][H/128] (zero between calls)
   alignas(64) unsigned char tmap_xg[128] = {};
   alignas(64) unsigned char tmap_bucket[128] = {};
   alignas(64) unsigned char tmap_xgb[128] = {};      // bf16 gathered rows (in ybuf's memory)
@@ -224,7 +223,7 @@ struct Carve {
 struct WsLayout {
   size_t logits, inv_rms, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
       x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, xg, xg_sa, dev_err,
-      sched_counts, router_counts, comb_counts, d_xi8, d_xsa, d_inv, d_hi8, d_hsa, d_out, total;
+      sched_counts, router_counts, d_xi8, d_xsa, d_inv, d_hi8, d_hsa, d_out, total;
 };
 
 WsLayout ws_layout(int max_tokens) {
@@ -255,7 +254,6 @@ WsLayout ws_layout(int max_tokens) {
   L.dev_err = c.take<int>(1);
   L.sched_counts = c.take<int32_t>(schedule_counts_ints(max_tokens));
   L.router_counts = c.take<int>(router_tile_counters(max_tokens));
-  L.comb_counts = c.take<int>(T * TC_COLS2);
   L.d_xi8 = c.take<int8_t>(T * H);
   L.d_xsa = c.take<float>(T);
   L.d_inv = c.take<float>(T);
@@ -363,7 +361,6 @@ int carve_workspace(gm_moe* h, int tokens) {
   h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
   h->sched_counts = reinterpret_cast<int32_t*>(b + L.sched_counts);
   h->router_counts = reinterpret_cast<int*>(b + L.router_counts);
-  h->comb_counts = reinterpret_cast<int*>(b + L.comb_counts);
   h->d_xi8 = reinterpret_cast<int8_t*>(b + L.d_xi8);
   h->d_xsa = reinterpret_cast<float*>(b + L.d_xsa);
   h->d_inv = reinterpret_cast<float*>(b + L.d_inv);
@@ -374,7 +371,6 @@ int carve_workspace(gm_moe* h, int tokens) {
                    make_tmap_i8(h->tmap_dh, h->d_hi8, (long)tokens, DENSE_I, 128);
   cudaMemset(h->dev_err, 0, sizeof(int));
   cudaMemset(h->router_counts, 0, sizeof(int) * router_tile_counters(tokens));
-  cudaMemset(h->comb_counts, 0, sizeof(int) * (size_t)tokens * TC_COLS2);
   h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)tokens * TOPK, H, 128) &&
              make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)tokens * TOPK, I, 128);
   // bf16 prefill: the gathered activation rows live in ybuf, which is idle
@@ -578,29 +574,6 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
                         const uint16_t* x_normed, const int32_t* route_idx, const CombineTarget& ct,
                         cudaStream_t s) {
   if (L.kind == 1) {
-    // butterquant: the down product's epilogue finishes each token's row
-    // (fused weighted combine), on the tcgen05 kernel and on the decode kernel
-    TcCombine c;
-    c.route_idx = route_idx;
-    c.route_pos = h->route_pos;
-    c.counts = h->comb_counts;
-    if (ct.peers) {
-      for (int q = 0; q < h->degree; ++q) {
-        c.contrib[q] = ct.peers->contrib[q];
-        c.cflag[q] = ct.peers->cflag[q];
-      }
-      c.cap = h->max_tokens;
-      c.my_rank = h->rank;
-      c.G = h->degree;
-      c.epoch = ct.epoch;
-      c.done_counter = h->ep_counters + 1;
-    } else {
-      c.out = ct.post ? h->out_stage : ct.out;
-      // a partial handle (degree > 1, no exchange) outputs zero for tokens
-      // with no route here; the fused combine writes only routed tokens
-      if (h->degree > 1 && !h->ep_on)
-        GM_TRY(h, cudaMemsetAsync(c.out, 0, (size_t)Tn * H * sizeof(uint16_t), s), "partial rows");
-    }
     if (L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
       // prefill: routed rows gathered in schedule order, then the tcgen05 GEMMs
       GM_STAGE(h, s, launch_gather_rows(x_i8, H, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
@@ -610,23 +583,17 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
                                       L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
                "bq_phase1_gate_up.tc");
       GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, Tn,
-                                      h->bucket_sa, h->routes, L.dn_scale, h->ybuf, c, h->dev_err, s),
-               ct.peers ? "bq_phase2_down.tc.p2p" : "bq_phase2_down.tc");
+                                      h->bucket_sa, h->routes, L.dn_scale, h->ybuf, h->dev_err, s),
+               "bq_phase2_down.tc");
     } else {
       GM_STAGE(h, s, launch_bq_phase1(x_i8, x_sa, h->expert_offset, h->routes, h->chunk_off, h->epr,
                                       Tn, L.gu_q, L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, s),
                "bq_phase1_gate_up");
       GM_STAGE(h, s, launch_bq_phase2(h->bucket_i8, h->bucket_sa, h->expert_offset, h->routes,
-                                      h->chunk_off, h->epr, Tn, L.dn_q, L.dn_scale, h->ybuf, true, s, &c),
-               ct.peers ? "bq_phase2_down.p2p" : "bq_phase2_down");
+                                      h->chunk_off, h->epr, Tn, L.dn_q, L.dn_scale, h->ybuf, true, s),
+               "bq_phase2_down");
     }
-    if (ct.post) {
-      if (join_dense(h, s)) return GM_ECUDA;
-      GM_STAGE(h, s, launch_post_tail(h->out_stage, Tn, *ct.post, s), "post_tail");
-    }
-    return GM_OK;
-  }
-  if (L.has_tc && h->tcb_ok && Tn >= h->tc_min_tokens) {
+  } else if (L.has_tc && h->tcb_ok && Tn >= h->tc_min_tokens) {
     GM_STAGE(h, s, launch_gather_rows(x_normed, 2 * H, nullptr, h->routes, h->expert_offset, h->epr, Tn,
                                       h->ybuf, nullptr, s),
              "gather_rows");
@@ -1649,7 +1616,6 @@ int gm_moe_device_status(gm_moe_t* h, int* device_error) {
   if (*device_error) {
     // a kernel that gave up may have left self-re-arming counters mid-count
     cudaMemset(h->router_counts, 0, sizeof(int) * router_tile_counters(h->ws_tokens));
-    cudaMemset(h->comb_counts, 0, sizeof(int) * (size_t)h->ws_tokens * TC_COLS2);
     if (h->ep_counters) cudaMemset(h->ep_counters, 0, 2 * sizeof(int));
     cudaDeviceSynchronize();
     return set_err(h, GM_ETIMEOUT, "a kernel's bounded wait expired (code %d)", *device_error);

@@ -106,13 +106,10 @@ cudaError_t launch_dense_down(const int8_t* hi8, const float* hsa, int T, const 
                               const float* dsc, uint16_t* out, cudaStream_t s);
 // bulk L2 prefetch of [base, base + bytes) (16-byte aligned base)
 cudaError_t launch_l2_prefetch(const void* base, size_t bytes, cudaStream_t s);
-struct TcCombine;
-// comb (may be null): the fused weighted combine of the tcgen05 kernel
-// (TcCombine below), on the decode kernel's 128-column groups
 cudaError_t launch_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t* expert_offset,
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_dn, const float* dn_scale, float* ybuf,
-                             bool after_phase1, cudaStream_t s, const TcCombine* comb = nullptr);
+                             bool after_phase1, cudaStream_t s);
 cudaError_t launch_bf16_phase1(const uint16_t* xn, const int32_t* expert_offset,
                                const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                                const uint16_t* w_gu, uint16_t* bucket, cudaStream_t s);
@@ -139,32 +136,9 @@ cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t
                              int epr, int T, const float* xg_sa, const float* gu_scale,
                              int8_t* bucket_i8, float* bucket_sa, uint16_t* bucket_bf16, int* err,
                              cudaStream_t s);
-// Where the tcgen05 down product's fused combine puts each token's finished
-// row (bf16, the reference's expert-ordered f32 sum): `out` [rows][H] on this
-// GPU, or -- expert parallelism over peer memory -- received row r's partial
-// into contrib[r / cap] at row my_rank*cap + r % cap, after which the last CTA
-// publishes cflag[d][my_rank] = epoch on every rank d.  counts: arrival
-// counters [rows][H/128] (zero between calls; the kernel re-arms them).
-struct TcCombine {
-  const int32_t* route_idx = nullptr;  // [rows][8]
-  const int32_t* route_pos = nullptr;  // [rows][8] schedule position, -1 if not local
-  int* counts = nullptr;
-  uint16_t* out = nullptr;
-  uint16_t* contrib[8] = {};
-  uint32_t* cflag[8] = {};
-  int cap = 0, my_rank = 0, G = 0;
-  uint32_t epoch = 0;
-  int* done_counter = nullptr;
-};
-constexpr int TC_COLS2 = H / 128;  // column slices of the down product (counters per row)
-// Down product + fused combine: ybuf [rows][H] f32 holds each route's
-// weighted output slice until its token's last route sums them.
 cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
                              int epr, int T, const float* bsa, const SparseRoute* routes,
-                             const float* dn_scale, float* ybuf, const TcCombine& comb, int* err,
-                             cudaStream_t s);
-// The post-MoE tail (post_moe.cuh) over finished bf16 MoE rows.
-cudaError_t launch_post_tail(const uint16_t* moe, int T, const PostParams& p, cudaStream_t s);
+                             const float* dn_scale, float* ybuf, int* err, cudaStream_t s);
 // butterquant attention (attention_bq.cu).  runs: device array of
 // {buf_start, base_pos, rows_off, page_count} (gm_kv_run_t)
 cudaError_t launch_attn_prep(const uint16_t* q_src, const uint16_t* k_src, const uint16_t* v_src,

@@ -190,26 +190,6 @@ __device__ __forceinline__ TileInfo tile_info(const TileTable& tt, int epr, int 
   return ti;
 }
 
-// Column-major order: tile t = (column tile t / M, m-tile t % M) with M the
-// total m-tiles, so that the CTAs of a persistent grid work through one
-// column slice of every route before the next (the slice's outputs are then
-// produced within a short window).
-__device__ __forceinline__ TileInfo tile_info_colmajor(const TileTable& tt, int epr, int t) {
-  const int mtiles = tt.moff[epr];
-  const int mg = t % mtiles;
-  TileInfo ti;
-  ti.col = t / mtiles;
-  int lo = 0, hi = epr;
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (tt.moff[mid] <= mg) lo = mid; else hi = mid;
-  }
-  ti.e = lo;
-  ti.row0 = tt.eoff[lo] + (mg - tt.moff[lo]) * TILE_M;
-  ti.nvalid = min(TILE_M, tt.eoff[lo + 1] - ti.row0);
-  return ti;
-}
-
 // m-tile prefix over this rank's experts (one warp, 4 experts per lane).
 __device__ __forceinline__ void build_tile_table(TileTable& tt, const int32_t* expert_offset, int epr,
                                                  int lane) {

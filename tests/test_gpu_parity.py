@@ -415,9 +415,7 @@ def test_forward_ffn_post_moe_tail(T, layer_stress):
     stats, _ = blk.profile_read()
     torch.cuda.synchronize()
     assert blk.device_status() == 0
-    # the down product finishes each token's row (fused combine); the tail
-    # kernel follows it
-    assert "post_tail" in stats and "combine" not in stats and "combine.post" not in stats
+    assert "combine.post" in stats and "combine" not in stats
     want = O.post_moe(host(moe), dense_np, x_np, w1, w2, w, 0.875)
     got = host(x_main)
     assert rel_err(got, want) < 1e-2
@@ -500,21 +498,20 @@ def test_stage_profiler_labels_and_launch_count(layer_stress):
     stats, launches = blk.profile_read()
     # decode batches (32 <= T < 1024) also launch an L2 prefetch on a side
     # stream (counted as a launch, not a stage of the forward's stream)
-    # the down products finish each token's row themselves (fused weighted
-    # combine): no combine stage
     assert list(stats) == ["bq_norm_quant", "router_expert", "router_merge.schedule",
-                           "bq_phase1_gate_up", "bq_phase2_down", "gather_rows",
+                           "bq_phase1_gate_up", "bq_phase2_down", "combine", "gather_rows",
                            "bq_phase1_gate_up.tc", "bq_phase2_down.tc"]
     assert stats["bq_phase1_gate_up"]["calls"] == 2 and stats["bq_phase1_gate_up.tc"]["calls"] == 1
+    assert stats["combine"]["calls"] == 3
     # 32 < T <= 1024: top-8 over T/4 CTAs, then the one-CTA schedule;
     # T > 1024: top-8, count, scatter
     assert stats["router_merge.schedule"]["kernels"] == 2 * 2 + 3
-    assert launches == 2 * 7 + 8
+    assert launches == 2 * 8 + 9
     for v in stats.values():
         assert 0 < v["min_ms"] <= v["avg_ms"] <= v["max_ms"] < 1e3
     # profiling off: launches still counted, no new stage records
     blk.profile(False)
     blk.forward(0, dev(tokens_np(64, seed=1)), out, 64)
     stats, launches = blk.profile_read()
-    assert stats == {} and launches == 7
+    assert stats == {} and launches == 8
     blk.close()
