@@ -7,6 +7,7 @@
 // this kernel re-creates exactly that summation order per token: the token's
 // <=8 local routes are sorted by expert id and added left to right starting
 // from 0.0f, then rounded to bf16 with RNE (butterquant/convert.mojo:13-17).
+#include "combine_dev.cuh"
 #include "gm_kernels.h"
 #include "post_moe.cuh"
 
@@ -15,38 +16,15 @@ namespace gm {
 __global__ void __launch_bounds__(352)
 combine_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict__ route_pos,
                const float* __restrict__ ybuf, int T, uint16_t* __restrict__ out) {
-  __shared__ int s_pos[TOPK];
-  __shared__ int s_n;
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
-  if (threadIdx.x == 0) {
-    int ex[TOPK], ps[TOPK], n = 0;
-    for (int k = 0; k < TOPK; ++k) {
-      const int p = route_pos[t * TOPK + k];
-      if (p < 0) continue;
-      const int e = route_idx[t * TOPK + k];
-      int m = n++;
-      while (m > 0 && ex[m - 1] > e) { ex[m] = ex[m - 1]; ps[m] = ps[m - 1]; --m; }
-      ex[m] = e;
-      ps[m] = p;
-    }
-    for (int k = 0; k < n; ++k) s_pos[k] = ps[k];
-    s_n = n;
-  }
-  __syncthreads();
-  const int n = s_n;
+  int pos[TOPK];
+  routes_by_expert(route_idx, route_pos, t, pos);
   // gridDim.y CTAs share the token's row (column slices)
   const int per = (H / 4) / gridDim.y;
   for (int c4 = blockIdx.y * per + threadIdx.x; c4 < (blockIdx.y + 1) * per; c4 += blockDim.x) {
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int k = 0; k < n; ++k) {
-      const float4 y = *reinterpret_cast<const float4*>(ybuf + (size_t)s_pos[k] * H + c4 * 4);
-      acc.x = __fadd_rn(acc.x, y.x);
-      acc.y = __fadd_rn(acc.y, y.y);
-      acc.z = __fadd_rn(acc.z, y.z);
-      acc.w = __fadd_rn(acc.w, y.w);
-    }
+    const float4 acc = sum_routes4(ybuf, pos, c4);
     uint2 o;
     o.x = (uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16);
     o.y = (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16);
@@ -59,40 +37,16 @@ combine_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict_
 __global__ void __launch_bounds__(POST_THREADS)
 combine_post_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict__ route_pos,
                     const float* __restrict__ ybuf, int T, PostParams p) {
-  __shared__ int s_pos[TOPK];
-  __shared__ int s_n;
   __shared__ float red[POST_THREADS / 32];
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
-  if (threadIdx.x == 0) {
-    int ex[TOPK], ps[TOPK], n = 0;
-    for (int k = 0; k < TOPK; ++k) {
-      const int q = route_pos[t * TOPK + k];
-      if (q < 0) continue;
-      const int e = route_idx[t * TOPK + k];
-      int j = n++;
-      while (j > 0 && ex[j - 1] > e) { ex[j] = ex[j - 1]; ps[j] = ps[j - 1]; --j; }
-      ex[j] = e;
-      ps[j] = q;
-    }
-    for (int k = 0; k < n; ++k) s_pos[k] = ps[k];
-    s_n = n;
-  }
-  __syncthreads();
-  const int n = s_n;
+  int pos[TOPK];
+  routes_by_expert(route_idx, route_pos, t, pos);
   float m[8];
 #pragma unroll
   for (int g = 0; g < 2; ++g) {
-    const int c4 = threadIdx.x + g * POST_THREADS;
-    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int k = 0; k < n; ++k) {
-      const float4 y = *reinterpret_cast<const float4*>(ybuf + (size_t)s_pos[k] * H + c4 * 4);
-      acc.x = __fadd_rn(acc.x, y.x);
-      acc.y = __fadd_rn(acc.y, y.y);
-      acc.z = __fadd_rn(acc.z, y.z);
-      acc.w = __fadd_rn(acc.w, y.w);
-    }
+    const float4 acc = sum_routes4(ybuf, pos, threadIdx.x + g * POST_THREADS);
     m[4 * g] = bf2f(f2bf(acc.x));
     m[4 * g + 1] = bf2f(f2bf(acc.y));
     m[4 * g + 2] = bf2f(f2bf(acc.z));

@@ -32,6 +32,7 @@
 #include <mutex>
 #include <string>
 
+#include "combine_dev.cuh"
 #include "ep.h"
 #include "ep_dev.cuh"
 #include "post_moe.cuh"
@@ -320,46 +321,21 @@ __global__ void __launch_bounds__(352)
 combine_p2p_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict__ route_pos,
                    const float* __restrict__ ybuf, int n, int cap, EpPeers peers, int G, int my_rank,
                    uint32_t epoch, int* __restrict__ done_counter) {
-  __shared__ int s_pos[TOPK];
-  __shared__ int s_n;
   pdl_wait();
   pdl_trigger();
   for (int r = blockIdx.x; r < n; r += gridDim.x) {
-    if (threadIdx.x == 0) {
-      int ex[TOPK], ps[TOPK], m = 0;
-      for (int k = 0; k < TOPK; ++k) {
-        const int q = route_pos[(size_t)r * TOPK + k];
-        if (q < 0) continue;
-        const int e = route_idx[(size_t)r * TOPK + k];
-        int j = m++;
-        while (j > 0 && ex[j - 1] > e) { ex[j] = ex[j - 1]; ps[j] = ps[j - 1]; --j; }
-        ex[j] = e;
-        ps[j] = q;
-      }
-      for (int k = 0; k < m; ++k) s_pos[k] = ps[k];
-      s_n = m;
+    int pos[TOPK];
+    routes_by_expert(route_idx, route_pos, r, pos);
+    if (pos[0] < 0) continue;  // rows with no route here were never sent (or are unused)
+    const int src = r / cap;
+    uint16_t* dst = peers.contrib[src] + ((size_t)my_rank * cap + (r % cap)) * H;
+    for (int c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
+      const float4 acc = sum_routes4(ybuf, pos, c4);
+      uint2 o;
+      o.x = (uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16);
+      o.y = (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16);
+      *reinterpret_cast<uint2*>(dst + c4 * 4) = o;
     }
-    __syncthreads();
-    const int m = s_n;
-    if (m > 0) {  // rows with no route here were never sent (or are unused)
-      const int src = r / cap;
-      uint16_t* dst = peers.contrib[src] + ((size_t)my_rank * cap + (r % cap)) * H;
-      for (int c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
-        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int k = 0; k < m; ++k) {
-          const float4 y = *reinterpret_cast<const float4*>(ybuf + (size_t)s_pos[k] * H + c4 * 4);
-          acc.x = __fadd_rn(acc.x, y.x);
-          acc.y = __fadd_rn(acc.y, y.y);
-          acc.z = __fadd_rn(acc.z, y.z);
-          acc.w = __fadd_rn(acc.w, y.w);
-        }
-        uint2 o;
-        o.x = (uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16);
-        o.y = (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16);
-        *reinterpret_cast<uint2*>(dst + c4 * 4) = o;
-      }
-    }
-    __syncthreads();  // s_pos / s_n reused by the next row
   }
   publish_when_last(done_counter, peers.cflag, G, my_rank, epoch);
 }
