@@ -690,9 +690,9 @@ int ep_phase_a(gm_moe* h, const Layer& L, const uint16_t* xb, int T, cudaStream_
       GM_STAGE(h, s, launch_bq_norm_quant(xb, L.gamma2, T, h->x_i8, h->x_sa, h->inv_rms, s), "bq_norm_quant");
     else
       GM_STAGE(h, s, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
-    GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, h->router_counts, s),
+    GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, T, h->logits, h->dev_err, h->router_counts, s),
              "router_expert");
-    GM_STAGE(h, s, launch_topk(h->logits, L.pes, T, h->route_idx, h->route_w, s), "router_merge");
+    GM_STAGE(h, s, launch_topk(h->logits, L.pes, h->inv_rms, T, h->route_idx, h->route_w, s), "router_merge");
   }
   const EpPlacement pl = ep_placement(h);
   GM_STAGE(h, s, launch_ep_plan(h->route_idx, T, G, h->epr, pl, h->ep_pos, h->ep_count, s), "ep_plan");
@@ -1055,9 +1055,9 @@ int forward_impl(gm_moe* h, int layer, const void* x, void* out, int T, void* st
   else
     GM_STAGE(h, s, launch_rms_norm_bf16(xb, L.gamma2, T, h->x_normed, h->inv_rms, s), "rms_norm");
   // 2. router logits, 3. top-8 + schedule
-  GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, h->inv_rms, T, h->logits, h->dev_err, h->router_counts, s), "router_expert");
+  GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, T, h->logits, h->dev_err, h->router_counts, s), "router_expert");
   const int rc_chunk = L.kind == 1 ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16;
-  GM_STAGE(h, s, launch_topk_schedule(h->logits, L.pes, T, h->route_idx, h->route_w, h->expert_base,
+  GM_STAGE(h, s, launch_topk_schedule(h->logits, L.pes, h->inv_rms, T, h->route_idx, h->route_w, h->expert_base,
                                  h->epr, rc_chunk, h->expert_offset, h->routes, h->route_pos,
                                  h->chunk_off, h->sched_counts, s),
          "router_merge.schedule");

@@ -54,26 +54,26 @@ int router_tile_counters(int T);
 // Router workspace: partials, inv_rms [T], an error word, tile counters.
 size_t router_workspace_floats(int T);
 
-// Router logits as split-K partials [ksplit][T][E].  With a device error word
-// and T >= ROUTER_TC_MIN_TOKENS the tcgen05 kernel (router_tc.cu) runs,
-// otherwise the FMA kernel.
+// Router dots as split-K partials [ksplit][T][E] over x * router_scale (the
+// top-8 step multiplies their sum by inv_rms).  With a device error word and
+// T >= ROUTER_TC_MIN_TOKENS the tcgen05 kernel (router_tc.cu) runs, otherwise
+// the FMA kernel.  Both read only x and the router weights, so they run beside
+// the norm kernel launched just before them (see router.cu).
 constexpr int ROUTER_TC_MIN_TOKENS = 512;
-cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
-                                 const float* inv_rms, int T, float* logits, int* err,
-                                 int* tile_counters, cudaStream_t s);
-cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
-                                    const float* inv_rms, int T, float* logits, int* err,
-                                    cudaStream_t s);
+cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale, int T,
+                                 float* logits, int* err, int* tile_counters, cudaStream_t s);
+cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale, int T,
+                                    float* logits, int* err, cudaStream_t s);
 cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_t s);
-cudaError_t launch_topk(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
-                        float* route_w, cudaStream_t s);
+cudaError_t launch_topk(float* logits, const uint16_t* pes, const float* inv_rms, int T,
+                        int32_t* route_idx, float* route_w, cudaStream_t s);
 // top-8 + softmax followed by the expert schedule (one CTA when T <= 1024;
 // otherwise a top-8 grid and, given `counts` scratch of schedule_counts_ints(T)
 // ints, the two-pass multi-CTA schedule)
-cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
-                                 float* route_w, int expert_base, int epr, int route_chunk,
-                                 int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
-                                 int32_t* chunk_off, int32_t* counts, cudaStream_t s);
+cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, const float* inv_rms, int T,
+                                 int32_t* route_idx, float* route_w, int expert_base, int epr,
+                                 int route_chunk, int32_t* expert_offset, SparseRoute* routes,
+                                 int32_t* route_pos, int32_t* chunk_off, int32_t* counts, cudaStream_t s);
 int schedule_counts_ints(int T);
 cudaError_t launch_schedule_multi(const int32_t* route_idx, const float* route_w, int T,
                                   int expert_base, int epr, int route_chunk, int32_t* counts,

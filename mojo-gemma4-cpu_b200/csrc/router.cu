@@ -9,11 +9,17 @@
 // B200 shape: the logits are a skinny [T x 2816] x [2816 x 128] product done
 // in f32 FMA (the reference's f32-activation x bf16-weight dot, no bf16
 // rounding of the activation), split along K into 11 slices of 256 so that
-// enough CTAs stream the 720 KB projection at every T.  inv_rms comes
-// from the activation-norm kernel that runs first (the reference computes the
-// same rms_reduce_row for both, kernels/rmsnorm.mojo:16-17).  Top-8 selection
-// is one warp per token with 8 rounds of warp arg-max under the reference's
-// ordering (logit descending, ties to the lower expert id).
+// enough CTAs stream the 720 KB projection at every T.  The dot is taken over
+// x * router_scale (exact in f32: a product of two bf16); the token's inv_rms
+// (from the activation-norm kernel; the reference computes the same
+// rms_reduce_row for both, kernels/rmsnorm.mojo:16-17) multiplies the summed
+// dot in the top-8 step, so the logits kernel does not depend on the norm
+// kernel and runs beside it: it waits for its predecessor (programmatic
+// dependent launch) only after its own stores, which makes its completion
+// imply the norm kernel's.  The result differs from the reference's
+// per-element (x * s) * inv_rms only by f32 rounding.  Top-8 selection is one
+// warp per token with 8 rounds of warp arg-max under the reference's ordering
+// (logit descending, ties to the lower expert id).
 #include "gm_kernels.h"
 #include "router_dev.cuh"
 
@@ -32,12 +38,13 @@ namespace gm {
 // so the top-8 kernel reads T*E logits instead of 11*T*E partials.
 __global__ void __launch_bounds__(256)
 router_logits_small_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
-                           const uint16_t* __restrict__ rscale, const float* __restrict__ inv_rms,
-                           int T, float* __restrict__ logits_base, int* __restrict__ tile_count) {
+                           const uint16_t* __restrict__ rscale, int T, float* __restrict__ logits_base,
+                           int* __restrict__ tile_count) {
   constexpr int TT = 8, KS = 256;
   __shared__ __align__(16) float s_s[TT][KS];
   __shared__ int s_last;
-  pdl_wait();
+  // Launched right after the norm kernel, which triggers only after its own
+  // wait: x is complete when this grid starts.  No wait here (see the end).
   pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t0 = blockIdx.x * TT, e0 = blockIdx.y * 32, kb = blockIdx.z * KS;
@@ -48,10 +55,10 @@ router_logits_small_kernel(const uint16_t* __restrict__ x, const uint16_t* __res
     if (t0 + t < T) {
       const uint32_t v = *reinterpret_cast<const uint32_t*>(x + (size_t)(t0 + t) * H + kb + kp);
       const uint32_t rs = *reinterpret_cast<const uint32_t*>(rscale + kb + kp);
-      const float inv = inv_rms[t0 + t];
-      // `xv * sv * inv_vec` (moe_router.mojo:175-178): (x*s)*inv, f32
-      a = __fmul_rn(__fmul_rn(bf2f(v & 0xFFFFu), bf2f(rs & 0xFFFFu)), inv);
-      b = __fmul_rn(__fmul_rn(bf2f(v >> 16), bf2f(rs >> 16)), inv);
+      // `xv * sv` of `xv * sv * inv_vec` (moe_router.mojo:175-178); inv_vec
+      // is applied to the summed dot by the top-8 step
+      a = __fmul_rn(bf2f(v & 0xFFFFu), bf2f(rs & 0xFFFFu));
+      b = __fmul_rn(bf2f(v >> 16), bf2f(rs >> 16));
     }
     s_s[t][kp] = a;
     s_s[t][kp + 1] = b;
@@ -108,6 +115,9 @@ router_logits_small_kernel(const uint16_t* __restrict__ x, const uint16_t* __res
       if (tid == 0) *ctr = 0;  // re-armed for the next call on this stream
     }
   }
+  // this grid completes only after its predecessor (the norm kernel) has:
+  // the top-8 step, which waits for this grid, then sees inv_rms
+  pdl_wait();
 }
 
 // inv_rms of each token (one warp per token): kernels/rmsnorm.mojo:16-17,45-46.
@@ -133,12 +143,13 @@ rms_inv_kernel(const uint16_t* __restrict__ x, int T, float* __restrict__ inv_rm
 
 __global__ void __launch_bounds__(128)
 topk_softmax_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __restrict__ pes,
-                    int T, int32_t* __restrict__ route_idx, float* __restrict__ route_w) {
+                    const float* __restrict__ inv_rms, int T, int32_t* __restrict__ route_idx,
+                    float* __restrict__ route_w) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
   if (t >= T) return;
-  topk_token(logits, ksplit, pes, T, t, threadIdx.x & 31, route_idx, route_w);
+  topk_token(logits, ksplit, pes, inv_rms, T, t, threadIdx.x & 31, route_idx, route_w);
 }
 
 // Up to 32 tokens the one-CTA top-8 + schedule kernel runs, so the router
@@ -153,18 +164,17 @@ size_t router_workspace_floats(int T) {
   return (size_t)ROUTER_SLICES * T * E + T + 1 + router_tile_counters(T);
 }
 
-cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
-                                 const float* inv_rms, int T, float* logits, int* err,
-                                 int* tile_counters, cudaStream_t s) {
+cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale, int T,
+                                 float* logits, int* err, int* tile_counters, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  if (T >= ROUTER_TC_MIN_TOKENS && err) return launch_router_logits_tc(x, wr, rscale, inv_rms, T, logits, err, s);
+  if (T >= ROUTER_TC_MIN_TOKENS && err) return launch_router_logits_tc(x, wr, rscale, T, logits, err, s);
   if (router_ksplit(T) > 1) {
     tile_counters = nullptr;  // ROUTER_SLICES separate partials, summed by the top-8 kernel
   } else if (!tile_counters) {
     return cudaErrorInvalidValue;
   }
   return launch_k(router_logits_small_kernel, dim3((T + 7) / 8, E / 32, ROUTER_SLICES), dim3(256), 0,
-                  s, x, wr, rscale, inv_rms, T, logits, tile_counters);
+                  s, x, wr, rscale, T, logits, tile_counters);
 }
 
 cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_t s) {
@@ -172,11 +182,11 @@ cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_
   return launch_k(rms_inv_kernel, dim3((T + 7) / 8), dim3(256), 0, s, x, T, inv_rms);
 }
 
-cudaError_t launch_topk(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
-                        float* route_w, cudaStream_t s) {
+cudaError_t launch_topk(float* logits, const uint16_t* pes, const float* inv_rms, int T,
+                        int32_t* route_idx, float* route_w, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   return launch_k(topk_softmax_kernel, dim3((T + 3) / 4), dim3(128), 0, s, logits,
-                  router_ksplit(T), pes, T, route_idx, route_w);
+                  router_ksplit(T), pes, inv_rms, T, route_idx, route_w);
 }
 
 // Standalone router (gm_router_select): inv_rms, a device error word and the
@@ -191,8 +201,8 @@ cudaError_t launch_router(const uint16_t* x, const uint16_t* wr, const uint16_t*
   int* counters = err + 1;
   cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int) * (1 + router_tile_counters(T)), s);
   if (e == cudaSuccess) e = launch_rms_inv(x, T, inv, s);
-  if (e == cudaSuccess) e = launch_router_logits(x, wr, rscale, inv, T, logits, err, counters, s);
-  if (e == cudaSuccess) e = launch_topk(logits, pes, T, route_idx, route_w, s);
+  if (e == cudaSuccess) e = launch_router_logits(x, wr, rscale, T, logits, err, counters, s);
+  if (e == cudaSuccess) e = launch_topk(logits, pes, inv, T, route_idx, route_w, s);
   return e;
 }
 

@@ -6,12 +6,15 @@
 namespace gm {
 
 // Top-8 of token t by one warp (lane l holds experts l, l+32, l+64, l+96).
-// The split-K partial logits are summed in slice order (deterministic) and the
-// total is written back to slice 0.  moe_router.mojo:44-57 ordering and
-// :276-293 softmax / per_expert_scale.
+// The split-K partial logits are dots of the un-normalised router input
+// (x * router_scale); they are summed in slice order (deterministic), times
+// the token's inv_rms (the reference's (x * s) * inv_rms scaling, moved after
+// the dot so that the router does not wait for the norm), and the logit is
+// written back to slice 0.  moe_router.mojo:44-57 ordering and :276-293
+// softmax / per_expert_scale.
 __device__ __forceinline__ void topk_token(float* __restrict__ logits, int ksplit, const uint16_t* __restrict__ pes,
-                           int T, int t, int lane, int32_t* __restrict__ route_idx,
-                           float* __restrict__ route_w) {
+                           const float* __restrict__ inv_rms, int T, int t, int lane,
+                           int32_t* __restrict__ route_idx, float* __restrict__ route_w) {
   // all partial loads are issued before any add (independent, one L2 round trip)
   constexpr int MAX_KSPLIT = 11;
   float part[4][MAX_KSPLIT];
@@ -20,6 +23,7 @@ __device__ __forceinline__ void topk_token(float* __restrict__ logits, int kspli
 #pragma unroll
     for (int z = 0; z < MAX_KSPLIT; ++z)
       part[j][z] = z < ksplit ? logits[(size_t)z * T * E + (size_t)t * E + lane + 32 * j] : 0.0f;
+  const float inv = inv_rms[t];
   float v[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -27,7 +31,8 @@ __device__ __forceinline__ void topk_token(float* __restrict__ logits, int kspli
 #pragma unroll
     for (int z = 1; z < MAX_KSPLIT; ++z)
       if (z < ksplit) a = __fadd_rn(a, part[j][z]);
-    if (ksplit > 1) logits[(size_t)t * E + lane + 32 * j] = a;
+    a = __fmul_rn(a, inv);
+    logits[(size_t)t * E + lane + 32 * j] = a;
     v[j] = a;
   }
   unsigned taken = 0;

@@ -97,10 +97,9 @@ int gm_router_select_noalloc(const void* x, const void* router_w, const void* ro
   if (e == cudaSuccess) e = launch_rms_inv(xb, T, inv, s);
   if (e == cudaSuccess)
     e = launch_router_logits(xb, static_cast<const uint16_t*>(router_w),
-                             static_cast<const uint16_t*>(router_scale), inv, T, scratch, nullptr,
-                             counters, s);
+                             static_cast<const uint16_t*>(router_scale), T, scratch, nullptr, counters, s);
   if (e == cudaSuccess)
-    e = launch_topk(scratch, static_cast<const uint16_t*>(per_expert_scale), T, route_idx, route_w, s);
+    e = launch_topk(scratch, static_cast<const uint16_t*>(per_expert_scale), inv, T, route_idx, route_w, s);
   if (e != cudaSuccess) return fail(GM_ECUDA, "gm_router_select_noalloc: launch failed", e);
   return GM_OK;
 }

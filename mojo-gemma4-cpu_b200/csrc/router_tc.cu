@@ -1,25 +1,28 @@
 // router_tc.cu -- router logits for many tokens on the tcgen05 tensor cores.
 //
 // Same product as router_logits_small_kernel (kernels/moe_router.mojo:
-// 164-191: s = (x * router_scale) * inv_rms in f32, logit = sum_k s_k * w_k
-// with the bf16 router projection), for T >= ROUTER_TC_MIN_TOKENS:
+// 164-191: logit = sum_k (x_k * router_scale_k) * w_k with the bf16 router
+// projection; the top-8 step multiplies the sum by inv_rms), for
+// T >= ROUTER_TC_MIN_TOKENS:
 //
-//  * every f32 activation is split exactly into three bf16 parts,
-//    s = hi + mid + lo (hi = bf16(s), mid = bf16(s - hi), lo = s - hi - mid:
-//    each rounding residual of an f32 is exact in f32 and the last one has at
-//    most 8 significant bits), and a bf16 x bf16 product is exact in f32, so
-//    the three kind::f16 MMAs (f32 accumulate) give the f32 dot up to the
+//  * s = x * router_scale is a product of two bf16, exact in f32 with at most
+//    16 significant bits, so it splits exactly into two bf16 parts,
+//    s = hi + lo (hi = bf16(s), lo = s - hi: the rounding residual has at most
+//    8 significant bits), and a bf16 x bf16 product is exact in f32, so the
+//    two kind::f16 MMAs (f32 accumulate) give the f32 dot up to the
 //    accumulation order -- the same class of difference as the reference's
 //    own split across workers;
 //  * one CTA = 128 tokens x all 128 experts x one 256-wide K slice (the same
 //    11 slices, and the same [slice][T][E] partial layout, as the FMA kernel,
 //    so the top-8 kernels are shared);
-//  * the router slice (64 KB) is fetched with cp.async before the
-//    programmatic-dependency wait (weights do not depend on earlier kernels),
-//    the activation parts are produced by all 256 threads into a 2-stage ring
-//    in the 128-byte-swizzled K-major layout the MMA descriptors read, and
-//    the TMEM accumulator is staged through shared memory for coalesced
-//    stores.
+//  * the kernel reads only x and the router weights, so it runs beside the
+//    norm kernel launched just before it (that kernel triggers only after its
+//    own wait, so x is complete); it waits for its predecessor only after its
+//    stores, so its completion implies the norm kernel's (router.cu);
+//  * the router slice (64 KB) is fetched with cp.async, the activation parts
+//    are produced by all 256 threads into a 2-stage ring in the
+//    128-byte-swizzled K-major layout the MMA descriptors read, and the TMEM
+//    accumulator is staged through shared memory for coalesced stores.
 //
 // Every mbarrier wait is bounded (tc::mbar_wait, ~1 s); on expiry the kernel
 // writes 1 into *err, skips the remaining MMAs, still frees its TMEM and
@@ -46,7 +49,7 @@ constexpr uint32_t IDESC_BF16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)
 
 struct RouterSmem {
   uint8_t b[RT_NCH][RT_TILE];     // router rows (experts) x 64 bf16 per chunk; 1024-aligned
-  uint8_t a[2][3][RT_TILE];       // 2 stages x {hi, mid, lo} x [128 tokens][64 bf16]
+  uint8_t a[2][3][RT_TILE];       // 2 stages x {hi, lo, (output staging room)} x [128 tokens][64 bf16]
   uint64_t done[2];
   uint32_t tmem_base;
   int failed;
@@ -70,16 +73,15 @@ __device__ __forceinline__ uint32_t pack_bf16(uint16_t lo, uint16_t hi) {
 
 __global__ void __launch_bounds__(RT_THREADS, 1)
 router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
-                 const uint16_t* __restrict__ rscale, const float* __restrict__ inv_rms, int T,
-                 float* __restrict__ logits, int* __restrict__ err) {
+                 const uint16_t* __restrict__ rscale, int T, float* __restrict__ logits,
+                 int* __restrict__ err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   RouterSmem& s =
       *reinterpret_cast<RouterSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * RT_BM, kb = blockIdx.y * RT_KS;
 
-  // router slice: 128 experts x 256 K = 4 chunks of [128][64] bf16 (weights
-  // are not written by any kernel of the stream: fetched before the wait)
+  // router slice: 128 experts x 256 K = 4 chunks of [128][64] bf16
   for (int i = tid; i < E * (RT_KS / 8); i += RT_THREADS) {
     const int e = i / (RT_KS / 8), u = i % (RT_KS / 8), c = u >> 3, j = u & 7;
     cp_async16(s.b[c] + sw128(e, j), wr + (size_t)e * H + kb + u * 8);
@@ -101,8 +103,7 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
-  pdl_wait();  // inv_rms comes from the norm kernel
-  pdl_trigger();
+  pdl_trigger();  // no wait before reading x: see the file comment
 
   // 8 consecutive router_scale values of each 16-byte unit this thread owns
   // (the unit column j = tid & 7 is the same for all 4 of its units)
@@ -117,33 +118,28 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
     for (int q = 0; q < 4; ++q) {
       const int r = (tid >> 3) + q * (RT_THREADS / 8);  // token row in the tile
       const int t = t0 + r;
-      uint32_t hi[4] = {0, 0, 0, 0}, mid[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
+      uint32_t hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
       if (t < T) {
         const uint4 xv = *reinterpret_cast<const uint4*>(x + (size_t)t * H + k0);
         const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
-        const float inv = inv_rms[t];
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          uint16_t h2[2], m2[2], l2[2];
+          uint16_t h2[2], l2[2];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const float xs = bf2f(h ? xw[p] >> 16 : xw[p] & 0xFFFFu);
             const float ss = bf2f(h ? rsw[p] >> 16 : rsw[p] & 0xFFFFu);
-            const float sv = __fmul_rn(__fmul_rn(xs, ss), inv);   // (x*s)*inv
+            const float sv = __fmul_rn(xs, ss);                   // x*s, exact
             h2[h] = f2bf(sv);
-            const float r1 = __fsub_rn(sv, bf2f(h2[h]));          // exact residual
-            m2[h] = f2bf(r1);
-            l2[h] = f2bf(__fsub_rn(r1, bf2f(m2[h])));             // exact (<= 8 bits)
+            l2[h] = f2bf(__fsub_rn(sv, bf2f(h2[h])));             // exact residual (<= 8 bits)
           }
           hi[p] = pack_bf16(h2[0], h2[1]);
-          mid[p] = pack_bf16(m2[0], m2[1]);
           lo[p] = pack_bf16(l2[0], l2[1]);
         }
       }
       const int off = sw128(r, j);
       *reinterpret_cast<uint4*>(s.a[st][0] + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      *reinterpret_cast<uint4*>(s.a[st][1] + off) = make_uint4(mid[0], mid[1], mid[2], mid[3]);
-      *reinterpret_cast<uint4*>(s.a[st][2] + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      *reinterpret_cast<uint4*>(s.a[st][1] + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
     if (c == 0) cp_async_wait_all();
     // generic-proxy shared-memory writes -> visible to the tensor core (async proxy)
@@ -155,7 +151,7 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
       for (int k = 0; k < RT_BK / 16; ++k) {
         const uint64_t db = kmajor_sw128_desc(smem_u32(s.b[c]) + k * 32);
 #pragma unroll
-        for (int p = 0; p < 3; ++p)
+        for (int p = 0; p < 2; ++p)
           mma_bf16_ss(tmem, kmajor_sw128_desc(smem_u32(s.a[st][p]) + k * 32), db,
                       (c | k | p) != 0);
       }
@@ -198,19 +194,20 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
         *reinterpret_cast<const float4*>(ystage + r * RT_YSTR + lane * 4);
   }
   if (tid == 0 && *(volatile int*)&s.failed) atomicExch(err, 1);
+  // this grid completes only after its predecessor (the norm kernel) has
+  pdl_wait();
 }
 
 }  // namespace tc
 
-cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale,
-                                    const float* inv_rms, int T, float* logits, int* err,
-                                    cudaStream_t s) {
+cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale, int T,
+                                    float* logits, int* err, cudaStream_t s) {
   const size_t smem = sizeof(tc::RouterSmem) + 1024;
   cudaError_t e = cudaFuncSetAttribute(tc::router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem);
   if (e != cudaSuccess) return e;
   return launch_k(tc::router_tc_kernel, dim3((T + tc::RT_BM - 1) / tc::RT_BM, H / tc::RT_KS),
-                  dim3(tc::RT_THREADS), smem, s, x, wr, rscale, inv_rms, T, logits, err);
+                  dim3(tc::RT_THREADS), smem, s, x, wr, rscale, T, logits, err);
 }
 
 }  // namespace gm

@@ -145,7 +145,8 @@ build_schedule_kernel(const int32_t* __restrict__ route_idx, const float* __rest
 // round trip of the routes through a separate kernel boundary.
 __global__ void __launch_bounds__(1024)
 topk_schedule_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __restrict__ pes,
-                     int T, int32_t* __restrict__ route_idx, float* __restrict__ route_w,
+                     const float* __restrict__ inv_rms, int T, int32_t* __restrict__ route_idx,
+                     float* __restrict__ route_w,
                      int expert_base, int epr, int route_chunk, int32_t* __restrict__ expert_offset,
                      SparseRoute* __restrict__ routes, int32_t* __restrict__ route_pos,
                      int32_t* __restrict__ chunk_off) {
@@ -154,7 +155,7 @@ topk_schedule_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __r
   pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int t = warp; t < T; t += 32)
-    topk_token(logits, ksplit, pes, T, t, lane, route_idx, route_w);
+    topk_token(logits, ksplit, pes, inv_rms, T, t, lane, route_idx, route_w);
   __syncthreads();  // route_idx / route_w written by this CTA are now visible to it
   schedule_body(route_idx, route_w, T, expert_base, epr, route_chunk, expert_offset, routes,
                 route_pos, chunk_off, sm);
@@ -309,17 +310,17 @@ cudaError_t launch_build_schedule(const int32_t* route_idx, const float* route_w
                   expert_base, epr, route_chunk, expert_offset, routes, route_pos, chunk_off);
 }
 
-cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, int T, int32_t* route_idx,
-                                 float* route_w, int expert_base, int epr, int route_chunk,
-                                 int32_t* expert_offset, SparseRoute* routes, int32_t* route_pos,
-                                 int32_t* chunk_off, int32_t* counts, cudaStream_t s) {
+cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, const float* inv_rms, int T,
+                                 int32_t* route_idx, float* route_w, int expert_base, int epr,
+                                 int route_chunk, int32_t* expert_offset, SparseRoute* routes,
+                                 int32_t* route_pos, int32_t* chunk_off, int32_t* counts, cudaStream_t s) {
   // one CTA when the logits arrive reduced (small T); otherwise the top-8 is
   // spread over T/4 CTAs first
   if (T <= 32 && router_ksplit(T) == 1)
     return launch_k(topk_schedule_kernel, dim3(1), dim3(1024), 0, s, logits, router_ksplit(T), pes,
-                    T, route_idx, route_w, expert_base, epr, route_chunk, expert_offset, routes,
+                    inv_rms, T, route_idx, route_w, expert_base, epr, route_chunk, expert_offset, routes,
                     route_pos, chunk_off);
-  cudaError_t e = launch_topk(logits, pes, T, route_idx, route_w, s);
+  cudaError_t e = launch_topk(logits, pes, inv_rms, T, route_idx, route_w, s);
   if (e != cudaSuccess) return e;
   if (counts && T > 1024)
     return launch_schedule_multi(route_idx, route_w, T, expert_base, epr, route_chunk, counts,
