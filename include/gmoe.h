@@ -147,6 +147,34 @@ int gm_moe_register_dense_bq(gm_moe_t* h, int layer, const void* gate_proj, cons
 int gm_dense_forward(gm_moe_t* h, int layer, const void* x, void* dense_out, int T, void* stream);
 int gm_ffn_forward(gm_moe_t* h, int layer, void* x_main, int T, void* stream);
 
+/* ----------------------------------------------- attention block products --
+ * The products of the butterquant attention block around the attention core
+ * (modeling/gemma_4_moe_bq.mojo:418-627), weights in the reference's VNNI
+ * layout (device pointers, async on `stream`):
+ * gm_bq_linear: dispatch_bq_linear (butterquant_kernels/linear.mojo:119-150):
+ *   out bf16 [T][n_rows] = (dot(x_i8, w) * (x_sa/127)) * w_scale over K = 2816
+ *   (x_i8/x_sa from gm_bq_norm_quant); n_rows a multiple of 32.
+ * gm_bq_qkv: dispatch_bq_qkv (linear.mojo:273-328): the q, k and v products of
+ *   one attention layer over the same activation in one launch (q [T][qn],
+ *   k and v [T][kvn]); v_w == NULL for the full layers, whose V is K.
+ * gm_bq_block_quant_ex: dispatch_bq_block_quant[block, apply_fwht]
+ *   (linear.mojo:182-205, butterquant/runtime.mojo:62-79): bf16 [rows][cols]
+ *   -> int8 + per-block amax [rows][cols/block]; block 64/128/256/512, FWHT
+ *   only with block 64.  The attention output uses block = head_dim, no FWHT.
+ * gm_bq_block_linear_ex: dispatch_bq_block_linear (linear.mojo:240-270,
+ *   butterquant/gemm.mojo:174-216) for any block: out bf16 [T][n_rows], the
+ *   per-block fma chain in block order; k/block a multiple of 4.  The
+ *   attention output projection (o_proj, block = head_dim). */
+int gm_bq_linear(const int8_t* x_i8, const float* x_sa, int T, const void* w, const float* w_scale,
+                 int n_rows, void* out, void* stream);
+int gm_bq_qkv(const int8_t* x_i8, const float* x_sa, int T, const void* q_w, const float* q_scale, int qn,
+              const void* k_w, const float* k_scale, const void* v_w, const float* v_scale, int kvn,
+              void* q_out, void* k_out, void* v_out, void* stream);
+int gm_bq_block_quant_ex(const void* x, long rows, int cols, int block, int apply_fwht, int8_t* q, float* sa,
+                         void* stream);
+int gm_bq_block_linear_ex(const int8_t* h_i8, const float* h_sa, int T, int k, int block, const void* w,
+                          const float* w_scale, int n_rows, void* out, void* stream);
+
 /* ------------------------------------------------------------ checkpoints --
  * Safetensors checkpoints as the reference reads and writes them
  * (safetensors/parser.mojo, safetensors/writer.mojo:39-75): an 8-byte

@@ -1723,6 +1723,53 @@ int gm_bq_block_linear(const int8_t* h_i8, const float* h_sa, int T, const void*
         "bq_block_linear");
 }
 
+int gm_bq_linear(const int8_t* x_i8, const float* x_sa, int T, const void* w, const float* w_scale,
+                 int n_rows, void* out, void* stream) {
+  if (T < 0 || n_rows <= 0 || n_rows % 32)
+    return set_err(nullptr, GM_EINVAL, "bq_linear: T=%d n_rows=%d (a multiple of 32)", T, n_rows);
+  const int8_t* wl[1] = {static_cast<const int8_t*>(w)};
+  const float* sl[1] = {w_scale};
+  uint16_t* ol[1] = {static_cast<uint16_t*>(out)};
+  STAGE(launch_bq_linear_multi(x_i8, x_sa, T, 1, wl, sl, ol, &n_rows, S(stream)), "bq_linear");
+}
+
+int gm_bq_qkv(const int8_t* x_i8, const float* x_sa, int T, const void* q_w, const float* q_scale, int qn,
+              const void* k_w, const float* k_scale, const void* v_w, const float* v_scale, int kvn,
+              void* q_out, void* k_out, void* v_out, void* stream) {
+  if (T < 0 || qn <= 0 || qn % 32 || kvn <= 0 || kvn % 32)
+    return set_err(nullptr, GM_EINVAL, "bq_qkv: T=%d qn=%d kvn=%d (multiples of 32)", T, qn, kvn);
+  if (!q_w || !k_w || !q_out || !k_out || (v_w && !v_out))
+    return set_err(nullptr, GM_EINVAL, "bq_qkv: NULL weight or output");
+  const int nseg = v_w ? 3 : 2;  // full layers: K = V, no v projection
+  const int8_t* wl[3] = {static_cast<const int8_t*>(q_w), static_cast<const int8_t*>(k_w),
+                         static_cast<const int8_t*>(v_w)};
+  const float* sl[3] = {q_scale, k_scale, v_scale};
+  uint16_t* ol[3] = {static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_out), static_cast<uint16_t*>(v_out)};
+  const int nl[3] = {qn, kvn, kvn};
+  STAGE(launch_bq_linear_multi(x_i8, x_sa, T, nseg, wl, sl, ol, nl, S(stream)), "bq_qkv");
+}
+
+int gm_bq_block_quant_ex(const void* x, long rows, int cols, int block, int apply_fwht, int8_t* q, float* sa,
+                         void* stream) {
+  if (rows < 0 || cols <= 0 || !(block == 64 || block == 128 || block == 256 || block == 512) ||
+      cols % block || (apply_fwht && block != 64))
+    return set_err(nullptr, GM_EINVAL, "bq_block_quant_ex: rows=%ld cols=%d block=%d fwht=%d", rows, cols,
+                   block, apply_fwht);
+  STAGE(launch_block_quant_ex(static_cast<const uint16_t*>(x), rows, cols, block, apply_fwht, q, sa, S(stream)),
+        "bq_block_quant_ex");
+}
+
+int gm_bq_block_linear_ex(const int8_t* h_i8, const float* h_sa, int T, int k, int block, const void* w,
+                          const float* w_scale, int n_rows, void* out, void* stream) {
+  if (T < 0 || !(block == 64 || block == 128 || block == 256 || block == 512) || k <= 0 || k % block ||
+      (k / block) % 4 || n_rows <= 0 || n_rows % 32 || (size_t)16 * (k + 16) > 200 * 1024)
+    return set_err(nullptr, GM_EINVAL, "bq_block_linear_ex: T=%d k=%d block=%d n_rows=%d (k/block a "
+                   "multiple of 4, k <= 12800, n_rows a multiple of 32)", T, k, block, n_rows);
+  STAGE(launch_block_linear_ex(h_i8, h_sa, T, k, block, static_cast<const int8_t*>(w), w_scale, n_rows,
+                               static_cast<uint16_t*>(out), S(stream)),
+        "bq_block_linear_ex");
+}
+
 namespace {
 int check_attn_geometry(int head_dim, int num_q, int num_kv, int cache_degree, int rank) {
   if (head_dim != 256 && head_dim != 512)

@@ -173,6 +173,17 @@ cudaError_t launch_tcb_phase2(const void* map_a, const void* map_b, const int32_
                               int epr, int T, const SparseRoute* routes, float* ybuf, int* err,
                               cudaStream_t s);
 
+// attention block products (attn_block.cu): up to 3 bq_linear products over
+// one activation (K = 2816), general block quant, general block linear
+cudaError_t launch_bq_linear_multi(const int8_t* xi8, const float* xsa, int T, int nseg,
+                                   const int8_t* const* w, const float* const* scale, uint16_t* const* out,
+                                   const int* n_rows, cudaStream_t s);
+cudaError_t launch_block_quant_ex(const uint16_t* src, long rows, int cols, int block, int fwht,
+                                  int8_t* qi8, float* sa, cudaStream_t s);
+cudaError_t launch_block_linear_ex(const int8_t* hi8, const float* hsa, int T, int k, int block,
+                                   const int8_t* w, const float* wsc, int n_rows, uint16_t* out,
+                                   cudaStream_t s);
+
 cudaError_t launch_quantize_rows(const uint16_t* w, long rows, int cols, const uint16_t* gamma,
                                  int block, int8_t* q, float* scale, cudaStream_t s);
 cudaError_t launch_vnni_permute(const int8_t* src, long rows, int cols, int8_t* dst, int dir,

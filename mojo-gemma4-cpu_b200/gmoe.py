@@ -79,6 +79,10 @@ SIGNATURES = {
     "gm_ffn_forward": (_i32, [_vp, _i32, _vp, _i32, _vp]),
     "gm_bq_dense_gate_up": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "gm_bq_block_linear": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "gm_bq_linear": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _vp, _vp]),
+    "gm_bq_qkv": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]),
+    "gm_bq_block_quant_ex": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
+    "gm_bq_block_linear_ex": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp, _vp, _i32, _vp, _vp]),
     "gm_bq_attn_prep": (_i32, [_vp] * 14 + [_vp, _i32, _vp] + [_i32] * 11 + [_vp]),
     "gm_bq_attention_decode": (_i32, [_vp] * 8 + [_i32] * 11 + [_vp, _vp, _sz, _vp]),
     "gm_bq_attention_workspace_bytes": (_sz, [_i32] * 5),

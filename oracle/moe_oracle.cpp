@@ -538,6 +538,56 @@ void orc_bq_block_quant(const uint16_t* bucket, long R, int cols, int block, int
   }
 }
 
+// prepare_block_activation[block, apply_fwht] (butterquant/runtime.mojo:62-79)
+// with the FWHT optional: the attention output is quantised per head (block =
+// head_dim) without one (modeling/gemma_4_moe_bq.mojo:516-518).
+void orc_bq_block_quant_ex(const uint16_t* src, long R, int cols, int block, int apply_fwht, int8_t* qi8,
+                           float* sa) {
+  int nb = cols / block;
+#pragma omp parallel
+  {
+    std::vector<float> v(cols);
+#pragma omp for schedule(static)
+    for (long r = 0; r < R; ++r) {
+      for (int k = 0; k < cols; ++k) v[k] = bf2f(src[r * cols + k]);
+      for (int b = 0; b < nb; ++b) {
+        float* vb = v.data() + b * block;
+        if (apply_fwht) fwht_block(vb, block);
+        float amax = 0.0f;
+        for (int k = 0; k < block; ++k) amax = std::max(amax, std::fabs(vb[k]));
+        sa[r * nb + b] = amax;
+        float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+        for (int k = 0; k < block; ++k) qi8[r * cols + b * block + k] = quantize_i8(vb[k], inv);
+      }
+    }
+  }
+}
+
+// gemm_i8_per_block_panel (butterquant/gemm.mojo:174-216) for any block: the
+// attention output projection uses block = head_dim.  cs block-major
+// [k/block][n_rows].
+void orc_bq_block_linear_ex(const int8_t* hi8, const float* hsa, int T, int k, int block, const int8_t* w,
+                            const float* ws, const float* cs, int n_rows, uint16_t* out) {
+  const float inv127 = 1.0f / 127.0f;
+  const int nb = k / block;
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    const uint8_t* ar = reinterpret_cast<const uint8_t*>(hi8 + (long)t * k);
+    for (int n = 0; n < n_rows; ++n) {
+      const int8_t* wr = w + (long)n * k;
+      float facc = 0.0f;
+      for (int b = 0; b < nb; ++b) {
+        int32_t ia = 0;
+        for (int j = b * block; j < (b + 1) * block; ++j)
+          ia += (int32_t)(uint8_t)(ar[j] ^ 0x80u) * (int32_t)wr[j];
+        const float corr = (float)ia - 128.0f * cs[(long)b * n_rows + n];
+        facc = std::fmaf(corr, hsa[(long)t * nb + b] * inv127, facc);
+      }
+      out[(long)t * n_rows + n] = f2bf(facc * ws[n]);
+    }
+  }
+}
+
 // butterquant_kernels/moe.mojo:168-295 BqPhase2DownKernel: for each record,
 // facc = fma(f32(iacc_b) - 128*cs[b][n], sa[r][b]/127, facc) over the 11 K
 // blocks; acc[tok][n] += facc*sw[n]*w (experts ascending); out = bf16(acc).

@@ -75,6 +75,8 @@ def _declare(L):
         "orc_bq_linear": (None, [vp, vp, i32, vp, vp, vp, i32, i32, vp]),
         "orc_gelu_gate_up": (None, [vp, vp, i64, vp]),
         "orc_bq_block_linear": (None, [vp, vp, i32, i32, vp, vp, vp, i32, vp]),
+        "orc_bq_block_quant_ex": (None, [vp, i64, i32, i32, i32, vp, vp]),
+        "orc_bq_block_linear_ex": (None, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp]),
         "orc_dense_mlp": (None, [vp, i32, vp, i32] + [vp] * 9 + [vp, vp, vp, vp]),
         "orc_prep_head": (f32, [vp, vp, vp, vp, i32, i32, i32, vp, vp]),
         "orc_bq_attn_prep": (None, [vp, vp, vp, vp, vp, i32, vp, vp, i32, i32, i32, i32, i32, vp, vp]
@@ -261,6 +263,26 @@ def bq_block_linear(hi8, hsa, w, ws, cs_block_major):
     out = np.empty((T, n), np.uint16)
     lib().orc_bq_block_linear(_p(np.ascontiguousarray(hi8)), _p(np.ascontiguousarray(hsa)), T, k,
                               _p(np.ascontiguousarray(w)), _p(ws), _p(cs_block_major), n, _p(out))
+    return out
+
+
+def bq_block_quant_ex(x, block, apply_fwht):
+    """prepare_block_activation[block, apply_fwht] on bf16 rows: (int8, amax [rows][cols/block])."""
+    x = np.ascontiguousarray(x)
+    R, cols = x.shape
+    q = np.empty((R, cols), np.int8)
+    sa = np.empty((R, cols // block), np.float32)
+    lib().orc_bq_block_quant_ex(_p(x), R, cols, block, 1 if apply_fwht else 0, _p(q), _p(sa))
+    return q, sa
+
+
+def bq_block_linear_ex(hi8, hsa, w, ws, cs_block_major, block):
+    """gemm_i8_per_block for any block: bf16 [T][n_rows]; cs [k/block][n_rows]."""
+    T, k = hi8.shape
+    n = w.shape[0]
+    out = np.empty((T, n), np.uint16)
+    lib().orc_bq_block_linear_ex(_p(np.ascontiguousarray(hi8)), _p(np.ascontiguousarray(hsa)), T, k, block,
+                                 _p(np.ascontiguousarray(w)), _p(ws), _p(cs_block_major), n, _p(out))
     return out
 
 
