@@ -163,7 +163,7 @@ int gm_ffn_forward(gm_moe_t* h, int layer, void* x_main, int T, void* stream);
  *   only with block 64.  The attention output uses block = head_dim, no FWHT.
  * gm_bq_block_linear_ex: dispatch_bq_block_linear (linear.mojo:240-270,
  *   butterquant/gemm.mojo:174-216) for any block: out bf16 [T][n_rows], the
- *   per-block fma chain in block order; k/block a multiple of 4.  The
+ *   per-block fma chain in block order; k/block a multiple of 4 or 3.  The
  *   attention output projection (o_proj, block = head_dim). */
 int gm_bq_linear(const int8_t* x_i8, const float* x_sa, int T, const void* w, const float* w_scale,
                  int n_rows, void* out, void* stream);

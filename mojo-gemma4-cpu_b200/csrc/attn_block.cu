@@ -255,13 +255,12 @@ block_quant_ex_kernel(const uint16_t* __restrict__ src, long rows, int cols, int
 }
 
 // ---------------------------------------------------------------- block linear
-// Item = (16-token chunk, 32-row output tile); warp w takes the contiguous
-// K blocks [w*BPW, (w+1)*BPW).  Warp 0 runs the fma chain over its own blocks
-// while it streams them; the later warps hand their per-block integer dots to
-// it through shared memory, and it continues the chain in block order.
-constexpr int BL_WARPS = 4;
-
-template <int BLOCK, int DEPTH>
+// Item = (16-token chunk, 32-row output tile); warp w of BL_WARPS (4, or 3
+// when the block count is not a multiple of 4) takes the contiguous K blocks
+// [w*BPW, (w+1)*BPW).  Warp 0 runs the fma chain over its own blocks while it
+// streams them; the later warps hand their per-block integer dots to it
+// through shared memory, and it continues the chain in block order.
+template <int BLOCK, int DEPTH, int BL_WARPS>
 __global__ void __launch_bounds__(32 * BL_WARPS, 1)
 block_linear_kernel(const int8_t* __restrict__ hi8, const float* __restrict__ hsa, int T, int k,
                     const int8_t* __restrict__ w, const float* __restrict__ wsc, int n_rows,
@@ -479,31 +478,42 @@ cudaError_t launch_block_quant_ex(const uint16_t* src, long rows, int cols, int 
   }
 }
 
-size_t block_linear_smem(int k, int block) {
+size_t block_linear_smem(int k, int block, int warps) {
   const int nb = k / block;
-  return (size_t)RCA * (k + 16) + (size_t)RCA * nb * 4 + (size_t)(BL_WARPS - 1) * (nb / BL_WARPS) * 16 * 32 * 4;
+  return (size_t)RCA * (k + 16) + (size_t)RCA * nb * 4 + (size_t)(warps - 1) * (nb / warps) * 16 * 32 * 4;
 }
 
 cudaError_t launch_block_linear_ex(const int8_t* hi8, const float* hsa, int T, int k, int block,
                                    const int8_t* w, const float* wsc, int n_rows, uint16_t* out,
                                    cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  if (block <= 0 || k % block || (k / block) % BL_WARPS || n_rows <= 0 || n_rows % 32 || k % 64)
-    return cudaErrorInvalidValue;
-  const size_t smem = block_linear_smem(k, block);
+  if (block <= 0 || k % block || n_rows <= 0 || n_rows % 32 || k % 64) return cudaErrorInvalidValue;
+  const int nb = k / block;
+  const int warps = nb % 4 == 0 ? 4 : nb % 3 == 0 ? 3 : 0;
+  if (!warps) return cudaErrorInvalidValue;
+  const size_t smem = block_linear_smem(k, block, warps);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   const int items = ((T + RCA - 1) / RCA) * (n_rows / 32);
   auto run = [&](auto kern) -> cudaError_t {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const int grid = grid_for(kern, 32 * BL_WARPS, smem, items);
-    return launch_k(kern, dim3(grid), dim3(32 * BL_WARPS), smem, s, hi8, hsa, T, k, w, wsc, n_rows, out);
+    const int grid = grid_for(kern, 32 * warps, smem, items);
+    return launch_k(kern, dim3(grid), dim3(32 * warps), smem, s, hi8, hsa, T, k, w, wsc, n_rows, out);
   };
+  if (warps == 4) {
+    switch (block) {
+      case 64: return run(block_linear_kernel<64, 4, 4>);
+      case 128: return run(block_linear_kernel<128, 4, 4>);
+      case 256: return run(block_linear_kernel<256, 4, 4>);
+      case 512: return run(block_linear_kernel<512, 4, 4>);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   switch (block) {
-    case 64: return run(block_linear_kernel<64, 4>);
-    case 128: return run(block_linear_kernel<128, 4>);
-    case 256: return run(block_linear_kernel<256, 4>);
-    case 512: return run(block_linear_kernel<512, 4>);
+    case 64: return run(block_linear_kernel<64, 4, 3>);
+    case 128: return run(block_linear_kernel<128, 4, 3>);
+    case 256: return run(block_linear_kernel<256, 4, 3>);
+    case 512: return run(block_linear_kernel<512, 4, 3>);
     default: return cudaErrorInvalidValue;
   }
 }

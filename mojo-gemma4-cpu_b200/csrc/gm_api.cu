@@ -1762,9 +1762,9 @@ int gm_bq_block_quant_ex(const void* x, long rows, int cols, int block, int appl
 int gm_bq_block_linear_ex(const int8_t* h_i8, const float* h_sa, int T, int k, int block, const void* w,
                           const float* w_scale, int n_rows, void* out, void* stream) {
   if (T < 0 || !(block == 64 || block == 128 || block == 256 || block == 512) || k <= 0 || k % block ||
-      (k / block) % 4 || n_rows <= 0 || n_rows % 32 || (size_t)16 * (k + 16) > 200 * 1024)
+      ((k / block) % 4 && (k / block) % 3) || n_rows <= 0 || n_rows % 32 || (size_t)16 * (k + 16) > 200 * 1024)
     return set_err(nullptr, GM_EINVAL, "bq_block_linear_ex: T=%d k=%d block=%d n_rows=%d (k/block a "
-                   "multiple of 4, k <= 12800, n_rows a multiple of 32)", T, k, block, n_rows);
+                   "multiple of 4 or 3, k <= 12800, n_rows a multiple of 32)", T, k, block, n_rows);
   STAGE(launch_block_linear_ex(h_i8, h_sa, T, k, block, static_cast<const int8_t*>(w), w_scale, n_rows,
                                static_cast<uint16_t*>(out), S(stream)),
         "bq_block_linear_ex");

@@ -140,4 +140,4 @@ def test_attention_block_argument_checks():
     with pytest.raises(gmoe.GmoeError, match="GM_EINVAL"):
         gmoe.call("gm_bq_block_quant_ex", z, 1, 256, 256, 1, z, z, None)  # FWHT only for 64
     with pytest.raises(gmoe.GmoeError, match="GM_EINVAL"):
-        gmoe.call("gm_bq_block_linear_ex", z, z, 1, 768, 256, z, z, 2816, z, None)  # 3 blocks
+        gmoe.call("gm_bq_block_linear_ex", z, z, 1, 1280, 256, z, z, 2816, z, None)  # 5 blocks
