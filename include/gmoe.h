@@ -529,9 +529,9 @@ int gm_bq_attn_prep(const void* q_src, const void* k_src, const void* v_src, con
  * (attention.mojo:333-472, kernels/attention_dispatch_kernels.mojo:36-130):
  * T tokens, token t the newest position of run t (runs[t].buf_start = t).
  * Sliding (window > 0): the last min(pos+1, window) positions; full (window =
- * 0): positions 0..pos.  cache_degree must be 1 (rank 0): a cache sharded by
- * position over ranks would need each rank's unnormalised partials merged
- * across ranks, which this call does not return.  The KV range is split over CTAs and the
+ * 0): positions 0..pos.  cache_degree must be 1 (rank 0); a cache sharded by
+ * position over ranks goes through gm_bq_attention_partial + _merge below.
+ * The KV range is split over CTAs and the
  * splits merged as kernels/logsum_merge.mojo does; out bf16 [T][num_q *
  * head_dim], in the rotated domain as the reference's.  The signed int8 dot
  * needs no qi_bias.  max_kv_len bounds the KV length of any token (sizes the
@@ -543,6 +543,29 @@ int gm_bq_attention_decode(const int8_t* q_i8, const float* f_q, const int8_t* k
                            int page_shift, int row_mask, int page_mask, int max_kv_len, void* out,
                            float* workspace, size_t workspace_bytes, void* stream);
 size_t gm_bq_attention_workspace_bytes(int T, int head_dim, int num_q, int num_kv, int max_kv_len);
+
+/* A full-layer cache sharded by position over cache_degree ranks (the
+ * reference's full attention at degree > 1, attention.mojo:236-332 with
+ * kernels/logsum_merge.mojo:29-117): gm_bq_attention_partial computes, on one
+ * rank, every token's attention over the positions this rank holds
+ * (pos % cache_degree == rank, at cache row pos / cache_degree) and writes
+ * the unnormalised log-sum partial per (token, head): partial f32
+ * [T][num_q][head_dim + 2] = (m, l, acc[head_dim]) of
+ * gm_bq_attention_partial_bytes(T, head_dim, num_q) bytes (arguments as
+ * gm_bq_attention_decode; window must be 0 when cache_degree > 1).
+ * gm_bq_attention_merge merges n_parts such partials (host array of device
+ * pointers, rank order; a peer GPU's buffer may be passed where peer access
+ * is enabled) with the reference's max-rescaled sums and writes
+ * bf16(acc / l) [T][num_q * head_dim] (0 where no rank had a position). */
+size_t gm_bq_attention_partial_bytes(int T, int head_dim, int num_q);
+int gm_bq_attention_partial(const int8_t* q_i8, const float* f_q, const int8_t* k_cache,
+                            const float* k_scale, const int8_t* v_cache, const float* v_scale,
+                            const gm_kv_run_t* runs, const int32_t* base_rows, int T, int head_dim,
+                            int num_q, int num_kv, int window, int cache_degree, int rank, int page_shift,
+                            int row_mask, int page_mask, int max_kv_len, float* partial,
+                            float* workspace, size_t workspace_bytes, void* stream);
+int gm_bq_attention_merge(const float* const* partials, int n_parts, int T, int num_q, int head_dim, void* out,
+                          void* stream);
 
 /* butterquant/vnni.mojo:31-83 pack (and its inverse). rows%32 == 0, cols%64 == 0. */
 int gm_vnni_pack(const int8_t* q, long rows, int cols, int8_t* packed, void* stream);

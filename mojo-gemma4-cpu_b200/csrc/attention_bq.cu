@@ -470,7 +470,84 @@ attn_merge_kernel(const float* __restrict__ partials, int n_splits, uint16_t* __
   out[th * HD + threadIdx.x] = L > 0.0f ? f2bf(__fmul_rn(o, __fdiv_rn(1.0f, L))) : (uint16_t)0;
 }
 
+// The splits of one (token, head) reduced to ONE unnormalised partial
+// (m, l, acc) over this rank's positions -- the value each rank of a
+// position-sharded full-layer cache contributes to the cross-rank merge
+// (kernels/logsum_merge.mojo:29-96): m = max_s m_s, c_s =
+// exp(m_s - m) (0 when l_s = 0), l = sum l_s c_s, acc = sum acc_s c_s.
+template <int HD>
+__global__ void __launch_bounds__(HD)
+attn_rank_partial_kernel(const float* __restrict__ partials, int n_splits, float* __restrict__ part) {
+  pdl_wait();
+  pdl_trigger();
+  const size_t th = blockIdx.x;  // token * num_q + head
+  const float* p = partials + th * n_splits * (HD + 2);
+  float M = NEG_BIG;
+  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, p[(size_t)s * (HD + 2)]);
+  float L = 0.0f, o = 0.0f;
+  for (int s = 0; s < n_splits; ++s) {
+    const float* ps = p + (size_t)s * (HD + 2);
+    const float ls = ps[1];
+    if (!(ls > 0.0f)) continue;
+    const float c = fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(ps[0], M)));
+    L = __fmaf_rn(ls, c, L);
+    o = __fmaf_rn(ps[2 + threadIdx.x], c, o);
+  }
+  float* dst = part + th * (HD + 2);
+  if (threadIdx.x == 0) {
+    dst[0] = M;
+    dst[1] = L;
+  }
+  dst[2 + threadIdx.x] = o;
+}
+
+// The ranks' partials (each [T * num_q][HD + 2], rank order) merged and
+// normalised: the same log-sum merge, then bf16(acc / l) (0 when l = 0).
+struct PartList {
+  const float* p[8];
+  int n;
+};
+template <int HD>
+__global__ void __launch_bounds__(HD)
+attn_merge_parts_kernel(const __grid_constant__ PartList parts, uint16_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const size_t th = blockIdx.x;
+  float M = NEG_BIG;
+  for (int r = 0; r < parts.n; ++r) M = fmaxf(M, parts.p[r][th * (HD + 2)]);
+  float L = 0.0f, o = 0.0f;
+  for (int r = 0; r < parts.n; ++r) {
+    const float* ps = parts.p[r] + th * (HD + 2);
+    const float ls = ps[1];
+    if (!(ls > 0.0f)) continue;
+    const float c = fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(ps[0], M)));
+    L = __fmaf_rn(ls, c, L);
+    o = __fmaf_rn(ps[2 + threadIdx.x], c, o);
+  }
+  out[th * HD + threadIdx.x] = L > 0.0f ? f2bf(__fmul_rn(o, __fdiv_rn(1.0f, L))) : (uint16_t)0;
+}
+
 }  // namespace
+
+cudaError_t launch_attn_rank_partial(const float* partials, int T, int num_q, int head_dim, int n_splits,
+                                     float* part, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  if (head_dim == 256)
+    return launch_k(attn_rank_partial_kernel<256>, dim3(T * num_q), dim3(256), 0, s, partials, n_splits, part);
+  return launch_k(attn_rank_partial_kernel<512>, dim3(T * num_q), dim3(512), 0, s, partials, n_splits, part);
+}
+
+cudaError_t launch_attn_merge_parts(const float* const* parts, int n, int T, int num_q, int head_dim,
+                                    uint16_t* out, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  if (n < 1 || n > 8) return cudaErrorInvalidValue;
+  PartList pl = {};
+  for (int r = 0; r < n; ++r) pl.p[r] = parts[r];
+  pl.n = n;
+  if (head_dim == 256)
+    return launch_k(attn_merge_parts_kernel<256>, dim3(T * num_q), dim3(256), 0, s, pl, out);
+  return launch_k(attn_merge_parts_kernel<512>, dim3(T * num_q), dim3(512), 0, s, pl, out);
+}
 
 // KV splits per (token, KV head): enough CTAs for every SM several times
 // over, at least 64 positions per split, at most 64 splits.
@@ -537,6 +614,7 @@ cudaError_t launch_attn_decode(const int8_t* q_i8, const float* f_q, const int8_
                            num_q, num_kv, window, cache_degree, rank, shift, row_mask, page_mask, n_splits,
                            partials);
   if (e != cudaSuccess) return e;
+  if (!out) return cudaSuccess;  // the caller reduces the splits (launch_attn_rank_partial)
   if (head_dim == 256)
     return launch_k(attn_merge_kernel<256>, dim3(T * num_q), dim3(256), 0, s, (const float*)partials,
                     n_splits, out);

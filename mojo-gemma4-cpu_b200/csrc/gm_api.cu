@@ -1839,6 +1839,49 @@ int gm_bq_attention_decode(const int8_t* q_i8, const float* f_q, const int8_t* k
         "bq_attention_decode");
 }
 
+size_t gm_bq_attention_partial_bytes(int T, int head_dim, int num_q) {
+  if (T <= 0 || num_q <= 0 || (head_dim != 256 && head_dim != 512)) return 0;
+  return (size_t)T * num_q * (head_dim + 2) * sizeof(float);
+}
+
+int gm_bq_attention_partial(const int8_t* q_i8, const float* f_q, const int8_t* k_cache,
+                            const float* k_scale, const int8_t* v_cache, const float* v_scale,
+                            const gm_kv_run_t* runs, const int32_t* base_rows, int T, int head_dim,
+                            int num_q, int num_kv, int window, int cache_degree, int rank, int page_shift,
+                            int row_mask, int page_mask, int max_kv_len, float* partial,
+                            float* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_attn_geometry(head_dim, num_q, num_kv, cache_degree, rank);
+  if (rc) return rc;
+  if (T < 0 || window < 0 || max_kv_len < 0 || !partial)
+    return set_err(nullptr, GM_EINVAL, "attention_partial: T=%d window=%d max_kv_len=%d", T, window, max_kv_len);
+  if (cache_degree > 1 && window > 0)
+    return set_err(nullptr, GM_EINVAL, "attention_partial: a sliding window keeps every position on each "
+                   "rank (cache_degree 1)");
+  const size_t need = gm_bq_attention_workspace_bytes(T, head_dim, num_q, num_kv, max_kv_len);
+  if (workspace_bytes < need)
+    return set_err(nullptr, GM_EINVAL, "attention_partial: workspace %zu bytes, %zu needed", workspace_bytes,
+                   need);
+  cudaError_t e = launch_attn_decode(q_i8, f_q, k_cache, k_scale, v_cache, v_scale, runs, base_rows, T,
+                                     head_dim, num_q, num_kv, window, cache_degree, rank, page_shift, row_mask,
+                                     page_mask, max_kv_len, workspace, nullptr, S(stream));
+  if (e == cudaSuccess)
+    e = launch_attn_rank_partial(workspace, T, num_q, head_dim, attention_splits(T, num_kv, max_kv_len),
+                                 partial, S(stream));
+  return cuda_check(nullptr, e, "bq_attention_partial");
+}
+
+int gm_bq_attention_merge(const float* const* partials, int n_parts, int T, int num_q, int head_dim, void* out,
+                          void* stream) {
+  if (!partials || n_parts < 1 || n_parts > 8 || T < 0 || num_q <= 0 || (head_dim != 256 && head_dim != 512) ||
+      !out)
+    return set_err(nullptr, GM_EINVAL, "attention_merge: n_parts=%d (1..8) T=%d num_q=%d head_dim=%d", n_parts, T,
+                   num_q, head_dim);
+  for (int r = 0; r < n_parts; ++r)
+    if (!partials[r]) return set_err(nullptr, GM_EINVAL, "attention_merge: partial %d is NULL", r);
+  STAGE(launch_attn_merge_parts(partials, n_parts, T, num_q, head_dim, static_cast<uint16_t*>(out), S(stream)),
+        "bq_attention_merge");
+}
+
 int gm_phase1_gate_up_bf16(const void* x_normed, const int32_t* expert_offset,
                            const gm_sparse_route_t* routes, const int32_t* chunk_off, int epr,
                            int T, const void* gate_up, void* bucket, void* stream) {

@@ -156,6 +156,13 @@ cudaError_t launch_attn_decode(const int8_t* q_i8, const float* f_q, const int8_
                                int num_kv, int window, int cache_degree, int rank, int shift, int row_mask,
                                int page_mask, int max_kv_len, float* partials, uint16_t* out, cudaStream_t s);
 int attention_splits(int T, int num_kv, int max_kv_len);
+// splits of launch_attn_decode (out == NULL) reduced to one unnormalised
+// (m, l, acc) per (token, head) [T*num_q][head_dim + 2]; the ranks' partials
+// merged in rank order and normalised into bf16 [T][num_q*head_dim]
+cudaError_t launch_attn_rank_partial(const float* partials, int T, int num_q, int head_dim, int n_splits,
+                                     float* part, cudaStream_t s);
+cudaError_t launch_attn_merge_parts(const float* const* parts, int n, int T, int num_q, int head_dim,
+                                    uint16_t* out, cudaStream_t s);
 size_t attention_workspace_floats(int T, int head_dim, int num_q, int num_kv, int max_kv_len);
 // tcgen05 path of the dense MLP (gemm_tc.cu): maps over the activation rows
 // (int8 [rows][2816], 128-row boxes), the row-major gate|up weight ([4224][2816],

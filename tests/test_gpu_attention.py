@@ -217,3 +217,58 @@ def test_reference_attention_scenario_on_gpu(full):
                                        fq_o[t, h], h, full=full)
                 worst = max(worst, float(np.abs(got[t, h * hd:(h + 1) * hd] - ref).max()))
     assert worst <= S.TOL, worst
+
+
+@pytest.mark.parametrize("degree", [2, 4])
+def test_sharded_full_cache_partials_and_merge(degree):
+    """A full-layer cache sharded by position over `degree` ranks (position p
+    on rank p % degree at row p // degree, kernels/attention_ops.mojo:167-173):
+    each rank's gm_bq_attention_partial over its positions, merged in rank
+    order by gm_bq_attention_merge (kernels/logsum_merge.mojo:29-117), equals
+    the unsharded decode within the attention tolerance and the float64
+    softmax within 1e-2 of max|ref|; a rank that holds no position of a token
+    (position 0 on rank 1) contributes nothing."""
+    cfg = FULL
+    hd, nq, nkv = cfg["head_dim"], cfg["num_q"], cfg["num_kv"]
+    rng = np.random.default_rng(77 + degree)
+    positions = [0, 1, 5, 64, 200, 511]
+    c = decode_case(cfg, 0, -1, positions, rng)
+    T = len(positions)
+    runs = dev(runs_array(c["runs"]))
+    ws_bytes = gmoe.lib().gm_bq_attention_workspace_bytes(T, hd, nq, nkv, c["max_kv"])
+    ws = torch.empty(ws_bytes // 4, dtype=torch.float32, device="cuda")
+    whole = torch.empty(T, nq * hd, dtype=torch.bfloat16, device="cuda")
+    gmoe.call("gm_bq_attention_decode", dev(c["q_i8"]), dev(c["fq"]), dev(c["kc"]), dev(c["ks"]),
+              dev(c["vc"]), dev(c["vs"]), runs, dev(c["base_rows"]), T, hd, nq, nkv, 0, 1, 0, SHIFT,
+              PAGE - 1, -1, c["max_kv"], whole, ws, ws_bytes, None)
+    pbytes = gmoe.lib().gm_bq_attention_partial_bytes(T, hd, nq)
+    parts = []
+    for r in range(degree):
+        kc, ks = np.zeros_like(c["kc"]), np.zeros_like(c["ks"])
+        vc, vs = np.zeros_like(c["vc"]), np.zeros_like(c["vs"])
+        for t, pmax in enumerate(positions):
+            for p in range(r, pmax + 1, degree):
+                src = slot_of(c["base_rows"], c["runs"][t], p, -1)
+                dst = slot_of(c["base_rows"], c["runs"][t], p // degree, -1)
+                kc[dst], ks[dst], vc[dst], vs[dst] = c["kc"][src], c["ks"][src], c["vc"][src], c["vs"][src]
+        part = torch.empty(pbytes // 4, dtype=torch.float32, device="cuda")
+        gmoe.call("gm_bq_attention_partial", dev(c["q_i8"]), dev(c["fq"]), dev(kc), dev(ks), dev(vc), dev(vs),
+                  runs, dev(c["base_rows"]), T, hd, nq, nkv, 0, degree, r, SHIFT, PAGE - 1, -1, c["max_kv"],
+                  part, ws, ws_bytes, None)
+        parts.append(part)
+    out = torch.empty(T, nq * hd, dtype=torch.bfloat16, device="cuda")
+    ptrs = (gmoe.C.c_void_p * degree)(*[p.data_ptr() for p in parts])
+    gmoe.check(gmoe.lib().gm_bq_attention_merge(ptrs, degree, T, nq, hd, out.data_ptr(), None))
+    torch.cuda.synchronize()
+    got = O.bf16_to_f32(host(out)).astype(np.float64)
+    ref = decode_f64(c["q_i8"], c["fq"], c["kc"], c["ks"], c["vc"], c["vs"], c["slots"], c["kv_len"], cfg)
+    scale = np.abs(ref).max()
+    assert np.abs(got - O.bf16_to_f32(host(whole))).max() <= 1e-2 * scale
+    assert np.abs(got - ref).max() <= 1e-2 * scale
+    # position 0's token lives on rank 0 alone: its rank-1 partial is empty
+    p1 = host(parts[1]).reshape(T, nq, hd + 2)
+    assert (p1[0, :, 1] == 0).all()
+    with pytest.raises(gmoe.GmoeError, match="GM_EINVAL"):  # sliding windows are never sharded
+        gmoe.call("gm_bq_attention_partial", dev(c["q_i8"]), dev(c["fq"]), dev(c["kc"]), dev(c["ks"]),
+                  dev(c["vc"]), dev(c["vs"]), runs, dev(c["base_rows"]), T, hd, nq, nkv, 64, degree, 0, SHIFT,
+                  PAGE - 1, -1, c["max_kv"], parts[0], ws, ws_bytes, None)
