@@ -544,6 +544,24 @@ int gm_bq_attention_decode(const int8_t* q_i8, const float* f_q, const int8_t* k
                            float* workspace, size_t workspace_bytes, void* stream);
 size_t gm_bq_attention_workspace_bytes(int T, int head_dim, int num_q, int num_kv, int max_kv_len);
 
+/* The prefill path of the same dispatchers (attention.mojo:150-332
+ * BqFlashPrefillSliding / BqFlashPrefillFull at cache_degree 1): runs as
+ * gm_bq_attn_prep takes them (num_runs runs in buf_start order, a run's
+ * tokens at consecutive positions from base_pos), every token attending to
+ * its own causal range of its run -- sliding (window > 0): the last
+ * min(pos+1, window) positions, full (window = 0): 0..pos -- in the cache the
+ * prep has written.  Each CTA serves a tile of consecutive tokens, so one K/V
+ * row read is shared by the tile's tokens and the GQA group's heads.  The
+ * Gemma-4 geometries only: head_dim 256 with num_q = 2*num_kv (sliding) and
+ * head_dim 512 with num_q = 8*num_kv (full).  out bf16 [T][num_q*head_dim]
+ * (same tolerance to the reference as the decode: the accumulation order of
+ * its tiles is not the reference's).  No workspace. */
+int gm_bq_attention_prefill(const int8_t* q_i8, const float* f_q, const int8_t* k_cache,
+                            const float* k_scale, const int8_t* v_cache, const float* v_scale,
+                            const gm_kv_run_t* runs, int num_runs, const int32_t* base_rows, int T,
+                            int head_dim, int num_q, int num_kv, int window, int page_shift, int row_mask,
+                            int page_mask, void* out, void* stream);
+
 /* A full-layer cache sharded by position over cache_degree ranks (the
  * reference's full attention at degree > 1, attention.mojo:236-332 with
  * kernels/logsum_merge.mojo:29-117): gm_bq_attention_partial computes, on one

@@ -448,6 +448,241 @@ attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_
   }
 }
 
+// Prefill (butterquant_kernels/attention.mojo:150-332 BqFlashPrefillSliding /
+// BqFlashPrefillFull at degree 1): every token of a chunk attends to its own
+// causal range of its run -- sliding: [max(0, p - window + 1), p], full:
+// [0, p] -- over the cache the prep has just written.  CTA = (QT consecutive
+// tokens, KV head g): its C = QT * G (token, head) columns share every K/V
+// tile, so each cache row is read once per QT tokens instead of once per
+// token.  Per tile of PF_TP positions (cp.async double buffer):
+//  A. scores on the tensor cores (mma.m16n8k32 s8): positions are M, the
+//     columns N (C / 8 N-tiles), K split over the 8 warps, exact int32 sums;
+//  B. online softmax per column (warp w owns columns w, w + 8, ...), with the
+//     positions outside a column's range (causal / window / other run)
+//     masked;
+//  C. PV on the CUDA cores: thread i owns columns [i*CPT, (i+1)*CPT) of the
+//     head dimension for every column, each V row converted once.
+// The tile's tokens may span runs (sequences): the runs are visited in turn,
+// each over the union of its tokens' ranges.  Output bf16(acc / l).
+constexpr int PF_TP = 16;
+
+template <int HD, int G, int QT>
+__global__ void __launch_bounds__(DEC_THREADS)
+attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_q,
+                    const int8_t* __restrict__ k_cache, const float* __restrict__ k_scale,
+                    const int8_t* __restrict__ v_cache, const float* __restrict__ v_scale,
+                    const KvRun* __restrict__ runs, int num_runs, const int32_t* __restrict__ base_rows,
+                    int T, int num_q, int num_kv, int window, int shift, int row_mask, int page_mask,
+                    uint16_t* __restrict__ out) {
+  using Sm = DecodeSmem<HD>;
+  static_assert(Sm::TP == PF_TP, "tile size");
+  constexpr int C = QT * G;                       // (token, head) columns
+  constexpr int NT = C / 8;                       // mma N-tiles
+  constexpr int NW = DEC_WARPS;
+  constexpr int CPT = HD / DEC_THREADS;           // head-dim columns per thread
+  constexpr int CPW = C / NW;                     // softmax columns per warp
+  constexpr int KSW = HD / 32 / NW;               // 32-wide K steps per warp
+  constexpr int TPR = DEC_THREADS / PF_TP;        // copying threads per row
+  constexpr int CHUNKS = HD / (16 * TPR);
+  static_assert(C % 8 == 0 && C % NW == 0 && CPT >= 1 && KSW >= 1 && CHUNKS >= 1, "tile geometry");
+  const int t0 = blockIdx.x * QT, g = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grp = lane >> 2, tig = lane & 3;
+  extern __shared__ __align__(16) uint8_t dsm[];
+  Sm& sm = *reinterpret_cast<Sm*>(dsm);
+  __shared__ __align__(16) int8_t qs[C * HD];
+  __shared__ int part[NW][C][PF_TP];
+  __shared__ __align__(16) float wv[PF_TP][C];
+  __shared__ float corr_s[C];
+  __shared__ float l_s[C];
+
+  pdl_wait();
+  pdl_trigger();
+  // the tile's queries: column col = tq * G + h is token t0 + tq, head g*G + h
+  for (int i = tid; i < C * HD / 16; i += DEC_THREADS) {
+    const int col = i / (HD / 16), u = i % (HD / 16);
+    const int t = t0 + col / G;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (t < T) v = __ldg(reinterpret_cast<const int4*>(q_i8 + ((size_t)t * num_q + g * G + col % G) * HD) + u);
+    reinterpret_cast<int4*>(qs)[i] = v;
+  }
+  __syncthreads();
+  uint32_t bq[KSW][NT][2];
+#pragma unroll
+  for (int ks = 0; ks < KSW; ++ks)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int k0 = (warp * KSW + ks) * 32 + 4 * tig;
+      const int8_t* qc = qs + (nt * 8 + grp) * HD + k0;
+      bq[ks][nt][0] = *reinterpret_cast<const uint32_t*>(qc);
+      bq[ks][nt][1] = *reinterpret_cast<const uint32_t*>(qc + 16);
+    }
+
+  const float inv127 = 1.0f / 127.0f;
+  const float inv127sq = __fmul_rn(inv127, inv127);
+  float fq[CPW], m[CPW], l[CPW];
+#pragma unroll
+  for (int j = 0; j < CPW; ++j) {
+    const int col = warp + NW * j, t = t0 + col / G;
+    fq[j] = t < T ? __ldg(f_q + (size_t)t * num_q + g * G + col % G) : 0.0f;
+    m[j] = NEG_BIG;
+    l[j] = 0.0f;
+  }
+  float acc[C][CPT];
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int x = 0; x < CPT; ++x) acc[c][x] = 0.0f;
+
+  const size_t kvs = (size_t)num_kv * HD;
+  const int t_end = min(t0 + QT, T);
+  const int r_first = find_run(runs, num_runs, t0), r_last = find_run(runs, num_runs, t_end - 1);
+  for (int r = r_first; r <= r_last; ++r) {
+    const KvRun run = runs[r];
+    const int run_end = r + 1 < num_runs ? __ldg(&runs[r + 1].buf_start) : T;
+    const int tb = max(t0, run.buf_start), te = min(t_end, run_end);
+    if (tb >= te) continue;
+    // positions of the run's tokens in this tile; the union of their ranges
+    const int pos_b = run.base_pos + (tb - run.buf_start), pos_e = run.base_pos + (te - 1 - run.buf_start);
+    const int p_first = window > 0 ? max(0, pos_b - window + 1) : 0;
+    const int p_last = pos_e;
+    // the owned columns' ranges (empty for tokens outside this run)
+    int c_lo[CPW], c_hi[CPW];
+#pragma unroll
+    for (int j = 0; j < CPW; ++j) {
+      const int t = t0 + (warp + NW * j) / G;
+      if (t >= tb && t < te) {
+        const int p = run.base_pos + (t - run.buf_start);
+        c_lo[j] = window > 0 ? max(0, p - window + 1) : 0;
+        c_hi[j] = p;
+      } else {
+        c_lo[j] = 1;
+        c_hi[j] = 0;
+      }
+    }
+    const int32_t* rows = base_rows + run.rows_off;
+    const int crow = tid / TPR, cpart = tid % TPR;
+    auto issue = [&](int p0, int buf) {
+      const int p = p0 + crow;
+      if (p <= p_last) {
+        const long slot = kv_slot(rows, shift, row_mask, page_mask, p);
+        const int8_t* kr = k_cache + slot * kvs + (size_t)g * HD + cpart * (HD / TPR);
+        const int8_t* vr = v_cache + slot * kvs + (size_t)g * HD + cpart * (HD / TPR);
+#pragma unroll
+        for (int cc = 0; cc < CHUNKS; ++cc) {
+          cp_async16(&sm.k[buf][crow][cpart * (HD / TPR) + 16 * cc], kr + 16 * cc);
+          cp_async16(&sm.v[buf][crow][cpart * (HD / TPR) + 16 * cc], vr + 16 * cc);
+        }
+        if (cpart == 0) cp_async4(&sm.ks[buf][crow], k_scale + slot * num_kv + g);
+        if (cpart == 1) cp_async4(&sm.vs[buf][crow], v_scale + slot * num_kv + g);
+      }
+      cp_async_commit();
+    };
+    issue(p_first, 0);
+    int buf = 0;
+    for (int p0 = p_first; p0 <= p_last; p0 += PF_TP, buf ^= 1) {
+      const int n = min(PF_TP, p_last + 1 - p0);
+      if (p0 + PF_TP <= p_last) {
+        issue(p0 + PF_TP, buf ^ 1);
+        cp_async_wait_group<1>();
+      } else {
+        cp_async_wait_group<0>();
+      }
+      __syncthreads();
+      // ---- A: scores
+      {
+        int cacc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) cacc[nt][i] = 0;
+#pragma unroll
+        for (int ks = 0; ks < KSW; ++ks) {
+          const int k0 = (warp * KSW + ks) * 32 + 4 * tig;
+          const int8_t* r0 = &sm.k[buf][grp][k0];
+          const int8_t* r1 = &sm.k[buf][grp + 8][k0];
+          const uint32_t a0 = *reinterpret_cast<const uint32_t*>(r0), a1 = *reinterpret_cast<const uint32_t*>(r1);
+          const uint32_t a2 = *reinterpret_cast<const uint32_t*>(r0 + 16),
+                         a3 = *reinterpret_cast<const uint32_t*>(r1 + 16);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_s8(cacc[nt], a0, a1, a2, a3, bq[ks][nt][0], bq[ks][nt][1]);
+        }
+        // cacc[nt][0..1]: position grp, columns nt*8 + 2*tig (+1); [2..3]: position grp + 8
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) part[warp][nt * 8 + 2 * tig + (i & 1)][grp + 8 * (i >> 1)] = cacc[nt][i];
+      }
+      __syncthreads();
+      // ---- B: online softmax of the owned columns (lane = position in the tile)
+      {
+        const bool in_tile = lane < n;
+        const float ksc = in_tile ? sm.ks[buf][lane] : 0.0f;
+        const float vsc = in_tile ? sm.vs[buf][lane] : 0.0f;
+        const int pl = lane < PF_TP ? lane : 0;
+        const int p = p0 + lane;
+#pragma unroll
+        for (int j = 0; j < CPW; ++j) {
+          const int col = warp + NW * j;
+          const bool ok = in_tile && p >= c_lo[j] && p <= c_hi[j];
+          int dot = 0;
+#pragma unroll
+          for (int w = 0; w < NW; ++w) dot += part[w][col][pl];
+          const float sc = ok ? __fmul_rn(__fmul_rn(__fmul_rn((float)dot, fq[j]), ksc), inv127sq) : NEG_BIG;
+          const float mn = fmaxf(m[j], warp_max(sc));
+          const float cr = fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(m[j], mn)));
+          const float w = ok ? fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(sc, mn))) : 0.0f;
+          l[j] = __fadd_rn(__fmul_rn(l[j], cr), warp_sum(w));
+          m[j] = mn;
+          if (lane < PF_TP) wv[lane][col] = __fmul_rn(__fmul_rn(w, vsc), inv127);
+          if (lane == 0) corr_s[col] = cr;
+        }
+      }
+      __syncthreads();
+      // ---- C: acc = acc*corr + sum_p v[p] * wv[p]
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const float cr = corr_s[c];
+#pragma unroll
+        for (int x = 0; x < CPT; ++x) acc[c][x] = __fmul_rn(acc[c][x], cr);
+      }
+      for (int pp = 0; pp < n; ++pp) {
+        uint32_t vw;
+        if constexpr (CPT == 2) vw = *reinterpret_cast<const uint16_t*>(&sm.v[buf][pp][tid * CPT]);
+        else vw = (uint32_t)(uint8_t)sm.v[buf][pp][tid * CPT];
+        float v[CPT];
+#pragma unroll
+        for (int x = 0; x < CPT; ++x) v[x] = (float)(int8_t)((vw >> (8 * x)) & 0xFFu);
+#pragma unroll
+        for (int c4 = 0; c4 < C / 4; ++c4) {
+          const float4 w4 = reinterpret_cast<const float4*>(&wv[pp][0])[c4];
+          const float a[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int x = 0; x < CPT; ++x) acc[4 * c4 + u][x] = __fmaf_rn(v[x], a[u], acc[4 * c4 + u][x]);
+        }
+      }
+      __syncthreads();  // this buffer and part / wv / corr_s are reused
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < CPW; ++j) l_s[warp + NW * j] = l[j];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int t = t0 + c / G;
+    if (t >= T) continue;
+    const float lc = l_s[c];
+    const float il = lc > 0.0f ? __fdiv_rn(1.0f, lc) : 0.0f;
+    uint16_t* dst = out + ((size_t)t * num_q + g * G + c % G) * HD + tid * CPT;
+#pragma unroll
+    for (int x = 0; x < CPT; ++x) dst[x] = lc > 0.0f ? f2bf(__fmul_rn(acc[c][x], il)) : (uint16_t)0;
+  }
+}
+
 // kernels/logsum_merge.mojo:29-117: one CTA per (token, head), a thread per column
 template <int HD>
 __global__ void __launch_bounds__(HD)
@@ -528,6 +763,37 @@ attn_merge_parts_kernel(const __grid_constant__ PartList parts, uint16_t* __rest
 }
 
 }  // namespace
+
+cudaError_t launch_attn_prefill(const int8_t* q_i8, const float* f_q, const int8_t* k_cache, const float* k_scale,
+                                const int8_t* v_cache, const float* v_scale, const void* runs, int num_runs,
+                                const int32_t* base_rows, int T, int head_dim, int num_q, int num_kv, int window,
+                                int shift, int row_mask, int page_mask, uint16_t* out, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const int G = num_q / num_kv;
+  const KvRun* r = static_cast<const KvRun*>(runs);
+  // 32 (token, head) columns per CTA: the GQA group's heads times the tokens
+  if (head_dim == 256 && G == 2) {
+    constexpr int QT = 16;
+    auto k = attn_prefill_kernel<256, 2, QT>;
+    const size_t smem = sizeof(DecodeSmem<256>);
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return launch_k(k, dim3((T + QT - 1) / QT, num_kv), dim3(DEC_THREADS), smem, s, q_i8, f_q, k_cache, k_scale,
+                    v_cache, v_scale, r, num_runs, base_rows, T, num_q, num_kv, window, shift, row_mask, page_mask,
+                    out);
+  }
+  if (head_dim == 512 && G == 8) {
+    constexpr int QT = 4;
+    auto k = attn_prefill_kernel<512, 8, QT>;
+    const size_t smem = sizeof(DecodeSmem<512>);
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return launch_k(k, dim3((T + QT - 1) / QT, num_kv), dim3(DEC_THREADS), smem, s, q_i8, f_q, k_cache, k_scale,
+                    v_cache, v_scale, r, num_runs, base_rows, T, num_q, num_kv, window, shift, row_mask, page_mask,
+                    out);
+  }
+  return cudaErrorInvalidValue;
+}
 
 cudaError_t launch_attn_rank_partial(const float* partials, int T, int num_q, int head_dim, int n_splits,
                                      float* part, cudaStream_t s) {

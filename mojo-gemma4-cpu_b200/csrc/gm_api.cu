@@ -1839,6 +1839,24 @@ int gm_bq_attention_decode(const int8_t* q_i8, const float* f_q, const int8_t* k
         "bq_attention_decode");
 }
 
+int gm_bq_attention_prefill(const int8_t* q_i8, const float* f_q, const int8_t* k_cache,
+                            const float* k_scale, const int8_t* v_cache, const float* v_scale,
+                            const gm_kv_run_t* runs, int num_runs, const int32_t* base_rows, int T,
+                            int head_dim, int num_q, int num_kv, int window, int page_shift, int row_mask,
+                            int page_mask, void* out, void* stream) {
+  int rc = check_attn_geometry(head_dim, num_q, num_kv, 1, 0);
+  if (rc) return rc;
+  if (!((head_dim == 256 && num_q == 2 * num_kv) || (head_dim == 512 && num_q == 8 * num_kv)))
+    return set_err(nullptr, GM_EINVAL, "attention_prefill: head_dim %d with %d query heads per KV head is not "
+                   "a Gemma-4 geometry (256 x 2, 512 x 8)", head_dim, num_q / num_kv);
+  if (T < 0 || window < 0 || (T > 0 && (num_runs < 1 || !runs || !out)))
+    return set_err(nullptr, GM_EINVAL, "attention_prefill: T=%d window=%d num_runs=%d", T, window, num_runs);
+  STAGE(launch_attn_prefill(q_i8, f_q, k_cache, k_scale, v_cache, v_scale, runs, num_runs, base_rows, T, head_dim,
+                            num_q, num_kv, window, page_shift, row_mask, page_mask, static_cast<uint16_t*>(out),
+                            S(stream)),
+        "bq_attention_prefill");
+}
+
 size_t gm_bq_attention_partial_bytes(int T, int head_dim, int num_q) {
   if (T <= 0 || num_q <= 0 || (head_dim != 256 && head_dim != 512)) return 0;
   return (size_t)T * num_q * (head_dim + 2) * sizeof(float);

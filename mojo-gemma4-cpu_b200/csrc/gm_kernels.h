@@ -156,6 +156,12 @@ cudaError_t launch_attn_decode(const int8_t* q_i8, const float* f_q, const int8_
                                int num_kv, int window, int cache_degree, int rank, int shift, int row_mask,
                                int page_mask, int max_kv_len, float* partials, uint16_t* out, cudaStream_t s);
 int attention_splits(int T, int num_kv, int max_kv_len);
+// prefill attention over multi-token runs (Gemma-4 geometries: head 256 with
+// 2 query heads per KV head, head 512 with 8)
+cudaError_t launch_attn_prefill(const int8_t* q_i8, const float* f_q, const int8_t* k_cache, const float* k_scale,
+                                const int8_t* v_cache, const float* v_scale, const void* runs, int num_runs,
+                                const int32_t* base_rows, int T, int head_dim, int num_q, int num_kv, int window,
+                                int shift, int row_mask, int page_mask, uint16_t* out, cudaStream_t s);
 // splits of launch_attn_decode (out == NULL) reduced to one unnormalised
 // (m, l, acc) per (token, head) [T*num_q][head_dim + 2]; the ranks' partials
 // merged in rank order and normalised into bf16 [T][num_q*head_dim]

@@ -85,6 +85,7 @@ SIGNATURES = {
     "gm_bq_block_linear_ex": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp, _vp, _i32, _vp, _vp]),
     "gm_bq_attn_prep": (_i32, [_vp] * 14 + [_vp, _i32, _vp] + [_i32] * 11 + [_vp]),
     "gm_bq_attention_decode": (_i32, [_vp] * 8 + [_i32] * 11 + [_vp, _vp, _sz, _vp]),
+    "gm_bq_attention_prefill": (_i32, [_vp] * 7 + [_i32, _vp] + [_i32] * 8 + [_vp, _vp]),
     "gm_bq_attention_workspace_bytes": (_sz, [_i32] * 5),
     "gm_bq_attention_partial_bytes": (_sz, [_i32] * 3),
     "gm_bq_attention_partial": (_i32, [_vp] * 8 + [_i32] * 11 + [_vp, _vp, _sz, _vp]),

@@ -198,8 +198,14 @@ def test_reference_attention_scenario_on_gpu(full):
         out = torch.empty(T, nq * hd, dtype=torch.bfloat16, device="cuda")
         gmoe.call("gm_bq_attention_decode", q_i8, fq, kc, ks, vc, vs, dev(tok_runs), base_rows, T,
                   hd, nq, nkv, window, 1, 0, 6, S.PAGE_LEN - 1, page_mask, max_kv, out, ws, wsb, None)
+        # the prefill kernel over the prep's own runs gives the same outputs
+        pout = torch.empty_like(out)
+        gmoe.call("gm_bq_attention_prefill", q_i8, fq, kc, ks, vc, vs, dev(prep_runs), len(runs), base_rows, T,
+                  hd, nq, nkv, window, 6, S.PAGE_LEN - 1, page_mask, pout, None)
         torch.cuda.synchronize()
         assert np.array_equal(host(q_i8), q_o) and np.array_equal(host(fq), fq_o)
+        pgot = O.bf16_to_f32(host(pout))
+        assert np.abs(pgot - O.bf16_to_f32(out_o)).max() <= 2e-2
         kc_o, ks_o, vc_o, vs_o = cache_o
         assert np.array_equal(host(kc), kc_o) and np.array_equal(host(vc), vc_o)
         assert np.array_equal(host(ks), ks_o) and np.array_equal(host(vs), vs_o)
@@ -215,7 +221,8 @@ def test_reference_attention_scenario_on_gpu(full):
             for h in range(nq):
                 ref = S.reference_head(kc_o, ks_o, vc_o, vs_o, seq, p, q_o[t, h * hd:(h + 1) * hd],
                                        fq_o[t, h], h, full=full)
-                worst = max(worst, float(np.abs(got[t, h * hd:(h + 1) * hd] - ref).max()))
+                worst = max(worst, float(np.abs(got[t, h * hd:(h + 1) * hd] - ref).max()),
+                            float(np.abs(pgot[t, h * hd:(h + 1) * hd] - ref).max()))
     assert worst <= S.TOL, worst
 
 
@@ -272,3 +279,68 @@ def test_sharded_full_cache_partials_and_merge(degree):
         gmoe.call("gm_bq_attention_partial", dev(c["q_i8"]), dev(c["fq"]), dev(c["kc"]), dev(c["ks"]),
                   dev(c["vc"]), dev(c["vs"]), runs, dev(c["base_rows"]), T, hd, nq, nkv, 64, degree, 0, SHIFT,
                   PAGE - 1, -1, c["max_kv"], parts[0], ws, ws_bytes, None)
+
+
+@pytest.mark.parametrize("cfg,window", [(SLIDING, 128), (SLIDING, 1024), (FULL, 0)],
+                         ids=["sliding-128", "sliding-1024", "full"])
+def test_attention_prefill_chunks(cfg, window):
+    """gm_bq_attention_prefill (attention.mojo:150-332) over two runs of one
+    step -- a 300-token chunk continuing a sequence at position 500 and a new
+    37-token sequence -- on randomly placed pages: every token equals the
+    decode kernel's output for the same token (each token as the newest
+    position of its own run) and a float64 softmax, within 1e-2 of max|ref|."""
+    rng = np.random.default_rng(150 + window)
+    hd, nq, nkv = cfg["head_dim"], cfg["num_q"], cfg["num_kv"]
+    seqs = [(500, 300), (0, 37)]  # (first position, tokens)
+    pages = [(p0 + n + PAGE - 1) // PAGE for p0, n in seqs]
+    perm = rng.permutation(sum(pages))
+    base_rows = (perm * PAGE).astype(np.int32)
+    rows_off = [0, pages[0]]
+    runs, tok_runs, positions = [], [], []
+    for i, (p0, n) in enumerate(seqs):
+        runs.append((len(positions), p0, rows_off[i], pages[i]))
+        for j in range(n):
+            tok_runs.append((len(positions), p0 + j, rows_off[i], pages[i]))
+            positions.append((i, p0 + j))
+    T = len(positions)
+    kc, ks, vc, vs = random_cache(rng, sum(pages) * PAGE, cfg)
+    ks *= 0.03
+    q_i8 = rng.integers(-127, 128, size=(T, nq * hd), dtype=np.int8)
+    fq = (rng.random((T, nq)) + 0.5).astype(np.float32)
+    max_kv = max(min(p + 1, window) if window else p + 1 for _, p in positions)
+    dq, dfq, dkc, dks, dvc, dvs, drows = (dev(x) for x in (q_i8, fq, kc, ks, vc, vs, base_rows))
+    out = torch.empty(T, nq * hd, dtype=torch.bfloat16, device="cuda")
+    gmoe.call("gm_bq_attention_prefill", dq, dfq, dkc, dks, dvc, dvs, dev(runs_array(runs)), len(runs), drows, T,
+              hd, nq, nkv, window, SHIFT, PAGE - 1, -1, out, None)
+    ws_bytes = gmoe.lib().gm_bq_attention_workspace_bytes(T, hd, nq, nkv, max_kv)
+    ws = torch.empty(ws_bytes // 4, dtype=torch.float32, device="cuda")
+    dec = torch.empty_like(out)
+    gmoe.call("gm_bq_attention_decode", dq, dfq, dkc, dks, dvc, dvs, dev(runs_array(tok_runs)), drows, T, hd, nq,
+              nkv, window, 1, 0, SHIFT, PAGE - 1, -1, max_kv, dec, ws, ws_bytes, None)
+    torch.cuda.synchronize()
+    got = O.bf16_to_f32(host(out)).astype(np.float64)
+    want = O.bf16_to_f32(host(dec)).astype(np.float64)
+    scale = np.abs(want).max()
+    assert np.abs(got - want).max() <= 1e-2 * scale
+    # float64 on a sample of tokens: both ends of each run and its window edge
+    sample = sorted({0, 1, 15, 16, 17, 63, 64, 299, 300, 301, 320, T - 1})
+    slots = np.zeros((len(sample), max_kv), np.int32)
+    kv_len = np.zeros(len(sample), np.int32)
+    for k, t in enumerate(sample):
+        i, p = positions[t]
+        valid = min(p + 1, window) if window else p + 1
+        start = p - valid + 1
+        kv_len[k] = valid
+        for j in range(valid):
+            q = start + j
+            slots[k, j] = base_rows[rows_off[i] + (q >> SHIFT)] + (q & (PAGE - 1))
+    ref = decode_f64(q_i8[sample], fq[sample], kc, ks, vc, vs, slots, kv_len, cfg)
+    assert np.abs(got[sample] - ref).max() <= 1e-2 * scale
+
+
+def test_attention_prefill_argument_checks():
+    z = torch.zeros(16, dtype=torch.int8, device="cuda")
+    with pytest.raises(gmoe.GmoeError, match="GM_EINVAL"):  # 4 query heads per KV head at 256
+        gmoe.call("gm_bq_attention_prefill", z, z, z, z, z, z, z, 1, z, 1, 256, 16, 4, 0, 6, 63, -1, z, None)
+    with pytest.raises(gmoe.GmoeError, match="GM_EINVAL"):  # tokens without runs
+        gmoe.call("gm_bq_attention_prefill", z, z, z, z, z, z, z, 0, z, 1, 512, 16, 2, 0, 6, 63, -1, z, None)
