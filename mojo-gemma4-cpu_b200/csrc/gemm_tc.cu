@@ -101,19 +101,11 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t da, uint64_t db
 // DENSE: the dense MLP's gate/up product (dense_bq.cu's mathematics, gate and
 // up rounded to bf16 before GeGLU) over dense_rows token rows in order, as one
 // "expert" with 2112 intermediate columns: B rows [0, 2112) gate, [2112, 4224) up.
-// MoE (!DENSE): the A operand is gathered by the producer warp itself -- row r
-// of a tile is activation row routes[row0 + r].token of x_rows ([T][2816]
-// int8, scale x_sa) -- with 16-byte cp.async copies into the stage's
-// 128-byte-swizzled K-major layout; each lane's copies complete on the
-// stage's full barrier (cp.async.mbarrier.arrive.noinc), so no gathered copy
-// of the routed rows is made.  DENSE: A is the token rows in order, by TMA
-// (map_a), and x_sa is indexed by row.
 template <bool DENSE>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                  const int32_t* __restrict__ expert_offset, int epr, int dense_rows,
-                 const int8_t* __restrict__ x_rows, const SparseRoute* __restrict__ routes,
-                 const float* __restrict__ x_sa, const float* __restrict__ gu_scale,
+                 const float* __restrict__ xg_sa, const float* __restrict__ gu_scale,
                  int8_t* __restrict__ bucket_i8, float* __restrict__ bucket_sa,
                  uint16_t* __restrict__ bucket_bf16, int* __restrict__ err, int max_rows,
                  int max_tiles) {
@@ -128,8 +120,7 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   pdl_trigger();
   if (tid == 0) {
     for (int i = 0; i < STAGES1; ++i) {
-      // MoE: the expect_tx arrival plus one cp.async arrival per producer lane
-      mbar_init(&s.full[i], DENSE ? 1 : 33);
+      mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -170,52 +161,26 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   }
 
   if (warp == 0) {
-    // ---------------- producer: B (and DENSE's A) by TMA from lane 0; the
-    // MoE A rows gathered by all 32 lanes (rows lane + 32*i)
-    int stage = 0;
-    uint32_t phase = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const TileInfo ti = tile_info(s.tt, epr, NJ, t);
-      const int brow_g = ti.e * GUW + ti.col * 64;
-      const int brow_u = ti.e * GUW + IW + ti.col * 64;
-      const int8_t* src_row[4];
-      if constexpr (!DENSE) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = lane + 32 * i;
-          // rows past the expert's routes are zero-filled (source size 0)
-          src_row[i] = r < ti.nvalid ? x_rows + (size_t)routes[ti.row0 + r].token * H : nullptr;
-        }
-      }
-      for (int kb = 0; kb < KB1; ++kb) {
-        if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done;
-        uint8_t* st = s.stage[stage];
-        if (lane == 0) {
-          mbar_expect_tx(&s.full[stage], DENSE ? STAGE_BYTES : B_BYTES);
-          if constexpr (DENSE) tma_load_2d(st, &map_a, kb * BK, ti.row0, &s.full[stage]);
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        const TileInfo ti = tile_info(s.tt, epr, NJ, t);
+        const int brow_g = ti.e * GUW + ti.col * 64;
+        const int brow_u = ti.e * GUW + IW + ti.col * 64;
+        for (int kb = 0; kb < KB1; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1, &s.failed)) goto producer_done;
+          uint8_t* st = s.stage[stage];
+          mbar_expect_tx(&s.full[stage], STAGE_BYTES);
+          tma_load_2d(st, &map_a, kb * BK, ti.row0, &s.full[stage]);
           tma_load_2d(st + A_BYTES, &map_b, kb * BK, brow_g, &s.full[stage]);
           tma_load_2d(st + A_BYTES + B_BYTES / 2, &map_b, kb * BK, brow_u, &s.full[stage]);
+          if (++stage == STAGES1) { stage = 0; phase ^= 1; }
         }
-        if constexpr (!DENSE) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int r = lane + 32 * i;
-            const int8_t* src = src_row[i] ? src_row[i] + kb * BK : x_rows;
-            const uint32_t n = src_row[i] ? 16u : 0u;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;"
-                           ::"r"(smem_u32(st + r * 128 + ((j ^ (r & 7)) << 4))), "l"(src + (n ? 16 * j : 0)),
-                             "r"(n)
-                           : "memory");
-          }
-          asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&s.full[stage]))
-                       : "memory");
-        }
-        if (++stage == STAGES1) { stage = 0; phase ^= 1; }
       }
+    producer_done:;
     }
-  producer_done:;
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
@@ -231,9 +196,6 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         for (int kb = 0; kb < KB1; ++kb) {
           if (!mbar_wait(&s.full[stage], phase, &s.failed)) { ok = false; break; }
           tc_fence_after();
-          // the gathered A rows are generic-proxy writes (cp.async): make them
-          // visible to the tensor core's async-proxy reads
-          if constexpr (!DENSE) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           const uint32_t a0 = smem_u32(s.stage[stage]);
           const uint32_t b0 = a0 + A_BYTES;
 #pragma unroll
@@ -262,8 +224,7 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       // per-tile operands are loaded before the accumulator wait
       const bool valid = r < ti.nvalid;
       const int row = ti.row0 + r;
-      const float ad =
-          valid ? __fmul_rn(x_sa[DENSE ? row : routes[row].token], inv127) : 0.0f;
+      const float ad = valid ? __fmul_rn(xg_sa[row], inv127) : 0.0f;
       const float* wsg = gu_scale + (size_t)ti.e * GUW + ti.col * 64 + 16 * cb;
       float sg[16], su[16];
 #pragma unroll
@@ -665,21 +626,20 @@ cudaError_t launch_gather_rows(const void* x, int row_bytes, const float* xsa,
                   static_cast<uint8_t*>(xg), xg_sa);
 }
 
-cudaError_t launch_tc_phase1(const void* map_b, const int32_t* expert_offset, int epr, int T,
-                             const int8_t* x_rows, const SparseRoute* routes, const float* x_sa,
-                             const float* gu_scale, int8_t* bucket_i8, float* bucket_sa,
-                             uint16_t* bucket_bf16, int* err, cudaStream_t s) {
+cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t* expert_offset,
+                             int epr, int T, const float* xg_sa, const float* gu_scale,
+                             int8_t* bucket_i8, float* bucket_sa, uint16_t* bucket_bf16, int* err,
+                             cudaStream_t s) {
   const int max_rows = T * TOPK;
   const int max_tiles = (max_rows / tc::BM + epr) * tc::NJ1;
   const size_t smem = sizeof(tc::Smem1) + 1024;
   auto k = tc::tc_phase1_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  // map_a is unused by the MoE variant (the producer gathers A itself)
   return launch_k(k, dim3(sm_count()), dim3(tc::THREADS), smem, s,
-                  *reinterpret_cast<const CUtensorMap*>(map_b),
-                  *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, 0, x_rows, routes, x_sa,
-                  gu_scale, bucket_i8, bucket_sa, bucket_bf16, err, max_rows, max_tiles);
+                  *reinterpret_cast<const CUtensorMap*>(map_a),
+                  *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, 0, xg_sa, gu_scale,
+                  bucket_i8, bucket_sa, bucket_bf16, err, max_rows, max_tiles);
 }
 
 cudaError_t launch_tc_dense_gate_up(const void* map_x, const void* map_w, int T, const float* xsa,
@@ -693,8 +653,8 @@ cudaError_t launch_tc_dense_gate_up(const void* map_x, const void* map_w, int T,
   if (e != cudaSuccess) return e;
   return launch_k(k, dim3(std::min(sm_count(), tiles)), dim3(tc::THREADS), smem, s,
                   *reinterpret_cast<const CUtensorMap*>(map_x),
-                  *reinterpret_cast<const CUtensorMap*>(map_w), nullptr, 1, T, nullptr, nullptr, xsa,
-                  gu_scale, h_i8, h_sa, h_bf16, err, T, tiles);
+                  *reinterpret_cast<const CUtensorMap*>(map_w), nullptr, 1, T, xsa, gu_scale, h_i8,
+                  h_sa, h_bf16, err, T, tiles);
 }
 
 cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,

@@ -88,9 +88,12 @@ struct gm_moe {
   float* ybuf = nullptr;
   uint16_t* x_stage = nullptr;
   uint16_t* out_stage = nullptr;
+  int8_t* xg = nullptr;         // routed activation rows in schedule order (tcgen05 A operand)
+  float* xg_sa = nullptr;
   int* dev_err = nullptr;       // device-side error word (bounded waits that expired)
   int32_t* sched_counts = nullptr;  // per-chunk expert counts of the multi-CTA schedule
   int* router_counts = nullptr;     // router tile counters (zero between calls)
+  alignas(64) unsigned char tmap_xg[128] = {};
   alignas(64) unsigned char tmap_bucket[128] = {};
   alignas(64) unsigned char tmap_xgb[128] = {};      // bf16 gathered rows (in ybuf's memory)
   alignas(64) unsigned char tmap_bucketb[128] = {};  // bf16 bucket
@@ -219,7 +222,7 @@ struct Carve {
 
 struct WsLayout {
   size_t logits, inv_rms, route_idx, route_w, route_pos, expert_offset, chunk_off, routes, x_i8, x_sa,
-      x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, dev_err,
+      x_normed, bucket, bucket_i8, bucket_sa, ybuf, x_stage, out_stage, xg, xg_sa, dev_err,
       sched_counts, router_counts, d_xi8, d_xsa, d_inv, d_hi8, d_hsa, d_out, total;
 };
 
@@ -246,6 +249,8 @@ WsLayout ws_layout(int max_tokens) {
   L.ybuf = c.take<float>(R * H);
   L.x_stage = c.take<uint16_t>(T * H);
   L.out_stage = c.take<uint16_t>(T * H);
+  L.xg = c.take<int8_t>(R * H);
+  L.xg_sa = c.take<float>(R);
   L.dev_err = c.take<int>(1);
   L.sched_counts = c.take<int32_t>(schedule_counts_ints(max_tokens));
   L.router_counts = c.take<int>(router_tile_counters(max_tokens));
@@ -351,6 +356,8 @@ int carve_workspace(gm_moe* h, int tokens) {
   h->ybuf = reinterpret_cast<float*>(b + L.ybuf);
   h->x_stage = reinterpret_cast<uint16_t*>(b + L.x_stage);
   h->out_stage = reinterpret_cast<uint16_t*>(b + L.out_stage);
+  h->xg = reinterpret_cast<int8_t*>(b + L.xg);
+  h->xg_sa = reinterpret_cast<float*>(b + L.xg_sa);
   h->dev_err = reinterpret_cast<int*>(b + L.dev_err);
   h->sched_counts = reinterpret_cast<int32_t*>(b + L.sched_counts);
   h->router_counts = reinterpret_cast<int*>(b + L.router_counts);
@@ -364,7 +371,8 @@ int carve_workspace(gm_moe* h, int tokens) {
                    make_tmap_i8(h->tmap_dh, h->d_hi8, (long)tokens, DENSE_I, 128);
   cudaMemset(h->dev_err, 0, sizeof(int));
   cudaMemset(h->router_counts, 0, sizeof(int) * router_tile_counters(tokens));
-  h->tc_ok = make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)tokens * TOPK, I, 128);
+  h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)tokens * TOPK, H, 128) &&
+             make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)tokens * TOPK, I, 128);
   // bf16 prefill: the gathered activation rows live in ybuf, which is idle
   // until the down product writes it
   h->tcb_ok = make_tmap_2d(h->tmap_xgb, h->ybuf, (long)tokens * TOPK, H, 2, 128) &&
@@ -567,8 +575,11 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
                         cudaStream_t s) {
   if (L.kind == 1) {
     if (L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
-      // prefill: the tcgen05 GEMMs (phase 1 gathers the routed rows itself)
-      GM_STAGE(h, s, launch_tc_phase1(L.tmap_gu, h->expert_offset, h->epr, Tn, x_i8, h->routes, x_sa,
+      // prefill: routed rows gathered in schedule order, then the tcgen05 GEMMs
+      GM_STAGE(h, s, launch_gather_rows(x_i8, H, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
+                                        h->xg_sa, s),
+               "gather_rows");
+      GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, Tn, h->xg_sa,
                                       L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
                "bq_phase1_gate_up.tc");
       GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, Tn,

@@ -132,12 +132,10 @@ size_t tmap_bytes();
 cudaError_t launch_gather_rows(const void* x, int row_bytes, const float* xsa,
                                const SparseRoute* routes, const int32_t* expert_offset, int epr,
                                int T, void* xg, float* xg_sa, cudaStream_t s);
-// gate/up product over the routed rows of x_rows ([T][2816] int8, scales
-// x_sa), gathered by the kernel in schedule order (routes)
-cudaError_t launch_tc_phase1(const void* map_b, const int32_t* expert_offset, int epr, int T,
-                             const int8_t* x_rows, const SparseRoute* routes, const float* x_sa,
-                             const float* gu_scale, int8_t* bucket_i8, float* bucket_sa,
-                             uint16_t* bucket_bf16, int* err, cudaStream_t s);
+cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t* expert_offset,
+                             int epr, int T, const float* xg_sa, const float* gu_scale,
+                             int8_t* bucket_i8, float* bucket_sa, uint16_t* bucket_bf16, int* err,
+                             cudaStream_t s);
 cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
                              int epr, int T, const float* bsa, const SparseRoute* routes,
                              const float* dn_scale, float* ybuf, int* err, cudaStream_t s);
