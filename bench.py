@@ -65,6 +65,8 @@ EXTRA = {
     "ffn-prefill-4k": ("ffn", 4096),
     "attn-decode-sliding-b64": ("attn-sliding", 64),
     "attn-decode-full-b64": ("attn-full", 64),
+    "attn-prefill-sliding-4k": ("attnp-sliding", 4096),
+    "attn-prefill-full-4k": ("attnp-full", 4096),
 }
 EXTRA_TRAFFIC = {"attn-decode-full-b64": 541_900_000 + 14_200_000}
 DENSE_I = 2112
@@ -356,6 +358,101 @@ def median_rate(fn, units, seconds):
     return units / float(np.median(samples)), len(samples), warm
 
 
+def run_attn_prefill(args, kind, T, stream, hbm):
+    """One prefill chunk of T tokens of one sequence (positions 0..T-1) through
+    gm_bq_attention_prefill: sliding layer (head 256, 16 / 8 heads, window
+    1024) or full layer (head 512, 16 / 2 heads, causal over the chunk).
+    `batches` distinct (q, KV cache) sets are cycled so that the inputs exceed
+    L2.  The bound is the CUDA-core PV product (fp32 FMA per position, head
+    column and query head); QK runs on the int8 tensor cores."""
+    import numpy as np
+    import torch
+    import gmoe
+    hd, nq, nkv, window, _, _ = ATTN["attn" + kind[5:]]
+    PAGE, SHIFT = 64, 6
+    pages = (T + PAGE - 1) // PAGE
+    g = torch.Generator(device="cuda").manual_seed(11)
+    sets = []
+    for _ in range(args.batches):
+        kc = torch.randint(-127, 128, (pages * PAGE, nkv * hd), dtype=torch.int8, device="cuda", generator=g)
+        vc = torch.randint(-127, 128, (pages * PAGE, nkv * hd), dtype=torch.int8, device="cuda", generator=g)
+        ks = torch.rand(pages * PAGE, nkv, device="cuda", generator=g) * 0.03
+        vs = torch.rand(pages * PAGE, nkv, device="cuda", generator=g) + 0.5
+        q = torch.randint(-127, 128, (T, nq * hd), dtype=torch.int8, device="cuda", generator=g)
+        fq = torch.rand(T, nq, device="cuda", generator=g) + 0.5
+        sets.append((q, fq, kc, ks, vc, vs))
+    base = (torch.randperm(pages, device="cuda", generator=g).int() * PAGE).contiguous()
+    runs = torch.tensor([[0, 0, 0, pages]], dtype=torch.int32, device="cuda")
+    out = torch.empty(T, nq * hd, dtype=torch.bfloat16, device="cuda")
+
+    def call(st, q, o):
+        gmoe.call("gm_bq_attention_prefill", q, st[1], st[2], st[3], st[4], st[5], runs, 1, base, T, hd, nq, nkv,
+                  window, SHIFT, PAGE - 1, -1, o, stream)
+
+    def step(i):
+        st = sets[i % len(sets)]
+        call(st, st[0], out)
+    ms = timed(step, args.steps, args.warmup, stream)
+    per_step = ms / args.steps
+    positions = sum(min(p + 1, window) if window else p + 1 for p in range(T))
+    fma = positions * nq * hd                     # PV: one FMA per position, head column, query head
+    # 128 FP32 lanes per SM at the maximum SM clock (2 FLOP per FMA)
+    fp32_peak = 2 * 128 * torch.cuda.get_device_properties(0).multi_processor_count * 1.965e9 / 1e12
+    roof = {"bound": "fp32", "achieved": 2 * fma / (per_step * 1e-3) / 1e12,
+            "peak": fp32_peak, "unit": "TFLOP/s",
+            "note": "PV on the CUDA cores; peak = 128 FP32 FMA lanes x SMs x 1965 MHz (nominal, not measured)"}
+    qh = [st[0].cpu().pin_memory() for st in sets]
+    oh = torch.empty(T, nq * hd, dtype=torch.bfloat16).pin_memory()
+    qd = torch.empty_like(sets[0][0])
+
+    def e2e_step(i):
+        qd.copy_(qh[i % len(qh)], non_blocking=True)
+        call(sets[i % len(sets)], qd, out)
+        oh.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    for i in range(3):
+        e2e_step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e2e_step(i)
+    e2e = T * args.steps / (time.perf_counter() - t0)
+    cpu = None
+    if not args.no_cpu_baseline:
+        O = oracle_native()
+        # a bounded sample: 8 tokens spread over the chunk, each over its own range
+        sample = [int((i + 0.5) * T / 8) for i in range(8)]
+        kv_len = np.array([min(p + 1, window) if window else p + 1 for p in sample], np.int32)
+        slots = np.zeros((len(sample), int(kv_len.max())), np.int32)
+        bh = base.cpu().numpy()
+        for k, p in enumerate(sample):
+            r = np.arange(p - kv_len[k] + 1, p + 1)
+            slots[k, :kv_len[k]] = bh[r >> SHIFT] + (r & (PAGE - 1))
+        st = sets[0]
+        kch, ksh, vch, vsh = (x.cpu().numpy() for x in st[2:])
+        qc = st[0][sample].cpu().numpy()
+        fqc = st[1][sample].cpu().numpy()
+        qbc = (qc.reshape(len(sample), nq, hd).astype(np.int64).sum(-1) * 128).astype(np.float32)
+        rate, n, warm = median_rate(
+            lambda: O.bq_flash_decode(qc, qbc, fqc, kch, ksh, vch, vsh, slots, kv_len, hd, nq, nkv,
+                                      O.lib().orc_num_threads()),
+            len(sample), args.cpu_seconds)
+        # tokens/s of the whole chunk: the sample's mean range stands for the chunk's
+        rate *= float(kv_len.mean()) / (positions / T)
+        cpu = dict({"value": rate, "unit": "tokens/s", "cores": O.lib().orc_num_threads(), "kind": "port",
+                    "sample": "%d warm-up + %d timed calls of 8 tokens spread over the chunk (mean %d KV "
+                              "positions), scaled to the chunk's mean range, median (C++ restatement, "
+                              "OpenMP)" % (warm, n, int(kv_len.mean()))}, **host_info())
+    kv_mb = sum(x.numel() * x.element_size() for st in sets for x in st) / 1e6
+    return {"metric": "prefill attention tokens/s (%s layer, %d-token chunk)" % (kind[6:], T),
+            "dtype": "i8", "config": {"workload": args.workload, "tokens_per_step": T, "head_dim": hd,
+                                      "q_heads": nq, "kv_heads": nkv, "window": window,
+                                      "parallelism": "single",
+                                      "l2": "%d distinct (q, KV cache) sets cycled, %.0f MB (larger than L2)"
+                                            % (len(sets), kv_mb)},
+            "_roof": roof, "_ms": ms, "_per_step": per_step, "_launches": args.steps,
+            "_e2e": e2e, "_e2e_io": (T * nq * hd, T * nq * hd * 2), "_cpu": cpu}
+
+
 def run_extra(args):
     """The FFN and attention workloads (one GPU; see EXTRA)."""
     import numpy as np
@@ -444,6 +541,10 @@ def run_extra(args):
                          "dtype": "i8", "config": {"workload": args.workload, "tokens_per_step": T,
                                                    "weights": "bq", "layers": 1, "parallelism": "single"}})
             blk.close()
+        elif kind.startswith("attnp"):
+            line.update(run_attn_prefill(args, kind, T, stream, hbm))
+            roof, ms, per_step, launches = line.pop("_roof"), line.pop("_ms"), line.pop("_per_step"), line.pop("_launches")
+            e2e, e2e_io, cpu = line.pop("_e2e"), line.pop("_e2e_io"), line.pop("_cpu")
         else:
             hd, nq, nkv, window, kv, ppr = ATTN[kind]
             PAGE, SHIFT = 1024, 10

@@ -248,7 +248,12 @@ int gm_moe_load_layer(gm_moe_t* h, int layer, const gm_checkpoint_t* ck, int ckp
  * compile time).  GM_OPT_TC_MIN_TOKENS: calls with T >= value run the
  * butterquant gate/up product on the tcgen05 grouped GEMM (prefill path),
  * smaller calls on the HBM-streaming decode kernel; both give bit-identical
- * results.  Default 1024.
+ * results.  Default 1024.  The prefill path reads a row-major copy of each
+ * butterquant layer's expert weights, made at registration only when the
+ * handle can reach it (max_tokens times the number of expert shards >=
+ * the value at that time); a decode-only handle keeps the VNNI weights
+ * alone, and layers registered without the copy run every call on the
+ * decode kernels. 
  * GM_OPT_PROFILE: 1 records a CUDA event pair around every stage that
  * gm_moe_forward launches, 0 (default) records none; setting it (either
  * value) clears the stage statistics and the kernel launch count.

@@ -246,7 +246,7 @@ bq_phase1_kernel(const int8_t* __restrict__ xi8, const float* __restrict__ xsa,
 // phase 1's bucket.  Only the fused forward sets it (it always runs phase 1
 // between the schedule and this kernel).
 template <int NTILE, int DEPTH>
-__global__ void __launch_bounds__(32 * NTILE, 5)
+__global__ void __launch_bounds__(32 * NTILE, 4)
 bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
                  const int32_t* __restrict__ expert_offset, const SparseRoute* __restrict__ routes,
                  const int32_t* __restrict__ chunk_off, int epr,
@@ -450,7 +450,8 @@ cudaError_t launch_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t*
                              const int8_t* w_dn, const float* dn_scale, float* ybuf,
                              bool after_phase1, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  constexpr int NTILE = 4, DEPTH = 4;
+  // 8 chunks (8 KB per warp) in flight: 52.2 us at 64 tokens against 54.8 with 4
+  constexpr int NTILE = 4, DEPTH = 8;
   const int items = max_route_chunks(T, epr, RC_BQ) * ((H / 32) / NTILE);
   auto k = bq_phase2_kernel<NTILE, DEPTH>;
   const int grid = resident_grid(k, 32 * NTILE, 0, items);

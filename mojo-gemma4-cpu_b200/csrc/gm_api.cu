@@ -969,14 +969,20 @@ int gm_moe_register_layer_bq(gm_moe_t* h, int layer, const void* gate_up,
   if ((rc = dev_copy(h, &L.pes, per_expert_scale, (size_t)E, "per_expert_scale"))) return rc;
   if ((rc = dev_copy(h, &L.gamma2, pre_ffn_norm_2, (size_t)H, "pre_ffn_norm_2"))) return rc;
   // Row-major (K-contiguous) copy of gate_up for the tcgen05 prefill path: the
-  // VNNI tile order is a byte permutation, undone once here on the device.
-  GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.gu_rm), epr * GU * H), "gate_up row-major copy");
-  GM_TRY(h, launch_vnni_permute(L.gu_q, (long)(epr * GU), H, L.gu_rm, 1, h->own_stream), "vnni unpack");
-  GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.dn_rm), epr * H * I), "down row-major copy");
-  GM_TRY(h, launch_vnni_permute(L.dn_q, (long)(epr * H), I, L.dn_rm, 1, h->own_stream), "vnni unpack");
-  GM_TRY(h, cudaStreamSynchronize(h->own_stream), "vnni unpack");
-  L.has_tc = make_tmap_i8(L.tmap_gu, L.gu_rm, (long)(epr * GU), H, 64) &&
-             make_tmap_i8(L.tmap_dn, L.dn_rm, (long)(epr * H), I, 128);
+  // VNNI tile order is a byte permutation, undone once here on the device.  A
+  // handle that can never reach the prefill path -- the most rows one call
+  // processes (max_tokens, times the expert shards under expert parallelism)
+  // below GM_OPT_TC_MIN_TOKENS -- keeps the VNNI copy only.
+  L.has_tc = false;
+  if ((long long)h->max_tokens * (E / h->epr) >= h->tc_min_tokens) {
+    GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.gu_rm), epr * GU * H), "gate_up row-major copy");
+    GM_TRY(h, launch_vnni_permute(L.gu_q, (long)(epr * GU), H, L.gu_rm, 1, h->own_stream), "vnni unpack");
+    GM_TRY(h, cudaMalloc(reinterpret_cast<void**>(&L.dn_rm), epr * H * I), "down row-major copy");
+    GM_TRY(h, launch_vnni_permute(L.dn_q, (long)(epr * H), I, L.dn_rm, 1, h->own_stream), "vnni unpack");
+    GM_TRY(h, cudaStreamSynchronize(h->own_stream), "vnni unpack");
+    L.has_tc = make_tmap_i8(L.tmap_gu, L.gu_rm, (long)(epr * GU), H, 64) &&
+               make_tmap_i8(L.tmap_dn, L.dn_rm, (long)(epr * H), I, 128);
+  }
   L.kind = 1;
   return GM_OK;
 }
@@ -1503,7 +1509,7 @@ std::vector<std::pair<void*, size_t>> expert_tensors(Layer& L) {
 int finish_placement(gm_moe* h, const std::vector<int32_t>& rank_of, const std::vector<int32_t>& local_of) {
   cudaStream_t s = h->own_stream;
   for (auto& L : h->layers)
-    if (L.kind == 1) {
+    if (L.kind == 1 && L.gu_rm) {
       GM_TRY(h, launch_vnni_permute(L.gu_q, (long)h->epr * GU, H, L.gu_rm, 1, s), "vnni unpack");
       GM_TRY(h, launch_vnni_permute(L.dn_q, (long)h->epr * H, I, L.dn_rm, 1, s), "vnni unpack");
     }

@@ -486,6 +486,46 @@ def test_expert_parallel_partials_match_reference_degree(degree, layer_stress):
     check_forward(out, gidx, rout, ridx, rlg, TOL_BQ)
 
 
+def test_decode_only_handle_keeps_one_weight_copy(layer_stress):
+    """A handle whose calls can never reach the tcgen05 path (max_tokens below
+    GM_OPT_TC_MIN_TOKENS) keeps the VNNI expert weights only: no row-major
+    copy (761 MB per layer) is made, a later lower threshold leaves its calls
+    on the decode kernels, and the output is the tcgen05 path's bit for bit."""
+    raw, ref, g = layer_stress
+    T = 64
+    x = dev(tokens_np(T, seed=77))
+
+    def registered(tc_min):
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        blk = gmoe.MoeBlock(T, 1)
+        if tc_min is not None:
+            blk.set_option(gmoe.OPT_TC_MIN_TOKENS, tc_min)
+        blk.register_bq(0, g["gate_up"], g["gate_up_scale"], g["down"], g["down_scale"], g["router_centered"],
+                        g["router_scale"], g["per_expert_scale"], g["pre_ffn_norm_2"])
+        torch.cuda.synchronize()
+        return blk, free0 - torch.cuda.mem_get_info()[0]
+
+    lean, used_lean = registered(None)
+    lean.set_option(gmoe.OPT_TC_MIN_TOKENS, 1)
+    lean.profile(True)
+    o1 = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    lean.forward(0, x, o1, T)
+    labels = list(lean.profile_read()[0])
+    lean.close()
+    full, used_full = registered(32)
+    full.profile(True)
+    o2 = torch.empty_like(o1)
+    full.forward(0, x, o2, T)
+    labels_tc = list(full.profile_read()[0])
+    full.close()
+    torch.cuda.synchronize()
+    assert "bq_phase1_gate_up" in labels and "bq_phase1_gate_up.tc" not in labels
+    assert "bq_phase1_gate_up.tc" in labels_tc
+    assert used_full - used_lean >= 0.9 * E * (GU * H + H * I)
+    assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+
+
 def test_stage_profiler_labels_and_launch_count(layer_stress):
     """GM_OPT_PROFILE: one record per forward stage under the reference's
     dispatch labels, event times that add up, and the kernel launch count."""
