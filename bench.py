@@ -87,6 +87,9 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0,
                    help="bounded CPU-baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--tokens", type=int, default=0,
+                   help="profiling small cases: tokens per GPU instead of the workload's (the line's config "
+                        "records the override; not a bench number)")
     p.add_argument("--batches", type=int, default=8, help="distinct token batches cycled")
     p.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                    help="expert placement of Zipf expert-parallel workloads")
@@ -660,6 +663,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     T, fmt, mode = WORKLOADS[args.workload]
+    if args.tokens > 0:
+        T = args.tokens * (world if mode == "ep-strong" else 1)
     assert args.warmup >= 3, "at least 3 warm-up steps"
     ep = mode.startswith("ep")
     if mode == "ep-strong":
@@ -804,7 +809,8 @@ def main():
         "scaling": "strong" if mode == "ep-strong" else "weak", "vs_baseline": None,
         "dtype": "i8" if fmt == "bq" else "bf16",
         "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights; random-init, no checkpoint)",
-        "config": {"workload": args.workload, "tokens_per_step": T * world, "tokens_per_gpu": T,
+        "config": {"workload": args.workload + (" (tokens override %d)" % args.tokens if args.tokens else ""),
+                   "tokens_per_step": T * world, "tokens_per_gpu": T,
                    "weights": fmt, "layers": nl, "expert_placement": placement if ep and world > 1 else None,
                    "parallelism": ("ep%d" % world) if ep and world > 1 else ("replicas" if world > 1 else "single"),
                    "l2": "inputs larger than L2: %d distinct token batches, routed expert weights %.0f MB per step"
