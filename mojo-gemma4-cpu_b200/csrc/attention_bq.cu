@@ -452,19 +452,32 @@ attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_
 // BqFlashPrefillFull at degree 1): every token of a chunk attends to its own
 // causal range of its run -- sliding: [max(0, p - window + 1), p], full:
 // [0, p] -- over the cache the prep has just written.  CTA = (QT consecutive
-// tokens, KV head g): its C = QT * G (token, head) columns share every K/V
-// tile, so each cache row is read once per QT tokens instead of once per
+// tokens, KV head g): its C = QT * G = 32 (token, head) columns share every
+// K/V tile, so each cache row is read once per QT tokens instead of once per
 // token.  Per tile of PF_TP positions (cp.async double buffer):
 //  A. scores on the tensor cores (mma.m16n8k32 s8): positions are M, the
 //     columns N (C / 8 N-tiles), K split over the 8 warps, exact int32 sums;
 //  B. online softmax per column (warp w owns columns w, w + 8, ...), with the
 //     positions outside a column's range (causal / window / other run)
-//     masked;
-//  C. PV on the CUDA cores: thread i owns columns [i*CPT, (i+1)*CPT) of the
-//     head dimension for every column, each V row converted once.
+//     masked; the weights p = w * vs / 127 are stored as two bf16 parts,
+//     hi = bf16(p) and lo = bf16(p - hi) (p to about 2^-17 relative); the V
+//     tile is converted once into a transposed bf16 tile (int8 is exact in
+//     bf16);
+//  C. PV on the tensor cores (mma.m16n8k16 bf16, f32 accumulate): the columns
+//     are M (2 M-tiles), the positions K, the head dimension N (warp w owns
+//     HD/8 of it); acc = acc * corr + P_hi V + P_lo V.
 // The tile's tokens may span runs (sequences): the runs are visited in turn,
 // each over the union of its tokens' ranges.  Output bf16(acc / l).
 constexpr int PF_TP = 16;
+constexpr int PF_STR = PF_TP + 8;  // bf16 row stride of the transposed tiles: conflict-free fragment loads
+
+template <int HD, int C>
+struct PrefillSmem {
+  DecodeSmem<HD> kv;
+  uint16_t vt[HD][PF_STR];   // V tile transposed: [head column][position]
+  uint16_t phi[C][PF_STR];   // weights, high bf16 part: [column][position]
+  uint16_t plo[C][PF_STR];   // low bf16 part
+};
 
 template <int HD, int G, int QT>
 __global__ void __launch_bounds__(DEC_THREADS)
@@ -474,17 +487,20 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
                     const KvRun* __restrict__ runs, int num_runs, const int32_t* __restrict__ base_rows,
                     int T, int num_q, int num_kv, int window, int shift, int row_mask, int page_mask,
                     uint16_t* __restrict__ out) {
-  using Sm = DecodeSmem<HD>;
-  static_assert(Sm::TP == PF_TP, "tile size");
   constexpr int C = QT * G;                       // (token, head) columns
-  constexpr int NT = C / 8;                       // mma N-tiles
+  using Sm = PrefillSmem<HD, C>;
+  static_assert(DecodeSmem<HD>::TP == PF_TP, "tile size");
+  static_assert(C == 32, "two 16-row M-tiles of columns");
+  constexpr int NT = C / 8;                       // QK mma N-tiles
   constexpr int NW = DEC_WARPS;
-  constexpr int CPT = HD / DEC_THREADS;           // head-dim columns per thread
   constexpr int CPW = C / NW;                     // softmax columns per warp
   constexpr int KSW = HD / 32 / NW;               // 32-wide K steps per warp
   constexpr int TPR = DEC_THREADS / PF_TP;        // copying threads per row
   constexpr int CHUNKS = HD / (16 * TPR);
-  static_assert(C % 8 == 0 && C % NW == 0 && CPT >= 1 && KSW >= 1 && CHUNKS >= 1, "tile geometry");
+  constexpr int NPW = HD / NW;                    // head columns per warp in PV
+  constexpr int NTW = NPW / 8;                    // PV mma N-tiles per warp
+  constexpr int VPT = HD / DEC_THREADS;           // V columns each thread transposes
+  static_assert(KSW >= 1 && CHUNKS >= 1 && NTW >= 1 && (VPT == 1 || VPT == 2), "tile geometry");
   const int t0 = blockIdx.x * QT, g = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int grp = lane >> 2, tig = lane & 3;
@@ -492,7 +508,6 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
   Sm& sm = *reinterpret_cast<Sm*>(dsm);
   __shared__ __align__(16) int8_t qs[C * HD];
   __shared__ int part[NW][C][PF_TP];
-  __shared__ __align__(16) float wv[PF_TP][C];
   __shared__ float corr_s[C];
   __shared__ float l_s[C];
 
@@ -528,11 +543,15 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
     m[j] = NEG_BIG;
     l[j] = 0.0f;
   }
-  float acc[C][CPT];
+  // acc[mt][nt]: columns mt*16 + grp (+8 for [2..3]), head columns
+  // warp*NPW + nt*8 + 2*tig (+1)
+  float acc[2][NTW][4];
 #pragma unroll
-  for (int c = 0; c < C; ++c)
+  for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int x = 0; x < CPT; ++x) acc[c][x] = 0.0f;
+    for (int nt = 0; nt < NTW; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.0f;
 
   const size_t kvs = (size_t)num_kv * HD;
   const int t_end = min(t0 + QT, T);
@@ -570,11 +589,11 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
         const int8_t* vr = v_cache + slot * kvs + (size_t)g * HD + cpart * (HD / TPR);
 #pragma unroll
         for (int cc = 0; cc < CHUNKS; ++cc) {
-          cp_async16(&sm.k[buf][crow][cpart * (HD / TPR) + 16 * cc], kr + 16 * cc);
-          cp_async16(&sm.v[buf][crow][cpart * (HD / TPR) + 16 * cc], vr + 16 * cc);
+          cp_async16(&sm.kv.k[buf][crow][cpart * (HD / TPR) + 16 * cc], kr + 16 * cc);
+          cp_async16(&sm.kv.v[buf][crow][cpart * (HD / TPR) + 16 * cc], vr + 16 * cc);
         }
-        if (cpart == 0) cp_async4(&sm.ks[buf][crow], k_scale + slot * num_kv + g);
-        if (cpart == 1) cp_async4(&sm.vs[buf][crow], v_scale + slot * num_kv + g);
+        if (cpart == 0) cp_async4(&sm.kv.ks[buf][crow], k_scale + slot * num_kv + g);
+        if (cpart == 1) cp_async4(&sm.kv.vs[buf][crow], v_scale + slot * num_kv + g);
       }
       cp_async_commit();
     };
@@ -599,8 +618,8 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
 #pragma unroll
         for (int ks = 0; ks < KSW; ++ks) {
           const int k0 = (warp * KSW + ks) * 32 + 4 * tig;
-          const int8_t* r0 = &sm.k[buf][grp][k0];
-          const int8_t* r1 = &sm.k[buf][grp + 8][k0];
+          const int8_t* r0 = &sm.kv.k[buf][grp][k0];
+          const int8_t* r1 = &sm.kv.k[buf][grp + 8][k0];
           const uint32_t a0 = *reinterpret_cast<const uint32_t*>(r0), a1 = *reinterpret_cast<const uint32_t*>(r1);
           const uint32_t a2 = *reinterpret_cast<const uint32_t*>(r0 + 16),
                          a3 = *reinterpret_cast<const uint32_t*>(r1 + 16);
@@ -613,12 +632,40 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
 #pragma unroll
           for (int i = 0; i < 4; ++i) part[warp][nt * 8 + 2 * tig + (i & 1)][grp + 8 * (i >> 1)] = cacc[nt][i];
       }
+      // V tile -> transposed bf16 (every position of the buffer: rows past n
+      // hold finite stale bytes and meet zero weights)
+      {
+        uint32_t pk[VPT][PF_TP / 2];
+#pragma unroll
+        for (int pp = 0; pp < PF_TP; pp += 2) {
+          uint32_t w0, w1;
+          if constexpr (VPT == 2) {
+            w0 = *reinterpret_cast<const uint16_t*>(&sm.kv.v[buf][pp][2 * tid]);
+            w1 = *reinterpret_cast<const uint16_t*>(&sm.kv.v[buf][pp + 1][2 * tid]);
+          } else {
+            w0 = (uint8_t)sm.kv.v[buf][pp][tid];
+            w1 = (uint8_t)sm.kv.v[buf][pp + 1][tid];
+          }
+#pragma unroll
+          for (int x = 0; x < VPT; ++x) {
+            const float v0 = (float)(int8_t)((w0 >> (8 * x)) & 0xFFu);
+            const float v1 = (float)(int8_t)((w1 >> (8 * x)) & 0xFFu);
+            pk[x][pp / 2] = (uint32_t)f2bf(v0) | ((uint32_t)f2bf(v1) << 16);
+          }
+        }
+#pragma unroll
+        for (int x = 0; x < VPT; ++x) {
+          uint4* dst = reinterpret_cast<uint4*>(&sm.vt[VPT * tid + x][0]);
+          dst[0] = make_uint4(pk[x][0], pk[x][1], pk[x][2], pk[x][3]);
+          dst[1] = make_uint4(pk[x][4], pk[x][5], pk[x][6], pk[x][7]);
+        }
+      }
       __syncthreads();
       // ---- B: online softmax of the owned columns (lane = position in the tile)
       {
         const bool in_tile = lane < n;
-        const float ksc = in_tile ? sm.ks[buf][lane] : 0.0f;
-        const float vsc = in_tile ? sm.vs[buf][lane] : 0.0f;
+        const float ksc = in_tile ? sm.kv.ks[buf][lane] : 0.0f;
+        const float vsc = in_tile ? sm.kv.vs[buf][lane] : 0.0f;
         const int pl = lane < PF_TP ? lane : 0;
         const int p = p0 + lane;
 #pragma unroll
@@ -634,36 +681,51 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
           const float w = ok ? fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(sc, mn))) : 0.0f;
           l[j] = __fadd_rn(__fmul_rn(l[j], cr), warp_sum(w));
           m[j] = mn;
-          if (lane < PF_TP) wv[lane][col] = __fmul_rn(__fmul_rn(w, vsc), inv127);
+          if (lane < PF_TP) {
+            const float pw = __fmul_rn(__fmul_rn(w, vsc), inv127);
+            const uint16_t hi = f2bf(pw);
+            sm.phi[col][lane] = hi;
+            sm.plo[col][lane] = f2bf(__fsub_rn(pw, bf2f(hi)));
+          }
           if (lane == 0) corr_s[col] = cr;
         }
       }
       __syncthreads();
-      // ---- C: acc = acc*corr + sum_p v[p] * wv[p]
+      // ---- C: acc = acc*corr + P V on the tensor cores
+      {
+        float cr[2][2];
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-        const float cr = corr_s[c];
+        for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-        for (int x = 0; x < CPT; ++x) acc[c][x] = __fmul_rn(acc[c][x], cr);
-      }
-      for (int pp = 0; pp < n; ++pp) {
-        uint32_t vw;
-        if constexpr (CPT == 2) vw = *reinterpret_cast<const uint16_t*>(&sm.v[buf][pp][tid * CPT]);
-        else vw = (uint32_t)(uint8_t)sm.v[buf][pp][tid * CPT];
-        float v[CPT];
+          for (int h = 0; h < 2; ++h) cr[mt][h] = corr_s[mt * 16 + grp + 8 * h];
+        uint32_t ah[2][4], al[2][4];
 #pragma unroll
-        for (int x = 0; x < CPT; ++x) v[x] = (float)(int8_t)((vw >> (8 * x)) & 0xFFu);
+        for (int mt = 0; mt < 2; ++mt) {
+          const int c0 = mt * 16 + grp;
+          ah[mt][0] = *reinterpret_cast<const uint32_t*>(&sm.phi[c0][2 * tig]);
+          ah[mt][1] = *reinterpret_cast<const uint32_t*>(&sm.phi[c0 + 8][2 * tig]);
+          ah[mt][2] = *reinterpret_cast<const uint32_t*>(&sm.phi[c0][2 * tig + 8]);
+          ah[mt][3] = *reinterpret_cast<const uint32_t*>(&sm.phi[c0 + 8][2 * tig + 8]);
+          al[mt][0] = *reinterpret_cast<const uint32_t*>(&sm.plo[c0][2 * tig]);
+          al[mt][1] = *reinterpret_cast<const uint32_t*>(&sm.plo[c0 + 8][2 * tig]);
+          al[mt][2] = *reinterpret_cast<const uint32_t*>(&sm.plo[c0][2 * tig + 8]);
+          al[mt][3] = *reinterpret_cast<const uint32_t*>(&sm.plo[c0 + 8][2 * tig + 8]);
+        }
 #pragma unroll
-        for (int c4 = 0; c4 < C / 4; ++c4) {
-          const float4 w4 = reinterpret_cast<const float4*>(&wv[pp][0])[c4];
-          const float a[4] = {w4.x, w4.y, w4.z, w4.w};
+        for (int nt = 0; nt < NTW; ++nt) {
+          const int hc = warp * NPW + nt * 8 + grp;
+          const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sm.vt[hc][2 * tig]);
+          const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sm.vt[hc][2 * tig + 8]);
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
+          for (int mt = 0; mt < 2; ++mt) {
 #pragma unroll
-            for (int x = 0; x < CPT; ++x) acc[4 * c4 + u][x] = __fmaf_rn(v[x], a[u], acc[4 * c4 + u][x]);
+            for (int i = 0; i < 4; ++i) acc[mt][nt][i] = __fmul_rn(acc[mt][nt][i], cr[mt][i >> 1]);
+            mma_bf16(acc[mt][nt], ah[mt][0], ah[mt][1], ah[mt][2], ah[mt][3], b0, b1);
+            mma_bf16(acc[mt][nt], al[mt][0], al[mt][1], al[mt][2], al[mt][3], b0, b1);
+          }
         }
       }
-      __syncthreads();  // this buffer and part / wv / corr_s are reused
+      __syncthreads();  // this buffer and part / vt / phi / plo / corr_s are reused
     }
   }
   if (lane == 0) {
@@ -672,15 +734,23 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
   }
   __syncthreads();
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int t = t0 + c / G;
-    if (t >= T) continue;
-    const float lc = l_s[c];
-    const float il = lc > 0.0f ? __fdiv_rn(1.0f, lc) : 0.0f;
-    uint16_t* dst = out + ((size_t)t * num_q + g * G + c % G) * HD + tid * CPT;
+  for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-    for (int x = 0; x < CPT; ++x) dst[x] = lc > 0.0f ? f2bf(__fmul_rn(acc[c][x], il)) : (uint16_t)0;
-  }
+    for (int h = 0; h < 2; ++h) {
+      const int c = mt * 16 + grp + 8 * h;
+      const int t = t0 + c / G;
+      if (t >= T) continue;
+      const float lc = l_s[c];
+      const float il = lc > 0.0f ? __fdiv_rn(1.0f, lc) : 0.0f;
+      uint16_t* dst = out + ((size_t)t * num_q + g * G + c % G) * HD + warp * NPW + 2 * tig;
+#pragma unroll
+      for (int nt = 0; nt < NTW; ++nt) {
+        const uint32_t o = lc > 0.0f ? (uint32_t)f2bf(__fmul_rn(acc[mt][nt][2 * h], il)) |
+                                           ((uint32_t)f2bf(__fmul_rn(acc[mt][nt][2 * h + 1], il)) << 16)
+                                     : 0u;
+        *reinterpret_cast<uint32_t*>(dst + nt * 8) = o;
+      }
+    }
 }
 
 // kernels/logsum_merge.mojo:29-117: one CTA per (token, head), a thread per column
@@ -775,7 +845,7 @@ cudaError_t launch_attn_prefill(const int8_t* q_i8, const float* f_q, const int8
   if (head_dim == 256 && G == 2) {
     constexpr int QT = 16;
     auto k = attn_prefill_kernel<256, 2, QT>;
-    const size_t smem = sizeof(DecodeSmem<256>);
+    const size_t smem = sizeof(PrefillSmem<256, QT * 2>);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     return launch_k(k, dim3((T + QT - 1) / QT, num_kv), dim3(DEC_THREADS), smem, s, q_i8, f_q, k_cache, k_scale,
@@ -785,7 +855,7 @@ cudaError_t launch_attn_prefill(const int8_t* q_i8, const float* f_q, const int8
   if (head_dim == 512 && G == 8) {
     constexpr int QT = 4;
     auto k = attn_prefill_kernel<512, 8, QT>;
-    const size_t smem = sizeof(DecodeSmem<512>);
+    const size_t smem = sizeof(PrefillSmem<512, QT * 8>);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     return launch_k(k, dim3((T + QT - 1) / QT, num_kv), dim3(DEC_THREADS), smem, s, q_i8, f_q, k_cache, k_scale,

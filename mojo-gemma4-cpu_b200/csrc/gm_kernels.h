@@ -43,11 +43,14 @@ int handle_shard(const ::gm_moe* h, int* device, int* expert_base, int* epr, int
 int handle_fail(::gm_moe* h, int code, const char* msg);
 
 int max_route_chunks(int T, int epr, int rc);
-// The router writes ROUTER_SLICES split-K partial logit slices [slice][T][E];
-// router_ksplit(T) is how many of them the top-8 kernels sum: up to 32 tokens
-// the FMA kernel reduces them itself into slice 0 (1), above the partials stay
-// separate (ROUTER_SLICES) and the top-8 kernel sums them in slice order.
+// The router writes split-K partial logit slices [slice][T][E];
+// router_ksplit(T) is how many the top-8 kernels sum, in slice order: up to 32
+// tokens the FMA kernel reduces its ROUTER_SLICES slices itself into slice 0
+// (1); from ROUTER_WIDE_MIN_TOKENS the tcgen05 kernel writes
+// ROUTER_WIDE_SLICES slices; in between ROUTER_SLICES.
 constexpr int ROUTER_SLICES = H / 256;
+constexpr int ROUTER_WIDE_SLICES = 4;
+constexpr int ROUTER_WIDE_MIN_TOKENS = 3584;
 int router_ksplit(int T);
 // Tile counters of the FMA kernel's in-kernel reduction (ints, zero between calls).
 int router_tile_counters(int T);

@@ -155,7 +155,9 @@ topk_softmax_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __re
 // Up to 32 tokens the one-CTA top-8 + schedule kernel runs, so the router
 // reduces its K slices itself (tile counters); above, the top-8 kernel (T/4
 // CTAs) sums the slices while it loads them.
-int router_ksplit(int T) { return T > 32 ? ROUTER_SLICES : 1; }
+int router_ksplit(int T) {
+  return T >= ROUTER_WIDE_MIN_TOKENS ? ROUTER_WIDE_SLICES : T > 32 ? ROUTER_SLICES : 1;
+}
 
 int router_tile_counters(int T) { return (T + 7) / 8 * (E / 32); }
 
@@ -168,6 +170,7 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const ui
                                  float* logits, int* err, int* tile_counters, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   if (T >= ROUTER_TC_MIN_TOKENS && err) return launch_router_logits_tc(x, wr, rscale, T, logits, err, s);
+  if (T >= ROUTER_WIDE_MIN_TOKENS) return cudaErrorInvalidValue;  // the wide slicing is the tcgen05 kernel's
   if (router_ksplit(T) > 1) {
     tile_counters = nullptr;  // ROUTER_SLICES separate partials, summed by the top-8 kernel
   } else if (!tile_counters) {

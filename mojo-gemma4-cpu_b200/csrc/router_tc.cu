@@ -12,16 +12,20 @@
 //    two kind::f16 MMAs (f32 accumulate) give the f32 dot up to the
 //    accumulation order -- the same class of difference as the reference's
 //    own split across workers;
-//  * one CTA = 128 tokens x all 128 experts x one 256-wide K slice (the same
-//    11 slices, and the same [slice][T][E] partial layout, as the FMA kernel,
-//    so the top-8 kernels are shared);
+//  * one CTA = 128 tokens x all 128 experts x one K slice, written as the
+//    same [slice][T][E] partial layout as the FMA kernel so that the top-8
+//    kernels are shared: the FMA kernel's 11 slices of 256 below
+//    ROUTER_WIDE_MIN_TOKENS, 4 slices of 704 from there on (about one CTA per
+//    SM at 4096 tokens, and fewer partials for the top-8 to sum);
 //  * the kernel reads only x and the router weights, so it runs beside the
 //    norm kernel launched just before it (that kernel triggers only after its
 //    own wait, so x is complete); it waits for its predecessor only after its
 //    stores, so its completion implies the norm kernel's (router.cu);
-//  * the router slice (64 KB) is fetched with cp.async, the activation parts
-//    are produced by all 256 threads into a 2-stage ring in the
-//    128-byte-swizzled K-major layout the MMA descriptors read, and the TMEM
+//  * the router chunks (64 K each) arrive by cp.async in a 4-stage ring, two
+//    chunks ahead; each thread loads its x units two chunks ahead into
+//    registers; the activation parts are produced by all 256 threads into a
+//    2-stage ring in the 128-byte-swizzled K-major layout the MMA descriptors
+//    read, so one chunk's MMAs run while the next chunk is prepared; the TMEM
 //    accumulator is staged through shared memory for coalesced stores.
 //
 // Every mbarrier wait is bounded (tc::mbar_wait, ~1 s); on expiry the kernel
@@ -35,11 +39,11 @@ namespace gm {
 namespace tc {
 
 constexpr int RT_BM = 128;               // tokens per CTA (TMEM lanes)
-constexpr int RT_KS = 256;               // K slice per CTA
-constexpr int RT_BK = 64;                // bf16 per 128-byte swizzle row
-constexpr int RT_NCH = RT_KS / RT_BK;    // 4 K chunks per slice
+constexpr int RT_BK = 64;                // bf16 per 128-byte swizzle row (one K chunk)
+constexpr int RT_CHUNKS = H / RT_BK;     // 44 K chunks in all
 constexpr int RT_THREADS = 256;
 constexpr int RT_TILE = 128 * 128;       // bytes of one [128 rows][64 bf16] operand tile
+constexpr int RT_BST = 4;                // router chunk ring (two chunks ahead)
 constexpr int RT_YSTR = E + 4;           // output staging row stride (floats)
 
 // kind::f16: D = f32 (bits 4-5 = 1), A = B = bf16 (bits 7-9, 10-12 = 1), both
@@ -48,13 +52,14 @@ constexpr uint32_t IDESC_BF16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)
                                 ((uint32_t)(RT_BM >> 4) << 24);
 
 struct RouterSmem {
-  uint8_t b[RT_NCH][RT_TILE];     // router rows (experts) x 64 bf16 per chunk; 1024-aligned
-  uint8_t a[2][3][RT_TILE];       // 2 stages x {hi, lo, (output staging room)} x [128 tokens][64 bf16]
-  uint64_t done[2];
+  uint8_t b[RT_BST][RT_TILE];     // router rows (experts) x 64 bf16 per chunk; 1024-aligned
+  uint8_t a[2][2][RT_TILE];       // 2 stages x {hi, lo} x [128 tokens][64 bf16]
+  uint64_t done[2];               // MMAs of the chunks using A stage 0 / 1 complete
   uint32_t tmem_base;
   int failed;
 };
-static_assert(sizeof(float) * RT_BM * RT_YSTR <= sizeof(((RouterSmem*)0)->a), "staging fits in a[]");
+static_assert(sizeof(float) * RT_BM * RT_YSTR <= sizeof(((RouterSmem*)0)->b) + sizeof(((RouterSmem*)0)->a),
+              "output staging fits in the operand rings");
 
 __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t da, uint64_t db, uint32_t accumulate) {
   asm volatile(
@@ -71,6 +76,13 @@ __device__ __forceinline__ uint32_t pack_bf16(uint16_t lo, uint16_t hi) {
   return (uint32_t)lo | ((uint32_t)hi << 16);
 }
 
+// One CTA: 128 tokens x all 128 experts x K chunks [blockIdx.y*CPS, +CPS).
+// Per chunk c: the router chunk arrives by cp.async two chunks ahead (4-stage
+// ring), the thread's x units two chunks ahead in registers; x*s is split
+// into its hi / lo bf16 parts in A stage c%2 (after the MMAs of chunk c-2,
+// which read that stage, complete), and thread 0 issues the chunk's 8 MMAs,
+// which then run while the threads prepare chunk c+1.
+template <int CPS>
 __global__ void __launch_bounds__(RT_THREADS, 1)
 router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
                  const uint16_t* __restrict__ rscale, int T, float* __restrict__ logits,
@@ -78,14 +90,35 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   RouterSmem& s =
       *reinterpret_cast<RouterSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = blockIdx.x * RT_BM, kb = blockIdx.y * RT_KS;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t0 = blockIdx.x * RT_BM, kb = blockIdx.y * CPS * RT_BK;
+  // this thread's 16-byte unit column j of token rows (tid >> 3) + 32q, and of
+  // expert rows (tid >> 3) + 32q in the router chunks
+  const int j = tid & 7, r0 = tid >> 3;
 
-  // router slice: 128 experts x 256 K = 4 chunks of [128][64] bf16
-  for (int i = tid; i < E * (RT_KS / 8); i += RT_THREADS) {
-    const int e = i / (RT_KS / 8), u = i % (RT_KS / 8), c = u >> 3, j = u & 7;
-    cp_async16(s.b[c] + sw128(e, j), wr + (size_t)e * H + kb + u * 8);
-  }
+  auto issue_b = [&](int c) {  // router chunk c -> ring stage c % RT_BST, one commit group
+    if (c < CPS) {
+      uint8_t* dst = s.b[c % RT_BST];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int e = r0 + 32 * q;
+        cp_async16(dst + sw128(e, j), wr + (size_t)e * H + kb + c * RT_BK + j * 8);
+      }
+    }
+    cp_async_commit();
+  };
+  auto load_x = [&](int c, uint4 (&v)[4], uint4& rs) {
+    const int k0 = kb + c * RT_BK + j * 8;
+    rs = *reinterpret_cast<const uint4*>(rscale + k0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int t = t0 + r0 + 32 * q;
+      v[q] = t < T ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)t * H + k0)) : make_uint4(0, 0, 0, 0);
+    }
+  };
+
+  issue_b(0);
+  issue_b(1);
   if (tid == 0) {
     mbar_init(&s.done[0], 1);
     mbar_init(&s.done[1], 1);
@@ -98,50 +131,47 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
                  "r"(128u));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
+  pdl_trigger();  // no wait before reading x: see the file comment
+  uint4 xv[3][4], rs[3];
+  load_x(0, xv[0], rs[0]);
+  if (CPS > 1) load_x(1, xv[1], rs[1]);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
 
-  pdl_trigger();  // no wait before reading x: see the file comment
-
-  // 8 consecutive router_scale values of each 16-byte unit this thread owns
-  // (the unit column j = tid & 7 is the same for all 4 of its units)
-  const int j = tid & 7;
-  for (int c = 0; c < RT_NCH; ++c) {
+#pragma unroll
+  for (int c = 0; c < CPS; ++c) {
     const int st = c & 1;
-    if (c >= 2) mbar_wait(&s.done[st], 0, &s.failed);  // MMAs of chunk c-2 read this stage
-    const int k0 = kb + c * RT_BK + j * 8;
-    const uint4 rs4 = *reinterpret_cast<const uint4*>(rscale + k0);
-    const uint32_t rsw[4] = {rs4.x, rs4.y, rs4.z, rs4.w};
+    if (c + 2 < CPS) load_x(c + 2, xv[(c + 2) % 3], rs[(c + 2) % 3]);
+    // the MMAs of chunk c-2 read A stage st and B stage (c+2) % RT_BST
+    if (c >= 2) mbar_wait(&s.done[st], (uint32_t)(((c >> 1) - 1) & 1), &s.failed);
+    issue_b(c + 2);
+    const uint32_t rsw[4] = {rs[c % 3].x, rs[c % 3].y, rs[c % 3].z, rs[c % 3].w};
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int r = (tid >> 3) + q * (RT_THREADS / 8);  // token row in the tile
-      const int t = t0 + r;
-      uint32_t hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
-      if (t < T) {
-        const uint4 xv = *reinterpret_cast<const uint4*>(x + (size_t)t * H + k0);
-        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+      const uint4 v = xv[c % 3][q];
+      const uint32_t xw[4] = {v.x, v.y, v.z, v.w};
+      uint32_t hi[4], lo[4];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          uint16_t h2[2], l2[2];
+      for (int p = 0; p < 4; ++p) {
+        uint16_t h2[2], l2[2];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const float xs = bf2f(h ? xw[p] >> 16 : xw[p] & 0xFFFFu);
-            const float ss = bf2f(h ? rsw[p] >> 16 : rsw[p] & 0xFFFFu);
-            const float sv = __fmul_rn(xs, ss);                   // x*s, exact
-            h2[h] = f2bf(sv);
-            l2[h] = f2bf(__fsub_rn(sv, bf2f(h2[h])));             // exact residual (<= 8 bits)
-          }
-          hi[p] = pack_bf16(h2[0], h2[1]);
-          lo[p] = pack_bf16(l2[0], l2[1]);
+        for (int h = 0; h < 2; ++h) {
+          const float xs = bf2f(h ? xw[p] >> 16 : xw[p] & 0xFFFFu);
+          const float ss = bf2f(h ? rsw[p] >> 16 : rsw[p] & 0xFFFFu);
+          const float sv = __fmul_rn(xs, ss);                   // x*s, exact
+          h2[h] = f2bf(sv);
+          l2[h] = f2bf(__fsub_rn(sv, bf2f(h2[h])));             // exact residual (<= 8 bits)
         }
+        hi[p] = pack_bf16(h2[0], h2[1]);
+        lo[p] = pack_bf16(l2[0], l2[1]);
       }
-      const int off = sw128(r, j);
+      const int off = sw128(r0 + 32 * q, j);
       *reinterpret_cast<uint4*>(s.a[st][0] + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
       *reinterpret_cast<uint4*>(s.a[st][1] + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
-    if (c == 0) cp_async_wait_all();
+    cp_async_wait_group<2>();  // router chunk c (two later groups may still fly)
     // generic-proxy shared-memory writes -> visible to the tensor core (async proxy)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
@@ -149,27 +179,27 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
       tc_fence_after();
 #pragma unroll
       for (int k = 0; k < RT_BK / 16; ++k) {
-        const uint64_t db = kmajor_sw128_desc(smem_u32(s.b[c]) + k * 32);
+        const uint64_t db = kmajor_sw128_desc(smem_u32(s.b[c % RT_BST]) + k * 32);
 #pragma unroll
         for (int p = 0; p < 2; ++p)
-          mma_bf16_ss(tmem, kmajor_sw128_desc(smem_u32(s.a[st][p]) + k * 32), db,
-                      (c | k | p) != 0);
+          mma_bf16_ss(tmem, kmajor_sw128_desc(smem_u32(s.a[st][p]) + k * 32), db, (c | k | p) != 0);
       }
       mma_commit(&s.done[st]);
     }
   }
-  // chunk 2 -> second completion of done[0], chunk 3 -> second of done[1]
-  mbar_wait(&s.done[0], 1, &s.failed);
-  mbar_wait(&s.done[1], 1, &s.failed);
+  // the last two chunks' completions
+  if (CPS >= 2) mbar_wait(&s.done[(CPS - 2) & 1], (uint32_t)(((CPS - 2) >> 1) & 1), &s.failed);
+  mbar_wait(&s.done[(CPS - 1) & 1], (uint32_t)(((CPS - 1) >> 1) & 1), &s.failed);
   tc_fence_after();
 
   // epilogue: warp w reads TMEM lanes 32*(w&3).. and columns 64*(w>>2)..,
-  // stages the f32 tile in shared memory (reusing the operand ring), then
+  // stages the f32 tile in shared memory (reusing the operand rings), then
   // whole 512-byte rows are stored
-  float* ystage = reinterpret_cast<float*>(&s.a[0][0][0]);
-  __syncthreads();  // every thread is past its last read of the ring
+  float* ystage = reinterpret_cast<float*>(&s.b[0][0]);
+  cp_async_wait_all();
+  __syncthreads();  // every thread is past its last read of the rings
   {
-    const int q = warp & 3, half = warp >> 2, row = q * 32 + lane;
+    const int q = warp & 3, half = warp >> 2, row = q * 32 + (tid & 31);
     float* dst = ystage + row * RT_YSTR + half * 64;
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
@@ -187,6 +217,7 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
   __syncthreads();
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128u));
   float* out = logits + (size_t)blockIdx.y * T * E;
+  const int lane = tid & 31;
   for (int r = warp; r < RT_BM; r += RT_THREADS / 32) {
     const int t = t0 + r;
     if (t >= T) break;
@@ -203,11 +234,16 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
 cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale, int T,
                                     float* logits, int* err, cudaStream_t s) {
   const size_t smem = sizeof(tc::RouterSmem) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(tc::router_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+  // router_ksplit(T) K slices: 11 chunks each for wide batches (about one CTA
+  // per SM at 4096 tokens), 4 chunks each below (more CTAs for fewer tokens)
+  const int ns = router_ksplit(T);
+  if (ns != ROUTER_WIDE_SLICES && ns != ROUTER_SLICES) return cudaErrorInvalidValue;
+  auto k = ns == ROUTER_WIDE_SLICES ? tc::router_tc_kernel<tc::RT_CHUNKS / ROUTER_WIDE_SLICES>
+                                    : tc::router_tc_kernel<tc::RT_CHUNKS / ROUTER_SLICES>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_k(tc::router_tc_kernel, dim3((T + tc::RT_BM - 1) / tc::RT_BM, H / tc::RT_KS),
-                  dim3(tc::RT_THREADS), smem, s, x, wr, rscale, T, logits, err);
+  return launch_k(k, dim3((T + tc::RT_BM - 1) / tc::RT_BM, ns), dim3(tc::RT_THREADS), smem, s, x, wr, rscale, T,
+                  logits, err);
 }
 
 }  // namespace gm

@@ -100,9 +100,10 @@ def run_router(g, x_np):
     return host(idx), host(w), ws[:T * E].reshape(T, E)
 
 
-# T >= 512 runs the tcgen05 router (three-way exact bf16 split of the f32
-# activations), smaller T the FMA kernel
-@pytest.mark.parametrize("T", [1, 16, 64, 300, 600, 2000])
+# T >= 512 runs the tcgen05 router (exact bf16 split of the f32 activations),
+# smaller T the FMA kernel; from 3584 tokens the tcgen05 router writes 4 wide
+# K slices instead of 11
+@pytest.mark.parametrize("T", [1, 16, 64, 300, 600, 2000, 3584, 4200])
 @pytest.mark.parametrize("which", ["default", "stress"])
 def test_router_parity(T, which, layer_default, layer_stress):
     raw, ref, g = layer_default if which == "default" else layer_stress
