@@ -471,9 +471,21 @@ attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_
 constexpr int PF_TP = 16;
 constexpr int PF_STR = PF_TP + 8;  // bf16 row stride of the transposed tiles: conflict-free fragment loads
 
+constexpr int PF_STAGES = 4;       // K/V tiles in the cp.async ring (three ahead of the one in use)
+
+template <int HD>
+struct PrefillRing {
+  static constexpr int TP = PF_TP;
+  static constexpr int RS = HD + 16;  // padded row, as DecodeSmem
+  int8_t k[PF_STAGES][TP][RS];
+  int8_t v[PF_STAGES][TP][RS];
+  float ks[PF_STAGES][TP];
+  float vs[PF_STAGES][TP];
+};
+
 template <int HD, int C>
 struct PrefillSmem {
-  DecodeSmem<HD> kv;
+  PrefillRing<HD> kv;
   uint16_t vt[HD][PF_STR];   // V tile transposed: [head column][position]
   uint16_t phi[C][PF_STR];   // weights, high bf16 part: [column][position]
   uint16_t plo[C][PF_STR];   // low bf16 part
@@ -489,7 +501,6 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
                     uint16_t* __restrict__ out) {
   constexpr int C = QT * G;                       // (token, head) columns
   using Sm = PrefillSmem<HD, C>;
-  static_assert(DecodeSmem<HD>::TP == PF_TP, "tile size");
   static_assert(C == 32, "two 16-row M-tiles of columns");
   constexpr int NT = C / 8;                       // QK mma N-tiles
   constexpr int NW = DEC_WARPS;
@@ -581,7 +592,7 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
     }
     const int32_t* rows = base_rows + run.rows_off;
     const int crow = tid / TPR, cpart = tid % TPR;
-    auto issue = [&](int p0, int buf) {
+    auto issue = [&](int p0, int buf) {  // one commit group per call, empty past the range
       const int p = p0 + crow;
       if (p <= p_last) {
         const long slot = kv_slot(rows, shift, row_mask, page_mask, p);
@@ -597,16 +608,15 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
       }
       cp_async_commit();
     };
-    issue(p_first, 0);
+#pragma unroll
+    for (int i = 0; i < PF_STAGES - 1; ++i) issue(p_first + i * PF_TP, i);
     int buf = 0;
-    for (int p0 = p_first; p0 <= p_last; p0 += PF_TP, buf ^= 1) {
+    for (int p0 = p_first; p0 <= p_last; p0 += PF_TP, buf = (buf + 1) % PF_STAGES) {
       const int n = min(PF_TP, p_last + 1 - p0);
-      if (p0 + PF_TP <= p_last) {
-        issue(p0 + PF_TP, buf ^ 1);
-        cp_async_wait_group<1>();
-      } else {
-        cp_async_wait_group<0>();
-      }
+      // tile p0 + 3*PF_TP into the stage the previous tile used (all threads
+      // are past it: the barrier that ends each tile)
+      issue(p0 + (PF_STAGES - 1) * PF_TP, (buf + PF_STAGES - 1) % PF_STAGES);
+      cp_async_wait_group<PF_STAGES - 1>();  // this tile's group has landed
       __syncthreads();
       // ---- A: scores
       {

@@ -54,7 +54,6 @@ constexpr int STAGES2 = 4;
 constexpr int RING = 4;            // phase-2 TMEM regions
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;  // 576
-constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr uint32_t TMEM_COLS1 = 256;         // two 128-column accumulators
 constexpr uint32_t TMEM_COLS2 = RING * BN;   // 512
 constexpr int XSTR = 64 + 4;       // phase-1 exchange row stride (floats)
@@ -125,7 +124,7 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
-      mbar_init(&s.acc_empty[i], EPI_THREADS);
+      mbar_init(&s.acc_empty[i], EPI_WARPS);  // one arrival per epilogue warp
     }
     s.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -245,7 +244,8 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       tmem_ld16(base + 64 + 16 * cb, ud);
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(&s.acc_empty[acc]);  // accumulator drained: MMA may reuse it
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[acc]);  // the warp's share drained: MMA may reuse it
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
 
       float hv[16];
@@ -363,7 +363,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     }
     for (int i = 0; i < RING; ++i) {
       mbar_init(&s.reg_full[i], 1);
-      mbar_init(&s.reg_empty[i], EPI_THREADS);
+      mbar_init(&s.reg_empty[i], EPI_WARPS);  // one arrival per epilogue warp
     }
     s.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -487,7 +487,8 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(reg * BN + 32 * cb), d);
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(&s.reg_empty[reg]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.reg_empty[reg]);  // the warp's columns read
         if (++reg == RING) { reg = 0; rphase ^= 1; }
         if (quarter_live) {
           const float2 a2 = make_float2(adv_b, adv_b);

@@ -47,7 +47,6 @@ constexpr int NJ1 = I / 64;              // 11 column tiles of 64 intermediate o
 constexpr int NT2 = H / BN;              // 22 hidden tiles
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
-constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr uint32_t TMEM_COLS = 2 * BN;   // two accumulators
 constexpr int YSTR = BN + 4;
 constexpr int ERR_TIMEOUT = 1;
@@ -97,7 +96,7 @@ __device__ __forceinline__ void setup(S& s, const int32_t* expert_offset, int ep
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
-      mbar_init(&s.acc_empty[i], EPI_THREADS);
+      mbar_init(&s.acc_empty[i], EPI_WARPS);  // one arrival per epilogue warp
     }
     s.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -204,7 +203,8 @@ tcb_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
       tmem_ld16(base + 64 + 16 * cb, u);
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(&s.acc_empty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
       if (++acc == 2) { acc = 0; aphase ^= 1; }
       if (r < ti.nvalid) {
         uint32_t o[8];
@@ -274,7 +274,8 @@ tcb_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
       tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + 32 * cb), d);
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(&s.acc_empty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
       if (++acc == 2) { acc = 0; aphase ^= 1; }
       float4* ys = reinterpret_cast<float4*>(&s.ystage[r][32 * cb]);
 #pragma unroll
