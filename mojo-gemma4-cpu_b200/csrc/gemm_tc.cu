@@ -49,20 +49,19 @@ constexpr int KC2 = (I + BK - 1) / BK;  // 6 K stages of 128 bytes (last half ze
 constexpr int A_BYTES = BM * BK;   // 16 KB
 constexpr int B_BYTES = BN * BK;   // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int STAGES1 = 5;
+constexpr int STAGES1 = 6;          // the FWHT exchange lives in TMEM, so a 6th stage fits
 constexpr int STAGES2 = 4;
 constexpr int RING = 4;            // phase-2 TMEM regions
 constexpr int EPI_WARPS = 16;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;  // 576
-constexpr uint32_t TMEM_COLS1 = 256;         // two 128-column accumulators
+constexpr uint32_t TMEM_COLS1 = 512;         // two 128-column accumulators + the FWHT exchange
+constexpr uint32_t XCOL1 = 2 * BN;           // phase-1 exchange columns [XCOL1, XCOL1 + 64)
 constexpr uint32_t TMEM_COLS2 = RING * BN;   // 512
-constexpr int XSTR = 64 + 4;       // phase-1 exchange row stride (floats)
 constexpr int YSTR = BN + 4;       // phase-2 output staging row stride (floats)
 constexpr int ERR_TIMEOUT = 1;
 
 struct Smem1 {
   uint8_t stage[STAGES1][STAGE_BYTES];  // first member: 1024-byte aligned
-  float xbuf[BM][XSTR];
   float amax[BM][4];
   uint64_t full[STAGES1];
   uint64_t empty[STAGES1];
@@ -282,25 +281,31 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           }
       // strides 16 and 32 pair this block with block cb^1, then cb^2 (the lower
       // block keeps a+b, the upper a-b with a from the lower block)
+      // (exchanged through TMEM columns [XCOL1, XCOL1 + 64) of the quarter's
+      // lanes: each of its 4 warps writes its 16 columns, then reads its partner's)
+      const uint32_t xq = tmem + ((uint32_t)(q * 32) << 16) + XCOL1;
 #pragma unroll
       for (int sx = 1; sx <= 2; sx <<= 1) {
-        float4* mine = reinterpret_cast<float4*>(&s.xbuf[r][16 * cb]);
+        uint32_t mine[16];
 #pragma unroll
-        for (int v = 0; v < 4; ++v) mine[v] = make_float4(hv[4 * v], hv[4 * v + 1], hv[4 * v + 2], hv[4 * v + 3]);
+        for (int i = 0; i < 16; ++i) mine[i] = __float_as_uint(hv[i]);
+        tmem_st16(xq + 16 * cb, mine);
+        tmem_st_wait();
+        tc_fence_before();
         quarter_sync(q);
-        const float4* other = reinterpret_cast<const float4*>(&s.xbuf[r][16 * (cb ^ sx)]);
+        tc_fence_after();
+        int other[16];
+        tmem_ld16(xq + 16 * (cb ^ sx), other);
+        tmem_ld_wait();
         const bool upper = (cb & sx) != 0;
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const float4 p = other[v];
-          const float pv[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int i = 4 * v + u;
-            hv[i] = upper ? __fsub_rn(pv[u], hv[i]) : __fadd_rn(hv[i], pv[u]);
-          }
+        for (int i = 0; i < 16; ++i) {
+          const float pv = __int_as_float(other[i]);
+          hv[i] = upper ? __fsub_rn(pv, hv[i]) : __fadd_rn(hv[i], pv);
         }
-        quarter_sync(q);  // partners have read before the buffer is reused
+        tc_fence_before();
+        quarter_sync(q);  // partners have read before the columns are rewritten
+        tc_fence_after();
       }
       float amax = 0.0f;
 #pragma unroll
