@@ -859,7 +859,7 @@ def cpu_leg(fmt, T, args, raw_dev):
 # bf16_prefill_4k_tcgen05.md); None where no capture of the current kernel
 # and workload exists.
 NCU_TRAFFIC = {
-    ("bq-decode-b64", "bq_phase1_gate_up"): 505_800_000 + 500_000,
+    ("bq-decode-b64", "bq_phase1_gate_up"): 508_446_720 + 7_229_952,
     ("bq-prefill-4k-zipf", "bq_phase2_down.tc"): 280_055_808 + 353_800_192,
     ("bf16-prefill-4k", "phase1_gate_up.tc"): 1_229_532_000 + 45_981_184,
 }
