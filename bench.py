@@ -361,13 +361,13 @@ def median_rate(fn, units, seconds):
     return units / float(np.median(samples)), len(samples), warm
 
 
-def run_attn_prefill(args, kind, T, stream, hbm):
+def run_attn_prefill(args, kind, T, stream, hbm, tflops):
     """One prefill chunk of T tokens of one sequence (positions 0..T-1) through
     gm_bq_attention_prefill: sliding layer (head 256, 16 / 8 heads, window
     1024) or full layer (head 512, 16 / 2 heads, causal over the chunk).
     `batches` distinct (q, KV cache) sets are cycled so that the inputs exceed
-    L2.  The bound is the CUDA-core PV product (fp32 FMA per position, head
-    column and query head); QK runs on the int8 tensor cores."""
+    L2.  QK runs on int8 and PV on bf16 tensor-core instructions (mma.sync);
+    the roofline counts both products of the algorithm."""
     import numpy as np
     import torch
     import gmoe
@@ -398,12 +398,11 @@ def run_attn_prefill(args, kind, T, stream, hbm):
     ms = timed(step, args.steps, args.warmup, stream)
     per_step = ms / args.steps
     positions = sum(min(p + 1, window) if window else p + 1 for p in range(T))
-    fma = positions * nq * hd                     # PV: one FMA per position, head column, query head
-    # 128 FP32 lanes per SM at the maximum SM clock (2 FLOP per FMA)
-    fp32_peak = 2 * 128 * torch.cuda.get_device_properties(0).multi_processor_count * 1.965e9 / 1e12
-    roof = {"bound": "fp32", "achieved": 2 * fma / (per_step * 1e-3) / 1e12,
-            "peak": fp32_peak, "unit": "TFLOP/s",
-            "note": "PV on the CUDA cores; peak = 128 FP32 FMA lanes x SMs x 1965 MHz (nominal, not measured)"}
+    # QK (int8) and PV (bf16 hi + lo weights) products, 2 FLOP per multiply-add
+    # of the algorithm (the hi / lo split is not counted)
+    flop = 2 * 2 * positions * nq * hd
+    roof = {"bound": "tensor", "achieved": flop / (per_step * 1e-3) / 1e12, "peak": tflops, "unit": "TFLOP/s",
+            "note": "QK and PV on mma.sync tensor-core instructions; peak = measured dense bf16 (tcgen05) rate"}
     qh = [st[0].cpu().pin_memory() for st in sets]
     oh = torch.empty(T, nq * hd, dtype=torch.bfloat16).pin_memory()
     qd = torch.empty_like(sets[0][0])
@@ -545,7 +544,7 @@ def run_extra(args):
                                                    "weights": "bq", "layers": 1, "parallelism": "single"}})
             blk.close()
         elif kind.startswith("attnp"):
-            line.update(run_attn_prefill(args, kind, T, stream, hbm))
+            line.update(run_attn_prefill(args, kind, T, stream, hbm, tflops))
             roof, ms, per_step, launches = line.pop("_roof"), line.pop("_ms"), line.pop("_per_step"), line.pop("_launches")
             e2e, e2e_io, cpu = line.pop("_e2e"), line.pop("_e2e_io"), line.pop("_cpu")
         else:

@@ -471,7 +471,7 @@ attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_
 constexpr int PF_TP = 16;
 constexpr int PF_STR = PF_TP + 8;  // bf16 row stride of the transposed tiles: conflict-free fragment loads
 
-constexpr int PF_STAGES = 4;       // K/V tiles in the cp.async ring (three ahead of the one in use)
+constexpr int PF_STAGES = 2;       // K/V tiles in the cp.async ring (one ahead of the one in use)
 
 template <int HD>
 struct PrefillRing {
@@ -492,7 +492,7 @@ struct PrefillSmem {
 };
 
 template <int HD, int G, int QT>
-__global__ void __launch_bounds__(DEC_THREADS)
+__global__ void __launch_bounds__(DEC_THREADS, 2)
 attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_q,
                     const int8_t* __restrict__ k_cache, const float* __restrict__ k_scale,
                     const int8_t* __restrict__ v_cache, const float* __restrict__ v_scale,
@@ -613,7 +613,7 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
     int buf = 0;
     for (int p0 = p_first; p0 <= p_last; p0 += PF_TP, buf = (buf + 1) % PF_STAGES) {
       const int n = min(PF_TP, p_last + 1 - p0);
-      // tile p0 + 3*PF_TP into the stage the previous tile used (all threads
+      // tile p0 + (PF_STAGES-1)*PF_TP into the stage the previous tile used (all threads
       // are past it: the barrier that ends each tile)
       issue(p0 + (PF_STAGES - 1) * PF_TP, (buf + PF_STAGES - 1) % PF_STAGES);
       cp_async_wait_group<PF_STAGES - 1>();  // this tile's group has landed
