@@ -13,7 +13,9 @@
 
 namespace gm {
 
-__global__ void __launch_bounds__(352)
+constexpr int COMBINE_THREADS = H / 8;  // 352: two float4 column groups per thread and row
+
+__global__ void __launch_bounds__(COMBINE_THREADS)
 combine_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict__ route_pos,
                const float* __restrict__ ybuf, int T, uint16_t* __restrict__ out) {
   pdl_wait();
@@ -21,6 +23,13 @@ combine_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restrict_
   const int t = blockIdx.x;
   int pos[TOPK];
   routes_by_expert(route_idx, route_pos, t, pos);
+  if (gridDim.y == 1) {  // one CTA per row: the thread's two column groups together
+    float4 a0, a1;
+    sum_routes4x2(ybuf, pos, threadIdx.x, threadIdx.x + COMBINE_THREADS, a0, a1);
+    *reinterpret_cast<uint2*>(out + (size_t)t * H + threadIdx.x * 4) = pack_bf16x4(a0);
+    *reinterpret_cast<uint2*>(out + (size_t)t * H + (threadIdx.x + COMBINE_THREADS) * 4) = pack_bf16x4(a1);
+    return;
+  }
   // gridDim.y CTAs share the token's row (column slices)
   const int per = (H / 4) / gridDim.y;
   for (int c4 = blockIdx.y * per + threadIdx.x; c4 < (blockIdx.y + 1) * per; c4 += blockDim.x) {
@@ -44,13 +53,14 @@ combine_post_kernel(const int32_t* __restrict__ route_idx, const int32_t* __rest
   int pos[TOPK];
   routes_by_expert(route_idx, route_pos, t, pos);
   float m[8];
+  float4 acc[2];
+  sum_routes4x2(ybuf, pos, threadIdx.x, threadIdx.x + POST_THREADS, acc[0], acc[1]);
 #pragma unroll
   for (int g = 0; g < 2; ++g) {
-    const float4 acc = sum_routes4(ybuf, pos, threadIdx.x + g * POST_THREADS);
-    m[4 * g] = bf2f(f2bf(acc.x));
-    m[4 * g + 1] = bf2f(f2bf(acc.y));
-    m[4 * g + 2] = bf2f(f2bf(acc.z));
-    m[4 * g + 3] = bf2f(f2bf(acc.w));
+    m[4 * g] = bf2f(f2bf(acc[g].x));
+    m[4 * g + 1] = bf2f(f2bf(acc[g].y));
+    m[4 * g + 2] = bf2f(f2bf(acc[g].z));
+    m[4 * g + 3] = bf2f(f2bf(acc[g].w));
   }
   post_moe_row(m, t, p, red);
 }
@@ -67,7 +77,7 @@ cudaError_t launch_combine(const int32_t* route_idx, const int32_t* route_pos, c
   if (T <= 0) return cudaSuccess;
   // small batches: two CTAs per token (half a row each) to spread the reads
   const int split = T < 256 ? 2 : 1;
-  return launch_k(combine_kernel, dim3(T, split), dim3(352), 0, s, route_idx, route_pos, ybuf, T, out);
+  return launch_k(combine_kernel, dim3(T, split), dim3(COMBINE_THREADS), 0, s, route_idx, route_pos, ybuf, T, out);
 }
 
 }  // namespace gm

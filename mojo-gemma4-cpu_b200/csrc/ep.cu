@@ -329,13 +329,11 @@ combine_p2p_kernel(const int32_t* __restrict__ route_idx, const int32_t* __restr
     if (pos[0] < 0) continue;  // rows with no route here were never sent (or are unused)
     const int src = r / cap;
     uint16_t* dst = peers.contrib[src] + ((size_t)my_rank * cap + (r % cap)) * H;
-    for (int c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
-      const float4 acc = sum_routes4(ybuf, pos, c4);
-      uint2 o;
-      o.x = (uint32_t)f2bf(acc.x) | ((uint32_t)f2bf(acc.y) << 16);
-      o.y = (uint32_t)f2bf(acc.z) | ((uint32_t)f2bf(acc.w) << 16);
-      *reinterpret_cast<uint2*>(dst + c4 * 4) = o;
-    }
+    // 352 threads: two column groups each, loads of both in flight together
+    float4 a0, a1;
+    sum_routes4x2(ybuf, pos, threadIdx.x, threadIdx.x + H / 8, a0, a1);
+    *reinterpret_cast<uint2*>(dst + threadIdx.x * 4) = pack_bf16x4(a0);
+    *reinterpret_cast<uint2*>(dst + (threadIdx.x + H / 8) * 4) = pack_bf16x4(a1);
   }
   publish_when_last(done_counter, peers.cflag, G, my_rank, epoch);
 }
