@@ -74,7 +74,12 @@ struct Smem1 {
 
 struct Smem2 {
   uint8_t stage[STAGES2][STAGE_BYTES];
-  float ystage[BM][YSTR];
+  // dense: the bf16 output rows staged as float [BM][YSTR]; MoE: 16 boxes of
+  // 32 x 32 f32 (one per epilogue warp, 128-byte swizzled) for TMA stores
+  union {
+    float ystage[BM][YSTR];
+    uint8_t ybox[EPI_WARPS][32 * 128];
+  };
   uint64_t full[STAGES2];
   uint64_t empty[STAGES2];
   uint64_t reg_full[RING];
@@ -348,6 +353,7 @@ tc_phase1_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 template <bool DENSE>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                 const __grid_constant__ CUtensorMap map_y,
                  const int32_t* __restrict__ expert_offset, int epr, int dense_rows,
                  const float* __restrict__ bsa, const SparseRoute* __restrict__ routes,
                  const float* __restrict__ dn_scale, void* __restrict__ yout,
@@ -502,8 +508,44 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             facc[i] = fma2(small_ints_to_float2(d[2 * i], d[2 * i + 1]), a2, facc[i]);
         }
       }
-      // y = facc * sw * w_route (dense: facc * sw), staged per row then
-      // written as whole rows
+      if constexpr (!DENSE) {
+        // y = facc * sw * w_route for this warp's 32 rows x 32 columns: a fully
+        // valid quarter goes out as one TMA store of the warp's swizzled box
+        // (issued by lane 0, no barrier with the other warps); a partial one
+        // is stored row by row from registers
+        const float2 wr2 = make_float2(wr, wr);
+        float4 yv[8];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const float4 sw = __ldg(reinterpret_cast<const float4*>(wsc) + v);
+          const float2 lo = mul2(mul2(facc[2 * v], make_float2(sw.x, sw.y)), wr2);
+          const float2 hi = mul2(mul2(facc[2 * v + 1], make_float2(sw.z, sw.w)), wr2);
+          yv[v] = make_float4(lo.x, lo.y, hi.x, hi.y);
+        }
+        if (q * 32 + 32 <= ti.nvalid) {
+          uint8_t* box = s.ybox[warp - 2];
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // box free again
+          __syncwarp();
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            *reinterpret_cast<float4*>(box + lane * 128 + ((v ^ (lane & 7)) << 4)) = yv[v];
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            asm volatile(
+                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                ::"l"(&map_y), "r"(ti.col * BN + 32 * cb), "r"(ti.row0 + q * 32), "r"(smem_u32(box))
+                : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        } else if (valid) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(yout) + (size_t)row * H + ti.col * BN + 32 * cb);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) dst[v] = yv[v];
+        }
+        continue;
+      }
+      // dense: y = facc * sw, staged per row then written as whole bf16 rows
       const float2 wr2 = make_float2(wr, wr);
       float4* ys = reinterpret_cast<float4*>(&s.ystage[r][32 * cb]);
 #pragma unroll
@@ -537,6 +579,7 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       }
       quarter_sync(q);  // staging rows read before the next tile overwrites them
     }
+    if (!DENSE && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // stores complete
   }
 
   tc_fence_before();
@@ -609,7 +652,8 @@ bool make_tmap_2d(void* map, const void* base, long rows, int cols, int elem_byt
   cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(reinterpret_cast<CUtensorMap*>(map),
-            elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+            elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+            : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -663,7 +707,7 @@ cudaError_t launch_tc_dense_gate_up(const void* map_x, const void* map_w, int T,
                   h_sa, h_bf16, err, T, tiles);
 }
 
-cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
+cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const void* map_y, const int32_t* expert_offset,
                              int epr, int T, const float* bsa, const SparseRoute* routes,
                              const float* dn_scale, float* ybuf, int* err, cudaStream_t s) {
   const int max_rows = T * TOPK;
@@ -674,8 +718,9 @@ cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t
   if (e != cudaSuccess) return e;
   return launch_k(k, dim3(sm_count()), dim3(tc::THREADS), smem, s,
                   *reinterpret_cast<const CUtensorMap*>(map_a),
-                  *reinterpret_cast<const CUtensorMap*>(map_b), expert_offset, epr, 0, bsa, routes,
-                  dn_scale, static_cast<void*>(ybuf), err, max_rows, max_tiles);
+                  *reinterpret_cast<const CUtensorMap*>(map_b), *reinterpret_cast<const CUtensorMap*>(map_y),
+                  expert_offset, epr, 0, bsa, routes, dn_scale, static_cast<void*>(ybuf), err, max_rows,
+                  max_tiles);
 }
 
 cudaError_t launch_tc_dense_down(const void* map_h, const void* map_w, int T, const float* hsa,
@@ -688,8 +733,8 @@ cudaError_t launch_tc_dense_down(const void* map_h, const void* map_w, int T, co
   if (e != cudaSuccess) return e;
   return launch_k(k, dim3(std::min(sm_count(), tiles)), dim3(tc::THREADS), smem, s,
                   *reinterpret_cast<const CUtensorMap*>(map_h),
-                  *reinterpret_cast<const CUtensorMap*>(map_w), nullptr, 1, T, hsa, nullptr, dn_scale,
-                  static_cast<void*>(out), err, T, tiles);
+                  *reinterpret_cast<const CUtensorMap*>(map_w), *reinterpret_cast<const CUtensorMap*>(map_w),
+                  nullptr, 1, T, hsa, nullptr, dn_scale, static_cast<void*>(out), err, T, tiles);
 }
 
 }  // namespace gm

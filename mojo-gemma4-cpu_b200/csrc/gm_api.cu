@@ -95,6 +95,7 @@ struct gm_moe {
   int* router_counts = nullptr;     // router tile counters (zero between calls)
   alignas(64) unsigned char tmap_xg[128] = {};
   alignas(64) unsigned char tmap_bucket[128] = {};
+  alignas(64) unsigned char tmap_y[128] = {};        // f32 route rows (TMA stores of the down product)
   alignas(64) unsigned char tmap_xgb[128] = {};      // bf16 gathered rows (in ybuf's memory)
   alignas(64) unsigned char tmap_bucketb[128] = {};  // bf16 bucket
   bool tc_ok = false;           // TMA descriptors available
@@ -372,7 +373,8 @@ int carve_workspace(gm_moe* h, int tokens) {
   cudaMemset(h->dev_err, 0, sizeof(int));
   cudaMemset(h->router_counts, 0, sizeof(int) * router_tile_counters(tokens));
   h->tc_ok = make_tmap_i8(h->tmap_xg, h->xg, (long)tokens * TOPK, H, 128) &&
-             make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)tokens * TOPK, I, 128);
+             make_tmap_i8(h->tmap_bucket, h->bucket_i8, (long)tokens * TOPK, I, 128) &&
+             make_tmap_2d(h->tmap_y, h->ybuf, (long)tokens * TOPK, H, 4, 32);
   // bf16 prefill: the gathered activation rows live in ybuf, which is idle
   // until the down product writes it
   h->tcb_ok = make_tmap_2d(h->tmap_xgb, h->ybuf, (long)tokens * TOPK, H, 2, 128) &&
@@ -582,7 +584,7 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
       GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, Tn, h->xg_sa,
                                       L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
                "bq_phase1_gate_up.tc");
-      GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->expert_offset, h->epr, Tn,
+      GM_STAGE(h, s, launch_tc_phase2(h->tmap_bucket, L.tmap_dn, h->tmap_y, h->expert_offset, h->epr, Tn,
                                       h->bucket_sa, h->routes, L.dn_scale, h->ybuf, h->dev_err, s),
                "bq_phase2_down.tc");
     } else {

@@ -139,7 +139,8 @@ cudaError_t launch_tc_phase1(const void* map_a, const void* map_b, const int32_t
                              int epr, int T, const float* xg_sa, const float* gu_scale,
                              int8_t* bucket_i8, float* bucket_sa, uint16_t* bucket_bf16, int* err,
                              cudaStream_t s);
-cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const int32_t* expert_offset,
+// map_y: make_tmap_2d(f32 route rows ybuf, 4-byte elements, 32-row boxes)
+cudaError_t launch_tc_phase2(const void* map_a, const void* map_b, const void* map_y, const int32_t* expert_offset,
                              int epr, int T, const float* bsa, const SparseRoute* routes,
                              const float* dn_scale, float* ybuf, int* err, cudaStream_t s);
 // butterquant attention (attention_bq.cu).  runs: device array of
