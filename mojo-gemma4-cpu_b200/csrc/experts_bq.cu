@@ -254,9 +254,9 @@ bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
                  float* __restrict__ ybuf, int prologue_prefetch) {
   constexpr int GROUPS = (H / 32) / NTILE;  // hidden tile groups per expert
   constexpr int KCH = I / 32;               // 22 K chunks, 2 per K-block
-  __shared__ __align__(16) int8_t xs[RC_BQ * BSTRIDE];
-  __shared__ float s_adv[RC_BQ * NB_DOWN];
-  __shared__ float s_w[RC_BQ];
+  __shared__ __align__(16) int8_t xs2[2][RC_BQ * BSTRIDE];
+  __shared__ float s_adv2[2][RC_BQ * NB_DOWN];
+  __shared__ float s_w2[2][RC_BQ];
 
   if (!prologue_prefetch) pdl_wait();
   const int total = __ldg(chunk_off + epr) * GROUPS;
@@ -273,22 +273,29 @@ bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
   if (prologue_prefetch) pdl_wait();
   pdl_trigger();
   if (!any) return;
+  // a task's nr bucket rows, their block scales and route weights, by
+  // asynchronous copy into buffer b (the next task's while this one computes)
+  auto stage = [&](const Task& tk, int b) {
+    for (int i = tid; i < tk.nr * (I / 16); i += blockDim.x) {
+      const int r = i / (I / 16), c = i % (I / 16);
+      cp_async16(xs2[b] + r * BSTRIDE + c * 16, bi8 + (size_t)(tk.rbeg + r) * I + c * 16);
+    }
+    for (int i = tid; i < tk.nr * NB_DOWN; i += blockDim.x) cp_async4(&s_adv2[b][i], bsa + (size_t)tk.rbeg * NB_DOWN + i);
+    if (tid < tk.nr) cp_async4(&s_w2[b][tid], &routes[tk.rbeg + tid].weight);
+    cp_async_commit();
+  };
+  stage(cur, 0);
+  int xb = 0;
 
   while (true) {
     const int nr = cur.nr, rbeg = cur.rbeg;
     const int tile = cur.blk * NTILE + warp;
     const int8_t* wt = w_dn + (size_t)cur.e * H * I + (size_t)tile * 32 * I;
-    // nr contiguous bucket rows by asynchronous copy (rows >= nr only feed B
-    // columns whose results are never stored)
-    for (int i = tid; i < nr * (I / 16); i += blockDim.x) {
-      const int r = i / (I / 16), c = i % (I / 16);
-      cp_async16(xs + r * BSTRIDE + c * 16, bi8 + (size_t)(rbeg + r) * I + c * 16);
-    }
-    for (int i = tid; i < nr * NB_DOWN; i += blockDim.x)
-      s_adv[i] = __fmul_rn(bsa[(size_t)rbeg * NB_DOWN + i], INV127);
-    if (tid < nr) s_w[tid] = routes[rbeg + tid].weight;
     cp_async_wait_all();
     __syncthreads();
+    const int8_t* xs = xs2[xb];
+    const float* s_adv = s_adv2[xb];
+    const float* s_w = s_w2[xb];
 
     const bool two_groups = nr > 8;
     int iacc[2][2][4];
@@ -334,7 +341,7 @@ bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
             for (int i = 0; i < 4; ++i) {
               const int r = a * 8 + 2 * q + (i & 1);
               facc[a][b][i] =
-                  __fmaf_rn((float)iacc[a][b][i], s_adv[r * NB_DOWN + blk], facc[a][b][i]);
+                  __fmaf_rn((float)iacc[a][b][i], __fmul_rn(s_adv[r * NB_DOWN + blk], INV127), facc[a][b][i]);
               iacc[a][b][i] = 0;
             }
       }
@@ -346,6 +353,7 @@ bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
     if (has_next) {
       const int8_t* wtn = w_dn + (size_t)nxt.e * H * I + (size_t)(nxt.blk * NTILE + warp) * 32 * I;
       prefetch_chunks<DEPTH>(buf, wtn, 0, g, q);
+      stage(nxt, xb ^ 1);
     }
 
     // y[route][n] = facc * sw[n] * w_route  (moe.mojo:218-225)
@@ -370,10 +378,10 @@ bq_phase2_kernel(const int8_t* __restrict__ bi8, const float* __restrict__ bsa,
         }
       }
     }
-    __syncthreads();
     if (!has_next) break;
     cur = nxt;
     task += gridDim.x;
+    xb ^= 1;
   }
 }
 
