@@ -376,7 +376,8 @@ int gm_moe_device_status(gm_moe_t* h, int* device_error);
 /* Blocking form with the reference's calling convention (the reference's
  * dispatchers fan out and join before returning, kernels/helpers.mojo:295-327):
  * x and out may be host or device memory; host buffers are staged through the
- * handle's device buffers. */
+ * handle's device buffers, except a page-locked, device-mapped `out` (for
+ * example cudaHostAlloc memory), which the last kernel writes directly. */
 int gm_moe_forward_sync(gm_moe_t* h, int layer, const void* x, void* out, int T);
 
 /* ----------------------------------------------------- per-stage kernels --

@@ -325,6 +325,18 @@ bool is_device_ptr(const void* p) {
   return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
+// The device address of page-locked host memory mapped into the device's
+// address space (cudaHostAlloc / pinned tensors), NULL for device, pageable or
+// unmapped memory.
+void* mapped_host_ptr(void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
 // (Re)allocates the workspace for `tokens` activation rows and carves it.
 int carve_workspace(gm_moe* h, int tokens) {
   if (h->ws) {
@@ -1646,9 +1658,13 @@ int gm_moe_forward_sync(gm_moe_t* h, int layer, const void* x, void* out, int T)
     GM_TRY(h, cudaMemcpyAsync(h->x_stage, x, bytes, cudaMemcpyHostToDevice, s), "stage x");
     xd = h->x_stage;
   }
-  void* od = o_dev ? out : h->out_stage;
+  // A mapped page-locked `out` is written by the last kernel directly over the
+  // bus (overlapped with its own work) instead of a copy after it; other host
+  // memory goes through the staging buffer.
+  void* o_map = o_dev ? nullptr : mapped_host_ptr(out);
+  void* od = o_dev ? out : o_map ? o_map : h->out_stage;
   if ((rc = gm_moe_forward(h, layer, xd, od, T, s))) return rc;
-  if (!o_dev) GM_TRY(h, cudaMemcpyAsync(out, od, bytes, cudaMemcpyDeviceToHost, s), "stage out");
+  if (!o_dev && !o_map) GM_TRY(h, cudaMemcpyAsync(out, od, bytes, cudaMemcpyDeviceToHost, s), "stage out");
   GM_TRY(h, cudaStreamSynchronize(s), "forward_sync");
   return GM_OK;
 }

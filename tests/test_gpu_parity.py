@@ -441,6 +441,13 @@ def test_forward_deterministic_and_sync_host_path(layer_stress):
     out_h = np.zeros((T, H), np.uint16)
     blk.forward_sync(0, np.ascontiguousarray(x_np), out_h, T)
     assert np.array_equal(out_h, host(outs[0]))
+    # page-locked host buffers: the output is written by the kernel directly
+    x_p = torch.from_numpy(np.ascontiguousarray(x_np).view(np.int16)).view(torch.bfloat16).pin_memory()
+    o_p = torch.zeros(T, H, dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):
+        blk.forward_sync(0, x_p, o_p, T)
+        assert torch.equal(o_p.view(torch.int16), outs[0].cpu().view(torch.int16))
+        o_p.zero_()
 
 
 def test_forward_errors_and_edges(layer_default):
