@@ -11,7 +11,7 @@
 //  * rms_norm_bf16: kernels/rmsnorm.mojo:21-47 bf16(x*inv_rms*gamma) for the
 //    bf16 expert path (modeling/gemma_4_moe.mojo:537-541).
 //
-// One warp per row.  For the 128-wide FWHT lane l holds elements 4l..4l+3 of
+// One warp per row (two for bq_norm_quant).  For the 128-wide FWHT lane l holds elements 4l..4l+3 of
 // each block (butterfly strides 1,2 in registers, 4..64 across lanes); for the
 // 64-wide FWHT lane l holds 2l, 2l+1 (stride 1 in registers, 2..32 across).
 #include "gm_kernels.h"
@@ -47,35 +47,64 @@ __device__ __forceinline__ void fwht64_lane2(float& v0, float& v1, int lane) {
   v1 = __fmul_rn(v1, fwht_scale_64());
 }
 
+// Two warps per row: warp h of the pair holds blocks [11h, 11h + 11).  The
+// sum of squares keeps the one-warp order exactly: lane l of warp 0 runs its
+// chain over blocks 0..10, hands the running sum to lane l of warp 1, which
+// continues over blocks 11..21 and does the warp tree; the absmax (a max, so
+// order-free) is combined across the pair.  Half the registers per thread and
+// twice the warps of a one-warp-per-row kernel.
+constexpr int NQ_ROWS = 4;  // rows per 256-thread CTA
 __global__ void __launch_bounds__(256)
 bq_norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma, int T,
                      int8_t* __restrict__ xi8, float* __restrict__ xsa, float* __restrict__ inv_out) {
+  __shared__ float s_ss[NQ_ROWS][32];
+  __shared__ float s_inv[NQ_ROWS];
+  __shared__ float s_amax[NQ_ROWS][2];
   pdl_wait();
   pdl_trigger();
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (t >= T) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int k = warp >> 1, h = warp & 1;
+  const int t = blockIdx.x * NQ_ROWS + k;
+  if (t >= T) return;  // both warps of the pair leave together
   constexpr int NBLK = H / NORM_BLOCK;  // 22
-  const uint16_t* xr = x + (size_t)t * H;
-  float v[NBLK][4];
-  float ss = 0.0f;
+  constexpr int NH = NBLK / 2;          // 11 per warp
+  const int bar = 1 + k;                // named barrier of the pair (64 threads)
+  const uint16_t* xr = x + (size_t)t * H + h * NH * NORM_BLOCK;
+  float v[NH][4];
 #pragma unroll
-  for (int b = 0; b < NBLK; ++b) {
+  for (int b = 0; b < NH; ++b) {
     uint2 raw = *reinterpret_cast<const uint2*>(xr + b * NORM_BLOCK + 4 * lane);
     v[b][0] = bf2f(raw.x & 0xFFFFu);
     v[b][1] = bf2f(raw.x >> 16);
     v[b][2] = bf2f(raw.y & 0xFFFFu);
     v[b][3] = bf2f(raw.y >> 16);
+  }
+  float ss = 0.0f;
+  if (h == 1) {
+    asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");  // warp 0's chain is in s_ss
+    ss = s_ss[k][lane];
+  }
+#pragma unroll
+  for (int b = 0; b < NH; ++b)
 #pragma unroll
     for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[b][j], v[b][j]));
+  if (h == 0) {
+    s_ss[k][lane] = ss;
+    asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");
+  } else {
+    ss = warp_sum(ss);
+    const float inv = inv_rms_from_sumsq(ss);
+    if (lane == 0) {
+      s_inv[k] = inv;
+      if (inv_out) inv_out[t] = inv;
+    }
   }
-  ss = warp_sum(ss);
-  const float inv = inv_rms_from_sumsq(ss);
-  if (inv_out && lane == 0) inv_out[t] = inv;
+  asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");  // s_inv written
+  const float inv = s_inv[k];
   float amax = 0.0f;
 #pragma unroll
-  for (int b = 0; b < NBLK; ++b) {
-    uint2 g = *reinterpret_cast<const uint2*>(gamma + b * NORM_BLOCK + 4 * lane);
+  for (int b = 0; b < NH; ++b) {
+    uint2 g = *reinterpret_cast<const uint2*>(gamma + (h * NH + b) * NORM_BLOCK + 4 * lane);
     float gv[4] = {bf2f(g.x & 0xFFFFu), bf2f(g.x >> 16), bf2f(g.y & 0xFFFFu), bf2f(g.y >> 16)};
 #pragma unroll
     for (int j = 0; j < 4; ++j) v[b][j] = __fmul_rn(__fmul_rn(v[b][j], inv), gv[j]);
@@ -84,16 +113,19 @@ bq_norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
     for (int j = 0; j < 4; ++j) amax = fmaxf(amax, fabsf(v[b][j]));
   }
   amax = warp_max(amax);
+  if (lane == 0) s_amax[k][h] = amax;
+  asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");
+  amax = fmaxf(s_amax[k][0], s_amax[k][1]);
   const float qinv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-  int8_t* dst = xi8 + (size_t)t * H;
+  int8_t* dst = xi8 + (size_t)t * H + h * NH * NORM_BLOCK;
 #pragma unroll
-  for (int b = 0; b < NBLK; ++b) {
+  for (int b = 0; b < NH; ++b) {
     uint32_t packed = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) packed |= (uint32_t)(quantize_i8(v[b][j], qinv) & 0xFF) << (8 * j);
     *reinterpret_cast<uint32_t*>(dst + b * NORM_BLOCK + 4 * lane) = packed;
   }
-  if (lane == 0) xsa[t] = amax;
+  if (h == 0 && lane == 0) xsa[t] = amax;
 }
 
 __global__ void __launch_bounds__(256)
@@ -161,9 +193,8 @@ rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
 cudaError_t launch_bq_norm_quant(const uint16_t* x, const uint16_t* gamma, int T, int8_t* xi8,
                                  float* xsa, float* inv_rms, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  // a warp per token; small batches spread over more SMs (2 warps per CTA)
-  const int wpb = T <= 512 ? 2 : 8;
-  return launch_k(bq_norm_quant_kernel, dim3((T + wpb - 1) / wpb), dim3(32 * wpb), 0, s, x, gamma, T, xi8,
+  // two warps per token, four tokens per CTA
+  return launch_k(bq_norm_quant_kernel, dim3((T + NQ_ROWS - 1) / NQ_ROWS), dim3(256), 0, s, x, gamma, T, xi8,
                   xsa, inv_rms);
 }
 

@@ -412,22 +412,29 @@ static int num_sms() {
 // the weights phase 1 reads first are pulled into L2 while the router and the
 // schedule -- latency-bound kernels that leave HBM idle -- run.  It reads
 // nothing another kernel writes, so it does not wait on its predecessor.
-__global__ void __launch_bounds__(256) l2_prefetch_kernel(const uint8_t* __restrict__ base, size_t bytes) {
+// Prefetches n_units units of unit_bytes: unit k starts at base + (first +
+// stride*k) * unit_bytes.
+__global__ void __launch_bounds__(256) l2_prefetch_kernel(const uint8_t* __restrict__ base, size_t unit_bytes,
+                                                         int n_units, int first, int stride) {
   pdl_trigger();
   constexpr size_t CHUNK = 32768;
+  const size_t bytes = unit_bytes * (size_t)n_units;
   for (size_t off = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) * CHUNK; off < bytes;
        off += (size_t)gridDim.x * blockDim.x * CHUNK) {
-    const uint32_t n = (uint32_t)min((size_t)CHUNK, bytes - off) & ~15u;
-    if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"(n) : "memory");
+    const size_t k = off / unit_bytes, in = off % unit_bytes;
+    const uint32_t n = (uint32_t)min((size_t)CHUNK, unit_bytes - in) & ~15u;
+    const uint8_t* p = base + ((size_t)first + (size_t)stride * k) * unit_bytes + in;
+    if (n) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(n) : "memory");
   }
 }
 
-cudaError_t launch_l2_prefetch(const void* base, size_t bytes, cudaStream_t s) {
-  if (!bytes) return cudaSuccess;
-  const size_t chunks = (bytes + 32767) / 32768;
+cudaError_t launch_l2_prefetch(const void* base, size_t unit_bytes, int n_units, int first, int stride,
+                               cudaStream_t s) {
+  if (!unit_bytes || n_units <= 0) return cudaSuccess;
+  const size_t chunks = (unit_bytes * n_units + 32767) / 32768;
   const int blocks = (int)std::min<size_t>(148, (chunks + 255) / 256);
-  return launch_k(l2_prefetch_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const uint8_t*>(base),
-                  bytes);
+  return launch_k(l2_prefetch_kernel, dim3(blocks), dim3(256), 0, s, static_cast<const uint8_t*>(base), unit_bytes,
+                  n_units, first, stride);
 }
 
 template <typename K>

@@ -173,7 +173,7 @@ struct gm_moe {
 
 namespace {
 
-constexpr int L2_PREFETCH_EXPERTS = 30;  // 30 x 3.97 MB of gate/up weights (L2 is 126 MB): 1-1.5 us per b64 step better than 20
+constexpr int L2_PREFETCH_EXPERTS = 30;  // 30 x 3.97 MB of gate/up weights (L2 is 126 MB)
 
 int set_err(gm_moe* h, int code, const char* fmt, ...) {
   char buf[512];
@@ -1063,8 +1063,13 @@ int forward_impl(gm_moe* h, int layer, const void* x, void* out, int T, void* st
     const bool pdl = tls_pdl;
     tls_pdl = false;
     const long n0 = tls_kernel_launches;
+    // every other expert from the second on (when the rank holds enough):
+    // the first wave of phase 1 then mixes experts already in L2 with experts
+    // streamed from HBM, instead of running from L2 while HBM idles
+    const int npf = std::min(h->epr, L2_PREFETCH_EXPERTS);
+    const int stride = 2 * npf <= h->epr ? 2 : 1;
     const cudaError_t pe =
-        launch_l2_prefetch(L.gu_q, (size_t)std::min(h->epr, L2_PREFETCH_EXPERTS) * GU * H, h->side_stream);
+        launch_l2_prefetch(L.gu_q, (size_t)GU * H, npf, stride == 2 ? 1 : 0, stride, h->side_stream);
     h->launches += tls_kernel_launches - n0;
     tls_pdl = pdl;
     GM_TRY(h, pe, "l2_prefetch");

@@ -108,7 +108,9 @@ cudaError_t launch_dense_gate_up(const int8_t* xi8, const float* xsa, int T, con
 cudaError_t launch_dense_down(const int8_t* hi8, const float* hsa, int T, const int8_t* wd,
                               const float* dsc, uint16_t* out, cudaStream_t s);
 // bulk L2 prefetch of [base, base + bytes) (16-byte aligned base)
-cudaError_t launch_l2_prefetch(const void* base, size_t bytes, cudaStream_t s);
+// L2 prefetch of n_units units of unit_bytes, unit k at (first + stride*k)
+cudaError_t launch_l2_prefetch(const void* base, size_t unit_bytes, int n_units, int first, int stride,
+                               cudaStream_t s);
 cudaError_t launch_bq_phase2(const int8_t* bi8, const float* bsa, const int32_t* expert_offset,
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_dn, const float* dn_scale, float* ybuf,
