@@ -505,20 +505,21 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
   constexpr int NT = C / 8;                       // QK mma N-tiles
   constexpr int NW = DEC_WARPS;
   constexpr int CPW = C / NW;                     // softmax columns per warp
-  constexpr int KSW = HD / 32 / NW;               // 32-wide K steps per warp
+  constexpr int KS2 = HD / 32 / 2;                // QK: warp pair (2nt, 2nt+1) = one N-tile, K in halves
   constexpr int TPR = DEC_THREADS / PF_TP;        // copying threads per row
   constexpr int CHUNKS = HD / (16 * TPR);
   constexpr int NPW = HD / NW;                    // head columns per warp in PV
   constexpr int NTW = NPW / 8;                    // PV mma N-tiles per warp
   constexpr int VPT = HD / DEC_THREADS;           // V columns each thread transposes
-  static_assert(KSW >= 1 && CHUNKS >= 1 && NTW >= 1 && (VPT == 1 || VPT == 2), "tile geometry");
+  static_assert(NT * 2 == NW && CPW == 4 && KS2 >= 1 && CHUNKS >= 1 && NTW >= 1 && (VPT == 1 || VPT == 2),
+                "tile geometry");
   const int t0 = blockIdx.x * QT, g = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int grp = lane >> 2, tig = lane & 3;
   extern __shared__ __align__(16) uint8_t dsm[];
   Sm& sm = *reinterpret_cast<Sm*>(dsm);
   __shared__ __align__(16) int8_t qs[C * HD];
-  __shared__ int part[NW][C][PF_TP];
+  __shared__ int part[2][C][PF_TP];  // the two K halves of every score
   __shared__ float corr_s[C];
   __shared__ float l_s[C];
 
@@ -533,16 +534,19 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
     reinterpret_cast<int4*>(qs)[i] = v;
   }
   __syncthreads();
-  uint32_t bq[KSW][NT][2];
+  // QK: warp w computes N-tile w/2 (8 columns) over K half w%2
+  const int qnt = warp >> 1, qkh = warp & 1;
+  uint32_t bq[KS2][2];
 #pragma unroll
-  for (int ks = 0; ks < KSW; ++ks)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int k0 = (warp * KSW + ks) * 32 + 4 * tig;
-      const int8_t* qc = qs + (nt * 8 + grp) * HD + k0;
-      bq[ks][nt][0] = *reinterpret_cast<const uint32_t*>(qc);
-      bq[ks][nt][1] = *reinterpret_cast<const uint32_t*>(qc + 16);
-    }
+  for (int ks = 0; ks < KS2; ++ks) {
+    const int k0 = (qkh * KS2 + ks) * 32 + 4 * tig;
+    const int8_t* qc = qs + (qnt * 8 + grp) * HD + k0;
+    bq[ks][0] = *reinterpret_cast<const uint32_t*>(qc);
+    bq[ks][1] = *reinterpret_cast<const uint32_t*>(qc + 16);
+  }
+  // softmax: half-warp hf = lane / 16 of warp w owns columns w + 8*(2*pp + hf),
+  // pp = 0, 1; lane % 16 is the position in the tile
+  const int hf = lane >> 4, l16 = lane & 15;
 
   const float inv127 = 1.0f / 127.0f;
   const float inv127sq = __fmul_rn(inv127, inv127);
@@ -618,29 +622,22 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
       issue(p0 + (PF_STAGES - 1) * PF_TP, (buf + PF_STAGES - 1) % PF_STAGES);
       cp_async_wait_group<PF_STAGES - 1>();  // this tile's group has landed
       __syncthreads();
-      // ---- A: scores
+      // ---- A: scores (exact int32 partials of the two K halves)
       {
-        int cacc[NT][4];
+        int cacc[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) cacc[nt][i] = 0;
-#pragma unroll
-        for (int ks = 0; ks < KSW; ++ks) {
-          const int k0 = (warp * KSW + ks) * 32 + 4 * tig;
+        for (int ks = 0; ks < KS2; ++ks) {
+          const int k0 = (qkh * KS2 + ks) * 32 + 4 * tig;
           const int8_t* r0 = &sm.kv.k[buf][grp][k0];
           const int8_t* r1 = &sm.kv.k[buf][grp + 8][k0];
           const uint32_t a0 = *reinterpret_cast<const uint32_t*>(r0), a1 = *reinterpret_cast<const uint32_t*>(r1);
           const uint32_t a2 = *reinterpret_cast<const uint32_t*>(r0 + 16),
                          a3 = *reinterpret_cast<const uint32_t*>(r1 + 16);
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma_s8(cacc[nt], a0, a1, a2, a3, bq[ks][nt][0], bq[ks][nt][1]);
+          mma_s8(cacc, a0, a1, a2, a3, bq[ks][0], bq[ks][1]);
         }
-        // cacc[nt][0..1]: position grp, columns nt*8 + 2*tig (+1); [2..3]: position grp + 8
+        // cacc[0..1]: position grp, columns qnt*8 + 2*tig (+1); [2..3]: position grp + 8
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) part[warp][nt * 8 + 2 * tig + (i & 1)][grp + 8 * (i >> 1)] = cacc[nt][i];
+        for (int i = 0; i < 4; ++i) part[qkh][qnt * 8 + 2 * tig + (i & 1)][grp + 8 * (i >> 1)] = cacc[i];
       }
       // V tile -> transposed bf16 (every position of the buffer: rows past n
       // hold finite stale bytes and meet zero weights)
@@ -671,33 +668,41 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
         }
       }
       __syncthreads();
-      // ---- B: online softmax of the owned columns (lane = position in the tile)
+      // ---- B: online softmax, two columns per warp at a time (one per
+      // half-warp; the 16-lane trees give the 32-lane trees' results, as the
+      // upper lanes only ever added -inf maxima and zero weights)
       {
-        const bool in_tile = lane < n;
-        const float ksc = in_tile ? sm.kv.ks[buf][lane] : 0.0f;
-        const float vsc = in_tile ? sm.kv.vs[buf][lane] : 0.0f;
-        const int pl = lane < PF_TP ? lane : 0;
-        const int p = p0 + lane;
+        const bool in_tile = l16 < n;
+        const float ksc = in_tile ? sm.kv.ks[buf][l16] : 0.0f;
+        const float vsc = in_tile ? sm.kv.vs[buf][l16] : 0.0f;
+        const int p = p0 + l16;
 #pragma unroll
-        for (int j = 0; j < CPW; ++j) {
-          const int col = warp + NW * j;
-          const bool ok = in_tile && p >= c_lo[j] && p <= c_hi[j];
-          int dot = 0;
+        for (int pp = 0; pp < 2; ++pp) {
+          const int j0 = 2 * pp;  // this half's column index is j0 + hf
+          const int col = warp + NW * (j0 + hf);
+          const float fqj = hf ? fq[j0 + 1] : fq[j0];
+          const float mj = hf ? m[j0 + 1] : m[j0];
+          const float lj = hf ? l[j0 + 1] : l[j0];
+          const int lo = hf ? c_lo[j0 + 1] : c_lo[j0], hi_p = hf ? c_hi[j0 + 1] : c_hi[j0];
+          const bool ok = in_tile && p >= lo && p <= hi_p;
+          const int dot = part[0][col][l16] + part[1][col][l16];
+          const float sc = ok ? __fmul_rn(__fmul_rn(__fmul_rn((float)dot, fqj), ksc), inv127sq) : NEG_BIG;
+          float mx = sc;
 #pragma unroll
-          for (int w = 0; w < NW; ++w) dot += part[w][col][pl];
-          const float sc = ok ? __fmul_rn(__fmul_rn(__fmul_rn((float)dot, fq[j]), ksc), inv127sq) : NEG_BIG;
-          const float mn = fmaxf(m[j], warp_max(sc));
-          const float cr = fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(m[j], mn)));
+          for (int o = 8; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          const float mn = fmaxf(mj, mx);
+          const float cr = fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(mj, mn)));
           const float w = ok ? fast_exp_softmax_biased(fmaxf(-87.0f, __fsub_rn(sc, mn))) : 0.0f;
-          l[j] = __fadd_rn(__fmul_rn(l[j], cr), warp_sum(w));
-          m[j] = mn;
-          if (lane < PF_TP) {
-            const float pw = __fmul_rn(__fmul_rn(w, vsc), inv127);
-            const uint16_t hi = f2bf(pw);
-            sm.phi[col][lane] = hi;
-            sm.plo[col][lane] = f2bf(__fsub_rn(pw, bf2f(hi)));
-          }
-          if (lane == 0) corr_s[col] = cr;
+          float ws = w;
+#pragma unroll
+          for (int o = 8; o >= 1; o >>= 1) ws = __fadd_rn(ws, __shfl_xor_sync(0xffffffffu, ws, o));
+          const float ln = __fadd_rn(__fmul_rn(lj, cr), ws);
+          if (hf) { m[j0 + 1] = mn; l[j0 + 1] = ln; } else { m[j0] = mn; l[j0] = ln; }
+          const float pw = __fmul_rn(__fmul_rn(w, vsc), inv127);
+          const uint16_t hb = f2bf(pw);
+          sm.phi[col][l16] = hb;
+          sm.plo[col][l16] = f2bf(__fsub_rn(pw, bf2f(hb)));
+          if (l16 == 0) corr_s[col] = cr;
         }
       }
       __syncthreads();
@@ -738,9 +743,9 @@ attn_prefill_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f
       __syncthreads();  // this buffer and part / vt / phi / plo / corr_s are reused
     }
   }
-  if (lane == 0) {
-#pragma unroll
-    for (int j = 0; j < CPW; ++j) l_s[warp + NW * j] = l[j];
+  if (l16 == 0) {
+    l_s[warp + NW * hf] = hf ? l[1] : l[0];
+    l_s[warp + NW * (2 + hf)] = hf ? l[3] : l[2];
   }
   __syncthreads();
 #pragma unroll
