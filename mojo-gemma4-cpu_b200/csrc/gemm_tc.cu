@@ -514,21 +514,25 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         // (issued by lane 0, no barrier with the other warps); a partial one
         // is stored row by row from registers
         const float2 wr2 = make_float2(wr, wr);
-        float4 yv[8];
+        const bool full = q * 32 + 32 <= ti.nvalid;  // warp-uniform
+        uint8_t* box = s.ybox[warp - 2];
+        if (full) {
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // box free again
+          __syncwarp();
+        }
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(yout) + (size_t)row * H + ti.col * BN + 32 * cb);
 #pragma unroll
         for (int v = 0; v < 8; ++v) {
           const float4 sw = __ldg(reinterpret_cast<const float4*>(wsc) + v);
           const float2 lo = mul2(mul2(facc[2 * v], make_float2(sw.x, sw.y)), wr2);
           const float2 hi = mul2(mul2(facc[2 * v + 1], make_float2(sw.z, sw.w)), wr2);
-          yv[v] = make_float4(lo.x, lo.y, hi.x, hi.y);
+          const float4 yv = make_float4(lo.x, lo.y, hi.x, hi.y);
+          if (full)
+            *reinterpret_cast<float4*>(box + lane * 128 + ((v ^ (lane & 7)) << 4)) = yv;
+          else if (valid)
+            dst[v] = yv;
         }
-        if (q * 32 + 32 <= ti.nvalid) {
-          uint8_t* box = s.ybox[warp - 2];
-          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // box free again
-          __syncwarp();
-#pragma unroll
-          for (int v = 0; v < 8; ++v)
-            *reinterpret_cast<float4*>(box + lane * 128 + ((v ^ (lane & 7)) << 4)) = yv[v];
+        if (full) {
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           __syncwarp();
           if (lane == 0) {
@@ -538,10 +542,6 @@ tc_phase2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 : "memory");
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
-        } else if (valid) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(yout) + (size_t)row * H + ti.col * BN + 32 * cb);
-#pragma unroll
-          for (int v = 0; v < 8; ++v) dst[v] = yv[v];
         }
         continue;
       }

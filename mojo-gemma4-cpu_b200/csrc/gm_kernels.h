@@ -52,6 +52,8 @@ constexpr int ROUTER_SLICES = H / 256;
 constexpr int ROUTER_WIDE_SLICES = 4;
 constexpr int ROUTER_WIDE_MIN_TOKENS = 3584;
 int router_ksplit(int T);
+// Up to this many tokens the top-8 and the schedule run as one CTA.
+constexpr int TOPK_SCHEDULE_FUSED_MAX = 32;
 // Tile counters of the FMA kernel's in-kernel reduction (ints, zero between calls).
 int router_tile_counters(int T);
 // Router workspace: partials, inv_rms [T], an error word, tile counters.

@@ -21,12 +21,14 @@
 //    norm kernel launched just before it (that kernel triggers only after its
 //    own wait, so x is complete); it waits for its predecessor only after its
 //    stores, so its completion implies the norm kernel's (router.cu);
-//  * the router chunks (64 K each) arrive by cp.async in a 4-stage ring, two
+//  * the router chunks (64 K each) arrive by cp.async in a 6-stage ring, two
 //    chunks ahead; each thread loads its x units two chunks ahead into
-//    registers; the activation parts are produced by all 256 threads into a
-//    2-stage ring in the 128-byte-swizzled K-major layout the MMA descriptors
-//    read, so one chunk's MMAs run while the next chunk is prepared; the TMEM
-//    accumulator is staged through shared memory for coalesced stores.
+//    registers; the activation parts are produced by all 256 threads (packed
+//    f32x2 products and bf16x2 roundings) into a 4-stage ring in the
+//    128-byte-swizzled K-major layout the MMA descriptors read, so a chunk's
+//    MMAs have four chunk periods to complete before its stages are reused;
+//    the TMEM accumulator is staged through shared memory for coalesced
+//    stores.
 //
 // Every mbarrier wait is bounded (tc::mbar_wait, ~1 s); on expiry the kernel
 // writes 1 into *err, skips the remaining MMAs, still frees its TMEM and
@@ -43,7 +45,11 @@ constexpr int RT_BK = 64;                // bf16 per 128-byte swizzle row (one K
 constexpr int RT_CHUNKS = H / RT_BK;     // 44 K chunks in all
 constexpr int RT_THREADS = 256;
 constexpr int RT_TILE = 128 * 128;       // bytes of one [128 rows][64 bf16] operand tile
-constexpr int RT_BST = 4;                // router chunk ring (two chunks ahead)
+constexpr int RT_AST = 4;                // activation (hi, lo) stages
+constexpr int RT_XLA = 2;                // x chunks loaded ahead into registers
+constexpr int RT_BST = RT_AST + 2;       // router chunk ring, filled two chunks ahead
+// chunk c's activation stage c % RT_AST and router stage (c + 2) % RT_BST were
+// both last read by the MMAs of chunk c - RT_AST
 constexpr int RT_YSTR = E + 4;           // output staging row stride (floats)
 
 // kind::f16: D = f32 (bits 4-5 = 1), A = B = bf16 (bits 7-9, 10-12 = 1), both
@@ -53,11 +59,12 @@ constexpr uint32_t IDESC_BF16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)
 
 struct RouterSmem {
   uint8_t b[RT_BST][RT_TILE];     // router rows (experts) x 64 bf16 per chunk; 1024-aligned
-  uint8_t a[2][2][RT_TILE];       // 2 stages x {hi, lo} x [128 tokens][64 bf16]
-  uint64_t done[2];               // MMAs of the chunks using A stage 0 / 1 complete
+  uint8_t a[RT_AST][2][RT_TILE];  // RT_AST stages x {hi, lo} x [128 tokens][64 bf16]
+  uint64_t done[RT_AST];          // MMAs of the chunks using A stage 0..RT_AST-1 complete
   uint32_t tmem_base;
   int failed;
 };
+static_assert(sizeof(RouterSmem) + 1024 <= 227 * 1024, "router shared memory (plus alignment) fits one CTA");
 static_assert(sizeof(float) * RT_BM * RT_YSTR <= sizeof(((RouterSmem*)0)->b) + sizeof(((RouterSmem*)0)->a),
               "output staging fits in the operand rings");
 
@@ -72,16 +79,30 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t da, uint64
 // Byte offset of 16-byte unit j (0..7) of row r in a 128-byte-swizzled tile.
 __device__ __forceinline__ int sw128(int r, int j) { return r * 128 + ((j ^ (r & 7)) << 4); }
 
-__device__ __forceinline__ uint32_t pack_bf16(uint16_t lo, uint16_t hi) {
-  return (uint32_t)lo | ((uint32_t)hi << 16);
+// (element 0 = low half, element 1 = high half) of a bf16 pair, as floats
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+// round-to-nearest-even bf16 pair: v.x -> low half, v.y -> high half
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float2 v) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(v.y), "f"(v.x));
+  return r;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 c;
+  asm("sub.rn.f32x2 %0, %1, %2;"
+      : "=l"(reinterpret_cast<uint64_t&>(c))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return c;
 }
 
 // One CTA: 128 tokens x all 128 experts x K chunks [blockIdx.y*CPS, +CPS).
-// Per chunk c: the router chunk arrives by cp.async two chunks ahead (4-stage
-// ring), the thread's x units two chunks ahead in registers; x*s is split
-// into its hi / lo bf16 parts in A stage c%2 (after the MMAs of chunk c-2,
+// Per chunk c: the router chunk arrives by cp.async two chunks ahead (6-stage
+// ring), the thread's x units RT_XLA chunks ahead in registers; x*s is split
+// into its hi / lo bf16 parts in A stage c%4 (after the MMAs of chunk c-4,
 // which read that stage, complete), and thread 0 issues the chunk's 8 MMAs,
-// which then run while the threads prepare chunk c+1.
+// which then run while the threads prepare the next chunks.
 template <int CPS>
 __global__ void __launch_bounds__(RT_THREADS, 1)
 router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
@@ -120,8 +141,7 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
   issue_b(0);
   issue_b(1);
   if (tid == 0) {
-    mbar_init(&s.done[0], 1);
-    mbar_init(&s.done[1], 1);
+    for (int i = 0; i < RT_AST; ++i) mbar_init(&s.done[i], 1);
     s.failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -132,9 +152,9 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
   pdl_trigger();  // no wait before reading x: see the file comment
-  uint4 xv[3][4], rs[3];
-  load_x(0, xv[0], rs[0]);
-  if (CPS > 1) load_x(1, xv[1], rs[1]);
+  uint4 xv[RT_XLA + 1][4], rs[RT_XLA + 1];
+#pragma unroll
+  for (int c = 0; c < RT_XLA && c < CPS; ++c) load_x(c, xv[c], rs[c]);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -142,30 +162,30 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
 
 #pragma unroll
   for (int c = 0; c < CPS; ++c) {
-    const int st = c & 1;
-    if (c + 2 < CPS) load_x(c + 2, xv[(c + 2) % 3], rs[(c + 2) % 3]);
-    // the MMAs of chunk c-2 read A stage st and B stage (c+2) % RT_BST
-    if (c >= 2) mbar_wait(&s.done[st], (uint32_t)(((c >> 1) - 1) & 1), &s.failed);
+    const int st = c % RT_AST;
+    if (c + RT_XLA < CPS) load_x(c + RT_XLA, xv[(c + RT_XLA) % (RT_XLA + 1)], rs[(c + RT_XLA) % (RT_XLA + 1)]);
+    // stage st and router stage (c+2) % RT_BST were read by the MMAs of chunk
+    // c - RT_AST (both rings are fresh before that)
+    if (c >= RT_AST) {
+      const int cw = c - RT_AST;
+      mbar_wait(&s.done[cw % RT_AST], (uint32_t)((cw / RT_AST) & 1), &s.failed);
+    }
     issue_b(c + 2);
-    const uint32_t rsw[4] = {rs[c % 3].x, rs[c % 3].y, rs[c % 3].z, rs[c % 3].w};
+    const uint4 rc = rs[c % (RT_XLA + 1)];
+    const uint32_t rsw[4] = {rc.x, rc.y, rc.z, rc.w};
+    float2 ss[4];  // this thread's 8 router scales of the chunk, as pairs
+#pragma unroll
+    for (int p = 0; p < 4; ++p) ss[p] = unpack_bf16x2(rsw[p]);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const uint4 v = xv[c % 3][q];
+      const uint4 v = xv[c % (RT_XLA + 1)][q];
       const uint32_t xw[4] = {v.x, v.y, v.z, v.w};
       uint32_t hi[4], lo[4];
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
-        uint16_t h2[2], l2[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float xs = bf2f(h ? xw[p] >> 16 : xw[p] & 0xFFFFu);
-          const float ss = bf2f(h ? rsw[p] >> 16 : rsw[p] & 0xFFFFu);
-          const float sv = __fmul_rn(xs, ss);                   // x*s, exact
-          h2[h] = f2bf(sv);
-          l2[h] = f2bf(__fsub_rn(sv, bf2f(h2[h])));             // exact residual (<= 8 bits)
-        }
-        hi[p] = pack_bf16(h2[0], h2[1]);
-        lo[p] = pack_bf16(l2[0], l2[1]);
+        const float2 sv = mul2(unpack_bf16x2(xw[p]), ss[p]);  // x*s, exact
+        hi[p] = pack_bf16x2_rn(sv);
+        lo[p] = pack_bf16x2_rn(sub2(sv, unpack_bf16x2(hi[p])));  // exact residual (<= 8 bits)
       }
       const int off = sw128(r0 + 32 * q, j);
       *reinterpret_cast<uint4*>(s.a[st][0] + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
@@ -187,9 +207,8 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
       mma_commit(&s.done[st]);
     }
   }
-  // the last two chunks' completions
-  if (CPS >= 2) mbar_wait(&s.done[(CPS - 2) & 1], (uint32_t)(((CPS - 2) >> 1) & 1), &s.failed);
-  mbar_wait(&s.done[(CPS - 1) & 1], (uint32_t)(((CPS - 1) >> 1) & 1), &s.failed);
+  // every chunk's MMAs complete (in order: the last commit covers them all)
+  mbar_wait(&s.done[(CPS - 1) % RT_AST], (uint32_t)(((CPS - 1) / RT_AST) & 1), &s.failed);
   tc_fence_after();
 
   // epilogue: warp w reads TMEM lanes 32*(w&3).. and columns 64*(w>>2)..,

@@ -314,9 +314,10 @@ cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, const float
                                  int32_t* route_idx, float* route_w, int expert_base, int epr,
                                  int route_chunk, int32_t* expert_offset, SparseRoute* routes,
                                  int32_t* route_pos, int32_t* chunk_off, int32_t* counts, cudaStream_t s) {
-  // one CTA when the logits arrive reduced (small T); otherwise the top-8 is
-  // spread over T/4 CTAs first
-  if (T <= 32 && router_ksplit(T) == 1)
+  // one CTA up to TOPK_SCHEDULE_FUSED_MAX tokens (32 warps, one token each;
+  // the router has reduced its K slices); above, the top-8 is spread over
+  // T/4 CTAs first
+  if (T <= TOPK_SCHEDULE_FUSED_MAX)
     return launch_k(topk_schedule_kernel, dim3(1), dim3(1024), 0, s, logits, router_ksplit(T), pes,
                     inv_rms, T, route_idx, route_w, expert_base, epr, route_chunk, expert_offset, routes,
                     route_pos, chunk_off);
