@@ -601,11 +601,27 @@ gather_rows_kernel(const uint8_t* __restrict__ x, int row_bytes, const float* __
   pdl_trigger();
   const int R = expert_offset[epr];
   const int lane = threadIdx.x & 31;
+  const int n16 = row_bytes / 16;
+  // GATHER_BATCH 16-byte units per lane are loaded before any is stored, so a
+  // row (176 units for int8 rows) costs one L2 round trip, not six
+  constexpr int GATHER_BATCH = 6;
   for (int pos = blockIdx.x * 8 + (threadIdx.x >> 5); pos < R; pos += gridDim.x * 8) {
     const int tok = routes[pos].token;
     const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok * row_bytes);
     uint4* dst = reinterpret_cast<uint4*>(xg + (size_t)pos * row_bytes);
-    for (int c = lane; c < row_bytes / 16; c += 32) dst[c] = src[c];
+    for (int c0 = 0; c0 < n16; c0 += 32 * GATHER_BATCH) {
+      uint4 v[GATHER_BATCH];
+#pragma unroll
+      for (int i = 0; i < GATHER_BATCH; ++i) {
+        const int c = c0 + i * 32 + lane;
+        if (c < n16) v[i] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int i = 0; i < GATHER_BATCH; ++i) {
+        const int c = c0 + i * 32 + lane;
+        if (c < n16) dst[c] = v[i];
+      }
+    }
     if (lane == 0 && xsa) xg_sa[pos] = xsa[tok];
   }
 }

@@ -42,11 +42,12 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
 }
 
 // simd_math/ops.mojo:25-31 quantize_i8: clamp(roundeven(v*inv), -128, 127)
+// Clamping before rounding gives the same integer for every input (NaN and
+// +-inf included); 1.5*2^23 + t for |t| <= 128 rounds to the nearest even
+// integer in the low mantissa bits, so no float-to-int conversion is needed.
 __device__ __forceinline__ int quantize_i8(float v, float inv) {
-  float r = rintf(__fmul_rn(v, inv));
-  r = fmaxf(r, -128.0f);
-  r = fminf(r, 127.0f);
-  return (int)r;
+  const float t = fminf(fmaxf(__fmul_rn(v, inv), -128.0f), 127.0f);
+  return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
 }
 
 // simd_math/ops.mojo:72-96 exp_f32_fast (~0.3% rel. error, x <= 0)
@@ -104,9 +105,10 @@ __host__ __device__ constexpr float fwht_scale_64() { return 0.125f; }
 
 // Butterfly stage across lanes: lane with bit `m` clear keeps a+b, the lane
 // with the bit set keeps a-b, where a is the lower lane's value (fwht.mojo:31-53).
+// p - v and v + p as one fma with v scaled by -1 or +1 (both products exact).
 __device__ __forceinline__ float fwht_xor_stage(float v, int lane, int m) {
   float p = __shfl_xor_sync(0xffffffffu, v, m);
-  return (lane & m) ? __fsub_rn(p, v) : __fadd_rn(v, p);
+  return __fmaf_rn(v, (lane & m) ? -1.0f : 1.0f, p);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
