@@ -899,6 +899,10 @@ def stage_model(label, fmt, T, distinct, R):
         return "hbm", T * H * 2 + H * 2 + T * H + T * 8
     if label == "rms_norm":
         return "hbm", T * H * 2 + H * 2 + T * H * 2 + T * 4
+    if label == "bq_norm_gather":
+        return "hbm", T * H * 2 + H * 2 + T * 4 + T * TOPK * 4 + R * (H + 4)
+    if label == "rms_norm_gather":
+        return "hbm", T * H * 2 + H * 2 + T * 4 + T * TOPK * 4 + R * H * 2
     if label == "gather_rows":
         return "hbm", R * (H + 4) * 2 + R * 8
     if label == "combine":

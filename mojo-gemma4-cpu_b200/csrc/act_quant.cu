@@ -128,6 +128,69 @@ bq_norm_quant_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
   if (h == 0 && lane == 0) xsa[t] = amax;
 }
 
+// bq_norm_quant_kernel for the tcgen05 prefill path: the pair of warps takes
+// the token's inv_rms from the top-8 kernel (the same chain and tree, so the
+// same bits), and the quantised row is stored once per local route, at
+// xg[route_pos[t*8+k]] in schedule order, with the raw amax as that route's
+// scale.
+__global__ void __launch_bounds__(256)
+bq_norm_gather_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma,
+                      const float* __restrict__ inv_rms, int T, const int32_t* __restrict__ route_pos,
+                      int8_t* __restrict__ xg, float* __restrict__ xg_sa) {
+  __shared__ float s_amax[NQ_ROWS][2];
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int k = warp >> 1, h = warp & 1;
+  const int t = blockIdx.x * NQ_ROWS + k;
+  if (t >= T) return;  // both warps of the pair leave together
+  constexpr int NBLK = H / NORM_BLOCK;  // 22
+  constexpr int NH = NBLK / 2;          // 11 per warp
+  const int bar = 1 + k;                // named barrier of the pair (64 threads)
+  const uint16_t* xr = x + (size_t)t * H + h * NH * NORM_BLOCK;
+  uint2 raw[NH];
+#pragma unroll
+  for (int b = 0; b < NH; ++b) raw[b] = *reinterpret_cast<const uint2*>(xr + b * NORM_BLOCK + 4 * lane);
+  // lanes 0..7 hold the token's 8 route positions (-1: expert not local)
+  const int my_pos = lane < TOPK ? route_pos[t * TOPK + lane] : -1;
+  const float inv = inv_rms[t];
+  float v[NH][4];
+  float amax = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NH; ++b) {
+    const uint2 g = *reinterpret_cast<const uint2*>(gamma + (h * NH + b) * NORM_BLOCK + 4 * lane);
+    const float gv[4] = {bf2f(g.x & 0xFFFFu), bf2f(g.x >> 16), bf2f(g.y & 0xFFFFu), bf2f(g.y >> 16)};
+    const float xv[4] = {bf2f(raw[b].x & 0xFFFFu), bf2f(raw[b].x >> 16), bf2f(raw[b].y & 0xFFFFu),
+                         bf2f(raw[b].y >> 16)};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[b][j] = __fmul_rn(__fmul_rn(xv[j], inv), gv[j]);
+    fwht128_lane4(v[b], lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) amax = fmaxf(amax, fabsf(v[b][j]));
+  }
+  amax = warp_max(amax);
+  if (lane == 0) s_amax[k][h] = amax;
+  asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");
+  amax = fmaxf(s_amax[k][0], s_amax[k][1]);
+  const float qinv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+  uint32_t packed[NH];
+#pragma unroll
+  for (int b = 0; b < NH; ++b) {
+    packed[b] = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) packed[b] |= (uint32_t)(quantize_i8(v[b][j], qinv) & 0xFF) << (8 * j);
+  }
+#pragma unroll
+  for (int r = 0; r < TOPK; ++r) {
+    const int pos = __shfl_sync(0xffffffffu, my_pos, r);
+    if (pos < 0) continue;
+    int8_t* dst = xg + (size_t)pos * H + h * NH * NORM_BLOCK;
+#pragma unroll
+    for (int b = 0; b < NH; ++b) *reinterpret_cast<uint32_t*>(dst + b * NORM_BLOCK + 4 * lane) = packed[b];
+    if (h == 0 && lane == 0) xg_sa[pos] = amax;
+  }
+}
+
 __global__ void __launch_bounds__(256)
 block_quant_kernel(const uint16_t* __restrict__ src, long rows, int8_t* __restrict__ qi8,
                    float* __restrict__ sa) {
@@ -190,12 +253,66 @@ rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
   }
 }
 
+// rms_norm_bf16_kernel for the tcgen05 prefill path of bf16 layers: the
+// token's inv_rms comes from the top-8 kernel (the same chain and tree), and
+// the normalised bf16 row is stored once per local route, at
+// xgb[route_pos[t*8+k]] (schedule order, rows of H bf16).
+__global__ void __launch_bounds__(256)
+rms_norm_gather_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma,
+                            const float* __restrict__ inv_rms, int T, const int32_t* __restrict__ route_pos,
+                            uint16_t* __restrict__ xgb) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  constexpr int NBLK = H / NORM_BLOCK;
+  const uint16_t* xr = x + (size_t)t * H;
+  const int my_pos = lane < TOPK ? route_pos[t * TOPK + lane] : -1;
+  const float inv = inv_rms[t];
+  uint2 w[NBLK];
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(xr + b * NORM_BLOCK + 4 * lane);
+    const uint2 g = *reinterpret_cast<const uint2*>(gamma + b * NORM_BLOCK + 4 * lane);
+    const float v[4] = {bf2f(raw.x & 0xFFFFu), bf2f(raw.x >> 16), bf2f(raw.y & 0xFFFFu), bf2f(raw.y >> 16)};
+    const float gv[4] = {bf2f(g.x & 0xFFFFu), bf2f(g.x >> 16), bf2f(g.y & 0xFFFFu), bf2f(g.y >> 16)};
+    uint16_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = f2bf(__fmul_rn(__fmul_rn(v[j], inv), gv[j]));
+    w[b].x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+    w[b].y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+  }
+#pragma unroll
+  for (int r = 0; r < TOPK; ++r) {
+    const int pos = __shfl_sync(0xffffffffu, my_pos, r);
+    if (pos < 0) continue;
+    uint16_t* dst = xgb + (size_t)pos * H;
+#pragma unroll
+    for (int b = 0; b < NBLK; ++b) *reinterpret_cast<uint2*>(dst + b * NORM_BLOCK + 4 * lane) = w[b];
+  }
+}
+
+cudaError_t launch_rms_norm_gather_bf16(const uint16_t* x, const uint16_t* gamma, const float* inv_rms, int T,
+                                        const int32_t* route_pos, uint16_t* xgb, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  return launch_k(rms_norm_gather_bf16_kernel, dim3((T + 7) / 8), dim3(256), 0, s, x, gamma, inv_rms, T,
+                  route_pos, xgb);
+}
+
 cudaError_t launch_bq_norm_quant(const uint16_t* x, const uint16_t* gamma, int T, int8_t* xi8,
                                  float* xsa, float* inv_rms, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
   // two warps per token, four tokens per CTA
   return launch_k(bq_norm_quant_kernel, dim3((T + NQ_ROWS - 1) / NQ_ROWS), dim3(256), 0, s, x, gamma, T, xi8,
                   xsa, inv_rms);
+}
+
+cudaError_t launch_bq_norm_gather(const uint16_t* x, const uint16_t* gamma, const float* inv_rms, int T,
+                                  const int32_t* route_pos, int8_t* xg, float* xg_sa, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  return launch_k(bq_norm_gather_kernel, dim3((T + NQ_ROWS - 1) / NQ_ROWS), dim3(256), 0, s, x, gamma,
+                  inv_rms, T, route_pos, xg, xg_sa);
 }
 
 cudaError_t launch_block_quant(const uint16_t* bucket, long rows, int8_t* qi8, float* sa,

@@ -586,13 +586,15 @@ struct CombineTarget {
 // x_i8/x_sa (butterquant) or x_normed (bf16), route_idx their top-8.
 int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, const float* x_sa,
                         const uint16_t* x_normed, const int32_t* route_idx, const CombineTarget& ct,
-                        cudaStream_t s) {
+                        cudaStream_t s, bool rows_gathered = false) {
   if (L.kind == 1) {
     if (L.has_tc && h->tc_ok && Tn >= h->tc_min_tokens) {
-      // prefill: routed rows gathered in schedule order, then the tcgen05 GEMMs
-      GM_STAGE(h, s, launch_gather_rows(x_i8, H, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
-                                        h->xg_sa, s),
-               "gather_rows");
+      // prefill: routed rows in schedule order (already there when the norm
+      // kernel wrote them itself), then the tcgen05 GEMMs
+      if (!rows_gathered)
+        GM_STAGE(h, s, launch_gather_rows(x_i8, H, x_sa, h->routes, h->expert_offset, h->epr, Tn, h->xg,
+                                          h->xg_sa, s),
+                 "gather_rows");
       GM_STAGE(h, s, launch_tc_phase1(h->tmap_xg, L.tmap_gu, h->expert_offset, h->epr, Tn, h->xg_sa,
                                       L.gu_scale, h->bucket_i8, h->bucket_sa, nullptr, h->dev_err, s),
                "bq_phase1_gate_up.tc");
@@ -608,9 +610,10 @@ int experts_and_combine(gm_moe* h, const Layer& L, int Tn, const int8_t* x_i8, c
                "bq_phase2_down");
     }
   } else if (L.has_tc && h->tcb_ok && Tn >= h->tc_min_tokens) {
-    GM_STAGE(h, s, launch_gather_rows(x_normed, 2 * H, nullptr, h->routes, h->expert_offset, h->epr, Tn,
-                                      h->ybuf, nullptr, s),
-             "gather_rows");
+    if (!rows_gathered)
+      GM_STAGE(h, s, launch_gather_rows(x_normed, 2 * H, nullptr, h->routes, h->expert_offset, h->epr, Tn,
+                                        h->ybuf, nullptr, s),
+               "gather_rows");
     GM_STAGE(h, s, launch_tcb_phase1(h->tmap_xgb, L.tmap_gu, h->expert_offset, h->epr, Tn, h->bucket,
                                      h->dev_err, s),
              "phase1_gate_up.tc");
@@ -1073,6 +1076,36 @@ int forward_impl(gm_moe* h, int layer, const void* x, void* out, int T, void* st
     h->launches += tls_kernel_launches - n0;
     tls_pdl = pdl;
     GM_TRY(h, pe, "l2_prefetch");
+  }
+  // (the order needs the tcgen05 router, which can wait before reading x)
+  const bool tc_rows = T >= h->tc_min_tokens && T >= ROUTER_TC_MIN_TOKENS && L.has_tc &&
+                       (L.kind == 1 ? h->tc_ok : h->tcb_ok);
+  if (tc_rows) {
+    // tcgen05 prefill: the router first (it waits for x), the top-8 computes
+    // each token's inv_rms itself, and the norm follows the schedule, writing
+    // every token's row (int8 for bq, bf16 otherwise) straight into its
+    // routes' rows of the gathered operand (no normalised copy and no gather
+    // pass)
+    GM_STAGE(h, s, launch_router_logits(xb, L.router, L.rscale, T, h->logits, h->dev_err, h->router_counts, s,
+                                        true),
+             "router_expert");
+    GM_STAGE(h, s, launch_topk_inv_schedule(xb, h->logits, L.pes, h->inv_rms, T, h->route_idx, h->route_w,
+                                            h->expert_base, h->epr,
+                                            L.kind == 1 ? GM_ROUTE_CHUNK_BQ : GM_ROUTE_CHUNK_BF16,
+                                            h->expert_offset, h->routes, h->route_pos, h->chunk_off,
+                                            h->sched_counts, s),
+             "router_merge.schedule");
+    if (L.kind == 1)
+      GM_STAGE(h, s, launch_bq_norm_gather(xb, L.gamma2, h->inv_rms, T, h->route_pos, h->xg, h->xg_sa, s),
+               "bq_norm_gather");
+    else
+      GM_STAGE(h, s, launch_rms_norm_gather_bf16(xb, L.gamma2, h->inv_rms, T, h->route_pos,
+                                                 reinterpret_cast<uint16_t*>(h->ybuf), s),
+               "rms_norm_gather");
+    CombineTarget ct;
+    ct.out = static_cast<uint16_t*>(out);
+    ct.post = post;
+    return experts_and_combine(h, L, T, nullptr, nullptr, nullptr, h->route_idx, ct, s, true);
   }
   // 1. activation norm (+ inv_rms shared with the router)
   if (L.kind == 1)

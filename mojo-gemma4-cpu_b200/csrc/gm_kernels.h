@@ -65,13 +65,18 @@ size_t router_workspace_floats(int T);
 // the FMA kernel.  Both read only x and the router weights, so they run beside
 // the norm kernel launched just before them (see router.cu).
 constexpr int ROUTER_TC_MIN_TOKENS = 512;
+// wait_first: the router is the forward's first kernel, so it waits for its
+// predecessor before reading x (the tcgen05 prefill path, see gm_api.cu).
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale, int T,
-                                 float* logits, int* err, int* tile_counters, cudaStream_t s);
+                                 float* logits, int* err, int* tile_counters, cudaStream_t s,
+                                 bool wait_first = false);
 cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale, int T,
-                                    float* logits, int* err, cudaStream_t s);
+                                    float* logits, int* err, cudaStream_t s, bool wait_first = false);
 cudaError_t launch_rms_inv(const uint16_t* x, int T, float* inv_rms, cudaStream_t s);
 cudaError_t launch_topk(float* logits, const uint16_t* pes, const float* inv_rms, int T,
                         int32_t* route_idx, float* route_w, cudaStream_t s);
+cudaError_t launch_topk_inv(const uint16_t* x, float* logits, const uint16_t* pes, float* inv_rms, int T,
+                            int32_t* route_idx, float* route_w, cudaStream_t s);
 // top-8 + softmax followed by the expert schedule (one CTA when T <= 1024;
 // otherwise a top-8 grid and, given `counts` scratch of schedule_counts_ints(T)
 // ints, the two-pass multi-CTA schedule)
@@ -79,6 +84,13 @@ cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, const float
                                  int32_t* route_idx, float* route_w, int expert_base, int epr,
                                  int route_chunk, int32_t* expert_offset, SparseRoute* routes,
                                  int32_t* route_pos, int32_t* chunk_off, int32_t* counts, cudaStream_t s);
+// The same, with each token's inv_rms computed from its x row by the top-8
+// warp (rms_inv_kernel's chain and reduction) and written to inv_rms: for the
+// tcgen05 prefill path, where the norm runs after the schedule.
+cudaError_t launch_topk_inv_schedule(const uint16_t* x, float* logits, const uint16_t* pes, float* inv_rms,
+                                     int T, int32_t* route_idx, float* route_w, int expert_base, int epr,
+                                     int route_chunk, int32_t* expert_offset, SparseRoute* routes,
+                                     int32_t* route_pos, int32_t* chunk_off, int32_t* counts, cudaStream_t s);
 int schedule_counts_ints(int T);
 cudaError_t launch_schedule_multi(const int32_t* route_idx, const float* route_w, int T,
                                   int expert_base, int epr, int route_chunk, int32_t* counts,
@@ -94,6 +106,16 @@ cudaError_t launch_build_schedule(const int32_t* route_idx, const float* route_w
                                   int32_t* chunk_off, cudaStream_t s);
 cudaError_t launch_bq_norm_quant(const uint16_t* x, const uint16_t* gamma, int T, int8_t* xi8,
                                  float* xsa, float* inv_rms, cudaStream_t s);
+// The norm + FWHT-128 + int8 of bq_norm_quant with the token's inv_rms read
+// from inv_rms (the top-8 kernel's) and the row stored once per local route,
+// at xg[route_pos[t*8+k]] (schedule order), with its scale at xg_sa[...]: the
+// tcgen05 prefill path's routed rows without an x_i8 copy or gather pass.
+cudaError_t launch_bq_norm_gather(const uint16_t* x, const uint16_t* gamma, const float* inv_rms, int T,
+                                  const int32_t* route_pos, int8_t* xg, float* xg_sa, cudaStream_t s);
+// The bf16 layers' counterpart: bf16(x * inv_rms * gamma) rows (rms_norm_bf16)
+// stored once per local route at xgb[route_pos[t*8+k]].
+cudaError_t launch_rms_norm_gather_bf16(const uint16_t* x, const uint16_t* gamma, const float* inv_rms, int T,
+                                        const int32_t* route_pos, uint16_t* xgb, cudaStream_t s);
 cudaError_t launch_block_quant(const uint16_t* bucket, long rows, int8_t* qi8, float* sa,
                                cudaStream_t s);
 cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int T, uint16_t* out,

@@ -152,6 +152,43 @@ topk_softmax_kernel(float* __restrict__ logits, int ksplit, const uint16_t* __re
   topk_token(logits, ksplit, pes, inv_rms, T, t, threadIdx.x & 31, route_idx, route_w);
 }
 
+// The top-8 of topk_softmax_kernel with the token's inv_rms computed first by
+// the same warp from its x row (rms_inv_kernel's per-lane chain over the 22
+// blocks, then the warp tree), stored for the norm kernel that follows the
+// schedule.
+__global__ void __launch_bounds__(128)
+topk_inv_softmax_kernel(const uint16_t* __restrict__ x, float* __restrict__ logits, int ksplit,
+                        const uint16_t* __restrict__ pes, float* __restrict__ inv_rms, int T,
+                        int32_t* __restrict__ route_idx, float* __restrict__ route_w) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const uint16_t* xr = x + (size_t)t * H;
+  uint2 raw[H / NORM_BLOCK];  // every load issued before the chain
+#pragma unroll
+  for (int b = 0; b < H / NORM_BLOCK; ++b) raw[b] = *reinterpret_cast<const uint2*>(xr + b * NORM_BLOCK + 4 * lane);
+  float ss = 0.0f;
+#pragma unroll
+  for (int b = 0; b < H / NORM_BLOCK; ++b) {
+    const float v[4] = {bf2f(raw[b].x & 0xFFFFu), bf2f(raw[b].x >> 16), bf2f(raw[b].y & 0xFFFFu),
+                        bf2f(raw[b].y >> 16)};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+  }
+  const float inv = inv_rms_from_sumsq(warp_sum(ss));  // the same value in every lane
+  if (lane == 0) inv_rms[t] = inv;
+  topk_token_inv(logits, ksplit, pes, inv, T, t, lane, route_idx, route_w);
+}
+
+cudaError_t launch_topk_inv(const uint16_t* x, float* logits, const uint16_t* pes, float* inv_rms, int T,
+                            int32_t* route_idx, float* route_w, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  return launch_k(topk_inv_softmax_kernel, dim3((T + 3) / 4), dim3(128), 0, s, x, logits,
+                  router_ksplit(T), pes, inv_rms, T, route_idx, route_w);
+}
+
 // Up to 32 tokens the one-CTA top-8 + schedule kernel runs, so the router
 // reduces its K slices itself (tile counters); above, the top-8 kernel (T/4
 // CTAs) sums the slices while it loads them.
@@ -167,9 +204,12 @@ size_t router_workspace_floats(int T) {
 }
 
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale, int T,
-                                 float* logits, int* err, int* tile_counters, cudaStream_t s) {
+                                 float* logits, int* err, int* tile_counters, cudaStream_t s,
+                                 bool wait_first) {
   if (T <= 0) return cudaSuccess;
-  if (T >= ROUTER_TC_MIN_TOKENS && err) return launch_router_logits_tc(x, wr, rscale, T, logits, err, s);
+  if (T >= ROUTER_TC_MIN_TOKENS && err)
+    return launch_router_logits_tc(x, wr, rscale, T, logits, err, s, wait_first);
+  if (wait_first) return cudaErrorInvalidValue;  // the FMA kernel always waits last
   if (T >= ROUTER_WIDE_MIN_TOKENS) return cudaErrorInvalidValue;  // the wide slicing is the tcgen05 kernel's
   if (router_ksplit(T) > 1) {
     tile_counters = nullptr;  // ROUTER_SLICES separate partials, summed by the top-8 kernel

@@ -12,9 +12,10 @@ namespace gm {
 // the dot so that the router does not wait for the norm), and the logit is
 // written back to slice 0.  moe_router.mojo:44-57 ordering and :276-293
 // softmax / per_expert_scale.
-__device__ __forceinline__ void topk_token(float* __restrict__ logits, int ksplit, const uint16_t* __restrict__ pes,
-                           const float* __restrict__ inv_rms, int T, int t, int lane,
-                           int32_t* __restrict__ route_idx, float* __restrict__ route_w) {
+__device__ __forceinline__ void topk_token_inv(float* __restrict__ logits, int ksplit,
+                                               const uint16_t* __restrict__ pes, float inv, int T, int t,
+                                               int lane, int32_t* __restrict__ route_idx,
+                                               float* __restrict__ route_w) {
   // all partial loads are issued before any add (independent, one L2 round trip)
   constexpr int MAX_KSPLIT = 11;
   float part[4][MAX_KSPLIT];
@@ -23,7 +24,6 @@ __device__ __forceinline__ void topk_token(float* __restrict__ logits, int kspli
 #pragma unroll
     for (int z = 0; z < MAX_KSPLIT; ++z)
       part[j][z] = z < ksplit ? logits[(size_t)z * T * E + (size_t)t * E + lane + 32 * j] : 0.0f;
-  const float inv = inv_rms[t];
   float v[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -76,6 +76,13 @@ __device__ __forceinline__ void topk_token(float* __restrict__ logits, int kspli
         route_w[t * TOPK + k] = __fmul_rn(__fmul_rn(ev[k], inv_sum), bf2f(pes[sel_e[k]]));
       }
   }
+}
+
+// The same with the token's inv_rms read from inv_rms[t].
+__device__ __forceinline__ void topk_token(float* __restrict__ logits, int ksplit, const uint16_t* __restrict__ pes,
+                           const float* __restrict__ inv_rms, int T, int t, int lane,
+                           int32_t* __restrict__ route_idx, float* __restrict__ route_w) {
+  topk_token_inv(logits, ksplit, pes, inv_rms[t], T, t, lane, route_idx, route_w);
 }
 
 }  // namespace gm

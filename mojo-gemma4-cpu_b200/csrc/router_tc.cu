@@ -20,7 +20,9 @@
 //  * the kernel reads only x and the router weights, so it runs beside the
 //    norm kernel launched just before it (that kernel triggers only after its
 //    own wait, so x is complete); it waits for its predecessor only after its
-//    stores, so its completion implies the norm kernel's (router.cu);
+//    stores, so its completion implies the norm kernel's (router.cu).  On the
+//    tcgen05 prefill path the router is the forward's first kernel (the norm
+//    follows the schedule there) and waits before reading x (wait_first);
 //  * the router chunks (64 K each) arrive by cp.async in a 6-stage ring, two
 //    chunks ahead; each thread loads its x units two chunks ahead into
 //    registers; the activation parts are produced by all 256 threads (packed
@@ -107,7 +109,7 @@ template <int CPS>
 __global__ void __launch_bounds__(RT_THREADS, 1)
 router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr,
                  const uint16_t* __restrict__ rscale, int T, float* __restrict__ logits,
-                 int* __restrict__ err) {
+                 int* __restrict__ err, int wait_first) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   RouterSmem& s =
       *reinterpret_cast<RouterSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -151,7 +153,11 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
                  "r"(128u));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
-  pdl_trigger();  // no wait before reading x: see the file comment
+  // no wait before reading x when a norm kernel that waited is the
+  // predecessor (see the file comment); as the forward's first kernel
+  // (wait_first) x may still be being written by the previous one
+  if (wait_first) pdl_wait();
+  pdl_trigger();
   uint4 xv[RT_XLA + 1][4], rs[RT_XLA + 1];
 #pragma unroll
   for (int c = 0; c < RT_XLA && c < CPS; ++c) load_x(c, xv[c], rs[c]);
@@ -245,13 +251,13 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
   }
   if (tid == 0 && *(volatile int*)&s.failed) atomicExch(err, 1);
   // this grid completes only after its predecessor (the norm kernel) has
-  pdl_wait();
+  if (!wait_first) pdl_wait();
 }
 
 }  // namespace tc
 
 cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const uint16_t* rscale, int T,
-                                    float* logits, int* err, cudaStream_t s) {
+                                    float* logits, int* err, cudaStream_t s, bool wait_first) {
   const size_t smem = sizeof(tc::RouterSmem) + 1024;
   // router_ksplit(T) K slices: 11 chunks each for wide batches (about one CTA
   // per SM at 4096 tokens), 4 chunks each below (more CTAs for fewer tokens)
@@ -262,7 +268,7 @@ cudaError_t launch_router_logits_tc(const uint16_t* x, const uint16_t* wr, const
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return launch_k(k, dim3((T + tc::RT_BM - 1) / tc::RT_BM, ns), dim3(tc::RT_THREADS), smem, s, x, wr, rscale, T,
-                  logits, err);
+                  logits, err, wait_first ? 1 : 0);
 }
 
 }  // namespace gm

@@ -330,4 +330,17 @@ cudaError_t launch_topk_schedule(float* logits, const uint16_t* pes, const float
                                routes, route_pos, chunk_off, s);
 }
 
+cudaError_t launch_topk_inv_schedule(const uint16_t* x, float* logits, const uint16_t* pes, float* inv_rms,
+                                     int T, int32_t* route_idx, float* route_w, int expert_base, int epr,
+                                     int route_chunk, int32_t* expert_offset, SparseRoute* routes,
+                                     int32_t* route_pos, int32_t* chunk_off, int32_t* counts, cudaStream_t s) {
+  cudaError_t e = launch_topk_inv(x, logits, pes, inv_rms, T, route_idx, route_w, s);
+  if (e != cudaSuccess) return e;
+  if (counts && T > 1024)
+    return launch_schedule_multi(route_idx, route_w, T, expert_base, epr, route_chunk, counts,
+                                 expert_offset, routes, route_pos, chunk_off, s);
+  return launch_build_schedule(route_idx, route_w, T, expert_base, epr, route_chunk, expert_offset,
+                               routes, route_pos, chunk_off, s);
+}
+
 }  // namespace gm
