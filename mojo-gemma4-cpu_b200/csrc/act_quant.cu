@@ -138,6 +138,7 @@ bq_norm_gather_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict
                       const float* __restrict__ inv_rms, int T, const int32_t* __restrict__ route_pos,
                       int8_t* __restrict__ xg, float* __restrict__ xg_sa) {
   __shared__ float s_amax[NQ_ROWS][2];
+  __shared__ __align__(16) uint32_t s_row[NQ_ROWS][H / 4];  // the pair's int8 row, then copied out
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -173,21 +174,24 @@ bq_norm_gather_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict
   asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");
   amax = fmaxf(s_amax[k][0], s_amax[k][1]);
   const float qinv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-  uint32_t packed[NH];
 #pragma unroll
   for (int b = 0; b < NH; ++b) {
-    packed[b] = 0;
+    uint32_t packed = 0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) packed[b] |= (uint32_t)(quantize_i8(v[b][j], qinv) & 0xFF) << (8 * j);
+    for (int j = 0; j < 4; ++j) packed |= (uint32_t)(quantize_i8(v[b][j], qinv) & 0xFF) << (8 * j);
+    s_row[k][(h * NH + b) * (NORM_BLOCK / 4) + lane] = packed;
   }
+  asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");  // the whole row is in s_row[k]
+  // the pair's 64 threads copy the row out in 16-byte units, once per local route
+  const uint4* src = reinterpret_cast<const uint4*>(s_row[k]);
+  const int pt = h * 32 + lane;
 #pragma unroll
   for (int r = 0; r < TOPK; ++r) {
     const int pos = __shfl_sync(0xffffffffu, my_pos, r);
     if (pos < 0) continue;
-    int8_t* dst = xg + (size_t)pos * H + h * NH * NORM_BLOCK;
-#pragma unroll
-    for (int b = 0; b < NH; ++b) *reinterpret_cast<uint32_t*>(dst + b * NORM_BLOCK + 4 * lane) = packed[b];
-    if (h == 0 && lane == 0) xg_sa[pos] = amax;
+    uint4* dst = reinterpret_cast<uint4*>(xg + (size_t)pos * H);
+    for (int c = pt; c < H / 16; c += 64) dst[c] = src[c];
+    if (pt == 0) xg_sa[pos] = amax;
   }
 }
 

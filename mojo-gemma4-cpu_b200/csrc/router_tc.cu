@@ -251,6 +251,7 @@ router_tc_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr
   }
   if (tid == 0 && *(volatile int*)&s.failed) atomicExch(err, 1);
   // this grid completes only after its predecessor (the norm kernel) has
+  // completed (with wait_first the wait came before the x loads)
   if (!wait_first) pdl_wait();
 }
 
