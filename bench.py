@@ -67,6 +67,9 @@ EXTRA = {
     "attn-decode-full-b64": ("attn-full", 64),
     "attn-prefill-sliding-4k": ("attnp-sliding", 4096),
     "attn-prefill-full-4k": ("attnp-full", 4096),
+    # config 5 as a whole decoder step: 64 sequences at 8k context through 30
+    # layers of attention block + FFN (dense MLP, MoE, post-FFN tail)
+    "decoder-b64-30L": ("decoder", 64),
 }
 EXTRA_TRAFFIC = {"attn-decode-full-b64": 541_900_000 + 14_200_000}
 DENSE_I = 2112
@@ -161,6 +164,268 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
                 "reasons": sorted(reasons), "samples": len(rows)}
+
+
+DEC_LAYERS, DEC_CTX = 30, 8192   # Gemma-4-26B-A4B: 30 layers, every 6th full attention
+
+
+def run_decoder(args, T, stream, hbm):
+    """One decode step of T sequences, each at position DEC_CTX - 1, through
+    DEC_LAYERS decoder layers (modeling/gemma_4_moe_bq.mojo:1080-1110): per
+    layer the attention block (norm-quant of x_main, q/k/v projections, head
+    prep into the paged int8 cache, decode attention over the window (sliding
+    layers: 1024 positions) or the whole context (full layers, (i+1) % 6 == 0:
+    8192 positions), head-block quantisation, output projection into
+    x_residual), the post-attention norm-residual into x_main, and the FFN
+    (dense MLP beside the MoE, post-FFN tail) in place on x_main.  Every layer
+    has its own weights and KV cache (random-init: the MoE, dense and q/k/v
+    weights are N(0, 0.02) bf16 through the device quantizer; o_proj, whose
+    K = heads x head_dim the device quantizer does not take, gets random int8
+    codes and scales of the same magnitude; caches random int8)."""
+    import numpy as np
+    import torch
+    import gmoe
+    import synth
+    PAGE, SHIFT = 1024, 10
+    pos = DEC_CTX - 1
+    g = torch.Generator(device="cuda").manual_seed(0xDEC)
+    blk = gmoe.MoeBlock(T, DEC_LAYERS)
+    gen = torch.Generator(device="cpu").manual_seed(0xDEC)
+
+    def gain(n):
+        return (1.0 + 0.1 * torch.randn(n, generator=gen)).to(torch.bfloat16).cuda()
+
+    def quant(w, gamma):
+        rows, cols = w.shape
+        q = torch.empty(rows, cols, dtype=torch.int8, device="cuda")
+        sc = torch.empty(rows, dtype=torch.float32, device="cuda")
+        gmoe.call("gm_bq_quantize_rows", w, rows, cols, gamma, 128, q, sc, None)
+        p = torch.empty_like(q)
+        gmoe.call("gm_vnni_pack", q, rows, cols, p, None)
+        return p, sc
+
+    layers, kv_bytes, attn_w_bytes = [], 0, 0
+    for l in range(DEC_LAYERS):
+        full = (l + 1) % 6 == 0
+        hd, nq, nkv, window, rope_half, pair_stride = (512, 16, 2, 0, 64, 256) if full else \
+            (256, 16, 8, 1024, 128, 128)
+        kv = DEC_CTX if full else window
+        ppr = DEC_CTX // PAGE if full else 2     # sliding layers: a ring of two window-sized pages
+        raw = synth.make_layer(seed=0x6E6D6F45 + 7919 * l, device="cuda")
+        register(blk, "bq", synth.bq_layer(raw), layer=l)
+        rawd = synth.make_dense(seed=0x0D3E + l, device="cuda")
+        if l == 0:
+            raw0, rawd0 = raw, rawd           # kept for the CPU leg's layers
+        del raw
+        D = synth.dense_layer(rawd)
+        blk.register_dense(l, D["gate"], D["gate_scale"], D["up"], D["up_scale"], D["down"], D["down_scale"],
+                           D["pre_ffn_norm"])
+        blk.register_post(l, gain(H), gain(H), gain(H), 1.0)
+        in_norm = gain(H)
+        in_baked = torch.empty_like(in_norm)
+        gmoe.call("gm_bake_split_gain", in_norm, in_baked, H, None)
+        qn, kvn = nq * hd, nkv * hd
+        wq = quant((torch.randn(qn, H, generator=g, device="cuda") * 0.02).to(torch.bfloat16), in_norm)
+        wk = quant((torch.randn(kvn, H, generator=g, device="cuda") * 0.02).to(torch.bfloat16), in_norm)
+        wv = None if full else quant((torch.randn(kvn, H, generator=g, device="cuda") * 0.02).to(torch.bfloat16),
+                                     in_norm)
+        wo = (torch.randint(-127, 128, (H, qn), dtype=torch.int8, device="cuda", generator=g),
+              torch.rand(H, device="cuda", generator=g) * 4e-4 + 4e-4)
+        n_slots = T * ppr * PAGE
+        kc = torch.randint(-127, 128, (n_slots, kvn), dtype=torch.int8, device="cuda", generator=g)
+        vc = torch.randint(-127, 128, (n_slots, kvn), dtype=torch.int8, device="cuda", generator=g)
+        ks = torch.rand(n_slots, nkv, device="cuda", generator=g) * 0.03
+        vs = torch.rand(n_slots, nkv, device="cuda", generator=g) + 0.5
+        base = (torch.randperm(T * ppr, device="cuda", generator=g).int() * PAGE).contiguous()
+        ang = np.arange(DEC_CTX, dtype=np.float64)[:, None] * \
+            (10000.0 ** (-np.arange(rope_half, dtype=np.float64) / rope_half))[None, :]
+        kv_bytes += T * kv * nkv * (2 * hd + 8)
+        attn_w_bytes += (qn + 2 * kvn if not full else qn + kvn) * (H + 4) + H * (qn + 4)
+        layers.append(dict(
+            full=full, hd=hd, nq=nq, nkv=nkv, window=window, kv=kv, rope_half=rope_half, pair_stride=pair_stride,
+            page_mask=(ppr - 1) if window else -1, in_baked=in_baked, wq=wq, wk=wk, wv=wv, wo=wo,
+            qnorm=gain(hd), knorm=gain(hd), post_attn=gain(H), kc=kc, vc=vc, ks=ks, vs=vs, base=base,
+            cos=torch.from_numpy(np.cos(ang).astype(np.float32)).cuda(),
+            sin=torch.from_numpy(np.sin(ang).astype(np.float32)).cuda(),
+            runs=torch.tensor([[t, pos, t * ppr, ppr] for t in range(T)], dtype=torch.int32, device="cuda")))
+    torch.cuda.empty_cache()
+    # activations, sized for the largest layer kind
+    xi8 = torch.empty(T, H, dtype=torch.int8, device="cuda")
+    xsa = torch.empty(T, dtype=torch.float32, device="cuda")
+    q_bf = torch.empty(T, 16 * 512, dtype=torch.bfloat16, device="cuda")
+    k_bf = torch.empty(T, 8 * 256, dtype=torch.bfloat16, device="cuda")
+    v_bf = torch.empty(T, 8 * 256, dtype=torch.bfloat16, device="cuda")
+    q_i8 = torch.empty(T, 16 * 512, dtype=torch.int8, device="cuda")
+    qb = torch.empty(T, 16, dtype=torch.float32, device="cuda")
+    fq = torch.empty(T, 16, dtype=torch.float32, device="cuda")
+    attn = torch.empty(T, 16 * 512, dtype=torch.bfloat16, device="cuda")
+    o_i8 = torch.empty(T, 16 * 512, dtype=torch.int8, device="cuda")
+    o_sa = torch.empty(T, 16, dtype=torch.float32, device="cuda")
+    x_res = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    wsb = max(gmoe.lib().gm_bq_attention_workspace_bytes(T, c["hd"], c["nq"], c["nkv"], c["kv"]) for c in layers)
+    ws = torch.empty(wsb // 4 + 1, dtype=torch.float32, device="cuda")
+
+    def attention(c, x_main):
+        hd, nq, nkv = c["hd"], c["nq"], c["nkv"]
+        qn, kvn = nq * hd, nkv * hd
+        gmoe.call("gm_bq_norm_quant", x_main, c["in_baked"], T, xi8, xsa, stream)
+        wv = c["wv"]
+        gmoe.call("gm_bq_qkv", xi8, xsa, T, c["wq"][0], c["wq"][1], qn, c["wk"][0], c["wk"][1],
+                  wv[0] if wv else None, wv[1] if wv else None, kvn, q_bf, k_bf, v_bf if wv else None, stream)
+        gmoe.call("gm_bq_attn_prep", q_bf, k_bf, v_bf if wv else k_bf, c["qnorm"], c["knorm"], q_i8, qb, fq,
+                  c["kc"], c["ks"], c["vc"], c["vs"], c["cos"], c["sin"], c["runs"], T, c["base"], T, hd, nq,
+                  nkv, c["rope_half"], c["pair_stride"], 1, 0, SHIFT, PAGE - 1, c["page_mask"], stream)
+        gmoe.call("gm_bq_attention_decode", q_i8, fq, c["kc"], c["ks"], c["vc"], c["vs"], c["runs"], c["base"],
+                  T, hd, nq, nkv, c["window"], 1, 0, SHIFT, PAGE - 1, c["page_mask"], c["kv"], attn, ws, wsb,
+                  stream)
+        gmoe.call("gm_bq_block_quant_ex", attn, T, qn, hd, 0, o_i8, o_sa, stream)
+        gmoe.call("gm_bq_block_linear_ex", o_i8, o_sa, T, qn, hd, c["wo"][0], c["wo"][1], H, x_res, stream)
+        gmoe.call("gm_norm_residual_add", x_res, x_main, c["post_attn"], T, x_main, stream)
+
+    xs = [synth.make_tokens(T, seed=300 + b, device="cuda") for b in range(args.batches)]
+    work = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+
+    def run_layers(x_main, marks=None):
+        for l, c in enumerate(layers):
+            if marks:
+                marks[l][0].record(stream)
+            attention(c, x_main)
+            if marks:
+                marks[l][1].record(stream)
+            blk.ffn_forward(l, x_main, T, stream)
+        if marks:
+            marks[-1][0].record(stream)
+
+    def step(i):
+        work.copy_(xs[i % len(xs)])
+        run_layers(work)
+    ms = timed(step, args.steps, args.warmup, stream)
+    per_step = ms / args.steps
+    # kernels per step: 8 per attention block (norm-quant, qkv, prep, decode +
+    # merge, head quant, o_proj, norm-residual) and the FFN's own count
+    blk.profile(False)
+    step(0)
+    torch.cuda.synchronize()
+    launches = (blk.profile_read()[1] + 8 * DEC_LAYERS) * args.steps
+    # where the step goes: events around every layer's attention block and FFN
+    marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(DEC_LAYERS + 1)]
+    attn_ms, ffn_ms = 0.0, 0.0
+    for i in range(3):
+        work.copy_(xs[i % len(xs)])
+        run_layers(work, marks)
+        torch.cuda.synchronize()
+        for l in range(DEC_LAYERS):
+            attn_ms += marks[l][0].elapsed_time(marks[l][1])
+            ffn_ms += marks[l][1].elapsed_time(marks[l + 1][0])
+    attn_ms, ffn_ms = attn_ms / 3, ffn_ms / 3
+    # algorithmic bytes: every layer's routed experts (expected distinct of
+    # T*8 uniform routes), dense MLP, attention weights and the KV it reads
+    distinct = E * (1.0 - (1.0 - TOPK / E) ** T)
+    moe_bytes = DEC_LAYERS * distinct * BQ_EXPERT_BYTES
+    algo = moe_bytes + DEC_LAYERS * DENSE_BYTES + attn_w_bytes + kv_bytes
+    roof = {"bound": "hbm", "achieved": algo / (per_step * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+            "note": "whole decoder step: %.2f GB of routed experts, %.2f GB dense MLP, %.2f GB attention "
+                    "weights, %.2f GB KV cache per step" % (moe_bytes / 1e9, DEC_LAYERS * DENSE_BYTES / 1e9,
+                                                          attn_w_bytes / 1e9, kv_bytes / 1e9)}
+    xh = [x.cpu().pin_memory() for x in xs]
+    oh = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(i):
+        work.copy_(xh[i % len(xh)], non_blocking=True)
+        run_layers(work)
+        oh.copy_(work, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    for i in range(3):
+        e2e_step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e2e_step(i)
+    e2e = T * args.steps / (time.perf_counter() - t0)
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = decoder_cpu_leg(args, layers, raw0, rawd0, xs[0])
+    blk.close()
+    return {"metric": "decoder-step tokens/s (%d layers: attention block + FFN with the MoE block)" % DEC_LAYERS,
+            "dtype": "i8", "config": {"workload": args.workload, "tokens_per_step": T, "layers": DEC_LAYERS,
+                                      "context": DEC_CTX, "sliding_layers": sum(not c["full"] for c in layers),
+                                      "full_layers": sum(c["full"] for c in layers), "parallelism": "single",
+                                      "l2": "every layer's weights and KV cache distinct, %.1f GB read per step "
+                                            "(larger than L2)" % (algo / 1e9)},
+            "step_split": {"attention_ms": attn_ms, "ffn_ms": ffn_ms,
+                           "note": "CUDA events around each layer's attention block and FFN (MoE + dense "
+                                   "MLP + tail), mean of 3 steps"},
+            "_roof": roof, "_ms": ms, "_per_step": per_step, "_launches": launches,
+            "_e2e": e2e, "_e2e_io": (T * H * 2, T * H * 2), "_cpu": cpu}
+
+
+def decoder_cpu_leg(args, layers, raw, rawd, x):
+    """The oracle (C++ restatement, all host threads) on a bounded sample: 4
+    tokens through the first sliding and the first full layer (norm-quant,
+    q/k/v products, flash decode over the layer's KV range, head quantisation,
+    output projection, norm-residual, MoE, dense MLP, post-FFN tail; the head
+    prep is left out), per-layer rates combined over the stack's 25 sliding
+    and 5 full layers."""
+    import numpy as np
+    import synth
+    O = oracle_native()
+    h = synth.to_numpy
+    Tc, PAGE, SHIFT, pos = 4, 1024, 10, DEC_CTX - 1
+    Lo = oracle_bq_layer(O, {k: h(v) for k, v in raw.items()})
+    Do = oracle_dense_layer(O, {k: h(v) for k, v in rawd.items()})
+    rng = np.random.default_rng(5)
+    xc = h(x[:Tc])
+    nth = O.lib().orc_num_threads()
+
+    def prepare(c):
+        hd, nq, nkv, kv = c["hd"], c["nq"], c["nkv"], c["kv"]
+        qn, kvn = nq * hd, nkv * hd
+        w = {}
+        for name, rows, cols, blk in (("wq", qn, H, None), ("wk", kvn, H, None), ("wv", kvn, H, None),
+                                      ("wo", H, qn, hd)):
+            if c[name] is None:
+                continue
+            q = O.vnni_unpack(h(c[name][0]), rows, cols)
+            cs = O.colsum(q, cols, True).reshape(-1) if blk is None else O.colsum(q, blk, False)
+            w[name] = (q, h(c[name][1]), cs)
+        bh = h(c["base"])
+        start = pos - kv + 1
+        p = np.arange(start, start + kv)
+        mask = c["page_mask"] if c["window"] else 0x7FFFFFFF
+        slots = np.stack([bh[t * (len(bh) // len(h(c["runs"]))) + ((p >> SHIFT) & mask)] + (p & (PAGE - 1))
+                          for t in range(Tc)]).astype(np.int32)
+        caches = [h(c[k]) for k in ("kc", "ks", "vc", "vs")]
+        qi = rng.integers(-127, 128, (Tc, qn), dtype=np.int8)
+        qbias = (qi.reshape(Tc, nq, hd).astype(np.int64).sum(-1) * 128).astype(np.float32)
+        fq = (rng.random((Tc, nq)) + 0.5).astype(np.float32)
+        attn = O.f32_to_bf16(rng.standard_normal((Tc, qn)).astype(np.float32) * 0.3)
+        gains = [h(c[k]) for k in ("in_baked", "post_attn")]
+
+        def once():
+            xi8, xsa = O.bq_norm_quant(xc, gains[0])
+            for name in ("wq", "wk", "wv"):
+                if name in w:
+                    O.bq_linear(xi8, xsa, *w[name])
+            O.bq_flash_decode(qi, qbias, fq, *caches, slots, np.full(Tc, kv, np.int32), hd, nq, nkv, nth)
+            oq, osa = O.bq_block_quant_ex(attn, hd, False)
+            xres = O.bq_block_linear_ex(oq, osa, *w["wo"], hd)
+            xm = O.norm_residual_add(xres, xc, gains[1])
+            moe = O.bq_forward(xm, Lo)[0]
+            dense = O.dense_mlp(xm, Do)[0]
+            O.post_moe(moe, dense, xm, gains[1], gains[1], gains[1], 1.0)
+        return once
+
+    sliding = next(c for c in layers if not c["full"])
+    full = next(c for c in layers if c["full"])
+    rate_s, n_s, w_s = median_rate(prepare(sliding), Tc, args.cpu_seconds / 2)
+    rate_f, n_f, w_f = median_rate(prepare(full), Tc, args.cpu_seconds / 2)
+    n_full = sum(c["full"] for c in layers)
+    rate = 1.0 / ((len(layers) - n_full) / rate_s + n_full / rate_f)
+    return dict({"value": rate, "unit": "tokens/s", "cores": nth, "kind": "port",
+                 "sample": "%d tokens through one sliding layer (%d timed, %.0f tokens/s) and one full layer "
+                           "(%d timed, %.0f tokens/s), combined over %d + %d layers; median (C++ restatement, "
+                           "OpenMP)" % (Tc, n_s, rate_s, n_f, rate_f, len(layers) - n_full, n_full)},
+                **host_info())
 
 
 def build_layer(fmt, seed, device_rank, zipf=False):
@@ -543,6 +808,10 @@ def run_extra(args):
                          "dtype": "i8", "config": {"workload": args.workload, "tokens_per_step": T,
                                                    "weights": "bq", "layers": 1, "parallelism": "single"}})
             blk.close()
+        elif kind == "decoder":
+            line.update(run_decoder(args, T, stream, hbm))
+            roof, ms, per_step, launches = line.pop("_roof"), line.pop("_ms"), line.pop("_per_step"), line.pop("_launches")
+            e2e, e2e_io, cpu = line.pop("_e2e"), line.pop("_e2e_io"), line.pop("_cpu")
         elif kind.startswith("attnp"):
             line.update(run_attn_prefill(args, kind, T, stream, hbm, tflops))
             roof, ms, per_step, launches = line.pop("_roof"), line.pop("_ms"), line.pop("_per_step"), line.pop("_launches")

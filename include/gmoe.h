@@ -429,6 +429,14 @@ int gm_build_expert_schedules(const int32_t* route_idx, const float* route_w, in
  * out = bf16(x*inv_rms*gamma). */
 int gm_rms_norm(const void* x, const void* gamma, int T, void* out, void* stream);
 
+/* fused_norm_residual_add (kernels/rmsnorm.mojo:48-64, norm_residual_add_row),
+ * as the decoder layer applies it after the attention block
+ * (modeling/gemma_4_moe_bq.mojo:1098-1102): per token,
+ * out = bf16(residual + (src * inv_rms(src)) * weight), bf16 [T][2816].  out
+ * may be residual itself (the residual stream updated in place). */
+int gm_norm_residual_add(const void* src, const void* residual, const void* weight, int T, void* out,
+                         void* stream);
+
 /* dispatch_bq_norm_quant (butterquant_kernels/linear.mojo:58-82, block 128):
  * x_i8 [T][2816], x_sa f32 [T] (raw absmax). */
 int gm_bq_norm_quant(const void* x, const void* gamma, int T, int8_t* x_i8, float* x_sa,

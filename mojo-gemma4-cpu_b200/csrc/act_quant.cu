@@ -257,6 +257,55 @@ rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
   }
 }
 
+// fused_norm_residual_add (kernels/rmsnorm.mojo:48-64 norm_residual_add_row):
+// out = bf16(residual + (src * inv_rms(src)) * w), one warp per token, the
+// sum of squares in rms_norm_bf16_kernel's order.  The decoder layer applies
+// it after the attention block's output projection (src = that output,
+// residual = x_main, out = x_main: modeling/gemma_4_moe_bq.mojo:1098-1102), so
+// out may alias residual: each lane reads its residual elements before it
+// stores the same elements.
+__global__ void __launch_bounds__(256)
+norm_residual_add_kernel(const uint16_t* __restrict__ src, const uint16_t* residual,
+                         const uint16_t* __restrict__ w, int T, uint16_t* out) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  constexpr int NBLK = H / NORM_BLOCK;
+  const uint16_t* sr = src + (size_t)t * H;
+  float v[NBLK][4];
+  float ss = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    uint2 raw = *reinterpret_cast<const uint2*>(sr + b * NORM_BLOCK + 4 * lane);
+    v[b][0] = bf2f(raw.x & 0xFFFFu);
+    v[b][1] = bf2f(raw.x >> 16);
+    v[b][2] = bf2f(raw.y & 0xFFFFu);
+    v[b][3] = bf2f(raw.y >> 16);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[b][j], v[b][j]));
+  }
+  ss = warp_sum(ss);
+  const float inv = inv_rms_from_sumsq(ss);
+  const uint16_t* rr = residual + (size_t)t * H;
+  uint16_t* dst = out + (size_t)t * H;
+#pragma unroll
+  for (int b = 0; b < NBLK; ++b) {
+    const uint2 g = *reinterpret_cast<const uint2*>(w + b * NORM_BLOCK + 4 * lane);
+    const uint2 r = *reinterpret_cast<const uint2*>(rr + b * NORM_BLOCK + 4 * lane);
+    const float gv[4] = {bf2f(g.x & 0xFFFFu), bf2f(g.x >> 16), bf2f(g.y & 0xFFFFu), bf2f(g.y >> 16)};
+    const float rv[4] = {bf2f(r.x & 0xFFFFu), bf2f(r.x >> 16), bf2f(r.y & 0xFFFFu), bf2f(r.y >> 16)};
+    uint16_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = f2bf(__fadd_rn(rv[j], __fmul_rn(__fmul_rn(v[b][j], inv), gv[j])));
+    uint2 st;
+    st.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+    st.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+    *reinterpret_cast<uint2*>(dst + b * NORM_BLOCK + 4 * lane) = st;
+  }
+}
+
 // rms_norm_bf16_kernel for the tcgen05 prefill path of bf16 layers: the
 // token's inv_rms comes from the top-8 kernel (the same chain and tree), and
 // the normalised bf16 row is stored once per local route, at
@@ -332,6 +381,14 @@ cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int T
   const int wpb = T <= 512 ? 2 : 8;
   return launch_k(rms_norm_bf16_kernel, dim3((T + wpb - 1) / wpb), dim3(32 * wpb), 0, s, x, gamma, T, out,
                   inv_rms);
+}
+
+cudaError_t launch_norm_residual_add(const uint16_t* src, const uint16_t* residual, const uint16_t* w, int T,
+                                     uint16_t* out, cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const int wpb = T <= 512 ? 2 : 8;
+  return launch_k(norm_residual_add_kernel, dim3((T + wpb - 1) / wpb), dim3(32 * wpb), 0, s, src, residual, w,
+                  T, out);
 }
 
 }  // namespace gm

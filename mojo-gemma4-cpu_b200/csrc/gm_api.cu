@@ -1745,6 +1745,16 @@ int gm_rms_norm(const void* x, const void* gamma, int T, void* out, void* stream
         "rms_norm");
 }
 
+int gm_norm_residual_add(const void* src, const void* residual, const void* weight, int T, void* out,
+                         void* stream) {
+  if (T < 0 || (T > 0 && (!src || !residual || !weight || !out)))
+    return set_err(nullptr, GM_EINVAL, "norm_residual_add: T=%d or a NULL pointer", T);
+  STAGE(launch_norm_residual_add(static_cast<const uint16_t*>(src), static_cast<const uint16_t*>(residual),
+                                 static_cast<const uint16_t*>(weight), T, static_cast<uint16_t*>(out),
+                                 S(stream)),
+        "norm_residual_add");
+}
+
 int gm_bq_norm_quant(const void* x, const void* gamma, int T, int8_t* x_i8, float* x_sa,
                      void* stream) {
   STAGE(launch_bq_norm_quant(static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(gamma),

@@ -120,6 +120,9 @@ cudaError_t launch_block_quant(const uint16_t* bucket, long rows, int8_t* qi8, f
                                cudaStream_t s);
 cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int T, uint16_t* out,
                                  float* inv_rms, cudaStream_t s);
+// out = bf16(residual + src * inv_rms(src) * w) per token; out may alias residual.
+cudaError_t launch_norm_residual_add(const uint16_t* src, const uint16_t* residual, const uint16_t* w, int T,
+                                     uint16_t* out, cudaStream_t s);
 cudaError_t launch_bq_phase1(const int8_t* xi8, const float* xsa, const int32_t* expert_offset,
                              const SparseRoute* routes, const int32_t* chunk_off, int epr, int T,
                              const int8_t* w_gu, const float* gu_scale, int8_t* bucket_i8,

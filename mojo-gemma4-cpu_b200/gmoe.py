@@ -61,6 +61,7 @@ SIGNATURES = {
     "gm_router_select_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),
     "gm_build_expert_schedules": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp]),
     "gm_rms_norm": (_i32, [_vp, _vp, _i32, _vp, _vp]),
+    "gm_norm_residual_add": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp]),
     "gm_bq_norm_quant": (_i32, [_vp, _vp, _i32, _vp, _vp, _vp]),
     "gm_bq_phase1_gate_up": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "gm_bq_block_quant": (_i32, [_vp, _i64, _vp, _vp, _vp]),

@@ -391,6 +391,19 @@ void orc_rms_norm(const uint16_t* x, const uint16_t* gamma, int T, uint16_t* out
   }
 }
 
+// kernels/rmsnorm.mojo:48-64 norm_residual_add_row, the decoder layer's step
+// after the attention block (modeling/gemma_4_moe_bq.mojo:1098-1102):
+// out = bf16(r + (s*inv_rms(s))*w).  out may alias r.
+void orc_norm_residual_add(const uint16_t* src, const uint16_t* r, const uint16_t* w, int T, uint16_t* out) {
+#pragma omp parallel for schedule(static)
+  for (int t = 0; t < T; ++t) {
+    const uint16_t* s = src + (long)t * H;
+    const float inv = inv_rms_row(s);
+    for (int k = 0; k < H; ++k)
+      out[(long)t * H + k] = f2bf(bf2f(r[(long)t * H + k]) + bf2f(s[k]) * inv * bf2f(w[k]));
+  }
+}
+
 // The tail of dispatch_bq_ffn after the MoE (modeling/gemma_4_moe_bq.mojo:
 // 785-805), per token:
 //   dense = rms_norm(dense, post_ffn_norm_1)                 (kernels/rmsnorm.mojo:21-47)

@@ -65,6 +65,7 @@ def _declare(L):
         "orc_router": (None, [vp, i32, vp, vp, vp, vp, vp, vp]),
         "orc_build_schedules": (None, [vp, vp, i32, i32, i32, vp, vp]),
         "orc_rms_norm": (None, [vp, vp, i32, vp]),
+        "orc_norm_residual_add": (None, [vp, vp, vp, i32, vp]),
         "orc_post_moe": (None, [vp, vp, vp, vp, vp, vp, C.c_float, i32, vp]),
         "orc_phase1_bf16": (None, [vp, vp, vp, vp, i32, vp]),
         "orc_phase2_bf16": (None, [vp, vp, vp, vp, i32, i32, vp]),
@@ -190,6 +191,13 @@ def build_schedules(idx, w, expert_base, epr):
 def rms_norm(x, gamma):
     out = np.empty_like(x)
     lib().orc_rms_norm(_p(x), _p(gamma), x.shape[0], _p(out))
+    return out
+
+
+def norm_residual_add(src, residual, w):
+    """bf16(residual + src * inv_rms(src) * w) per token (kernels/rmsnorm.mojo:48-64)."""
+    out = np.empty_like(residual)
+    lib().orc_norm_residual_add(_p(src), _p(residual), _p(w), src.shape[0], _p(out))
     return out
 
 

@@ -141,3 +141,27 @@ def test_attention_block_argument_checks():
         gmoe.call("gm_bq_block_quant_ex", z, 1, 256, 256, 1, z, z, None)  # FWHT only for 64
     with pytest.raises(gmoe.GmoeError, match="GM_EINVAL"):
         gmoe.call("gm_bq_block_linear_ex", z, z, 1, 1280, 256, z, z, 2816, z, None)  # 5 blocks
+
+
+@pytest.mark.parametrize("T", [1, 37, 600])
+def test_norm_residual_add_bit_exact(T, activations):
+    """gm_norm_residual_add, the decoder layer's step after the attention
+    block (kernels/rmsnorm.mojo:48-64), against the oracle, into a separate
+    output and in place over the residual stream (the two bit-identical).  The
+    sum of squares is a warp reduction, not the reference's SIMD-lane order, so
+    an inv_rms can differ in its last bit and an output by one bf16 step (the
+    same bound as the RMSNorm and post-MoE tail tests)."""
+    rng, gain = activations
+    src = bf(rng.standard_normal((T, H), dtype=np.float32) * 0.7)
+    res = bf(rng.standard_normal((T, H), dtype=np.float32))
+    ref = O.norm_residual_add(src, res, gain)
+    d_src, d_res, d_w = dev(src), dev(res), dev(gain)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    gmoe.call("gm_norm_residual_add", d_src, d_res, d_w, T, out, None)
+    gmoe.call("gm_norm_residual_add", d_src, d_res, d_w, T, d_res, None)   # in place
+    torch.cuda.synchronize()
+    got = host(out)
+    assert np.array_equal(host(d_res), got)
+    g, r = O.bf16_to_f32(got), O.bf16_to_f32(ref)
+    assert np.abs(g - r).max() <= 2 ** -7 * np.abs(r).max()
+    assert (got == ref).mean() > 0.97

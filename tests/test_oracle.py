@@ -400,6 +400,21 @@ def test_post_moe_tail():
     assert np.abs(got - ref).max() <= 0.02 * np.abs(ref).max()
 
 
+def test_norm_residual_add_oracle():
+    """orc_norm_residual_add (kernels/rmsnorm.mojo:48-64): with a zero
+    residual it is rms_norm bit for bit; composed with rms_norm it rebuilds the
+    post-MoE tail's two norm-residual steps bit for bit (layer scalar 1)."""
+    rng = np.random.default_rng(6)
+    T = 5
+    bf = lambda a: O.f32_to_bf16(np.asarray(a, np.float32))
+    moe, dense, x = (bf(rng.standard_normal((T, H)) * s) for s in (0.3, 2.0, 1.0))
+    w1, w2, w = (bf(1.0 + 0.2 * rng.standard_normal(H)) for _ in range(3))
+    zeros = np.zeros((T, H), np.uint16)
+    assert np.array_equal(O.norm_residual_add(moe, zeros, w2), O.rms_norm(moe, w2))
+    d2 = O.norm_residual_add(moe, O.rms_norm(dense, w1), w2)
+    assert np.array_equal(O.norm_residual_add(d2, x, w), O.post_moe(moe, dense, x, w1, w2, w, 1.0))
+
+
 def test_dense_mlp_oracle():
     """orc_dense_mlp (modeling/gemma_4_moe_bq.mojo:749-783): equals its own
     stages composed, the signed-dot form of bq_linear (the u8 x s8 - 128*colsum
