@@ -265,31 +265,43 @@ def run_decoder(args, T, stream, hbm):
     wsb = max(gmoe.lib().gm_bq_attention_workspace_bytes(T, c["hd"], c["nq"], c["nkv"], c["kv"]) for c in layers)
     ws = torch.empty(wsb // 4 + 1, dtype=torch.float32, device="cuda")
 
-    def attention(c, x_main):
+    ATTN_STAGES = ("norm_quant", "qkv", "prep", "decode", "head_quant", "o_proj", "norm_residual")
+
+    def attention(c, x_main, ev=None):
+        """ev: None, or one CUDA event per stage boundary (len(ATTN_STAGES) + 1)."""
         hd, nq, nkv = c["hd"], c["nq"], c["nkv"]
         qn, kvn = nq * hd, nkv * hd
+        mark = (lambda k: ev[k].record(stream)) if ev else (lambda k: None)
+        mark(0)
         gmoe.call("gm_bq_norm_quant", x_main, c["in_baked"], T, xi8, xsa, stream)
+        mark(1)
         wv = c["wv"]
         gmoe.call("gm_bq_qkv", xi8, xsa, T, c["wq"][0], c["wq"][1], qn, c["wk"][0], c["wk"][1],
                   wv[0] if wv else None, wv[1] if wv else None, kvn, q_bf, k_bf, v_bf if wv else None, stream)
+        mark(2)
         gmoe.call("gm_bq_attn_prep", q_bf, k_bf, v_bf if wv else k_bf, c["qnorm"], c["knorm"], q_i8, qb, fq,
                   c["kc"], c["ks"], c["vc"], c["vs"], c["cos"], c["sin"], c["runs"], T, c["base"], T, hd, nq,
                   nkv, c["rope_half"], c["pair_stride"], 1, 0, SHIFT, PAGE - 1, c["page_mask"], stream)
+        mark(3)
         gmoe.call("gm_bq_attention_decode", q_i8, fq, c["kc"], c["ks"], c["vc"], c["vs"], c["runs"], c["base"],
                   T, hd, nq, nkv, c["window"], 1, 0, SHIFT, PAGE - 1, c["page_mask"], c["kv"], attn, ws, wsb,
                   stream)
+        mark(4)
         gmoe.call("gm_bq_block_quant_ex", attn, T, qn, hd, 0, o_i8, o_sa, stream)
+        mark(5)
         gmoe.call("gm_bq_block_linear_ex", o_i8, o_sa, T, qn, hd, c["wo"][0], c["wo"][1], H, x_res, stream)
+        mark(6)
         gmoe.call("gm_norm_residual_add", x_res, x_main, c["post_attn"], T, x_main, stream)
+        mark(7)
 
     xs = [synth.make_tokens(T, seed=300 + b, device="cuda") for b in range(args.batches)]
     work = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
 
-    def run_layers(x_main, marks=None):
+    def run_layers(x_main, marks=None, stage_ev=None):
         for l, c in enumerate(layers):
             if marks:
                 marks[l][0].record(stream)
-            attention(c, x_main)
+            attention(c, x_main, stage_ev[l] if stage_ev else None)
             if marks:
                 marks[l][1].record(stream)
             blk.ffn_forward(l, x_main, T, stream)
@@ -319,6 +331,21 @@ def run_decoder(args, T, stream, hbm):
             attn_ms += marks[l][0].elapsed_time(marks[l][1])
             ffn_ms += marks[l][1].elapsed_time(marks[l + 1][0])
     attn_ms, ffn_ms = attn_ms / 3, ffn_ms / 3
+    # the attention block's stages, per layer kind (separate passes, so that
+    # the stage events do not disturb the split above)
+    stage_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(ATTN_STAGES) + 1)]
+                for _ in range(DEC_LAYERS)]
+    stage_us = {kind: {n: 0.0 for n in ATTN_STAGES} for kind in ("sliding", "full")}
+    for i in range(3):
+        work.copy_(xs[i % len(xs)])
+        run_layers(work, stage_ev=stage_ev)
+        torch.cuda.synchronize()
+        for l, c in enumerate(layers):
+            kind = "full" if c["full"] else "sliding"
+            n_kind = sum(1 for d in layers if d["full"] == c["full"])
+            for k, n in enumerate(ATTN_STAGES):
+                stage_us[kind][n] += 1e3 * stage_ev[l][k].elapsed_time(stage_ev[l][k + 1]) / (3 * n_kind)
+    stage_us = {kind: {n: round(v, 1) for n, v in d.items()} for kind, d in stage_us.items()}
     # algorithmic bytes: every layer's routed experts (expected distinct of
     # T*8 uniform routes), dense MLP, attention weights and the KV it reads
     distinct = E * (1.0 - (1.0 - TOPK / E) ** T)
@@ -352,7 +379,7 @@ def run_decoder(args, T, stream, hbm):
                                       "full_layers": sum(c["full"] for c in layers), "parallelism": "single",
                                       "l2": "every layer's weights and KV cache distinct, %.1f GB read per step "
                                             "(larger than L2)" % (algo / 1e9)},
-            "step_split": {"attention_ms": attn_ms, "ffn_ms": ffn_ms,
+            "step_split": {"attention_ms": attn_ms, "ffn_ms": ffn_ms, "attention_stage_us_per_layer": stage_us,
                            "note": "CUDA events around each layer's attention block and FFN (MoE + dense "
                                    "MLP + tail), mean of 3 steps"},
             "_roof": roof, "_ms": ms, "_per_step": per_step, "_launches": launches,

@@ -489,7 +489,10 @@ cudaError_t launch_block_linear_ex(const int8_t* hi8, const float* hsa, int T, i
   if (T <= 0) return cudaSuccess;
   if (block <= 0 || k % block || n_rows <= 0 || n_rows % 32 || k % 64) return cudaErrorInvalidValue;
   const int nb = k / block;
-  const int warps = nb % 4 == 0 ? 4 : nb % 3 == 0 ? 3 : 0;
+  // K split over as many warps as the block count allows (16 for the output
+  // projections, whose 16 head blocks give one block per warp): more weight
+  // loads in flight per SM, and the token chunk staged by more threads
+  const int warps = nb % 16 == 0 ? 16 : nb % 8 == 0 ? 8 : nb % 4 == 0 ? 4 : nb % 3 == 0 ? 3 : 0;
   if (!warps) return cudaErrorInvalidValue;
   const size_t smem = block_linear_smem(k, block, warps);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
@@ -500,6 +503,24 @@ cudaError_t launch_block_linear_ex(const int8_t* hi8, const float* hsa, int T, i
     const int grid = grid_for(kern, 32 * warps, smem, items);
     return launch_k(kern, dim3(grid), dim3(32 * warps), smem, s, hi8, hsa, T, k, w, wsc, n_rows, out);
   };
+  if (warps == 16) {
+    switch (block) {
+      case 64: return run(block_linear_kernel<64, 4, 16>);
+      case 128: return run(block_linear_kernel<128, 4, 16>);
+      case 256: return run(block_linear_kernel<256, 4, 16>);
+      case 512: return run(block_linear_kernel<512, 4, 16>);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  if (warps == 8) {
+    switch (block) {
+      case 64: return run(block_linear_kernel<64, 4, 8>);
+      case 128: return run(block_linear_kernel<128, 4, 8>);
+      case 256: return run(block_linear_kernel<256, 4, 8>);
+      case 512: return run(block_linear_kernel<512, 4, 8>);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   if (warps == 4) {
     switch (block) {
       case 64: return run(block_linear_kernel<64, 4, 4>);
