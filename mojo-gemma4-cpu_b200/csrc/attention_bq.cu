@@ -900,16 +900,65 @@ cudaError_t launch_attn_merge_parts(const float* const* parts, int n, int T, int
   return launch_k(attn_merge_parts_kernel<512>, dim3(T * num_q), dim3(512), 0, s, pl, out);
 }
 
-// KV splits per (token, KV head): enough CTAs for every SM several times
-// over, at least 64 positions per split, at most 64 splits.
-int attention_splits(int T, int num_kv, int max_kv_len) {
-  const int want = (148 * 8 + T * num_kv - 1) / (T * num_kv);
-  const int cap = std::max(1, (max_kv_len + 63) / 64);
-  return std::max(1, std::min({want, cap, 64}));
+using DecodeKernel = void (*)(const int8_t*, const float*, const int8_t*, const float*, const int8_t*,
+                              const float*, const KvRun*, const int32_t*, int, int, int, int, int, int, int,
+                              int, int, float*);
+
+DecodeKernel decode_kernel_for(int head_dim, int G) {
+  if (head_dim == 256) {
+    if (G == 2) return attn_decode_kernel<256, 2>;
+    if (G == 4) return attn_decode_kernel<256, 4>;
+    if (G == 8) return attn_decode_kernel<256, 8>;
+  } else if (head_dim == 512) {
+    if (G == 2) return attn_decode_kernel<512, 2>;
+    if (G == 4) return attn_decode_kernel<512, 4>;
+    if (G == 8) return attn_decode_kernel<512, 8>;
+  }
+  return nullptr;
+}
+
+size_t decode_smem(int head_dim) {
+  return head_dim == 256 ? sizeof(DecodeSmem<256>) : sizeof(DecodeSmem<512>);
+}
+
+// KV splits per (token, KV head).  Every split is one CTA; the decode kernel
+// is latency-bound per CTA, so the time of a call is about (waves of resident
+// CTAs) x (positions per split + a fixed per-CTA cost of ~48 positions).  The
+// split count minimises that over 1..min(64, max_kv_len / 64) (at least 64
+// positions per split), the resident CTAs per SM from the occupancy of the
+// kernel that runs; the smallest count wins a tie (fewer partials to merge).
+int attention_splits(int T, int head_dim, int num_q, int num_kv, int max_kv_len) {
+  if (T <= 0 || num_kv <= 0 || max_kv_len <= 0) return 1;
+  int per_sm = 0;
+  const DecodeKernel k = decode_kernel_for(head_dim, num_q / num_kv);
+  if (!k || cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, DEC_THREADS, decode_smem(head_dim)) !=
+                cudaSuccess || per_sm <= 0) {
+    cudaGetLastError();
+    per_sm = 2048 / DEC_THREADS;
+  }
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  const long slots = (long)sms * per_sm, units = (long)T * num_kv;
+  const int cap = std::max(1, std::min(64, (max_kv_len + 63) / 64));
+  int best = 1;
+  long best_cost = -1;
+  for (int s = 1; s <= cap; ++s) {
+    const long waves = (units * s + slots - 1) / slots;
+    const long cost = waves * ((max_kv_len + s - 1) / s + 48);
+    if (best_cost < 0 || cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 size_t attention_workspace_floats(int T, int head_dim, int num_q, int num_kv, int max_kv_len) {
-  return (size_t)T * num_q * attention_splits(T, num_kv, max_kv_len) * (head_dim + 2);
+  return (size_t)T * num_q * attention_splits(T, head_dim, num_q, num_kv, max_kv_len) * (head_dim + 2);
 }
 
 cudaError_t launch_attn_prep(const uint16_t* q_src, const uint16_t* k_src, const uint16_t* v_src,
@@ -942,23 +991,12 @@ cudaError_t launch_attn_decode(const int8_t* q_i8, const float* f_q, const int8_
                                int num_kv, int window, int cache_degree, int rank, int shift, int row_mask,
                                int page_mask, int max_kv_len, float* partials, uint16_t* out, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  const int n_splits = attention_splits(T, num_kv, max_kv_len);
-  const int G = num_q / num_kv;
+  const int n_splits = attention_splits(T, head_dim, num_q, num_kv, max_kv_len);
   const KvRun* r = static_cast<const KvRun*>(runs);
   const dim3 grid(n_splits, num_kv, T);
-  void (*k)(const int8_t*, const float*, const int8_t*, const float*, const int8_t*, const float*,
-            const KvRun*, const int32_t*, int, int, int, int, int, int, int, int, int, float*) = nullptr;
-  if (head_dim == 256) {
-    if (G == 2) k = attn_decode_kernel<256, 2>;
-    else if (G == 4) k = attn_decode_kernel<256, 4>;
-    else if (G == 8) k = attn_decode_kernel<256, 8>;
-  } else {
-    if (G == 2) k = attn_decode_kernel<512, 2>;
-    else if (G == 4) k = attn_decode_kernel<512, 4>;
-    else if (G == 8) k = attn_decode_kernel<512, 8>;
-  }
+  const DecodeKernel k = decode_kernel_for(head_dim, num_q / num_kv);
   if (!k) return cudaErrorInvalidValue;
-  const size_t smem = head_dim == 256 ? sizeof(DecodeSmem<256>) : sizeof(DecodeSmem<512>);
+  const size_t smem = decode_smem(head_dim);
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   e = launch_k(k, grid, dim3(DEC_THREADS), smem, s, q_i8, f_q, k_cache, k_scale, v_cache, v_scale, r, base_rows,

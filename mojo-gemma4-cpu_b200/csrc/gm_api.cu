@@ -1966,7 +1966,7 @@ int gm_bq_attention_partial(const int8_t* q_i8, const float* f_q, const int8_t* 
                                      head_dim, num_q, num_kv, window, cache_degree, rank, page_shift, row_mask,
                                      page_mask, max_kv_len, workspace, nullptr, S(stream));
   if (e == cudaSuccess)
-    e = launch_attn_rank_partial(workspace, T, num_q, head_dim, attention_splits(T, num_kv, max_kv_len),
+    e = launch_attn_rank_partial(workspace, T, num_q, head_dim, attention_splits(T, head_dim, num_q, num_kv, max_kv_len),
                                  partial, S(stream));
   return cuda_check(nullptr, e, "bq_attention_partial");
 }

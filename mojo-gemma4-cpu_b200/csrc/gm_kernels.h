@@ -186,7 +186,7 @@ cudaError_t launch_attn_decode(const int8_t* q_i8, const float* f_q, const int8_
                                const void* runs, const int32_t* base_rows, int T, int head_dim, int num_q,
                                int num_kv, int window, int cache_degree, int rank, int shift, int row_mask,
                                int page_mask, int max_kv_len, float* partials, uint16_t* out, cudaStream_t s);
-int attention_splits(int T, int num_kv, int max_kv_len);
+int attention_splits(int T, int head_dim, int num_q, int num_kv, int max_kv_len);
 // prefill attention over multi-token runs (Gemma-4 geometries: head 256 with
 // 2 query heads per KV head, head 512 with 8)
 cudaError_t launch_attn_prefill(const int8_t* q_i8, const float* f_q, const int8_t* k_cache, const float* k_scale,
