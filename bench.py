@@ -267,7 +267,7 @@ def run_decoder(args, T, stream, hbm):
 
     ATTN_STAGES = ("norm_quant", "qkv", "prep", "decode", "head_quant", "o_proj", "norm_residual")
 
-    def attention(c, x_main, ev=None):
+    def attention(c, x_main, stream, ev=None):
         """ev: None, or one CUDA event per stage boundary (len(ATTN_STAGES) + 1)."""
         hd, nq, nkv = c["hd"], c["nq"], c["nkv"]
         qn, kvn = nq * hd, nkv * hd
@@ -297,26 +297,35 @@ def run_decoder(args, T, stream, hbm):
     xs = [synth.make_tokens(T, seed=300 + b, device="cuda") for b in range(args.batches)]
     work = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
 
-    def run_layers(x_main, marks=None, stage_ev=None):
+    def run_layers(x_main, st, marks=None, stage_ev=None):
         for l, c in enumerate(layers):
             if marks:
-                marks[l][0].record(stream)
-            attention(c, x_main, stage_ev[l] if stage_ev else None)
+                marks[l][0].record(st)
+            attention(c, x_main, st, stage_ev[l] if stage_ev else None)
             if marks:
-                marks[l][1].record(stream)
-            blk.ffn_forward(l, x_main, T, stream)
+                marks[l][1].record(st)
+            blk.ffn_forward(l, x_main, T, st)
         if marks:
-            marks[-1][0].record(stream)
+            marks[-1][0].record(st)
+
+    # The step's ~20 launches per layer are captured once into a CUDA graph
+    # (after an eager run), so that the host's per-launch cost is paid once
+    run_layers(work, stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+        run_layers(work, torch.cuda.current_stream())
+    torch.cuda.synchronize()
 
     def step(i):
         work.copy_(xs[i % len(xs)])
-        run_layers(work)
+        graph.replay()
     ms = timed(step, args.steps, args.warmup, stream)
     per_step = ms / args.steps
     # kernels per step: 8 per attention block (norm-quant, qkv, prep, decode +
     # merge, head quant, o_proj, norm-residual) and the FFN's own count
     blk.profile(False)
-    step(0)
+    run_layers(work, stream)
     torch.cuda.synchronize()
     launches = (blk.profile_read()[1] + 8 * DEC_LAYERS) * args.steps
     # where the step goes: events around every layer's attention block and FFN
@@ -325,7 +334,7 @@ def run_decoder(args, T, stream, hbm):
     attn_ms, ffn_ms = 0.0, 0.0
     for i in range(3):
         work.copy_(xs[i % len(xs)])
-        run_layers(work, marks)
+        run_layers(work, stream, marks)
         torch.cuda.synchronize()
         for l in range(DEC_LAYERS):
             attn_ms += marks[l][0].elapsed_time(marks[l][1])
@@ -338,7 +347,7 @@ def run_decoder(args, T, stream, hbm):
     stage_us = {kind: {n: 0.0 for n in ATTN_STAGES} for kind in ("sliding", "full")}
     for i in range(3):
         work.copy_(xs[i % len(xs)])
-        run_layers(work, stage_ev=stage_ev)
+        run_layers(work, stream, stage_ev=stage_ev)
         torch.cuda.synchronize()
         for l, c in enumerate(layers):
             kind = "full" if c["full"] else "sliding"
@@ -360,7 +369,7 @@ def run_decoder(args, T, stream, hbm):
 
     def e2e_step(i):
         work.copy_(xh[i % len(xh)], non_blocking=True)
-        run_layers(work)
+        graph.replay()
         oh.copy_(work, non_blocking=True)
         torch.cuda.current_stream().synchronize()
     for i in range(3):
@@ -372,16 +381,18 @@ def run_decoder(args, T, stream, hbm):
     cpu = None
     if not args.no_cpu_baseline:
         cpu = decoder_cpu_leg(args, layers, raw0, rawd0, xs[0])
+    del graph
     blk.close()
     return {"metric": "decoder-step tokens/s (%d layers: attention block + FFN with the MoE block)" % DEC_LAYERS,
             "dtype": "i8", "config": {"workload": args.workload, "tokens_per_step": T, "layers": DEC_LAYERS,
                                       "context": DEC_CTX, "sliding_layers": sum(not c["full"] for c in layers),
                                       "full_layers": sum(c["full"] for c in layers), "parallelism": "single",
+                                      "launch": "one CUDA graph per step (captured once)",
                                       "l2": "every layer's weights and KV cache distinct, %.1f GB read per step "
                                             "(larger than L2)" % (algo / 1e9)},
             "step_split": {"attention_ms": attn_ms, "ffn_ms": ffn_ms, "attention_stage_us_per_layer": stage_us,
                            "note": "CUDA events around each layer's attention block and FFN (MoE + dense "
-                                   "MLP + tail), mean of 3 steps"},
+                                   "MLP + tail), mean of 3 eager steps (the timed steps replay a CUDA graph)"},
             "_roof": roof, "_ms": ms, "_per_step": per_step, "_launches": launches,
             "_e2e": e2e, "_e2e_io": (T * H * 2, T * H * 2), "_cpu": cpu}
 

@@ -104,6 +104,7 @@ struct gm_moe {
   cudaStream_t own_stream = nullptr;
   cudaStream_t side_stream = nullptr;  // L2 prefetches forked off the forward's stream
   cudaEvent_t fork_event = nullptr;
+  cudaEvent_t side_done = nullptr;   // joins the side stream back under stream capture
   // dense MLP of gm_ffn_forward, forked off the forward's stream and joined
   // before the post-MoE tail
   cudaStream_t dense_stream = nullptr;
@@ -908,7 +909,8 @@ int gm_moe_create(gm_moe_t** out, int device, int max_tokens, int num_layers, in
     return rc;
   }
   if (cudaStreamCreateWithFlags(&h->side_stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaEventCreateWithFlags(&h->fork_event, cudaEventDisableTiming) != cudaSuccess) {
+      cudaEventCreateWithFlags(&h->fork_event, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&h->side_done, cudaEventDisableTiming) != cudaSuccess) {
     cudaGetLastError();
     h->side_stream = nullptr;  // prefetch disabled; everything else works
   }
@@ -957,6 +959,7 @@ int gm_moe_destroy(gm_moe_t* h) {
   if (h->own_stream) cudaStreamDestroy(h->own_stream);
   if (h->side_stream) cudaStreamDestroy(h->side_stream);
   if (h->fork_event) cudaEventDestroy(h->fork_event);
+  if (h->side_done) cudaEventDestroy(h->side_done);
   if (h->dense_stream) cudaStreamDestroy(h->dense_stream);
   if (h->dense_fork) cudaEventDestroy(h->dense_fork);
   if (h->dense_done) cudaEventDestroy(h->dense_done);
@@ -1060,7 +1063,9 @@ int forward_impl(gm_moe* h, int layer, const void* x, void* out, int T, void* st
   // 0. decode batches route to nearly every expert: pull the gate/up weights
   // phase 1 reads first into L2 while the router runs (HBM is idle then).  The
   // prefetch runs on a side stream forked from `s`: nothing waits for it.
+  bool forked = false;
   if (L.kind == 1 && T >= 32 && !(L.has_tc && h->tc_ok && T >= h->tc_min_tokens) && h->side_stream) {
+    forked = true;
     GM_TRY(h, cudaEventRecord(h->fork_event, s), "prefetch fork");
     GM_TRY(h, cudaStreamWaitEvent(h->side_stream, h->fork_event, 0), "prefetch fork");
     const bool pdl = tls_pdl;
@@ -1123,7 +1128,19 @@ int forward_impl(gm_moe* h, int layer, const void* x, void* out, int T, void* st
   CombineTarget ct;
   ct.out = static_cast<uint16_t*>(out);
   ct.post = post;
-  return experts_and_combine(h, L, T, h->x_i8, h->x_sa, h->x_normed, h->route_idx, ct, s);
+  rc = experts_and_combine(h, L, T, h->x_i8, h->x_sa, h->x_normed, h->route_idx, ct, s);
+  if (rc == GM_OK && forked) {
+    // Nothing waits for the prefetch when the forward runs eagerly; while `s`
+    // is being captured into a CUDA graph, every stream forked from it must
+    // join it again before the capture ends, so the side stream joins here.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    GM_TRY(h, cudaStreamIsCapturing(s, &cs), "capture status");
+    if (cs == cudaStreamCaptureStatusActive) {
+      GM_TRY(h, cudaEventRecord(h->side_done, h->side_stream), "prefetch join");
+      GM_TRY(h, cudaStreamWaitEvent(s, h->side_done, 0), "prefetch join");
+    }
+  }
+  return rc;
 }
 }  // namespace
 
