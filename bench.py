@@ -52,7 +52,7 @@ WORKLOADS = {
 }
 ZIPF = {"bq-prefill-4k-zipf", "bf16-prefill-4k-zipf", "ep-prefill-16k"}
 # config 5: one decode step of 64 sequences through 30 MoE layers (distinct
-# weights per layer, the attention block between layers is an identity stand-in)
+# weights per layer; the MoE blocks alone, as the config states it -- decoder-b64-30L runs the whole step)
 WORKLOADS["bq-decode-b64-30L"] = (64, "bq", "replicas")
 LAYERS = {"bq-decode-b64-30L": 30}
 REF_SAMPLE_TOKENS = 512   # tokens per step of the --impl reference arm (CPU)

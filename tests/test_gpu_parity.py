@@ -423,6 +423,35 @@ def test_forward_ffn_post_moe_tail(T, layer_stress):
     assert (got == want).mean() > 0.97
 
 
+def test_forward_replays_from_a_cuda_graph(layer_stress):
+    """A decode forward (T = 64: the path that forks the L2 prefetch onto a
+    side stream) captured into a CUDA graph: the capture ends cleanly (every
+    forked stream joined) and each replay on new input equals the eager
+    forward bit for bit."""
+    raw, ref, g = layer_stress
+    blk = make_block(g, max_tokens=128)
+    T = 64
+    xs = [dev(tokens_np(T, seed=810 + i)) for i in range(3)]
+    want = []
+    for x in xs:
+        o = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        blk.forward(0, x, o, T)
+        want.append(o)
+    x_in = xs[0].clone()
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="relaxed"):
+        blk.forward(0, x_in, out, T, torch.cuda.current_stream())
+    for x, w in zip(xs[::-1], want[::-1]):
+        x_in.copy_(x)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), w.view(torch.int16))
+    assert blk.device_status() == 0
+    del graph
+
+
 def test_forward_deterministic_and_sync_host_path(layer_stress):
     raw, ref, g = layer_stress
     blk = make_block(g, max_tokens=128)
