@@ -477,6 +477,15 @@ def test_forward_deterministic_and_sync_host_path(layer_stress):
         blk.forward_sync(0, x_p, o_p, T)
         assert torch.equal(o_p.view(torch.int16), outs[0].cpu().view(torch.int16))
         o_p.zero_()
+    # the same buffers with new input content each call
+    for i in range(3):
+        x2_np = tokens_np(T, seed=820 + i)
+        want = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        blk.forward(0, dev(x2_np), want, T)
+        torch.cuda.synchronize()   # one handle's forwards must not overlap
+        x_p.copy_(torch.from_numpy(x2_np.view(np.int16)).view(torch.bfloat16))
+        blk.forward_sync(0, x_p, o_p, T)
+        assert torch.equal(o_p.view(torch.int16), want.cpu().view(torch.int16))
 
 
 def test_forward_errors_and_edges(layer_default):
