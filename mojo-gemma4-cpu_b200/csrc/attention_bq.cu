@@ -241,7 +241,16 @@ attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_
   using Sm = DecodeSmem<HD>;
   constexpr int TP = Sm::TP;
   constexpr int NW = DEC_WARPS;
-  constexpr int CPT = HD / DEC_THREADS;           // V columns per thread
+  constexpr int CPT = HD / DEC_THREADS;           // V columns per thread (the partial's layout)
+  // Phase C: a thread accumulates PVC adjacent columns (one shared load of
+  // PVC int8) over every PG-th position of the tile; with PG > 1 the PG
+  // position groups' sums are added in group order at the end of the split.
+  // Head 256 with 2 heads per group (the sliding layers): 4 columns x 4
+  // groups, fewer loads and conversions per FMA than one column per thread;
+  // otherwise CPT columns, one group.
+  constexpr int PVC = (HD == 256 && G == 2) ? 4 : CPT;
+  constexpr int PG = DEC_THREADS * PVC / HD;
+  static_assert(PG == 1 || HD == DEC_THREADS, "the group sum maps one column to a thread");
   constexpr int HPW = (G + NW - 1) / NW;          // heads whose softmax state a warp keeps
   constexpr int TPR = DEC_THREADS / TP;           // copying threads per row
   constexpr int CHUNKS = HD / (16 * TPR);         // 16-byte chunks per copying thread
@@ -318,11 +327,12 @@ attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_
     m[j] = NEG_BIG;
     l[j] = 0.0f;
   }
-  float acc[G][CPT];
+  const int cg = tid % (HD / PVC), pg = tid / (HD / PVC);
+  float acc[G][PVC];
 #pragma unroll
   for (int h = 0; h < G; ++h)
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) acc[h][c] = 0.0f;
+    for (int c = 0; c < PVC; ++c) acc[h][c] = 0.0f;
 
   if (b < e) issue(b, 0);
   int buf = 0;
@@ -396,18 +406,23 @@ attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_
     for (int h = 0; h < G; ++h) {
       const float cr = corr_s[h];
 #pragma unroll
-      for (int c = 0; c < CPT; ++c) acc[h][c] = __fmul_rn(acc[h][c], cr);
+      for (int c = 0; c < PVC; ++c) acc[h][c] = __fmul_rn(acc[h][c], cr);
     }
 #pragma unroll 4
-    for (int p = 0; p < n; ++p) {
+    for (int p = pg; p < n; p += PG) {
       uint32_t vw;
-      if constexpr (CPT == 2) vw = *reinterpret_cast<const uint16_t*>(&sm.v[buf][p][tid * CPT]);
-      else vw = (uint32_t)(uint8_t)sm.v[buf][p][tid * CPT];
-      float v[CPT];
+      if constexpr (PVC == 4) vw = *reinterpret_cast<const uint32_t*>(&sm.v[buf][p][cg * PVC]);
+      else if constexpr (PVC == 2) vw = *reinterpret_cast<const uint16_t*>(&sm.v[buf][p][cg * PVC]);
+      else vw = (uint32_t)(uint8_t)sm.v[buf][p][cg * PVC];
+      float v[PVC];
 #pragma unroll
-      for (int c = 0; c < CPT; ++c) v[c] = (float)(int8_t)((vw >> (8 * c)) & 0xFFu);
+      for (int c = 0; c < PVC; ++c) v[c] = (float)(int8_t)((vw >> (8 * c)) & 0xFFu);
       float a[G];
-      if constexpr (G % 4 == 0) {
+      if constexpr (G == 2) {
+        const float2 w2 = *reinterpret_cast<const float2*>(&wv[p][0]);
+        a[0] = w2.x;
+        a[1] = w2.y;
+      } else if constexpr (G % 4 == 0) {
 #pragma unroll
         for (int h4 = 0; h4 < G / 4; ++h4) {
           const float4 w4 = reinterpret_cast<const float4*>(&wv[p][0])[h4];
@@ -423,17 +438,36 @@ attn_decode_kernel(const int8_t* __restrict__ q_i8, const float* __restrict__ f_
 #pragma unroll
       for (int h = 0; h < G; ++h)
 #pragma unroll
-        for (int c = 0; c < CPT; ++c) acc[h][c] = __fmaf_rn(v[c], a[h], acc[h][c]);
+        for (int c = 0; c < PVC; ++c) acc[h][c] = __fmaf_rn(v[c], a[h], acc[h][c]);
     }
     __syncthreads();  // this buffer and part / wv / corr_s are reused
   }
 
   // one partial (m, l, acc) per head of the group
+  if constexpr (PG > 1) {
+    // the position groups' sums meet in the K buffers (free after the loop's
+    // last barrier), then thread tid adds column tid's groups in order
+    static_assert(PVC == 4 && sizeof(sm.k) >= sizeof(float) * PG * G * HD, "group sum fits the K buffers");
+    float* red = reinterpret_cast<float*>(&sm.k[0][0][0]);
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    float* dst = partials + (((size_t)t * num_q + g * G + h) * n_splits + s) * (HD + 2);
+    for (int h = 0; h < G; ++h)
+      reinterpret_cast<float4*>(red + (size_t)(pg * G + h) * HD)[cg] =
+          make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    __syncthreads();
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) dst[2 + tid * CPT + c] = acc[h][c];
+    for (int h = 0; h < G; ++h) {
+      float sum = red[(size_t)h * HD + tid];
+#pragma unroll
+      for (int q = 1; q < PG; ++q) sum = __fadd_rn(sum, red[(size_t)(q * G + h) * HD + tid]);
+      partials[(((size_t)t * num_q + g * G + h) * n_splits + s) * (HD + 2) + 2 + tid] = sum;
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float* dst = partials + (((size_t)t * num_q + g * G + h) * n_splits + s) * (HD + 2);
+#pragma unroll
+      for (int c = 0; c < PVC; ++c) dst[2 + cg * PVC + c] = acc[h][c];
+    }
   }
   if (lane == 0) {
 #pragma unroll
