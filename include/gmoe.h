@@ -432,8 +432,9 @@ int gm_rms_norm(const void* x, const void* gamma, int T, void* out, void* stream
 /* fused_norm_residual_add (kernels/rmsnorm.mojo:48-64, norm_residual_add_row),
  * as the decoder layer applies it after the attention block
  * (modeling/gemma_4_moe_bq.mojo:1098-1102): per token,
- * out = bf16(residual + (src * inv_rms(src)) * weight), bf16 [T][2816].  out
- * may be residual itself (the residual stream updated in place). */
+ * out = bf16(residual + (src * inv_rms(src)) * weight), bf16 [T][2816]
+ * (16-byte aligned).  out may be residual itself (the residual stream updated
+ * in place). */
 int gm_norm_residual_add(const void* src, const void* residual, const void* weight, int T, void* out,
                          void* stream);
 

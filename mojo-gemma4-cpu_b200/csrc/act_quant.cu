@@ -258,52 +258,56 @@ rms_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict_
 }
 
 // fused_norm_residual_add (kernels/rmsnorm.mojo:48-64 norm_residual_add_row):
-// out = bf16(residual + (src * inv_rms(src)) * w), one warp per token, the
-// sum of squares in rms_norm_bf16_kernel's order.  The decoder layer applies
+// out = bf16(residual + (src * inv_rms(src)) * w).  The decoder layer applies
 // it after the attention block's output projection (src = that output,
 // residual = x_main, out = x_main: modeling/gemma_4_moe_bq.mojo:1098-1102), so
-// out may alias residual: each lane reads its residual elements before it
-// stores the same elements.
-__global__ void __launch_bounds__(256)
+// out may alias residual: each thread reads its residual elements before it
+// stores the same elements.  One CTA of H/8 threads per token, thread i holds
+// elements [8i, 8i+8) (16-byte loads); the sum of squares is each thread's
+// chain, a warp tree, then the warps' sums in warp order.
+constexpr int NRA_THREADS = H / 8;  // 352
+
+__global__ void __launch_bounds__(NRA_THREADS)
 norm_residual_add_kernel(const uint16_t* __restrict__ src, const uint16_t* residual,
                          const uint16_t* __restrict__ w, int T, uint16_t* out) {
+  __shared__ float red[NRA_THREADS / 32];
   pdl_wait();
   pdl_trigger();
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int t = blockIdx.x;
   if (t >= T) return;
-  constexpr int NBLK = H / NORM_BLOCK;
-  const uint16_t* sr = src + (size_t)t * H;
-  float v[NBLK][4];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const size_t off = (size_t)t * H + 8 * threadIdx.x;
+  const uint4 sv = *reinterpret_cast<const uint4*>(src + off);
+  const uint4 rv = *reinterpret_cast<const uint4*>(residual + off);
+  const uint4 gv = *reinterpret_cast<const uint4*>(w + 8 * threadIdx.x);
+  const uint32_t su[4] = {sv.x, sv.y, sv.z, sv.w}, ru[4] = {rv.x, rv.y, rv.z, rv.w},
+                 gu[4] = {gv.x, gv.y, gv.z, gv.w};
+  float v[8];
   float ss = 0.0f;
 #pragma unroll
-  for (int b = 0; b < NBLK; ++b) {
-    uint2 raw = *reinterpret_cast<const uint2*>(sr + b * NORM_BLOCK + 4 * lane);
-    v[b][0] = bf2f(raw.x & 0xFFFFu);
-    v[b][1] = bf2f(raw.x >> 16);
-    v[b][2] = bf2f(raw.y & 0xFFFFu);
-    v[b][3] = bf2f(raw.y >> 16);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[b][j], v[b][j]));
+  for (int i = 0; i < 8; ++i) {
+    v[i] = bf2f((su[i >> 1] >> (16 * (i & 1))) & 0xFFFFu);
+    ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
   }
   ss = warp_sum(ss);
-  const float inv = inv_rms_from_sumsq(ss);
-  const uint16_t* rr = residual + (size_t)t * H;
-  uint16_t* dst = out + (size_t)t * H;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.0f;
 #pragma unroll
-  for (int b = 0; b < NBLK; ++b) {
-    const uint2 g = *reinterpret_cast<const uint2*>(w + b * NORM_BLOCK + 4 * lane);
-    const uint2 r = *reinterpret_cast<const uint2*>(rr + b * NORM_BLOCK + 4 * lane);
-    const float gv[4] = {bf2f(g.x & 0xFFFFu), bf2f(g.x >> 16), bf2f(g.y & 0xFFFFu), bf2f(g.y >> 16)};
-    const float rv[4] = {bf2f(r.x & 0xFFFFu), bf2f(r.x >> 16), bf2f(r.y & 0xFFFFu), bf2f(r.y >> 16)};
-    uint16_t o[4];
+  for (int i = 0; i < NRA_THREADS / 32; ++i) tot = __fadd_rn(tot, red[i]);
+  const float inv = inv_rms_from_sumsq(tot);
+  uint32_t o[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) o[j] = f2bf(__fadd_rn(rv[j], __fmul_rn(__fmul_rn(v[b][j], inv), gv[j])));
-    uint2 st;
-    st.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
-    st.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
-    *reinterpret_cast<uint2*>(dst + b * NORM_BLOCK + 4 * lane) = st;
+  for (int i = 0; i < 4; ++i) {
+    uint32_t pair = 0;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float r = bf2f((ru[i] >> (16 * k)) & 0xFFFFu), g = bf2f((gu[i] >> (16 * k)) & 0xFFFFu);
+      pair |= (uint32_t)f2bf(__fadd_rn(r, __fmul_rn(__fmul_rn(v[2 * i + k], inv), g))) << (16 * k);
+    }
+    o[i] = pair;
   }
+  *reinterpret_cast<uint4*>(out + off) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // rms_norm_bf16_kernel for the tcgen05 prefill path of bf16 layers: the
@@ -386,9 +390,7 @@ cudaError_t launch_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int T
 cudaError_t launch_norm_residual_add(const uint16_t* src, const uint16_t* residual, const uint16_t* w, int T,
                                      uint16_t* out, cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  const int wpb = T <= 512 ? 2 : 8;
-  return launch_k(norm_residual_add_kernel, dim3((T + wpb - 1) / wpb), dim3(32 * wpb), 0, s, src, residual, w,
-                  T, out);
+  return launch_k(norm_residual_add_kernel, dim3(T), dim3(NRA_THREADS), 0, s, src, residual, w, T, out);
 }
 
 }  // namespace gm

@@ -1766,6 +1766,8 @@ int gm_norm_residual_add(const void* src, const void* residual, const void* weig
                          void* stream) {
   if (T < 0 || (T > 0 && (!src || !residual || !weight || !out)))
     return set_err(nullptr, GM_EINVAL, "norm_residual_add: T=%d or a NULL pointer", T);
+  if (((uintptr_t)src | (uintptr_t)residual | (uintptr_t)weight | (uintptr_t)out) & 15)
+    return set_err(nullptr, GM_EINVAL, "norm_residual_add: buffers must be 16-byte aligned");
   STAGE(launch_norm_residual_add(static_cast<const uint16_t*>(src), static_cast<const uint16_t*>(residual),
                                  static_cast<const uint16_t*>(weight), T, static_cast<uint16_t*>(out),
                                  S(stream)),
