@@ -105,6 +105,19 @@ def test_attention_entry_points_validate_before_any_launch():
     assert b"geometry" in L.gm_last_error(None)
 
 
+def test_norm_residual_add_validates_before_any_launch():
+    """gm_norm_residual_add rejects NULL, negative T and buffers that are not
+    16-byte aligned on the host (no address is read), and T = 0 is a no-op."""
+    L = gmoe.lib()
+    p = ctypes.c_void_p
+    assert L.gm_norm_residual_add(p(0), p(256), p(256), 1, p(256), p(0)) == -1
+    assert b"NULL" in L.gm_last_error(None)
+    assert L.gm_norm_residual_add(p(256), p(256), p(256), -1, p(256), p(0)) == -1
+    assert L.gm_norm_residual_add(p(256), p(258), p(256), 1, p(256), p(0)) == -1
+    assert b"16-byte" in L.gm_last_error(None)
+    assert L.gm_norm_residual_add(p(0), p(0), p(0), 0, p(0), p(0)) == 0
+
+
 def test_header_compiles_as_c_and_cxx_and_links(tmp_path):
     """A C99 consumer (what Mojo's external_call, cgo or a ctypes user sees):
     the header compiles warning-free as C99 and C++17, every declared entry
